@@ -1,0 +1,342 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized decode/prefill hot path.
+
+Workload (one step = one greedy decode token): Llama-3-8B-shaped model with
+random-init N(0, 0.02) weights quantized to Q4_0 (32 layers, dim 4096, 32/8
+heads, head_dim 128, FFN 14336, vocab 128256, interleaved RoPE theta 5e5), a
+2048-token prefill of uniform-random ids, then batch-1 greedy decode with a
+paged fp16 KV cache.  `value` is decode tokens/s over all ranks (each rank
+runs an independent replica: weak scaling), timed on the device with CUDA
+events around K steps; the weights (4.2 GB) exceed L2 many times, so no
+flush is needed between steps.  The JSON line also carries the prefill rate,
+the quant-GEMV op sweep (HBM GB/s vs the measured peak), the roofline of the
+dominant decode kernel, an end-to-end figure through the C ABI with host
+buffers, the CPU baseline (the oracle port on the host cores) and clocks.
+
+`--impl reference` times the reference's portable CPU path (the oracle port,
+since the Rust crate cannot be built here) on the host cores.
+"""
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "jero-arch-llama_b200")
+METRIC = "Q4_0 decode tok/s (bs=1) + quant-GEMV HBM GB/s vs peak; prefill tok/s"
+SWEEP = [(4096, 4096), (11008, 4096), (4096, 11008), (14336, 4096)]
+L2_BYTES = 126 * 1024 * 1024
+SEED = 20251201
+
+
+def load_jal():
+    name = "jero_arch_llama_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    if not os.path.exists(os.path.join(PKG_DIR, "libjal.so")):
+        subprocess.run(["make", "-C", PKG_DIR, "-j", "16"], check=True)
+    spec = importlib.util.spec_from_file_location(name, os.path.join(PKG_DIR, "__init__.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic():
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def ev_time(torch, fn, stream):
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record(stream)
+    fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / 1e3
+
+
+def gemv_sweep(jal, torch, peak, quants, iters=200):
+    """Op sweep: M x K quant GEMV, rotating weight copies (> 4x L2) so each
+    launch streams from HBM."""
+    stream = torch.cuda.current_stream()
+    res = []
+    for qname in quants:
+        q = getattr(jal, qname)
+        bpb = 18 if q == jal.Q4_0 else 34
+        for rows, cols in SWEEP:
+            raw = jal.synth_matrix(q, rows, cols, seed=SEED, name=f"sweep.{rows}x{cols}")
+            copies = max(2, -(-4 * L2_BYTES // raw.nbytes))
+            mats = [jal.CachedMatrix.repack(raw, q, rows, cols) for _ in range(copies)]
+            x = torch.from_numpy(jal.synth_normal(cols, seed=SEED, name="sweep.act")).cuda()
+            q8 = torch.zeros(cols, dtype=torch.int8, device="cuda")
+            sc = torch.zeros(cols // 32, dtype=torch.float32, device="cuda")
+            jal.act_quantize_q8(x, 1, cols, q8, sc, stream)
+            y = torch.zeros(rows, dtype=torch.float32, device="cuda")
+            for i in range(2 * copies):
+                mats[i % copies].gemv_q8(q8, sc, y, stream)
+
+            def run():
+                for i in range(iters):
+                    mats[i % copies].gemv_q8(q8, sc, y, stream)
+
+            t = ev_time(torch, run, stream) / iters
+            alg = rows * cols // 32 * bpb + 4 * cols + 4 * rows
+            res.append({"quant": qname, "M": rows, "K": cols, "us": round(t * 1e6, 3),
+                        "GBps": round(alg / t / 1e9, 1), "frac_of_peak": round(alg / t / 1e9 / peak, 4),
+                        "bytes": alg})
+            del mats
+    return res
+
+
+def cpu_baseline(jal, gguf, spec, steps):
+    """The oracle port timed on the host cores: a 1-layer model of the same
+    shape (layer 0 + embedding + head) is decoded for `steps` tokens and the
+    LM head projection is timed alone; tok/s = 1 / (L * t_layer + t_head)."""
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    import gguf_py  # noqa: E402
+    import numpy as np  # noqa: E402
+    import oracle_py  # noqa: E402
+
+    _, tensors = gguf_py.parse(gguf)
+    keep = {k: v for k, v in tensors.items() if not k.startswith("blk.") or k.startswith("blk.0.")}
+    threads = os.cpu_count() or 1
+    geom = dict(num_layers=1, hidden_dim=spec.hidden_dim, ffn_dim=spec.ffn_dim, n_heads_q=spec.n_heads_q,
+                n_heads_kv=spec.n_heads_kv, head_dim=spec.head_dim, vocab_size=spec.vocab_size,
+                rms_eps=spec.rms_eps, rope_theta=spec.rope_theta)
+    m = oracle_py.Model(keep, geom, nthreads=threads)
+    cap = 64
+    kv = m.new_kv(cap)
+    m.prefill(kv, cap, [1, 2, 3, 4], 0)
+    head = tensors["output.weight"]
+    w = oracle_py.RepackedWeight(head.data, head.qtype, spec.vocab_size, spec.hidden_dim)
+    x = np.ones(spec.hidden_dim, dtype=np.float32)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        m.decode(kv, cap, 5 + i, 4 + i)
+    t_step = (time.perf_counter() - t0) / steps
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        w.project_batch(x, 1, nthreads=threads)
+    t_head = (time.perf_counter() - t0) / steps
+    t_layer = max(t_step - t_head, 1e-9)
+    t_tok = spec.num_layers * t_layer + t_head
+    return {"value": round(1.0 / t_tok, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} decode steps of layer 0 + LM head of the same model ({t_step * 1e3:.1f} ms/step), "
+                      f"head alone {t_head * 1e3:.1f} ms; extrapolated to {spec.num_layers} layers"}
+
+
+def reference_arm(args):
+    """--impl reference: the reference's portable CPU path (oracle port)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    jal = load_jal()
+    spec = jal.LLAMA3_8B_Q4_0
+    t0 = time.perf_counter()
+    gguf = jal.synth_gguf(spec, SEED)
+    gen_s = time.perf_counter() - t0
+    steps = max(1, args.steps)
+    base = cpu_baseline(jal, gguf, spec, steps)
+    line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(1e3 / base["value"], 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic: seeded N(0,0.02) weights quantized to Q4_0, uniform token ids",
+            "config": {"workload": "llama3-8b-shaped Q4_0 decode bs=1 (CPU port of the reference's portable path)",
+                       "layers": spec.num_layers, "hidden": spec.hidden_dim, "ffn": spec.ffn_dim,
+                       "vocab": spec.vocab_size, "gguf_gen_s": round(gen_s, 1)},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="jal", choices=["jal", "reference"])
+    ap.add_argument("--prefill", type=int, default=2048)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="llama3-8b-q4_0", choices=["llama3-8b-q4_0", "tiny"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import numpy as np
+    import torch
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    jal = load_jal()
+    jal.set_device(local)
+    spec = jal.LLAMA3_8B_Q4_0 if args.workload == "llama3-8b-q4_0" else jal.TINY_LLAMA
+    peak, peak_kind = measured_peaks()
+
+    t0 = time.perf_counter()
+    gguf = jal.synth_gguf(spec, SEED)
+    gen_s = time.perf_counter() - t0
+    recipe = jal.LlamaRecipe.from_gguf(gguf)
+    t0 = time.perf_counter()
+    cache = recipe.build_repack_cache(gguf, device=local)
+    build_s = time.perf_counter() - t0
+    n_prefill = min(args.prefill, spec.context_length - args.warmup - args.steps - 8)
+    n_ctx = n_prefill + 2 * (args.warmup + args.steps) + 16
+    ctx = jal.ExecutionContext(recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F16)
+    stream = torch.cuda.current_stream()
+    ctx.set_stream(stream)
+    rng = np.random.Generator(np.random.PCG64(SEED + rank))
+    prompt = rng.integers(0, spec.vocab_size, n_prefill).astype(np.uint32)
+
+    # Prefill (device-timed; includes the token upload and the logits read).
+    logits = None
+
+    def do_prefill():
+        nonlocal logits
+        logits = ctx.prefill_step(prompt, 0)
+
+    t_prefill = ev_time(torch, do_prefill, stream)
+    tok = int(np.argmax(logits))
+    # Decode warm-up, then K timed steps (one CUDA graph launch per token).
+    ctx.decode_greedy(tok, args.warmup)
+    tok = int(rng.integers(0, spec.vocab_size))
+    if dist:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        t_dec = ev_time(torch, lambda: ctx.decode_greedy(tok, args.steps), stream)
+    if dist:
+        tt = torch.tensor([t_dec, t_prefill], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_dec, t_prefill = float(tt[0]), float(tt[1])
+    # End to end through the C ABI with host buffers: per step the token goes
+    # up from pinned memory and the full logits row comes back.
+    pos0 = ctx.position()
+    t_e2e = ev_time(torch, lambda: [ctx.decode_step(tok) for _ in range(args.steps)], stream)
+    if dist:
+        tt = torch.tensor([t_e2e], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_e2e = float(tt[0])
+    assert ctx.position() == pos0 + args.steps
+
+    launches = ctx.launches_per_step()
+    bytes_token = cache.total_aligned_bytes() - spec.vocab_size * 0  # layer weights + head + norms
+    kv_bytes = 2 * spec.num_layers * spec.n_heads_kv * spec.head_dim * 2 * (n_prefill + args.warmup + args.steps // 2)
+    step_s = t_dec / args.steps
+    line = {"metric": METRIC, "value": round(world * args.steps / t_dec, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic: seeded N(0,0.02) weights quantized to Q4_0, uniform-random token ids",
+            "config": {"workload": f"{args.workload} decode bs=1 greedy after a {n_prefill}-token prefill",
+                       "layers": spec.num_layers, "hidden": spec.hidden_dim, "heads": [spec.n_heads_q, spec.n_heads_kv],
+                       "head_dim": spec.head_dim, "ffn": spec.ffn_dim, "vocab": spec.vocab_size,
+                       "weights": "Q4_0 (4.5 bpw in HBM)", "kv_cache": "paged fp16", "parallelism": f"replicas x{world}",
+                       "l2": "no flush: each step streams the 4.2 GB of weights (> L2)",
+                       "gguf_gen_s": round(gen_s, 1), "repack_s": round(build_s, 2)},
+            "decode_step": {"bytes_per_token": bytes_token + kv_bytes,
+                            "GBps": round((bytes_token + kv_bytes) / step_s / 1e9, 1),
+                            "frac_of_peak": round((bytes_token + kv_bytes) / step_s / 1e9 / peak, 4),
+                            "peak_GBps": peak, "peak_kind": peak_kind},
+            "prefill": {"tokens": int(n_prefill), "s": round(t_prefill, 4),
+                        "tok_per_s": round(world * n_prefill / t_prefill, 1)},
+            "e2e": {"value": round(world * args.steps / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 8,
+                    "d2h_bytes_per_step": 4 * spec.vocab_size},
+            "gpu_launches": launches * (args.steps + args.warmup) + 0,
+            "clocks": clk.summary()}
+    if rank == 0 and not args.no_sweep:
+        sweep = gemv_sweep(jal, torch, peak, ["Q4_0", "Q8_0"])
+        line["gemv_sweep"] = sweep
+        dom = next(s for s in sweep if s["quant"] == "Q4_0" and s["M"] == 14336)
+        traffic = committed_traffic().get("gemv_q4_0_14336x4096")
+        line["roofline"] = {"kernel": "k_gemv<Q4_0,M=1> 14336x4096 (decode quant-GEMV)", "bound": "hbm",
+                            "achieved": dom["GBps"], "peak": peak, "unit": "GB/s",
+                            "frac": round(dom["GBps"] / peak, 4), "traffic": traffic,
+                            "algorithmic_bytes": dom["bytes"], "peak_kind": peak_kind}
+        line["gpu_launches"] += sum(200 + 2 * max(2, -(-4 * L2_BYTES // (s["bytes"]))) for s in sweep)
+    if rank == 0 and world == 1 and not args.no_cpu and args.workload == "llama3-8b-q4_0":
+        line["cpu_baseline"] = cpu_baseline(jal, gguf, spec, steps=3)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del ctx
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,290 @@
+/*
+ * jal.h -- C ABI of the B200-native (sm_100a) quantized decode/prefill hot
+ * path of jero-arch-llama.
+ *
+ * Every entry point below replaces one public item of the reference crate's
+ * recipe / repack_cache / decode_gemv / dispatch surface; the comment beside
+ * each names the reference item it stands in for (file:line in the reference
+ * crate).  Conventions:
+ *   - every function returns an int status (JAL_OK = 0); the codes mirror
+ *     jero_core::K3Error.  Nothing aborts; jal_last_error() gives the reason.
+ *   - "device pointer" arguments point into CUDA device memory of the current
+ *     device; "host pointer" arguments point into host memory.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy stream).
+ *   - handles are owned by the caller and released with the matching _free.
+ *   - a context is single-threaded; independent contexts may run concurrently.
+ */
+#ifndef JAL_H
+#define JAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (jero_core::K3Error) ---------------------------------- */
+#define JAL_OK 0
+#define JAL_ERR_TENSOR_BOUNDS 1           /* K3Error::TensorBoundsError */
+#define JAL_ERR_CAPABILITY_MISMATCH 2     /* K3Error::CapabilityMismatch */
+#define JAL_ERR_CONTEXT_LENGTH_EXCEEDED 3 /* K3Error::ContextLengthExceeded */
+#define JAL_ERR_CUDA 4                    /* a CUDA runtime call failed */
+#define JAL_ERR_INVALID_ARGUMENT 5        /* null handle / pointer */
+#define JAL_ERR_NCCL 6                    /* an NCCL call failed */
+#define JAL_ERR_TIMEOUT 7                 /* a bounded device wait gave up */
+
+/* ---- GGML tensor types (jero_core::QuantType; GGUF type ids) ------------ */
+#define JAL_F32 0
+#define JAL_F16 1
+#define JAL_Q4_0 2
+#define JAL_Q5_0 6
+#define JAL_Q8_0 8
+#define JAL_Q4_K 12
+#define JAL_Q5_K 13
+#define JAL_Q6_K 14
+#define JAL_BF16 30
+#define JAL_TQ1_0 34
+#define JAL_TQ2_0 35
+
+/* Human-readable reason for the last non-zero status on this thread. */
+const char *jal_last_error(void);
+/* Library version string. */
+const char *jal_version(void);
+/* Select the CUDA device used by later calls on this thread. */
+int jal_set_device(int device);
+/* Number of SMs of the current device (for launch sizing by callers). */
+int jal_device_sm_count(int *out);
+
+/* ========================================================================
+ * repack_cache.rs -- CachedMatrix
+ * ====================================================================== */
+typedef struct jal_cached_matrix jal_cached_matrix;
+
+/* CachedMatrix::repack (repack_cache.rs:1516-1579).  `raw` holds `rows` GGUF
+ * rows of `cols` elements of type `quant` (host pointer if raw_on_device == 0,
+ * else a device pointer).  The device repack keeps Q4_0 at 4.5 bits per
+ * weight and Q8_0 at 8.5.  Errors: JAL_ERR_CAPABILITY_MISMATCH for an
+ * unsupported quant, JAL_ERR_TENSOR_BOUNDS for a length / shape mismatch. */
+int jal_cached_matrix_repack(const void *raw, size_t raw_len, int raw_on_device,
+                             int quant, size_t rows, size_t cols,
+                             void *stream, jal_cached_matrix **out);
+void jal_cached_matrix_free(jal_cached_matrix *m);
+/* CachedMatrix::{rows, cols, quant, aligned_bytes, uses_repacked_storage}
+ * (repack_cache.rs:1583-1628).  aligned_bytes is the device bytes held. */
+size_t jal_cached_matrix_rows(const jal_cached_matrix *m);
+size_t jal_cached_matrix_cols(const jal_cached_matrix *m);
+int jal_cached_matrix_quant(const jal_cached_matrix *m);
+size_t jal_cached_matrix_aligned_bytes(const jal_cached_matrix *m);
+
+/* Export the device repack in the reference's portable tile layout
+ * (repack_cache.rs:639-694): tiles[(r/8)*k_chunks + ch] of 128 i8 with byte
+ * (r%8)*16+t = q[r][ch*16+t]; scales[((r/8)*groups+g)*8 + r%8] as f32 from
+ * f16_to_f32_finite.  Host output buffers; lengths are element counts:
+ * tiles_len >= ceil(rows/8)*cols/16*128, scales_len >= ceil(rows/8)*groups*8.
+ * Used to prove the repack bit-exact. */
+int jal_cached_matrix_export_ref_layout(const jal_cached_matrix *m,
+                                        int8_t *tiles, size_t tiles_len,
+                                        float *scales, size_t scales_len);
+
+/* CachedMatrix::project_batch / gemm_rows (repack_cache.rs:1709-1787):
+ * quantize the [m, cols] f32 activations per 32-block (QuantizedActQ8,
+ * repack_cache.rs:390-422) and compute y[m, rows].  Device pointers. */
+int jal_cached_matrix_gemm(const jal_cached_matrix *mat, const float *x,
+                           size_t m, float *y, void *stream);
+/* CachedMatrix::gemv_with_act_view (repack_cache.rs:1636-1672) with an
+ * already quantized activation (q8: cols int8, scales: cols/32 f32). */
+int jal_cached_matrix_gemv_q8(const jal_cached_matrix *mat, const int8_t *q8,
+                              const float *scales, float *y, void *stream);
+/* Integer 16-element block-dot partials of rows [r0, r1) against one
+ * quantized activation (the i32 `dot_i32` of repack_cache.rs:759-762):
+ * out[(r - r0) * (cols/16) + ch].  Device pointers. */
+int jal_cached_matrix_dot16_partials(const jal_cached_matrix *mat,
+                                     const int8_t *q8, size_t r0, size_t r1,
+                                     int32_t *out, void *stream);
+
+/* QuantizedActQ8::quantize_into (repack_cache.rs:491-531): per 32-block
+ * scale = amax/127, inv = 1/scale, q = clamp(round(v*inv), -127, 127),
+ * non-finite inputs count as 0.  x: [m, k]; q8: [m, ceil(k/32)*32];
+ * scales: [m, ceil(k/32)].  Device pointers. */
+int jal_act_quantize_q8(const float *x, size_t m, size_t k, int8_t *q8,
+                        float *scales, void *stream);
+/* quantize_row_q8_0 (decode_gemv.rs:294-313): BlockQ8_0 {f32 d; i8 qs[32]}
+ * (36 bytes) with inv = 127/amax.  n % 32 == 0.  Device pointers. */
+int jal_quantize_row_q8_0(const float *x, size_t n, void *blocks,
+                          void *stream);
+
+/* ========================================================================
+ * decode_gemv.rs / dispatch.rs -- streaming raw-GGUF GEMV
+ * ====================================================================== */
+/* gemv_decode_projection (decode_gemv.rs:1395-1407) and
+ * project_lm_head_row_split (dispatch.rs:191-289) for Q4_0/Q5_0/Q8_0 rows
+ * in raw GGUF block order: y = W x with the BlockQ8_0 activation quantizer
+ * and per-32-block f32(sumi) * (dw * dx) accumulation (decode_gemv.rs:
+ * 394-439, 622-642).  raw: device pointer to rows*cols GGUF elements. */
+int jal_gemv_decode_projection(const void *raw, size_t raw_len, int quant,
+                               size_t rows, size_t cols, const float *x,
+                               float *y, void *stream);
+
+/* ========================================================================
+ * recipe.rs -- fused per-op entry points (device pointers, f32)
+ * ====================================================================== */
+/* rmsnorm_row over m rows (recipe.rs:2534-2558, eps as given). */
+int jal_op_rmsnorm(const float *x, const float *w, size_t m, size_t n,
+                   float eps, float *out, void *stream);
+/* apply_rope_compat (recipe.rs:2775-2834) on m rows of `row_len` floats at
+ * positions pos0..pos0+m-1, using the inv_freq table (rotary_dim/2 floats,
+ * device).  neox = 0: pairs (2i, 2i+1); 1: pairs (i, i+rotary_dim/2). */
+int jal_op_rope(float *qk, size_t m, size_t row_len, size_t head_dim,
+                size_t rotary_dim, int neox, size_t pos0,
+                const float *inv_freq, void *stream);
+/* swiglu_compat (recipe.rs:3024-3050): out = (g*sigmoid(g))*u. */
+int jal_op_swiglu(const float *gate, const float *up, size_t n, float *out,
+                  void *stream);
+/* gqa_attention_prefill_portable (recipe.rs:2949-3022): m queries at
+ * start_pos.. over f32 K/V planes [total_seq][n_kv*head_dim]; causal, with
+ * an optional sliding window (0 = none). */
+int jal_op_gqa_attention(const float *q, const float *k, const float *v,
+                         size_t m, size_t n_heads_q, size_t n_heads_kv,
+                         size_t head_dim, size_t total_seq, size_t start_pos,
+                         size_t sliding_window, float scale, float *out,
+                         void *stream);
+
+/* ========================================================================
+ * recipe.rs -- LlamaRecipe
+ * ====================================================================== */
+typedef struct jal_recipe jal_recipe;
+
+#define JAL_ROPE_NORM 0 /* RopeType::Norm: interleaved pairs */
+#define JAL_ROPE_NEOX 1 /* RopeType::NeoX: split-half pairs */
+
+#define JAL_ROPE_SCALING_NONE 0
+#define JAL_ROPE_SCALING_LINEAR 1
+#define JAL_ROPE_SCALING_LLAMA3 2
+#define JAL_ROPE_SCALING_LONGROPE 3
+
+/* The public fields of LlamaRecipe (recipe.rs:110-139). */
+typedef struct jal_recipe_fields {
+  char architecture[16];
+  uint64_t num_layers, hidden_dim, ffn_dim, n_heads_q, n_heads_kv, head_dim,
+      vocab_size;
+  float rms_eps, rope_theta;
+  int32_t rope_type;   /* JAL_ROPE_NORM / JAL_ROPE_NEOX */
+  int64_t rotary_dim;  /* -1 = None (use head_dim) */
+  int32_t rope_scaling_kind;
+  float rope_factor, rope_low_freq_factor, rope_high_freq_factor;
+  uint64_t rope_original_max_position_embeddings;
+} jal_recipe_fields;
+
+/* LlamaRecipe::new / new_llama4 / new_qwen2 (recipe.rs:163-222) by
+ * architecture string "llama" / "llama4" / "qwen2". */
+int jal_recipe_new(const char *architecture, jal_recipe **out);
+/* LlamaRecipe::from_gguf (recipe.rs:336-422): hydrate from GGUF v3 bytes. */
+int jal_recipe_from_gguf(const void *gguf, size_t len, jal_recipe **out);
+void jal_recipe_free(jal_recipe *r);
+int jal_recipe_get_fields(const jal_recipe *r, jal_recipe_fields *out);
+int jal_recipe_set_fields(jal_recipe *r, const jal_recipe_fields *in);
+/* with_irope_mask (recipe.rs:452-455) / should_skip_rope (recipe.rs:466-472) */
+int jal_recipe_set_irope_mask(jal_recipe *r, const uint8_t *mask, size_t n);
+int jal_recipe_should_skip_rope(const jal_recipe *r, size_t layer);
+/* with_rope_scaling LongRope tables (recipe.rs:56-64, 2638-2657). */
+int jal_recipe_set_longrope(jal_recipe *r, const float *short_factor,
+                            const float *long_factor, size_t n,
+                            uint64_t original_max_position_embeddings);
+/* ArchRecipe::supports_quant (recipe.rs:1819-1832): 1 / 0. */
+int jal_recipe_supports_quant(const jal_recipe *r, int quant);
+/* ArchRecipe::validate_model (recipe.rs:1834-1931) over GGUF bytes. */
+int jal_recipe_validate_model(const jal_recipe *r, const void *gguf,
+                              size_t len);
+/* decode_scratch_bytes (recipe.rs:529-547): device scratch bytes one
+ * context needs for decode up to seq_len_upper_bound positions. */
+size_t jal_recipe_decode_scratch_bytes(const jal_recipe *r,
+                                       size_t seq_len_upper_bound);
+
+/* ========================================================================
+ * repack_cache.rs -- ModelRepackCache
+ * ====================================================================== */
+typedef struct jal_model_cache jal_model_cache;
+
+/* LlamaRecipe::build_repack_cache (recipe.rs:481-509) ->
+ * ModelRepackCache::build (repack_cache.rs:2166-2257): upload and repack
+ * every layer matrix, norm and bias of the GGUF model onto `device`. */
+int jal_model_repack_cache_build(const jal_recipe *r, const void *gguf,
+                                 size_t len, int device,
+                                 jal_model_cache **out);
+void jal_model_repack_cache_free(jal_model_cache *c);
+/* ModelRepackCache accessors (repack_cache.rs:2259-2380). */
+size_t jal_model_cache_num_layers(const jal_model_cache *c);
+size_t jal_model_cache_hidden_dim(const jal_model_cache *c);
+size_t jal_model_cache_ffn_dim(const jal_model_cache *c);
+size_t jal_model_cache_total_q(const jal_model_cache *c);
+size_t jal_model_cache_total_kv(const jal_model_cache *c);
+size_t jal_model_cache_vocab_size(const jal_model_cache *c);
+size_t jal_model_cache_norm_count(const jal_model_cache *c);
+size_t jal_model_cache_bias_count(const jal_model_cache *c);
+size_t jal_model_cache_repacked_matrix_count(const jal_model_cache *c);
+size_t jal_model_cache_total_aligned_bytes(const jal_model_cache *c);
+/* Borrow layer matrices (LayerRepackCache fields, repack_cache.rs:
+ * 2084-2111): which = 0 q, 1 k, 2 v, 3 output, 4 gate, 5 up, 6 down;
+ * layer = num_layers selects the LM head.  Owned by the cache. */
+const jal_cached_matrix *jal_model_cache_matrix(const jal_model_cache *c,
+                                                size_t layer, int which);
+
+/* ========================================================================
+ * ExecutionContext + prefill_step / decode_step
+ * ====================================================================== */
+typedef struct jal_context jal_context;
+
+#define JAL_KV_F32 0 /* parity mode: f32 K/V like the reference */
+#define JAL_KV_F16 1 /* paged fp16 K/V */
+
+typedef struct jal_context_config {
+  uint64_t n_ctx;          /* max positions (ExecutionContext::n_ctx) */
+  int32_t kv_dtype;        /* JAL_KV_F32 / JAL_KV_F16 */
+  uint32_t page_size;      /* tokens per KV page (0 = 64) */
+  uint64_t sliding_window; /* KvGeometry::sliding_window, 0 = none */
+  int32_t use_graphs;      /* capture the decode step in a CUDA graph */
+} jal_context_config;
+
+int jal_context_new(const jal_recipe *r, const jal_model_cache *c,
+                    const jal_context_config *cfg, jal_context **out);
+void jal_context_free(jal_context *ctx);
+/* ExecutionContext::position. */
+size_t jal_context_position(const jal_context *ctx);
+/* Drop all positions (KV content becomes stale). */
+int jal_context_reset(jal_context *ctx);
+/* prefill_step_with_cache (recipe.rs:517-524, 564-608): n prompt tokens at
+ * start_pos (chunked prefill when start_pos > 0).  When compute_logits,
+ * logits (host, logits_len == vocab) receive the last token's logits.
+ * Position becomes start_pos + n; unchanged on error. */
+int jal_prefill_step(jal_context *ctx, const uint32_t *tokens, size_t n,
+                     size_t start_pos, int compute_logits, float *logits,
+                     size_t logits_len);
+/* decode_step_with_cache (recipe.rs:555-562, 718-1163): one token at the
+ * current position; logits (host, vocab floats) may be NULL.  Position
+ * advances by one; unchanged on error. */
+int jal_decode_step(jal_context *ctx, uint32_t token, float *logits,
+                    size_t logits_len);
+/* Greedy decode of n_steps tokens on the device, starting from `token` at
+ * the current position (argmax, lowest index wins ties; the reference
+ * leaves sampling to the engine).  tokens_out (host) gets n_steps ids. */
+int jal_decode_greedy(jal_context *ctx, uint32_t token, size_t n_steps,
+                      uint32_t *tokens_out);
+/* Copy the KV cache of positions [0, n_pos) into the reference's f32 layout
+ * [layer][K|V][n_pos][n_kv*head_dim] (host buffer, len floats). */
+int jal_context_export_kv(const jal_context *ctx, size_t n_pos, float *out,
+                          size_t len);
+/* Device pointer to the last logits (vocab f32) for zero-copy callers. */
+int jal_context_logits_device(const jal_context *ctx, const float **out);
+/* Number of kernels one decode step launches (graph nodes when graphs are
+ * on). */
+int jal_context_last_step_launches(const jal_context *ctx, size_t *out);
+/* Issue the context's work on `stream` (a cudaStream_t; NULL restores the
+ * context's own stream).  Lets callers order it with their own work and
+ * time it with events recorded on the same stream. */
+int jal_context_set_stream(jal_context *ctx, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JAL_H */

@@ -1,0 +1,83 @@
+// Device helpers shared by the sm_100a kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace jal {
+
+// f16_to_f32_finite (repack_cache.rs:160-181): IEEE half -> f32, with the
+// Inf/NaN encodings mapped to +-0.0625.  Subnormals convert exactly.
+__device__ __forceinline__ float f16_finite(uint16_t h) {
+  if ((h & 0x7C00u) == 0x7C00u) return (h & 0x8000u) ? -0.0625f : 0.0625f;
+  return __half2float(__ushort_as_half(h));
+}
+
+// bf16_to_f32_finite (repack_cache.rs:184-191).
+__device__ __forceinline__ float bf16_finite(uint16_t h) {
+  if (((h >> 7) & 0xFF) == 0xFF) return (h & 0x8000u) ? -0.0625f : 0.0625f;
+  return __uint_as_float((uint32_t)h << 16);
+}
+
+// sanitize_f32_weight (repack_cache.rs:1028-1036).
+__device__ __forceinline__ float sanitize_weight(float v) {
+  if (!isfinite(v)) return 0.0f;
+  if (fabsf(v) > 1.0e6f) return signbit(v) ? -0.0625f : 0.0625f;
+  return v;
+}
+
+// Sum of four u8 x s8 products plus c (PTX dp4a.u32.s32).
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// 16-byte streaming load that does not allocate in L1 (weights are read
+// once per step).
+__device__ __forceinline__ uint4 ldg_stream16(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint16_t ldg_stream2(const uint16_t *p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+// Per-32-block activation quantization of QuantizedActQ8
+// (repack_cache.rs:390-422): non-finite -> 0, scale = amax/127,
+// inv = 1/scale, q = clamp(round(v*inv), -127, 127).  Correctly rounded
+// division/multiplication keep every value bit-identical to the reference.
+__device__ __forceinline__ float act_scale_from_amax(float amax) {
+  return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 0.0f;
+}
+__device__ __forceinline__ float act_inv_from_scale(float scale) {
+  return scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+}
+__device__ __forceinline__ int8_t act_quant_one(float v, float inv) {
+  float q = roundf(__fmul_rn(v, inv));
+  q = fminf(fmaxf(q, -127.0f), 127.0f);
+  return (int8_t)q;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Programmatic dependent launch controls (no-ops without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+}  // namespace jal

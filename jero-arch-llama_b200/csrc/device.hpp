@@ -1,0 +1,170 @@
+// Device-side data layout shared by the host orchestration and the kernels.
+//
+// HBM layout of a repacked quantized matrix (B200 layout):
+//   qs : rows x qs_stride bytes.  Q4_0: the 16 nibble bytes of each GGUF
+//        block back to back (byte i = elem i | elem i+16 << 4), so a row is
+//        cols/2 bytes and every block starts on a 16-byte boundary.  Q8_0:
+//        the 32 int8 of each block back to back (cols bytes per row).
+//   d  : rows x d_stride f16 bit patterns, one per 32-block, with d_stride
+//        rounded up to a multiple of 8 (16 bytes) so every row starts
+//        16-byte aligned.  Decoded with the reference's f16_to_f32_finite.
+// Weight bytes therefore stay at 4.5 (Q4_0) / 8.5 (Q8_0) bits per weight.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace jal {
+
+struct DevMat {
+  int quant = 0;          // JAL_Q4_0, JAL_Q8_0, or JAL_F32 for dense rows
+  int64_t rows = 0, cols = 0;
+  const uint8_t *qs = nullptr;
+  const uint16_t *d = nullptr;
+  const float *dense = nullptr;  // dense f32 rows (cols stride), float types
+  int64_t qs_stride = 0;  // bytes per row
+  int64_t d_stride = 0;   // f16 scales per row (multiple of 8)
+};
+
+inline int64_t d_stride_for(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
+
+// ---- GEMV (decode, M tokens <= kGemvMaxM) ------------------------------
+enum GemvIn : int { GEMV_IN_Q8 = 0, GEMV_IN_F32 = 1, GEMV_IN_NORM = 2 };
+enum GemvOut : int { GEMV_OUT_STORE = 0, GEMV_OUT_ADD = 1, GEMV_OUT_SWIGLU_Q = 2 };
+constexpr int kGemvMaxM = 8;
+
+struct GemvArgs {
+  DevMat w;
+  int64_t rows = 0;        // logical output rows (pairs for SWIGLU)
+  int m = 1;               // tokens
+  int in_mode = GEMV_IN_Q8;
+  const float *x = nullptr;     // [m][x_stride] f32 (IN_F32 / IN_NORM)
+  const float *norm_w = nullptr;
+  float eps = 1e-5f;
+  const int8_t *xq = nullptr;   // [m][xq_stride] int8 (IN_Q8)
+  const float *xs = nullptr;    // [m][xq_stride/32] f32 scales (IN_Q8)
+  int64_t x_stride = 0, xq_stride = 0;
+  int out_mode = GEMV_OUT_STORE;
+  float *y = nullptr;           // [m][y_stride]
+  int64_t y_stride = 0;
+  const float *bias = nullptr;  // per output row (OUT_STORE / OUT_ADD)
+  int64_t up_offset = 0;        // SWIGLU: physical row offset of the up half
+  int8_t *yq = nullptr;         // SWIGLU_Q: [m][rows] int8
+  float *ys = nullptr;          // SWIGLU_Q: [m][rows/32] scales
+  unsigned *group_cnt = nullptr;  // SWIGLU_Q: [m][rows/32] zero-initialised
+  int grid = 0;                 // CTAs (0 = auto)
+  int pdl = 0;                  // launch with programmatic dependent launch
+};
+
+void launch_gemv(const GemvArgs &a, cudaStream_t s);
+int gemv_default_grid(const GemvArgs &a);
+
+// ---- repack / export / activation quantizers ---------------------------
+void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, uint8_t *qs, uint16_t *d,
+                   int64_t qs_stride, int64_t d_stride, cudaStream_t s);
+void launch_repack_dense(const uint8_t *raw, int quant, int64_t rows, int64_t cols, float *out,
+                         cudaStream_t s);
+void launch_export_ref(const DevMat &w, int8_t *tiles, float *scales, cudaStream_t s);
+void launch_act_quant(const float *x, int64_t m, int64_t k, int64_t x_stride, int8_t *q8, float *scales,
+                      cudaStream_t s);
+void launch_quantize_row_q8_0(const float *x, int64_t n, void *blocks, cudaStream_t s);
+void launch_rmsnorm(const float *x, const float *w, int64_t m, int64_t n, float eps, float *out,
+                    cudaStream_t s);
+// Per-row RMSNorm then QuantizedActQ8 of the normed row (prefill).
+void launch_rmsnorm_quant(const float *x, const float *w, int64_t m, int64_t n, float eps, int8_t *q8,
+                          float *scales, cudaStream_t s);
+void launch_dot16_partials(const DevMat &w, const int8_t *q8, int64_t r0, int64_t r1, int32_t *out,
+                           cudaStream_t s);
+void launch_gemv_raw(const uint8_t *raw, int quant, int64_t rows, int64_t cols, const void *xblocks,
+                     float *y, cudaStream_t s);
+
+// ---- GEMM (prefill) -------------------------------------------------------
+// y[m][rows] (= or +=) q8[m][K] x W^T with per-16-chunk integer partials.
+struct GemmArgs {
+  DevMat w;
+  int64_t m = 0, rows = 0;
+  const int8_t *xq = nullptr;  // [m][K]
+  const float *xs = nullptr;   // [m][K/32]
+  float *y = nullptr;
+  int64_t y_stride = 0;
+  const float *bias = nullptr;
+  int accumulate = 0;          // y += result
+};
+void launch_gemm(const GemmArgs &a, cudaStream_t s);
+
+// ---- elementwise / attention ---------------------------------------------
+void launch_rope_rows(float *qk, int64_t m, int64_t row_len, int64_t head_dim, int64_t rotary_dim, int neox,
+                      int64_t pos0, const float *inv_freq, cudaStream_t s);
+void launch_swiglu(const float *g, const float *u, int64_t n, float *out, cudaStream_t s);
+void launch_swiglu_rows(const float *gu, int64_t m, int64_t f, int64_t stride, float *out, cudaStream_t s);
+void launch_gqa_attention_ref(const float *q, const float *k, const float *v, int64_t m, int64_t nq, int64_t nkv,
+                              int64_t hd, int64_t total_seq, int64_t start_pos, int64_t window, float scale,
+                              float *out, cudaStream_t s);
+
+// KV cache pool: element (layer, page, head, slot, dim) at
+// (((layer * n_pages + page) * n_kv + head) * page_size + slot) * head_dim + dim,
+// one pool for K and one for V; dtype f32 or f16.
+struct KvView {
+  void *k = nullptr, *v = nullptr;
+  int f16 = 1;
+  int64_t n_pages = 0, page_size = 64, n_kv = 0, head_dim = 0, n_layers = 0;
+  const int32_t *page_table = nullptr;  // logical page -> physical page
+};
+
+struct AttnDecodeArgs {
+  const float *qkv = nullptr;  // [q | k | v] f32 of one token
+  const float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+  const float *cos_tab = nullptr, *sin_tab = nullptr;  // [n_ctx][rot/2]
+  const float *cos_tab_long = nullptr, *sin_tab_long = nullptr;
+  int64_t long_threshold = -1;  // use long tables when pos + 1 > threshold
+  int skip_rope = 0, neox = 0;
+  int64_t n_heads_q = 0, rotary_dim = 0;
+  KvView kv;
+  int64_t layer = 0;
+  const int64_t *d_pos = nullptr;  // current position (device)
+  int64_t window = 0;
+  float scale = 1.f;
+  int n_splits = 1;
+  float *part = nullptr;        // [n_kv][n_splits][G][head_dim + 2]
+  unsigned *split_cnt = nullptr;  // [n_kv], zero-initialised
+  float *out = nullptr;         // [n_heads_q * head_dim]
+  int8_t *out_q = nullptr;      // quantized out (QuantizedActQ8)
+  float *out_s = nullptr;
+  int pdl = 0;
+};
+void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
+
+// Prefill: bias + RoPE on q/k rows, append k/v of m tokens into the cache.
+struct RopeAppendArgs {
+  float *qkv = nullptr;  // [m][qkv_stride]: q | k | v
+  int64_t m = 0, qkv_stride = 0, start_pos = 0;
+  const float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+  const float *cos_tab = nullptr, *sin_tab = nullptr;
+  int skip_rope = 0, neox = 0;
+  int64_t n_heads_q = 0, rotary_dim = 0;
+  KvView kv;
+  int64_t layer = 0;
+};
+void launch_rope_append(const RopeAppendArgs &a, cudaStream_t s);
+
+struct AttnPrefillArgs {
+  const float *qkv = nullptr;  // q rows at stride qkv_stride
+  int64_t m = 0, qkv_stride = 0, start_pos = 0;
+  int64_t n_heads_q = 0;
+  KvView kv;
+  int64_t layer = 0, window = 0;
+  float scale = 1.f;
+  float *out = nullptr;  // [m][n_heads_q*head_dim]
+};
+void launch_attn_prefill(const AttnPrefillArgs &a, cudaStream_t s);
+
+// Embedding row decode (repack_cache.rs:1166-1301 semantics) for tokens
+// read from device memory.
+void launch_embed(const uint8_t *emb_raw, int quant, int64_t hidden, int64_t vocab, const uint32_t *tokens,
+                  int64_t m, float *out, int *err_flag, int pdl, cudaStream_t s);
+// Greedy argmax over logits (lowest index wins ties); writes next token and
+// advances the device position.
+void launch_argmax(const float *logits, int64_t n, float *part_val, int *part_idx, unsigned *cnt, int n_blocks,
+                   uint32_t *token_out, int64_t *d_pos, uint32_t *hist, int pdl, cudaStream_t s);
+
+}  // namespace jal

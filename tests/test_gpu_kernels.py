@@ -1,0 +1,201 @@
+"""Device kernels against the oracle (needs a B200).
+
+Bars: repack, activation quantizers and 16-element integer partials are
+bit-exact; f32 outputs within max|y - y_ref| / max|y_ref| <= 1e-3 (REL_TOL).
+Inputs are seeded synthetic tensors with the shapes of the quant-GEMV op
+sweep (M x K in {4096x4096, 11008x4096, 4096x11008, 14336x4096}).
+"""
+import math
+
+import numpy as np
+import pytest
+
+import ref_fixtures as fx
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-3
+SWEEP = [(4096, 4096), (11008, 4096), (4096, 11008), (14336, 4096)]
+
+
+def rel_err(got, ref):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
+@pytest.mark.parametrize("rows,cols", SWEEP)
+def test_repack_bit_exact_and_gemv_op_sweep(jal, oracle, torch_cuda, quant_name, rows, cols):
+    torch = torch_cuda
+    quant = getattr(jal, quant_name)
+    raw = jal.synth_matrix(quant, rows, cols, seed=1234, name=f"sweep.{rows}x{cols}")
+    mat = jal.CachedMatrix.repack(raw, quant, rows, cols)
+    assert mat.rows() == rows and mat.cols() == cols
+    # 4.5 / 8.5 bits per weight in HBM (GGUF bytes, scales padded per row to 16 B)
+    assert mat.aligned_bytes() >= raw.nbytes and mat.aligned_bytes() <= raw.nbytes * 1.01
+    ref = oracle.RepackedWeight(raw, quant, rows, cols)
+    tiles, scales = mat.export_ref_layout()
+    assert np.array_equal(tiles, ref.tiles())
+    assert np.array_equal(scales.view(np.uint32), ref.scales().view(np.uint32))
+    x = jal.synth_normal(cols, seed=99, name="sweep.act")
+    y = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    mat.gemm(dev(torch, x), 1, y)
+    torch.cuda.synchronize()
+    want = ref.project_batch(x, 1)[0]
+    assert rel_err(y.cpu().numpy(), want) <= REL_TOL
+
+
+@pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
+def test_dot16_partials_exact(jal, oracle, torch_cuda, quant_name):
+    torch = torch_cuda
+    quant = getattr(jal, quant_name)
+    rows, cols = 200, 4096
+    raw = jal.synth_matrix(quant, rows, cols, seed=5, name="partials")
+    mat = jal.CachedMatrix.repack(raw, quant, rows, cols)
+    ref = oracle.RepackedWeight(raw, quant, rows, cols)
+    x = jal.synth_normal(cols, seed=6, name="partials.act")
+    q8, _ = oracle.quantize_act_rows(x, 1, cols)
+    out = torch.zeros((rows - 17) * (cols // 16), dtype=torch.int32, device="cuda")
+    mat.dot16_partials(dev(torch, q8[0]), 17, rows, out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().reshape(rows - 17, -1), ref.dot16_partials(q8[0], 17, rows))
+
+
+def test_act_quantizer_bit_exact(jal, oracle, torch_cuda):
+    torch = torch_cuda
+    m, k = 5, 4096 + 96
+    x = jal.synth_normal(m * k, seed=3, name="act.q").reshape(m, k)
+    x[1, 40:72] = 0.0
+    x[2, 3] = np.inf
+    x[2, 7] = np.nan
+    x[3, 100:132] *= 1e-30
+    q = torch.zeros(m * k, dtype=torch.int8, device="cuda")
+    s = torch.zeros(m * (k // 32), dtype=torch.float32, device="cuda")
+    jal.act_quantize_q8(dev(torch, x), m, k, q, s)
+    torch.cuda.synchronize()
+    rq, rs = oracle.quantize_act_rows(x.ravel(), m, k)
+    assert np.array_equal(q.cpu().numpy().reshape(m, k), rq)
+    assert np.array_equal(s.cpu().numpy().reshape(m, -1).view(np.uint32), rs.view(np.uint32))
+
+
+def test_quantize_row_q8_0_bit_exact(jal, oracle, torch_cuda):
+    torch = torch_cuda
+    n = 4096
+    x = jal.synth_normal(n, seed=4, name="q80")
+    x[64:96] = 0.0
+    x[5] = np.nan
+    blocks = torch.zeros(n // 32 * 36, dtype=torch.uint8, device="cuda")
+    jal.quantize_row_q8_0(dev(torch, x), n, blocks)
+    torch.cuda.synchronize()
+    assert np.array_equal(blocks.cpu().numpy(), oracle.quantize_row_q8_0(x))
+
+
+@pytest.mark.parametrize("m", [2, 3, 4, 8, 37])
+@pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
+def test_small_batch_gemv_and_gemm(jal, oracle, torch_cuda, m, quant_name):
+    torch = torch_cuda
+    quant = getattr(jal, quant_name)
+    rows, cols = 1000, 2048
+    raw = jal.synth_matrix(quant, rows, cols, seed=8, name="batch")
+    mat = jal.CachedMatrix.repack(raw, quant, rows, cols)
+    x = jal.synth_normal(m * cols, seed=9, name="batch.act")
+    y = torch.zeros(m * rows, dtype=torch.float32, device="cuda")
+    mat.gemm(dev(torch, x), m, y)
+    torch.cuda.synchronize()
+    want = oracle.RepackedWeight(raw, quant, rows, cols).project_batch(x, m)
+    got = y.cpu().numpy().reshape(m, rows)
+    for t in range(m):
+        assert rel_err(got[t], want[t]) <= REL_TOL
+
+
+@pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
+def test_wave2_shapes_vs_compute_row_dot(jal, oracle, torch_cuda, quant_name):
+    # tests/repack_wave2_parity.rs:182-236 on the device (rows 73, cols 256, m 3)
+    torch = torch_cuda
+    quant = getattr(jal, quant_name)
+    rows, cols, m = 73, 256, 3
+    raw = fx.fill_quant_bytes(rows, cols, quant, 2)
+    act = fx.wave2_activation(m, cols)
+    mat = jal.CachedMatrix.repack(raw, quant, rows, cols)
+    y = torch.zeros(m * rows, dtype=torch.float32, device="cuda")
+    mat.gemm(dev(torch, act), m, y)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy().reshape(m, rows)
+    want = oracle.RepackedWeight(raw, quant, rows, cols).project_batch(act, m)
+    for t in range(m):
+        x = act[t * cols:(t + 1) * cols]
+        bound = max(float(np.sqrt(np.sum(x * x))) * math.sqrt(cols), 1.0)
+        for r in range(rows):
+            exp = oracle.compute_row_dot(r, cols, quant, raw, x)
+            assert abs(got[t, r] - exp) / max(bound, abs(exp)) < 1e-2
+        assert rel_err(got[t], want[t]) <= REL_TOL
+
+
+@pytest.mark.parametrize("quant_name", ["Q4_0", "Q5_0", "Q8_0"])
+def test_streaming_raw_gemv_decode_projection(jal, oracle, torch_cuda, quant_name):
+    # gemv_decode_projection (decode_gemv.rs:1289-1388) for a 4096-column head
+    torch = torch_cuda
+    quant = getattr(jal, quant_name)
+    rows, cols = 3000, 4096
+    if quant == jal.Q5_0:
+        raw = fx.fill_q4_0_or_q5_0(rows, cols, 6, 4)
+    else:
+        raw = jal.synth_matrix(quant, rows, cols, seed=10, name="head")
+    x = jal.synth_normal(cols, seed=11, name="head.act")
+    y = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    jal.gemv_decode_projection(dev(torch, raw), raw.nbytes, quant, rows, cols, dev(torch, x), y)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.gemv_decode_projection(raw, quant, rows, cols, x)) <= REL_TOL
+
+
+def test_unsupported_quant_fails_closed(jal, torch_cuda):
+    with pytest.raises(jal.CapabilityMismatch):
+        jal.CachedMatrix.repack(np.zeros(84, np.uint8), 10, 1, 256)
+    with pytest.raises(jal.TensorBoundsError):
+        jal.CachedMatrix.repack(np.zeros(10, np.uint8), jal.Q4_0, 1, 256)
+
+
+def test_ops_rmsnorm_rope_swiglu_attention(jal, oracle, torch_cuda):
+    torch = torch_cuda
+    n = 4096
+    x = jal.synth_normal(3 * n, seed=21, name="ops.x")
+    w = (1.0 + 0.1 * jal.synth_normal(n, seed=22, name="ops.w")).astype(np.float32)
+    out = torch.zeros(3 * n, dtype=torch.float32, device="cuda")
+    jal.rmsnorm(dev(torch, x), dev(torch, w), 3, n, 1e-5, out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(3, n)
+    for t in range(3):
+        assert rel_err(got[t], oracle.rmsnorm_row(x[t * n:(t + 1) * n], w, 1e-5)) <= 1e-5
+    # RoPE: 4 rows, 8 heads of 128 at positions 5..8, Norm and NeoX
+    inv = oracle.fill_inv_freq(128, 500000.0, 16)
+    for neox in (False, True):
+        qk = jal.synth_normal(4 * 1024, seed=23, name="ops.qk")
+        d = dev(torch, qk)
+        jal.rope(d, 4, 1024, 128, 128, neox, 5, dev(torch, inv))
+        torch.cuda.synchronize()
+        want = np.concatenate([oracle.apply_rope(qk[t * 1024:(t + 1) * 1024], 128, 128, neox, 5 + t, inv)
+                               for t in range(4)])
+        assert rel_err(d.cpu().numpy(), want) <= 1e-5
+    g = jal.synth_normal(n, seed=24, name="ops.g", std=4.0)
+    g[:4] = [25.0, -25.0, 20.0, -20.0]
+    u = jal.synth_normal(n, seed=25, name="ops.u")
+    o = torch.zeros(n, dtype=torch.float32, device="cuda")
+    jal.swiglu(dev(torch, g), dev(torch, u), n, o)
+    torch.cuda.synchronize()
+    assert rel_err(o.cpu().numpy(), oracle.swiglu(g, u)) <= 1e-6
+    # GQA attention: 5 queries at start_pos 11 over 16 positions, 8/2 heads, hd 64, window 0 and 6
+    nq, nkv, hd, total, m, sp = 8, 2, 64, 16, 5, 11
+    q = jal.synth_normal(m * nq * hd, seed=26, name="att.q")
+    k = jal.synth_normal(total * nkv * hd, seed=27, name="att.k")
+    v = jal.synth_normal(total * nkv * hd, seed=28, name="att.v")
+    for window in (0, 6):
+        o = torch.zeros(m * nq * hd, dtype=torch.float32, device="cuda")
+        jal.gqa_attention(dev(torch, q), dev(torch, k), dev(torch, v), m, nq, nkv, hd, total, sp, window, 0.125, o)
+        torch.cuda.synchronize()
+        want = oracle.gqa_attention(q, k, v, m, nq, nkv, hd, total, sp, window, 0.125)
+        assert rel_err(o.cpu().numpy(), want) <= 1e-5

@@ -1,0 +1,159 @@
+"""End-to-end decode / prefill on the device against the oracle (needs a B200).
+
+The tiny Llama workload: 4 layers, dim 512, 8/2 heads, head_dim 64, FFN 1376,
+vocab 4096, Q4_0 layer weights, Q8_0 embedding and head, RoPE theta 1e4; a
+16-token prompt uniform in [0, 4096) and 64 greedy decode steps.  Bars: every
+step's logits within LOGIT_ATOL of the oracle's and an identical greedy
+token sequence.
+"""
+import numpy as np
+import pytest
+
+import gguf_py
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_ATOL = 1e-2
+N_DECODE = 64
+
+
+def geom_of(spec, neox=False):
+    return dict(num_layers=spec.num_layers, hidden_dim=spec.hidden_dim, ffn_dim=spec.ffn_dim,
+                n_heads_q=spec.n_heads_q, n_heads_kv=spec.n_heads_kv, head_dim=spec.head_dim,
+                vocab_size=spec.vocab_size, rms_eps=spec.rms_eps, rope_theta=spec.rope_theta, neox=neox)
+
+
+def make(jal, oracle, spec, seed, neox=False, kv_dtype=None, n_ctx=256, recipe_hook=None, oracle_kwargs=None,
+         sliding_window=0):
+    buf = jal.synth_gguf(spec, seed)
+    _, tensors = gguf_py.parse(buf)
+    om = oracle.Model(tensors, geom_of(spec, neox), nthreads=8, sliding_window=sliding_window,
+                      **(oracle_kwargs or {}))
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    if recipe_hook:
+        recipe_hook(recipe)
+    cache = recipe.build_repack_cache(buf)
+    ctx = jal.ExecutionContext(recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F32 if kv_dtype is None else kv_dtype,
+                               sliding_window=sliding_window)
+    return buf, om, recipe, cache, ctx
+
+
+def prompt_of(seed, n=16, vocab=4096):
+    return np.random.Generator(np.random.PCG64(seed)).integers(0, vocab, n).astype(np.uint32)
+
+
+def run_parity(om, ctx, prompt, n_decode, cap, atol=LOGIT_ATOL):
+    kvo = om.new_kv(cap)
+    lo = om.prefill(kvo, cap, prompt, 0)
+    lg = ctx.prefill_step(prompt, 0)
+    assert np.max(np.abs(lo - lg)) <= atol
+    tokens = []
+    tok = int(np.argmax(lo))
+    assert tok == int(np.argmax(lg))
+    worst = float(np.max(np.abs(lo - lg)))
+    for step in range(n_decode):
+        tokens.append(tok)
+        lo = om.decode(kvo, cap, tok, len(prompt) + step)
+        lg = ctx.decode_step(tok)
+        worst = max(worst, float(np.max(np.abs(lo - lg))))
+        assert np.max(np.abs(lo - lg)) <= atol, f"step {step}"
+        to, tg = int(np.argmax(lo)), int(np.argmax(lg))
+        assert to == tg, f"greedy token differs at step {step}: oracle {to} device {tg}"
+        tok = to
+    return tokens, kvo, worst
+
+
+def test_tiny_llama_greedy_64_matches_oracle_f32_kv(jal, oracle, torch_cuda):
+    spec = jal.TINY_LLAMA
+    buf, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2024)
+    assert cache.num_layers() == 4 and cache.vocab_size() == 4096
+    assert cache.norm_count() == 9 and cache.bias_count() == 0 and cache.repacked_matrix_count() == 29
+    prompt = prompt_of(7)
+    tokens, kvo, worst = run_parity(om, ctx, prompt, N_DECODE, 256)
+    print(f"tiny llama f32-KV worst |dlogit| = {worst:.3e}")
+    # KV cache agrees with the reference layout [layer][K|V][pos][kv_dim]
+    n_pos = len(prompt) + N_DECODE
+    kvg = ctx.export_kv(n_pos, spec.num_layers, spec.n_heads_kv * spec.head_dim)
+    kvr = kvo.reshape(spec.num_layers, 2, 256, -1)[:, :, :n_pos, :].ravel()
+    assert np.max(np.abs(kvg - kvr)) / np.max(np.abs(kvr)) <= 1e-3
+    # The on-device greedy loop (CUDA graph, argmax on device) yields the same ids.
+    ctx2 = jal.ExecutionContext(recipe, cache, n_ctx=256, kv_dtype=jal.KV_F32)
+    l0 = ctx2.prefill_step(prompt, 0)
+    first = int(np.argmax(l0))
+    seq = ctx2.decode_greedy(first, N_DECODE)
+    assert [first] + [int(t) for t in seq[:-1]] == tokens
+    assert ctx2.position() == len(prompt) + N_DECODE
+    assert ctx2.launches_per_step() == 1 + 5 * spec.num_layers + 2
+
+
+def test_tiny_llama_greedy_fp16_paged_kv(jal, oracle, torch_cuda):
+    spec = jal.TINY_LLAMA
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2024, kv_dtype=jal.KV_F16)
+    _, _, worst = run_parity(om, ctx, prompt_of(7), N_DECODE, 256)
+    print(f"tiny llama fp16-KV worst |dlogit| = {worst:.3e}")
+
+
+def test_tiny_qwen2_neox_bias_q8_0(jal, oracle, torch_cuda):
+    spec = jal.SynthSpec(architecture="qwen2", weight_quant=jal.Q8_0, qkv_bias=True, rope_theta=1e6, rms_eps=1e-6,
+                         head_quant=-1)
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=77, neox=True)
+    assert recipe.fields().rope_type == jal.ROPE_NEOX and cache.bias_count() == 3 * spec.num_layers
+    run_parity(om, ctx, prompt_of(9), 24, 256)
+
+
+def test_llama4_irope_and_sliding_window(jal, oracle, torch_cuda):
+    spec = jal.SynthSpec(architecture="llama4", num_layers=4)
+    mask = [False, True, False, True]
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=5, recipe_hook=lambda r: r.with_irope_mask(mask),
+                                     oracle_kwargs=dict(skip_rope=np.array(mask, np.uint8)), sliding_window=8)
+    run_parity(om, ctx, prompt_of(3, n=12), 12, 256)
+
+
+def test_llama3_smooth_scaling_model(jal, oracle, torch_cuda):
+    spec = jal.TINY_LLAMA
+
+    def hook(r):
+        f = r.fields()
+        f.rope_scaling_kind, f.rope_factor, f.rope_low_freq_factor, f.rope_high_freq_factor = 2, 8.0, 1.0, 4.0
+        f.rope_original_max_position_embeddings = 64
+        r.set_fields(f)
+
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=6, recipe_hook=hook,
+                                     oracle_kwargs=dict(scaling=dict(kind=2, factor=8.0, low=1.0, high=4.0, orig=64)))
+    run_parity(om, ctx, prompt_of(4), 8, 256)
+
+
+def test_batched_prefill_equals_sequential_and_chunked(jal, oracle, torch_cuda):
+    # tests/batched_prefill_wave3.rs:398-637 on the device
+    spec = jal.TINY_LLAMA
+    buf, om, recipe, cache, ctx = make(jal, oracle, spec, seed=31)
+    prompt = prompt_of(5, n=20)
+    la = ctx.prefill_step(prompt, 0)
+    ctx_b = jal.ExecutionContext(recipe, cache, n_ctx=256, kv_dtype=jal.KV_F32)
+    ctx_b.prefill_step(prompt[:1], 0, compute_logits=False)
+    lb = None
+    for t in prompt[1:]:
+        lb = ctx_b.decode_step(int(t))
+    assert np.max(np.abs(la - lb)) <= 1e-3
+    ctx_c = jal.ExecutionContext(recipe, cache, n_ctx=256, kv_dtype=jal.KV_F32)
+    ctx_c.prefill_step(prompt[:7], 0, compute_logits=False)
+    lc = ctx_c.prefill_step(prompt[7:], 7)
+    assert np.max(np.abs(la - lc)) <= 1e-3
+    assert ctx_c.position() == 20
+
+
+def test_fail_closed_errors_keep_position(jal, oracle, torch_cuda):
+    # lib.rs:783-871, 963-1036: fail closed without advancing the position
+    spec = jal.TINY_LLAMA
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2, n_ctx=20)
+    ctx.prefill_step(prompt_of(1, n=19), 0)
+    with pytest.raises(jal.TensorBoundsError):
+        ctx.decode_step(4096)
+    assert ctx.position() == 19
+    ctx.decode_step(3)
+    assert ctx.position() == 20
+    with pytest.raises(jal.ContextLengthExceeded):
+        ctx.decode_step(3)
+    assert ctx.position() == 20
+    with pytest.raises(jal.ContextLengthExceeded):
+        ctx.prefill_step(prompt_of(1, n=21), 0)

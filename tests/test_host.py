@@ -1,0 +1,213 @@
+"""CPU tests of the host side: the C ABI surface, the GGUF writer/reader, the
+seeded generator, recipe hydration (recipe.rs) and fail-closed validation.
+Each test names the reference test it restates."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+import gguf_py
+from conftest import REPO
+
+
+def header_functions():
+    names = []
+    for h in ("jal.h", "jal_synth.h"):
+        src = open(os.path.join(REPO, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        names += re.findall(r"\b(jal_[a-z0-9_]+)\s*\(", src)
+    return sorted(set(names))
+
+
+def test_library_loads_and_exports_every_declared_symbol(jal):
+    lib = jal.lib()
+    missing = [n for n in header_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    assert "sm_100a" in jal.version()
+    assert len(header_functions()) >= 60
+
+
+def test_synth_gguf_deterministic_and_parseable(jal):
+    spec = jal.SynthSpec(num_layers=1, hidden_dim=128, ffn_dim=256, n_heads_q=4, n_heads_kv=2, head_dim=32,
+                         vocab_size=64)
+    a = jal.synth_gguf(spec, seed=7, nthreads=1)
+    b = jal.synth_gguf(spec, seed=7, nthreads=4)
+    c = jal.synth_gguf(spec, seed=8, nthreads=4)
+    assert np.array_equal(a, b)
+    assert not np.array_equal(a, c)
+    kv, t = gguf_py.parse(a)
+    assert kv["general.architecture"] == "llama" and kv["llama.block_count"] == 1
+    assert t["blk.0.attn_q.weight"].dims == [128, 128] and t["blk.0.attn_q.weight"].qtype == jal.Q4_0
+    assert t["blk.0.attn_k.weight"].dims == [128, 64]
+    assert t["token_embd.weight"].qtype == jal.Q8_0 and t["output.weight"].dims == [128, 64]
+    assert np.all(t["blk.0.attn_norm.weight"].data.view(np.float32) == 1.0)
+
+
+def test_synth_weights_are_normal_0_02(jal, oracle):
+    raw = jal.synth_matrix(jal.Q8_0, 256, 1024, seed=3, name="probe", std=0.02)
+    vals = np.concatenate([oracle.dequantize_block(8, raw[i * 34:(i + 1) * 34]) for i in range(raw.size // 34)])
+    assert abs(float(vals.mean())) < 2e-4
+    assert abs(float(vals.std()) - 0.02) < 4e-4
+    x = jal.synth_normal(1 << 16, seed=1, name="act")
+    assert abs(float(x.std()) - 1.0) < 0.02 and abs(float(x.mean())) < 0.02
+
+
+def test_f16_rounding_is_nearest_even(jal):
+    for v in [1.0, 0.5, 1e-3, 65504.0, 7e-8, 3.0517578125e-05, 1.0009765625, 1.00048828125, -2.5]:
+        want = int(np.array([v], dtype=np.float32).astype(np.float16).view(np.uint16)[0])
+        assert jal.f32_to_f16_bits(v) == want, v
+
+
+@pytest.mark.parametrize("case", [
+    ("qwen2", 896, 4864, 14, 2, 64, 151_936, 24, None, 1),
+    ("qwen2", 1536, 8960, 12, 2, 128, 151_936, 28, None, 1),
+    ("llama", 3072, 8192, 24, 8, 128, 128_256, 28, 64, 0),
+    ("llama4", 5120, 16384, 40, 8, 128, 202_048, 48, 96, 0),
+])
+def test_recipe_from_metadata_non_8b_scales(jal, case):
+    # lib.rs:389-487 test_from_metadata_non_8b_scales_and_rotary_dim
+    arch, hidden, ffn, hq, hkv, hd, vocab, layers, rot, rope = case
+    kvs = [("general.architecture", arch), (f"{arch}.block_count", layers), (f"{arch}.embedding_length", hidden),
+           (f"{arch}.feed_forward_length", ffn), (f"{arch}.attention.head_count", hq),
+           (f"{arch}.attention.head_count_kv", hkv), (f"{arch}.attention.key_length", hd),
+           (f"{arch}.vocab_size", vocab), (f"{arch}.attention.layer_norm_rms_epsilon", 1e-6),
+           (f"{arch}.rope.freq_base", 10000.0)]
+    if rot is not None:
+        kvs.append((f"{arch}.rope.dimension_count", rot))
+    r = jal.LlamaRecipe.from_gguf(gguf_py.write(kvs, []))
+    assert r.architecture_id() == arch
+    f = r.fields()
+    assert (f.hidden_dim, f.ffn_dim, f.n_heads_q, f.n_heads_kv, f.head_dim, f.vocab_size, f.num_layers) == \
+        (hidden, ffn, hq, hkv, hd, vocab, layers)
+    assert f.rope_type == rope
+    assert r.effective_rotary_dim() == (rot if rot is not None else hd)
+
+
+def test_llama3_smooth_rope_scaling_from_gguf(jal):
+    # lib.rs:554-633
+    kvs = [("general.architecture", "llama"), ("llama.context_length", 131_072), ("llama.attention.key_length", 128),
+           ("llama.rope.freq_base", 500000.0), ("llama.rope.scaling.type", "llama3"),
+           ("llama.rope.scaling.factor", 8.0), ("llama.rope.scaling.low_freq_factor", 1.0),
+           ("llama.rope.scaling.high_freq_factor", 4.0), ("llama.rope.scaling.original_context_length", 8192)]
+    f = jal.LlamaRecipe.from_gguf(gguf_py.write(kvs, [])).fields()
+    assert f.rope_scaling_kind == jal.ROPE_SCALING_LLAMA3
+    assert (f.rope_factor, f.rope_low_freq_factor, f.rope_high_freq_factor) == (8.0, 1.0, 4.0)
+    assert f.rope_original_max_position_embeddings == 8192
+    kvs32 = [("general.architecture", "llama"), ("llama.rope.scaling.type", "llama3"),
+             ("llama.rope.scaling.factor", 32.0), ("llama.rope.scaling.orig_ctx_len", 4096)]
+    f = jal.LlamaRecipe.from_gguf(gguf_py.write(kvs32, [])).fields()
+    assert (f.rope_scaling_kind, f.rope_factor, f.rope_low_freq_factor, f.rope_high_freq_factor) == (2, 32.0, 1.0, 4.0)
+    assert f.rope_original_max_position_embeddings == 4096
+    kvsf = [("general.architecture", "llama"), ("llama.rope.scaling.factors", ("f32[]", [1.5, 2.5]))]
+    f = jal.LlamaRecipe.from_gguf(gguf_py.write(kvsf, [])).fields()
+    assert f.rope_scaling_kind == jal.ROPE_SCALING_LONGROPE
+    bad = [("general.architecture", "llama"), ("llama.rope.scaling.type", "bogus")]
+    with pytest.raises(jal.CapabilityMismatch):
+        jal.LlamaRecipe.from_gguf(gguf_py.write(bad, []))
+
+
+def test_recipe_capabilities_and_irope(jal):
+    # lib.rs:71-105
+    r = jal.LlamaRecipe.new()
+    assert r.architecture_id() == "llama"
+    for q in (jal.Q4_K, jal.Q5_K, jal.Q5_0, jal.Q8_0, jal.Q4_0, jal.Q6_K, jal.F32, jal.F16, jal.BF16):
+        assert r.supports_quant(q)
+    assert not r.supports_quant(jal.TQ1_0) and not r.supports_quant(10)
+    q = jal.LlamaRecipe.new_qwen2()
+    assert q.architecture_id() == "qwen2" and abs(q.rms_eps - 1e-6) < 1e-10 and abs(q.rope_theta - 1e6) < 1.0
+    l4 = jal.LlamaRecipe.new_llama4().with_irope_mask([False, True, False, True])
+    assert l4.architecture_id() == "llama4"
+    assert [l4.should_skip_rope(i) for i in (0, 1, 2, 3, 10)] == [False, True, False, True, False]
+    kvs = [("general.architecture", "llama4"), ("llama4.block_count", 8), ("llama4.attention.no_rope_layer_step", 4)]
+    r4 = jal.LlamaRecipe.from_gguf(gguf_py.write(kvs, []))
+    assert [r4.should_skip_rope(i) for i in range(8)] == [False, False, False, True, False, False, False, True]
+
+
+def compact_arch_gguf(arch, omit=None, extra=(), fill=None):
+    """lib.rs:326-387 build_compact_arch_gguf (hidden 16, ffn 24, 2/1 heads, hd 8, vocab 12, F32)."""
+    hidden, ffn, nq, nkv, hd, vocab = 16, 24, 2, 1, 8, 12
+    kvs = [("general.architecture", arch), (f"{arch}.block_count", 1), (f"{arch}.embedding_length", 16),
+           (f"{arch}.feed_forward_length", 24), (f"{arch}.attention.head_count", 2),
+           (f"{arch}.attention.head_count_kv", 1), (f"{arch}.attention.key_length", 8),
+           (f"{arch}.attention.layer_norm_rms_epsilon", 1e-5), (f"{arch}.rope.freq_base", 10000.0),
+           (f"{arch}.context_length", 16)] + list(extra)
+    specs = [("token_embd.weight", [hidden, vocab]), ("blk.0.attn_norm.weight", [hidden]),
+             ("blk.0.attn_q.weight", [hidden, nq * hd]), ("blk.0.attn_k.weight", [hidden, nkv * hd]),
+             ("blk.0.attn_v.weight", [hidden, nkv * hd]), ("blk.0.attn_output.weight", [nq * hd, hidden]),
+             ("blk.0.ffn_norm.weight", [hidden]), ("blk.0.ffn_gate.weight", [hidden, ffn]),
+             ("blk.0.ffn_up.weight", [hidden, ffn]), ("blk.0.ffn_down.weight", [ffn, hidden]),
+             ("output_norm.weight", [hidden]), ("output.weight", [hidden, vocab])]
+    ts = []
+    for idx, (n, d) in enumerate(specs):
+        if n == omit:
+            continue
+        payload = fill(idx, n, d) if fill else None
+        ts.append((n, 0, d, payload))
+    return gguf_py.write(kvs, ts)
+
+
+@pytest.mark.parametrize("omit", ["blk.0.attn_k.weight", "blk.0.ffn_gate.weight", "output_norm.weight"])
+def test_validate_model_rejects_missing_tensors(jal, omit):
+    # lib.rs:783-808
+    g = compact_arch_gguf("llama", omit=omit)
+    r = jal.LlamaRecipe.from_gguf(g)
+    with pytest.raises(jal.K3Error):
+        r.validate_model(g)
+
+
+def test_validate_model_arch_rotary_and_quant(jal):
+    # lib.rs:810-856
+    g = compact_arch_gguf("llama")
+    r = jal.LlamaRecipe.from_gguf(g)
+    r.validate_model(g)
+    with pytest.raises(jal.CapabilityMismatch):
+        r.validate_model(compact_arch_gguf("gpt2"))
+    r.with_rotary_dim(6).validate_model(g)
+    with pytest.raises(jal.CapabilityMismatch):
+        jal.LlamaRecipe.from_gguf(g).with_rotary_dim(5).validate_model(g)
+    q2k = gguf_py.write([("general.architecture", "llama")], [("blk.0.attn_q.weight", 10, [256, 1], None)])
+    with pytest.raises(jal.CapabilityMismatch):
+        jal.LlamaRecipe.from_gguf(g).validate_model(q2k)
+    with pytest.raises(jal.CapabilityMismatch):
+        jal.LlamaRecipe.from_gguf(compact_arch_gguf("gpt2"))
+
+
+TINY = dict(num_layers=2, hidden_dim=128, ffn_dim=352, n_heads_q=4, n_heads_kv=2, head_dim=32, vocab_size=256,
+            rms_eps=1e-5, rope_theta=10000.0)
+
+
+def tiny_oracle_model(jal, oracle, seed=11, **over):
+    spec = jal.SynthSpec(**{**TINY, **{k: v for k, v in over.items() if k in jal.SynthSpec.__dataclass_fields__}})
+    buf = jal.synth_gguf(spec, seed)
+    _, tensors = gguf_py.parse(buf)
+    geom = dict(TINY, neox=over.get("neox", False))
+    return oracle.Model(tensors, geom, nthreads=2), buf
+
+
+def test_oracle_batched_prefill_equals_sequential_decode(jal, oracle):
+    # lib.rs:205-324 and tests/batched_prefill_wave3.rs:398-471: batched prefill
+    # of [1, 3, 5] == prefill [1] + decode 3 + decode 5 (bit-exact in the oracle).
+    m, _ = tiny_oracle_model(jal, oracle)
+    cap = 16
+    kv_a = m.new_kv(cap)
+    la = m.prefill(kv_a, cap, [1, 3, 5], 0)
+    kv_b = m.new_kv(cap)
+    m.prefill(kv_b, cap, [1], 0)
+    m.decode(kv_b, cap, 3, 1)
+    lb = m.decode(kv_b, cap, 5, 2)
+    assert np.array_equal(la, lb)
+    assert np.array_equal(kv_a, kv_b)
+
+
+def test_oracle_chunked_prefill_equals_single_shot(jal, oracle):
+    # tests/batched_prefill_wave3.rs:473-637 / lib.rs:873-961
+    m, _ = tiny_oracle_model(jal, oracle, seed=5)
+    cap = 16
+    prompt = [7, 2, 9, 4, 4, 1, 0, 200]
+    kv_a = m.new_kv(cap)
+    la = m.prefill(kv_a, cap, prompt, 0)
+    kv_b = m.new_kv(cap)
+    m.prefill(kv_b, cap, prompt[:3], 0, compute_logits=False)
+    lb = m.prefill(kv_b, cap, prompt[3:], 3)
+    assert np.array_equal(la, lb) and np.array_equal(kv_a, kv_b)
