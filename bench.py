@@ -125,7 +125,8 @@ def ev_time(torch, fn, stream):
 
 def gemv_sweep(jal, torch, peak, quants, iters=200):
     """Op sweep: M x K quant GEMV, rotating weight copies (> 4x L2) so each
-    launch streams from HBM."""
+    launch streams from HBM.  The launches are captured in a CUDA graph so
+    the timing is the kernels', not the host's launch rate."""
     stream = torch.cuda.current_stream()
     res = []
     for qname in quants:
@@ -143,11 +144,13 @@ def gemv_sweep(jal, torch, peak, quants, iters=200):
             for i in range(2 * copies):
                 mats[i % copies].gemv_q8(q8, sc, y, stream)
 
-            def run():
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
                 for i in range(iters):
                     mats[i % copies].gemv_q8(q8, sc, y, stream)
-
-            t = ev_time(torch, run, stream) / iters
+            graph.replay()
+            t = ev_time(torch, graph.replay, stream) / iters
+            del graph
             alg = rows * cols // 32 * bpb + 4 * cols + 4 * rows
             res.append({"quant": qname, "M": rows, "K": cols, "us": round(t * 1e6, 3),
                         "GBps": round(alg / t / 1e9, 1), "frac_of_peak": round(alg / t / 1e9 / peak, 4),
@@ -259,7 +262,8 @@ def main():
     n_prefill = min(args.prefill, spec.context_length - args.warmup - args.steps - 8)
     n_ctx = n_prefill + 2 * (args.warmup + args.steps) + 16
     ctx = jal.ExecutionContext(recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F16)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # a capturable stream: decode steps replay a CUDA graph on it
+    torch.cuda.set_stream(stream)
     ctx.set_stream(stream)
     rng = np.random.Generator(np.random.PCG64(SEED + rank))
     prompt = rng.integers(0, spec.vocab_size, n_prefill).astype(np.uint32)

@@ -252,8 +252,8 @@ class CachedMatrix:
         return cls(out.value)
 
     def __del__(self):
-        if getattr(self, "_owned", False) and self._h:
-            lib().jal_cached_matrix_free(self._h)
+        if getattr(self, "_owned", False) and self._h and _lib is not None:
+            _lib.jal_cached_matrix_free(self._h)
             self._h = None
 
     @property
@@ -359,8 +359,8 @@ class LlamaRecipe:
         return cls(out.value)
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib().jal_recipe_free(self._h)
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.jal_recipe_free(self._h)
             self._h = None
 
     @property
@@ -459,8 +459,8 @@ class ModelRepackCache:
         self._h = handle
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib().jal_model_repack_cache_free(self._h)
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.jal_model_repack_cache_free(self._h)
             self._h = None
 
     @property
@@ -499,8 +499,8 @@ class ExecutionContext:
         self.vocab = cache.vocab_size()
 
     def __del__(self):
-        if getattr(self, "_h", None):
-            lib().jal_context_free(self._h)
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.jal_context_free(self._h)
             self._h = None
 
     @property

@@ -1,17 +1,19 @@
 // Attention kernels over the paged KV cache.
 //
-// Decode (one token): split-K ("flash decoding") over the sequence.  Grid
-// (n_kv heads, n_splits); each CTA loads its group of query heads from the
-// QKV projection output, adds the optional biases and applies RoPE, scores
-// its slice of positions, and keeps an online softmax.  The CTA whose slice
-// holds the current position appends the new K/V.  The last CTA of each KV
-// head (atomic counter) merges the split partials, writes the f32 head
-// outputs and quantizes them per 32-block for the output projection.
+// Decode (one token): split-K ("flash decoding") over the sequence with one
+// thread-block cluster per KV head.  Each CTA of the cluster loads the head
+// group's queries from the QKV projection output, adds the optional biases,
+// applies RoPE, scores its slice of positions and keeps an online softmax.
+// The CTA whose slice holds the current position appends the new K/V.  The
+// split partials are merged through distributed shared memory (no global
+// round trip); every rank finalises and quantizes a share of the 32-blocks
+// of the head outputs for the output projection.
 // Math follows gqa_attention_prefill_portable (recipe.rs:2949-3022) up to the
 // order of f32 sums: score = (q . k) * scale, exp(s - max), sum, weighted V.
 //
 // Prefill: RoPE + KV append of m tokens, then a causal flash kernel with f32
 // accumulation.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include "dev_util.cuh"
@@ -25,6 +27,7 @@ namespace {
 constexpr int kAttnThreads = 128;
 constexpr int kSub = 128;  // positions per sub-chunk
 constexpr int kMaxG = 8;   // query heads per KV head
+constexpr int kMaxClusterCtas = 16;  // CTAs per KV head (one cluster)
 
 __device__ __forceinline__ int64_t kv_elem(const KvView &kv, int64_t layer, int64_t h, int64_t pos) {
   int64_t page = kv.page_table[pos / kv.page_size], slot = pos % kv.page_size;
@@ -46,14 +49,19 @@ __device__ __forceinline__ void rot(float &x0, float &x1, float c, float s) {
 
 template <int HD, bool F16>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeArgs a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   __shared__ float q_s[kMaxG][HD];
   __shared__ float kn_s[HD], vn_s[HD];
   __shared__ float p_s[kMaxG][kSub];
   __shared__ float red_s[4][kMaxG];
   __shared__ float alpha_s[kMaxG];
-  __shared__ float acc_s[4][kMaxG][HD];
-  __shared__ unsigned last_s;
-  const int h = blockIdx.x, split = blockIdx.y, tid = threadIdx.x;
+  __shared__ float acc_s[4][kMaxG][HD];  // acc_s[0] holds this CTA's partial after the reduction
+  __shared__ float ml_s[2][kMaxG];       // running max / denominator of this CTA
+  __shared__ float wgt_s[kMaxClusterCtas][kMaxG];
+  __shared__ float den_s[kMaxG];
+  const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
+  const int h = blockIdx.x / cs, tid = threadIdx.x;
   const int warp = tid / 32, lane = tid % 32;
   const int G = (int)(a.n_heads_q / a.kv.n_kv);
   const int64_t Q = a.n_heads_q * HD, KVD = a.kv.n_kv * HD;
@@ -61,8 +69,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
   pdl_wait();
   const int64_t pos = *a.d_pos, seq = pos + 1;
   const int64_t lo = (a.window > 0 && seq > a.window) ? seq - a.window : 0;
-  const int64_t span = seq - lo, per = (span + a.n_splits - 1) / a.n_splits;
-  const int64_t s0 = lo + split * per, s1 = s0 + per < seq ? s0 + per : seq;
+  const int64_t span = seq - lo, per = (span + cs - 1) / cs;
+  const int64_t s0 = lo + rank * per, s1 = s0 + per < seq ? s0 + per : seq;
 
   // q / new k / new v of this head group (+ bias), then RoPE.
   for (int i = tid; i < G * HD; i += kAttnThreads) {
@@ -242,84 +250,94 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
     __syncthreads();
   }
 
-  // Reduce the 4 warps' accumulators and publish this split's partial.
+  // Reduce the 4 warps' accumulators into acc_s[0]: this CTA's partial.
 #pragma unroll
   for (int g = 0; g < kMaxG; g++)
     if (g < G) {
 #pragma unroll
       for (int j = 0; j < DPL; j++) acc_s[warp][g][lane * DPL + j] = acc[g][j];
     }
-  __syncthreads();
-  const int64_t pstride = HD + 2;
-  float *part = a.part + ((int64_t)h * a.n_splits + split) * G * pstride;
-  for (int i = tid; i < G * HD; i += kAttnThreads) {
-    int g = i / HD, d = i % HD;
-    part[g * pstride + 2 + d] = (acc_s[0][g][d] + acc_s[1][g][d]) + (acc_s[2][g][d] + acc_s[3][g][d]);
-  }
   if (tid < G) {
     float mg = -INFINITY, lg = 0.0f;
 #pragma unroll
     for (int g = 0; g < kMaxG; g++)
       if (g == tid) { mg = m_run[g]; lg = l_run[g]; }
-    part[tid * pstride] = mg;
-    part[tid * pstride + 1] = lg;
+    ml_s[0][tid] = mg;
+    ml_s[1][tid] = lg;
   }
-  __threadfence();
   __syncthreads();
-  if (tid == 0) last_s = atomicAdd(&a.split_cnt[h], 1u) == (unsigned)(a.n_splits - 1);
-  __syncthreads();
-  if (!last_s) {
-    pdl_trigger();
-    return;
-  }
-  __threadfence();
-  // Merge splits: out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s.
-  const float *base = a.part + (int64_t)h * a.n_splits * G * pstride;
   for (int i = tid; i < G * HD; i += kAttnThreads) {
     int g = i / HD, d = i % HD;
-    float M = -INFINITY;
-    for (int s = 0; s < a.n_splits; s++) M = fmaxf(M, __ldcg(base + (s * G + g) * pstride));
-    float num = 0.0f, den = 0.0f;
-    for (int s = 0; s < a.n_splits; s++) {
-      const float *ps = base + (s * G + g) * pstride;
-      float ms = __ldcg(ps);
-      if (ms == -INFINITY) continue;
-      float w = expf(ms - M);
-      num = fmaf(w, __ldcg(ps + 2 + d), num);
-      den = fmaf(w, __ldcg(ps + 1), den);
-    }
-    float o = den > 0.0f ? __fdiv_rn(num, den) : 0.0f;
-    q_s[g][d] = o;
-    a.out[(int64_t)(h * G + g) * HD + d] = o;
+    acc_s[0][g][d] = (acc_s[0][g][d] + acc_s[1][g][d]) + (acc_s[2][g][d] + acc_s[3][g][d]);
+  }
+  cluster.sync();
+  // Merge the cluster's partials through distributed shared memory:
+  // out = sum_r e^(m_r - M) acc_r / sum_r e^(m_r - M) l_r.  Every remote
+  // read of a phase is issued independently (one DSMEM round trip each).
+  if (tid < cs * G) {
+    const int r = tid / G, g = tid % G;
+    wgt_s[r][g] = cluster.map_shared_rank(&ml_s[0][0], r)[g];
+    p_s[g][r] = cluster.map_shared_rank(&ml_s[1][0], r)[g];  // l_r, staged in p_s (free now)
   }
   __syncthreads();
-  // QuantizedActQ8 of this head group (head boundaries are 32-block aligned).
-  for (int b = warp; b < G * HD / 32; b += 4) {
-    int g = (b * 32) / HD, d = (b * 32) % HD + lane;
-    float v = q_s[g][d];
-    if (!isfinite(v)) v = 0.0f;
-    float amax = warp_max(fabsf(v));
-    float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
-    int64_t gb = ((int64_t)h * G * HD) / 32 + b;
-    a.out_q[gb * 32 + lane] = act_quant_one(v, inv);
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int r = 0; r < cs; r++) M = fmaxf(M, wgt_s[r][tid]);
+    float den = 0.0f;
+    for (int r = 0; r < cs; r++) {
+      const float mr = wgt_s[r][tid];
+      const float w = mr == -INFINITY ? 0.0f : expf(mr - M);
+      wgt_s[r][tid] = w;
+      den = fmaf(w, p_s[tid][r], den);
+    }
+    den_s[tid] = den;
+  }
+  __syncthreads();
+  // Rank r finalises 32-blocks r, r + cs, ... of this head group and
+  // quantizes them (QuantizedActQ8; head boundaries are 32-aligned).
+  for (int bi = rank + warp * cs; bi < G * HD / 32; bi += 4 * cs) {
+    const int e = bi * 32 + lane, g = e / HD, d = e % HD;
+    float part[kMaxClusterCtas];
+#pragma unroll
+    for (int r = 0; r < kMaxClusterCtas; r++)
+      part[r] = r < cs ? cluster.map_shared_rank(&acc_s[0][0][0], r)[g * HD + d] : 0.0f;
+    float num = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxClusterCtas; r++)
+      if (r < cs) num = fmaf(wgt_s[r][g], part[r], num);
+    float o = den_s[g] > 0.0f ? __fdiv_rn(num, den_s[g]) : 0.0f;
+    a.out[(int64_t)h * G * HD + e] = o;
+    if (!isfinite(o)) o = 0.0f;
+    const float amax = warp_max(fabsf(o));
+    const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
+    const int64_t gb = ((int64_t)h * G * HD) / 32 + bi;
+    a.out_q[gb * 32 + lane] = act_quant_one(o, inv);
     if (lane == 0) a.out_s[gb] = scale;
   }
-  if (tid == 0) a.split_cnt[h] = 0u;
+  // Keep this CTA's shared memory alive until every rank has read it.
+  cluster.sync();
   pdl_trigger();
 }
 
 template <int HD, bool F16>
 void launch_decode_t(const AttnDecodeArgs &a, cudaStream_t s) {
+  auto kern = k_attn_decode<HD, F16>;
+  const int cs = a.n_splits;
+  if (cs > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)a.kv.n_kv, (unsigned)a.n_splits);
+  cfg.gridDim = dim3((unsigned)(a.kv.n_kv * cs));
   cfg.blockDim = dim3(kAttnThreads);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = a.pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, k_attn_decode<HD, F16>, a);
+  cfg.numAttrs = a.pdl ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 // ---- prefill: bias + RoPE + KV append -------------------------------------
@@ -464,6 +482,28 @@ void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s) {
     if (f16) launch_decode_t<64, true>(a, s);
     else launch_decode_t<64, false>(a, s);
   }
+}
+
+int attn_decode_cluster_size(int head_dim, int f16, int want) {
+  for (int cs = want; cs >= 1; cs /= 2) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cs);
+    cfg.blockDim = dim3(kAttnThreads);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const void *kern = head_dim == 128 ? (f16 ? (const void *)k_attn_decode<128, true> : (const void *)k_attn_decode<128, false>)
+                                       : (f16 ? (const void *)k_attn_decode<64, true> : (const void *)k_attn_decode<64, false>);
+    if (cs > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) return cs;
+    cudaGetLastError();
+  }
+  return 1;
 }
 
 void launch_rope_append(const RopeAppendArgs &a, cudaStream_t s) {

@@ -30,8 +30,9 @@ inline int64_t d_stride_for(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
 
 // ---- GEMV (decode, M tokens <= kGemvMaxM) ------------------------------
 enum GemvIn : int { GEMV_IN_Q8 = 0, GEMV_IN_F32 = 1, GEMV_IN_NORM = 2 };
-enum GemvOut : int { GEMV_OUT_STORE = 0, GEMV_OUT_ADD = 1, GEMV_OUT_SWIGLU_Q = 2 };
+enum GemvOut : int { GEMV_OUT_STORE = 0, GEMV_OUT_ADD = 1, GEMV_OUT_SWIGLU = 2 };
 constexpr int kGemvMaxM = 8;
+constexpr int kGemvMaxSmem = 200 * 1024;
 
 struct GemvArgs {
   DevMat w;
@@ -49,15 +50,15 @@ struct GemvArgs {
   int64_t y_stride = 0;
   const float *bias = nullptr;  // per output row (OUT_STORE / OUT_ADD)
   int64_t up_offset = 0;        // SWIGLU: physical row offset of the up half
-  int8_t *yq = nullptr;         // SWIGLU_Q: [m][rows] int8
-  float *ys = nullptr;          // SWIGLU_Q: [m][rows/32] scales
-  unsigned *group_cnt = nullptr;  // SWIGLU_Q: [m][rows/32] zero-initialised
   int grid = 0;                 // CTAs (0 = auto)
   int pdl = 0;                  // launch with programmatic dependent launch
 };
 
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
 int gemv_default_grid(const GemvArgs &a);
+// Sets the kernels' shared-memory limits (call before any stream capture).
+void gemv_init();
+size_t gemv_smem_bytes(int in_mode, int m, int64_t cols);
 
 // ---- repack / export / activation quantizers ---------------------------
 void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, uint8_t *qs, uint16_t *d,
@@ -124,15 +125,15 @@ struct AttnDecodeArgs {
   const int64_t *d_pos = nullptr;  // current position (device)
   int64_t window = 0;
   float scale = 1.f;
-  int n_splits = 1;
-  float *part = nullptr;        // [n_kv][n_splits][G][head_dim + 2]
-  unsigned *split_cnt = nullptr;  // [n_kv], zero-initialised
+  int n_splits = 1;             // CTAs per KV head = thread-block cluster size (<= 16)
   float *out = nullptr;         // [n_heads_q * head_dim]
   int8_t *out_q = nullptr;      // quantized out (QuantizedActQ8)
   float *out_s = nullptr;
   int pdl = 0;
 };
 void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
+// Largest cluster size (<= want) the decode attention kernel can run with.
+int attn_decode_cluster_size(int head_dim, int f16, int want);
 
 // Prefill: bias + RoPE on q/k rows, append k/v of m tokens into the cache.
 struct RopeAppendArgs {

@@ -1,21 +1,31 @@
 // Decode GEMV for the repacked Q4_0 / Q8_0 B200 layout (M <= 8 tokens).
 //
-// Semantics (repack_cache.rs:739-783): for every output row r and 16-element
-// chunk ch, dot16 = sum(a_q8 * w_q) in int32 (exact), and the row value is
-// the f32 sum over chunks of (f32(dot16) * a_sc[ch/2]) * w_sc[ch/2].  Each
-// term is computed with correctly rounded multiplies, so it is bit-identical
-// to the reference's term; only the order of the f32 sum differs (lanes own
-// blocks, then a warp butterfly).
+// Semantics (repack_cache.rs:739-783): the integer block dot of the int8
+// activation with the weight quants is exact (int32), and the row value is
+// the f32 sum over blocks of f32(dot) * a_sc * w_sc.  The two 16-element
+// chunks of a 32-block share both scales, so they are summed in int32 first
+// (exactly the sum of the reference's two dot16 partials); the f32 order of
+// the accumulation differs from the reference's sequential loop.
 //
-// Structure: persistent CTAs of 8 warps; warp w of CTA c owns logical rows
-// gw, gw + nw, ... (gw = c*8 + w, nw = 8*grid).  A row is streamed in chunks
-// of 32*U blocks (lane l loads blocks l, l+32, ... with 16-byte loads that do
-// not allocate in L1), double-buffered in registers.  The first chunk is
-// loaded before griddepcontrol.wait, so weight traffic starts while the
-// previous kernel drains.  The activation prologue (optionally RMSNorm, then
-// the QuantizedActQ8 quantizer) writes per-block int8 halves, the f32 scale
-// and the two 16-element sums into shared memory.
+// Structure: one persistent CTA of WARPS warps per SM; warp w of CTA c owns
+// logical rows gw, gw + nw, ... (gw = c*WARPS + w, nw = WARPS*grid).  A row is
+// streamed in chunks of 32*U blocks (lane l loads blocks l, l+32, ... with
+// 16-byte loads that do not allocate in L1), DEPTH chunks in flight per warp.
+// The first DEPTH chunks are loaded before griddepcontrol.wait, so weight
+// traffic starts while the previous kernel drains.  The activation prologue
+// (optionally RMSNorm, then the QuantizedActQ8 quantizer) writes per-block
+// int8 halves, the f32 scale and the 32-element int sum into shared memory.
+//
+// Per block and token the inner loop is 3 shared loads, 8 LOP3, 8 IDP4A,
+// a shift and two integer adds, one half->float, one I2F, FMUL and FFMA:
+// the high nibbles are masked in place (w & 0xF0F0F0F0) and the product,
+// a multiple of 16, is shifted back; the -8 nibble offset is applied with
+// the activation block sum.  The f16 scales were sanitized at repack time
+// (Inf/NaN -> +-0.0625, the reference's f16_to_f32_finite), so a plain
+// conversion is exact here.
 #include <cuda_fp16.h>
+
+#include <cstdlib>
 
 #include "dev_util.cuh"
 #include "device.hpp"
@@ -25,20 +35,27 @@ namespace jal {
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-
 // Shared-memory activation layout for token t (nbp = nb rounded up to 4):
-//   [lo: nbp x 16 B][hi: nbp x 16 B][scale: nbp x f32][sums: nbp x int2]
-__host__ __device__ inline size_t act_bytes(int nbp) { return (size_t)nbp * 44; }
+//   [lo: nbp x 16 B][hi: nbp x 16 B][scale, sum32: nbp x 8 B]
+// followed, for f32 inputs, by a staging copy of the f32 activations
+// (M x K floats) and, for RMSNorm inputs, the norm weights (K floats).
+__host__ __device__ inline size_t act_bytes(int nbp) { return (size_t)nbp * 40; }
+__host__ __device__ inline size_t smem_bytes(int in_mode, int M, int nb) {
+  const int nbp = (nb + 3) & ~3;
+  size_t b = act_bytes(nbp) * M;
+  if (in_mode != GEMV_IN_Q8) b += (size_t)M * nb * 32 * 4;
+  if (in_mode == GEMV_IN_NORM) b += (size_t)nb * 32 * 4;
+  return b;
+}
 
+template <int WARPS>
 __device__ float block_reduce_sum(float v, float *red) {
   v = warp_sum(v);
   int w = threadIdx.x / 32, l = threadIdx.x % 32;
   if (l == 0) red[w] = v;
   __syncthreads();
   if (w == 0) {
-    float t = l < kWarps ? red[l] : 0.0f;
+    float t = l < WARPS ? red[l] : 0.0f;
     t = warp_sum(t);
     if (l == 0) red[32] = t;
   }
@@ -48,49 +65,88 @@ __device__ float block_reduce_sum(float v, float *red) {
   return r;
 }
 
-template <int M>
+__device__ __forceinline__ void put_scale_sum(char *base, int nbp, int b, float scale, int sum32) {
+  ((float2 *)(base + nbp * 32))[b] = make_float2(scale, __int_as_float(sum32));
+}
+
+// All global reads of the prologue are issued as independent wide loads
+// (one memory latency), then the per-block quantization runs from shared
+// memory.
+template <int M, int WARPS>
 __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, float *red) {
-  float inv_norm[M];
+  constexpr int T = WARPS * 32;
+  const int K = nb * 32, tid = threadIdx.x;
+  const int warp = tid / 32, lane = tid % 32;
+  if (a.in_mode == GEMV_IN_Q8) {
+    for (int i = tid; i < M * nb * 2; i += T) {
+      const int t = i / (2 * nb), j = i % (2 * nb);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (t < a.m) v = *(const uint4 *)(a.xq + t * a.xq_stride + j * 16);
+      char *base = smem + t * act_bytes(nbp) + (j & 1) * nbp * 16;
+      ((uint4 *)base)[j >> 1] = v;
+    }
+    __syncthreads();
+    for (int i = tid; i < M * nb; i += T) {
+      const int t = i / nb, b = i % nb;
+      char *base = smem + t * act_bytes(nbp);
+      const int4 lo = ((const int4 *)base)[b], hi = ((const int4 *)(base + nbp * 16))[b];
+      int s = dp4a_ss(lo.x, 0x01010101, 0);
+      s = dp4a_ss(lo.y, 0x01010101, s);
+      s = dp4a_ss(lo.z, 0x01010101, s);
+      s = dp4a_ss(lo.w, 0x01010101, s);
+      s = dp4a_ss(hi.x, 0x01010101, s);
+      s = dp4a_ss(hi.y, 0x01010101, s);
+      s = dp4a_ss(hi.z, 0x01010101, s);
+      s = dp4a_ss(hi.w, 0x01010101, s);
+      put_scale_sum(base, nbp, b, t < a.m ? a.xs[t * (a.xq_stride / 32) + b] : 0.0f, s);
+    }
+    __syncthreads();
+    return;
+  }
+  float *stage = (float *)(smem + act_bytes(nbp) * M);
+  float *normw = stage + M * K;
+  float ss[M];
 #pragma unroll
-  for (int t = 0; t < M; t++) inv_norm[t] = 1.0f;
-  const int K = nb * 32;
-  if (a.in_mode == GEMV_IN_NORM) {
-#pragma unroll
-    for (int t = 0; t < M; t++) {
-      if (t >= a.m) break;
-      const float *x = a.x + t * a.x_stride;
-      float ss = 0.0f;
-      for (int i = threadIdx.x * 4; i < K; i += kThreads * 4) {
-        float4 v = *(const float4 *)(x + i);
-        ss = fmaf(v.x, v.x, ss);
-        ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss);
-        ss = fmaf(v.w, v.w, ss);
+  for (int t = 0; t < M; t++) {
+    ss[t] = 0.0f;
+    if (t < a.m) {
+      const float4 *x4 = (const float4 *)(a.x + t * a.x_stride);
+      for (int i = tid; i < K / 4; i += T) {
+        float4 v = x4[i];
+        ((float4 *)(stage + t * K))[i] = v;
+        ss[t] = fmaf(v.x, v.x, ss[t]);
+        ss[t] = fmaf(v.y, v.y, ss[t]);
+        ss[t] = fmaf(v.z, v.z, ss[t]);
+        ss[t] = fmaf(v.w, v.w, ss[t]);
       }
-      ss = block_reduce_sum(ss, red);
-      inv_norm[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
     }
   }
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  for (int wb = warp; wb < M * nb; wb += kWarps) {
+  if (a.in_mode == GEMV_IN_NORM) {
+    for (int i = tid; i < K / 4; i += T) ((float4 *)normw)[i] = ((const float4 *)a.norm_w)[i];
+  }
+  __syncthreads();
+  float inv_norm[M];
+#pragma unroll
+  for (int t = 0; t < M; t++) {
+    inv_norm[t] = 1.0f;
+    if (a.in_mode == GEMV_IN_NORM && t < a.m) {
+      float tot = block_reduce_sum<WARPS>(ss[t], red);
+      inv_norm[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+    }
+  }
+  for (int wb = warp; wb < M * nb; wb += WARPS) {
     const int t = wb / nb, b = wb % nb;
     char *base = smem + t * act_bytes(nbp);
-    int8_t q;
-    float scale;
-    if (t >= a.m) {
-      q = 0;
-      scale = 0.0f;
-    } else if (a.in_mode == GEMV_IN_Q8) {
-      q = a.xq[t * a.xq_stride + b * 32 + lane];
-      scale = a.xs[t * (a.xq_stride / 32) + b];
-    } else {
-      float v = a.x[t * a.x_stride + b * 32 + lane];
+    int8_t q = 0;
+    float scale = 0.0f;
+    if (t < a.m) {
+      float v = stage[t * K + b * 32 + lane];
       if (a.in_mode == GEMV_IN_NORM) {
         float invn = inv_norm[0];
 #pragma unroll
         for (int tt = 1; tt < M; tt++)
           if (tt == t) invn = inv_norm[tt];
-        v = __fmul_rn(__fmul_rn(v, invn), a.norm_w[b * 32 + lane]);
+        v = __fmul_rn(__fmul_rn(v, invn), normw[b * 32 + lane]);
       }
       if (!isfinite(v)) v = 0.0f;
       float amax = warp_max(fabsf(v));
@@ -103,12 +159,8 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
     else hi[lane - 16] = q;
     int s = q;
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) {
-      ((float *)(base + nbp * 32))[b] = scale;
-      ((int *)(base + nbp * 36))[2 * b] = s;
-    }
-    if (lane == 16) ((int *)(base + nbp * 36))[2 * b + 1] = s;
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) put_scale_sum(base, nbp, b, scale, s);
   }
   __syncthreads();
 }
@@ -119,13 +171,13 @@ template <>
 struct ChunkRegs<JAL_Q4_0> {
   static constexpr int U = 4;  // blocks per lane per chunk (64 B / lane)
   uint4 w[U];
-  uint16_t d[U];
+  unsigned short d[U];
 };
 template <>
 struct ChunkRegs<JAL_Q8_0> {
   static constexpr int U = 2;  // blocks per lane per chunk (64 B / lane)
   uint4 w[2 * U];
-  uint16_t d[U];
+  unsigned short d[U];
 };
 
 template <int QUANT>
@@ -149,41 +201,38 @@ __device__ __forceinline__ void load_chunk(const DevMat &w, int64_t row, int par
   }
 }
 
-// Terms of one block for one token: (f32(dot16) * a_sc) * w_sc per chunk.
+// acc + f32(int dot of block b) * (a_sc * w_sc) for one token.
 template <int QUANT>
-__device__ __forceinline__ float block_terms(const ChunkRegs<QUANT> &r, int v, const char *base, int nbp, int b,
-                                             float ws) {
+__device__ __forceinline__ float block_fma(const ChunkRegs<QUANT> &r, int v, const char *base, int nbp, int b,
+                                           float ws, float acc) {
   const int4 alo = ((const int4 *)base)[b];
   const int4 ahi = ((const int4 *)(base + nbp * 16))[b];
-  const float as = ((const float *)(base + nbp * 32))[b];
-  int dlo, dhi;
+  const float2 ss = ((const float2 *)(base + nbp * 32))[b];
+  int dot;
   if (QUANT == JAL_Q4_0) {
-    const int2 sm = ((const int2 *)(base + nbp * 36))[b];
     const uint4 w = r.w[v];
-    dlo = dp4a_us(w.x & 0x0F0F0F0Fu, alo.x, 0);
-    dlo = dp4a_us(w.y & 0x0F0F0F0Fu, alo.y, dlo);
-    dlo = dp4a_us(w.z & 0x0F0F0F0Fu, alo.z, dlo);
-    dlo = dp4a_us(w.w & 0x0F0F0F0Fu, alo.w, dlo);
-    dhi = dp4a_us((w.x >> 4) & 0x0F0F0F0Fu, ahi.x, 0);
-    dhi = dp4a_us((w.y >> 4) & 0x0F0F0F0Fu, ahi.y, dhi);
-    dhi = dp4a_us((w.z >> 4) & 0x0F0F0F0Fu, ahi.z, dhi);
-    dhi = dp4a_us((w.w >> 4) & 0x0F0F0F0Fu, ahi.w, dhi);
-    dlo -= 8 * sm.x;  // nibble n encodes n - 8
-    dhi -= 8 * sm.y;
+    int d0 = dp4a_us(w.x & 0x0F0F0F0Fu, alo.x, 0);
+    int d1 = dp4a_us(w.x & 0xF0F0F0F0u, ahi.x, 0);
+    d0 = dp4a_us(w.y & 0x0F0F0F0Fu, alo.y, d0);
+    d1 = dp4a_us(w.y & 0xF0F0F0F0u, ahi.y, d1);
+    d0 = dp4a_us(w.z & 0x0F0F0F0Fu, alo.z, d0);
+    d1 = dp4a_us(w.z & 0xF0F0F0F0u, ahi.z, d1);
+    d0 = dp4a_us(w.w & 0x0F0F0F0Fu, alo.w, d0);
+    d1 = dp4a_us(w.w & 0xF0F0F0F0u, ahi.w, d1);
+    dot = d0 + (d1 >> 4) - 8 * __float_as_int(ss.y);  // nibble n encodes n - 8
   } else {
     const uint4 w0 = r.w[2 * v], w1 = r.w[2 * v + 1];
-    dlo = dp4a_ss((int)w0.x, alo.x, 0);
-    dlo = dp4a_ss((int)w0.y, alo.y, dlo);
-    dlo = dp4a_ss((int)w0.z, alo.z, dlo);
-    dlo = dp4a_ss((int)w0.w, alo.w, dlo);
-    dhi = dp4a_ss((int)w1.x, ahi.x, 0);
-    dhi = dp4a_ss((int)w1.y, ahi.y, dhi);
-    dhi = dp4a_ss((int)w1.z, ahi.z, dhi);
-    dhi = dp4a_ss((int)w1.w, ahi.w, dhi);
+    int d0 = dp4a_ss((int)w0.x, alo.x, 0);
+    int d1 = dp4a_ss((int)w1.x, ahi.x, 0);
+    d0 = dp4a_ss((int)w0.y, alo.y, d0);
+    d1 = dp4a_ss((int)w1.y, ahi.y, d1);
+    d0 = dp4a_ss((int)w0.z, alo.z, d0);
+    d1 = dp4a_ss((int)w1.z, ahi.z, d1);
+    d0 = dp4a_ss((int)w0.w, alo.w, d0);
+    d1 = dp4a_ss((int)w1.w, ahi.w, d1);
+    dot = d0 + d1;
   }
-  float tlo = __fmul_rn(__fmul_rn(__int2float_rn(dlo), as), ws);
-  float thi = __fmul_rn(__fmul_rn(__int2float_rn(dhi), as), ws);
-  return tlo + thi;  // the pair is summed first, then added to the lane's running sum
+  return fmaf(__int2float_rn(dot), ss.x * ws, acc);
 }
 
 __device__ __forceinline__ float swiglu_one(float g, float u) {
@@ -192,119 +241,119 @@ __device__ __forceinline__ float swiglu_one(float g, float u) {
   return __fmul_rn(__fmul_rn(g, sig), u);
 }
 
-// Last writer of each 32-row group quantizes it (QuantizedActQ8 of the
-// SwiGLU output) so the down projection reads int8 directly.
-__device__ void swiglu_group_quant(const GemvArgs &a, int t, int64_t lr) {
-  const int64_t groups = (a.rows + 31) / 32, g = lr / 32;
-  const int64_t need = a.rows - g * 32 < 32 ? a.rows - g * 32 : 32;
-  __threadfence();
-  unsigned old = atomicAdd(&a.group_cnt[t * groups + g], 1u);
-  if ((int64_t)old != need - 1) return;
-  __threadfence();
-  const float *src = a.y + t * a.y_stride + g * 32;
-  float v[32];
-  float amax = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 32; j++) {
-    v[j] = j < need ? __ldcg(src + j) : 0.0f;
-    if (!isfinite(v[j])) v[j] = 0.0f;
-    amax = fmaxf(amax, fabsf(v[j]));
+// Position in a warp's chunk sequence: logical row index i (rows gw + i*nw),
+// unit (0 = the row itself or the gate half, 1 = the up half) and part (the
+// chunk of 32*U blocks within the row).  Advanced by increments only.
+struct Cursor {
+  int i = 0, unit = 0, part = 0;
+  __device__ __forceinline__ void next(int parts, int units) {
+    if (++part == parts) {
+      part = 0;
+      if (++unit == units) { unit = 0; ++i; }
+    }
   }
-  float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
-  int8_t *dq = a.yq + t * groups * 32 + g * 32;
-#pragma unroll
-  for (int j = 0; j < 32; j++) dq[j] = j < need ? act_quant_one(v[j], inv) : (int8_t)0;
-  a.ys[t * groups + g] = scale;
-  a.group_cnt[t * groups + g] = 0u;
-}
+};
 
-template <int QUANT, int M, int OUT>
-__global__ void __launch_bounds__(kThreads, 2) k_gemv(const GemvArgs a) {
+template <int QUANT, int M, int OUT, int WARPS, int DEPTH>
+__global__ void __launch_bounds__(WARPS * 32, 1) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) char smem[];
   __shared__ float red[33];
   constexpr int U = ChunkRegs<QUANT>::U;
-  constexpr int UNITS = OUT == GEMV_OUT_SWIGLU_Q ? 2 : 1;
+  constexpr int UNITS = OUT == GEMV_OUT_SWIGLU ? 2 : 1;
   const int nb = (int)(a.w.cols / 32), nbp = (nb + 3) & ~3;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int64_t gw = (int64_t)blockIdx.x * kWarps + warp, nw = (int64_t)gridDim.x * kWarps;
+  const int64_t gw = (int64_t)blockIdx.x * WARPS + warp, nw = (int64_t)gridDim.x * WARPS;
   const int parts = (nb + 32 * U - 1) / (32 * U);
-  const int64_t my_rows = gw < a.rows ? (a.rows - 1 - gw) / nw + 1 : 0;
-  const int64_t n_chunks = my_rows * UNITS * parts;
+  const int my_rows = gw < a.rows ? (int)((a.rows - 1 - gw) / nw + 1) : 0;
 
-  ChunkRegs<QUANT> cur, nxt;
-  if (n_chunks > 0) load_chunk<QUANT>(a.w, gw, 0, nb, lane, cur);
+  Cursor ld, cp;  // next chunk to load / to compute
+  ChunkRegs<QUANT> buf[DEPTH];
+#pragma unroll
+  for (int k = 0; k < DEPTH; k++) {
+    if (ld.i < my_rows) {
+      load_chunk<QUANT>(a.w, gw + ld.i * nw + (ld.unit ? a.up_offset : 0), ld.part, nb, lane, buf[k]);
+      ld.next(parts, UNITS);
+    }
+  }
   pdl_wait();
-  gemv_prologue<M>(a, smem, nb, nbp, red);
+  gemv_prologue<M, WARPS>(a, smem, nb, nbp, red);
   pdl_trigger();
 
   float acc0[M], acc1[M];
 #pragma unroll
   for (int t = 0; t < M; t++) acc0[t] = acc1[t] = 0.0f;
 
-  int part = 0, unit = 0;
-  int64_t li = 0;  // index of the logical row within this warp's list
-  for (int64_t c = 0; c < n_chunks; c++) {
-    // Position of chunk c + 1.
-    int npart = part + 1, nunit = unit;
-    int64_t nli = li;
-    if (npart == parts) { npart = 0; nunit++; if (nunit == UNITS) { nunit = 0; nli++; } }
-    if (c + 1 < n_chunks) {
-      int64_t nrow = gw + nli * nw + (nunit ? a.up_offset : 0);
-      load_chunk<QUANT>(a.w, nrow, npart, nb, lane, nxt);
-    }
+  while (cp.i < my_rows) {
 #pragma unroll
-    for (int v = 0; v < U; v++) {
-      int b = part * 32 * U + v * 32 + lane;
-      if (b < nb) {
-        float ws = f16_finite(cur.d[v]);
+    for (int k = 0; k < DEPTH; k++) {
+      if (cp.i < my_rows) {
 #pragma unroll
-        for (int t = 0; t < M; t++) {
-          float term = block_terms<QUANT>(cur, v, smem + t * act_bytes(nbp), nbp, b, ws);
-          if (unit == 0) acc0[t] += term;
-          else acc1[t] += term;
+        for (int v = 0; v < U; v++) {
+          const int b = cp.part * 32 * U + v * 32 + lane;
+          if (b < nb) {
+            const float ws = __half2float(__ushort_as_half(buf[k].d[v]));
+#pragma unroll
+            for (int t = 0; t < M; t++) {
+              if (cp.unit == 0) acc0[t] = block_fma<QUANT>(buf[k], v, smem + t * act_bytes(nbp), nbp, b, ws, acc0[t]);
+              else acc1[t] = block_fma<QUANT>(buf[k], v, smem + t * act_bytes(nbp), nbp, b, ws, acc1[t]);
+            }
+          }
         }
-      }
-    }
-    if (part == parts - 1 && unit == UNITS - 1) {
-      const int64_t lr = gw + li * nw;
-      float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-      for (int t = 0; t < M; t++) {
-        float r0 = warp_sum(acc0[t]);
-        float r1 = UNITS == 2 ? warp_sum(acc1[t]) : 0.0f;
-        if (lane == t) { s0 = r0; s1 = r1; }
-        acc0[t] = acc1[t] = 0.0f;
-      }
-      if (lane < a.m) {
-        const int t = lane;
-        float *yp = a.y + t * a.y_stride + lr;
-        if (OUT == GEMV_OUT_STORE) {
-          *yp = a.bias ? s0 + a.bias[lr] : s0;
-        } else if (OUT == GEMV_OUT_ADD) {
-          float p = a.bias ? s0 + a.bias[lr] : s0;
-          *yp = *yp + p;
-        } else {
-          *yp = swiglu_one(s0, s1);
-          swiglu_group_quant(a, t, lr);
+        if (ld.i < my_rows) {
+          load_chunk<QUANT>(a.w, gw + ld.i * nw + (ld.unit ? a.up_offset : 0), ld.part, nb, lane, buf[k]);
+          ld.next(parts, UNITS);
         }
+        if (cp.part == parts - 1 && cp.unit == UNITS - 1) {
+          const int64_t lr = gw + cp.i * nw;
+          float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+          for (int t = 0; t < M; t++) {
+            const float r0 = warp_sum(acc0[t]);
+            const float r1 = UNITS == 2 ? warp_sum(acc1[t]) : 0.0f;
+            if (lane == t) { s0 = r0; s1 = r1; }
+            acc0[t] = acc1[t] = 0.0f;
+          }
+          if (lane < a.m) {
+            float *yp = a.y + lane * a.y_stride + lr;
+            if (OUT == GEMV_OUT_STORE) {
+              *yp = a.bias ? s0 + a.bias[lr] : s0;
+            } else if (OUT == GEMV_OUT_ADD) {
+              const float p = a.bias ? s0 + a.bias[lr] : s0;
+              *yp = *yp + p;
+            } else {
+              *yp = swiglu_one(s0, s1);
+            }
+          }
+        }
+        cp.next(parts, UNITS);
       }
     }
-    part = npart;
-    unit = nunit;
-    li = nli;
-    cur = nxt;
   }
 }
 
-template <int QUANT, int M, int OUT>
+// Launch shapes: (warps per CTA, chunks in flight per warp).
+constexpr int kWarpsA = 16, kDepthA = 3;  // 128 registers / thread
+constexpr int kWarpsB = 32, kDepthB = 2;  // 64 registers / thread
+
+int g_shape = -1;  // 0 = A, 1 = B
+int g_sm_count = 0;
+
+int shape() {
+  if (g_shape < 0) {
+    const char *e = getenv("JAL_GEMV_SHAPE");
+    g_shape = (e && *e == 'B') ? 1 : 0;
+  }
+  return g_shape;
+}
+
+template <int QUANT, int M, int OUT, int WARPS, int DEPTH>
 void launch_t(const GemvArgs &a, int grid, cudaStream_t s) {
-  const int nb = (int)(a.w.cols / 32), nbp = (nb + 3) & ~3;
-  size_t smem = act_bytes(nbp) * M;
-  auto kern = k_gemv<QUANT, M, OUT>;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int nb = (int)(a.w.cols / 32);
+  size_t smem = smem_bytes(a.in_mode, M, nb);
+  auto kern = k_gemv<QUANT, M, OUT, WARPS, DEPTH>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(WARPS * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -315,19 +364,55 @@ void launch_t(const GemvArgs &a, int grid, cudaStream_t s) {
   cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-template <int QUANT, int OUT>
+template <int QUANT, int OUT, int WARPS, int DEPTH>
 void launch_m(const GemvArgs &a, int grid, cudaStream_t s) {
   switch (a.m) {
-    case 1: launch_t<QUANT, 1, OUT>(a, grid, s); break;
-    case 2: launch_t<QUANT, 2, OUT>(a, grid, s); break;
-    case 3: case 4: launch_t<QUANT, 4, OUT>(a, grid, s); break;
-    default: launch_t<QUANT, 8, OUT>(a, grid, s); break;
+    case 1: launch_t<QUANT, 1, OUT, WARPS, DEPTH>(a, grid, s); break;
+    case 2: launch_t<QUANT, 2, OUT, WARPS, DEPTH>(a, grid, s); break;
+    case 3: case 4: launch_t<QUANT, 4, OUT, WARPS, DEPTH>(a, grid, s); break;
+    default: launch_t<QUANT, 8, OUT, WARPS, DEPTH>(a, grid, s); break;
   }
 }
 
-int g_sm_count = 0;
+template <int QUANT, int OUT>
+void launch_q(const GemvArgs &a, int grid, cudaStream_t s) {
+  if (shape() == 1 && a.m <= 2) launch_m<QUANT, OUT, kWarpsB, kDepthB>(a, grid, s);
+  else launch_m<QUANT, OUT, kWarpsA, kDepthA>(a, grid, s);
+}
+
+template <int QUANT, int OUT, int WARPS, int DEPTH>
+void set_attrs() {
+  const int lim = kGemvMaxSmem;
+  cudaFuncSetAttribute(k_gemv<QUANT, 1, OUT, WARPS, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  cudaFuncSetAttribute(k_gemv<QUANT, 2, OUT, WARPS, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  cudaFuncSetAttribute(k_gemv<QUANT, 4, OUT, WARPS, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  cudaFuncSetAttribute(k_gemv<QUANT, 8, OUT, WARPS, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+}
+
+template <int WARPS, int DEPTH>
+void set_attrs_all() {
+  set_attrs<JAL_Q4_0, GEMV_OUT_STORE, WARPS, DEPTH>();
+  set_attrs<JAL_Q4_0, GEMV_OUT_ADD, WARPS, DEPTH>();
+  set_attrs<JAL_Q4_0, GEMV_OUT_SWIGLU, WARPS, DEPTH>();
+  set_attrs<JAL_Q8_0, GEMV_OUT_STORE, WARPS, DEPTH>();
+  set_attrs<JAL_Q8_0, GEMV_OUT_ADD, WARPS, DEPTH>();
+  set_attrs<JAL_Q8_0, GEMV_OUT_SWIGLU, WARPS, DEPTH>();
+}
 
 }  // namespace
+
+void gemv_init() {
+  static bool done = false;
+  if (done) return;
+  set_attrs_all<kWarpsA, kDepthA>();
+  set_attrs_all<kWarpsB, kDepthB>();
+  done = true;
+}
+
+size_t gemv_smem_bytes(int in_mode, int m, int64_t cols) {
+  int M = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
+  return smem_bytes(in_mode, M, (int)(cols / 32));
+}
 
 int gemv_default_grid(const GemvArgs &a) {
   if (!g_sm_count) {
@@ -336,25 +421,27 @@ int gemv_default_grid(const GemvArgs &a) {
     cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (g_sm_count <= 0) g_sm_count = 148;
   }
-  int64_t need = (a.rows + kWarps - 1) / kWarps;
-  int64_t cap = (int64_t)g_sm_count * 2;
+  const int warps = (shape() == 1 && a.m <= 2) ? kWarpsB : kWarpsA;
+  int64_t need = (a.rows + warps - 1) / warps;
+  int64_t cap = (int64_t)g_sm_count;
   return (int)(need < cap ? need : cap);
 }
 
 void launch_gemv(const GemvArgs &a0, cudaStream_t s) {
   if (a0.rows <= 0) return;
+  gemv_init();
   GemvArgs a = a0;
   // Token counts between template sizes run the next larger instantiation;
   // token slots t >= m quantize to zero and are never written.
   int grid = a.grid > 0 ? a.grid : gemv_default_grid(a);
   if (a.w.quant == JAL_Q4_0) {
-    if (a.out_mode == GEMV_OUT_STORE) launch_m<JAL_Q4_0, GEMV_OUT_STORE>(a, grid, s);
-    else if (a.out_mode == GEMV_OUT_ADD) launch_m<JAL_Q4_0, GEMV_OUT_ADD>(a, grid, s);
-    else launch_m<JAL_Q4_0, GEMV_OUT_SWIGLU_Q>(a, grid, s);
+    if (a.out_mode == GEMV_OUT_STORE) launch_q<JAL_Q4_0, GEMV_OUT_STORE>(a, grid, s);
+    else if (a.out_mode == GEMV_OUT_ADD) launch_q<JAL_Q4_0, GEMV_OUT_ADD>(a, grid, s);
+    else launch_q<JAL_Q4_0, GEMV_OUT_SWIGLU>(a, grid, s);
   } else {
-    if (a.out_mode == GEMV_OUT_STORE) launch_m<JAL_Q8_0, GEMV_OUT_STORE>(a, grid, s);
-    else if (a.out_mode == GEMV_OUT_ADD) launch_m<JAL_Q8_0, GEMV_OUT_ADD>(a, grid, s);
-    else launch_m<JAL_Q8_0, GEMV_OUT_SWIGLU_Q>(a, grid, s);
+    if (a.out_mode == GEMV_OUT_STORE) launch_q<JAL_Q8_0, GEMV_OUT_STORE>(a, grid, s);
+    else if (a.out_mode == GEMV_OUT_ADD) launch_q<JAL_Q8_0, GEMV_OUT_ADD>(a, grid, s);
+    else launch_q<JAL_Q8_0, GEMV_OUT_SWIGLU>(a, grid, s);
   }
 }
 

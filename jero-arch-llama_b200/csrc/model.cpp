@@ -782,6 +782,10 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
       fail(JAL_ERR_CAPABILITY_MISMATCH, "the device forward needs Q4_0/Q8_0 layer matrices with uniform q/k/v and gate/up quants");
   }
   if (!device_quant(c.lm_head.quant)) fail(JAL_ERR_CAPABILITY_MISMATCH, "LM head quant %d not supported on the device path", c.lm_head.quant);
+  gemv_init();
+  if (gemv_smem_bytes(GEMV_IN_F32, 1, (int64_t)g.ffn_dim) > (size_t)kGemvMaxSmem ||
+      gemv_smem_bytes(GEMV_IN_NORM, 1, (int64_t)g.hidden_dim) > (size_t)kGemvMaxSmem)
+    fail(JAL_ERR_CAPABILITY_MISMATCH, "hidden/ffn dims exceed the decode GEMV shared-memory staging");
   JAL_CUDA(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking));
   ctx->stream = ctx->own_stream;
   const uint64_t n_ctx = ctx->cfg.n_ctx, ps = ctx->cfg.page_size, n_pages = (n_ctx + ps - 1) / ps;
@@ -825,12 +829,11 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   }
   // Decode buffers.
   const int sms = sm_count();
-  ctx->n_splits = (int)std::max<uint64_t>(1, std::min<uint64_t>((2 * sms + g.n_heads_kv - 1) / g.n_heads_kv, (n_ctx + 63) / 64));
+  ctx->n_splits = attn_decode_cluster_size((int)g.head_dim, kv.f16, n_ctx >= 512 ? 16 : 4);
   ctx->am_blocks = sms;
-  const uint64_t G = g.n_heads_q / g.n_heads_kv;
-  size_t f32s = H + (Q + 2 * KV) + Q + Q / 32 + F + (F + 31) / 32 + V + (size_t)g.n_heads_kv * ctx->n_splits * G * (g.head_dim + 2) + sms;
-  size_t bytes = f32s * 4 + Q + ((F + 31) / 32) * 32 + 4096 + (F / 32 + 1) * 4 + g.n_heads_kv * 4 + 64 +
-                 (size_t)sms * 4 + (n_ctx + 2) * 4 + 64;
+  size_t f32s = H + (Q + 2 * KV) + Q + Q / 32 + F + (F + 31) / 32 + V + sms;
+  size_t bytes = f32s * 4 + Q + ((F + 31) / 32) * 32 + 4096 + (F / 32 + 1) * 4 + 64 + (size_t)sms * 4 + (n_ctx + 2) * 4 +
+                 32 * 256;
   auto db = alloc(bytes + 1024);
   ctx->bufs.push_back(db);
   JAL_CUDA(cudaMemset(db->ptr, 0, db->bytes));
@@ -849,8 +852,6 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->ffn_s = (float *)take((F + 31) / 32 * 4);
   ctx->ffn_cnt = (unsigned *)take((F + 31) / 32 * 4);
   ctx->logits = (float *)take(V * 4);
-  ctx->part = (float *)take((size_t)g.n_heads_kv * ctx->n_splits * G * (g.head_dim + 2) * 4);
-  ctx->split_cnt = (unsigned *)take(g.n_heads_kv * 4);
   ctx->am_val = (float *)take(sms * 4);
   ctx->am_idx = (int *)take(sms * 4);
   ctx->am_cnt = (unsigned *)take(4);
@@ -903,7 +904,7 @@ void Context::enqueue_decode_step(bool pdl) {
     aa.n_heads_q = (int64_t)g.n_heads_q; aa.rotary_dim = (int64_t)g.rotary_dim;
     aa.kv = kv; aa.layer = (int64_t)l; aa.d_pos = d_pos; aa.window = (int64_t)cfg.sliding_window;
     aa.scale = 1.0f / sqrtf((float)g.head_dim);
-    aa.n_splits = n_splits; aa.part = part; aa.split_cnt = split_cnt;
+    aa.n_splits = n_splits;
     aa.out = attn; aa.out_q = attn_q; aa.out_s = attn_s; aa.pdl = pdl;
     launch_attn_decode(aa, stream);
     GemvArgs oa;
@@ -914,12 +915,11 @@ void Context::enqueue_decode_step(bool pdl) {
     GemvArgs ga;
     ga.w = L.gateup; ga.rows = (int64_t)F; ga.m = 1; ga.in_mode = GEMV_IN_NORM;
     ga.x = hidden; ga.x_stride = (int64_t)H; ga.norm_w = L.ffn_norm; ga.eps = eps;
-    ga.out_mode = GEMV_OUT_SWIGLU_Q; ga.y = ffn; ga.y_stride = (int64_t)F; ga.up_offset = (int64_t)F;
-    ga.yq = ffn_q; ga.ys = ffn_s; ga.group_cnt = ffn_cnt; ga.pdl = pdl;
+    ga.out_mode = GEMV_OUT_SWIGLU; ga.y = ffn; ga.y_stride = (int64_t)F; ga.up_offset = (int64_t)F; ga.pdl = pdl;
     launch_gemv(ga, stream);
     GemvArgs da;
-    da.w = L.wdown.dm; da.rows = (int64_t)H; da.m = 1; da.in_mode = GEMV_IN_Q8;
-    da.xq = ffn_q; da.xs = ffn_s; da.xq_stride = (int64_t)((F + 31) / 32 * 32);
+    da.w = L.wdown.dm; da.rows = (int64_t)H; da.m = 1; da.in_mode = GEMV_IN_F32;
+    da.x = ffn; da.x_stride = (int64_t)F;
     da.out_mode = GEMV_OUT_ADD; da.y = hidden; da.y_stride = (int64_t)H; da.pdl = pdl;
     launch_gemv(da, stream);
     n += 5;

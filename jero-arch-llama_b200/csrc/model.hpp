@@ -130,9 +130,9 @@ struct Context {
   int *d_err = nullptr;
   float *cos_tab = nullptr, *sin_tab = nullptr, *cos_long = nullptr, *sin_long = nullptr;
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *attn_s = nullptr, *ffn = nullptr, *ffn_s = nullptr,
-        *logits = nullptr, *part = nullptr, *am_val = nullptr;
+        *logits = nullptr, *am_val = nullptr;
   int8_t *attn_q = nullptr, *ffn_q = nullptr;
-  unsigned *ffn_cnt = nullptr, *split_cnt = nullptr, *am_cnt = nullptr;
+  unsigned *ffn_cnt = nullptr, *am_cnt = nullptr;
   int *am_idx = nullptr;
   int n_splits = 1, am_blocks = 148;
   // prefill scratch (grown on demand)

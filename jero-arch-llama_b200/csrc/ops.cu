@@ -142,18 +142,34 @@ __global__ void k_argmax(const float *logits, int64_t n, float *pv, int *pi, uns
     last = atomicAdd(cnt, 1u) == gridDim.x - 1;
   }
   __syncthreads();
-  if (!last || threadIdx.x != 0) {
+  if (!last) {
     if (pdl) pdl_trigger();
     return;
   }
+  // The last CTA reduces the per-CTA winners with all its threads at once.
   __threadfence();
   float fv = -INFINITY;
   int fi = 0x7fffffff;
-  for (unsigned k = 0; k < gridDim.x; k++) {
+  for (unsigned k = threadIdx.x; k < gridDim.x; k += blockDim.x) {
     float v = __ldcg(pv + k);
     int i = __ldcg(pi + k);
     if (better(v, i, fv, fi)) { fv = v; fi = i; }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, fv, o);
+    int oi = __shfl_xor_sync(0xffffffffu, fi, o);
+    if (better(ov, oi, fv, fi)) { fv = ov; fi = oi; }
+  }
+  __syncthreads();
+  if (l == 0) { sv[w] = fv; si[w] = fi; }
+  __syncthreads();
+  if (threadIdx.x != 0) {
+    if (pdl) pdl_trigger();
+    return;
+  }
+  for (int k = 1; k < (int)(blockDim.x / 32); k++)
+    if (better(sv[k], si[k], fv, fi)) { fv = sv[k]; fi = si[k]; }
   const uint32_t tok = (uint32_t)(fi == 0x7fffffff ? 0 : fi);
   *token_out = tok;
   if (d_pos) {

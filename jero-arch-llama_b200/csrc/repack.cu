@@ -10,6 +10,13 @@
 
 namespace jal {
 
+// The reference decodes block scales with f16_to_f32_finite (Inf/NaN ->
+// +-0.0625).  0.0625 = 2^-4 is exactly representable in f16 (0x2C00), so the
+// repack stores the sanitized half and every kernel may convert it plainly.
+__device__ __forceinline__ uint16_t sanitize_f16(uint16_t h) {
+  return (h & 0x7C00u) == 0x7C00u ? (uint16_t)((h & 0x8000u) | 0x2C00u) : h;
+}
+
 // ---- repack: GGUF block rows -> qs plane + f16 scale plane ---------------
 // unpack_row_i8 (repack_cache.rs:840-871) keeps the nibbles/bytes and the
 // f16 scale of every block; the B200 layout stores them split into two
@@ -29,7 +36,7 @@ __global__ void k_repack_q4_0(const uint8_t *__restrict__ raw, int64_t rows, int
   v.z = (uint32_t)h[5] | ((uint32_t)h[6] << 16);
   v.w = (uint32_t)h[7] | ((uint32_t)h[8] << 16);
   *(uint4 *)(qs + r * qs_stride + g * 16) = v;
-  d[r * d_stride + g] = h[0];
+  d[r * d_stride + g] = sanitize_f16(h[0]);
 }
 
 __global__ void k_repack_q8_0(const uint8_t *__restrict__ raw, int64_t rows, int64_t nb, uint8_t *__restrict__ qs,
@@ -53,7 +60,7 @@ __global__ void k_repack_q8_0(const uint8_t *__restrict__ raw, int64_t rows, int
   uint4 *dst = (uint4 *)(qs + r * qs_stride + g * 32);
   dst[0] = a;
   dst[1] = b;
-  d[r * d_stride + g] = h[0];
+  d[r * d_stride + g] = sanitize_f16(h[0]);
 }
 
 void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, uint8_t *qs, uint16_t *d,
