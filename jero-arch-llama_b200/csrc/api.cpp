@@ -454,6 +454,22 @@ int jal_context_reset(jal_context *ctx) {
   });
 }
 
+// Reads the context's device error word after a synchronised step: bit 1 =
+// an embedding lookup saw an out-of-range token, bit 2 = a bounded wait for
+// a KV copy in decode attention gave up.  The word is cleared afterwards.
+static void enqueue_error_read(Context &c) {
+  JAL_CUDA(cudaMemcpyAsync(&c.h_token[4], c.d_err, 4, cudaMemcpyDeviceToHost, c.stream));
+}
+static void check_device_error(Context &c) {
+  const uint32_t e = c.h_token[4];
+  if (!e) return;
+  c.h_token[4] = 0;
+  JAL_CUDA(cudaMemsetAsync(c.d_err, 0, 4, c.stream));
+  JAL_CUDA(cudaStreamSynchronize(c.stream));
+  if (e & 2u) fail(JAL_ERR_TIMEOUT, "decode attention: a bounded wait for KV tile copies gave up");
+  fail(JAL_ERR_TENSOR_BOUNDS, "embedding lookup saw an out-of-range token id");
+}
+
 static void check_tokens(const Context &c, const uint32_t *t, size_t n) {
   for (size_t i = 0; i < n; i++)
     if (t[i] >= c.cache->emb_rows)
@@ -475,7 +491,9 @@ int jal_prefill_step(jal_context *h, const uint32_t *tokens, size_t n, size_t st
     c.prefill(tokens, n, start_pos, compute_logits != 0);
     if (compute_logits && logits)
       JAL_CUDA(cudaMemcpyAsync(logits, c.logits, logits_len * 4, cudaMemcpyDeviceToHost, c.stream));
+    enqueue_error_read(c);
     JAL_CUDA(cudaStreamSynchronize(c.stream));
+    check_device_error(c);
     c.position = start_pos + n;
   });
 }
@@ -497,7 +515,9 @@ int jal_decode_step(jal_context *h, uint32_t token, float *logits, size_t logits
     JAL_CUDA(cudaMemcpyAsync(c.d_token, c.h_token, 4, cudaMemcpyHostToDevice, c.stream));
     c.run_decode_step();
     if (logits) JAL_CUDA(cudaMemcpyAsync(logits, c.logits, logits_len * 4, cudaMemcpyDeviceToHost, c.stream));
+    enqueue_error_read(c);
     JAL_CUDA(cudaStreamSynchronize(c.stream));
+    check_device_error(c);
     c.position += 1;
   });
 }
@@ -519,7 +539,9 @@ int jal_decode_greedy(jal_context *h, uint32_t token, size_t n_steps, uint32_t *
     JAL_CUDA(cudaMemcpyAsync(c.d_token, c.h_token, 4, cudaMemcpyHostToDevice, c.stream));
     for (size_t i = 0; i < n_steps; i++) c.run_decode_step();
     JAL_CUDA(cudaMemcpyAsync(tokens_out, c.d_hist + c.position + 1, n_steps * 4, cudaMemcpyDeviceToHost, c.stream));
+    enqueue_error_read(c);
     JAL_CUDA(cudaStreamSynchronize(c.stream));
+    check_device_error(c);
     c.position += n_steps;
   });
 }

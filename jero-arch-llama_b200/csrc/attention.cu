@@ -24,10 +24,13 @@ namespace jal {
 
 namespace {
 
-constexpr int kAttnThreads = 128;
-constexpr int kSub = 128;  // positions per sub-chunk
-constexpr int kMaxG = 8;   // query heads per KV head
+constexpr int kAttnWarps = 8;
+constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxClusterCtas = 16;  // CTAs per KV head (one cluster)
+constexpr int kStages = 3;           // shared-memory ring of K/V tiles
+constexpr int kStageBytes = 32 * 1024;
+constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polls
+constexpr int kErrAttnWait = 2;            // bit set in the context error word
 
 __device__ __forceinline__ int64_t kv_elem(const KvView &kv, int64_t layer, int64_t h, int64_t pos) {
   int64_t page = kv.page_table[pos / kv.page_size], slot = pos % kv.page_size;
@@ -47,39 +50,170 @@ __device__ __forceinline__ void rot(float &x0, float &x1, float c, float s) {
   x1 = b;
 }
 
+// ---- mbarrier / bulk-copy helpers (shared::cta barrier, own-CTA destination)
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Polls at most kWaitLimit times; false when the wait gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+  for (uint32_t it = 0; it < kWaitLimit; it++)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Tile geometry for head_dim HD and KV element type.
 template <int HD, bool F16>
-__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeArgs a) {
+struct AttnGeom {
+  static constexpr int ES = F16 ? 2 : 4;              // bytes per element
+  static constexpr int ROW = HD * ES;                 // bytes of one position's K (or V)
+  static constexpr int TP = kStageBytes / (2 * ROW);  // positions per tile
+  static constexpr int LG = ROW / 16;                 // lanes per position when scoring
+  static constexpr int PPS = 32 / LG;                 // positions per warp step when scoring
+  static constexpr int DPL = 16 / ES;                 // dims per lane when scoring
+  static constexpr int TPW = TP / kAttnWarps;         // positions per warp per tile
+  static constexpr int VD = HD / 32;                  // dims per lane in P.V
+  static_assert(TPW % PPS == 0, "tile split");
+};
+
+// Copies positions [t0, t0 + n) of KV head h (K then V) into a ring stage;
+// one bulk copy per page run.  Caller: one thread.
+template <int HD, bool F16>
+__device__ void issue_tile(const AttnDecodeArgs &a, char *stage, uint64_t *bar, int64_t t0, int n, int h) {
+  using Gm = AttnGeom<HD, F16>;
+  const KvView &kv = a.kv;
+  mbar_expect_tx(bar, (uint32_t)(2 * n * Gm::ROW));
+  int done = 0;
+  while (done < n) {
+    const int64_t p = t0 + done;
+    const int64_t page = kv.page_table[p / kv.page_size], slot = p % kv.page_size;
+    const int run = (int)(kv.page_size - slot < n - done ? kv.page_size - slot : n - done);
+    const int64_t e = (((a.layer * kv.n_pages + page) * kv.n_kv + h) * kv.page_size + slot) * HD;
+    bulk_g2s(stage + done * Gm::ROW, (const char *)kv.k + e * Gm::ES, (uint32_t)(run * Gm::ROW), bar);
+    bulk_g2s(stage + Gm::TP * Gm::ROW + done * Gm::ROW, (const char *)kv.v + e * Gm::ES, (uint32_t)(run * Gm::ROW),
+             bar);
+    done += run;
+  }
+}
+
+template <bool F16, int N>
+__device__ __forceinline__ void load_vals(const char *p, float (&o)[N]) {
+  if (F16) {
+    if (N == 8) {
+      const uint4 raw = *(const uint4 *)p;
+      const __half2 *r = (const __half2 *)&raw;
+#pragma unroll
+      for (int k = 0; k < 4; k++) { float2 f = __half22float2(r[k]); o[2 * k] = f.x; o[2 * k + 1] = f.y; }
+    } else if (N == 4) {
+      const uint2 raw = *(const uint2 *)p;
+      const __half2 *r = (const __half2 *)&raw;
+#pragma unroll
+      for (int k = 0; k < 2; k++) { float2 f = __half22float2(r[k]); o[2 * k] = f.x; o[2 * k + 1] = f.y; }
+    } else {
+      const __half2 *h2 = (const __half2 *)p;
+#pragma unroll
+      for (int k = 0; k < N / 2; k++) { float2 f = __half22float2(h2[k]); o[2 * k] = f.x; o[2 * k + 1] = f.y; }
+    }
+  } else {
+    if (N == 4) {
+      const float4 v = *(const float4 *)p;
+      o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < N / 2; k++) { float2 f = ((const float2 *)p)[k]; o[2 * k] = f.x; o[2 * k + 1] = f.y; }
+    }
+  }
+}
+
+// Decode attention for one token.  Grid: n_kv clusters of cs CTAs; CTA rank r
+// of cluster h handles positions [s0, s1) of KV head h, split evenly.
+//
+// Before griddepcontrol.wait (the cache rows below the current position were
+// written by earlier launches) one thread starts bulk copies of the CTA's
+// K/V rows into a ring of kStages shared-memory tiles.  After the wait the
+// CTA builds q (bias, RoPE) for the head group and the new k/v; the CTA
+// holding the current position appends it to the cache and patches its tile.
+// Each warp scores its share of a tile (a group of LG lanes per position, q
+// held in registers), keeps its own online softmax (max, denominator, P.V
+// accumulator with lanes over dims), and the warps are merged at the end.
+// Cluster partials are merged through distributed shared memory and every
+// rank finalises and quantizes (QuantizedActQ8) a share of the 32-blocks.
+template <int HD, bool F16, int GP>
+__global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnDecodeArgs a) {
   namespace cg = cooperative_groups;
+  using Gm = AttnGeom<HD, F16>;
+  constexpr int TP = Gm::TP, LG = Gm::LG, PPS = Gm::PPS, DPL = Gm::DPL, TPW = Gm::TPW, VD = Gm::VD;
   cg::cluster_group cluster = cg::this_cluster();
-  __shared__ float q_s[kMaxG][HD];
-  __shared__ float kn_s[HD], vn_s[HD];
-  __shared__ float p_s[kMaxG][kSub];
-  __shared__ float red_s[4][kMaxG];
-  __shared__ float alpha_s[kMaxG];
-  __shared__ float acc_s[4][kMaxG][HD];  // acc_s[0] holds this CTA's partial after the reduction
-  __shared__ float ml_s[2][kMaxG];       // running max / denominator of this CTA
-  __shared__ float wgt_s[kMaxClusterCtas][kMaxG];
-  __shared__ float den_s[kMaxG];
+  extern __shared__ __align__(128) char ring[];  // kStages x kStageBytes, reused for the warp merge
+  __shared__ __align__(8) uint64_t bars[kStages];
+  __shared__ __align__(16) float q_s[GP][HD];
+  __shared__ __align__(16) float kn_s[HD], vn_s[HD];
+  __shared__ __align__(16) float p_w[kAttnWarps][TPW * GP];
+  __shared__ __align__(16) float acc_s[GP][HD];  // this CTA's partial (unnormalised)
+  __shared__ float ml_s[2][GP];                  // its max / denominator per head
+  __shared__ float wgt_s[kMaxClusterCtas][GP];
+  __shared__ float lsum_s[kMaxClusterCtas][GP];
+  __shared__ float den_s[GP];
+  __shared__ float wm_s[kAttnWarps][GP];         // warp merge weights
   const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
   const int h = blockIdx.x / cs, tid = threadIdx.x;
   const int warp = tid / 32, lane = tid % 32;
   const int G = (int)(a.n_heads_q / a.kv.n_kv);
   const int64_t Q = a.n_heads_q * HD, KVD = a.kv.n_kv * HD;
 
-  pdl_wait();
+  // Slice of this CTA.  d_pos was written before the previous kernel started.
   const int64_t pos = *a.d_pos, seq = pos + 1;
   const int64_t lo = (a.window > 0 && seq > a.window) ? seq - a.window : 0;
   const int64_t span = seq - lo, per = (span + cs - 1) / cs;
-  const int64_t s0 = lo + rank * per, s1 = s0 + per < seq ? s0 + per : seq;
+  const int64_t s0 = lo + rank * per;
+  const int64_t s1 = s0 + per < seq ? s0 + per : seq;
+  const int64_t len = s1 > s0 ? s1 - s0 : 0;
+  const int nt = (int)((len + TP - 1) / TP);
+  if (tid == 0) {
+    for (int s = 0; s < kStages; s++) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+    fence_proxy_async();
+    for (int k = 0; k < nt && k < kStages; k++) {
+      const int64_t t0 = s0 + (int64_t)k * TP;
+      const int n = (int)(s1 - t0 < TP ? s1 - t0 : TP);
+      issue_tile<HD, F16>(a, ring + k * kStageBytes, &bars[k], t0, n, h);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
 
   // q / new k / new v of this head group (+ bias), then RoPE.
-  for (int i = tid; i < G * HD; i += kAttnThreads) {
-    int g = i / HD, d = i % HD;
-    int64_t e = (int64_t)(h * G + g) * HD + d;
-    q_s[g][d] = a.bq ? __fadd_rn(a.qkv[e], a.bq[e]) : a.qkv[e];
+  for (int i = tid; i < GP * HD; i += kAttnThreads) {
+    const int g = i / HD, d = i % HD;
+    float v = 0.0f;
+    if (g < G) {
+      const int64_t e = (int64_t)(h * G + g) * HD + d;
+      v = a.bq ? __fadd_rn(a.qkv[e], a.bq[e]) : a.qkv[e];
+    }
+    q_s[g][d] = v;
   }
   for (int d = tid; d < HD; d += kAttnThreads) {
-    int64_t ek = (int64_t)h * HD + d;
+    const int64_t ek = (int64_t)h * HD + d;
     kn_s[d] = a.bk ? __fadd_rn(a.qkv[Q + ek], a.bk[ek]) : a.qkv[Q + ek];
     vn_s[d] = a.bv ? __fadd_rn(a.qkv[Q + KVD + ek], a.bv[ek]) : a.qkv[Q + KVD + ek];
   }
@@ -90,9 +224,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
     const float *ct = (use_long ? a.cos_tab_long : a.cos_tab) + pos * half;
     const float *st = (use_long ? a.sin_tab_long : a.sin_tab) + pos * half;
     for (int i = tid; i < (G + 1) * half; i += kAttnThreads) {
-      int g = i / half, j = i % half;
+      const int g = i / half, j = i % half;
       float *row = g < G ? q_s[g] : kn_s;
-      int i0 = a.neox ? j : 2 * j, i1 = a.neox ? j + half : 2 * j + 1;
+      const int i0 = a.neox ? j : 2 * j, i1 = a.neox ? j + half : 2 * j + 1;
       float x0 = row[i0], x1 = row[i1];
       rot(x0, x1, ct[j], st[j]);
       row[i0] = x0;
@@ -100,187 +234,204 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
     }
     __syncthreads();
   }
-  // Append the new K/V (recipe.rs:2319-2326) from the CTA owning `pos`.
-  if (pos >= s0 && pos < s1) {
-    int64_t e = kv_elem(a.kv, a.layer, h, pos);
+  // The stored (possibly f16-rounded) new k/v are what every later step
+  // reads, so this step uses the same values.
+  if (F16) {
+    for (int d = tid; d < HD; d += kAttnThreads) {
+      kn_s[d] = __half2float(__float2half_rn(kn_s[d]));
+      vn_s[d] = __half2float(__float2half_rn(vn_s[d]));
+    }
+  }
+  const bool own_pos = pos >= s0 && pos < s1;
+  if (own_pos) {  // append (recipe.rs:2319-2326)
+    const int64_t e = kv_elem(a.kv, a.layer, h, pos);
     for (int d = tid; d < HD; d += kAttnThreads) {
       store_kv(a.kv.k, a.kv.f16, e + d, kn_s[d]);
       store_kv(a.kv.v, a.kv.f16, e + d, vn_s[d]);
     }
   }
+  __syncthreads();
 
-  float m_run[kMaxG], l_run[kMaxG];
-  constexpr int DPL = HD / 32;  // dims per lane in the PV phase
-  float acc[kMaxG][DPL];
+  // q slice of this lane for scoring: dims c*DPL .. c*DPL + DPL - 1.
+  const int c = lane % LG, grp = lane / LG;
+  float qr[GP][DPL];
 #pragma unroll
-  for (int g = 0; g < kMaxG; g++) {
+  for (int g = 0; g < GP; g++)
+#pragma unroll
+    for (int k = 0; k < DPL; k++) qr[g][k] = q_s[g][c * DPL + k];
+
+  float m_run[GP], acc[GP][VD];
+  float l_lane = 0.0f;  // denominator of head lane % GP
+#pragma unroll
+  for (int g = 0; g < GP; g++) {
     m_run[g] = -INFINITY;
-    l_run[g] = 0.0f;
 #pragma unroll
-    for (int j = 0; j < DPL; j++) acc[g][j] = 0.0f;
+    for (int j = 0; j < VD; j++) acc[g][j] = 0.0f;
   }
+  bool ok = true;
+  float *pw = p_w[warp];
 
-  for (int64_t c0 = s0; c0 < s1; c0 += kSub) {
-    const int n = (int)(s1 - c0 < kSub ? s1 - c0 : kSub);
-    // Phase 1: scores, one position per thread, K streamed 8 dims at a time.
-    if (tid < n) {
-      const int64_t s = c0 + tid;
-      float dot[kMaxG];
-#pragma unroll
-      for (int g = 0; g < kMaxG; g++) dot[g] = 0.0f;
-      const bool fresh = s == pos;
-      const int64_t e = fresh ? 0 : kv_elem(a.kv, a.layer, h, s);
-#pragma unroll 4
-      for (int j = 0; j < HD / 8; j++) {
-        float kr[8];
-        if (fresh) {
-#pragma unroll
-          for (int k = 0; k < 8; k++) kr[k] = kn_s[j * 8 + k];
-        } else if (F16) {
-          uint4 v = *((const uint4 *)((const __half *)a.kv.k + e) + j);
-          const __half2 *hv = (const __half2 *)&v;
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            float2 f = __half22float2(hv[k]);
-            kr[2 * k] = f.x;
-            kr[2 * k + 1] = f.y;
-          }
-        } else {
-          const float4 *fp = (const float4 *)((const float *)a.kv.k + e) + 2 * j;
-          float4 v0 = fp[0], v1 = fp[1];
-          kr[0] = v0.x; kr[1] = v0.y; kr[2] = v0.z; kr[3] = v0.w;
-          kr[4] = v1.x; kr[5] = v1.y; kr[6] = v1.z; kr[7] = v1.w;
-        }
-#pragma unroll
-        for (int g = 0; g < kMaxG; g++) {
-          if (g < G) {
-#pragma unroll
-            for (int k = 0; k < 8; k++) dot[g] = fmaf(q_s[g][j * 8 + k], kr[k], dot[g]);
-          }
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < kMaxG; g++)
-        if (g < G) p_s[g][tid] = __fmul_rn(dot[g], a.scale);
-    }
-    __syncthreads();
-    // Phase 2: chunk max per head, rescale factors, probabilities.
-    float cm[kMaxG];
-#pragma unroll
-    for (int g = 0; g < kMaxG; g++) {
-      float v = (g < G && tid < n) ? p_s[g][tid] : -INFINITY;
-      cm[g] = warp_max(v);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int g = 0; g < kMaxG; g++) red_s[warp][g] = cm[g];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < kMaxG; g++) {
-      float mx = fmaxf(fmaxf(red_s[0][g], red_s[1][g]), fmaxf(red_s[2][g], red_s[3][g]));
-      float mn = fmaxf(m_run[g], mx);
-      float al = (m_run[g] == -INFINITY) ? 0.0f : expf(m_run[g] - mn);
-      if (tid == 0 && g < G) alpha_s[g] = al;
-      m_run[g] = mn;
-      cm[g] = mn;
-    }
-    __syncthreads();
-    float ps[kMaxG];
-#pragma unroll
-    for (int g = 0; g < kMaxG; g++) {
-      float p = 0.0f;
-      if (g < G && tid < n) {
-        p = expf(p_s[g][tid] - cm[g]);
-        p_s[g][tid] = p;
-      }
-      ps[g] = warp_sum(p);
-    }
-    __syncthreads();
-    if (lane == 0) {
-#pragma unroll
-      for (int g = 0; g < kMaxG; g++) red_s[warp][g] = ps[g];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < kMaxG; g++) {
-      if (g < G) {
-        float al = alpha_s[g];
-        l_run[g] = l_run[g] * al + ((red_s[0][g] + red_s[1][g]) + (red_s[2][g] + red_s[3][g]));
-#pragma unroll
-        for (int j = 0; j < DPL; j++) acc[g][j] *= al;
-      }
-    }
-    // Phase 3: P.V, warp w takes positions w, w+4, ...; lane owns DPL dims.
-    for (int t = warp; t < n; t += 4) {
-      const int64_t s = c0 + t;
-      float vr[DPL];
-      if (s == pos) {
-#pragma unroll
-        for (int j = 0; j < DPL; j++) vr[j] = vn_s[lane * DPL + j];
-      } else {
-        int64_t e = kv_elem(a.kv, a.layer, h, s) + lane * DPL;
+  for (int k = 0; k < nt; k++) {
+    const int st = k % kStages;
+    if (!mbar_wait_bounded(&bars[st], (uint32_t)((k / kStages) & 1))) ok = false;
+    const int64_t t0 = s0 + (int64_t)k * TP;
+    const int n = (int)(s1 - t0 < TP ? s1 - t0 : TP);
+    char *Ks = ring + st * kStageBytes;
+    char *Vs = Ks + TP * Gm::ROW;
+    if (own_pos && pos >= t0 && pos < t0 + n) {
+      const int j = (int)(pos - t0);
+      for (int d = tid; d < HD; d += kAttnThreads) {
         if (F16) {
-          const __half2 *vp = (const __half2 *)((const __half *)a.kv.v + e);
-#pragma unroll
-          for (int j = 0; j < DPL / 2; j++) {
-            float2 f = __half22float2(vp[j]);
-            vr[2 * j] = f.x;
-            vr[2 * j + 1] = f.y;
-          }
+          ((__half *)(Ks + j * Gm::ROW))[d] = __float2half_rn(kn_s[d]);
+          ((__half *)(Vs + j * Gm::ROW))[d] = __float2half_rn(vn_s[d]);
         } else {
-          const float2 *vp = (const float2 *)((const float *)a.kv.v + e);
-#pragma unroll
-          for (int j = 0; j < DPL / 2; j++) {
-            float2 f = vp[j];
-            vr[2 * j] = f.x;
-            vr[2 * j + 1] = f.y;
-          }
+          ((float *)(Ks + j * Gm::ROW))[d] = kn_s[d];
+          ((float *)(Vs + j * Gm::ROW))[d] = vn_s[d];
         }
       }
-#pragma unroll
-      for (int g = 0; g < kMaxG; g++) {
-        if (g < G) {
-          float p = p_s[g][t];
-#pragma unroll
-          for (int j = 0; j < DPL; j++) acc[g][j] = fmaf(p, vr[j], acc[g][j]);
-        }
-      }
+      __syncthreads();
     }
-    __syncthreads();
+    // Scores of this warp's TPW positions.
+    float mt[GP];
+#pragma unroll
+    for (int g = 0; g < GP; g++) mt[g] = -INFINITY;
+#pragma unroll
+    for (int sp = 0; sp < TPW / PPS; sp++) {
+      const int jl = sp * PPS + grp;  // position within the warp's share
+      const int j = warp * TPW + jl;  // position within the tile
+      float d[GP];
+#pragma unroll
+      for (int g = 0; g < GP; g++) d[g] = 0.0f;
+      if (j < n) {
+        float kv[DPL];
+        load_vals<F16, DPL>(Ks + j * Gm::ROW + c * 16, kv);
+#pragma unroll
+        for (int g = 0; g < GP; g++)
+#pragma unroll
+          for (int e = 0; e < DPL; e++) d[g] = fmaf(qr[g][e], kv[e], d[g]);
+      }
+#pragma unroll
+      for (int o = 1; o < LG; o <<= 1)
+#pragma unroll
+        for (int g = 0; g < GP; g++) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
+      float mine = -INFINITY;
+#pragma unroll
+      for (int g = 0; g < GP; g++) {
+        const float sc = j < n ? __fmul_rn(d[g], a.scale) : -INFINITY;
+        mt[g] = fmaxf(mt[g], sc);
+        if (g == c) mine = sc;
+      }
+      if (c < GP) pw[jl * GP + c] = mine;
+    }
+#pragma unroll
+    for (int o = LG; o < 32; o <<= 1)
+#pragma unroll
+      for (int g = 0; g < GP; g++) mt[g] = fmaxf(mt[g], __shfl_xor_sync(0xffffffffu, mt[g], o));
+    float alpha[GP], mg = -INFINITY, ag = 0.0f;
+#pragma unroll
+    for (int g = 0; g < GP; g++) {
+      const float mn = fmaxf(m_run[g], mt[g]);
+      alpha[g] = m_run[g] == -INFINITY ? 0.0f : expf(m_run[g] - mn);
+      m_run[g] = mn;
+      if (g == lane % GP) { mg = mn; ag = alpha[g]; }
+    }
+    __syncwarp();
+    // Probabilities (entry e = position * GP + head; head = lane % GP).
+    float ls = 0.0f;
+#pragma unroll
+    for (int e = lane; e < TPW * GP; e += 32) {
+      const float sv = pw[e];
+      const float p = sv == -INFINITY ? 0.0f : expf(sv - mg);
+      pw[e] = p;
+      ls += p;
+    }
+#pragma unroll
+    for (int o = GP; o < 32; o <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    l_lane = l_lane * ag + ls;
+#pragma unroll
+    for (int g = 0; g < GP; g++)
+#pragma unroll
+      for (int j = 0; j < VD; j++) acc[g][j] *= alpha[g];
+    __syncwarp();
+    // P.V over this warp's positions; lane owns dims lane*VD ...
+#pragma unroll 4
+    for (int jl = 0; jl < TPW; jl++) {
+      const int j = warp * TPW + jl;
+      if (j >= n) break;
+      float v[VD];
+      load_vals<F16, VD>(Vs + j * Gm::ROW + lane * VD * Gm::ES, v);
+      float p[GP];
+#pragma unroll
+      for (int g = 0; g < GP; g++) p[g] = pw[jl * GP + g];
+#pragma unroll
+      for (int g = 0; g < GP; g++)
+#pragma unroll
+        for (int e = 0; e < VD; e++) acc[g][e] = fmaf(p[g], v[e], acc[g][e]);
+    }
+    __syncthreads();  // every warp is done with this stage
+    if (tid == 0 && k + kStages < nt) {
+      fence_proxy_async();
+      const int64_t t1 = s0 + (int64_t)(k + kStages) * TP;
+      const int n1 = (int)(s1 - t1 < TP ? s1 - t1 : TP);
+      issue_tile<HD, F16>(a, Ks, &bars[st], t1, n1, h);
+    }
+  }
+  if (!ok) {
+    if (a.err) atomicOr(a.err, kErrAttnWait);
+    // Give copies that may still be in flight a bounded chance to land
+    // before the ring is reused.
+    for (int k = nt > kStages ? nt - kStages : 0; k < nt; k++)
+      mbar_wait_bounded(&bars[k % kStages], (uint32_t)((k / kStages) & 1));
   }
 
-  // Reduce the 4 warps' accumulators into acc_s[0]: this CTA's partial.
+  // Merge the warps: partials in the (now idle) ring.
+  float *acc_w = (float *)ring;               // [W][GP][HD]
+  float *m_w = acc_w + kAttnWarps * GP * HD;  // [W][GP]
+  float *l_w = m_w + kAttnWarps * GP;         // [W][GP]
 #pragma unroll
-  for (int g = 0; g < kMaxG; g++)
-    if (g < G) {
+  for (int g = 0; g < GP; g++)
 #pragma unroll
-      for (int j = 0; j < DPL; j++) acc_s[warp][g][lane * DPL + j] = acc[g][j];
-    }
-  if (tid < G) {
-    float mg = -INFINITY, lg = 0.0f;
+    for (int j = 0; j < VD; j++) acc_w[(warp * GP + g) * HD + lane * VD + j] = acc[g][j];
+  if (lane < GP) {
+    float mm = -INFINITY;
 #pragma unroll
-    for (int g = 0; g < kMaxG; g++)
-      if (g == tid) { mg = m_run[g]; lg = l_run[g]; }
-    ml_s[0][tid] = mg;
-    ml_s[1][tid] = lg;
+    for (int g = 0; g < GP; g++)
+      if (g == lane) mm = m_run[g];
+    m_w[warp * GP + lane] = mm;
+    l_w[warp * GP + lane] = l_lane;
   }
   __syncthreads();
-  for (int i = tid; i < G * HD; i += kAttnThreads) {
-    int g = i / HD, d = i % HD;
-    acc_s[0][g][d] = (acc_s[0][g][d] + acc_s[1][g][d]) + (acc_s[2][g][d] + acc_s[3][g][d]);
+  if (tid < GP) {
+    float M = -INFINITY;
+    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, m_w[w * GP + tid]);
+    float l = 0.0f;
+    for (int w = 0; w < kAttnWarps; w++) {
+      const float mw = m_w[w * GP + tid];
+      const float wt = mw == -INFINITY ? 0.0f : expf(mw - M);
+      wm_s[w][tid] = wt;
+      l = fmaf(wt, l_w[w * GP + tid], l);
+    }
+    ml_s[0][tid] = M;
+    ml_s[1][tid] = l;
+  }
+  __syncthreads();
+  for (int i = tid; i < GP * HD; i += kAttnThreads) {
+    const int g = i / HD;
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) s = fmaf(wm_s[w][g], acc_w[(w * GP) * HD + i], s);
+    acc_s[g][i % HD] = s;
   }
   cluster.sync();
   // Merge the cluster's partials through distributed shared memory:
-  // out = sum_r e^(m_r - M) acc_r / sum_r e^(m_r - M) l_r.  Every remote
-  // read of a phase is issued independently (one DSMEM round trip each).
-  if (tid < cs * G) {
-    const int r = tid / G, g = tid % G;
+  // out = sum_r e^(m_r - M) acc_r / sum_r e^(m_r - M) l_r.
+  if (tid < cs * GP) {
+    const int r = tid / GP, g = tid % GP;
     wgt_s[r][g] = cluster.map_shared_rank(&ml_s[0][0], r)[g];
-    p_s[g][r] = cluster.map_shared_rank(&ml_s[1][0], r)[g];  // l_r, staged in p_s (free now)
+    lsum_s[r][g] = cluster.map_shared_rank(&ml_s[1][0], r)[g];
   }
   __syncthreads();
-  if (tid < G) {
+  if (tid < GP) {
     float M = -INFINITY;
     for (int r = 0; r < cs; r++) M = fmaxf(M, wgt_s[r][tid]);
     float den = 0.0f;
@@ -288,19 +439,19 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
       const float mr = wgt_s[r][tid];
       const float w = mr == -INFINITY ? 0.0f : expf(mr - M);
       wgt_s[r][tid] = w;
-      den = fmaf(w, p_s[tid][r], den);
+      den = fmaf(w, lsum_s[r][tid], den);
     }
     den_s[tid] = den;
   }
   __syncthreads();
   // Rank r finalises 32-blocks r, r + cs, ... of this head group and
   // quantizes them (QuantizedActQ8; head boundaries are 32-aligned).
-  for (int bi = rank + warp * cs; bi < G * HD / 32; bi += 4 * cs) {
+  for (int bi = rank + warp * cs; bi < G * HD / 32; bi += kAttnWarps * cs) {
     const int e = bi * 32 + lane, g = e / HD, d = e % HD;
     float part[kMaxClusterCtas];
 #pragma unroll
     for (int r = 0; r < kMaxClusterCtas; r++)
-      part[r] = r < cs ? cluster.map_shared_rank(&acc_s[0][0][0], r)[g * HD + d] : 0.0f;
+      part[r] = r < cs ? cluster.map_shared_rank(&acc_s[0][0], r)[g * HD + d] : 0.0f;
     float num = 0.0f;
 #pragma unroll
     for (int r = 0; r < kMaxClusterCtas; r++)
@@ -316,28 +467,31 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(const AttnDecodeAr
   }
   // Keep this CTA's shared memory alive until every rank has read it.
   cluster.sync();
-  pdl_trigger();
 }
 
-template <int HD, bool F16>
-void launch_decode_t(const AttnDecodeArgs &a, cudaStream_t s) {
-  auto kern = k_attn_decode<HD, F16>;
-  const int cs = a.n_splits;
-  if (cs > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(a.kv.n_kv * cs));
-  cfg.blockDim = dim3(kAttnThreads);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = a.pdl ? 2 : 1;
-  cudaLaunchKernelEx(&cfg, kern, a);
+template <int HD, bool F16, int GP>
+const void *decode_fn() {
+  return (const void *)k_attn_decode<HD, F16, GP>;
+}
+
+const void *pick_decode(int hd, int f16, int G) {
+  const int gp = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+#define JAL_PICK(HDV, F, GPV) \
+  if (hd == HDV && (f16 != 0) == F && gp == GPV) return decode_fn<HDV, F, GPV>();
+  JAL_PICK(128, true, 1) JAL_PICK(128, true, 2) JAL_PICK(128, true, 4) JAL_PICK(128, true, 8)
+  JAL_PICK(128, false, 1) JAL_PICK(128, false, 2) JAL_PICK(128, false, 4) JAL_PICK(128, false, 8)
+  JAL_PICK(64, true, 1) JAL_PICK(64, true, 2) JAL_PICK(64, true, 4) JAL_PICK(64, true, 8)
+  JAL_PICK(64, false, 1) JAL_PICK(64, false, 2) JAL_PICK(64, false, 4) JAL_PICK(64, false, 8)
+#undef JAL_PICK
+  return nullptr;
+}
+
+constexpr size_t kDecodeSmem = (size_t)kStages * kStageBytes;
+
+void prepare_decode_fn(const void *fn, int cs) {
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDecodeSmem);
+  cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (cs > 8) cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
 
 // ---- prefill: bias + RoPE + KV append -------------------------------------
@@ -474,21 +628,38 @@ __global__ void __launch_bounds__(128) k_attn_prefill(const AttnPrefillArgs a) {
 }  // namespace
 
 void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s) {
-  const bool f16 = a.kv.f16;
-  if (a.kv.head_dim == 128) {
-    if (f16) launch_decode_t<128, true>(a, s);
-    else launch_decode_t<128, false>(a, s);
-  } else {
-    if (f16) launch_decode_t<64, true>(a, s);
-    else launch_decode_t<64, false>(a, s);
-  }
+  const int G = (int)(a.n_heads_q / a.kv.n_kv);
+  const void *fn = pick_decode((int)a.kv.head_dim, a.kv.f16, G);
+  if (!fn) return;
+  const int cs = a.n_splits;
+  prepare_decode_fn(fn, cs);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(a.kv.n_kv * cs));
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = kDecodeSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 2 : 1;
+  void *args[] = {(void *)&a};
+  cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-int attn_decode_cluster_size(int head_dim, int f16, int want) {
+int attn_decode_cluster_size(int head_dim, int f16, int G, int want) {
+  const void *fn = pick_decode(head_dim, f16, G);
+  if (!fn) return 0;
   for (int cs = want; cs >= 1; cs /= 2) {
+    prepare_decode_fn(fn, cs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cs);
     cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = kDecodeSmem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = (unsigned)cs;
@@ -496,11 +667,8 @@ int attn_decode_cluster_size(int head_dim, int f16, int want) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    const void *kern = head_dim == 128 ? (f16 ? (const void *)k_attn_decode<128, true> : (const void *)k_attn_decode<128, false>)
-                                       : (f16 ? (const void *)k_attn_decode<64, true> : (const void *)k_attn_decode<64, false>);
-    if (cs > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) return cs;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n > 0) return cs;
     cudaGetLastError();
   }
   return 1;

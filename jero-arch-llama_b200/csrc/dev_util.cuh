@@ -77,6 +77,20 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Programmatic dependent launch controls (no-ops without the attribute).
+// Bulk prefetch of [p, p + bytes) into L2 by the copy engine (no registers or
+// shared memory held).  p must be 16-byte aligned; bytes is rounded down to a
+// multiple of 16 and split into pieces of at most 1 GiB.
+__device__ __forceinline__ void l2_prefetch_bulk(const void *p, uint64_t bytes) {
+  const char *c = (const char *)p;
+  bytes &= ~(uint64_t)15;
+  while (bytes) {
+    const uint32_t n = bytes > (1u << 30) ? (1u << 30) : (uint32_t)bytes;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
+    c += n;
+    bytes -= n;
+  }
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -52,6 +52,7 @@ struct GemvArgs {
   int64_t up_offset = 0;        // SWIGLU: physical row offset of the up half
   int grid = 0;                 // CTAs (0 = auto)
   int pdl = 0;                  // launch with programmatic dependent launch
+  int64_t pf_bytes = -1;        // L2 prefetch budget per CTA (-1 = default)
 };
 
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
@@ -129,11 +130,13 @@ struct AttnDecodeArgs {
   float *out = nullptr;         // [n_heads_q * head_dim]
   int8_t *out_q = nullptr;      // quantized out (QuantizedActQ8)
   float *out_s = nullptr;
+  int *err = nullptr;           // error word: bit 2 = a bounded copy wait gave up
   int pdl = 0;
 };
 void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
-// Largest cluster size (<= want) the decode attention kernel can run with.
-int attn_decode_cluster_size(int head_dim, int f16, int want);
+// Largest cluster size (<= want) the decode attention kernel can run with
+// for head_dim, KV element type and G query heads per KV head.
+int attn_decode_cluster_size(int head_dim, int f16, int G, int want);
 
 // Prefill: bias + RoPE on q/k rows, append k/v of m tokens into the cache.
 struct RopeAppendArgs {

@@ -7,14 +7,18 @@
 // (exactly the sum of the reference's two dot16 partials); the f32 order of
 // the accumulation differs from the reference's sequential loop.
 //
-// Structure: one persistent CTA of WARPS warps per SM; warp w of CTA c owns
-// logical rows gw, gw + nw, ... (gw = c*WARPS + w, nw = WARPS*grid).  A row is
-// streamed in chunks of 32*U blocks (lane l loads blocks l, l+32, ... with
-// 16-byte loads that do not allocate in L1), DEPTH chunks in flight per warp.
-// The first DEPTH chunks are loaded before griddepcontrol.wait, so weight
-// traffic starts while the previous kernel drains.  The activation prologue
-// (optionally RMSNorm, then the QuantizedActQ8 quantizer) writes per-block
-// int8 halves, the f32 scale and the 32-element int sum into shared memory.
+// Structure: one persistent CTA of WARPS warps per SM owns a contiguous
+// range of rows (balanced to within one row); warp w of the CTA takes rows
+// r0 + w, r0 + w + WARPS, ...  A row is streamed in chunks of 32*U blocks
+// (lane l loads blocks l, l+32, ... with 16-byte loads that do not allocate
+// in L1), DEPTH chunks in flight per warp.  Before griddepcontrol.wait the
+// CTA asks the copy engine to prefetch the first pf_bytes of its rows into
+// L2 (cp.async.bulk.prefetch.L2) and loads its first DEPTH chunks, so weight
+// traffic starts while the previous kernel drains; afterwards each warp keeps
+// its own L2 prefetch a fixed number of rows ahead.  The
+// activation prologue (optionally RMSNorm, then the QuantizedActQ8
+// quantizer) writes per-block int8 halves, the f32 scale and the 32-element
+// int sum into shared memory.
 //
 // Per block and token the inner loop is 3 shared loads, 8 LOP3, 8 IDP4A,
 // a shift and two integer adds, one half->float, one I2F, FMUL and FFMA:
@@ -121,9 +125,6 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
       }
     }
   }
-  if (a.in_mode == GEMV_IN_NORM) {
-    for (int i = tid; i < K / 4; i += T) ((float4 *)normw)[i] = ((const float4 *)a.norm_w)[i];
-  }
   __syncthreads();
   float inv_norm[M];
 #pragma unroll
@@ -163,6 +164,15 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
     if (lane == 0) put_scale_sum(base, nbp, b, scale, s);
   }
   __syncthreads();
+}
+
+// Norm weights are static, so they are staged before griddepcontrol.wait.
+template <int M, int WARPS>
+__device__ void gemv_prologue_pre(const GemvArgs &a, char *smem, int nb, int nbp) {
+  if (a.in_mode != GEMV_IN_NORM) return;
+  const int K = nb * 32;
+  float *normw = (float *)(smem + act_bytes(nbp) * M) + M * K;
+  for (int i = threadIdx.x; i < K / 4; i += WARPS * 32) ((float4 *)normw)[i] = ((const float4 *)a.norm_w)[i];
 }
 
 template <int QUANT>
@@ -241,7 +251,7 @@ __device__ __forceinline__ float swiglu_one(float g, float u) {
   return __fmul_rn(__fmul_rn(g, sig), u);
 }
 
-// Position in a warp's chunk sequence: logical row index i (rows gw + i*nw),
+// Position in a warp's chunk sequence: logical row index i (row gw + i*WARPS),
 // unit (0 = the row itself or the gate half, 1 = the up half) and part (the
 // chunk of 32*U blocks within the row).  Advanced by increments only.
 struct Cursor {
@@ -255,29 +265,47 @@ struct Cursor {
 };
 
 template <int QUANT, int M, int OUT, int WARPS, int DEPTH>
-__global__ void __launch_bounds__(WARPS * 32, 1) k_gemv(const GemvArgs a) {
+__global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv(const GemvArgs a) {
   extern __shared__ __align__(16) char smem[];
   __shared__ float red[33];
   constexpr int U = ChunkRegs<QUANT>::U;
   constexpr int UNITS = OUT == GEMV_OUT_SWIGLU ? 2 : 1;
   const int nb = (int)(a.w.cols / 32), nbp = (nb + 3) & ~3;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int64_t gw = (int64_t)blockIdx.x * WARPS + warp, nw = (int64_t)gridDim.x * WARPS;
   const int parts = (nb + 32 * U - 1) / (32 * U);
-  const int my_rows = gw < a.rows ? (int)((a.rows - 1 - gw) / nw + 1) : 0;
+  // Contiguous, balanced row range [r0, r0 + cnt) of this CTA.
+  const int64_t base = a.rows / gridDim.x, rem = a.rows % gridDim.x;
+  const int64_t r0 = (int64_t)blockIdx.x * base + ((int64_t)blockIdx.x < rem ? blockIdx.x : rem);
+  const int64_t cnt = base + ((int64_t)blockIdx.x < rem ? 1 : 0);
+  const int my_rows = cnt > warp ? (int)((cnt - 1 - warp) / WARPS + 1) : 0;
+  const int64_t gw = r0 + warp;  // row of logical index i is gw + i * WARPS
+  const int64_t qrow = a.w.qs_stride, drow = a.w.d_stride * 2;
+  // L2 prefetch distance in rows per warp, from the per-CTA prefetch budget.
+  int pd = (int)(a.pf_bytes / (UNITS * (qrow + drow) * WARPS));
+  if (pd < 1) pd = 1;
+  if (threadIdx.x == 0 && a.pf_bytes > 0) {
+    const int64_t pr = cnt < (int64_t)pd * WARPS ? cnt : (int64_t)pd * WARPS;
+#pragma unroll
+    for (int u = 0; u < UNITS; u++) {
+      const int64_t rr = r0 + (u ? a.up_offset : 0);
+      l2_prefetch_bulk(a.w.qs + rr * qrow, (uint64_t)(pr * qrow));
+      l2_prefetch_bulk((const char *)a.w.d + rr * drow, (uint64_t)(pr * drow));
+    }
+  }
 
   Cursor ld, cp;  // next chunk to load / to compute
   ChunkRegs<QUANT> buf[DEPTH];
 #pragma unroll
   for (int k = 0; k < DEPTH; k++) {
     if (ld.i < my_rows) {
-      load_chunk<QUANT>(a.w, gw + ld.i * nw + (ld.unit ? a.up_offset : 0), ld.part, nb, lane, buf[k]);
+      load_chunk<QUANT>(a.w, gw + ld.i * WARPS + (ld.unit ? a.up_offset : 0), ld.part, nb, lane, buf[k]);
       ld.next(parts, UNITS);
     }
   }
+  gemv_prologue_pre<M, WARPS>(a, smem, nb, nbp);
   pdl_wait();
-  gemv_prologue<M, WARPS>(a, smem, nb, nbp, red);
   pdl_trigger();
+  gemv_prologue<M, WARPS>(a, smem, nb, nbp, red);
 
   float acc0[M], acc1[M];
 #pragma unroll
@@ -300,11 +328,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_gemv(const GemvArgs a) {
           }
         }
         if (ld.i < my_rows) {
-          load_chunk<QUANT>(a.w, gw + ld.i * nw + (ld.unit ? a.up_offset : 0), ld.part, nb, lane, buf[k]);
+          load_chunk<QUANT>(a.w, gw + ld.i * WARPS + (ld.unit ? a.up_offset : 0), ld.part, nb, lane, buf[k]);
           ld.next(parts, UNITS);
         }
+        if (cp.part == 0 && cp.unit == 0 && lane == 0 && a.pf_bytes > 0 && cp.i + pd < my_rows) {
+          const int64_t pr = gw + (int64_t)(cp.i + pd) * WARPS;
+#pragma unroll
+          for (int u = 0; u < UNITS; u++) {
+            const int64_t rr = pr + (u ? a.up_offset : 0);
+            l2_prefetch_bulk(a.w.qs + rr * qrow, (uint64_t)qrow);
+            l2_prefetch_bulk((const char *)a.w.d + rr * drow, (uint64_t)drow);
+          }
+        }
         if (cp.part == parts - 1 && cp.unit == UNITS - 1) {
-          const int64_t lr = gw + cp.i * nw;
+          const int64_t lr = gw + (int64_t)cp.i * WARPS;
           float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
           for (int t = 0; t < M; t++) {
@@ -331,12 +368,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_gemv(const GemvArgs a) {
   }
 }
 
-// Launch shapes: (warps per CTA, chunks in flight per warp).
-constexpr int kWarpsA = 16, kDepthA = 3;  // 128 registers / thread
-constexpr int kWarpsB = 32, kDepthB = 2;  // 64 registers / thread
+// Launch shapes: (warps per CTA, chunks in flight per warp).  The default
+// is one 16-warp CTA per SM; JAL_GEMV_SHAPE=B selects 8-warp CTAs (<= 128
+// registers) that leave room on each SM for a CTA of the next kernel, which
+// measured slower on B200 for the Llama-3-8B decode shapes.
+constexpr int kWarpsA = 16, kDepthA = 3;
+constexpr int kWarpsB = 8, kDepthB = 3;
+constexpr int64_t kDefaultPrefetchBytes = 96 * 1024;
 
 int g_shape = -1;  // 0 = A, 1 = B
 int g_sm_count = 0;
+int64_t g_pf_bytes = -1;
 
 int shape() {
   if (g_shape < 0) {
@@ -344,6 +386,14 @@ int shape() {
     g_shape = (e && *e == 'B') ? 1 : 0;
   }
   return g_shape;
+}
+
+int64_t prefetch_bytes() {
+  if (g_pf_bytes < 0) {
+    const char *e = getenv("JAL_GEMV_PF_KB");
+    g_pf_bytes = e ? (int64_t)atoll(e) * 1024 : kDefaultPrefetchBytes;
+  }
+  return g_pf_bytes;
 }
 
 template <int QUANT, int M, int OUT, int WARPS, int DEPTH>
@@ -376,17 +426,19 @@ void launch_m(const GemvArgs &a, int grid, cudaStream_t s) {
 
 template <int QUANT, int OUT>
 void launch_q(const GemvArgs &a, int grid, cudaStream_t s) {
-  if (shape() == 1 && a.m <= 2) launch_m<QUANT, OUT, kWarpsB, kDepthB>(a, grid, s);
+  if (shape() == 1) launch_m<QUANT, OUT, kWarpsB, kDepthB>(a, grid, s);
   else launch_m<QUANT, OUT, kWarpsA, kDepthA>(a, grid, s);
 }
 
 template <int QUANT, int OUT, int WARPS, int DEPTH>
 void set_attrs() {
   const int lim = kGemvMaxSmem;
-  cudaFuncSetAttribute(k_gemv<QUANT, 1, OUT, WARPS, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  cudaFuncSetAttribute(k_gemv<QUANT, 2, OUT, WARPS, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  cudaFuncSetAttribute(k_gemv<QUANT, 4, OUT, WARPS, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-  cudaFuncSetAttribute(k_gemv<QUANT, 8, OUT, WARPS, DEPTH>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  const void *fns[4] = {(const void *)k_gemv<QUANT, 1, OUT, WARPS, DEPTH>, (const void *)k_gemv<QUANT, 2, OUT, WARPS, DEPTH>,
+                        (const void *)k_gemv<QUANT, 4, OUT, WARPS, DEPTH>, (const void *)k_gemv<QUANT, 8, OUT, WARPS, DEPTH>};
+  for (const void *f : fns) {
+    cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  }
 }
 
 template <int WARPS, int DEPTH>
@@ -421,7 +473,7 @@ int gemv_default_grid(const GemvArgs &a) {
     cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (g_sm_count <= 0) g_sm_count = 148;
   }
-  const int warps = (shape() == 1 && a.m <= 2) ? kWarpsB : kWarpsA;
+  const int warps = shape() == 1 ? kWarpsB : kWarpsA;
   int64_t need = (a.rows + warps - 1) / warps;
   int64_t cap = (int64_t)g_sm_count;
   return (int)(need < cap ? need : cap);
@@ -434,6 +486,7 @@ void launch_gemv(const GemvArgs &a0, cudaStream_t s) {
   // Token counts between template sizes run the next larger instantiation;
   // token slots t >= m quantize to zero and are never written.
   int grid = a.grid > 0 ? a.grid : gemv_default_grid(a);
+  if (a.pf_bytes < 0) a.pf_bytes = prefetch_bytes();
   if (a.w.quant == JAL_Q4_0) {
     if (a.out_mode == GEMV_OUT_STORE) launch_q<JAL_Q4_0, GEMV_OUT_STORE>(a, grid, s);
     else if (a.out_mode == GEMV_OUT_ADD) launch_q<JAL_Q4_0, GEMV_OUT_ADD>(a, grid, s);

@@ -829,7 +829,7 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   }
   // Decode buffers.
   const int sms = sm_count();
-  ctx->n_splits = attn_decode_cluster_size((int)g.head_dim, kv.f16, n_ctx >= 512 ? 16 : 4);
+  ctx->n_splits = attn_decode_cluster_size((int)g.head_dim, kv.f16, (int)(g.n_heads_q / g.n_heads_kv), n_ctx >= 512 ? 16 : 4);
   ctx->am_blocks = sms;
   size_t f32s = H + (Q + 2 * KV) + Q + Q / 32 + F + (F + 31) / 32 + V + sms;
   size_t bytes = f32s * 4 + Q + ((F + 31) / 32) * 32 + 4096 + (F / 32 + 1) * 4 + 64 + (size_t)sms * 4 + (n_ctx + 2) * 4 +
@@ -905,7 +905,7 @@ void Context::enqueue_decode_step(bool pdl) {
     aa.kv = kv; aa.layer = (int64_t)l; aa.d_pos = d_pos; aa.window = (int64_t)cfg.sliding_window;
     aa.scale = 1.0f / sqrtf((float)g.head_dim);
     aa.n_splits = n_splits;
-    aa.out = attn; aa.out_q = attn_q; aa.out_s = attn_s; aa.pdl = pdl;
+    aa.out = attn; aa.out_q = attn_q; aa.out_s = attn_s; aa.err = d_err; aa.pdl = pdl;
     launch_attn_decode(aa, stream);
     GemvArgs oa;
     oa.w = L.wo.dm; oa.rows = (int64_t)H; oa.m = 1; oa.in_mode = GEMV_IN_Q8;

@@ -311,7 +311,7 @@ __global__ void k_embed(const uint8_t *__restrict__ emb, int quant, int64_t hidd
   uint32_t tok = tokens[blockIdx.x];
   float *o = out + (int64_t)blockIdx.x * hidden;
   if (tok >= vocab) {
-    if (threadIdx.x == 0 && err_flag) atomicExch(err_flag, 1);
+    if (threadIdx.x == 0 && err_flag) atomicOr(err_flag, 1);
     for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) o[i] = 0.0f;
     if (pdl) pdl_trigger();
     return;
