@@ -92,6 +92,22 @@ int jal_cached_matrix_export_ref_layout(const jal_cached_matrix *m,
  * repack_cache.rs:390-422) and compute y[m, rows].  Device pointers. */
 int jal_cached_matrix_gemm(const jal_cached_matrix *mat, const float *x,
                            size_t m, float *y, void *stream);
+/* Same result as jal_cached_matrix_gemm, for callers that cannot allocate
+ * device memory while they run: a process whose free device memory belongs
+ * to another allocator's pool, or a serving loop that must not call
+ * cudaMalloc/cudaFree because they can synchronise the whole device.  No
+ * counterpart in the reference.  The quantized activations are kept in one
+ * fixed 2 MiB device array that the library holds on every GPU where its
+ * kernels are loaded, until the process exits; the call allocates nothing.
+ * Limit: round_up(m*cols, 256) + m*(cols/32)*4 <= 2097152 bytes (cols=4096:
+ * m <= 455), else JAL_ERR_TENSOR_BOUNDS and no work.  The first call on a
+ * device looks up the array's device address (done once per device, with
+ * that device current); make that first call before any stream capture.
+ * The work is only enqueued on `stream` (no synchronisation): every call
+ * shares the array, so calls whose GPU work can overlap (other streams,
+ * other threads) race; calls on one stream are ordered and safe. */
+int jal_cached_matrix_gemm_noalloc(const jal_cached_matrix *mat, const float *x,
+                                   size_t m, float *y, void *stream);
 /* CachedMatrix::gemv_with_act_view (repack_cache.rs:1636-1672) with an
  * already quantized activation (q8: cols int8, scales: cols/32 f32). */
 int jal_cached_matrix_gemv_q8(const jal_cached_matrix *mat, const int8_t *q8,

@@ -121,6 +121,7 @@ _SIGS = {
     "jal_cached_matrix_aligned_bytes": (_SZ, [_P]),
     "jal_cached_matrix_export_ref_layout": (C.c_int, [_P, _P, _SZ, _P, _SZ]),
     "jal_cached_matrix_gemm": (C.c_int, [_P, _P, _SZ, _P, _P]),
+    "jal_cached_matrix_gemm_noalloc": (C.c_int, [_P, _P, _SZ, _P, _P]),
     "jal_cached_matrix_gemv_q8": (C.c_int, [_P, _P, _P, _P, _P]),
     "jal_cached_matrix_dot16_partials": (C.c_int, [_P, _P, _SZ, _SZ, _P, _P]),
     "jal_act_quantize_q8": (C.c_int, [_P, _SZ, _SZ, _P, _P, _P]),
@@ -287,6 +288,12 @@ class CachedMatrix:
     def gemm(self, x, m: int, y, stream=None) -> None:
         """project_batch (repack_cache.rs:1724): y[m, rows] = quant(x[m, cols]) . W^T."""
         _check(lib().jal_cached_matrix_gemm(self._h, _ptr(x), m, _ptr(y), _stream(stream)))
+
+    def gemm_noalloc(self, x, m: int, y, stream=None) -> None:
+        """Like gemm, but allocates no device memory: the activation scratch is a
+        fixed 2 MiB device array shared by every call (calls that overlap on the
+        GPU race); the work is only enqueued on the stream."""
+        _check(lib().jal_cached_matrix_gemm_noalloc(self._h, _ptr(x), m, _ptr(y), _stream(stream)))
 
     def gemv_q8(self, q8, scales, y, stream=None) -> None:
         """gemv_with_act_view (repack_cache.rs:1636) with a quantized activation."""

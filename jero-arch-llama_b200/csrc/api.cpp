@@ -152,6 +152,17 @@ int jal_cached_matrix_gemm(const jal_cached_matrix *mat, const float *x, size_t 
   });
 }
 
+int jal_cached_matrix_gemm_noalloc(const jal_cached_matrix *mat, const float *x, size_t m, float *y, void *stream) {
+  return guard([&] {
+    NEED(mat);
+    NEED(x);
+    NEED(y);
+    if (m == 0) return;
+    check_block_scaled(mat);
+    gemm_noalloc(mat->m.dm, x, (int64_t)m, y, as_stream(stream));
+  });
+}
+
 int jal_cached_matrix_gemv_q8(const jal_cached_matrix *mat, const int8_t *q8, const float *scales, float *y,
                               void *stream) {
   return guard([&] {

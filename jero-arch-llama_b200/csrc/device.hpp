@@ -94,6 +94,10 @@ struct GemmArgs {
 };
 void launch_gemm(const GemmArgs &a, cudaStream_t s);
 
+// Quantize-then-project with the activation scratch in a fixed file-scope
+// device array (noalloc.cu) instead of a per-call allocation.
+void gemm_noalloc(const DevMat &w, const float *x, int64_t m, float *y, cudaStream_t s);
+
 // ---- elementwise / attention ---------------------------------------------
 void launch_rope_rows(float *qk, int64_t m, int64_t row_len, int64_t head_dim, int64_t rotary_dim, int neox,
                       int64_t pos0, const float *inv_freq, cudaStream_t s);

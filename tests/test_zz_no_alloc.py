@@ -1,0 +1,84 @@
+"""The allocation-free GEMM entry point (needs a B200).
+
+jal_cached_matrix_gemm_noalloc exists for callers that cannot allocate device
+memory while they run: a process whose free device memory already belongs to
+another allocator's pool, or a serving loop that must not call
+cudaMalloc/cudaFree because they can synchronise the whole device.  It keeps
+the quantized activations in a fixed 2 MiB device array instead of a per-call
+buffer.  These tests call it through the C ABI, twice in a row on one stream
+(so the second call runs over what the first left in the shared array), and
+compare each result with jal_cached_matrix_gemm within the device-kernel
+tolerance (max|y - y_ref| / max|y_ref| <= 1e-3).
+
+The file is named so that pytest collects it last.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-3
+SCRATCH_BYTES = 2 << 20
+
+
+def rel_err(got, ref):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def _dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
+def test_noalloc_gemm_matches_gemm_on_two_calls(jal, torch_cuda, quant_name):
+    torch = torch_cuda
+    quant = getattr(jal, quant_name)
+    rows, cols = 1000, 4096
+    raw = jal.synth_matrix(quant, rows, cols, seed=31, name="noalloc")
+    mat = jal.CachedMatrix.repack(raw, quant, rows, cols)
+    lib = jal.lib()
+    # First call: 40 tokens (tiled GEMM path); second: 3 tokens (GEMV path)
+    # with different activations over the array the first call filled.
+    cases = [(40, jal.synth_normal(40 * cols, seed=32, name="noalloc.a")),
+             (3, 5.0 * jal.synth_normal(3 * cols, seed=33, name="noalloc.b"))]
+    xs = [_dev(torch, x) for _, x in cases]
+    outs = [torch.full((m * rows,), float("nan"), dtype=torch.float32, device="cuda") for m, _ in cases]
+    torch.cuda.synchronize()
+    for (m, _), x, y in zip(cases, xs, outs):
+        rc = lib.jal_cached_matrix_gemm_noalloc(mat._h, x.data_ptr(), m, y.data_ptr(), None)
+        assert rc == 0, lib.jal_last_error().decode()
+    torch.cuda.synchronize()
+    for (m, _), x, y in zip(cases, xs, outs):
+        want = torch.zeros(m * rows, dtype=torch.float32, device="cuda")
+        rc = lib.jal_cached_matrix_gemm(mat._h, x.data_ptr(), m, want.data_ptr(), None)
+        assert rc == 0, lib.jal_last_error().decode()
+        torch.cuda.synchronize()
+        got, ref = y.cpu().numpy(), want.cpu().numpy()
+        assert np.all(np.isfinite(got))
+        for t in range(m):
+            assert rel_err(got[t * rows:(t + 1) * rows], ref[t * rows:(t + 1) * rows]) <= REL_TOL
+
+
+def test_noalloc_gemm_rejects_oversize(jal, torch_cuda):
+    torch = torch_cuda
+    rows, cols = 64, 4096
+    raw = jal.synth_matrix(jal.Q4_0, rows, cols, seed=34, name="noalloc.big")
+    mat = jal.CachedMatrix.repack(raw, jal.Q4_0, rows, cols)
+    # 456 tokens x 4096 cols needs 456*4096 + 456*128*4 bytes > 2 MiB.
+    m = 456
+    assert m * cols + m * (cols // 32) * 4 > SCRATCH_BYTES
+    x = torch.zeros(m * cols, dtype=torch.float32, device="cuda")
+    y = torch.full((m * rows,), 7.0, dtype=torch.float32, device="cuda")
+    lib = jal.lib()
+    rc = lib.jal_cached_matrix_gemm_noalloc(mat._h, x.data_ptr(), m, y.data_ptr(), None)
+    assert rc == jal.ERR_TENSOR_BOUNDS
+    assert "scratch" in lib.jal_last_error().decode()
+    torch.cuda.synchronize()
+    assert bool(torch.all(y == 7.0))
+    # The largest size that fits still runs.
+    m_ok = 455
+    rc = lib.jal_cached_matrix_gemm_noalloc(mat._h, x.data_ptr(), m_ok, y.data_ptr(), None)
+    assert rc == 0, lib.jal_last_error().decode()
+    torch.cuda.synchronize()
