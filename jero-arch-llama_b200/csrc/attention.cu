@@ -29,7 +29,6 @@ constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxClusterCtas = 16;  // CTAs per KV head (one cluster)
 constexpr int kStages = 3;           // shared-memory ring of K/V tiles
 constexpr int kStageBytes = 32 * 1024;
-constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polls
 constexpr int kErrAttnWait = 2;            // bit set in the context error word
 
 __device__ __forceinline__ int64_t kv_elem(const KvView &kv, int64_t layer, int64_t h, int64_t pos) {
@@ -49,38 +48,6 @@ __device__ __forceinline__ void rot(float &x0, float &x1, float c, float s) {
   x0 = a;
   x1 = b;
 }
-
-// ---- mbarrier / bulk-copy helpers (shared::cta barrier, own-CTA destination)
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Polls at most kWaitLimit times; false when the wait gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-  for (uint32_t it = 0; it < kWaitLimit; it++)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Tile geometry for head_dim HD and KV element type.
 template <int HD, bool F16>

@@ -1,14 +1,15 @@
 // Device-side data layout shared by the host orchestration and the kernels.
 //
-// HBM layout of a repacked quantized matrix (B200 layout):
-//   qs : rows x qs_stride bytes.  Q4_0: the 16 nibble bytes of each GGUF
-//        block back to back (byte i = elem i | elem i+16 << 4), so a row is
-//        cols/2 bytes and every block starts on a 16-byte boundary.  Q8_0:
-//        the 32 int8 of each block back to back (cols bytes per row).
-//   d  : rows x d_stride f16 bit patterns, one per 32-block, with d_stride
-//        rounded up to a multiple of 8 (16 bytes) so every row starts
-//        16-byte aligned.  Decoded with the reference's f16_to_f32_finite.
-// Weight bytes therefore stay at 4.5 (Q4_0) / 8.5 (Q8_0) bits per weight.
+// HBM layout of a repacked quantized matrix (B200 layout), row-interleaved:
+// row r occupies qs_stride bytes at qs + r * qs_stride:
+//   quants: Q4_0 the 16 nibble bytes of each GGUF block back to back (byte i
+//           = elem i | elem i+16 << 4), cols/2 bytes; Q8_0 the 32 int8 of each
+//           block back to back, cols bytes.  Every block starts 16-byte aligned.
+//   scales: right after the quants (d = qs + quant bytes, d_stride = qs_stride
+//           / 2 halves per row), one f16 bit pattern per 32-block, padded to a
+//           multiple of 8 (16 bytes), sanitized at repack (f16_to_f32_finite).
+// A contiguous range of rows is therefore one contiguous byte range (one
+// bulk copy); weight bytes stay at 4.5 (Q4_0) / 8.5 (Q8_0) bits per weight.
 #pragma once
 
 #include <cstdint>
@@ -22,8 +23,8 @@ struct DevMat {
   const uint8_t *qs = nullptr;
   const uint16_t *d = nullptr;
   const float *dense = nullptr;  // dense f32 rows (cols stride), float types
-  int64_t qs_stride = 0;  // bytes per row
-  int64_t d_stride = 0;   // f16 scales per row (multiple of 8)
+  int64_t qs_stride = 0;  // bytes per row (quants + scales)
+  int64_t d_stride = 0;   // row stride of d in halves (qs_stride / 2)
 };
 
 inline int64_t d_stride_for(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }

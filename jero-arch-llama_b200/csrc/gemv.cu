@@ -39,33 +39,42 @@ namespace jal {
 
 namespace {
 
-// Shared-memory activation layout for token t (nbp = nb rounded up to 4):
+// Shared-memory activation layout for token t (nbp = nb rounded up to 32,
+// the padding blocks zero):
 //   [lo: nbp x 16 B][hi: nbp x 16 B][scale, sum32: nbp x 8 B]
 // followed, for f32 inputs, by a staging copy of the f32 activations
 // (M x K floats) and, for RMSNorm inputs, the norm weights (K floats).
 __host__ __device__ inline size_t act_bytes(int nbp) { return (size_t)nbp * 40; }
 __host__ __device__ inline size_t smem_bytes(int in_mode, int M, int nb) {
-  const int nbp = (nb + 3) & ~3;
+  const int nbp = (nb + 31) & ~31;
   size_t b = act_bytes(nbp) * M;
   if (in_mode != GEMV_IN_Q8) b += (size_t)M * nb * 32 * 4;
   if (in_mode == GEMV_IN_NORM) b += (size_t)nb * 32 * 4;
   return b;
 }
 
-template <int WARPS>
+// Barrier over the first NT threads: __syncthreads for BAR 0, else the named
+// barrier BAR (for kernels where some warps skip the activation prologue).
+template <int BAR, int NT>
+__device__ __forceinline__ void group_sync() {
+  if constexpr (BAR == 0) __syncthreads();
+  else asm volatile("bar.sync %0, %1;" ::"n"(BAR), "n"(NT) : "memory");
+}
+
+template <int WARPS, int BAR = 0>
 __device__ float block_reduce_sum(float v, float *red) {
   v = warp_sum(v);
   int w = threadIdx.x / 32, l = threadIdx.x % 32;
   if (l == 0) red[w] = v;
-  __syncthreads();
+  group_sync<BAR, WARPS * 32>();
   if (w == 0) {
     float t = l < WARPS ? red[l] : 0.0f;
     t = warp_sum(t);
     if (l == 0) red[32] = t;
   }
-  __syncthreads();
+  group_sync<BAR, WARPS * 32>();
   float r = red[32];
-  __syncthreads();
+  group_sync<BAR, WARPS * 32>();
   return r;
 }
 
@@ -76,11 +85,20 @@ __device__ __forceinline__ void put_scale_sum(char *base, int nbp, int b, float 
 // All global reads of the prologue are issued as independent wide loads
 // (one memory latency), then the per-block quantization runs from shared
 // memory.
-template <int M, int WARPS>
+template <int M, int WARPS, int BAR = 0>
 __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, float *red) {
   constexpr int T = WARPS * 32;
   const int K = nb * 32, tid = threadIdx.x;
   const int warp = tid / 32, lane = tid % 32;
+  if (nbp > nb) {  // padding blocks: zero quants, zero scale and sum
+    for (int i = tid; i < M * (nbp - nb); i += T) {
+      const int t = i / (nbp - nb), b = nb + i % (nbp - nb);
+      char *base = smem + t * act_bytes(nbp);
+      ((uint4 *)base)[b] = make_uint4(0, 0, 0, 0);
+      ((uint4 *)(base + nbp * 16))[b] = make_uint4(0, 0, 0, 0);
+      put_scale_sum(base, nbp, b, 0.0f, 0);
+    }
+  }
   if (a.in_mode == GEMV_IN_Q8) {
     for (int i = tid; i < M * nb * 2; i += T) {
       const int t = i / (2 * nb), j = i % (2 * nb);
@@ -89,7 +107,7 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
       char *base = smem + t * act_bytes(nbp) + (j & 1) * nbp * 16;
       ((uint4 *)base)[j >> 1] = v;
     }
-    __syncthreads();
+    group_sync<BAR, WARPS * 32>();
     for (int i = tid; i < M * nb; i += T) {
       const int t = i / nb, b = i % nb;
       char *base = smem + t * act_bytes(nbp);
@@ -104,7 +122,7 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
       s = dp4a_ss(hi.w, 0x01010101, s);
       put_scale_sum(base, nbp, b, t < a.m ? a.xs[t * (a.xq_stride / 32) + b] : 0.0f, s);
     }
-    __syncthreads();
+    group_sync<BAR, WARPS * 32>();
     return;
   }
   float *stage = (float *)(smem + act_bytes(nbp) * M);
@@ -125,13 +143,13 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
       }
     }
   }
-  __syncthreads();
+  group_sync<BAR, WARPS * 32>();
   float inv_norm[M];
 #pragma unroll
   for (int t = 0; t < M; t++) {
     inv_norm[t] = 1.0f;
     if (a.in_mode == GEMV_IN_NORM && t < a.m) {
-      float tot = block_reduce_sum<WARPS>(ss[t], red);
+      float tot = block_reduce_sum<WARPS, BAR>(ss[t], red);
       inv_norm[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
     }
   }
@@ -163,7 +181,7 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (lane == 0) put_scale_sum(base, nbp, b, scale, s);
   }
-  __syncthreads();
+  group_sync<BAR, WARPS * 32>();
 }
 
 // Norm weights are static, so they are staged before griddepcontrol.wait.
@@ -270,7 +288,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv(const GemvArgs 
   __shared__ float red[33];
   constexpr int U = ChunkRegs<QUANT>::U;
   constexpr int UNITS = OUT == GEMV_OUT_SWIGLU ? 2 : 1;
-  const int nb = (int)(a.w.cols / 32), nbp = (nb + 3) & ~3;
+  const int nb = (int)(a.w.cols / 32), nbp = (nb + 31) & ~31;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int parts = (nb + 32 * U - 1) / (32 * U);
   // Contiguous, balanced row range [r0, r0 + cnt) of this CTA.
@@ -368,6 +386,169 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv(const GemvArgs 
   }
 }
 
+// ---- 4096-column fast path (M = 1) ------------------------------------------
+//
+// Every decode projection of a 4096-wide model except the down projection
+// has 128 blocks per row.  Lane l owns blocks 4l .. 4l+3 of every row: its
+// quants are one contiguous 64-byte (Q4_0) / 128-byte (Q8_0) piece read with
+// 32-byte loads, its four scales one 8-byte load, and its four blocks of the
+// quantized activation stay in registers for the whole kernel.  A row costs
+// the loads, 4 block dots and one warp reduction; DEPTH rows are in flight
+// per warp (issued before griddepcontrol.wait for the first ones).
+constexpr int kW4Blocks = 128;
+
+template <int QUANT>
+struct W4Row {
+  static constexpr int NQ = QUANT == JAL_Q4_0 ? 16 : 32;  // u32 of quants per lane
+  uint32_t q[NQ];
+  uint2 d;  // four f16 scales
+};
+
+template <int QUANT>
+__device__ __forceinline__ void w4_load(const DevMat &w, int64_t row, int lane, W4Row<QUANT> &r) {
+  constexpr int NQ = W4Row<QUANT>::NQ;
+  const uint8_t *q = w.qs + row * w.qs_stride + (size_t)lane * NQ * 4;
+#pragma unroll
+  for (int j = 0; j < NQ / 8; j++) ldg_stream32(q + 32 * j, &r.q[8 * j]);
+  r.d = ldg_stream8(w.d + row * w.d_stride + lane * 4);
+}
+
+struct W4Act {
+  int4 lo[4], hi[4];
+  float sc[4];
+  int sum[4];
+};
+
+template <int QUANT>
+__device__ __forceinline__ float w4_dot(const W4Row<QUANT> &r, const W4Act &x) {
+  const __half2 d01 = *reinterpret_cast<const __half2 *>(&r.d.x);
+  const __half2 d23 = *reinterpret_cast<const __half2 *>(&r.d.y);
+  const float ws[4] = {__low2float(d01), __high2float(d01), __low2float(d23), __high2float(d23)};
+  float acc = 0.0f;
+#pragma unroll
+  for (int v = 0; v < 4; v++) {
+    int dot;
+    if constexpr (QUANT == JAL_Q4_0) {
+      const uint32_t *w = &r.q[4 * v];
+      int d0 = dp4a_us(w[0] & 0x0F0F0F0Fu, x.lo[v].x, 0);
+      int d1 = dp4a_us(w[0] & 0xF0F0F0F0u, x.hi[v].x, 0);
+      d0 = dp4a_us(w[1] & 0x0F0F0F0Fu, x.lo[v].y, d0);
+      d1 = dp4a_us(w[1] & 0xF0F0F0F0u, x.hi[v].y, d1);
+      d0 = dp4a_us(w[2] & 0x0F0F0F0Fu, x.lo[v].z, d0);
+      d1 = dp4a_us(w[2] & 0xF0F0F0F0u, x.hi[v].z, d1);
+      d0 = dp4a_us(w[3] & 0x0F0F0F0Fu, x.lo[v].w, d0);
+      d1 = dp4a_us(w[3] & 0xF0F0F0F0u, x.hi[v].w, d1);
+      dot = d0 + (d1 >> 4) - 8 * x.sum[v];  // nibble n encodes n - 8
+    } else {
+      const uint32_t *w = &r.q[8 * v];
+      int d0 = dp4a_ss((int)w[0], x.lo[v].x, 0);
+      int d1 = dp4a_ss((int)w[4], x.hi[v].x, 0);
+      d0 = dp4a_ss((int)w[1], x.lo[v].y, d0);
+      d1 = dp4a_ss((int)w[5], x.hi[v].y, d1);
+      d0 = dp4a_ss((int)w[2], x.lo[v].z, d0);
+      d1 = dp4a_ss((int)w[6], x.hi[v].z, d1);
+      d0 = dp4a_ss((int)w[3], x.lo[v].w, d0);
+      d1 = dp4a_ss((int)w[7], x.hi[v].w, d1);
+      dot = d0 + d1;
+    }
+    acc = fmaf(__int2float_rn(dot), x.sc[v] * ws[v], acc);
+  }
+  return acc;
+}
+
+template <int QUANT, int OUT, int WARPS, int DEPTH>
+__global__ void __launch_bounds__(WARPS * 32, 1) k_gemv_w4(const GemvArgs a) {
+  extern __shared__ __align__(16) char smem[];
+  __shared__ float red[33];
+  constexpr int UNITS = OUT == GEMV_OUT_SWIGLU ? 2 : 1;
+  constexpr int nb = kW4Blocks, nbp = kW4Blocks;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int64_t base = a.rows / gridDim.x, rem = a.rows % gridDim.x;
+  const int64_t r0 = (int64_t)blockIdx.x * base + ((int64_t)blockIdx.x < rem ? blockIdx.x : rem);
+  const int64_t cnt = base + ((int64_t)blockIdx.x < rem ? 1 : 0);
+  const int my_rows = cnt > warp ? (int)((cnt - 1 - warp) / WARPS + 1) : 0;
+  const int64_t gw = r0 + warp;
+  const int total = my_rows * UNITS;  // unit k: row index k / UNITS, half k % UNITS
+  auto unit_row = [&](int k) -> int64_t {
+    return gw + (int64_t)(k / UNITS) * WARPS + ((UNITS == 2 && (k & 1)) ? a.up_offset : 0);
+  };
+
+  W4Row<QUANT> buf[DEPTH];
+#pragma unroll
+  for (int j = 0; j < DEPTH; j++)
+    if (j < total) w4_load<QUANT>(a.w, unit_row(j), lane, buf[j]);
+  gemv_prologue_pre<1, WARPS>(a, smem, nb, nbp);
+  pdl_wait();
+  pdl_trigger();
+  gemv_prologue<1, WARPS>(a, smem, nb, nbp, red);
+  W4Act x;
+#pragma unroll
+  for (int v = 0; v < 4; v++) {
+    const int b = 4 * lane + v;
+    x.lo[v] = ((const int4 *)smem)[b];
+    x.hi[v] = ((const int4 *)(smem + nbp * 16))[b];
+    const float2 ss = ((const float2 *)(smem + nbp * 32))[b];
+    x.sc[v] = ss.x;
+    x.sum[v] = __float_as_int(ss.y);
+  }
+
+  float gate = 0.0f;
+  for (int k0 = 0; k0 < total; k0 += DEPTH) {
+#pragma unroll
+    for (int j = 0; j < DEPTH; j++) {
+      const int k = k0 + j;
+      if (k < total) {
+        float s = w4_dot<QUANT>(buf[j], x);
+        if (k + DEPTH < total) w4_load<QUANT>(a.w, unit_row(k + DEPTH), lane, buf[j]);
+        s = warp_sum(s);
+        if (UNITS == 2 && (k & 1) == 0) {
+          gate = s;
+        } else if (lane == 0) {
+          const int64_t lr = gw + (int64_t)(k / UNITS) * WARPS;
+          float *yp = a.y + lr;
+          if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
+          else if (OUT == GEMV_OUT_ADD) *yp = *yp + (a.bias ? s + a.bias[lr] : s);
+          else *yp = swiglu_one(gate, s);
+        }
+      }
+    }
+  }
+}
+
+constexpr int kW4Warps = 16;
+
+template <int QUANT, int OUT>
+void launch_w4_t(const GemvArgs &a, int grid, cudaStream_t s) {
+  constexpr int DEPTH = QUANT == JAL_Q4_0 ? 3 : 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kW4Warps * 32);
+  cfg.dynamicSmemBytes = smem_bytes(a.in_mode, 1, kW4Blocks);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, k_gemv_w4<QUANT, OUT, kW4Warps, DEPTH>, a);
+}
+
+template <int QUANT, int OUT>
+void set_w4_attrs() {
+  constexpr int DEPTH = QUANT == JAL_Q4_0 ? 3 : 2;
+  const void *f = (const void *)k_gemv_w4<QUANT, OUT, kW4Warps, DEPTH>;
+  cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem);
+}
+
+int g_use_w4 = -1;
+bool use_w4() {
+  if (g_use_w4 < 0) {
+    const char *e = getenv("JAL_GEMV_KERNEL");
+    g_use_w4 = (e && e[0] == 'c') ? 0 : 1;
+  }
+  return g_use_w4 != 0;
+}
+
 // Launch shapes: (warps per CTA, chunks in flight per warp).  The default
 // is one 16-warp CTA per SM; JAL_GEMV_SHAPE=B selects 8-warp CTAs (<= 128
 // registers) that leave room on each SM for a CTA of the next kernel, which
@@ -458,6 +639,12 @@ void gemv_init() {
   if (done) return;
   set_attrs_all<kWarpsA, kDepthA>();
   set_attrs_all<kWarpsB, kDepthB>();
+  set_w4_attrs<JAL_Q4_0, GEMV_OUT_STORE>();
+  set_w4_attrs<JAL_Q4_0, GEMV_OUT_ADD>();
+  set_w4_attrs<JAL_Q4_0, GEMV_OUT_SWIGLU>();
+  set_w4_attrs<JAL_Q8_0, GEMV_OUT_STORE>();
+  set_w4_attrs<JAL_Q8_0, GEMV_OUT_ADD>();
+  set_w4_attrs<JAL_Q8_0, GEMV_OUT_SWIGLU>();
   done = true;
 }
 
@@ -485,8 +672,24 @@ void launch_gemv(const GemvArgs &a0, cudaStream_t s) {
   GemvArgs a = a0;
   // Token counts between template sizes run the next larger instantiation;
   // token slots t >= m quantize to zero and are never written.
-  int grid = a.grid > 0 ? a.grid : gemv_default_grid(a);
   if (a.pf_bytes < 0) a.pf_bytes = prefetch_bytes();
+  if (use_w4() && a.m == 1 && a.w.cols == 32 * kW4Blocks) {
+    int sms = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = a.grid > 0 ? a.grid : (int)(a.rows < sms ? a.rows : sms);
+    if (a.w.quant == JAL_Q4_0) {
+      if (a.out_mode == GEMV_OUT_STORE) launch_w4_t<JAL_Q4_0, GEMV_OUT_STORE>(a, grid, s);
+      else if (a.out_mode == GEMV_OUT_ADD) launch_w4_t<JAL_Q4_0, GEMV_OUT_ADD>(a, grid, s);
+      else launch_w4_t<JAL_Q4_0, GEMV_OUT_SWIGLU>(a, grid, s);
+    } else {
+      if (a.out_mode == GEMV_OUT_STORE) launch_w4_t<JAL_Q8_0, GEMV_OUT_STORE>(a, grid, s);
+      else if (a.out_mode == GEMV_OUT_ADD) launch_w4_t<JAL_Q8_0, GEMV_OUT_ADD>(a, grid, s);
+      else launch_w4_t<JAL_Q8_0, GEMV_OUT_SWIGLU>(a, grid, s);
+    }
+    return;
+  }
+  int grid = a.grid > 0 ? a.grid : gemv_default_grid(a);
   if (a.w.quant == JAL_Q4_0) {
     if (a.out_mode == GEMV_OUT_STORE) launch_q<JAL_Q4_0, GEMV_OUT_STORE>(a, grid, s);
     else if (a.out_mode == GEMV_OUT_ADD) launch_q<JAL_Q4_0, GEMV_OUT_ADD>(a, grid, s);

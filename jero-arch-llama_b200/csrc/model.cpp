@@ -394,20 +394,21 @@ void repack_stacked(const std::vector<const uint8_t *> &raws, const std::vector<
   parts.clear();
   if (device_quant(quant)) {
     if (cols % 32) fail(JAL_ERR_TENSOR_BOUNDS, "cols %llu not a multiple of 32", (unsigned long long)cols);
-    int64_t qs_stride = quant == JAL_Q4_0 ? (int64_t)cols / 2 : (int64_t)cols;
-    int64_t d_stride = d_stride_for((int64_t)cols);
-    DevBufferPtr qs = alloc((size_t)total * qs_stride), d = alloc((size_t)total * d_stride * 2);
-    JAL_CUDA(cudaMemsetAsync(d->ptr, 0, d->bytes, s));
-    storage.push_back(qs);
-    storage.push_back(d);
+    // Row-interleaved: each row is its quants then its padded f16 scales.
+    const int64_t nib = quant == JAL_Q4_0 ? (int64_t)cols / 2 : (int64_t)cols;
+    const int64_t row_bytes = nib + 2 * d_stride_for((int64_t)cols);
+    const int64_t qs_stride = row_bytes, d_stride = row_bytes / 2;
+    DevBufferPtr buf = alloc((size_t)total * row_bytes);
+    JAL_CUDA(cudaMemsetAsync(buf->ptr, 0, buf->bytes, s));
+    storage.push_back(buf);
     stacked = DevMat{};
     stacked.quant = quant; stacked.rows = (int64_t)total; stacked.cols = (int64_t)cols;
-    stacked.qs = qs->as<uint8_t>(); stacked.d = d->as<uint16_t>();
+    stacked.qs = buf->as<uint8_t>(); stacked.d = (const uint16_t *)(buf->as<uint8_t>() + nib);
     stacked.qs_stride = qs_stride; stacked.d_stride = d_stride;
     uint64_t r0 = 0;
     for (size_t i = 0; i < raws.size(); i++) {
-      launch_repack(raws[i], quant, (int64_t)rows[i], (int64_t)cols, qs->as<uint8_t>() + r0 * qs_stride,
-                    d->as<uint16_t>() + r0 * d_stride, qs_stride, d_stride, s);
+      launch_repack(raws[i], quant, (int64_t)rows[i], (int64_t)cols, buf->as<uint8_t>() + r0 * qs_stride,
+                    (uint16_t *)(buf->as<uint8_t>() + nib) + r0 * d_stride, qs_stride, d_stride, s);
       JAL_CUDA(cudaGetLastError());
       CachedMatrix m;
       m.quant = quant; m.rows = rows[i]; m.cols = cols;
@@ -415,7 +416,7 @@ void repack_stacked(const std::vector<const uint8_t *> &raws, const std::vector<
       m.dm.rows = (int64_t)rows[i];
       m.dm.qs = stacked.qs + r0 * qs_stride;
       m.dm.d = stacked.d + r0 * d_stride;
-      m.aligned_bytes = (size_t)rows[i] * (qs_stride + d_stride * 2);
+      m.aligned_bytes = (size_t)rows[i] * row_bytes;
       parts.push_back(m);
       r0 += rows[i];
     }
