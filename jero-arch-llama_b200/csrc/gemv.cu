@@ -42,13 +42,11 @@ namespace {
 // Shared-memory activation layout for token t (nbp = nb rounded up to 32,
 // the padding blocks zero):
 //   [lo: nbp x 16 B][hi: nbp x 16 B][scale, sum32: nbp x 8 B]
-// followed, for f32 inputs, by a staging copy of the f32 activations
-// (M x K floats) and, for RMSNorm inputs, the norm weights (K floats).
+// followed, for RMSNorm inputs, by the norm weights (K floats).
 __host__ __device__ inline size_t act_bytes(int nbp) { return (size_t)nbp * 40; }
 __host__ __device__ inline size_t smem_bytes(int in_mode, int M, int nb) {
   const int nbp = (nb + 31) & ~31;
   size_t b = act_bytes(nbp) * M;
-  if (in_mode != GEMV_IN_Q8) b += (size_t)M * nb * 32 * 4;
   if (in_mode == GEMV_IN_NORM) b += (size_t)nb * 32 * 4;
   return b;
 }
@@ -82,14 +80,16 @@ __device__ __forceinline__ void put_scale_sum(char *base, int nbp, int b, float 
   ((float2 *)(base + nbp * 32))[b] = make_float2(scale, __int_as_float(sum32));
 }
 
-// All global reads of the prologue are issued as independent wide loads
-// (one memory latency), then the per-block quantization runs from shared
-// memory.
+// One thread quantizes one whole 32-block (QuantizedActQ8: amax over the
+// block, scale = amax / 127, q = clamp(round(v * (1 / scale)))): no shuffle
+// chains, one barrier at the end (plus one block reduction for RMSNorm).
+// Inputs are read straight from global memory (L1-cached; the second pass
+// over a block hits L1); norm weights were staged in shared memory before
+// griddepcontrol.wait.
 template <int M, int WARPS, int BAR = 0>
 __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, float *red) {
   constexpr int T = WARPS * 32;
   const int K = nb * 32, tid = threadIdx.x;
-  const int warp = tid / 32, lane = tid % 32;
   if (nbp > nb) {  // padding blocks: zero quants, zero scale and sum
     for (int i = tid; i < M * (nbp - nb); i += T) {
       const int t = i / (nbp - nb), b = nb + i % (nbp - nb);
@@ -100,18 +100,17 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
     }
   }
   if (a.in_mode == GEMV_IN_Q8) {
-    for (int i = tid; i < M * nb * 2; i += T) {
-      const int t = i / (2 * nb), j = i % (2 * nb);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (t < a.m) v = *(const uint4 *)(a.xq + t * a.xq_stride + j * 16);
-      char *base = smem + t * act_bytes(nbp) + (j & 1) * nbp * 16;
-      ((uint4 *)base)[j >> 1] = v;
-    }
-    group_sync<BAR, WARPS * 32>();
     for (int i = tid; i < M * nb; i += T) {
       const int t = i / nb, b = i % nb;
       char *base = smem + t * act_bytes(nbp);
-      const int4 lo = ((const int4 *)base)[b], hi = ((const int4 *)(base + nbp * 16))[b];
+      int4 lo = make_int4(0, 0, 0, 0), hi = lo;
+      float sc = 0.0f;
+      if (t < a.m) {
+        const int4 *p = (const int4 *)(a.xq + t * a.xq_stride + b * 32);
+        lo = p[0];
+        hi = p[1];
+        sc = a.xs[t * (a.xq_stride / 32) + b];
+      }
       int s = dp4a_ss(lo.x, 0x01010101, 0);
       s = dp4a_ss(lo.y, 0x01010101, s);
       s = dp4a_ss(lo.z, 0x01010101, s);
@@ -120,66 +119,91 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
       s = dp4a_ss(hi.y, 0x01010101, s);
       s = dp4a_ss(hi.z, 0x01010101, s);
       s = dp4a_ss(hi.w, 0x01010101, s);
-      put_scale_sum(base, nbp, b, t < a.m ? a.xs[t * (a.xq_stride / 32) + b] : 0.0f, s);
+      ((int4 *)base)[b] = lo;
+      ((int4 *)(base + nbp * 16))[b] = hi;
+      put_scale_sum(base, nbp, b, sc, s);
     }
     group_sync<BAR, WARPS * 32>();
     return;
   }
-  float *stage = (float *)(smem + act_bytes(nbp) * M);
-  float *normw = stage + M * K;
-  float ss[M];
-#pragma unroll
-  for (int t = 0; t < M; t++) {
-    ss[t] = 0.0f;
-    if (t < a.m) {
-      const float4 *x4 = (const float4 *)(a.x + t * a.x_stride);
-      for (int i = tid; i < K / 4; i += T) {
-        float4 v = x4[i];
-        ((float4 *)(stage + t * K))[i] = v;
-        ss[t] = fmaf(v.x, v.x, ss[t]);
-        ss[t] = fmaf(v.y, v.y, ss[t]);
-        ss[t] = fmaf(v.z, v.z, ss[t]);
-        ss[t] = fmaf(v.w, v.w, ss[t]);
-      }
-    }
-  }
-  group_sync<BAR, WARPS * 32>();
+  const bool norm = a.in_mode == GEMV_IN_NORM;
+  const float *normw = (const float *)(smem + act_bytes(nbp) * M);
   float inv_norm[M];
 #pragma unroll
-  for (int t = 0; t < M; t++) {
-    inv_norm[t] = 1.0f;
-    if (a.in_mode == GEMV_IN_NORM && t < a.m) {
-      float tot = block_reduce_sum<WARPS, BAR>(ss[t], red);
-      inv_norm[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+  for (int t = 0; t < M; t++) inv_norm[t] = 1.0f;
+  if (norm) {
+    float ss[M];
+#pragma unroll
+    for (int t = 0; t < M; t++) ss[t] = 0.0f;
+    for (int b = tid; b < nb; b += T) {
+#pragma unroll
+      for (int t = 0; t < M; t++) {
+        if (t < a.m) {
+          const float4 *xp = (const float4 *)(a.x + t * a.x_stride + b * 32);
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            const float4 v = xp[j];
+            ss[t] = fmaf(v.x, v.x, ss[t]);
+            ss[t] = fmaf(v.y, v.y, ss[t]);
+            ss[t] = fmaf(v.z, v.z, ss[t]);
+            ss[t] = fmaf(v.w, v.w, ss[t]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < M; t++) {
+      if (t < a.m) {
+        const float tot = block_reduce_sum<WARPS, BAR>(ss[t], red);
+        inv_norm[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+      }
     }
   }
-  for (int wb = warp; wb < M * nb; wb += WARPS) {
-    const int t = wb / nb, b = wb % nb;
+  for (int i = tid; i < M * nb; i += T) {
+    const int t = i / nb, b = i % nb;
     char *base = smem + t * act_bytes(nbp);
-    int8_t q = 0;
-    float scale = 0.0f;
-    if (t < a.m) {
-      float v = stage[t * K + b * 32 + lane];
-      if (a.in_mode == GEMV_IN_NORM) {
-        float invn = inv_norm[0];
-#pragma unroll
-        for (int tt = 1; tt < M; tt++)
-          if (tt == t) invn = inv_norm[tt];
-        v = __fmul_rn(__fmul_rn(v, invn), normw[b * 32 + lane]);
-      }
-      if (!isfinite(v)) v = 0.0f;
-      float amax = warp_max(fabsf(v));
-      scale = act_scale_from_amax(amax);
-      q = act_quant_one(v, act_inv_from_scale(scale));
+    if (t >= a.m) {
+      ((uint4 *)base)[b] = make_uint4(0, 0, 0, 0);
+      ((uint4 *)(base + nbp * 16))[b] = make_uint4(0, 0, 0, 0);
+      put_scale_sum(base, nbp, b, 0.0f, 0);
+      continue;
     }
-    int8_t *lo = (int8_t *)base + b * 16;
-    int8_t *hi = (int8_t *)(base + nbp * 16) + b * 16;
-    if (lane < 16) lo[lane] = q;
-    else hi[lane - 16] = q;
-    int s = q;
+    float invn = inv_norm[0];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) put_scale_sum(base, nbp, b, scale, s);
+    for (int tt = 1; tt < M; tt++)
+      if (tt == t) invn = inv_norm[tt];
+    const float4 *xp = (const float4 *)(a.x + t * a.x_stride + b * 32);
+    const float4 *wp = (const float4 *)(normw + b * 32);
+    auto prep = [&](float v, float w) {
+      if (norm) v = __fmul_rn(__fmul_rn(v, invn), w);
+      return isfinite(v) ? v : 0.0f;
+    };
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float4 v = xp[j];
+      const float4 w = norm ? wp[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      amax = fmaxf(amax, fabsf(prep(v.x, w.x)));
+      amax = fmaxf(amax, fabsf(prep(v.y, w.y)));
+      amax = fmaxf(amax, fabsf(prep(v.z, w.z)));
+      amax = fmaxf(amax, fabsf(prep(v.w, w.w)));
+    }
+    const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
+    uint32_t packed[8];
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float4 v = xp[j];
+      const float4 w = norm ? wp[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int q0 = act_quant_one(prep(v.x, w.x), inv), q1 = act_quant_one(prep(v.y, w.y), inv);
+      const int q2 = act_quant_one(prep(v.z, w.z), inv), q3 = act_quant_one(prep(v.w, w.w), inv);
+      s += q0 + q1 + q2 + q3;
+      packed[j] = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+                  ((uint32_t)(q3 & 0xff) << 24);
+    }
+    ((uint4 *)base)[b] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    ((uint4 *)(base + nbp * 16))[b] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    put_scale_sum(base, nbp, b, scale, s);
   }
   group_sync<BAR, WARPS * 32>();
 }
@@ -189,7 +213,7 @@ template <int M, int WARPS>
 __device__ void gemv_prologue_pre(const GemvArgs &a, char *smem, int nb, int nbp) {
   if (a.in_mode != GEMV_IN_NORM) return;
   const int K = nb * 32;
-  float *normw = (float *)(smem + act_bytes(nbp) * M) + M * K;
+  float *normw = (float *)(smem + act_bytes(nbp) * M);
   for (int i = threadIdx.x; i < K / 4; i += WARPS * 32) ((float4 *)normw)[i] = ((const float4 *)a.norm_w)[i];
 }
 
