@@ -135,6 +135,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnDecod
   __shared__ __align__(8) uint64_t bars[kStages];
   __shared__ __align__(16) float q_s[GP][HD];
   __shared__ __align__(16) float kn_s[HD], vn_s[HD];
+  __shared__ float cs_s[2][HD / 2];  // RoPE cos / sin of this position
   __shared__ __align__(16) float p_w[kAttnWarps][TPW * GP];
   __shared__ __align__(16) float acc_s[GP][HD];  // this CTA's partial (unnormalised)
   __shared__ float ml_s[2][GP];                  // its max / denominator per head
@@ -166,55 +167,55 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnDecod
       issue_tile<HD, F16>(a, ring + k * kStageBytes, &bars[k], t0, n, h);
     }
   }
-  pdl_wait();
-  pdl_trigger();
-
-  // q / new k / new v of this head group (+ bias), then RoPE.
-  for (int i = tid; i < GP * HD; i += kAttnThreads) {
-    const int g = i / HD, d = i % HD;
-    float v = 0.0f;
-    if (g < G) {
-      const int64_t e = (int64_t)(h * G + g) * HD + d;
-      v = a.bq ? __fadd_rn(a.qkv[e], a.bq[e]) : a.qkv[e];
-    }
-    q_s[g][d] = v;
-  }
-  for (int d = tid; d < HD; d += kAttnThreads) {
-    const int64_t ek = (int64_t)h * HD + d;
-    kn_s[d] = a.bk ? __fadd_rn(a.qkv[Q + ek], a.bk[ek]) : a.qkv[Q + ek];
-    vn_s[d] = a.bv ? __fadd_rn(a.qkv[Q + KVD + ek], a.bv[ek]) : a.qkv[Q + KVD + ek];
-  }
-  __syncthreads();
-  if (!a.skip_rope && pos > 0) {
-    const int half = (int)(a.rotary_dim / 2);
+  // RoPE rows of this position (static tables) are staged before the wait.
+  const bool rope = !a.skip_rope && pos > 0;
+  const int half = (int)(a.rotary_dim / 2);
+  if (rope) {
     const bool use_long = a.long_threshold >= 0 && seq > a.long_threshold;
     const float *ct = (use_long ? a.cos_tab_long : a.cos_tab) + pos * half;
     const float *st = (use_long ? a.sin_tab_long : a.sin_tab) + pos * half;
-    for (int i = tid; i < (G + 1) * half; i += kAttnThreads) {
-      const int g = i / half, j = i % half;
-      float *row = g < G ? q_s[g] : kn_s;
-      const int i0 = a.neox ? j : 2 * j, i1 = a.neox ? j + half : 2 * j + 1;
-      float x0 = row[i0], x1 = row[i1];
-      rot(x0, x1, ct[j], st[j]);
-      row[i0] = x0;
-      row[i1] = x1;
-    }
-    __syncthreads();
-  }
-  // The stored (possibly f16-rounded) new k/v are what every later step
-  // reads, so this step uses the same values.
-  if (F16) {
-    for (int d = tid; d < HD; d += kAttnThreads) {
-      kn_s[d] = __half2float(__float2half_rn(kn_s[d]));
-      vn_s[d] = __half2float(__float2half_rn(vn_s[d]));
+    for (int j = tid; j < half; j += kAttnThreads) {
+      cs_s[0][j] = ct[j];
+      cs_s[1][j] = st[j];
     }
   }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+
+  // q / new k (+ bias, RoPE) and new v (+ bias) in one pass: each thread
+  // produces one element, reading its rotation partner directly
+  // (recipe.rs:2750-2767 for the rotation).  The stored (possibly
+  // f16-rounded) new k/v are what every later step reads, so this step uses
+  // the same values; the CTA holding the current position appends them.
   const bool own_pos = pos >= s0 && pos < s1;
-  if (own_pos) {  // append (recipe.rs:2319-2326)
-    const int64_t e = kv_elem(a.kv, a.layer, h, pos);
-    for (int d = tid; d < HD; d += kAttnThreads) {
-      store_kv(a.kv.k, a.kv.f16, e + d, kn_s[d]);
-      store_kv(a.kv.v, a.kv.f16, e + d, vn_s[d]);
+  const int64_t app = own_pos ? kv_elem(a.kv, a.layer, h, pos) : 0;
+  for (int i = tid; i < (GP + 2) * HD; i += kAttnThreads) {
+    const int g = i / HD, d = i % HD;  // g < GP: q head, GP: k, GP + 1: v
+    if (g < GP && g >= G) { q_s[g][d] = 0.0f; continue; }
+    const int64_t off = g < GP ? (int64_t)(h * G + g) * HD : (g == GP ? Q : Q + KVD) + (int64_t)h * HD;
+    const float *bias = g < GP ? a.bq : (g == GP ? a.bk : a.bv);
+    auto ld = [&](int dd) {
+      const float x = a.qkv[off + dd];
+      return bias ? __fadd_rn(x, bias[(g < GP ? (int64_t)(h * G + g) * HD : (int64_t)h * HD) + dd]) : x;
+    };
+    float o = ld(d);
+    if (rope && g <= GP && d < 2 * half) {
+      const bool first = a.neox ? d < half : (d & 1) == 0;
+      const int j = a.neox ? (first ? d : d - half) : d / 2;
+      const int partner = a.neox ? (first ? d + half : d - half) : (d ^ 1);
+      const float other = ld(partner);
+      const float c = cs_s[0][j], sn = cs_s[1][j];
+      const float x0 = first ? o : other, x1 = first ? other : o;
+      o = first ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+    if (g < GP) {
+      q_s[g][d] = o;
+    } else {
+      if (F16) o = __half2float(__float2half_rn(o));
+      if (g == GP) kn_s[d] = o;
+      else vn_s[d] = o;
+      if (own_pos) store_kv(g == GP ? a.kv.k : a.kv.v, a.kv.f16, app + d, o);  // append (recipe.rs:2319-2326)
     }
   }
   __syncthreads();

@@ -80,12 +80,11 @@ __device__ __forceinline__ void put_scale_sum(char *base, int nbp, int b, float 
   ((float2 *)(base + nbp * 32))[b] = make_float2(scale, __int_as_float(sum32));
 }
 
-// One thread quantizes one whole 32-block (QuantizedActQ8: amax over the
-// block, scale = amax / 127, q = clamp(round(v * (1 / scale)))): no shuffle
-// chains, one barrier at the end (plus one block reduction for RMSNorm).
-// Inputs are read straight from global memory (L1-cached; the second pass
-// over a block hits L1); norm weights were staged in shared memory before
-// griddepcontrol.wait.
+// Activation prologue (QuantizedActQ8 per 32-block: amax over the block,
+// scale = amax / 127, q = clamp(round(v * (1 / scale)))), written to shared
+// memory with the block's int sum; one barrier at the end (plus one block
+// reduction for RMSNorm).  Inputs are read straight from global memory; norm
+// weights were staged in shared memory before griddepcontrol.wait.
 template <int M, int WARPS, int BAR = 0>
 __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, float *red) {
   constexpr int T = WARPS * 32;
@@ -126,8 +125,11 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
     group_sync<BAR, WARPS * 32>();
     return;
   }
+  // f32 inputs: four lanes per 32-block (8 consecutive elements each; the
+  // block max and int sum combine over the 4-lane group with two shuffles).
   const bool norm = a.in_mode == GEMV_IN_NORM;
   const float *normw = (const float *)(smem + act_bytes(nbp) * M);
+  const int jobs = M * nb * 4, jobs_r = (jobs + 31) & ~31;  // whole warps per iteration
   float inv_norm[M];
 #pragma unroll
   for (int t = 0; t < M; t++) inv_norm[t] = 1.0f;
@@ -135,13 +137,13 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
     float ss[M];
 #pragma unroll
     for (int t = 0; t < M; t++) ss[t] = 0.0f;
-    for (int b = tid; b < nb; b += T) {
+    for (int i = tid; i < nb * 4; i += T) {
 #pragma unroll
       for (int t = 0; t < M; t++) {
         if (t < a.m) {
-          const float4 *xp = (const float4 *)(a.x + t * a.x_stride + b * 32);
+          const float4 *xp = (const float4 *)(a.x + t * a.x_stride + i * 8);
 #pragma unroll
-          for (int j = 0; j < 8; j++) {
+          for (int j = 0; j < 2; j++) {
             const float4 v = xp[j];
             ss[t] = fmaf(v.x, v.x, ss[t]);
             ss[t] = fmaf(v.y, v.y, ss[t]);
@@ -159,51 +161,60 @@ __device__ void gemv_prologue(const GemvArgs &a, char *smem, int nb, int nbp, fl
       }
     }
   }
-  for (int i = tid; i < M * nb; i += T) {
-    const int t = i / nb, b = i % nb;
-    char *base = smem + t * act_bytes(nbp);
-    if (t >= a.m) {
-      ((uint4 *)base)[b] = make_uint4(0, 0, 0, 0);
-      ((uint4 *)(base + nbp * 16))[b] = make_uint4(0, 0, 0, 0);
-      put_scale_sum(base, nbp, b, 0.0f, 0);
-      continue;
-    }
+  for (int i = tid; i < jobs_r; i += T) {
+    const bool valid = i < jobs;
+    const int blk = i >> 2, sub = i & 3;
+    const int t = valid ? blk / nb : 0, b = valid ? blk % nb : 0;
+    const bool live = valid && t < a.m;
     float invn = inv_norm[0];
 #pragma unroll
     for (int tt = 1; tt < M; tt++)
       if (tt == t) invn = inv_norm[tt];
-    const float4 *xp = (const float4 *)(a.x + t * a.x_stride + b * 32);
-    const float4 *wp = (const float4 *)(normw + b * 32);
-    auto prep = [&](float v, float w) {
-      if (norm) v = __fmul_rn(__fmul_rn(v, invn), w);
-      return isfinite(v) ? v : 0.0f;
-    };
+    float v[8];
+    if (live) {
+      const float4 *xp = (const float4 *)(a.x + t * a.x_stride + b * 32 + sub * 8);
+      const float4 x0 = xp[0], x1 = xp[1];
+      v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+      v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+      if (norm) {
+        const float4 *wp = (const float4 *)(normw + b * 32 + sub * 8);
+        const float4 w0 = wp[0], w1 = wp[1];
+        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(v[e], invn), w[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; e++)
+        if (!isfinite(v[e])) v[e] = 0.0f;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = 0.0f;
+    }
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const float4 v = xp[j];
-      const float4 w = norm ? wp[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-      amax = fmaxf(amax, fabsf(prep(v.x, w.x)));
-      amax = fmaxf(amax, fabsf(prep(v.y, w.y)));
-      amax = fmaxf(amax, fabsf(prep(v.z, w.z)));
-      amax = fmaxf(amax, fabsf(prep(v.w, w.w)));
-    }
+    for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(v[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
-    uint32_t packed[8];
-    int s = 0;
+    int q[8], s = 0;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const float4 v = xp[j];
-      const float4 w = norm ? wp[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-      const int q0 = act_quant_one(prep(v.x, w.x), inv), q1 = act_quant_one(prep(v.y, w.y), inv);
-      const int q2 = act_quant_one(prep(v.z, w.z), inv), q3 = act_quant_one(prep(v.w, w.w), inv);
-      s += q0 + q1 + q2 + q3;
-      packed[j] = (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
-                  ((uint32_t)(q3 & 0xff) << 24);
+    for (int e = 0; e < 8; e++) {
+      q[e] = act_quant_one(v[e], inv);
+      s += q[e];
     }
-    ((uint4 *)base)[b] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    ((uint4 *)(base + nbp * 16))[b] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-    put_scale_sum(base, nbp, b, scale, s);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (valid) {
+      char *base = smem + t * act_bytes(nbp);
+      const uint32_t p0 = (uint32_t)(q[0] & 0xff) | ((uint32_t)(q[1] & 0xff) << 8) | ((uint32_t)(q[2] & 0xff) << 16) |
+                          ((uint32_t)(q[3] & 0xff) << 24);
+      const uint32_t p1 = (uint32_t)(q[4] & 0xff) | ((uint32_t)(q[5] & 0xff) << 8) | ((uint32_t)(q[6] & 0xff) << 16) |
+                          ((uint32_t)(q[7] & 0xff) << 24);
+      // elements sub*8 .. sub*8+7: sub 0, 1 in the low 16 bytes, 2, 3 in the high
+      char *half = sub < 2 ? base + b * 16 : base + nbp * 16 + b * 16;
+      *(uint2 *)(half + (sub & 1) * 8) = make_uint2(p0, p1);
+      if (sub == 0) put_scale_sum(base, nbp, b, live ? scale : 0.0f, live ? s : 0);
+    }
   }
   group_sync<BAR, WARPS * 32>();
 }
@@ -497,14 +508,35 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_gemv_w4(const GemvArgs a) {
     return gw + (int64_t)(k / UNITS) * WARPS + ((UNITS == 2 && (k & 1)) ? a.up_offset : 0);
   };
 
+  // Before griddepcontrol.wait: either the copy engine prefetches the
+  // CTA's first pf_bytes into L2 (no load slots held, so the activation
+  // loads after the wait are not queued behind weight traffic), or, with
+  // pf_bytes == 0, the warps load their first DEPTH rows into registers.
   W4Row<QUANT> buf[DEPTH];
+  const bool l2_first = a.pf_bytes > 0;
+  if (l2_first) {
+    if (threadIdx.x == 0 && cnt > 0) {
+      int64_t pr = a.pf_bytes / (UNITS * a.w.qs_stride);
+      if (pr < 1) pr = 1;
+      if (pr > cnt) pr = cnt;
 #pragma unroll
-  for (int j = 0; j < DEPTH; j++)
-    if (j < total) w4_load<QUANT>(a.w, unit_row(j), lane, buf[j]);
+      for (int u = 0; u < UNITS; u++)
+        l2_prefetch_bulk(a.w.qs + (r0 + (u ? a.up_offset : 0)) * a.w.qs_stride, (uint64_t)(pr * a.w.qs_stride));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < DEPTH; j++)
+      if (j < total) w4_load<QUANT>(a.w, unit_row(j), lane, buf[j]);
+  }
   gemv_prologue_pre<1, WARPS>(a, smem, nb, nbp);
   pdl_wait();
   pdl_trigger();
   gemv_prologue<1, WARPS>(a, smem, nb, nbp, red);
+  if (l2_first) {
+#pragma unroll
+    for (int j = 0; j < DEPTH; j++)
+      if (j < total) w4_load<QUANT>(a.w, unit_row(j), lane, buf[j]);
+  }
   W4Act x;
 #pragma unroll
   for (int v = 0; v < 4; v++) {
@@ -541,8 +573,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_gemv_w4(const GemvArgs a) {
 
 constexpr int kW4Warps = 16;
 
+int64_t g_w4_pf = -1;
+int64_t w4_prefetch_bytes() {
+  if (g_w4_pf < 0) {
+    const char *e = getenv("JAL_W4_PF_KB");
+    g_w4_pf = e ? (int64_t)atoll(e) * 1024 : 64 * 1024;
+  }
+  return g_w4_pf;
+}
+
 template <int QUANT, int OUT>
-void launch_w4_t(const GemvArgs &a, int grid, cudaStream_t s) {
+void launch_w4_t(GemvArgs a, int grid, cudaStream_t s) {
+  a.pf_bytes = w4_prefetch_bytes();
   constexpr int DEPTH = QUANT == JAL_Q4_0 ? 3 : 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
