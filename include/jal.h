@@ -260,7 +260,16 @@ typedef struct jal_context_config {
   uint32_t page_size;      /* tokens per KV page (0 = 64) */
   uint64_t sliding_window; /* KvGeometry::sliding_window, 0 = none */
   int32_t use_graphs;      /* capture the decode step in a CUDA graph */
+  int32_t numerics;        /* JAL_NUMERICS_FAST or JAL_NUMERICS_REFERENCE */
 } jal_context_config;
+
+/* Numerics of an execution context.  FAST reorders f32 reductions for
+ * bandwidth (tree sums, fused multiply-adds); REFERENCE performs every f32
+ * reduction in the reference's order (recipe.rs / repack_cache.rs) so a run
+ * can be compared with it token for token; it is a validation mode, far
+ * slower than FAST.  No counterpart setting in the reference. */
+#define JAL_NUMERICS_FAST 0
+#define JAL_NUMERICS_REFERENCE 1
 
 int jal_context_new(const jal_recipe *r, const jal_model_cache *c,
                     const jal_context_config *cfg, jal_context **out);

@@ -36,6 +36,7 @@ F32, F16, Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K, BF16, TQ1_0, TQ2_0 = 0, 1, 2, 6, 8
 ROPE_NORM, ROPE_NEOX = 0, 1
 ROPE_SCALING_NONE, ROPE_SCALING_LINEAR, ROPE_SCALING_LLAMA3, ROPE_SCALING_LONGROPE = 0, 1, 2, 3
 KV_F32, KV_F16 = 0, 1
+NUMERICS_FAST, NUMERICS_REFERENCE = 0, 1  # jal_context_config.numerics
 
 BLOCK_GEOMETRY = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q5_0: (32, 22), Q8_0: (32, 34),
                   Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210), TQ1_0: (256, 54), TQ2_0: (256, 66)}
@@ -91,7 +92,7 @@ class RecipeFields(C.Structure):
 
 class ContextConfig(C.Structure):
     _fields_ = [("n_ctx", C.c_uint64), ("kv_dtype", C.c_int32), ("page_size", C.c_uint32),
-                ("sliding_window", C.c_uint64), ("use_graphs", C.c_int32)]
+                ("sliding_window", C.c_uint64), ("use_graphs", C.c_int32), ("numerics", C.c_int32)]
 
 
 class SynthConfig(C.Structure):
@@ -497,8 +498,11 @@ class ModelRepackCache:
 # ---- ExecutionContext + prefill_step / decode_step --------------------------
 class ExecutionContext:
     def __init__(self, recipe: LlamaRecipe, cache: ModelRepackCache, n_ctx: int, kv_dtype: int = KV_F16,
-                 page_size: int = 64, sliding_window: int = 0, use_graphs: bool = True):
-        cfg = ContextConfig(n_ctx, kv_dtype, page_size, sliding_window, 1 if use_graphs else 0)
+                 page_size: int = 64, sliding_window: int = 0, use_graphs: bool = True,
+                 numerics: int = None):
+        if numerics is None:
+            numerics = NUMERICS_FAST
+        cfg = ContextConfig(n_ctx, kv_dtype, page_size, sliding_window, 1 if use_graphs else 0, numerics)
         out = _P()
         _check(lib().jal_context_new(recipe.handle, cache.handle, C.byref(cfg), C.byref(out)))
         self._h = out.value

@@ -448,6 +448,9 @@ int jal_context_new(const jal_recipe *r, const jal_model_cache *c, const jal_con
     cc.page_size = cfg->page_size ? cfg->page_size : 64;
     cc.sliding_window = cfg->sliding_window;
     cc.use_graphs = cfg->use_graphs != 0;
+    if (cfg->numerics != JAL_NUMERICS_FAST && cfg->numerics != JAL_NUMERICS_REFERENCE)
+      fail(JAL_ERR_INVALID_ARGUMENT, "unknown numerics mode %d", cfg->numerics);
+    cc.numerics = cfg->numerics;
     auto h = std::make_unique<jal_context>();
     h->ctx = create_context(r->r, *c->c, cc);
     *out = h.release();

@@ -143,6 +143,36 @@ void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
 // for head_dim, KV element type and G query heads per KV head.
 int attn_decode_cluster_size(int head_dim, int f16, int G, int want);
 
+// ---- reference-order decode (strict.cu) -----------------------------------
+struct StrictQkvArgs {
+  const float *qkv = nullptr;  // [q | k | v] projection output of one token
+  const float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+  const float *cos_tab = nullptr, *sin_tab = nullptr, *cos_tab_long = nullptr, *sin_tab_long = nullptr;
+  int64_t long_threshold = -1;
+  int skip_rope = 0, neox = 0;
+  int64_t n_heads_q = 0, rotary_dim = 0, layer = 0;
+  KvView kv;
+  const int64_t *d_pos = nullptr;
+  float *qbuf = nullptr;  // [n_heads_q * head_dim]
+};
+struct StrictAttnArgs {
+  const float *qbuf = nullptr;
+  KvView kv;
+  int64_t n_heads_q = 0, layer = 0, window = 0;
+  const int64_t *d_pos = nullptr;
+  float scale = 1.f;
+  float *out = nullptr;  // [n_heads_q * head_dim]
+};
+void launch_strict_rmsnorm(const float *x, const float *w, int64_t n, float eps, float *out, cudaStream_t s);
+size_t strict_gemv_smem(int64_t cols);
+void launch_strict_gemv(const DevMat &w, const int8_t *q8, const float *scales, int64_t rows, bool add, float *y,
+                        const float *bias, cudaStream_t s);
+void launch_strict_swiglu(const float *g, const float *u, int64_t n, float *out, cudaStream_t s);
+void launch_strict_qkv_prep(const StrictQkvArgs &a, cudaStream_t s);
+void launch_strict_attn(const StrictAttnArgs &a, int64_t n_ctx, cudaStream_t s);
+// Sets the device token and position (stream-ordered, no host staging).
+void launch_set_token_pos(uint32_t *d_token, uint32_t token, int64_t *d_pos, int64_t pos, cudaStream_t s);
+
 // Prefill: bias + RoPE on q/k rows, append k/v of m tokens into the cache.
 struct RopeAppendArgs {
   float *qkv = nullptr;  // [m][qkv_stride]: q | k | v

@@ -421,16 +421,19 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv(const GemvArgs 
   }
 }
 
-// ---- 4096-column fast path (M = 1) ------------------------------------------
+// ---- segmented fast path (M = 1) ------------------------------------------
 //
-// Every decode projection of a 4096-wide model except the down projection
-// has 128 blocks per row.  Lane l owns blocks 4l .. 4l+3 of every row: its
-// quants are one contiguous 64-byte (Q4_0) / 128-byte (Q8_0) piece read with
-// 32-byte loads, its four scales one 8-byte load, and its four blocks of the
-// quantized activation stay in registers for the whole kernel.  A row costs
-// the loads, 4 block dots and one warp reduction; DEPTH rows are in flight
-// per warp (issued before griddepcontrol.wait for the first ones).
-constexpr int kW4Blocks = 128;
+// A row is split into nseg segments of 128 blocks (nseg = 1 for 4096
+// columns, 4 for the 14336-column down projection, whose last segment holds
+// 64 blocks).  Warp w owns segment w % nseg of rows r0 + w / nseg,
+// r0 + w / nseg + WARPS / nseg, ...  Within a segment lane l owns blocks
+// 4l .. 4l+3: its quants are one contiguous 64-byte (Q4_0) / 128-byte (Q8_0)
+// piece read with 32-byte loads, its four scales one 8-byte load, and its
+// four blocks of the quantized activation stay in registers for the whole
+// kernel.  A segment costs the loads, 4 block dots and one warp reduction;
+// DEPTH segments are in flight per warp.  With nseg > 1 the per-segment sums
+// of a row are added in segment order at the end of the kernel.
+constexpr int kSegBlocks = 128;
 
 template <int QUANT>
 struct W4Row {
@@ -439,13 +442,22 @@ struct W4Row {
   uint2 d;  // four f16 scales
 };
 
+// Segment `seg` of `row`; lanes past the row end (ragged last segment) load
+// zeros.
 template <int QUANT>
-__device__ __forceinline__ void w4_load(const DevMat &w, int64_t row, int lane, W4Row<QUANT> &r) {
+__device__ __forceinline__ void w4_load(const DevMat &w, int64_t row, int seg, int nb, int lane, W4Row<QUANT> &r) {
   constexpr int NQ = W4Row<QUANT>::NQ;
-  const uint8_t *q = w.qs + row * w.qs_stride + (size_t)lane * NQ * 4;
+  const int b0 = seg * kSegBlocks + 4 * lane;
+  if (b0 < nb) {
+    const uint8_t *q = w.qs + row * w.qs_stride + (size_t)b0 * (NQ / 4) * 4;
 #pragma unroll
-  for (int j = 0; j < NQ / 8; j++) ldg_stream32(q + 32 * j, &r.q[8 * j]);
-  r.d = ldg_stream8(w.d + row * w.d_stride + lane * 4);
+    for (int j = 0; j < NQ / 8; j++) ldg_stream32(q + 32 * j, &r.q[8 * j]);
+    r.d = ldg_stream8(w.d + row * w.d_stride + b0);
+  } else {
+#pragma unroll
+    for (int j = 0; j < NQ; j++) r.q[j] = 0u;
+    r.d = make_uint2(0u, 0u);
+  }
 }
 
 struct W4Act {
@@ -491,27 +503,42 @@ __device__ __forceinline__ float w4_dot(const W4Row<QUANT> &r, const W4Act &x) {
   return acc;
 }
 
+__host__ __device__ inline int seg_count(int64_t cols) { return (int)((cols / 32 + kSegBlocks - 1) / kSegBlocks); }
+// Activation area of the segmented path: blocks padded to nseg * 128 (the
+// padding zero), then the norm weights for RMSNorm inputs.
+__host__ __device__ inline size_t w4_act_region(int in_mode, int nb, int nseg) {
+  size_t b = act_bytes(nseg * kSegBlocks);
+  if (in_mode == GEMV_IN_NORM) b += (size_t)nb * 32 * 4;
+  return (b + 15) / 16 * 16;
+}
+__host__ __device__ inline size_t w4_smem(int in_mode, int nb, int nseg, int64_t max_rows) {
+  const size_t act = w4_act_region(in_mode, nb, nseg);
+  return nseg > 1 ? act + (size_t)max_rows * nseg * 4 : act;
+}
+
 template <int QUANT, int OUT, int WARPS, int DEPTH>
-__global__ void __launch_bounds__(WARPS * 32, 1) k_gemv_w4(const GemvArgs a) {
+__global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvArgs a) {
   extern __shared__ __align__(16) char smem[];
   __shared__ float red[33];
   constexpr int UNITS = OUT == GEMV_OUT_SWIGLU ? 2 : 1;
-  constexpr int nb = kW4Blocks, nbp = kW4Blocks;
+  const int nb = (int)(a.w.cols / 32), nseg = seg_count(a.w.cols), nbp = nseg * kSegBlocks;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int seg = warp % nseg, phase = warp / nseg, nph = WARPS / nseg;
   const int64_t base = a.rows / gridDim.x, rem = a.rows % gridDim.x;
   const int64_t r0 = (int64_t)blockIdx.x * base + ((int64_t)blockIdx.x < rem ? blockIdx.x : rem);
   const int64_t cnt = base + ((int64_t)blockIdx.x < rem ? 1 : 0);
-  const int my_rows = cnt > warp ? (int)((cnt - 1 - warp) / WARPS + 1) : 0;
-  const int64_t gw = r0 + warp;
+  const int my_rows = cnt > phase ? (int)((cnt - 1 - phase) / nph + 1) : 0;
+  const int64_t gw = r0 + phase;
   const int total = my_rows * UNITS;  // unit k: row index k / UNITS, half k % UNITS
+  float *part = (float *)(smem + w4_act_region(a.in_mode, nb, nseg));  // [cnt][nseg]
   auto unit_row = [&](int k) -> int64_t {
-    return gw + (int64_t)(k / UNITS) * WARPS + ((UNITS == 2 && (k & 1)) ? a.up_offset : 0);
+    return gw + (int64_t)(k / UNITS) * nph + ((UNITS == 2 && (k & 1)) ? a.up_offset : 0);
   };
 
   // Before griddepcontrol.wait: either the copy engine prefetches the
   // CTA's first pf_bytes into L2 (no load slots held, so the activation
   // loads after the wait are not queued behind weight traffic), or, with
-  // pf_bytes == 0, the warps load their first DEPTH rows into registers.
+  // pf_bytes == 0, the warps load their first DEPTH segments into registers.
   W4Row<QUANT> buf[DEPTH];
   const bool l2_first = a.pf_bytes > 0;
   if (l2_first) {
@@ -526,7 +553,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_gemv_w4(const GemvArgs a) {
   } else {
 #pragma unroll
     for (int j = 0; j < DEPTH; j++)
-      if (j < total) w4_load<QUANT>(a.w, unit_row(j), lane, buf[j]);
+      if (j < total) w4_load<QUANT>(a.w, unit_row(j), seg, nb, lane, buf[j]);
   }
   gemv_prologue_pre<1, WARPS>(a, smem, nb, nbp);
   pdl_wait();
@@ -535,12 +562,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_gemv_w4(const GemvArgs a) {
   if (l2_first) {
 #pragma unroll
     for (int j = 0; j < DEPTH; j++)
-      if (j < total) w4_load<QUANT>(a.w, unit_row(j), lane, buf[j]);
+      if (j < total) w4_load<QUANT>(a.w, unit_row(j), seg, nb, lane, buf[j]);
   }
   W4Act x;
 #pragma unroll
   for (int v = 0; v < 4; v++) {
-    const int b = 4 * lane + v;
+    const int b = seg * kSegBlocks + 4 * lane + v;  // < nbp; padding blocks are zero
     x.lo[v] = ((const int4 *)smem)[b];
     x.hi[v] = ((const int4 *)(smem + nbp * 16))[b];
     const float2 ss = ((const float2 *)(smem + nbp * 32))[b];
@@ -555,12 +582,15 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_gemv_w4(const GemvArgs a) {
       const int k = k0 + j;
       if (k < total) {
         float s = w4_dot<QUANT>(buf[j], x);
-        if (k + DEPTH < total) w4_load<QUANT>(a.w, unit_row(k + DEPTH), lane, buf[j]);
+        if (k + DEPTH < total) w4_load<QUANT>(a.w, unit_row(k + DEPTH), seg, nb, lane, buf[j]);
         s = warp_sum(s);
+        const int li = phase + (k / UNITS) * nph;  // row within the CTA
         if (UNITS == 2 && (k & 1) == 0) {
           gate = s;
+        } else if (nseg > 1) {
+          if (lane == 0) part[li * nseg + seg] = s;
         } else if (lane == 0) {
-          const int64_t lr = gw + (int64_t)(k / UNITS) * WARPS;
+          const int64_t lr = r0 + li;
           float *yp = a.y + lr;
           if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
           else if (OUT == GEMV_OUT_ADD) *yp = *yp + (a.bias ? s + a.bias[lr] : s);
@@ -569,9 +599,27 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_gemv_w4(const GemvArgs a) {
       }
     }
   }
+  if (nseg > 1 && OUT != GEMV_OUT_SWIGLU) {
+    __syncthreads();
+    for (int li = threadIdx.x; li < cnt; li += WARPS * 32) {
+      float s = 0.0f;
+      for (int q = 0; q < nseg; q++) s += part[li * nseg + q];
+      const int64_t lr = r0 + li;
+      float *yp = a.y + lr;
+      if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
+      else *yp = *yp + (a.bias ? s + a.bias[lr] : s);
+    }
+  }
 }
 
-constexpr int kW4Warps = 16;
+int g_w4_warps = -1;
+int w4_warps() {
+  if (g_w4_warps < 0) {
+    const char *e = getenv("JAL_W4_WARPS");
+    g_w4_warps = (e && atoi(e) == 8) ? 8 : 16;
+  }
+  return g_w4_warps;
+}
 
 int64_t g_w4_pf = -1;
 int64_t w4_prefetch_bytes() {
@@ -582,28 +630,50 @@ int64_t w4_prefetch_bytes() {
   return g_w4_pf;
 }
 
-template <int QUANT, int OUT>
-void launch_w4_t(GemvArgs a, int grid, cudaStream_t s) {
-  a.pf_bytes = w4_prefetch_bytes();
+template <int QUANT, int OUT, int WARPS>
+void launch_w4_w(GemvArgs a, int grid, cudaStream_t s) {
   constexpr int DEPTH = QUANT == JAL_Q4_0 ? 3 : 2;
+  a.pf_bytes = w4_prefetch_bytes();
+  const int nb = (int)(a.w.cols / 32), nseg = seg_count(a.w.cols);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(kW4Warps * 32);
-  cfg.dynamicSmemBytes = smem_bytes(a.in_mode, 1, kW4Blocks);
+  cfg.blockDim = dim3(WARPS * 32);
+  cfg.dynamicSmemBytes = w4_smem(a.in_mode, nb, nseg, (a.rows + grid - 1) / grid);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, k_gemv_w4<QUANT, OUT, kW4Warps, DEPTH>, a);
+  cudaLaunchKernelEx(&cfg, k_gemv_w4<QUANT, OUT, WARPS, DEPTH>, a);
+}
+
+template <int QUANT, int OUT>
+void launch_w4_t(const GemvArgs &a, int grid, cudaStream_t s) {
+  if (w4_warps() == 8) launch_w4_w<QUANT, OUT, 8>(a, grid, s);
+  else launch_w4_w<QUANT, OUT, 16>(a, grid, s);
 }
 
 template <int QUANT, int OUT>
 void set_w4_attrs() {
   constexpr int DEPTH = QUANT == JAL_Q4_0 ? 3 : 2;
-  const void *f = (const void *)k_gemv_w4<QUANT, OUT, kW4Warps, DEPTH>;
-  cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem);
+  const void *fns[2] = {(const void *)k_gemv_w4<QUANT, OUT, 16, DEPTH>, (const void *)k_gemv_w4<QUANT, OUT, 8, DEPTH>};
+  for (const void *f : fns) cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvMaxSmem);
+}
+
+// Shapes the segmented path takes: M = 1, 1, 2 or 4 segments (cols up to
+// 16384, a multiple of 128), SwiGLU only with one segment, and per-CTA
+// partials that fit in shared memory.
+bool w4_fits(const GemvArgs &a, int grid) {
+  const int64_t nb = a.w.cols / 32;
+  if (a.m != 1 || nb % 4 != 0) return false;
+  // 32-byte loads: every row must start 32-byte aligned.
+  if (a.w.qs_stride % 32 != 0 || (reinterpret_cast<uintptr_t>(a.w.qs) & 31) != 0) return false;
+  const int nseg = seg_count(a.w.cols);
+  if (nseg != 1 && nseg != 2 && nseg != 4) return false;
+  if (nseg > 1 && a.out_mode == GEMV_OUT_SWIGLU) return false;
+  if (nseg > w4_warps()) return false;
+  return w4_smem(a.in_mode, (int)nb, nseg, (a.rows + grid - 1) / grid) <= (size_t)kGemvMaxSmem;
 }
 
 int g_use_w4 = -1;
@@ -739,11 +809,15 @@ void launch_gemv(const GemvArgs &a0, cudaStream_t s) {
   // Token counts between template sizes run the next larger instantiation;
   // token slots t >= m quantize to zero and are never written.
   if (a.pf_bytes < 0) a.pf_bytes = prefetch_bytes();
-  if (use_w4() && a.m == 1 && a.w.cols == 32 * kW4Blocks) {
+  int w4_grid = a.grid;
+  if (w4_grid <= 0) {
     int sms = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = a.grid > 0 ? a.grid : (int)(a.rows < sms ? a.rows : sms);
+    w4_grid = (int)(a.rows < sms ? a.rows : sms);
+  }
+  if (use_w4() && w4_fits(a, w4_grid)) {
+    const int grid = w4_grid;
     if (a.w.quant == JAL_Q4_0) {
       if (a.out_mode == GEMV_OUT_STORE) launch_w4_t<JAL_Q4_0, GEMV_OUT_STORE>(a, grid, s);
       else if (a.out_mode == GEMV_OUT_ADD) launch_w4_t<JAL_Q4_0, GEMV_OUT_ADD>(a, grid, s);

@@ -858,6 +858,18 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->am_cnt = (unsigned *)take(4);
   ctx->d_hist = (uint32_t *)take((n_ctx + 2) * 4);
   if ((size_t)(p - db->as<char>()) > db->bytes) fail(JAL_ERR_INVALID_ARGUMENT, "internal: decode scratch layout overflow");
+  {  // reference-order scratch: normed row, int8 activations + scales, gate|up, q
+    const uint64_t kmax = std::max<uint64_t>(std::max<uint64_t>(H, Q), F), kp = (kmax + 31) / 32 * 32;
+    auto sb = alloc((H + kp / 32 + 2 * F + Q) * 4 + kp + 5 * 256);
+    ctx->bufs.push_back(sb);
+    char *q = sb->as<char>();
+    auto take2 = [&](size_t n) { char *r = q; q += (n + 255) / 256 * 256; return r; };
+    ctx->s_norm = (float *)take2(H * 4);
+    ctx->s_sc = (float *)take2(kp / 32 * 4);
+    ctx->s_gu = (float *)take2(2 * F * 4);
+    ctx->s_qbuf = (float *)take2(Q * 4);
+    ctx->s_q8 = (int8_t *)take2(kp);
+  }
   JAL_CUDA(cudaMallocHost(&ctx->h_pos, 8));
   JAL_CUDA(cudaMallocHost(&ctx->h_token, 4 * 8));
   JAL_CUDA(cudaStreamSynchronize(ctx->stream));
@@ -935,7 +947,57 @@ void Context::enqueue_decode_step(bool pdl) {
   launches_per_step = n;
 }
 
+// Reference-order step (see strict.cu): the same layer sequence as
+// forward_tokens of the reference for one token.
+void Context::enqueue_strict_token(bool logits_out, bool argmax) {
+  const ModelCache &c = *cache;
+  const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv;
+  const float eps = std::max(recipe.rms_eps, 1.0e-7f);
+  launch_embed(c.emb_raw->as<uint8_t>(), c.emb_quant, (int64_t)H, (int64_t)c.emb_rows, d_token, 1, hidden, d_err, 0,
+               stream);
+  for (size_t l = 0; l < c.layers.size(); l++) {
+    const Layer &L = c.layers[l];
+    launch_strict_rmsnorm(hidden, L.attn_norm, (int64_t)H, eps, s_norm, stream);
+    launch_act_quant(s_norm, 1, (int64_t)H, (int64_t)H, s_q8, s_sc, stream);
+    launch_strict_gemv(L.qkv, s_q8, s_sc, (int64_t)(Q + 2 * KV), false, qkv, nullptr, stream);
+    StrictQkvArgs qa;
+    qa.qkv = qkv; qa.bq = L.bq; qa.bk = L.bk; qa.bv = L.bv;
+    qa.cos_tab = cos_tab; qa.sin_tab = sin_tab; qa.cos_tab_long = cos_long; qa.sin_tab_long = sin_long;
+    qa.long_threshold = recipe.scaling.kind == JAL_ROPE_SCALING_LONGROPE
+                            ? (int64_t)recipe.scaling.original_max_position_embeddings : -1;
+    qa.skip_rope = recipe.should_skip_rope(l); qa.neox = recipe.rope_type == JAL_ROPE_NEOX;
+    qa.n_heads_q = (int64_t)g.n_heads_q; qa.rotary_dim = (int64_t)g.rotary_dim; qa.layer = (int64_t)l;
+    qa.kv = kv; qa.d_pos = d_pos; qa.qbuf = s_qbuf;
+    launch_strict_qkv_prep(qa, stream);
+    StrictAttnArgs aa;
+    aa.qbuf = s_qbuf; aa.kv = kv; aa.n_heads_q = (int64_t)g.n_heads_q; aa.layer = (int64_t)l;
+    aa.window = (int64_t)cfg.sliding_window; aa.d_pos = d_pos; aa.scale = 1.0f / sqrtf((float)g.head_dim);
+    aa.out = attn;
+    launch_strict_attn(aa, (int64_t)cfg.n_ctx, stream);
+    launch_act_quant(attn, 1, (int64_t)Q, (int64_t)Q, s_q8, s_sc, stream);
+    launch_strict_gemv(L.wo.dm, s_q8, s_sc, (int64_t)H, true, hidden, L.bo, stream);
+    launch_strict_rmsnorm(hidden, L.ffn_norm, (int64_t)H, eps, s_norm, stream);
+    launch_act_quant(s_norm, 1, (int64_t)H, (int64_t)H, s_q8, s_sc, stream);
+    launch_strict_gemv(L.gateup, s_q8, s_sc, (int64_t)(2 * F), false, s_gu, nullptr, stream);
+    launch_strict_swiglu(s_gu, s_gu + F, (int64_t)F, ffn, stream);
+    launch_act_quant(ffn, 1, (int64_t)F, (int64_t)F, s_q8, s_sc, stream);
+    launch_strict_gemv(L.wdown.dm, s_q8, s_sc, (int64_t)H, true, hidden, nullptr, stream);
+  }
+  if (logits_out) {
+    launch_strict_rmsnorm(hidden, c.output_norm->as<float>(), (int64_t)H, eps, s_norm, stream);
+    launch_act_quant(s_norm, 1, (int64_t)H, (int64_t)H, s_q8, s_sc, stream);
+    launch_strict_gemv(c.lm_head.dm, s_q8, s_sc, (int64_t)c.vocab_size, false, logits, nullptr, stream);
+  }
+  if (argmax)
+    launch_argmax(logits, (int64_t)c.vocab_size, am_val, am_idx, am_cnt, am_blocks, d_token, d_pos, d_hist, 0, stream);
+}
+
 void Context::run_decode_step() {
+  if (cfg.numerics == JAL_NUMERICS_REFERENCE) {
+    enqueue_strict_token(true, true);
+    JAL_CUDA(cudaGetLastError());
+    return;
+  }
   if (cfg.use_graphs) {
     if (!graph) {
       bool pdl = !env_flag("JAL_NO_PDL");
@@ -981,6 +1043,16 @@ void Context::ensure_prefill_capacity(uint64_t m) {
 
 // prefill_step_with_cache (recipe.rs:564-608, execute_batch_forward :1489-1756)
 void Context::prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bool compute_logits) {
+  if (cfg.numerics == JAL_NUMERICS_REFERENCE) {
+    // The reference's batched forward is per-token identical math, so the
+    // reference-order path runs the prompt one token at a time.
+    for (uint64_t t = 0; t < n; t++) {
+      launch_set_token_pos(d_token, tokens[t], d_pos, (int64_t)(start_pos + t), stream);
+      enqueue_strict_token(compute_logits && t + 1 == n, false);
+    }
+    JAL_CUDA(cudaGetLastError());
+    return;
+  }
   const ModelCache &c = *cache;
   const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv;
   const float eps = std::max(recipe.rms_eps, 1.0e-7f);

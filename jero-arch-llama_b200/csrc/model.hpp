@@ -111,6 +111,7 @@ struct ContextConfig {
   uint64_t sliding_window = 0;
   bool use_graphs = true;
   uint64_t prefill_chunk = 2048;
+  int numerics = JAL_NUMERICS_FAST;  // JAL_NUMERICS_REFERENCE: reference-order f32 (strict.cu)
 };
 
 struct Context {
@@ -145,12 +146,18 @@ struct Context {
   // host staging
   int64_t *h_pos = nullptr;
   uint32_t *h_token = nullptr;
+  // reference-order decode scratch
+  float *s_norm = nullptr, *s_sc = nullptr, *s_gu = nullptr, *s_qbuf = nullptr;
+  int8_t *s_q8 = nullptr;
   // graph
   cudaGraphExec_t graph = nullptr;
   size_t launches_per_step = 0;
 
   ~Context();
   void enqueue_decode_step(bool pdl);
+  // One token through the reference-order kernels; d_token / d_pos hold the
+  // token and its position.  argmax advances d_pos like the fast step.
+  void enqueue_strict_token(bool logits, bool argmax);
   void run_decode_step();
   void prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bool compute_logits);
   void ensure_prefill_capacity(uint64_t m);

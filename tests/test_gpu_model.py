@@ -2,9 +2,20 @@
 
 The tiny Llama workload: 4 layers, dim 512, 8/2 heads, head_dim 64, FFN 1376,
 vocab 4096, Q4_0 layer weights, Q8_0 embedding and head, RoPE theta 1e4; a
-16-token prompt uniform in [0, 4096) and 64 greedy decode steps.  Bars: every
-step's logits within LOGIT_ATOL of the oracle's and an identical greedy
-token sequence.
+16-token prompt uniform in [0, 4096) and 64 greedy decode steps.
+
+Two numerics modes are checked:
+  - NUMERICS_REFERENCE performs every f32 reduction in the reference's order.
+    Bars: every step's logits within LOGIT_ATOL of the oracle's and an
+    identical greedy token sequence (exp is the correctly rounded value; the
+    reference's glibc expf differs by one ulp on ~6e-4 of arguments, which
+    moves logits by ~1e-7).
+  - NUMERICS_FAST (the serving path) reorders f32 sums.  Because the int8
+    activation quantizer is discontinuous, a one-ulp difference can flip one
+    rounding and move logits by up to ~3e-2 a few layers later; the fast path
+    is therefore checked teacher-forced against the oracle with bounds on the
+    worst and mean logit error, and its argmax may differ from the oracle's
+    only where the oracle's top logits are within that error of each other.
 """
 import numpy as np
 import pytest
@@ -13,8 +24,10 @@ import gguf_py
 
 pytestmark = pytest.mark.gpu
 
-LOGIT_ATOL = 1e-2
+LOGIT_ATOL = 1e-4      # reference numerics vs oracle, per logit
 N_DECODE = 64
+FAST_MAX_ATOL = 6e-2   # fast numerics vs oracle: worst logit
+FAST_MEAN_ATOL = 1e-2  # fast numerics vs oracle: mean |dlogit| per step (measured 4-6e-3 on the tiny models)
 
 
 def geom_of(spec, neox=False):
@@ -24,7 +37,7 @@ def geom_of(spec, neox=False):
 
 
 def make(jal, oracle, spec, seed, neox=False, kv_dtype=None, n_ctx=256, recipe_hook=None, oracle_kwargs=None,
-         sliding_window=0):
+         sliding_window=0, numerics=None):
     buf = jal.synth_gguf(spec, seed)
     _, tensors = gguf_py.parse(buf)
     om = oracle.Model(tensors, geom_of(spec, neox), nthreads=8, sliding_window=sliding_window,
@@ -33,9 +46,15 @@ def make(jal, oracle, spec, seed, neox=False, kv_dtype=None, n_ctx=256, recipe_h
     if recipe_hook:
         recipe_hook(recipe)
     cache = recipe.build_repack_cache(buf)
-    ctx = jal.ExecutionContext(recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F32 if kv_dtype is None else kv_dtype,
-                               sliding_window=sliding_window)
+    ctx = new_ctx(jal, recipe, cache, n_ctx=n_ctx, kv_dtype=kv_dtype, sliding_window=sliding_window,
+                  numerics=jal.NUMERICS_REFERENCE if numerics is None else numerics)
     return buf, om, recipe, cache, ctx
+
+
+def new_ctx(jal, recipe, cache, n_ctx=256, kv_dtype=None, sliding_window=0, numerics=None):
+    return jal.ExecutionContext(recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F32 if kv_dtype is None else kv_dtype,
+                                sliding_window=sliding_window,
+                                numerics=jal.NUMERICS_REFERENCE if numerics is None else numerics)
 
 
 def prompt_of(seed, n=16, vocab=4096):
@@ -43,6 +62,7 @@ def prompt_of(seed, n=16, vocab=4096):
 
 
 def run_parity(om, ctx, prompt, n_decode, cap, atol=LOGIT_ATOL):
+    """Reference numerics: logits within atol every step, identical greedy ids."""
     kvo = om.new_kv(cap)
     lo = om.prefill(kvo, cap, prompt, 0)
     lg = ctx.prefill_step(prompt, 0)
@@ -63,6 +83,33 @@ def run_parity(om, ctx, prompt, n_decode, cap, atol=LOGIT_ATOL):
     return tokens, kvo, worst
 
 
+def run_fast(om, ctx, prompt, n_decode, cap):
+    """Fast numerics, teacher-forced on the oracle's greedy tokens."""
+    kvo = om.new_kv(cap)
+    lo = om.prefill(kvo, cap, prompt, 0)
+    lg = ctx.prefill_step(prompt, 0)
+    errs, means, agree = [], [], []
+
+    def check(lo, lg, step):
+        errs.append(float(np.max(np.abs(lo - lg))))
+        means.append(float(np.mean(np.abs(lo - lg))))
+        to, tg = int(np.argmax(lo)), int(np.argmax(lg))
+        agree.append(to == tg)
+        # A different argmax is allowed only at a near-tie of the oracle's logits.
+        assert to == tg or lo[tg] >= lo[to] - FAST_MAX_ATOL, f"step {step}: argmax {tg} vs oracle {to}"
+
+    check(lo, lg, -1)
+    tok = int(np.argmax(lo))
+    for step in range(n_decode):
+        lo = om.decode(kvo, cap, tok, len(prompt) + step)
+        lg = ctx.decode_step(tok)
+        check(lo, lg, step)
+        tok = int(np.argmax(lo))
+    assert max(errs) <= FAST_MAX_ATOL, f"worst |dlogit| {max(errs):.3e}"
+    assert max(means) <= FAST_MEAN_ATOL, f"worst mean |dlogit| {max(means):.3e}"
+    return max(errs), float(np.mean(agree))
+
+
 def test_tiny_llama_greedy_64_matches_oracle_f32_kv(jal, oracle, torch_cuda):
     spec = jal.TINY_LLAMA
     buf, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2024)
@@ -70,27 +117,32 @@ def test_tiny_llama_greedy_64_matches_oracle_f32_kv(jal, oracle, torch_cuda):
     assert cache.norm_count() == 9 and cache.bias_count() == 0 and cache.repacked_matrix_count() == 29
     prompt = prompt_of(7)
     tokens, kvo, worst = run_parity(om, ctx, prompt, N_DECODE, 256)
-    print(f"tiny llama f32-KV worst |dlogit| = {worst:.3e}")
+    print(f"tiny llama f32-KV reference numerics worst |dlogit| = {worst:.3e}")
     # KV cache agrees with the reference layout [layer][K|V][pos][kv_dim]
     n_pos = len(prompt) + N_DECODE
     kvg = ctx.export_kv(n_pos, spec.num_layers, spec.n_heads_kv * spec.head_dim)
     kvr = kvo.reshape(spec.num_layers, 2, 256, -1)[:, :, :n_pos, :].ravel()
-    assert np.max(np.abs(kvg - kvr)) / np.max(np.abs(kvr)) <= 1e-3
-    # The on-device greedy loop (CUDA graph, argmax on device) yields the same ids.
-    ctx2 = jal.ExecutionContext(recipe, cache, n_ctx=256, kv_dtype=jal.KV_F32)
+    assert np.max(np.abs(kvg - kvr)) / np.max(np.abs(kvr)) <= 1e-5
+    # The on-device greedy loop (argmax on device) yields the same ids.
+    ctx2 = new_ctx(jal, recipe, cache)
     l0 = ctx2.prefill_step(prompt, 0)
     first = int(np.argmax(l0))
     seq = ctx2.decode_greedy(first, N_DECODE)
     assert [first] + [int(t) for t in seq[:-1]] == tokens
     assert ctx2.position() == len(prompt) + N_DECODE
-    assert ctx2.launches_per_step() == 1 + 5 * spec.num_layers + 2
+    # Fast numerics: bounded error, one CUDA graph of 1 + 5L + 2 kernels per step.
+    ctx3 = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST)
+    worst_f, agree = run_fast(om, ctx3, prompt, N_DECODE, 256)
+    print(f"tiny llama fast numerics worst |dlogit| = {worst_f:.3e}, top-1 agreement {agree:.2f}")
+    assert ctx3.launches_per_step() == 1 + 5 * spec.num_layers + 2
 
 
 def test_tiny_llama_greedy_fp16_paged_kv(jal, oracle, torch_cuda):
     spec = jal.TINY_LLAMA
-    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2024, kv_dtype=jal.KV_F16)
-    _, _, worst = run_parity(om, ctx, prompt_of(7), N_DECODE, 256)
-    print(f"tiny llama fp16-KV worst |dlogit| = {worst:.3e}")
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2024, kv_dtype=jal.KV_F16,
+                                     numerics=jal.NUMERICS_FAST)
+    worst, agree = run_fast(om, ctx, prompt_of(7), N_DECODE, 256)
+    print(f"tiny llama fp16-KV fast worst |dlogit| = {worst:.3e}, top-1 agreement {agree:.2f}")
 
 
 def test_tiny_qwen2_neox_bias_q8_0(jal, oracle, torch_cuda):
@@ -99,6 +151,7 @@ def test_tiny_qwen2_neox_bias_q8_0(jal, oracle, torch_cuda):
     _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=77, neox=True)
     assert recipe.fields().rope_type == jal.ROPE_NEOX and cache.bias_count() == 3 * spec.num_layers
     run_parity(om, ctx, prompt_of(9), 24, 256)
+    run_fast(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(9), 24, 256)
 
 
 def test_llama4_irope_and_sliding_window(jal, oracle, torch_cuda):
@@ -107,6 +160,8 @@ def test_llama4_irope_and_sliding_window(jal, oracle, torch_cuda):
     _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=5, recipe_hook=lambda r: r.with_irope_mask(mask),
                                      oracle_kwargs=dict(skip_rope=np.array(mask, np.uint8)), sliding_window=8)
     run_parity(om, ctx, prompt_of(3, n=12), 12, 256)
+    run_fast(om, new_ctx(jal, recipe, cache, sliding_window=8, numerics=jal.NUMERICS_FAST), prompt_of(3, n=12), 12,
+             256)
 
 
 def test_llama3_smooth_scaling_model(jal, oracle, torch_cuda):
@@ -128,32 +183,35 @@ def test_batched_prefill_equals_sequential_and_chunked(jal, oracle, torch_cuda):
     spec = jal.TINY_LLAMA
     buf, om, recipe, cache, ctx = make(jal, oracle, spec, seed=31)
     prompt = prompt_of(5, n=20)
-    la = ctx.prefill_step(prompt, 0)
-    ctx_b = jal.ExecutionContext(recipe, cache, n_ctx=256, kv_dtype=jal.KV_F32)
-    ctx_b.prefill_step(prompt[:1], 0, compute_logits=False)
-    lb = None
-    for t in prompt[1:]:
-        lb = ctx_b.decode_step(int(t))
-    assert np.max(np.abs(la - lb)) <= 1e-3
-    ctx_c = jal.ExecutionContext(recipe, cache, n_ctx=256, kv_dtype=jal.KV_F32)
-    ctx_c.prefill_step(prompt[:7], 0, compute_logits=False)
-    lc = ctx_c.prefill_step(prompt[7:], 7)
-    assert np.max(np.abs(la - lc)) <= 1e-3
-    assert ctx_c.position() == 20
+    for numerics, atol in ((jal.NUMERICS_REFERENCE, 0.0), (jal.NUMERICS_FAST, FAST_MAX_ATOL)):
+        ca = new_ctx(jal, recipe, cache, numerics=numerics)
+        la = ca.prefill_step(prompt, 0)
+        cb = new_ctx(jal, recipe, cache, numerics=numerics)
+        cb.prefill_step(prompt[:1], 0, compute_logits=False)
+        lb = None
+        for t in prompt[1:]:
+            lb = cb.decode_step(int(t))
+        assert np.max(np.abs(la - lb)) <= atol
+        cc = new_ctx(jal, recipe, cache, numerics=numerics)
+        cc.prefill_step(prompt[:7], 0, compute_logits=False)
+        lc = cc.prefill_step(prompt[7:], 7)
+        assert np.max(np.abs(la - lc)) <= atol
+        assert cc.position() == 20
 
 
 def test_fail_closed_errors_keep_position(jal, oracle, torch_cuda):
     # lib.rs:783-871, 963-1036: fail closed without advancing the position
     spec = jal.TINY_LLAMA
-    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2, n_ctx=20)
-    ctx.prefill_step(prompt_of(1, n=19), 0)
-    with pytest.raises(jal.TensorBoundsError):
-        ctx.decode_step(4096)
-    assert ctx.position() == 19
-    ctx.decode_step(3)
-    assert ctx.position() == 20
-    with pytest.raises(jal.ContextLengthExceeded):
+    for numerics in (jal.NUMERICS_FAST, jal.NUMERICS_REFERENCE):
+        _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2, n_ctx=20, numerics=numerics)
+        ctx.prefill_step(prompt_of(1, n=19), 0)
+        with pytest.raises(jal.TensorBoundsError):
+            ctx.decode_step(4096)
+        assert ctx.position() == 19
         ctx.decode_step(3)
-    assert ctx.position() == 20
-    with pytest.raises(jal.ContextLengthExceeded):
-        ctx.prefill_step(prompt_of(1, n=21), 0)
+        assert ctx.position() == 20
+        with pytest.raises(jal.ContextLengthExceeded):
+            ctx.decode_step(3)
+        assert ctx.position() == 20
+        with pytest.raises(jal.ContextLengthExceeded):
+            ctx.prefill_step(prompt_of(1, n=21), 0)
