@@ -220,6 +220,56 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def profile_mode(args):
+    """Small fixed workloads for ncu (no JSON line):
+      gemv   - four launches of the 14336x4096 Q4_0 decode GEMV (M = 1);
+      decode - Llama-3-8B Q4_0, 32-token prompt, two decode steps between
+               cudaProfilerStart / Stop;
+      attn   - the same attention geometry with 2 layers, a --prefill prompt
+               and one decode step between cudaProfilerStart / Stop."""
+    import dataclasses
+
+    import numpy as np
+    import torch
+    jal = load_jal()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    if args.profile == "gemv":
+        rows, cols = 14336, 4096
+        raw = jal.synth_matrix(jal.Q4_0, rows, cols, seed=SEED, name="profile.gemv")
+        mat = jal.CachedMatrix.repack(raw, jal.Q4_0, rows, cols)
+        x = torch.from_numpy(jal.synth_normal(cols, seed=SEED, name="profile.act")).cuda()
+        q8 = torch.zeros(cols, dtype=torch.int8, device="cuda")
+        sc = torch.zeros(cols // 32, dtype=torch.float32, device="cuda")
+        jal.act_quantize_q8(x, 1, cols, q8, sc, stream)
+        y = torch.zeros(rows, dtype=torch.float32, device="cuda")
+        for _ in range(4):
+            mat.gemv_q8(q8, sc, y, stream)
+        torch.cuda.synchronize()
+        print("profile gemv ok", float(y.abs().sum()))
+        return 0
+    spec = jal.LLAMA3_8B_Q4_0
+    n_prompt, n_steps = 32, 2
+    if args.profile == "attn":
+        spec = dataclasses.replace(spec, num_layers=2)
+        n_prompt, n_steps = args.prefill, 1
+    gguf = jal.synth_gguf(spec, SEED)
+    recipe = jal.LlamaRecipe.from_gguf(gguf)
+    cache = recipe.build_repack_cache(gguf)
+    ctx = jal.ExecutionContext(recipe, cache, n_ctx=n_prompt + 64, kv_dtype=jal.KV_F16)
+    ctx.set_stream(stream)
+    prompt = np.random.Generator(np.random.PCG64(SEED)).integers(0, spec.vocab_size, n_prompt).astype(np.uint32)
+    logits = ctx.prefill_step(prompt, 0)
+    ctx.decode_greedy(int(np.argmax(logits)), 3)  # captures the decode graph
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    ctx.decode_greedy(5, n_steps)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(f"profile {args.profile} ok")
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -230,7 +280,11 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="llama3-8b-q4_0", choices=["llama3-8b-q4_0", "tiny"])
+    ap.add_argument("--profile", choices=["gemv", "decode", "attn"],
+                    help="run a small fixed workload for ncu instead of the benchmark")
     args = ap.parse_args()
+    if args.profile:
+        return profile_mode(args)
     if args.impl == "reference":
         return reference_arm(args)
     args.warmup = max(args.warmup, 3)
@@ -327,7 +381,7 @@ def main():
         line["gemv_sweep"] = sweep
         dom = next(s for s in sweep if s["quant"] == "Q4_0" and s["M"] == 14336)
         traffic = committed_traffic().get("gemv_q4_0_14336x4096")
-        line["roofline"] = {"kernel": "k_gemv<Q4_0,M=1> 14336x4096 (decode quant-GEMV)", "bound": "hbm",
+        line["roofline"] = {"kernel": "k_gemv_w4<Q4_0,M=1> 14336x4096 (decode quant-GEMV)", "bound": "hbm",
                             "achieved": dom["GBps"], "peak": peak, "unit": "GB/s",
                             "frac": round(dom["GBps"] / peak, 4), "traffic": traffic,
                             "algorithmic_bytes": dom["bytes"], "peak_kind": peak_kind}
