@@ -16,6 +16,7 @@
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
+#include "attn_dev.cuh"
 #include "dev_util.cuh"
 #include "device.hpp"
 #include "jal.h"
@@ -24,93 +25,12 @@ namespace jal {
 
 namespace {
 
+using namespace adev;
+
 constexpr int kAttnWarps = 8;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kMaxClusterCtas = 16;  // CTAs per KV head (one cluster)
-constexpr int kStages = 3;           // shared-memory ring of K/V tiles
-constexpr int kStageBytes = 32 * 1024;
 constexpr int kErrAttnWait = 2;            // bit set in the context error word
-
-__device__ __forceinline__ int64_t kv_elem(const KvView &kv, int64_t layer, int64_t h, int64_t pos) {
-  int64_t page = kv.page_table[pos / kv.page_size], slot = pos % kv.page_size;
-  return (((layer * kv.n_pages + page) * kv.n_kv + h) * kv.page_size + slot) * kv.head_dim;
-}
-
-__device__ __forceinline__ void store_kv(void *base, int f16, int64_t e, float v) {
-  if (f16) ((__half *)base)[e] = __float2half_rn(v);
-  else ((float *)base)[e] = v;
-}
-
-// Rotate pair (x0, x1) by (c, s): recipe.rs:2750-2767.
-__device__ __forceinline__ void rot(float &x0, float &x1, float c, float s) {
-  float a = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-  float b = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-  x0 = a;
-  x1 = b;
-}
-
-// Tile geometry for head_dim HD and KV element type.
-template <int HD, bool F16>
-struct AttnGeom {
-  static constexpr int ES = F16 ? 2 : 4;              // bytes per element
-  static constexpr int ROW = HD * ES;                 // bytes of one position's K (or V)
-  static constexpr int TP = kStageBytes / (2 * ROW);  // positions per tile
-  static constexpr int LG = ROW / 16;                 // lanes per position when scoring
-  static constexpr int PPS = 32 / LG;                 // positions per warp step when scoring
-  static constexpr int DPL = 16 / ES;                 // dims per lane when scoring
-  static constexpr int TPW = TP / kAttnWarps;         // positions per warp per tile
-  static constexpr int VD = HD / 32;                  // dims per lane in P.V
-  static_assert(TPW % PPS == 0, "tile split");
-};
-
-// Copies positions [t0, t0 + n) of KV head h (K then V) into a ring stage;
-// one bulk copy per page run.  Caller: one thread.
-template <int HD, bool F16>
-__device__ void issue_tile(const AttnDecodeArgs &a, char *stage, uint64_t *bar, int64_t t0, int n, int h) {
-  using Gm = AttnGeom<HD, F16>;
-  const KvView &kv = a.kv;
-  mbar_expect_tx(bar, (uint32_t)(2 * n * Gm::ROW));
-  int done = 0;
-  while (done < n) {
-    const int64_t p = t0 + done;
-    const int64_t page = kv.page_table[p / kv.page_size], slot = p % kv.page_size;
-    const int run = (int)(kv.page_size - slot < n - done ? kv.page_size - slot : n - done);
-    const int64_t e = (((a.layer * kv.n_pages + page) * kv.n_kv + h) * kv.page_size + slot) * HD;
-    bulk_g2s(stage + done * Gm::ROW, (const char *)kv.k + e * Gm::ES, (uint32_t)(run * Gm::ROW), bar);
-    bulk_g2s(stage + Gm::TP * Gm::ROW + done * Gm::ROW, (const char *)kv.v + e * Gm::ES, (uint32_t)(run * Gm::ROW),
-             bar);
-    done += run;
-  }
-}
-
-template <bool F16, int N>
-__device__ __forceinline__ void load_vals(const char *p, float (&o)[N]) {
-  if (F16) {
-    if (N == 8) {
-      const uint4 raw = *(const uint4 *)p;
-      const __half2 *r = (const __half2 *)&raw;
-#pragma unroll
-      for (int k = 0; k < 4; k++) { float2 f = __half22float2(r[k]); o[2 * k] = f.x; o[2 * k + 1] = f.y; }
-    } else if (N == 4) {
-      const uint2 raw = *(const uint2 *)p;
-      const __half2 *r = (const __half2 *)&raw;
-#pragma unroll
-      for (int k = 0; k < 2; k++) { float2 f = __half22float2(r[k]); o[2 * k] = f.x; o[2 * k + 1] = f.y; }
-    } else {
-      const __half2 *h2 = (const __half2 *)p;
-#pragma unroll
-      for (int k = 0; k < N / 2; k++) { float2 f = __half22float2(h2[k]); o[2 * k] = f.x; o[2 * k + 1] = f.y; }
-    }
-  } else {
-    if (N == 4) {
-      const float4 v = *(const float4 *)p;
-      o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
-    } else {
-#pragma unroll
-      for (int k = 0; k < N / 2; k++) { float2 f = ((const float2 *)p)[k]; o[2 * k] = f.x; o[2 * k + 1] = f.y; }
-    }
-  }
-}
 
 // Decode attention for one token.  Grid: n_kv clusters of cs CTAs; CTA rank r
 // of cluster h handles positions [s0, s1) of KV head h, split evenly.
@@ -128,7 +48,7 @@ __device__ __forceinline__ void load_vals(const char *p, float (&o)[N]) {
 template <int HD, bool F16, int GP>
 __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnDecodeArgs a) {
   namespace cg = cooperative_groups;
-  using Gm = AttnGeom<HD, F16>;
+  using Gm = AttnGeom<HD, F16, kAttnWarps>;
   constexpr int TP = Gm::TP, LG = Gm::LG, PPS = Gm::PPS, DPL = Gm::DPL, TPW = Gm::TPW, VD = Gm::VD;
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(128) char ring[];  // kStages x kStageBytes, reused for the warp merge
@@ -164,7 +84,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnDecod
     for (int k = 0; k < nt && k < kStages; k++) {
       const int64_t t0 = s0 + (int64_t)k * TP;
       const int n = (int)(s1 - t0 < TP ? s1 - t0 : TP);
-      issue_tile<HD, F16>(a, ring + k * kStageBytes, &bars[k], t0, n, h);
+      issue_tile<HD, F16>(a.kv, a.layer, ring + k * kStageBytes, &bars[k], t0, n, h);
     }
   }
   // RoPE rows of this position (static tables) are staged before the wait.
@@ -341,7 +261,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn_decode(const AttnDecod
       fence_proxy_async();
       const int64_t t1 = s0 + (int64_t)(k + kStages) * TP;
       const int n1 = (int)(s1 - t1 < TP ? s1 - t1 : TP);
-      issue_tile<HD, F16>(a, Ks, &bars[st], t1, n1, h);
+      issue_tile<HD, F16>(a.kv, a.layer, Ks, &bars[st], t1, n1, h);
     }
   }
   if (!ok) {

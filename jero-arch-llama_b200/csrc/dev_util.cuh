@@ -4,6 +4,8 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "jal.h"
+
 namespace jal {
 
 // f16_to_f32_finite (repack_cache.rs:160-181): IEEE half -> f32, with the
@@ -100,6 +102,32 @@ __device__ __forceinline__ void l2_prefetch_bulk(const void *p, uint64_t bytes) 
     c += n;
     bytes -= n;
   }
+}
+
+// Element i of embedding row tok (embed_tokens / decode_row_to_f32,
+// recipe.rs:1395-1440, repack_cache.rs:1166-1301): f32 / f16 / bf16 rows
+// sanitized, Q4_0 / Q5_0 / Q8_0 blocks dequantized as d * q.
+__device__ __forceinline__ float embed_value(const uint8_t *emb, int quant, int64_t hidden, uint32_t tok, int64_t i) {
+  if (quant == JAL_F32) return sanitize_weight(((const float *)emb)[(int64_t)tok * hidden + i]);
+  if (quant == JAL_F16) return f16_finite(((const uint16_t *)emb)[(int64_t)tok * hidden + i]);
+  if (quant == JAL_BF16) return bf16_finite(((const uint16_t *)emb)[(int64_t)tok * hidden + i]);
+  const int64_t g = i / 32, e = i % 32;
+  const int64_t bb = quant == JAL_Q4_0 ? 18 : quant == JAL_Q5_0 ? 22 : 34;
+  const uint8_t *blk = emb + ((int64_t)tok * (hidden / 32) + g) * bb;
+  const float d = f16_finite((uint16_t)(blk[0] | (blk[1] << 8)));
+  int q;
+  if (quant == JAL_Q4_0) {
+    q = (int)(e < 16 ? (blk[2 + e] & 15) : (blk[2 + e - 16] >> 4)) - 8;
+  } else if (quant == JAL_Q5_0) {
+    const uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
+    const int j = e & 15;
+    const uint32_t nib = e < 16 ? (blk[6 + j] & 15u) : (uint32_t)(blk[6 + j] >> 4);
+    const uint32_t hb = ((qh >> (e < 16 ? j : j + 16)) & 1u) << 4;
+    q = (int)(nib | hb) - 16;
+  } else {
+    q = (int8_t)blk[2 + e];
+  }
+  return d == 0.0f ? 0.0f : __fmul_rn(d, (float)q);
 }
 
 // ---- mbarrier / bulk-copy helpers (shared::cta barrier, own-CTA destination;

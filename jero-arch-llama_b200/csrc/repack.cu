@@ -316,29 +316,7 @@ __global__ void k_embed(const uint8_t *__restrict__ emb, int quant, int64_t hidd
     if (pdl) pdl_trigger();
     return;
   }
-  for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
-    float v;
-    if (quant == JAL_F32) v = sanitize_weight(((const float *)emb)[(int64_t)tok * hidden + i]);
-    else if (quant == JAL_F16) v = f16_finite(((const uint16_t *)emb)[(int64_t)tok * hidden + i]);
-    else if (quant == JAL_BF16) v = bf16_finite(((const uint16_t *)emb)[(int64_t)tok * hidden + i]);
-    else {
-      int64_t g = i / 32, e = i % 32;
-      int64_t bb = quant == JAL_Q4_0 ? 18 : quant == JAL_Q5_0 ? 22 : 34;
-      const uint8_t *blk = emb + ((int64_t)tok * (hidden / 32) + g) * bb;
-      float d = f16_finite((uint16_t)(blk[0] | (blk[1] << 8)));
-      int q;
-      if (quant == JAL_Q4_0) q = (int)(e < 16 ? (blk[2 + e] & 15) : (blk[2 + e - 16] >> 4)) - 8;
-      else if (quant == JAL_Q5_0) {
-        uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
-        int j = e & 15;
-        uint32_t nib = e < 16 ? (blk[6 + j] & 15u) : (uint32_t)(blk[6 + j] >> 4);
-        uint32_t hb = ((qh >> (e < 16 ? j : j + 16)) & 1u) << 4;
-        q = (int)(nib | hb) - 16;
-      } else q = (int8_t)blk[2 + e];
-      v = d == 0.0f ? 0.0f : __fmul_rn(d, (float)q);
-    }
-    o[i] = v;
-  }
+  for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) o[i] = embed_value(emb, quant, hidden, tok, i);
   if (pdl) pdl_trigger();
 }
 
