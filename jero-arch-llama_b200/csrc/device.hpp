@@ -173,6 +173,56 @@ void launch_strict_attn(const StrictAttnArgs &a, int64_t n_ctx, cudaStream_t s);
 // Sets the device token and position (stream-ordered, no host staging).
 void launch_set_token_pos(uint32_t *d_token, uint32_t token, int64_t *d_pos, int64_t pos, cudaStream_t s);
 
+// ---- persistent decode step (decode_mega.cu) --------------------------------
+struct MegaLayer {
+  DevMat qkv, wo, gateup, wdown;  // Q|K|V and gate|up stacked
+  const float *attn_norm = nullptr, *ffn_norm = nullptr;
+  const float *bq = nullptr, *bk = nullptr, *bv = nullptr, *bo = nullptr;
+  int skip_rope = 0;
+};
+struct MegaArgs {
+  int n_layers = 0;
+  int64_t H = 0, F = 0, V = 0, n_heads_q = 0, n_kv = 0, rotary_dim = 0;
+  float eps = 1e-5f, scale = 1.f;
+  const MegaLayer *layers = nullptr;  // device array [n_layers]
+  DevMat lm_head;
+  const float *out_norm = nullptr;
+  const uint8_t *emb = nullptr;
+  int emb_quant = 0;
+  int64_t emb_rows = 0;
+  const float *cos_tab = nullptr, *sin_tab = nullptr, *cos_long = nullptr, *sin_long = nullptr;
+  int64_t long_threshold = -1;
+  int neox = 0;
+  KvView kv;
+  int64_t window = 0;
+  int64_t *d_pos = nullptr;
+  uint32_t *d_token = nullptr, *d_hist = nullptr;
+  float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn = nullptr, *logits = nullptr;
+  int8_t *attn_q = nullptr;
+  float *attn_s = nullptr;
+  float *attn_part = nullptr;   // [n_kv][splits][4 * hd + 8] attention split partials
+  unsigned *head_cnt = nullptr; // [n_kv] split arrival counters (zero between steps)
+  unsigned *bar = nullptr;      // grid barrier: count, generation
+  float *am_val = nullptr;
+  int *am_idx = nullptr;
+  unsigned *am_cnt = nullptr;
+  int *err = nullptr;           // error word (bit 1 token, 2 KV wait, 8 grid wait)
+  int splits = 1;               // attention CTAs per KV head (<= 64)
+};
+// Whether the persistent decode step supports this model shape at `grid`
+// CTAs (head_dim, KV type, query heads per KV head, segment counts, shared
+// memory).
+int mega_check(const MegaArgs &a, int grid);
+// Bytes of the attention split partials (MegaArgs::attn_part).
+size_t mega_part_bytes(const MegaArgs &a);
+// Launches one decode token as a cooperative kernel of `grid` CTAs; the
+// kernel reads its arguments from dev_args, a device copy of `a`.  Returns 0
+// when no instantiation fits or the launch was rejected.
+int launch_decode_mega(const MegaArgs &a, const MegaArgs *dev_args, int grid, cudaStream_t s);
+// Whether a matrix can run the segmented decode GEMV (cols a multiple of 128
+// blocks of at most 16 segments, 32-byte aligned rows, Q4_0 / Q8_0).
+bool w4_matrix_ok(const DevMat &w);
+
 // Prefill: bias + RoPE on q/k rows, append k/v of m tokens into the cache.
 struct RopeAppendArgs {
   float *qkv = nullptr;  // [m][qkv_stride]: q | k | v

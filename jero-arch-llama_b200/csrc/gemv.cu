@@ -495,6 +495,15 @@ void set_attrs_all() {
 
 }  // namespace
 
+bool w4_matrix_ok(const DevMat &w) {
+  if (w.quant != JAL_Q4_0 && w.quant != JAL_Q8_0) return false;
+  const int64_t nb = w.cols / 32;
+  if (w.cols % 32 || nb % 4 != 0) return false;
+  if (w.qs_stride % 32 != 0 || (reinterpret_cast<uintptr_t>(w.qs) & 31) != 0) return false;
+  const int nseg = seg_count(w.cols);
+  return nseg >= 1 && nseg <= 16;
+}
+
 void gemv_init() {
   static bool done = false;
   if (done) return;

@@ -220,14 +220,28 @@ struct W4Row {
 
 // Segment `seg` of `row`; lanes past the row end (ragged last segment) load
 // zeros.
-template <int QUANT>
+// WIDE selects 32-byte loads; the 16-byte form is for code that ptxas
+// compiles as a separate (non-inlined) function, where the 32-byte form is
+// rejected.
+template <int QUANT, bool WIDE = true>
 __device__ __forceinline__ void w4_load(const DevMat &w, int64_t row, int seg, int nb, int lane, W4Row<QUANT> &r) {
   constexpr int NQ = W4Row<QUANT>::NQ;
   const int b0 = seg * kSegBlocks + 4 * lane;
   if (b0 < nb) {
     const uint8_t *q = w.qs + row * w.qs_stride + (size_t)b0 * (NQ / 4) * 4;
+    if constexpr (WIDE) {
 #pragma unroll
-    for (int j = 0; j < NQ / 8; j++) ldg_stream32(q + 32 * j, &r.q[8 * j]);
+      for (int j = 0; j < NQ / 8; j++) ldg_stream32(q + 32 * j, &r.q[8 * j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < NQ / 4; j++) {
+        const uint4 v = ldg_stream16(q + 16 * j);
+        r.q[4 * j] = v.x;
+        r.q[4 * j + 1] = v.y;
+        r.q[4 * j + 2] = v.z;
+        r.q[4 * j + 3] = v.w;
+      }
+    }
     r.d = ldg_stream8(w.d + row * w.d_stride + b0);
   } else {
 #pragma unroll

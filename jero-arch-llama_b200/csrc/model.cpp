@@ -766,6 +766,72 @@ static bool env_flag(const char *n) {
   return v && *v && *v != '0';
 }
 
+// Persistent decode step: one cooperative launch of one CTA per SM per
+// token (decode_mega.cu).  Opt-in with JAL_DECODE=mega, fast numerics only;
+// the context keeps the graph path when the model shape or the device does
+// not fit it.
+static void setup_mega(Context &ctx, int sms) {
+  const char *e = getenv("JAL_DECODE");
+  if (!e || strcmp(e, "mega") != 0 || ctx.cfg.numerics != JAL_NUMERICS_FAST) return;
+  const ModelCache &c = *ctx.cache;
+  const Geometry &g = ctx.g;
+  int coop = 0;
+  JAL_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c.device));
+  if (!coop) return;
+  std::vector<MegaLayer> layers(c.layers.size());
+  for (size_t l = 0; l < c.layers.size(); l++) {
+    const Layer &L = c.layers[l];
+    MegaLayer &m = layers[l];
+    m.qkv = L.qkv; m.wo = L.wo.dm; m.gateup = L.gateup; m.wdown = L.wdown.dm;
+    m.attn_norm = L.attn_norm; m.ffn_norm = L.ffn_norm;
+    m.bq = L.bq; m.bk = L.bk; m.bv = L.bv; m.bo = L.bo;
+    m.skip_rope = ctx.recipe.should_skip_rope(l) ? 1 : 0;
+    if (!w4_matrix_ok(m.qkv) || !w4_matrix_ok(m.wo) || !w4_matrix_ok(m.gateup) || !w4_matrix_ok(m.wdown)) return;
+  }
+  if (!w4_matrix_ok(c.lm_head.dm)) return;
+  MegaArgs &a = ctx.margs;
+  a.n_layers = (int)c.layers.size();
+  a.H = (int64_t)g.hidden_dim; a.F = (int64_t)g.ffn_dim; a.V = (int64_t)c.vocab_size;
+  a.n_heads_q = (int64_t)g.n_heads_q; a.n_kv = (int64_t)g.n_heads_kv; a.rotary_dim = (int64_t)g.rotary_dim;
+  a.eps = std::max(ctx.recipe.rms_eps, 1.0e-7f);
+  a.scale = 1.0f / sqrtf((float)g.head_dim);
+  a.lm_head = c.lm_head.dm;
+  a.out_norm = c.output_norm->as<float>();
+  a.emb = c.emb_raw->as<uint8_t>(); a.emb_quant = c.emb_quant; a.emb_rows = (int64_t)c.emb_rows;
+  a.cos_tab = ctx.cos_tab; a.sin_tab = ctx.sin_tab; a.cos_long = ctx.cos_long; a.sin_long = ctx.sin_long;
+  a.long_threshold = ctx.recipe.scaling.kind == JAL_ROPE_SCALING_LONGROPE
+                         ? (int64_t)ctx.recipe.scaling.original_max_position_embeddings : -1;
+  a.neox = ctx.recipe.rope_type == JAL_ROPE_NEOX;
+  a.kv = ctx.kv;
+  a.window = (int64_t)ctx.cfg.sliding_window;
+  a.d_pos = ctx.d_pos; a.d_token = ctx.d_token; a.d_hist = ctx.d_hist;
+  a.hidden = ctx.hidden; a.qkv = ctx.qkv; a.attn = ctx.attn; a.ffn = ctx.ffn; a.logits = ctx.logits;
+  a.attn_q = ctx.attn_q; a.attn_s = ctx.attn_s;
+  a.am_val = ctx.am_val; a.am_idx = ctx.am_idx; a.am_cnt = ctx.am_cnt;
+  a.err = ctx.d_err;
+  a.splits = std::max(1, std::min(64, sms / (int)g.n_heads_kv));
+  if (!mega_check(a, sms)) return;
+  const size_t part = mega_part_bytes(a);
+  auto lb = alloc(layers.size() * sizeof(MegaLayer) + 256 + part + 256 + g.n_heads_kv * 4 + 256 + 64 + 256 +
+                  sizeof(MegaArgs));
+  ctx.bufs.push_back(lb);
+  JAL_CUDA(cudaMemset(lb->ptr, 0, lb->bytes));
+  char *p = lb->as<char>();
+  auto take = [&](size_t n) { char *q = p; p += (n + 255) / 256 * 256; return q; };
+  MegaLayer *dl = (MegaLayer *)take(layers.size() * sizeof(MegaLayer));
+  JAL_CUDA(cudaMemcpy(dl, layers.data(), layers.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice));
+  a.layers = dl;
+  a.attn_part = (float *)take(part);
+  a.head_cnt = (unsigned *)take(g.n_heads_kv * 4);
+  a.bar = (unsigned *)take(8);
+  MegaArgs *da = (MegaArgs *)take(sizeof(MegaArgs));
+  if ((size_t)(p - lb->as<char>()) > lb->bytes) fail(JAL_ERR_INVALID_ARGUMENT, "internal: persistent decode layout overflow");
+  JAL_CUDA(cudaMemcpy(da, &a, sizeof(MegaArgs), cudaMemcpyHostToDevice));
+  ctx.mega_dev_args = da;
+  ctx.mega = true;
+  ctx.mega_grid = sms;
+}
+
 std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, const ContextConfig &cfg0) {
   JAL_CUDA(cudaSetDevice(c.device));
   auto ctx = std::make_unique<Context>();
@@ -870,6 +936,7 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
     ctx->s_qbuf = (float *)take2(Q * 4);
     ctx->s_q8 = (int8_t *)take2(kp);
   }
+  setup_mega(*ctx, sms);
   JAL_CUDA(cudaMallocHost(&ctx->h_pos, 8));
   JAL_CUDA(cudaMallocHost(&ctx->h_token, 4 * 8));
   JAL_CUDA(cudaStreamSynchronize(ctx->stream));
@@ -997,6 +1064,15 @@ void Context::run_decode_step() {
     enqueue_strict_token(true, true);
     JAL_CUDA(cudaGetLastError());
     return;
+  }
+  if (mega) {
+    if (launch_decode_mega(margs, mega_dev_args, mega_grid, stream)) {
+      launches_per_step = 1;
+      JAL_CUDA(cudaGetLastError());
+      return;
+    }
+    cudaGetLastError();  // launch rejected: keep the graph path from now on
+    mega = false;
   }
   if (cfg.use_graphs) {
     if (!graph) {

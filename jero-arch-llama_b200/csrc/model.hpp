@@ -152,6 +152,11 @@ struct Context {
   // graph
   cudaGraphExec_t graph = nullptr;
   size_t launches_per_step = 0;
+  // persistent decode step (decode_mega.cu), opt-in with JAL_DECODE=mega
+  bool mega = false;
+  int mega_grid = 0;
+  MegaArgs margs;                         // host copy
+  const MegaArgs *mega_dev_args = nullptr;  // device copy the kernel reads
 
   ~Context();
   void enqueue_decode_step(bool pdl);

@@ -215,3 +215,44 @@ def test_fail_closed_errors_keep_position(jal, oracle, torch_cuda):
         assert ctx.position() == 20
         with pytest.raises(jal.ContextLengthExceeded):
             ctx.prefill_step(prompt_of(1, n=21), 0)
+
+
+@pytest.mark.parametrize("kv_name", ["KV_F32", "KV_F16"])
+def test_persistent_decode_kernel_matches_oracle(jal, oracle, torch_cuda, monkeypatch, kv_name):
+    """JAL_DECODE=mega: one cooperative launch per token (decode_mega.cu).
+
+    Same fast-numerics bars as the graph path (teacher-forced against the
+    oracle), plus self-consistency of the on-device greedy loop: the argmax
+    phase picks the host argmax of the same kernel's logits at every step.
+    FFN 1536 keeps every projection on the segmented path (blocks per row a
+    multiple of 4).
+    """
+    spec = jal.SynthSpec(ffn_dim=1536)
+    kv = getattr(jal, kv_name)
+    buf = jal.synth_gguf(spec, 909)
+    _, tensors = gguf_py.parse(buf)
+    om = oracle.Model(tensors, geom_of(spec), nthreads=8)
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    cache = recipe.build_repack_cache(buf)
+    monkeypatch.setenv("JAL_DECODE", "mega")
+    ctx = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_FAST)
+    ctx_greedy = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_FAST)
+    monkeypatch.delenv("JAL_DECODE")
+    prompt = prompt_of(21)
+    worst, agree = run_fast(om, ctx, prompt, 48, 256)
+    assert ctx.launches_per_step() == 1
+    print(f"persistent decode {kv_name} worst |dlogit| = {worst:.3e}, top-1 agreement {agree:.2f}")
+    # Host argmax of step-by-step logits == the kernel's own greedy loop.
+    lg = ctx_greedy.prefill_step(prompt, 0)
+    first = int(np.argmax(lg))
+    monkeypatch.setenv("JAL_DECODE", "mega")
+    ctx_host = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_FAST)
+    monkeypatch.delenv("JAL_DECODE")
+    ctx_host.prefill_step(prompt, 0)
+    host, tok = [], first
+    for _ in range(32):
+        host.append(tok)
+        tok = int(np.argmax(ctx_host.decode_step(tok)))
+    seq = ctx_greedy.decode_greedy(first, 32)
+    assert [first] + [int(t) for t in seq[:-1]] == host
+    assert ctx_greedy.position() == len(prompt) + 32
