@@ -483,10 +483,11 @@ static void check_device_error(Context &c) {
     JAL_CUDA(cudaMemsetAsync(c.margs.bar, 0, 8, c.stream));
     JAL_CUDA(cudaMemsetAsync(c.margs.head_cnt, 0, (size_t)c.margs.n_kv * 4, c.stream));
     JAL_CUDA(cudaMemsetAsync(c.margs.am_cnt, 0, 4, c.stream));
+    JAL_CUDA(cudaMemsetAsync(c.margs.ffn_cnt, 0, (size_t)(c.margs.F / 32) * 4, c.stream));
   }
   JAL_CUDA(cudaStreamSynchronize(c.stream));
   if (e & 8u) fail(JAL_ERR_TIMEOUT, "persistent decode step: a bounded grid barrier wait gave up");
-  if (e & 2u) fail(JAL_ERR_TIMEOUT, "decode attention: a bounded wait for KV tile copies gave up");
+  if (e & 2u) fail(JAL_ERR_TIMEOUT, "decode step: a bounded wait for KV-tile or weight copies gave up");
   fail(JAL_ERR_TENSOR_BOUNDS, "embedding lookup saw an out-of-range token id");
 }
 

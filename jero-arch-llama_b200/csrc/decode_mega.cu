@@ -4,25 +4,37 @@
 // embedding, every layer's five phases (Q/K/V projection, attention, O
 // projection + residual, gate/up projection + SwiGLU, down projection +
 // residual) and the LM head with greedy argmax.  Phases are separated by a
-// grid barrier instead of kernel boundaries, so no CTA has to be scheduled
-// between phases, and each CTA starts the next phases' memory traffic before
-// it waits:
-//   - before each barrier, thread 0 asks the copy engine to prefetch this
-//     CTA's first rows of the projection after next into L2;
-//   - at the end of the Q/K/V phase the CTA starts the bulk copies of its
-//     attention slice of the cache (positions below the current one).
-// Projection phases run the segmented fast path of gemv_dev.cuh on the
-// CTA's contiguous row range.  Attention splits every KV head over
-// grid / n_kv CTAs; each writes its partial (max, denominator, P.V) to global
-// memory and the last CTA of a head to finish merges the partials in split
-// order and writes the head group's output and its QuantizedActQ8 form.
-// Every wait is bounded: a grid barrier that gives up sets bit 8 of the
-// context error word (a KV tile wait bit 2) and later barriers stop waiting,
-// so the kernel always finishes.
+// grid barrier instead of kernel boundaries.
 //
-// The phases are separate (non-inlined) device functions so that each gets
-// its own register allocation; the projection phase uses 16-byte loads
-// because ptxas rejects the 32-byte form in a non-inlined function.
+// Weight streaming.  Every byte a CTA reads from HBM in the step is known
+// when the step starts: its contiguous row slice of each projection (the
+// row-interleaved layout makes a row range one byte range) and the KV-cache
+// tiles of its attention slice (positions before the current one).  Thread 0
+// walks that sequence (the CTA's "stream": layer by layer Q/K/V rows, KV
+// tiles, O rows, gate and up rows in pairs, down rows; then LM head rows)
+// and keeps it flowing through a ring of kSlots x 32 KB shared-memory slots
+// with bulk copies (cp.async.bulk, one mbarrier per slot).  The warps
+// consume the slots in stream order and thread 0 refills each slot with the
+// chunk kSlots ahead as soon as it is released, so HBM keeps streaming
+// through grid barriers, activation prologues and attention, up to the
+// ring's depth (bulk copies of >= 16 KB kept 4+ deep per SM sustain the
+// full HBM rate).
+//
+// Projection phases: the activation (QuantizedActQ8 per 32-block, RMSNorm
+// first where the layer has one) is formed in the work area of shared memory
+// and held in registers per warp (warp w takes 128-block segment w % nseg of
+// every row, lane l blocks l, l + 32, l + 64, l + 96 of the segment, so the
+// shared-memory reads of a row are conflict-free); the weight rows come from
+// the ring.  Attention: each KV head is split over up to `splits` CTAs (one
+// split per attn_split_tokens attended positions); a CTA consumes its tiles
+// from the ring, and with several splits the last CTA of a head to finish
+// merges the partials in split order.  The gate/up phase also writes the
+// SwiGLU row as QuantizedActQ8 (the CTA completing a 32-block quantizes
+// it), which the down projection reads directly.
+//
+// Every wait is bounded: a grid barrier that gives up sets bit 8 of the
+// context error word (a ring wait bit 2) and later barriers stop waiting, so
+// the kernel always finishes.
 #include <cuda_fp16.h>
 
 #include "attn_dev.cuh"
@@ -41,45 +53,49 @@ using namespace adev;
 constexpr int kMW = 8;  // warps per CTA (up to 255 registers per thread)
 constexpr int kMT = kMW * 32;
 constexpr uint32_t kGridSpin = 1u << 22;  // bounded polls of a grid barrier
-constexpr int kErrAttnWait = 2, kErrGridWait = 8;
-constexpr int64_t kPrefetchBytes = 64 * 1024;
-constexpr size_t kAttnWs = 16 * 1024;  // attention workspace after the K/V ring
-#ifndef JAL_MEGA_DQ4
-#define JAL_MEGA_DQ4 4
-#endif
-constexpr int kDepthQ4 = JAL_MEGA_DQ4, kDepthQ8 = 3;  // rows in flight per warp
+constexpr int kErrRingWait = 2, kErrGridWait = 8;
+constexpr int kSlots = 6;
+constexpr int kSlotBytes = kStageBytes;  // 32 KB: one KV tile (K then V) or whole weight rows
+constexpr size_t kRingBytes = (size_t)kSlots * kSlotBytes;
+constexpr size_t kWorkBytes = 25 * 1024;  // activation / attention workspace after the ring
+constexpr int kMaxLayers = 64;
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
-// Sense-reversing barrier over all CTAs of the cooperative grid.  bar[0]
-// counts arrivals, bar[1] is the generation.  Once a wait gives up, this CTA
-// stops waiting at later barriers (*broken).
-__device__ __noinline__ void grid_sync(unsigned *bar, int *err, int *broken) {
+// Barrier over all CTAs of the cooperative grid: bar[0] counts arrivals
+// over the whole launch (one per CTA per barrier) and barrier k completes
+// when it reaches k * gridDim.x, so an arrival is a single atomic and the
+// waiters poll one word.  The last CTA of the argmax phase returns the
+// counter to zero.  A wait that gives up sets bit 8 of the error word and
+// this CTA stops waiting at later barriers (*broken), still arriving at each
+// so the count stays consistent.
+struct GridBar {
+  unsigned *bar;
+  int *err;
+  int *broken;
+  unsigned *seq;  // barriers passed by this CTA (shared)
+};
+
+__device__ __noinline__ void grid_sync(const GridBar &g) {
   __syncthreads();
-  if (threadIdx.x == 0 && !*broken) {
-    unsigned *count = bar, *gen = bar + 1;
-    const unsigned g = ld_acquire(gen);
+  if (threadIdx.x == 0) {
+    const unsigned k = *g.seq + 1;
+    *g.seq = k;
+    const unsigned target = k * gridDim.x;
     __threadfence();
-    if (atomicAdd(count, 1u) == gridDim.x - 1) {
-      atomicExch(count, 0u);
-      __threadfence();
-      st_release(gen, g + 1);
-    } else {
+    atomicAdd(g.bar, 1u);
+    if (!*g.broken) {
       uint32_t it = 0;
-      while (ld_acquire(gen) == g) {
+      while (ld_acquire(g.bar) < target) {
         if (++it > kGridSpin) {
-          *broken = 1;
-          if (err) atomicOr(err, kErrGridWait);
+          *g.broken = 1;
+          if (g.err) atomicOr(g.err, kErrGridWait);
           break;
         }
-        __nanosleep(32);
       }
     }
     __threadfence();
@@ -93,196 +109,414 @@ __device__ __forceinline__ void cta_rows(int64_t rows, int64_t &r0, int64_t &cnt
   cnt = base + (c < rem ? 1 : 0);
 }
 
-// Thread 0: L2 prefetch of this CTA's first rows of a projection.
-__device__ __forceinline__ void prefetch_rows(const DevMat &w, int64_t rows, int units, int64_t up_offset) {
-  if (threadIdx.x != 0) return;
-  int64_t r0, cnt;
-  cta_rows(rows, r0, cnt);
-  if (cnt <= 0) return;
-  int64_t pr = kPrefetchBytes / (units * w.qs_stride);
-  if (pr < 1) pr = 1;
-  if (pr > cnt) pr = cnt;
-  for (int u = 0; u < units; u++)
-    l2_prefetch_bulk(w.qs + (r0 + (u ? up_offset : 0)) * w.qs_stride, (uint64_t)(pr * w.qs_stride));
+// Attention work of this CTA: KV head h, split si of S (S <= a.splits grows
+// with the attended span, one split per attn_split_tokens positions), tiles
+// of tp positions.
+struct Slice {
+  int h, si, S;
+  int64_t pos, s0, s1;
+  int nt;
+  bool active;
+};
+
+__device__ __forceinline__ Slice attn_slice(const MegaArgs &a, int64_t pos, int tp) {
+  Slice s;
+  const int c = blockIdx.x;
+  s.h = c / a.splits;
+  s.si = c % a.splits;
+  s.pos = pos;
+  const int64_t seq = pos + 1;
+  const int64_t lo = (a.window > 0 && seq > a.window) ? seq - a.window : 0;
+  const int64_t span = seq - lo, st = a.attn_split_tokens > 0 ? a.attn_split_tokens : 1;
+  int64_t se = (span + st - 1) / st;
+  se = se < 1 ? 1 : (se > a.splits ? a.splits : se);
+  s.S = (int)se;
+  s.active = c < a.n_kv * a.splits && s.si < s.S;
+  const int64_t per = (span + s.S - 1) / s.S;
+  s.s0 = lo + s.si * per;
+  s.s1 = s.s0 + per < seq ? s.s0 + per : seq;
+  const int64_t len = s.s1 > s.s0 ? s.s1 - s.s0 : 0;
+  s.nt = s.active ? (int)((len + tp - 1) / tp) : 0;
+  return s;
 }
 
-// One projection on this CTA's contiguous row range (segmented fast path of
-// the per-projection kernel, with the output mode a run-time value).
+// ---- the CTA's stream ----------------------------------------------------
+// A row slice of one projection, cut into chunks of rpc whole rows.
+struct Rows {
+  int64_t r0, cnt;
+  int rpc, n;
+};
+
+__device__ __forceinline__ Rows make_rows(int64_t rows, int64_t qs_stride) {
+  Rows r;
+  cta_rows(rows, r.r0, r.cnt);
+  const int64_t rpc = kSlotBytes / qs_stride;
+  r.rpc = (int)(rpc < 1 ? 1 : rpc);
+  r.n = (int)((r.cnt + r.rpc - 1) / r.rpc);
+  return r;
+}
+
+// Per-CTA stream layout, computed once per launch (shared memory), with
+// everything thread 0 needs to issue any chunk without touching global
+// memory (except the KV page table).
+struct Plan {
+  int64_t pos;
+  Slice sl;
+  Rows q, o, gu, dn, head;  // gu: gate rows (its chunks come in gate/up pairs)
+  int per_layer, total;     // chunks per layer; chunks in the launch
+  int n_layers;
+  int64_t up_offset;        // rows from a gate row to its up row (F)
+  int64_t st[5];            // row bytes: Q/K/V, O, gate/up, down, LM head
+  const uint8_t *head_qs;
+  KvView kv;
+  const uint8_t *qs[kMaxLayers][4];  // per layer: Q/K/V, O, gate/up, down
+};
+
+// All threads: the per-layer weight table; then thread 0 the rest.
+__device__ __forceinline__ void make_plan(const MegaArgs &a, int64_t pos, int tp, Plan &p) {
+  for (int i = threadIdx.x; i < a.n_layers * 4; i += kMT) {
+    const MegaLayer &L = a.layers[i / 4];
+    const int k = i % 4;
+    p.qs[i / 4][k] = k == 0 ? L.qkv.qs : k == 1 ? L.wo.qs : k == 2 ? L.gateup.qs : L.wdown.qs;
+  }
+  if (threadIdx.x != 0) return;
+  const int64_t HD = a.kv.head_dim, QKV = (a.n_heads_q + 2 * a.n_kv) * HD;
+  const MegaLayer &L0 = a.layers[0];
+  p.pos = pos;
+  p.sl = attn_slice(a, pos, tp);
+  p.st[0] = L0.qkv.qs_stride;
+  p.st[1] = L0.wo.qs_stride;
+  p.st[2] = L0.gateup.qs_stride;
+  p.st[3] = L0.wdown.qs_stride;
+  p.st[4] = a.lm_head.qs_stride;
+  p.q = make_rows(QKV, p.st[0]);
+  p.o = make_rows(a.H, p.st[1]);
+  p.gu = make_rows(a.F, p.st[2]);
+  p.dn = make_rows(a.H, p.st[3]);
+  p.head = make_rows(a.V, p.st[4]);
+  p.per_layer = p.q.n + p.sl.nt + p.o.n + 2 * p.gu.n + p.dn.n;
+  p.n_layers = a.n_layers;
+  p.total = a.n_layers * p.per_layer + p.head.n;
+  p.up_offset = a.F;
+  p.head_qs = a.lm_head.qs;
+  p.kv = a.kv;
+}
+
+struct Ring {
+  char *base;      // kSlots x kSlotBytes
+  uint64_t *full;  // [kSlots] one mbarrier per slot (completes when its bytes land)
+};
+
+__device__ __forceinline__ char *slot_ptr(const Ring &r, unsigned j) { return r.base + (size_t)(j % kSlots) * kSlotBytes; }
+
+__device__ __forceinline__ void issue_rows(const uint8_t *qs, int64_t stride, const Rows &rs, int i, int64_t row_offset,
+                                           char *dst, uint64_t *bar) {
+  const int64_t first = rs.r0 + (int64_t)i * rs.rpc;
+  const int64_t n = rs.cnt - (int64_t)i * rs.rpc < rs.rpc ? rs.cnt - (int64_t)i * rs.rpc : rs.rpc;
+  const uint32_t bytes = (uint32_t)(n * stride);
+  mbar_expect_tx(bar, bytes);
+  bulk_g2s(dst, qs + (first + row_offset) * stride, bytes, bar);
+}
+
+// Thread 0: copy stream chunk j into its slot (nothing past the end).
+template <int HD, bool F16>
+__device__ __forceinline__ void ring_issue(const Plan &p, const Ring &r, unsigned j) {
+  if ((int)j >= p.total) return;
+  char *dst = slot_ptr(r, j);
+  uint64_t *bar = &r.full[j % kSlots];
+  const int lay_chunks = p.n_layers * p.per_layer;
+  if ((int)j >= lay_chunks) {
+    issue_rows(p.head_qs, p.st[4], p.head, (int)j - lay_chunks, 0, dst, bar);
+    return;
+  }
+  const int l = (int)j / p.per_layer;
+  int o = (int)j - l * p.per_layer;
+  if (o < p.q.n) { issue_rows(p.qs[l][0], p.st[0], p.q, o, 0, dst, bar); return; }
+  o -= p.q.n;
+  if (o < p.sl.nt) {
+    using Gm = AttnGeom<HD, F16, 1>;
+    const int64_t t0 = p.sl.s0 + (int64_t)o * Gm::TP;
+    const int n = (int)(p.sl.s1 - t0 < Gm::TP ? p.sl.s1 - t0 : Gm::TP);
+    issue_tile<HD, F16>(p.kv, l, dst, bar, t0, n, p.sl.h);
+    return;
+  }
+  o -= p.sl.nt;
+  if (o < p.o.n) { issue_rows(p.qs[l][1], p.st[1], p.o, o, 0, dst, bar); return; }
+  o -= p.o.n;
+  if (o < 2 * p.gu.n) { issue_rows(p.qs[l][2], p.st[2], p.gu, o / 2, (o & 1) ? p.up_offset : 0, dst, bar); return; }
+  o -= 2 * p.gu.n;
+  issue_rows(p.qs[l][3], p.st[3], p.dn, o, 0, dst, bar);
+}
+
+// All threads: wait until stream chunk j has landed.
+__device__ __forceinline__ void ring_wait(const Ring &r, unsigned j, int *err) {
+  if (!mbar_wait_bounded(&r.full[j % kSlots], (j / kSlots) & 1u) && err) atomicOr(err, kErrRingWait);
+}
+
+// After every thread is done with chunk j (the caller synchronises), thread
+// 0 refills its slot with chunk j + kSlots.  `wrote`: the slot was also
+// written through the generic proxy, which must be ordered before the
+// async-proxy refill.
+template <int HD, bool F16>
+__device__ __forceinline__ void ring_release(const Plan &p, const Ring &r, unsigned j, bool wrote) {
+  if (threadIdx.x == 0) {
+    if (wrote) fence_proxy_async();
+    ring_issue<HD, F16>(p, r, j + kSlots);
+  }
+}
+
+// ---- projection phases -----------------------------------------------------
+// SwiGLU rows [r0, r0 + cnt) of this CTA are in a.y.  Each 32-block they
+// touch gets this CTA's row count added to its counter; the CTA that brings
+// a block to 32 quantizes it (QuantizedActQ8, the same values the consumer
+// would compute from the f32 row) and clears the counter.
+__device__ __forceinline__ void quantize_done_blocks(const GemvArgs &a, int64_t r0, int64_t cnt) {
+  __shared__ int done_s[kMW];
+  if (cnt <= 0) return;  // CTA-uniform
+  const int64_t b0 = r0 / 32, b1 = (r0 + cnt - 1) / 32;
+  __threadfence();  // this thread's rows are visible before the counters move
+  __syncthreads();
+  const int w = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int64_t bb = b0; bb <= b1; bb += kMW) {
+    if (threadIdx.x < kMW) {
+      const int64_t b = bb + threadIdx.x;
+      int done = 0;
+      if (b <= b1) {
+        const int64_t lo = r0 > b * 32 ? r0 : b * 32;
+        const int64_t hi = r0 + cnt < b * 32 + 32 ? r0 + cnt : b * 32 + 32;
+        const unsigned n = (unsigned)(hi - lo);
+        done = atomicAdd(&a.ycnt[b], n) + n == 32u;
+      }
+      done_s[threadIdx.x] = done;
+    }
+    __syncthreads();
+    const int64_t b = bb + w;
+    if (b <= b1 && done_s[w]) {
+      __threadfence();
+      float v = __ldcg(a.y + b * 32 + lane);
+      if (!isfinite(v)) v = 0.0f;
+      const float amax = warp_max(fabsf(v));
+      const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
+      a.yq[b * 32 + lane] = act_quant_one(v, inv);
+      if (lane == 0) {
+        a.ys[b] = scale;
+        a.ycnt[b] = 0u;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Row segment of one weight row in a ring slot (same layout as in HBM:
+// quants, then the f16 scales): blocks seg * 128 + lane + 32 v, v < 4.
 template <int QUANT>
-__device__ __forceinline__ void gemv_phase(const GemvArgs &a, char *smem, float *red) {
-  constexpr int DEPTH = QUANT == JAL_Q4_0 ? kDepthQ4 : kDepthQ8;
-  const int out = a.out_mode;
-  const int ush = out == GEMV_OUT_SWIGLU ? 1 : 0;  // log2 of units per row
-  const int nb = (int)(a.w.cols / 32), nseg = seg_count(a.w.cols), nbp = nseg * kSegBlocks;
+__device__ __forceinline__ void w4s_load(const char *row, int nb, int seg, int lane, W4Row<QUANT> &r) {
+  constexpr int BQ = QUANT == JAL_Q4_0 ? 16 : 32;  // quant bytes per block
+  const uint16_t *d = (const uint16_t *)(row + (size_t)nb * BQ);
+  uint32_t h[4];
+#pragma unroll
+  for (int v = 0; v < 4; v++) {
+    const int b = seg * kSegBlocks + lane + 32 * v;
+    if (b < nb) {
+      const uint4 q0 = *(const uint4 *)(row + (size_t)b * BQ);
+      r.q[(BQ / 4) * v + 0] = q0.x; r.q[(BQ / 4) * v + 1] = q0.y;
+      r.q[(BQ / 4) * v + 2] = q0.z; r.q[(BQ / 4) * v + 3] = q0.w;
+      if (BQ == 32) {
+        const uint4 q1 = *(const uint4 *)(row + (size_t)b * BQ + 16);
+        r.q[(BQ / 4) * v + 4] = q1.x; r.q[(BQ / 4) * v + 5] = q1.y;
+        r.q[(BQ / 4) * v + 6] = q1.z; r.q[(BQ / 4) * v + 7] = q1.w;
+      }
+      h[v] = d[b];
+    } else {
+#pragma unroll
+      for (int k = 0; k < BQ / 4; k++) r.q[(BQ / 4) * v + k] = 0u;
+      h[v] = 0u;
+    }
+  }
+  r.d = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+}
+
+// One projection over this CTA's row slice, weights from the ring.  j is the
+// stream index of the phase's first chunk; returns the index after its last.
+template <int QUANT, int HD, bool F16>
+__device__ __noinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, const Ring &r, const GemvArgs &g,
+                                             const Rows &rs, unsigned j, char *work, float *red) {
+  const int nb = (int)(g.w.cols / 32), nseg = seg_count(g.w.cols), nbp = nseg * kSegBlocks;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int seg = warp % nseg, phase = warp / nseg, nph = kMW / nseg;
-  int64_t r0, cnt;
-  cta_rows(a.rows, r0, cnt);
-  const int my_rows = (phase < nph && cnt > phase) ? (int)((cnt - 1 - phase) / nph + 1) : 0;
-  const int64_t gw = r0 + phase;
-  const int total = my_rows << ush;
-  float *part = (float *)(smem + w4_act_region(a.in_mode, nb, nseg));  // [cnt][nseg]
-#define UNIT_ROW(k) (gw + (int64_t)((k) >> ush) * nph + ((ush && ((k) & 1)) ? a.up_offset : 0))
-  gemv_prologue_pre<1, kMW>(a, smem, nb, nbp);
-  gemv_prologue<1, kMW>(a, smem, nb, nbp, red);
-  W4Row<QUANT> buf[DEPTH];
-#pragma unroll
-  for (int j = 0; j < DEPTH; j++)
-    if (j < total) w4_load<QUANT, false>(a.w, UNIT_ROW(j), seg, nb, lane, buf[j]);
+  const bool swiglu = g.out_mode == GEMV_OUT_SWIGLU;
+  if (g.out_mode == GEMV_OUT_ADD) {  // residual rows of this CTA, read once (visible after the prologue's barrier)
+    float *yb = (float *)(work + w4_act_region(g.in_mode, nb, nseg)) + rs.rpc * nseg;
+    for (int i = threadIdx.x; i < rs.cnt; i += kMT) yb[i] = g.y[rs.r0 + i];
+  }
+  if (g.in_mode == GEMV_IN_NORM && nb * 4 <= 4 * kMT) {
+    prologue_m1_impl<kMW, 4, true>(g, work, nb, nbp, red);
+  } else {
+    gemv_prologue_pre<1, kMW>(g, work, nb, nbp);
+    gemv_prologue<1, kMW>(g, work, nb, nbp, red);
+  }
   W4Act x;
 #pragma unroll
   for (int v = 0; v < 4; v++) {
-    const int b = seg * kSegBlocks + 4 * lane + v;
-    x.lo[v] = ((const int4 *)smem)[b];
-    x.hi[v] = ((const int4 *)(smem + nbp * 16))[b];
-    const float2 ss = ((const float2 *)(smem + nbp * 32))[b];
+    const int b = seg * kSegBlocks + lane + 32 * v;  // < nbp; padding blocks are zero
+    x.lo[v] = ((const int4 *)work)[b];
+    x.hi[v] = ((const int4 *)(work + nbp * 16))[b];
+    const float2 ss = ((const float2 *)(work + nbp * 32))[b];
     x.sc[v] = ss.x;
     x.sum[v] = __float_as_int(ss.y);
   }
-  float gate = 0.0f;
-  for (int k0 = 0; k0 < total; k0 += DEPTH) {
+  float *part = (float *)(work + w4_act_region(g.in_mode, nb, nseg));  // [rpc][nseg]
+  const int64_t qs = g.w.qs_stride, r0 = rs.r0, cnt = rs.cnt;
+  const int rpc = rs.rpc, nch = rs.n;
+  const bool add = g.out_mode == GEMV_OUT_ADD;
+  float *y = g.y, *ybase = part + rpc * nseg;  // ybase: [cnt] residual + bias of this CTA's rows
+  const float *bias = g.bias;
+  const char *rbase = r.base;
+  uint64_t *full = r.full;
+  int *err = a.err;
+  // output row i of this CTA: y + bias (ADD) or bias (STORE) added to the dot
+  auto finish = [&](int64_t i, float s) -> float {
+    return add ? ybase[i] + (bias ? s + bias[r0 + i] : s) : (bias ? s + bias[r0 + i] : s);
+  };
+  for (int c = 0; c < nch; c++) {
+    const int64_t first = (int64_t)c * rpc;  // first row of the chunk, relative to r0
+    const int n = (int)(cnt - first < rpc ? cnt - first : rpc);
+    if (!mbar_wait_bounded(&full[j % kSlots], (j / kSlots) & 1u) && err) atomicOr(err, kErrRingWait);
+    if (swiglu && !mbar_wait_bounded(&full[(j + 1) % kSlots], ((j + 1) / kSlots) & 1u) && err)
+      atomicOr(err, kErrRingWait);
+    const char *wg = rbase + (size_t)(j % kSlots) * kSlotBytes;
+    const char *wu = rbase + (size_t)((j + 1) % kSlots) * kSlotBytes;
+    if (phase < nph) {
+      if (swiglu) {
+        for (int lr = phase; lr < n; lr += nph) {
+          W4Row<QUANT> wa, wb;
+          w4s_load<QUANT>(wg + (size_t)lr * qs, nb, seg, lane, wa);
+          w4s_load<QUANT>(wu + (size_t)lr * qs, nb, seg, lane, wb);
+          float sa = w4_dot<QUANT>(wa, x), sb = w4_dot<QUANT>(wb, x);
 #pragma unroll
-    for (int j = 0; j < DEPTH; j++) {
-      const int k = k0 + j;
-      if (k < total) {
-        float s = w4_dot<QUANT>(buf[j], x);
-        if (k + DEPTH < total) w4_load<QUANT, false>(a.w, UNIT_ROW(k + DEPTH), seg, nb, lane, buf[j]);
-        s = warp_sum(s);
-        const int li = phase + (k >> ush) * nph;
-        if (ush && (k & 1) == 0) {
-          gate = s;
-        } else if (nseg > 1) {
-          if (lane == 0) part[li * nseg + seg] = s;
-        } else if (lane == 0) {
-          const int64_t lr = r0 + li;
-          float *yp = a.y + lr;
-          if (out == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
-          else if (out == GEMV_OUT_ADD) *yp = *yp + (a.bias ? s + a.bias[lr] : s);
-          else *yp = swiglu_one(gate, s);
+          for (int o = 16; o > 0; o >>= 1) {
+            sa += __shfl_xor_sync(0xffffffffu, sa, o);
+            sb += __shfl_xor_sync(0xffffffffu, sb, o);
+          }
+          if (lane == 0) y[r0 + first + lr] = swiglu_one(sa, sb);
+        }
+      } else {
+        for (int lr = phase; lr < n; lr += 2 * nph) {  // two rows at a time
+          const int lr2 = lr + nph;
+          const bool two = lr2 < n;
+          W4Row<QUANT> wa, wb;
+          w4s_load<QUANT>(wg + (size_t)lr * qs, nb, seg, lane, wa);
+          if (two) w4s_load<QUANT>(wg + (size_t)lr2 * qs, nb, seg, lane, wb);
+          float sa = w4_dot<QUANT>(wa, x), sb = two ? w4_dot<QUANT>(wb, x) : 0.0f;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            sa += __shfl_xor_sync(0xffffffffu, sa, o);
+            sb += __shfl_xor_sync(0xffffffffu, sb, o);
+          }
+          if (lane == 0) {
+            if (nseg > 1) {
+              part[lr * nseg + seg] = sa;
+              if (two) part[lr2 * nseg + seg] = sb;
+            } else {
+              y[r0 + first + lr] = finish(first + lr, sa);
+              if (two) y[r0 + first + lr2] = finish(first + lr2, sb);
+            }
+          }
+        }
+      }
+    }
+    if (nseg > 1 && !swiglu) {
+      __syncthreads();
+      if ((int)threadIdx.x < n) {
+        float sum = 0.0f;
+        for (int q = 0; q < nseg; q++) sum += part[threadIdx.x * nseg + q];
+        y[r0 + first + threadIdx.x] = finish(first + threadIdx.x, sum);
+      }
+    }
+    __syncthreads();
+    ring_release<HD, F16>(p, r, j, false);
+    if (swiglu) ring_release<HD, F16>(p, r, j + 1, false);
+    j += swiglu ? 2 : 1;
+  }
+  if (swiglu && g.yq) quantize_done_blocks(g, rs.r0, rs.cnt);
+  __syncthreads();
+  return j;
+}
+
+// ---- attention -------------------------------------------------------------
+template <int HD, bool F16, int GP>
+__device__ __noinline__ unsigned attn_stream(const MegaArgs &a, const Plan &p, const Ring &r, int layer, unsigned j,
+                                             char *work) {
+  using Gm = AttnGeom<HD, F16, kMW>;
+  constexpr int TP = Gm::TP, LG = Gm::LG, PPS = Gm::PPS, DPL = Gm::DPL, TPW = Gm::TPW, VD = Gm::VD;
+  const Slice &sl = p.sl;
+  if (!sl.active) return j;
+  const MegaLayer &L = a.layers[layer];
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int G = (int)(a.n_heads_q / a.n_kv), h = sl.h, S = a.splits;
+  const int64_t Q = a.n_heads_q * HD, KVD = a.n_kv * HD, pos = sl.pos, seq = pos + 1;
+  float(*q_s)[HD] = (float(*)[HD])work;                  // [GP][HD]
+  float *kn_s = (float *)(work + GP * HD * 4);          // [HD]
+  float *vn_s = kn_s + HD;                              // [HD]
+  float *p_all = vn_s + HD;                             // [kMW][TPW * GP]
+  float *wm_s = p_all + kMW * TPW * GP;                 // [64 + 1][GP]: warp, then split merge weights
+  float *den = wm_s + 65 * GP;                          // [GP]
+  int *flag_s = (int *)(den + GP);
+  float *acc_w = (float *)(work + 8192);                // [kMW][GP][HD] warp partials
+  float *m_w = acc_w + kMW * GP * HD;                   // [kMW][GP]
+  float *l_w = m_w + kMW * GP;                          // [kMW][GP]
+  const bool rope = !L.skip_rope && pos > 0;
+  const int half = (int)(a.rotary_dim / 2);
+  const bool use_long = a.long_threshold >= 0 && seq > a.long_threshold;
+  const float *ct = (use_long ? a.cos_long : a.cos_tab) + pos * half;
+  const float *st = (use_long ? a.sin_long : a.sin_tab) + pos * half;
+  const bool own_pos = pos >= sl.s0 && pos < sl.s1;
+  const int64_t app = own_pos ? kv_elem(a.kv, layer, h, pos) : 0;
+  // q heads (GP rows, zero past G), then the new k and v: bias, RoPE
+  // (recipe.rs:2750-2767) and, for k / v, the value the cache stores.  All
+  // global loads of the pass are issued first, then the values are formed.
+  constexpr int NIT = ((GP + 2) * HD + kMT - 1) / kMT;
+  float xv[NIT], pv[NIT], cv[NIT], sv[NIT];
+#pragma unroll
+  for (int it = 0; it < NIT; it++) {
+    const int i = tid + it * kMT;
+    xv[it] = 0.0f; pv[it] = 0.0f; cv[it] = 1.0f; sv[it] = 0.0f;
+    if (i < (GP + 2) * HD) {
+      const int g = i / HD, d = i % HD;
+      if (g >= GP || g < G) {
+        const int64_t off = g < GP ? (int64_t)(h * G + g) * HD : (g == GP ? Q : Q + KVD) + (int64_t)h * HD;
+        const float *bias = g < GP ? L.bq : (g == GP ? L.bk : L.bv);
+        const int64_t boff = g < GP ? (int64_t)(h * G + g) * HD : (int64_t)h * HD;
+        float o = a.qkv[off + d];
+        if (bias) o = __fadd_rn(o, bias[boff + d]);
+        xv[it] = o;
+        if (rope && g <= GP && d < 2 * half) {
+          const bool first = a.neox ? d < half : (d & 1) == 0;
+          const int jj = a.neox ? (first ? d : d - half) : d / 2;
+          const int partner = a.neox ? (first ? d + half : d - half) : (d ^ 1);
+          float other = a.qkv[off + partner];
+          if (bias) other = __fadd_rn(other, bias[boff + partner]);
+          pv[it] = other;
+          cv[it] = ct[jj];
+          sv[it] = st[jj];
         }
       }
     }
   }
-#undef UNIT_ROW
-  if (nseg > 1 && !ush) {
-    __syncthreads();
-    for (int li = threadIdx.x; li < cnt; li += kMT) {
-      float s = 0.0f;
-      for (int q = 0; q < nseg; q++) s += part[li * nseg + q];
-      const int64_t lr = r0 + li;
-      float *yp = a.y + lr;
-      if (out == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
-      else *yp = *yp + (a.bias ? s + a.bias[lr] : s);
-    }
-  }
-  __syncthreads();
-}
-
-// The one projection routine of the kernel: a single non-inlined function
-// for every projection phase (ptxas splits the register file between
-// several large callees of one kernel, which made each of them spill).
-__device__ __noinline__ void gemv_run(const GemvArgs &a, char *smem, float *red) {
-  if (a.w.quant == JAL_Q4_0) gemv_phase<JAL_Q4_0>(a, smem, red);
-  else gemv_phase<JAL_Q8_0>(a, smem, red);
-}
-
-struct Slice {
-  int h = 0, si = 0;
-  int64_t pos = 0, s0 = 0, s1 = 0;
-  int nt = 0;
-  bool active = false;
-};
-
-template <int TP>
-__device__ __forceinline__ Slice attn_slice(const MegaArgs &a) {
-  Slice s;
-  const int S = a.splits, c = blockIdx.x;
-  s.active = c < a.n_kv * S;
-  s.h = c / S;
-  s.si = c % S;
-  s.pos = *a.d_pos;
-  const int64_t seq = s.pos + 1;
-  const int64_t lo = (a.window > 0 && seq > a.window) ? seq - a.window : 0;
-  const int64_t per = (seq - lo + S - 1) / S;
-  s.s0 = lo + s.si * per;
-  s.s1 = s.s0 + per < seq ? s.s0 + per : seq;
-  const int64_t len = s.s1 > s.s0 ? s.s1 - s.s0 : 0;
-  s.nt = (int)((len + TP - 1) / TP);
-  return s;
-}
-
-// End of the Q/K/V phase: start the copies of this CTA's cache slice.
-template <int HD, bool F16>
-__device__ __forceinline__ void attn_issue(const MegaArgs &a, int layer, char *ring, uint64_t *bars) {
-  using Gm = AttnGeom<HD, F16, kMW>;
-  if (threadIdx.x != 0) return;
-  const Slice sl = attn_slice<Gm::TP>(a);
-  if (!sl.active) return;
-  fence_proxy_async();  // the projection phase's shared-memory reads precede the copies
-  for (int k = 0; k < sl.nt && k < kStages; k++) {
-    const int64_t t0 = sl.s0 + (int64_t)k * Gm::TP;
-    const int n = (int)(sl.s1 - t0 < Gm::TP ? sl.s1 - t0 : Gm::TP);
-    issue_tile<HD, F16>(a.kv, layer, ring + k * kStageBytes, &bars[k], t0, n, sl.h);
-  }
-}
-
-template <int HD, bool F16, int GP>
-__device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, int layer, char *ring,
-                                        uint64_t *bars, uint32_t *par_s) {
-  using Gm = AttnGeom<HD, F16, kMW>;
-  constexpr int TP = Gm::TP, LG = Gm::LG, PPS = Gm::PPS, DPL = Gm::DPL, TPW = Gm::TPW, VD = Gm::VD;
-  const Slice sl = attn_slice<TP>(a);
-  if (!sl.active) return;
-  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  const int G = (int)(a.n_heads_q / a.n_kv), h = sl.h, S = a.splits;
-  const int64_t Q = a.n_heads_q * HD, KVD = a.n_kv * HD, pos = sl.pos, seq = pos + 1;
-  // workspace after the ring
-  char *ws = ring + kStages * kStageBytes;
-  float(*q_s)[HD] = (float(*)[HD])ws;                   // [GP][HD]
-  float *kn_s = (float *)(ws + GP * HD * 4);            // [HD]
-  float *vn_s = kn_s + HD;                              // [HD]
-  float *cs_s = vn_s + HD;                              // [2][HD/2]
-  float *p_all = cs_s + HD;                             // [kMW][TPW * GP]
-  float *wm_s = p_all + kMW * TPW * GP;                 // [64][GP]: warp, then split merge weights
-  float *den = wm_s + 64 * GP;                          // [GP]
-  int *flag_s = (int *)(den + GP);
-  const bool rope = !L.skip_rope && pos > 0;
-  const int half = (int)(a.rotary_dim / 2);
-  if (rope) {
-    const bool use_long = a.long_threshold >= 0 && seq > a.long_threshold;
-    const float *ct = (use_long ? a.cos_long : a.cos_tab) + pos * half;
-    const float *st = (use_long ? a.sin_long : a.sin_tab) + pos * half;
-    for (int j = tid; j < half; j += kMT) {
-      cs_s[j] = ct[j];
-      cs_s[HD / 2 + j] = st[j];
-    }
-  }
-  __syncthreads();
-  const bool own_pos = pos >= sl.s0 && pos < sl.s1;
-  const int64_t app = own_pos ? kv_elem(a.kv, layer, h, pos) : 0;
-  for (int i = tid; i < (GP + 2) * HD; i += kMT) {
+#pragma unroll
+  for (int it = 0; it < NIT; it++) {
+    const int i = tid + it * kMT;
+    if (i >= (GP + 2) * HD) break;
     const int g = i / HD, d = i % HD;
-    if (g < GP && g >= G) {
-      q_s[g][d] = 0.0f;
-      continue;
-    }
-    const int64_t off = g < GP ? (int64_t)(h * G + g) * HD : (g == GP ? Q : Q + KVD) + (int64_t)h * HD;
-    const float *bias = g < GP ? L.bq : (g == GP ? L.bk : L.bv);
-    const int64_t boff = g < GP ? (int64_t)(h * G + g) * HD : (int64_t)h * HD;
-    float o = a.qkv[off + d];
-    if (bias) o = __fadd_rn(o, bias[boff + d]);
+    float o = xv[it];
     if (rope && g <= GP && d < 2 * half) {
       const bool first = a.neox ? d < half : (d & 1) == 0;
-      const int j = a.neox ? (first ? d : d - half) : d / 2;
-      const int partner = a.neox ? (first ? d + half : d - half) : (d ^ 1);
-      float other = a.qkv[off + partner];
-      if (bias) other = __fadd_rn(other, bias[boff + partner]);
-      const float c = cs_s[j], sn = cs_s[HD / 2 + j];
+      const float other = pv[it], c = cv[it], sn = sv[it];
       const float x0 = first ? o : other, x1 = first ? other : o;
       o = first ? __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn)) : __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
     }
     if (g < GP) {
-      q_s[g][d] = o;
+      q_s[g][d] = o;  // zero for g >= G
     } else {
       if (F16) o = __half2float(__float2half_rn(o));
       if (g == GP) kn_s[d] = o;
@@ -304,28 +538,24 @@ __device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, i
   for (int g = 0; g < GP; g++) {
     m_run[g] = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < VD; j++) acc[g][j] = 0.0f;
+    for (int jj = 0; jj < VD; jj++) acc[g][jj] = 0.0f;
   }
-  bool ok = true;
   float *pw = p_all + warp * TPW * GP;
-  const uint32_t par = *par_s;
-  for (int k = 0; k < sl.nt; k++) {
-    const int st = k % kStages;
-    const uint32_t parity = ((par >> st) & 1u) ^ (uint32_t)((k / kStages) & 1);
-    if (!mbar_wait_bounded(&bars[st], parity)) ok = false;
+  for (int k = 0; k < sl.nt; k++, j++) {
+    ring_wait(r, j, a.err);
     const int64_t t0 = sl.s0 + (int64_t)k * TP;
     const int n = (int)(sl.s1 - t0 < TP ? sl.s1 - t0 : TP);
-    char *Ks = ring + st * kStageBytes;
+    char *Ks = slot_ptr(r, j);
     char *Vs = Ks + TP * Gm::ROW;
-    if (own_pos && pos >= t0 && pos < t0 + n) {
-      const int j = (int)(pos - t0);
+    if (own_pos && pos >= t0 && pos < t0 + n) {  // the new k / v are not in the cache copy yet
+      const int jp = (int)(pos - t0);
       for (int d = tid; d < HD; d += kMT) {
         if (F16) {
-          ((__half *)(Ks + j * Gm::ROW))[d] = __float2half_rn(kn_s[d]);
-          ((__half *)(Vs + j * Gm::ROW))[d] = __float2half_rn(vn_s[d]);
+          ((__half *)(Ks + jp * Gm::ROW))[d] = __float2half_rn(kn_s[d]);
+          ((__half *)(Vs + jp * Gm::ROW))[d] = __float2half_rn(vn_s[d]);
         } else {
-          ((float *)(Ks + j * Gm::ROW))[d] = kn_s[d];
-          ((float *)(Vs + j * Gm::ROW))[d] = vn_s[d];
+          ((float *)(Ks + jp * Gm::ROW))[d] = kn_s[d];
+          ((float *)(Vs + jp * Gm::ROW))[d] = vn_s[d];
         }
       }
       __syncthreads();
@@ -336,13 +566,13 @@ __device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, i
 #pragma unroll
     for (int sp = 0; sp < TPW / PPS; sp++) {
       const int jl = sp * PPS + grp;
-      const int j = warp * TPW + jl;
+      const int jt = warp * TPW + jl;
       float d[GP];
 #pragma unroll
       for (int g = 0; g < GP; g++) d[g] = 0.0f;
-      if (j < n) {
+      if (jt < n) {
         float kv[DPL];
-        load_vals<F16, DPL>(Ks + j * Gm::ROW + c * 16, kv);
+        load_vals<F16, DPL>(Ks + jt * Gm::ROW + c * 16, kv);
 #pragma unroll
         for (int g = 0; g < GP; g++)
 #pragma unroll
@@ -355,7 +585,7 @@ __device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, i
       float mine = -INFINITY;
 #pragma unroll
       for (int g = 0; g < GP; g++) {
-        const float sc = j < n ? __fmul_rn(d[g], a.scale) : -INFINITY;
+        const float sc = jt < n ? __fmul_rn(d[g], a.scale) : -INFINITY;
         mt[g] = fmaxf(mt[g], sc);
         if (g == c) mine = sc;
       }
@@ -377,10 +607,10 @@ __device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, i
     float ls = 0.0f;
 #pragma unroll
     for (int e = lane; e < TPW * GP; e += 32) {
-      const float sv = pw[e];
-      const float p = sv == -INFINITY ? 0.0f : expf(sv - mg);
-      pw[e] = p;
-      ls += p;
+      const float s = pw[e];
+      const float pe = s == -INFINITY ? 0.0f : expf(s - mg);
+      pw[e] = pe;
+      ls += pe;
     }
 #pragma unroll
     for (int o = GP; o < 32; o <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
@@ -388,50 +618,30 @@ __device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, i
 #pragma unroll
     for (int g = 0; g < GP; g++)
 #pragma unroll
-      for (int j = 0; j < VD; j++) acc[g][j] *= alpha[g];
+      for (int jj = 0; jj < VD; jj++) acc[g][jj] *= alpha[g];
     __syncwarp();
 #pragma unroll 4
     for (int jl = 0; jl < TPW; jl++) {
-      const int j = warp * TPW + jl;
-      if (j >= n) break;
+      const int jt = warp * TPW + jl;
+      if (jt >= n) break;
       float v[VD];
-      load_vals<F16, VD>(Vs + j * Gm::ROW + lane * VD * Gm::ES, v);
-      float p[GP];
+      load_vals<F16, VD>(Vs + jt * Gm::ROW + lane * VD * Gm::ES, v);
+      float pg[GP];
 #pragma unroll
-      for (int g = 0; g < GP; g++) p[g] = pw[jl * GP + g];
+      for (int g = 0; g < GP; g++) pg[g] = pw[jl * GP + g];
 #pragma unroll
       for (int g = 0; g < GP; g++)
 #pragma unroll
-        for (int e = 0; e < VD; e++) acc[g][e] = fmaf(p[g], v[e], acc[g][e]);
+        for (int e = 0; e < VD; e++) acc[g][e] = fmaf(pg[g], v[e], acc[g][e]);
     }
     __syncthreads();
-    if (tid == 0 && k + kStages < sl.nt) {
-      fence_proxy_async();
-      const int64_t t1 = sl.s0 + (int64_t)(k + kStages) * TP;
-      const int n1 = (int)(sl.s1 - t1 < TP ? sl.s1 - t1 : TP);
-      issue_tile<HD, F16>(a.kv, layer, Ks, &bars[st], t1, n1, h);
-    }
+    ring_release<HD, F16>(p, r, j, own_pos);
   }
-  if (!ok) {
-    if (a.err) atomicOr(a.err, kErrAttnWait);
-    for (int k = sl.nt > kStages ? sl.nt - kStages : 0; k < sl.nt; k++)
-      mbar_wait_bounded(&bars[k % kStages], ((par >> (k % kStages)) & 1u) ^ (uint32_t)((k / kStages) & 1));
-  }
-  __syncthreads();
-  if (tid == 0) {  // parity of the next use of each stage
-    uint32_t np = par;
-    for (int st = 0; st < kStages; st++)
-      if (sl.nt > st && (((sl.nt - st + kStages - 1) / kStages) & 1)) np ^= 1u << st;
-    *par_s = np;
-  }
-  // Warp merge into this split's partial (in the idle ring), then to global.
-  float *acc_w = (float *)ring;             // [W][GP][HD]
-  float *m_w = acc_w + kMW * GP * HD;       // [W][GP]
-  float *l_w = m_w + kMW * GP;              // [W][GP]
+  // Warp merge of this CTA's split.
 #pragma unroll
   for (int g = 0; g < GP; g++)
 #pragma unroll
-    for (int j = 0; j < VD; j++) acc_w[(warp * GP + g) * HD + lane * VD + j] = acc[g][j];
+    for (int jj = 0; jj < VD; jj++) acc_w[(warp * GP + g) * HD + lane * VD + jj] = acc[g][jj];
   if (lane < GP) {
     float mm = -INFINITY;
 #pragma unroll
@@ -442,7 +652,7 @@ __device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, i
   }
   __syncthreads();
   constexpr int PSTR = GP * HD + 2 * GP;  // acc[GP][HD], m[GP], l[GP]
-  float *mine = a.attn_part + (size_t)(h * S + sl.si) * PSTR;
+  const int Se = sl.S;
   if (tid < GP) {
     float M = -INFINITY;
     for (int w = 0; w < kMW; w++) M = fmaxf(M, m_w[w * GP + tid]);
@@ -453,38 +663,66 @@ __device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, i
       wm_s[w * GP + tid] = wt;
       l = fmaf(wt, l_w[w * GP + tid], l);
     }
-    mine[GP * HD + tid] = M;
-    mine[GP * HD + GP + tid] = l;
+    den[tid] = l;
+    wm_s[64 * GP + tid] = M;
   }
   __syncthreads();
+  const int64_t ob = (int64_t)h * G * HD;  // first output element of this head group
+  if (Se == 1) {
+    // The only split of this head: normalise and write the output directly.
+    for (int bi = warp; bi < G * HD / 32; bi += kMW) {
+      const int e = bi * 32 + lane, g = e / HD;
+      float num = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kMW; w++) num = fmaf(wm_s[w * GP + g], acc_w[(w * GP) * HD + e], num);
+      float o = den[g] > 0.0f ? __fdiv_rn(num, den[g]) : 0.0f;
+      a.attn[ob + e] = o;
+      if (!isfinite(o)) o = 0.0f;
+      const float amax = warp_max(fabsf(o));
+      const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
+      a.attn_q[ob + e] = act_quant_one(o, inv);
+      if (lane == 0) a.attn_s[ob / 32 + bi] = scale;
+    }
+    __syncthreads();
+    return j;
+  }
+  float *mine = a.attn_part + (size_t)(h * S + sl.si) * PSTR;
+  if (tid < GP) {
+    mine[GP * HD + tid] = wm_s[64 * GP + tid];
+    mine[GP * HD + GP + tid] = den[tid];
+  }
   for (int i = tid; i < GP * HD; i += kMT) {
     const int g = i / HD;
-    float s = 0.0f;
+    float v = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kMW; w++) s = fmaf(wm_s[w * GP + g], acc_w[(w * GP) * HD + i], s);
-    mine[i] = s;
+    for (int w = 0; w < kMW; w++) v = fmaf(wm_s[w * GP + g], acc_w[(w * GP) * HD + i], v);
+    mine[i] = v;
   }
   // The last split of this head to finish merges all splits in split order.
   __threadfence();
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    *flag_s = atomicAdd(&a.head_cnt[h], 1u) == (unsigned)(S - 1);
-  }
+  if (tid == 0) *flag_s = atomicAdd(&a.head_cnt[h], 1u) == (unsigned)(Se - 1);
   __syncthreads();
-  if (!*flag_s) return;
+  if (!*flag_s) return j;
   __threadfence();
   const float *allp = a.attn_part + (size_t)h * S * PSTR;
-  float *mw = wm_s;  // [S][GP] merge weights (S <= 64)
+  float *ms_s = acc_w;             // [Se][GP] split maxima, then merge weights
+  float *ls_s = acc_w + 64 * GP;   // [Se][GP] split denominators
+  for (int i = tid; i < Se * GP; i += kMT) {
+    const int sp = i / GP, g = i % GP;
+    ms_s[i] = __ldcg(allp + (size_t)sp * PSTR + GP * HD + g);
+    ls_s[i] = __ldcg(allp + (size_t)sp * PSTR + GP * HD + GP + g);
+  }
+  __syncthreads();
   if (tid < GP) {
     float M = -INFINITY;
-    for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(allp + (size_t)s * PSTR + GP * HD + tid));
+    for (int sp = 0; sp < Se; sp++) M = fmaxf(M, ms_s[sp * GP + tid]);
     float dsum = 0.0f;
-    for (int s = 0; s < S; s++) {
-      const float ms = __ldcg(allp + (size_t)s * PSTR + GP * HD + tid);
-      const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
-      mw[s * GP + tid] = w;
-      dsum = fmaf(w, __ldcg(allp + (size_t)s * PSTR + GP * HD + GP + tid), dsum);
+    for (int sp = 0; sp < Se; sp++) {
+      const float m = ms_s[sp * GP + tid];
+      const float w = m == -INFINITY ? 0.0f : expf(m - M);
+      ms_s[sp * GP + tid] = w;
+      dsum = fmaf(w, ls_s[sp * GP + tid], dsum);
     }
     den[tid] = dsum;
   }
@@ -494,17 +732,31 @@ __device__ __noinline__ void attn_phase(const MegaArgs &a, const MegaLayer &L, i
   for (int bi = warp; bi < G * HD / 32; bi += kMW) {
     const int e = bi * 32 + lane, g = e / HD;
     float num = 0.0f;
-    for (int s = 0; s < S; s++) num = fmaf(mw[s * GP + g], __ldcg(allp + (size_t)s * PSTR + e), num);
+#pragma unroll 4
+    for (int sp = 0; sp < Se; sp++) num = fmaf(ms_s[sp * GP + g], __ldcg(allp + (size_t)sp * PSTR + e), num);
     float o = den[g] > 0.0f ? __fdiv_rn(num, den[g]) : 0.0f;
-    a.attn[(int64_t)h * G * HD + e] = o;
+    a.attn[ob + e] = o;
     if (!isfinite(o)) o = 0.0f;
     const float amax = warp_max(fabsf(o));
     const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
-    const int64_t gb = ((int64_t)h * G * HD) / 32 + bi;
-    a.attn_q[gb * 32 + lane] = act_quant_one(o, inv);
-    if (lane == 0) a.attn_s[gb] = scale;
+    a.attn_q[ob + e] = act_quant_one(o, inv);
+    if (lane == 0) a.attn_s[ob / 32 + bi] = scale;
   }
   if (tid == 0) a.head_cnt[h] = 0u;
+  __syncthreads();
+  return j;
+}
+
+// ---- embedding and argmax ------------------------------------------------------
+__device__ __noinline__ void ph_embed(const MegaArgs &a) {
+  const int64_t H = a.H;
+  const uint32_t tok = *a.d_token;
+  const int64_t per = (H + gridDim.x - 1) / gridDim.x, e0 = blockIdx.x * per;
+  const int64_t e1 = e0 + per < H ? e0 + per : H;
+  const bool bad = tok >= (uint32_t)a.emb_rows;
+  if (bad && blockIdx.x == 0 && threadIdx.x == 0 && a.err) atomicOr(a.err, 1);
+  for (int64_t i = e0 + threadIdx.x; i < e1; i += kMT)
+    a.hidden[i] = bad ? 0.0f : embed_value(a.emb, a.emb_quant, H, tok, i);
 }
 
 __device__ __forceinline__ bool am_better(float v, int i, float bv, int bi) {
@@ -558,169 +810,154 @@ __device__ __noinline__ void argmax_phase(const MegaArgs &a, float *red) {
   if (a.d_hist) a.d_hist[*a.d_pos + 1] = tok;
   *a.d_pos += 1;
   *a.am_cnt = 0u;
+  *a.bar = 0u;  // every CTA is past its last barrier wait
 }
 
-// ---- phases.  Each is a separate function that reads its arguments from
-// the MegaArgs block in global memory, so that the kernel's own loop keeps
-// almost nothing live across the calls (a call preserves the caller's live
-// registers, which otherwise costs spills in every phase).
-
-__device__ __noinline__ void ph_embed(const MegaArgs &a) {
-  const int64_t H = a.H;
-  const uint32_t tok = *a.d_token;
-  const int64_t per = (H + gridDim.x - 1) / gridDim.x, e0 = blockIdx.x * per;
-  const int64_t e1 = e0 + per < H ? e0 + per : H;
-  const bool bad = tok >= (uint32_t)a.emb_rows;
-  if (bad && blockIdx.x == 0 && threadIdx.x == 0 && a.err) atomicOr(a.err, 1);
-  for (int64_t i = e0 + threadIdx.x; i < e1; i += kMT)
-    a.hidden[i] = bad ? 0.0f : embed_value(a.emb, a.emb_quant, H, tok, i);
-  const int64_t HD = a.kv.head_dim;
-  prefetch_rows(a.layers[0].qkv, (a.n_heads_q + 2 * a.n_kv) * HD, 1, 0);
-}
-
-// Q/K/V projection (RMSNorm prologue); then this CTA's first KV tile copies
-// and the L2 prefetch of its O-projection rows.
-template <int HD, bool F16>
-__device__ __noinline__ void ph_qkv(const MegaArgs &a, int l, char *smem, float *red, uint64_t *bars) {
-  const MegaLayer &L = a.layers[l];
-  const int64_t QKV = (a.n_heads_q + 2 * a.n_kv) * HD;
+// ---- phases: build the projection's arguments and run it from the ring ------
+template <int HD, bool F16, int QW>
+__device__ __noinline__ unsigned ph_proj(const MegaArgs &a, const Plan &p, const Ring &r, int kind, int l, unsigned j,
+                                         char *work, float *red) {
   GemvArgs g;
-  g.w = L.qkv; g.rows = QKV; g.m = 1; g.in_mode = GEMV_IN_NORM;
-  g.x = a.hidden; g.x_stride = a.H; g.norm_w = L.attn_norm; g.eps = a.eps;
-  g.out_mode = GEMV_OUT_STORE; g.y = a.qkv; g.y_stride = QKV;
-  gemv_run(g, smem, red);
-  attn_issue<HD, F16>(a, l, smem, bars);
-  prefetch_rows(L.wo, a.H, 1, 0);
+  g.m = 1;
+  const Rows *rs;
+  if (kind == 4) {  // LM head (final RMSNorm prologue)
+    g.w = a.lm_head; g.rows = a.V; g.in_mode = GEMV_IN_NORM;
+    g.x = a.hidden; g.x_stride = a.H; g.norm_w = a.out_norm; g.eps = a.eps;
+    g.out_mode = GEMV_OUT_STORE; g.y = a.logits; g.y_stride = a.V;
+    rs = &p.head;
+  } else {
+    const MegaLayer &L = a.layers[l];
+    if (kind == 0) {  // Q/K/V (RMSNorm prologue)
+      const int64_t QKV = (a.n_heads_q + 2 * a.n_kv) * HD;
+      g.w = L.qkv; g.rows = QKV; g.in_mode = GEMV_IN_NORM;
+      g.x = a.hidden; g.x_stride = a.H; g.norm_w = L.attn_norm; g.eps = a.eps;
+      g.out_mode = GEMV_OUT_STORE; g.y = a.qkv; g.y_stride = QKV;
+      rs = &p.q;
+    } else if (kind == 1) {  // O + residual (+ bias)
+      g.w = L.wo; g.rows = a.H; g.in_mode = GEMV_IN_Q8;
+      g.xq = a.attn_q; g.xs = a.attn_s; g.xq_stride = a.n_heads_q * HD;
+      g.out_mode = GEMV_OUT_ADD; g.y = a.hidden; g.y_stride = a.H; g.bias = L.bo;
+      rs = &p.o;
+    } else if (kind == 2) {  // gate/up + SwiGLU (RMSNorm prologue), also quantized
+      g.w = L.gateup; g.rows = a.F; g.in_mode = GEMV_IN_NORM;
+      g.x = a.hidden; g.x_stride = a.H; g.norm_w = L.ffn_norm; g.eps = a.eps;
+      g.out_mode = GEMV_OUT_SWIGLU; g.y = a.ffn; g.y_stride = a.F; g.up_offset = a.F;
+      g.yq = a.ffn_q; g.ys = a.ffn_s; g.ycnt = a.ffn_cnt;
+      rs = &p.gu;
+    } else {  // down + residual (input quantized by the gate/up phase)
+      g.w = L.wdown; g.rows = a.H; g.in_mode = GEMV_IN_Q8;
+      g.xq = a.ffn_q; g.xs = a.ffn_s; g.xq_stride = a.F;
+      g.out_mode = GEMV_OUT_ADD; g.y = a.hidden; g.y_stride = a.H;
+      rs = &p.dn;
+    }
+  }
+  return gemv_stream<QW, HD, F16>(a, p, r, g, *rs, j, work, red);
 }
 
-template <int HD, bool F16, int GP>
-__device__ __noinline__ void ph_attn(const MegaArgs &a, int l, char *smem, uint64_t *bars, uint32_t *par_s) {
-  const MegaLayer &L = a.layers[l];
-  attn_phase<HD, F16, GP>(a, L, l, smem, bars, par_s);
-  prefetch_rows(L.gateup, a.F, 2, a.F);
-}
-
-// O projection + residual (+ bias).
-__device__ __noinline__ void ph_o(const MegaArgs &a, int l, char *smem, float *red) {
-  const MegaLayer &L = a.layers[l];
-  const int64_t Q = a.n_heads_q * a.kv.head_dim;
-  GemvArgs g;
-  g.w = L.wo; g.rows = a.H; g.m = 1; g.in_mode = GEMV_IN_Q8;
-  g.xq = a.attn_q; g.xs = a.attn_s; g.xq_stride = Q;
-  g.out_mode = GEMV_OUT_ADD; g.y = a.hidden; g.y_stride = a.H; g.bias = L.bo;
-  gemv_run(g, smem, red);
-  prefetch_rows(L.wdown, a.H, 1, 0);
-}
-
-// gate/up projection + SwiGLU (RMSNorm prologue).
-__device__ __noinline__ void ph_gateup(const MegaArgs &a, int l, char *smem, float *red) {
-  const MegaLayer &L = a.layers[l];
-  GemvArgs g;
-  g.w = L.gateup; g.rows = a.F; g.m = 1; g.in_mode = GEMV_IN_NORM;
-  g.x = a.hidden; g.x_stride = a.H; g.norm_w = L.ffn_norm; g.eps = a.eps;
-  g.out_mode = GEMV_OUT_SWIGLU; g.y = a.ffn; g.y_stride = a.F; g.up_offset = a.F;
-  gemv_run(g, smem, red);
-  if (l + 1 < a.n_layers) prefetch_rows(a.layers[l + 1].qkv, (a.n_heads_q + 2 * a.n_kv) * a.kv.head_dim, 1, 0);
-  else prefetch_rows(a.lm_head, a.V, 1, 0);
-}
-
-// down projection + residual.
-__device__ __noinline__ void ph_down(const MegaArgs &a, int l, char *smem, float *red) {
-  const MegaLayer &L = a.layers[l];
-  GemvArgs g;
-  g.w = L.wdown; g.rows = a.H; g.m = 1; g.in_mode = GEMV_IN_F32;
-  g.x = a.ffn; g.x_stride = a.F;
-  g.out_mode = GEMV_OUT_ADD; g.y = a.hidden; g.y_stride = a.H;
-  gemv_run(g, smem, red);
-  if (l + 1 < a.n_layers) prefetch_rows(a.layers[l + 1].wo, a.H, 1, 0);
-}
-
-// LM head (final RMSNorm prologue).
-__device__ __noinline__ void ph_head(const MegaArgs &a, char *smem, float *red) {
-  GemvArgs g;
-  g.w = a.lm_head; g.rows = a.V; g.m = 1; g.in_mode = GEMV_IN_NORM;
-  g.x = a.hidden; g.x_stride = a.H; g.norm_w = a.out_norm; g.eps = a.eps;
-  g.out_mode = GEMV_OUT_STORE; g.y = a.logits; g.y_stride = a.V;
-  gemv_run(g, smem, red);
-}
-
-template <int HD, bool F16, int GP>
+template <int HD, bool F16, int GP, int QW>
 __global__ void __launch_bounds__(kMT, 1) k_decode_mega(const MegaArgs *__restrict__ ap) {
   extern __shared__ __align__(128) char smem[];
   __shared__ float red[33];
-  __shared__ __align__(8) uint64_t bars[kStages];
-  __shared__ uint32_t par_s;
+  __shared__ __align__(8) uint64_t full[kSlots];
   __shared__ int broken;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; s++) mbar_init(&bars[s], 1);
-    fence_barrier_init();
-    fence_proxy_async();
-    par_s = 0;
-    broken = 0;
-  }
-  __syncthreads();
+  __shared__ unsigned seq;
+  __shared__ Plan plan;
   const MegaArgs &a = *ap;
+  const Ring ring{smem, full};
+  char *work = smem + kRingBytes;
+  if (threadIdx.x == 0) {
+    broken = 0;
+    seq = 0;
+    for (int s = 0; s < kSlots; s++) mbar_init(&full[s], 1);
+    fence_barrier_init();
+  }
+  make_plan(a, *a.d_pos, AttnGeom<HD, F16, 1>::TP, plan);
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int s = 0; s < kSlots; s++) ring_issue<HD, F16>(plan, ring, (unsigned)s);
+  const GridBar gb{a.bar, a.err, &broken, &seq};
   ph_embed(a);
-  grid_sync(a.bar, a.err, &broken);
+  grid_sync(gb);
+  unsigned j = 0;  // stream index of the next chunk (the same in every thread)
   const int n_layers = a.n_layers;
   for (int l = 0; l < n_layers; l++) {
-    ph_qkv<HD, F16>(a, l, smem, red, bars);
-    grid_sync(a.bar, a.err, &broken);
-    ph_attn<HD, F16, GP>(a, l, smem, bars, &par_s);
-    grid_sync(a.bar, a.err, &broken);
-    ph_o(a, l, smem, red);
-    grid_sync(a.bar, a.err, &broken);
-    ph_gateup(a, l, smem, red);
-    grid_sync(a.bar, a.err, &broken);
-    ph_down(a, l, smem, red);
-    grid_sync(a.bar, a.err, &broken);
+    j = ph_proj<HD, F16, QW>(a, plan, ring, 0, l, j, work, red);
+    grid_sync(gb);
+    j = attn_stream<HD, F16, GP>(a, plan, ring, l, j, work);
+    grid_sync(gb);
+    j = ph_proj<HD, F16, QW>(a, plan, ring, 1, l, j, work, red);
+    grid_sync(gb);
+    j = ph_proj<HD, F16, QW>(a, plan, ring, 2, l, j, work, red);
+    grid_sync(gb);
+    j = ph_proj<HD, F16, QW>(a, plan, ring, 3, l, j, work, red);
+    grid_sync(gb);
   }
-  ph_head(a, smem, red);
+  j = ph_proj<HD, F16, QW>(a, plan, ring, 4, 0, j, work, red);
   argmax_phase(a, red);
+  // Every issued chunk was waited for; after a wait that gave up, wait again
+  // (bounded) so that no copy is still landing when the CTA exits.
+  if (threadIdx.x == 0)
+    for (int k = plan.total > kSlots ? plan.total - kSlots : 0; k < plan.total; k++)
+      mbar_wait_bounded(&full[k % kSlots], ((unsigned)k / kSlots) & 1u);
 }
 
-template <int HD, bool F16, int GP>
+template <int HD, bool F16, int GP, int QW>
 const void *mega_fn() {
-  return (const void *)k_decode_mega<HD, F16, GP>;
+  return (const void *)k_decode_mega<HD, F16, GP, QW>;
 }
 
-const void *pick_mega(int hd, int f16, int G) {
-  const int gp = G <= 4 ? 4 : 0;
-  if (hd == 128 && f16 && gp == 4) return mega_fn<128, true, 4>();
-  if (hd == 128 && !f16 && gp == 4) return mega_fn<128, false, 4>();
-  if (hd == 64 && f16 && gp == 4) return mega_fn<64, true, 4>();
-  if (hd == 64 && !f16 && gp == 4) return mega_fn<64, false, 4>();
+// One weight type for every projection (Q/K/V, O, gate/up, down, LM head).
+int mega_quant(const MegaArgs &a) {
+  const int q = a.lm_head.quant;
+  if (q != JAL_Q4_0 && q != JAL_Q8_0) return -1;
+  return q;
+}
+
+const void *pick_mega(int hd, int f16, int G, int qw) {
+  if (G > 4) return nullptr;
+#define JAL_PICK(HDV, F, QV) \
+  if (hd == HDV && (f16 != 0) == F && qw == QV) return mega_fn<HDV, F, 4, QV>();
+  JAL_PICK(128, true, JAL_Q4_0) JAL_PICK(128, false, JAL_Q4_0) JAL_PICK(64, true, JAL_Q4_0) JAL_PICK(64, false, JAL_Q4_0)
+  JAL_PICK(128, true, JAL_Q8_0) JAL_PICK(128, false, JAL_Q8_0) JAL_PICK(64, true, JAL_Q8_0) JAL_PICK(64, false, JAL_Q8_0)
+#undef JAL_PICK
   return nullptr;
 }
 
-// Shared memory of one projection phase: activation region, plus the
-// per-segment partials when the input spans several segments.
-size_t proj_smem(int in_mode, int64_t cols, int64_t rows, int grid) {
+// Work area of one projection phase: activation region plus the
+// per-segment partials of one chunk's rows.
+size_t proj_work(int in_mode, int64_t cols, int64_t qs_stride) {
   const int nb = (int)(cols / 32), nseg = seg_count(cols);
-  return w4_smem(in_mode, nb, nseg, (rows + grid - 1) / grid);
+  int64_t rpc = kSlotBytes / qs_stride;
+  if (rpc < 1) rpc = 1;
+  return w4_act_region(in_mode, nb, nseg) + (size_t)rpc * nseg * 4;
 }
 
-size_t mega_smem(const MegaArgs &a, int grid) {
-  const int64_t Q = a.n_heads_q * a.kv.head_dim, KV = a.n_kv * a.kv.head_dim;
-  size_t m = (size_t)kStages * kStageBytes + kAttnWs;
-  const size_t p[5] = {proj_smem(GEMV_IN_NORM, a.H, Q + 2 * KV, grid), proj_smem(GEMV_IN_Q8, Q, a.H, grid),
-                       proj_smem(GEMV_IN_NORM, a.H, a.F, grid), proj_smem(GEMV_IN_F32, a.F, a.H, grid),
-                       proj_smem(GEMV_IN_NORM, a.H, a.V, grid)};
-  for (size_t v : p)
-    if (v > m) m = v;
-  return m;
-}
+constexpr size_t mega_smem() { return kRingBytes + kWorkBytes; }
 
 }  // namespace
 
 int mega_check(const MegaArgs &a, int grid) {
   if (grid < 1 || a.n_kv < 1 || a.n_heads_q % a.n_kv) return 0;
-  if (!pick_mega((int)a.kv.head_dim, a.kv.f16, (int)(a.n_heads_q / a.n_kv))) return 0;
+  const int qw = mega_quant(a);
+  const int64_t HD = a.kv.head_dim, Q = a.n_heads_q * HD;
+  if (!pick_mega((int)HD, a.kv.f16, (int)(a.n_heads_q / a.n_kv), qw)) return 0;
   // SwiGLU pairs need the whole gate/up row in one segment; other inputs
-  // may span up to 16 segments (one warp each).
+  // may span up to one segment per warp.
   if (seg_count(a.H) != 1) return 0;
+  if (seg_count(Q) > kMW || seg_count(a.F) > kMW) return 0;
   if (a.splits < 1 || a.splits > 64 || a.n_kv * a.splits > grid) return 0;
-  return mega_smem(a, grid) <= (size_t)kGemvMaxSmem ? 1 : 0;
+  // Whole rows per ring slot, and the work area of every phase.
+  const int64_t row_q = (int64_t)(qw == JAL_Q4_0 ? 18 : 34);  // bytes per 32 weights
+  const int64_t strides[3] = {a.H / 32 * row_q, Q / 32 * row_q, a.F / 32 * row_q};
+  for (int64_t s : strides)
+    if (s + 256 > kSlotBytes) return 0;
+  const size_t resid = (size_t)(a.H / grid + 1) * 4;  // staged residual rows (O and down)
+  if (a.n_layers > kMaxLayers) return 0;
+  if (proj_work(GEMV_IN_Q8, a.F, a.F / 32 * row_q + 256) + resid > kWorkBytes) return 0;
+  if (proj_work(GEMV_IN_Q8, Q, Q / 32 * row_q + 256) + resid > kWorkBytes) return 0;
+  if (proj_work(GEMV_IN_NORM, a.H, a.H / 32 * row_q) > kWorkBytes) return 0;
+  if (8192 + (size_t)(kMW + 1) * 4 * HD * 4 > kWorkBytes) return 0;  // attention workspace
+  return 1;
 }
 
 size_t mega_part_bytes(const MegaArgs &a) {
@@ -729,10 +966,9 @@ size_t mega_part_bytes(const MegaArgs &a) {
 }
 
 int launch_decode_mega(const MegaArgs &a, const MegaArgs *dev_args, int grid, cudaStream_t s) {
-  const void *fn = pick_mega((int)a.kv.head_dim, a.kv.f16, (int)(a.n_heads_q / a.n_kv));
-  if (!fn) return 0;
   if (!mega_check(a, grid)) return 0;
-  const size_t smem = mega_smem(a, grid);
+  const void *fn = pick_mega((int)a.kv.head_dim, a.kv.f16, (int)(a.n_heads_q / a.n_kv), mega_quant(a));
+  const size_t smem = mega_smem();
   cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);

@@ -51,6 +51,9 @@ struct GemvArgs {
   int64_t y_stride = 0;
   const float *bias = nullptr;  // per output row (OUT_STORE / OUT_ADD)
   int64_t up_offset = 0;        // SWIGLU: physical row offset of the up half
+  int8_t *yq = nullptr;         // SWIGLU (persistent step): y also as QuantizedActQ8,
+  float *ys = nullptr;          //   each 32-block quantized by the CTA that completes it
+  unsigned *ycnt = nullptr;     //   per-block row counters (zero between uses)
   int grid = 0;                 // CTAs (0 = auto)
   int pdl = 0;                  // launch with programmatic dependent launch
   int64_t pf_bytes = -1;        // L2 prefetch budget per CTA (-1 = default)
@@ -198,16 +201,18 @@ struct MegaArgs {
   int64_t *d_pos = nullptr;
   uint32_t *d_token = nullptr, *d_hist = nullptr;
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *ffn = nullptr, *logits = nullptr;
-  int8_t *attn_q = nullptr;
-  float *attn_s = nullptr;
+  int8_t *attn_q = nullptr, *ffn_q = nullptr;
+  float *attn_s = nullptr, *ffn_s = nullptr;
+  unsigned *ffn_cnt = nullptr;  // [F / 32] block counters of the SwiGLU output (zero between steps)
   float *attn_part = nullptr;   // [n_kv][splits][4 * hd + 8] attention split partials
   unsigned *head_cnt = nullptr; // [n_kv] split arrival counters (zero between steps)
   unsigned *bar = nullptr;      // grid barrier: count, generation
   float *am_val = nullptr;
   int *am_idx = nullptr;
   unsigned *am_cnt = nullptr;
-  int *err = nullptr;           // error word (bit 1 token, 2 KV wait, 8 grid wait)
+  int *err = nullptr;           // error word (bit 1 token, 2 copy wait, 8 grid wait)
   int splits = 1;               // attention CTAs per KV head (<= 64)
+  int attn_split_tokens = 128;  // attended positions per attention split (fewer splits for short spans)
 };
 // Whether the persistent decode step supports this model shape at `grid`
 // CTAs (head_dim, KV type, query heads per KV head, segment counts, shared

@@ -280,15 +280,14 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvAr
     for (int j = 0; j < DEPTH; j++)
       if (j < total) w4_load<QUANT>(a.w, unit_row(j), seg, nb, lane, buf[j]);
   }
-  gemv_prologue_pre<1, WARPS>(a, smem, nb, nbp);
   pdl_wait();
   pdl_trigger();
-  gemv_prologue<1, WARPS>(a, smem, nb, nbp, red);
-  if (l2_first) {
+  if (l2_first) {  // weight loads first: they overlap the prologue's round trip
 #pragma unroll
     for (int j = 0; j < DEPTH; j++)
       if (j < total) w4_load<QUANT>(a.w, unit_row(j), seg, nb, lane, buf[j]);
   }
+  gemv_prologue_m1<WARPS>(a, smem, nb, nbp, red);
   W4Act x;
 #pragma unroll
   for (int v = 0; v < 4; v++) {

@@ -203,6 +203,108 @@ __device__ void gemv_prologue_pre(const GemvArgs &a, char *smem, int nb, int nbp
   for (int i = threadIdx.x; i < K / 4; i += WARPS * 32) ((float4 *)normw)[i] = ((const float4 *)a.norm_w)[i];
 }
 
+// M = 1 prologue for f32 / RMSNorm inputs with every global load issued
+// before any use: each thread reads its JMAX jobs of 8 consecutive elements
+// (and their norm weights) into registers at once, so the prologue costs one
+// memory round trip plus the norm reduction.  Same quantization as
+// gemv_prologue; padding blocks [nb, nbp) are zeroed.
+template <int WARPS, int JMAX, bool NORM>
+__device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, int nb, int nbp, float *red) {
+  constexpr int T = WARPS * 32;
+  const int tid = threadIdx.x, jobs = nb * 4;
+  for (int b = nb + tid; b < nbp; b += T) {
+    ((uint4 *)smem)[b] = make_uint4(0, 0, 0, 0);
+    ((uint4 *)(smem + nbp * 16))[b] = make_uint4(0, 0, 0, 0);
+    put_scale_sum(smem, nbp, b, 0.0f, 0);
+  }
+  float v[JMAX][8], w[NORM ? JMAX : 1][8];
+#pragma unroll
+  for (int j = 0; j < JMAX; j++) {
+    const int i = tid + j * T;
+    if (i < jobs) {
+      const float4 *xp = (const float4 *)(a.x + i * 8);
+      const float4 x0 = xp[0], x1 = xp[1];
+      v[j][0] = x0.x; v[j][1] = x0.y; v[j][2] = x0.z; v[j][3] = x0.w;
+      v[j][4] = x1.x; v[j][5] = x1.y; v[j][6] = x1.z; v[j][7] = x1.w;
+      if (NORM) {
+        const float4 *wp = (const float4 *)(a.norm_w + i * 8);
+        const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+        w[NORM ? j : 0][0] = w0.x; w[NORM ? j : 0][1] = w0.y; w[NORM ? j : 0][2] = w0.z; w[NORM ? j : 0][3] = w0.w;
+        w[NORM ? j : 0][4] = w1.x; w[NORM ? j : 0][5] = w1.y; w[NORM ? j : 0][6] = w1.z; w[NORM ? j : 0][7] = w1.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[j][e] = 0.0f;
+    }
+  }
+  float invn = 1.0f;
+  if (NORM) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < JMAX; j++)
+#pragma unroll
+      for (int e = 0; e < 8; e++) ss = fmaf(v[j][e], v[j][e], ss);
+    const float tot = block_reduce_sum<WARPS>(ss, red);
+    invn = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)(nb * 32)), a.eps)));
+  }
+  const int jobs_r = (jobs + 31) & ~31;  // whole warps take part in the shuffles
+#pragma unroll
+  for (int j = 0; j < JMAX; j++) {
+    const int i = tid + j * T;
+    if (j * T >= jobs_r) break;
+    if (i >= jobs_r) continue;
+    const bool valid = i < jobs;
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      float t = v[j][e];
+      if (NORM && valid) t = __fmul_rn(__fmul_rn(t, invn), w[NORM ? j : 0][e]);
+      x[e] = isfinite(t) ? t : 0.0f;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(x[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
+    int q[8], s = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      q[e] = act_quant_one(x[e], inv);
+      s += q[e];
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (valid) {
+      const int b = i >> 2, sub = i & 3;
+      const uint32_t p0 = (uint32_t)(q[0] & 0xff) | ((uint32_t)(q[1] & 0xff) << 8) | ((uint32_t)(q[2] & 0xff) << 16) |
+                          ((uint32_t)(q[3] & 0xff) << 24);
+      const uint32_t p1 = (uint32_t)(q[4] & 0xff) | ((uint32_t)(q[5] & 0xff) << 8) | ((uint32_t)(q[6] & 0xff) << 16) |
+                          ((uint32_t)(q[7] & 0xff) << 24);
+      char *half = sub < 2 ? smem + b * 16 : smem + nbp * 16 + b * 16;
+      *(uint2 *)(half + (sub & 1) * 8) = make_uint2(p0, p1);
+      if (sub == 0) put_scale_sum(smem, nbp, b, scale, s);
+    }
+  }
+  __syncthreads();
+}
+
+// M = 1 prologue: the one-round-trip form when the row fits (RMSNorm rows up
+// to 8192 elements, f32 rows up to 16384), else gemv_prologue.  Q8 inputs
+// are already one round trip in gemv_prologue.
+template <int WARPS>
+__device__ __forceinline__ void gemv_prologue_m1(const GemvArgs &a, char *smem, int nb, int nbp, float *red) {
+  constexpr int T = WARPS * 32, JN = 1024 / T, JF = 2048 / T;
+  if (a.in_mode == GEMV_IN_NORM && nb * 4 <= JN * T) {
+    prologue_m1_impl<WARPS, JN, true>(a, smem, nb, nbp, red);
+  } else if (a.in_mode == GEMV_IN_F32 && nb * 4 <= JF * T) {
+    prologue_m1_impl<WARPS, JF, false>(a, smem, nb, nbp, red);
+  } else {
+    gemv_prologue_pre<1, WARPS>(a, smem, nb, nbp);
+    gemv_prologue<1, WARPS>(a, smem, nb, nbp, red);
+  }
+}
+
 __device__ __forceinline__ float swiglu_one(float g, float u) {
   // swiglu_compat (recipe.rs:3037-3047)
   float sig = g <= -20.0f ? 0.0f : (g >= 20.0f ? 1.0f : __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));

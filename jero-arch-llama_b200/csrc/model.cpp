@@ -787,6 +787,9 @@ static void setup_mega(Context &ctx, int sms) {
     m.bq = L.bq; m.bk = L.bk; m.bv = L.bv; m.bo = L.bo;
     m.skip_rope = ctx.recipe.should_skip_rope(l) ? 1 : 0;
     if (!w4_matrix_ok(m.qkv) || !w4_matrix_ok(m.wo) || !w4_matrix_ok(m.gateup) || !w4_matrix_ok(m.wdown)) return;
+    // one weight type for every projection (the kernel is instantiated per type)
+    const int q = c.lm_head.dm.quant;
+    if (m.qkv.quant != q || m.wo.quant != q || m.gateup.quant != q || m.wdown.quant != q) return;
   }
   if (!w4_matrix_ok(c.lm_head.dm)) return;
   MegaArgs &a = ctx.margs;
@@ -807,9 +810,11 @@ static void setup_mega(Context &ctx, int sms) {
   a.d_pos = ctx.d_pos; a.d_token = ctx.d_token; a.d_hist = ctx.d_hist;
   a.hidden = ctx.hidden; a.qkv = ctx.qkv; a.attn = ctx.attn; a.ffn = ctx.ffn; a.logits = ctx.logits;
   a.attn_q = ctx.attn_q; a.attn_s = ctx.attn_s;
+  a.ffn_q = ctx.ffn_q; a.ffn_s = ctx.ffn_s; a.ffn_cnt = ctx.ffn_cnt;
   a.am_val = ctx.am_val; a.am_idx = ctx.am_idx; a.am_cnt = ctx.am_cnt;
   a.err = ctx.d_err;
   a.splits = std::max(1, std::min(64, sms / (int)g.n_heads_kv));
+  if (const char *v = getenv("JAL_MEGA_SPLIT_TOKENS")) a.attn_split_tokens = std::max(1, atoi(v));
   if (!mega_check(a, sms)) return;
   const size_t part = mega_part_bytes(a);
   auto lb = alloc(layers.size() * sizeof(MegaLayer) + 256 + part + 256 + g.n_heads_kv * 4 + 256 + 64 + 256 +

@@ -217,17 +217,19 @@ def test_fail_closed_errors_keep_position(jal, oracle, torch_cuda):
             ctx.prefill_step(prompt_of(1, n=21), 0)
 
 
-@pytest.mark.parametrize("kv_name", ["KV_F32", "KV_F16"])
-def test_persistent_decode_kernel_matches_oracle(jal, oracle, torch_cuda, monkeypatch, kv_name):
+@pytest.mark.parametrize("kv_name,quant_name", [("KV_F32", "Q4_0"), ("KV_F16", "Q4_0"), ("KV_F16", "Q8_0")])
+def test_persistent_decode_kernel_matches_oracle(jal, oracle, torch_cuda, monkeypatch, kv_name, quant_name):
     """JAL_DECODE=mega: one cooperative launch per token (decode_mega.cu).
 
     Same fast-numerics bars as the graph path (teacher-forced against the
     oracle), plus self-consistency of the on-device greedy loop: the argmax
     phase picks the host argmax of the same kernel's logits at every step.
     FFN 1536 keeps every projection on the segmented path (blocks per row a
-    multiple of 4).
+    multiple of 4); the LM head has the layers' weight type (the kernel is
+    instantiated per weight type).
     """
-    spec = jal.SynthSpec(ffn_dim=1536)
+    q = getattr(jal, quant_name)
+    spec = jal.SynthSpec(ffn_dim=1536, weight_quant=q, head_quant=q)
     kv = getattr(jal, kv_name)
     buf = jal.synth_gguf(spec, 909)
     _, tensors = gguf_py.parse(buf)
@@ -241,7 +243,7 @@ def test_persistent_decode_kernel_matches_oracle(jal, oracle, torch_cuda, monkey
     prompt = prompt_of(21)
     worst, agree = run_fast(om, ctx, prompt, 48, 256)
     assert ctx.launches_per_step() == 1
-    print(f"persistent decode {kv_name} worst |dlogit| = {worst:.3e}, top-1 agreement {agree:.2f}")
+    print(f"persistent decode {kv_name} {quant_name} worst |dlogit| = {worst:.3e}, top-1 agreement {agree:.2f}")
     # Host argmax of step-by-step logits == the kernel's own greedy loop.
     lg = ctx_greedy.prefill_step(prompt, 0)
     first = int(np.argmax(lg))
