@@ -60,6 +60,14 @@ constexpr size_t kRingBytes = (size_t)kSlots * kSlotBytes;
 constexpr size_t kWorkBytes = 25 * 1024;  // activation / attention workspace after the ring
 constexpr int kMaxLayers = 64;
 
+// Dynamic shared memory: the ring, then the work area.  Functions address it
+// through these file-scope symbols (not through pointer parameters) so that
+// every access compiles to a shared-memory instruction.
+extern __shared__ __align__(128) char mega_dsmem[];
+__shared__ float mega_red[33];
+__shared__ unsigned mega_done[kSlots];  // warps done with the chunk in each slot
+__device__ __forceinline__ char *work_area() { return mega_dsmem + kRingBytes; }
+
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -203,11 +211,10 @@ __device__ __forceinline__ void make_plan(const MegaArgs &a, int64_t pos, int tp
 }
 
 struct Ring {
-  char *base;      // kSlots x kSlotBytes
   uint64_t *full;  // [kSlots] one mbarrier per slot (completes when its bytes land)
 };
 
-__device__ __forceinline__ char *slot_ptr(const Ring &r, unsigned j) { return r.base + (size_t)(j % kSlots) * kSlotBytes; }
+__device__ __forceinline__ char *slot_ptr(unsigned j) { return mega_dsmem + (j % kSlots) * kSlotBytes; }
 
 __device__ __forceinline__ void issue_rows(const uint8_t *qs, int64_t stride, const Rows &rs, int i, int64_t row_offset,
                                            char *dst, uint64_t *bar) {
@@ -218,11 +225,13 @@ __device__ __forceinline__ void issue_rows(const uint8_t *qs, int64_t stride, co
   bulk_g2s(dst, qs + (first + row_offset) * stride, bytes, bar);
 }
 
-// Thread 0: copy stream chunk j into its slot (nothing past the end).
+// One thread: copy stream chunk j into its slot (nothing past the end).
+// Not inlined: it runs once per chunk and stays out of the consumers' loop
+// code.
 template <int HD, bool F16>
-__device__ __forceinline__ void ring_issue(const Plan &p, const Ring &r, unsigned j) {
+__device__ __noinline__ void ring_issue(const Plan &p, const Ring &r, unsigned j) {
   if ((int)j >= p.total) return;
-  char *dst = slot_ptr(r, j);
+  char *dst = slot_ptr(j);
   uint64_t *bar = &r.full[j % kSlots];
   const int lay_chunks = p.n_layers * p.per_layer;
   if ((int)j >= lay_chunks) {
@@ -253,13 +262,15 @@ __device__ __forceinline__ void ring_wait(const Ring &r, unsigned j, int *err) {
   if (!mbar_wait_bounded(&r.full[j % kSlots], (j / kSlots) & 1u) && err) atomicOr(err, kErrRingWait);
 }
 
-// After every thread is done with chunk j (the caller synchronises), thread
-// 0 refills its slot with chunk j + kSlots.  `wrote`: the slot was also
-// written through the generic proxy, which must be ordered before the
-// async-proxy refill.
+// After every thread is done with chunk j (the caller synchronises), one
+// thread refills its slot with chunk j + kSlots: lane 0 of the last warp,
+// which has the fewest rows of a chunk.  `wrote`: the slot was also written
+// through the generic proxy, which must be ordered before the async-proxy
+// refill.
+constexpr int kProducer = (kMW - 1) * 32;
 template <int HD, bool F16>
 __device__ __forceinline__ void ring_release(const Plan &p, const Ring &r, unsigned j, bool wrote) {
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == kProducer) {
     if (wrote) fence_proxy_async();
     ring_issue<HD, F16>(p, r, j + kSlots);
   }
@@ -308,30 +319,27 @@ __device__ __forceinline__ void quantize_done_blocks(const GemvArgs &a, int64_t 
 }
 
 // Row segment of one weight row in a ring slot (same layout as in HBM:
-// quants, then the f16 scales): blocks seg * 128 + lane + 32 v, v < 4.
+// quants, then the f16 scales): blocks bq[v] = seg * 128 + lane + 32 v, v < 4.
+// Blocks past the row end (ragged last segment) read block 0 and are zeroed
+// by mask bit v, without branches.
 template <int QUANT>
-__device__ __forceinline__ void w4s_load(const char *row, int nb, int seg, int lane, W4Row<QUANT> &r) {
+__device__ __forceinline__ void w4s_load(const char *row, int nb, const int (&bq)[4], unsigned vmask,
+                                         W4Row<QUANT> &r) {
   constexpr int BQ = QUANT == JAL_Q4_0 ? 16 : 32;  // quant bytes per block
   const uint16_t *d = (const uint16_t *)(row + (size_t)nb * BQ);
   uint32_t h[4];
 #pragma unroll
   for (int v = 0; v < 4; v++) {
-    const int b = seg * kSegBlocks + lane + 32 * v;
-    if (b < nb) {
-      const uint4 q0 = *(const uint4 *)(row + (size_t)b * BQ);
-      r.q[(BQ / 4) * v + 0] = q0.x; r.q[(BQ / 4) * v + 1] = q0.y;
-      r.q[(BQ / 4) * v + 2] = q0.z; r.q[(BQ / 4) * v + 3] = q0.w;
-      if (BQ == 32) {
-        const uint4 q1 = *(const uint4 *)(row + (size_t)b * BQ + 16);
-        r.q[(BQ / 4) * v + 4] = q1.x; r.q[(BQ / 4) * v + 5] = q1.y;
-        r.q[(BQ / 4) * v + 6] = q1.z; r.q[(BQ / 4) * v + 7] = q1.w;
-      }
-      h[v] = d[b];
-    } else {
-#pragma unroll
-      for (int k = 0; k < BQ / 4; k++) r.q[(BQ / 4) * v + k] = 0u;
-      h[v] = 0u;
+    const bool ok = (vmask >> v) & 1u;
+    const uint4 q0 = *(const uint4 *)(row + (size_t)bq[v] * BQ);
+    r.q[(BQ / 4) * v + 0] = ok ? q0.x : 0u; r.q[(BQ / 4) * v + 1] = ok ? q0.y : 0u;
+    r.q[(BQ / 4) * v + 2] = ok ? q0.z : 0u; r.q[(BQ / 4) * v + 3] = ok ? q0.w : 0u;
+    if (BQ == 32) {
+      const uint4 q1 = *(const uint4 *)(row + (size_t)bq[v] * BQ + 16);
+      r.q[(BQ / 4) * v + 4] = ok ? q1.x : 0u; r.q[(BQ / 4) * v + 5] = ok ? q1.y : 0u;
+      r.q[(BQ / 4) * v + 6] = ok ? q1.z : 0u; r.q[(BQ / 4) * v + 7] = ok ? q1.w : 0u;
     }
+    h[v] = ok ? (uint32_t)d[bq[v]] : 0u;
   }
   r.d = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
 }
@@ -339,14 +347,16 @@ __device__ __forceinline__ void w4s_load(const char *row, int nb, int seg, int l
 // One projection over this CTA's row slice, weights from the ring.  j is the
 // stream index of the phase's first chunk; returns the index after its last.
 template <int QUANT, int HD, bool F16>
-__device__ __noinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, const Ring &r, const GemvArgs &g,
-                                             const Rows &rs, unsigned j, char *work, float *red) {
+__device__ __forceinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, const Ring &r, const GemvArgs &g,
+                                             const Rows &rs, unsigned j) {
+  char *work = work_area();
+  float *red = mega_red;
   const int nb = (int)(g.w.cols / 32), nseg = seg_count(g.w.cols), nbp = nseg * kSegBlocks;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int seg = warp % nseg, phase = warp / nseg, nph = kMW / nseg;
   const bool swiglu = g.out_mode == GEMV_OUT_SWIGLU;
   if (g.out_mode == GEMV_OUT_ADD) {  // residual rows of this CTA, read once (visible after the prologue's barrier)
-    float *yb = (float *)(work + w4_act_region(g.in_mode, nb, nseg)) + rs.rpc * nseg;
+    float *yb = (float *)(work + w4_act_region(g.in_mode, nb, nseg)) + kSlots * rs.rpc * nseg;
     for (int i = threadIdx.x; i < rs.cnt; i += kMT) yb[i] = g.y[rs.r0 + i];
   }
   if (g.in_mode == GEMV_IN_NORM && nb * 4 <= 4 * kMT) {
@@ -354,6 +364,14 @@ __device__ __noinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, c
   } else {
     gemv_prologue_pre<1, kMW>(g, work, nb, nbp);
     gemv_prologue<1, kMW>(g, work, nb, nbp, red);
+  }
+  int bq[4];
+  unsigned vmask = 0;
+#pragma unroll
+  for (int v = 0; v < 4; v++) {
+    const int b = seg * kSegBlocks + lane + 32 * v;
+    bq[v] = b < nb ? b : 0;
+    vmask |= (b < nb ? 1u : 0u) << v;
   }
   W4Act x;
 #pragma unroll
@@ -365,33 +383,39 @@ __device__ __noinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, c
     x.sc[v] = ss.x;
     x.sum[v] = __float_as_int(ss.y);
   }
-  float *part = (float *)(work + w4_act_region(g.in_mode, nb, nseg));  // [rpc][nseg]
+  float *part = (float *)(work + w4_act_region(g.in_mode, nb, nseg));  // [kSlots][rpc][nseg]
   const int64_t qs = g.w.qs_stride, r0 = rs.r0, cnt = rs.cnt;
   const int rpc = rs.rpc, nch = rs.n;
   const bool add = g.out_mode == GEMV_OUT_ADD;
-  float *y = g.y, *ybase = part + rpc * nseg;  // ybase: [cnt] residual + bias of this CTA's rows
+  float *y = g.y, *ybase = part + kSlots * rpc * nseg;  // ybase: [cnt] residual of this CTA's rows
   const float *bias = g.bias;
-  const char *rbase = r.base;
   uint64_t *full = r.full;
   int *err = a.err;
   // output row i of this CTA: y + bias (ADD) or bias (STORE) added to the dot
   auto finish = [&](int64_t i, float s) -> float {
     return add ? ybase[i] + (bias ? s + bias[r0 + i] : s) : (bias ? s + bias[r0 + i] : s);
   };
+  // Warps run through the chunks independently: each takes the rows of its
+  // 128-block segment whose index in the CTA's slice is congruent to its
+  // phase (balanced over the whole slice), then counts itself done with the
+  // chunk; the last warp to finish a chunk combines the segment partials (in
+  // segment order) and refills the chunk's slot.
   for (int c = 0; c < nch; c++) {
     const int64_t first = (int64_t)c * rpc;  // first row of the chunk, relative to r0
     const int n = (int)(cnt - first < rpc ? cnt - first : rpc);
     if (!mbar_wait_bounded(&full[j % kSlots], (j / kSlots) & 1u) && err) atomicOr(err, kErrRingWait);
     if (swiglu && !mbar_wait_bounded(&full[(j + 1) % kSlots], ((j + 1) / kSlots) & 1u) && err)
       atomicOr(err, kErrRingWait);
-    const char *wg = rbase + (size_t)(j % kSlots) * kSlotBytes;
-    const char *wu = rbase + (size_t)((j + 1) % kSlots) * kSlotBytes;
+    const char *wg = slot_ptr(j);
+    const char *wu = slot_ptr(j + 1);
+    float *pslot = part + (j % kSlots) * rpc * nseg;  // [rpc][nseg]
     if (phase < nph) {
+      int lr = (int)((phase - (int)(first % nph) + nph) % nph);
       if (swiglu) {
-        for (int lr = phase; lr < n; lr += nph) {
+        for (; lr < n; lr += nph) {
           W4Row<QUANT> wa, wb;
-          w4s_load<QUANT>(wg + (size_t)lr * qs, nb, seg, lane, wa);
-          w4s_load<QUANT>(wu + (size_t)lr * qs, nb, seg, lane, wb);
+          w4s_load<QUANT>(wg + (size_t)lr * qs, nb, bq, vmask, wa);
+          w4s_load<QUANT>(wu + (size_t)lr * qs, nb, bq, vmask, wb);
           float sa = w4_dot<QUANT>(wa, x), sb = w4_dot<QUANT>(wb, x);
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) {
@@ -401,12 +425,12 @@ __device__ __noinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, c
           if (lane == 0) y[r0 + first + lr] = swiglu_one(sa, sb);
         }
       } else {
-        for (int lr = phase; lr < n; lr += 2 * nph) {  // two rows at a time
+        for (; lr < n; lr += 2 * nph) {  // two rows at a time
           const int lr2 = lr + nph;
           const bool two = lr2 < n;
           W4Row<QUANT> wa, wb;
-          w4s_load<QUANT>(wg + (size_t)lr * qs, nb, seg, lane, wa);
-          if (two) w4s_load<QUANT>(wg + (size_t)lr2 * qs, nb, seg, lane, wb);
+          w4s_load<QUANT>(wg + (size_t)lr * qs, nb, bq, vmask, wa);
+          if (two) w4s_load<QUANT>(wg + (size_t)lr2 * qs, nb, bq, vmask, wb);
           float sa = w4_dot<QUANT>(wa, x), sb = two ? w4_dot<QUANT>(wb, x) : 0.0f;
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) {
@@ -415,8 +439,8 @@ __device__ __noinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, c
           }
           if (lane == 0) {
             if (nseg > 1) {
-              part[lr * nseg + seg] = sa;
-              if (two) part[lr2 * nseg + seg] = sb;
+              pslot[lr * nseg + seg] = sa;
+              if (two) pslot[lr2 * nseg + seg] = sb;
             } else {
               y[r0 + first + lr] = finish(first + lr, sa);
               if (two) y[r0 + first + lr2] = finish(first + lr2, sb);
@@ -425,17 +449,27 @@ __device__ __noinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, c
         }
       }
     }
-    if (nseg > 1 && !swiglu) {
-      __syncthreads();
-      if ((int)threadIdx.x < n) {
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(&mega_done[j % kSlots], 1u) == kMW - 1;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence_block();
+      if (nseg > 1 && !swiglu && lane < n) {
         float sum = 0.0f;
-        for (int q = 0; q < nseg; q++) sum += part[threadIdx.x * nseg + q];
-        y[r0 + first + threadIdx.x] = finish(first + threadIdx.x, sum);
+        for (int q = 0; q < nseg; q++) sum += pslot[lane * nseg + q];
+        y[r0 + first + lane] = finish(first + lane, sum);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mega_done[j % kSlots] = 0u;
+        ring_issue<HD, F16>(p, r, j + kSlots);
+        if (swiglu) ring_issue<HD, F16>(p, r, j + 1 + kSlots);
       }
     }
-    __syncthreads();
-    ring_release<HD, F16>(p, r, j, false);
-    if (swiglu) ring_release<HD, F16>(p, r, j + 1, false);
     j += swiglu ? 2 : 1;
   }
   if (swiglu && g.yq) quantize_done_blocks(g, rs.r0, rs.cnt);
@@ -445,8 +479,8 @@ __device__ __noinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p, c
 
 // ---- attention -------------------------------------------------------------
 template <int HD, bool F16, int GP>
-__device__ __noinline__ unsigned attn_stream(const MegaArgs &a, const Plan &p, const Ring &r, int layer, unsigned j,
-                                             char *work) {
+__device__ __forceinline__ unsigned attn_stream(const MegaArgs &a, const Plan &p, const Ring &r, int layer, unsigned j) {
+  char *work = work_area();
   using Gm = AttnGeom<HD, F16, kMW>;
   constexpr int TP = Gm::TP, LG = Gm::LG, PPS = Gm::PPS, DPL = Gm::DPL, TPW = Gm::TPW, VD = Gm::VD;
   const Slice &sl = p.sl;
@@ -545,7 +579,7 @@ __device__ __noinline__ unsigned attn_stream(const MegaArgs &a, const Plan &p, c
     ring_wait(r, j, a.err);
     const int64_t t0 = sl.s0 + (int64_t)k * TP;
     const int n = (int)(sl.s1 - t0 < TP ? sl.s1 - t0 : TP);
-    char *Ks = slot_ptr(r, j);
+    char *Ks = slot_ptr(j);
     char *Vs = Ks + TP * Gm::ROW;
     if (own_pos && pos >= t0 && pos < t0 + n) {  // the new k / v are not in the cache copy yet
       const int jp = (int)(pos - t0);
@@ -815,8 +849,7 @@ __device__ __noinline__ void argmax_phase(const MegaArgs &a, float *red) {
 
 // ---- phases: build the projection's arguments and run it from the ring ------
 template <int HD, bool F16, int QW>
-__device__ __noinline__ unsigned ph_proj(const MegaArgs &a, const Plan &p, const Ring &r, int kind, int l, unsigned j,
-                                         char *work, float *red) {
+__device__ __forceinline__ unsigned ph_proj(const MegaArgs &a, const Plan &p, const Ring &r, int kind, int l, unsigned j) {
   GemvArgs g;
   g.m = 1;
   const Rows *rs;
@@ -851,24 +884,48 @@ __device__ __noinline__ unsigned ph_proj(const MegaArgs &a, const Plan &p, const
       rs = &p.dn;
     }
   }
-  return gemv_stream<QW, HD, F16>(a, p, r, g, *rs, j, work, red);
+  return gemv_stream<QW, HD, F16>(a, p, r, g, *rs, j);
+}
+
+// Q4_0 kernels inline every phase into the kernel (no calls between the
+// phases' loops); Q8_0 rows need more registers, so there each phase stays
+// a separate function.
+template <int HD, bool F16, int QW>
+__device__ __noinline__ unsigned ph_proj_call(const MegaArgs &a, const Plan &p, const Ring &r, int kind, int l,
+                                              unsigned j) {
+  return ph_proj<HD, F16, QW>(a, p, r, kind, l, j);
+}
+template <int HD, bool F16, int GP>
+__device__ __noinline__ unsigned attn_call(const MegaArgs &a, const Plan &p, const Ring &r, int l, unsigned j) {
+  return attn_stream<HD, F16, GP>(a, p, r, l, j);
+}
+template <int HD, bool F16, int GP, int QW>
+__device__ __forceinline__ unsigned run_proj(const MegaArgs &a, const Plan &p, const Ring &r, int kind, int l,
+                                             unsigned j) {
+  if constexpr (QW == JAL_Q4_0) return ph_proj<HD, F16, QW>(a, p, r, kind, l, j);
+  else return ph_proj_call<HD, F16, QW>(a, p, r, kind, l, j);
+}
+template <int HD, bool F16, int GP, int QW>
+__device__ __forceinline__ unsigned run_attn(const MegaArgs &a, const Plan &p, const Ring &r, int l, unsigned j) {
+  if constexpr (QW == JAL_Q4_0) return attn_stream<HD, F16, GP>(a, p, r, l, j);
+  else return attn_call<HD, F16, GP>(a, p, r, l, j);
 }
 
 template <int HD, bool F16, int GP, int QW>
 __global__ void __launch_bounds__(kMT, 1) k_decode_mega(const MegaArgs *__restrict__ ap) {
-  extern __shared__ __align__(128) char smem[];
-  __shared__ float red[33];
   __shared__ __align__(8) uint64_t full[kSlots];
   __shared__ int broken;
   __shared__ unsigned seq;
   __shared__ Plan plan;
   const MegaArgs &a = *ap;
-  const Ring ring{smem, full};
-  char *work = smem + kRingBytes;
+  const Ring ring{full};
   if (threadIdx.x == 0) {
     broken = 0;
     seq = 0;
-    for (int s = 0; s < kSlots; s++) mbar_init(&full[s], 1);
+    for (int s = 0; s < kSlots; s++) {
+      mbar_init(&full[s], 1);
+      mega_done[s] = 0u;
+    }
     fence_barrier_init();
   }
   make_plan(a, *a.d_pos, AttnGeom<HD, F16, 1>::TP, plan);
@@ -881,19 +938,19 @@ __global__ void __launch_bounds__(kMT, 1) k_decode_mega(const MegaArgs *__restri
   unsigned j = 0;  // stream index of the next chunk (the same in every thread)
   const int n_layers = a.n_layers;
   for (int l = 0; l < n_layers; l++) {
-    j = ph_proj<HD, F16, QW>(a, plan, ring, 0, l, j, work, red);
+    j = run_proj<HD, F16, GP, QW>(a, plan, ring, 0, l, j);
     grid_sync(gb);
-    j = attn_stream<HD, F16, GP>(a, plan, ring, l, j, work);
+    j = run_attn<HD, F16, GP, QW>(a, plan, ring, l, j);
     grid_sync(gb);
-    j = ph_proj<HD, F16, QW>(a, plan, ring, 1, l, j, work, red);
+    j = run_proj<HD, F16, GP, QW>(a, plan, ring, 1, l, j);
     grid_sync(gb);
-    j = ph_proj<HD, F16, QW>(a, plan, ring, 2, l, j, work, red);
+    j = run_proj<HD, F16, GP, QW>(a, plan, ring, 2, l, j);
     grid_sync(gb);
-    j = ph_proj<HD, F16, QW>(a, plan, ring, 3, l, j, work, red);
+    j = run_proj<HD, F16, GP, QW>(a, plan, ring, 3, l, j);
     grid_sync(gb);
   }
-  j = ph_proj<HD, F16, QW>(a, plan, ring, 4, 0, j, work, red);
-  argmax_phase(a, red);
+  j = run_proj<HD, F16, GP, QW>(a, plan, ring, 4, 0, j);
+  argmax_phase(a, mega_red);
   // Every issued chunk was waited for; after a wait that gave up, wait again
   // (bounded) so that no copy is still landing when the CTA exits.
   if (threadIdx.x == 0)
@@ -929,7 +986,7 @@ size_t proj_work(int in_mode, int64_t cols, int64_t qs_stride) {
   const int nb = (int)(cols / 32), nseg = seg_count(cols);
   int64_t rpc = kSlotBytes / qs_stride;
   if (rpc < 1) rpc = 1;
-  return w4_act_region(in_mode, nb, nseg) + (size_t)rpc * nseg * 4;
+  return w4_act_region(in_mode, nb, nseg) + (size_t)kSlots * rpc * nseg * 4;
 }
 
 constexpr size_t mega_smem() { return kRingBytes + kWorkBytes; }
@@ -956,7 +1013,7 @@ int mega_check(const MegaArgs &a, int grid) {
   if (proj_work(GEMV_IN_Q8, a.F, a.F / 32 * row_q + 256) + resid > kWorkBytes) return 0;
   if (proj_work(GEMV_IN_Q8, Q, Q / 32 * row_q + 256) + resid > kWorkBytes) return 0;
   if (proj_work(GEMV_IN_NORM, a.H, a.H / 32 * row_q) > kWorkBytes) return 0;
-  if (8192 + (size_t)(kMW + 1) * 4 * HD * 4 > kWorkBytes) return 0;  // attention workspace
+  if (8192 + (size_t)kMW * 4 * HD * 4 + 2 * kMW * 4 * 4 > kWorkBytes) return 0;  // attention workspace
   return 1;
 }
 
