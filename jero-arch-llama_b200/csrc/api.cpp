@@ -484,6 +484,7 @@ static void check_device_error(Context &c) {
     JAL_CUDA(cudaMemsetAsync(c.margs.head_cnt, 0, (size_t)c.margs.n_kv * 4, c.stream));
     JAL_CUDA(cudaMemsetAsync(c.margs.am_cnt, 0, 4, c.stream));
     JAL_CUDA(cudaMemsetAsync(c.margs.ffn_cnt, 0, (size_t)(c.margs.F / 32) * 4, c.stream));
+    JAL_CUDA(cudaMemsetAsync(c.margs.hcnt, 0, (size_t)(c.margs.H / 32) * 4, c.stream));
   }
   JAL_CUDA(cudaStreamSynchronize(c.stream));
   if (e & 8u) fail(JAL_ERR_TIMEOUT, "persistent decode step: a bounded grid barrier wait gave up");

@@ -225,11 +225,18 @@ __device__ __forceinline__ void issue_rows(const uint8_t *qs, int64_t stride, co
   bulk_g2s(dst, qs + (first + row_offset) * stride, bytes, bar);
 }
 
-// One thread: copy stream chunk j into its slot (nothing past the end).
-// Not inlined: it runs once per chunk and stays out of the consumers' loop
-// code.
+// KV tile o of layer l (several bulk copies when the tile spans pages).
 template <int HD, bool F16>
-__device__ __noinline__ void ring_issue(const Plan &p, const Ring &r, unsigned j) {
+__device__ __noinline__ void issue_kv(const Plan &p, char *dst, uint64_t *bar, int l, int o) {
+  using Gm = AttnGeom<HD, F16, 1>;
+  const int64_t t0 = p.sl.s0 + (int64_t)o * Gm::TP;
+  const int n = (int)(p.sl.s1 - t0 < Gm::TP ? p.sl.s1 - t0 : Gm::TP);
+  issue_tile<HD, F16>(p.kv, l, dst, bar, t0, n, p.sl.h);
+}
+
+// One thread: copy stream chunk j into its slot (nothing past the end).
+template <int HD, bool F16>
+__device__ __forceinline__ void ring_issue(const Plan &p, const Ring &r, unsigned j) {
   if ((int)j >= p.total) return;
   char *dst = slot_ptr(j);
   uint64_t *bar = &r.full[j % kSlots];
@@ -242,13 +249,7 @@ __device__ __noinline__ void ring_issue(const Plan &p, const Ring &r, unsigned j
   int o = (int)j - l * p.per_layer;
   if (o < p.q.n) { issue_rows(p.qs[l][0], p.st[0], p.q, o, 0, dst, bar); return; }
   o -= p.q.n;
-  if (o < p.sl.nt) {
-    using Gm = AttnGeom<HD, F16, 1>;
-    const int64_t t0 = p.sl.s0 + (int64_t)o * Gm::TP;
-    const int n = (int)(p.sl.s1 - t0 < Gm::TP ? p.sl.s1 - t0 : Gm::TP);
-    issue_tile<HD, F16>(p.kv, l, dst, bar, t0, n, p.sl.h);
-    return;
-  }
+  if (o < p.sl.nt) { issue_kv<HD, F16>(p, dst, bar, l, o); return; }
   o -= p.sl.nt;
   if (o < p.o.n) { issue_rows(p.qs[l][1], p.st[1], p.o, o, 0, dst, bar); return; }
   o -= p.o.n;
@@ -281,7 +282,8 @@ __device__ __forceinline__ void ring_release(const Plan &p, const Ring &r, unsig
 // touch gets this CTA's row count added to its counter; the CTA that brings
 // a block to 32 quantizes it (QuantizedActQ8, the same values the consumer
 // would compute from the f32 row) and clears the counter.
-__device__ __forceinline__ void quantize_done_blocks(const GemvArgs &a, int64_t r0, int64_t cnt) {
+__device__ __forceinline__ void quantize_done_blocks(const float *y, int8_t *yq, float *ys, unsigned *ycnt, int64_t r0,
+                                                    int64_t cnt) {
   __shared__ int done_s[kMW];
   if (cnt <= 0) return;  // CTA-uniform
   const int64_t b0 = r0 / 32, b1 = (r0 + cnt - 1) / 32;
@@ -296,7 +298,7 @@ __device__ __forceinline__ void quantize_done_blocks(const GemvArgs &a, int64_t 
         const int64_t lo = r0 > b * 32 ? r0 : b * 32;
         const int64_t hi = r0 + cnt < b * 32 + 32 ? r0 + cnt : b * 32 + 32;
         const unsigned n = (unsigned)(hi - lo);
-        done = atomicAdd(&a.ycnt[b], n) + n == 32u;
+        done = atomicAdd(&ycnt[b], n) + n == 32u;
       }
       done_s[threadIdx.x] = done;
     }
@@ -304,14 +306,14 @@ __device__ __forceinline__ void quantize_done_blocks(const GemvArgs &a, int64_t 
     const int64_t b = bb + w;
     if (b <= b1 && done_s[w]) {
       __threadfence();
-      float v = __ldcg(a.y + b * 32 + lane);
+      float v = __ldcg(y + b * 32 + lane);
       if (!isfinite(v)) v = 0.0f;
       const float amax = warp_max(fabsf(v));
       const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
-      a.yq[b * 32 + lane] = act_quant_one(v, inv);
+      yq[b * 32 + lane] = act_quant_one(v, inv);
       if (lane == 0) {
-        a.ys[b] = scale;
-        a.ycnt[b] = 0u;
+        ys[b] = scale;
+        ycnt[b] = 0u;
       }
     }
     __syncthreads();
@@ -344,6 +346,60 @@ __device__ __forceinline__ void w4s_load(const char *row, int nb, const int (&bq
   r.d = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
 }
 
+// GEMV_IN_PREQ prologue: the block-quantized (row x norm weights) and its
+// scales go to shared memory like a Q8 input; warp 0 sums the producers'
+// partial sums of squares (fixed order) for the norm scale, returned to
+// every thread.
+__device__ __forceinline__ float prologue_preq(const GemvArgs &g, char *smem, int nb, int nbp, float *red) {
+  const int tid = threadIdx.x;
+  if (tid < 32) {
+    float ss = 0.0f;
+    for (int i = tid; i < g.ss_n; i += 32) ss += __ldcg(g.ss_part + i);
+    ss = warp_sum(ss);
+    if (tid == 0) red[32] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(nb * 32)), g.eps)));
+  }
+  for (int b = nb + tid; b < nbp; b += kMT) {
+    ((uint4 *)smem)[b] = make_uint4(0, 0, 0, 0);
+    ((uint4 *)(smem + nbp * 16))[b] = make_uint4(0, 0, 0, 0);
+    put_scale_sum(smem, nbp, b, 0.0f, 0);
+  }
+  for (int b = tid; b < nb; b += kMT) {
+    const int4 *q = (const int4 *)(g.xq + (size_t)b * 32);
+    const int4 lo = __ldcg(q), hi = __ldcg(q + 1);
+    const float sc = __ldcg(g.xs + b);
+    int s = dp4a_ss(lo.x, 0x01010101, 0);
+    s = dp4a_ss(lo.y, 0x01010101, s);
+    s = dp4a_ss(lo.z, 0x01010101, s);
+    s = dp4a_ss(lo.w, 0x01010101, s);
+    s = dp4a_ss(hi.x, 0x01010101, s);
+    s = dp4a_ss(hi.y, 0x01010101, s);
+    s = dp4a_ss(hi.z, 0x01010101, s);
+    s = dp4a_ss(hi.w, 0x01010101, s);
+    ((int4 *)smem)[b] = lo;
+    ((int4 *)(smem + nbp * 16))[b] = hi;
+    put_scale_sum(smem, nbp, b, sc, s);
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// The finished hidden rows [r0, r0 + cnt) of this CTA (rows[i]) become the
+// next RMSNorm input: u = row x norm weights, block-quantized by the CTA
+// completing each 32-block, and this CTA's sum of squares of the rows.
+__device__ __forceinline__ void next_norm_input(const float *norm, float *u, int8_t *q, float *s, unsigned *cnt_b,
+                                                float *ss_out, const float *rows, int64_t r0, int64_t cnt) {
+  __syncthreads();  // every row of the slice is final
+  float ss = 0.0f;
+  for (int64_t i = threadIdx.x; i < cnt; i += kMT) {
+    const float h = rows[i];
+    ss = fmaf(h, h, ss);
+    u[r0 + i] = __fmul_rn(h, norm[r0 + i]);
+  }
+  const float tot = block_reduce_sum<kMW>(ss, mega_red);
+  if (threadIdx.x == 0) ss_out[blockIdx.x] = tot;
+  quantize_done_blocks(u, q, s, cnt_b, r0, cnt);
+}
+
 // One projection over this CTA's row slice, weights from the ring.  j is the
 // stream index of the phase's first chunk; returns the index after its last.
 template <int QUANT, int HD, bool F16>
@@ -359,7 +415,10 @@ __device__ __forceinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p
     float *yb = (float *)(work + w4_act_region(g.in_mode, nb, nseg)) + kSlots * rs.rpc * nseg;
     for (int i = threadIdx.x; i < rs.cnt; i += kMT) yb[i] = g.y[rs.r0 + i];
   }
-  if (g.in_mode == GEMV_IN_NORM && nb * 4 <= 4 * kMT) {
+  float invn = 1.0f;  // norm scale folded into the block scales (GEMV_IN_PREQ)
+  if (g.in_mode == GEMV_IN_PREQ) {
+    invn = prologue_preq(g, work, nb, nbp, red);
+  } else if (g.in_mode == GEMV_IN_NORM && nb * 4 <= 4 * kMT) {
     prologue_m1_impl<kMW, 4, true>(g, work, nb, nbp, red);
   } else {
     gemv_prologue_pre<1, kMW>(g, work, nb, nbp);
@@ -380,7 +439,7 @@ __device__ __forceinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p
     x.lo[v] = ((const int4 *)work)[b];
     x.hi[v] = ((const int4 *)(work + nbp * 16))[b];
     const float2 ss = ((const float2 *)(work + nbp * 32))[b];
-    x.sc[v] = ss.x;
+    x.sc[v] = g.in_mode == GEMV_IN_PREQ ? __fmul_rn(ss.x, invn) : ss.x;
     x.sum[v] = __float_as_int(ss.y);
   }
   float *part = (float *)(work + w4_act_region(g.in_mode, nb, nseg));  // [kSlots][rpc][nseg]
@@ -393,7 +452,10 @@ __device__ __forceinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p
   int *err = a.err;
   // output row i of this CTA: y + bias (ADD) or bias (STORE) added to the dot
   auto finish = [&](int64_t i, float s) -> float {
-    return add ? ybase[i] + (bias ? s + bias[r0 + i] : s) : (bias ? s + bias[r0 + i] : s);
+    if (!add) return bias ? s + bias[r0 + i] : s;
+    const float v = ybase[i] + (bias ? s + bias[r0 + i] : s);
+    ybase[i] = v;  // the finished row, for the next RMSNorm input
+    return v;
   };
   // Warps run through the chunks independently: each takes the rows of its
   // 128-block segment whose index in the CTA's slice is congruent to its
@@ -472,7 +534,8 @@ __device__ __forceinline__ unsigned gemv_stream(const MegaArgs &a, const Plan &p
     }
     j += swiglu ? 2 : 1;
   }
-  if (swiglu && g.yq) quantize_done_blocks(g, rs.r0, rs.cnt);
+  if (swiglu && g.yq) quantize_done_blocks(g.y, g.yq, g.ys, g.ycnt, rs.r0, rs.cnt);
+  if (add && g.nx_u) next_norm_input(g.nx_norm, g.nx_u, g.nx_q, g.nx_s, g.nx_cnt, g.nx_ss, ybase, rs.r0, rs.cnt);
   __syncthreads();
   return j;
 }
@@ -789,8 +852,18 @@ __device__ __noinline__ void ph_embed(const MegaArgs &a) {
   const int64_t e1 = e0 + per < H ? e0 + per : H;
   const bool bad = tok >= (uint32_t)a.emb_rows;
   if (bad && blockIdx.x == 0 && threadIdx.x == 0 && a.err) atomicOr(a.err, 1);
-  for (int64_t i = e0 + threadIdx.x; i < e1; i += kMT)
-    a.hidden[i] = bad ? 0.0f : embed_value(a.emb, a.emb_quant, H, tok, i);
+  const float *norm = a.layers[0].attn_norm;
+  float ss = 0.0f;
+  for (int64_t i = e0 + threadIdx.x; i < e1; i += kMT) {
+    const float h = bad ? 0.0f : embed_value(a.emb, a.emb_quant, H, tok, i);
+    a.hidden[i] = h;
+    ss = fmaf(h, h, ss);
+    a.hu[i] = __fmul_rn(h, norm[i]);
+  }
+  // the first layer's RMSNorm input (see next_norm_input)
+  const float tot = block_reduce_sum<kMW>(ss, mega_red);
+  if (threadIdx.x == 0) a.hss[blockIdx.x] = tot;
+  quantize_done_blocks(a.hu, a.hq, a.hs, a.hcnt, e0, e1 - e0);
 }
 
 __device__ __forceinline__ bool am_better(float v, int i, float bv, int bi) {
@@ -853,27 +926,28 @@ __device__ __forceinline__ unsigned ph_proj(const MegaArgs &a, const Plan &p, co
   GemvArgs g;
   g.m = 1;
   const Rows *rs;
-  if (kind == 4) {  // LM head (final RMSNorm prologue)
-    g.w = a.lm_head; g.rows = a.V; g.in_mode = GEMV_IN_NORM;
-    g.x = a.hidden; g.x_stride = a.H; g.norm_w = a.out_norm; g.eps = a.eps;
+  g.eps = a.eps;
+  g.ss_part = a.hss; g.ss_n = (int)gridDim.x;  // RMSNorm inputs (GEMV_IN_PREQ)
+  if (kind == 4) {  // LM head (final RMSNorm)
+    g.w = a.lm_head; g.rows = a.V; g.in_mode = GEMV_IN_PREQ; g.xq = a.hq; g.xs = a.hs;
     g.out_mode = GEMV_OUT_STORE; g.y = a.logits; g.y_stride = a.V;
     rs = &p.head;
   } else {
     const MegaLayer &L = a.layers[l];
     if (kind == 0) {  // Q/K/V (RMSNorm prologue)
       const int64_t QKV = (a.n_heads_q + 2 * a.n_kv) * HD;
-      g.w = L.qkv; g.rows = QKV; g.in_mode = GEMV_IN_NORM;
-      g.x = a.hidden; g.x_stride = a.H; g.norm_w = L.attn_norm; g.eps = a.eps;
+      g.w = L.qkv; g.rows = QKV; g.in_mode = GEMV_IN_PREQ; g.xq = a.hq; g.xs = a.hs;
       g.out_mode = GEMV_OUT_STORE; g.y = a.qkv; g.y_stride = QKV;
       rs = &p.q;
     } else if (kind == 1) {  // O + residual (+ bias)
       g.w = L.wo; g.rows = a.H; g.in_mode = GEMV_IN_Q8;
       g.xq = a.attn_q; g.xs = a.attn_s; g.xq_stride = a.n_heads_q * HD;
       g.out_mode = GEMV_OUT_ADD; g.y = a.hidden; g.y_stride = a.H; g.bias = L.bo;
+      g.nx_norm = L.ffn_norm;  // the gate/up phase's RMSNorm input
+      g.nx_u = a.hu; g.nx_q = a.hq; g.nx_s = a.hs; g.nx_cnt = a.hcnt; g.nx_ss = a.hss;
       rs = &p.o;
     } else if (kind == 2) {  // gate/up + SwiGLU (RMSNorm prologue), also quantized
-      g.w = L.gateup; g.rows = a.F; g.in_mode = GEMV_IN_NORM;
-      g.x = a.hidden; g.x_stride = a.H; g.norm_w = L.ffn_norm; g.eps = a.eps;
+      g.w = L.gateup; g.rows = a.F; g.in_mode = GEMV_IN_PREQ; g.xq = a.hq; g.xs = a.hs;
       g.out_mode = GEMV_OUT_SWIGLU; g.y = a.ffn; g.y_stride = a.F; g.up_offset = a.F;
       g.yq = a.ffn_q; g.ys = a.ffn_s; g.ycnt = a.ffn_cnt;
       rs = &p.gu;
@@ -881,6 +955,8 @@ __device__ __forceinline__ unsigned ph_proj(const MegaArgs &a, const Plan &p, co
       g.w = L.wdown; g.rows = a.H; g.in_mode = GEMV_IN_Q8;
       g.xq = a.ffn_q; g.xs = a.ffn_s; g.xq_stride = a.F;
       g.out_mode = GEMV_OUT_ADD; g.y = a.hidden; g.y_stride = a.H;
+      g.nx_norm = l + 1 < a.n_layers ? a.layers[l + 1].attn_norm : a.out_norm;  // next RMSNorm input
+      g.nx_u = a.hu; g.nx_q = a.hq; g.nx_s = a.hs; g.nx_cnt = a.hcnt; g.nx_ss = a.hss;
       rs = &p.dn;
     }
   }
@@ -1012,7 +1088,7 @@ int mega_check(const MegaArgs &a, int grid) {
   if (a.n_layers > kMaxLayers) return 0;
   if (proj_work(GEMV_IN_Q8, a.F, a.F / 32 * row_q + 256) + resid > kWorkBytes) return 0;
   if (proj_work(GEMV_IN_Q8, Q, Q / 32 * row_q + 256) + resid > kWorkBytes) return 0;
-  if (proj_work(GEMV_IN_NORM, a.H, a.H / 32 * row_q) > kWorkBytes) return 0;
+  if (proj_work(GEMV_IN_PREQ, a.H, a.H / 32 * row_q) > kWorkBytes) return 0;
   if (8192 + (size_t)kMW * 4 * HD * 4 + 2 * kMW * 4 * 4 > kWorkBytes) return 0;  // attention workspace
   return 1;
 }
@@ -1022,11 +1098,16 @@ size_t mega_part_bytes(const MegaArgs &a) {
   return (size_t)a.n_kv * a.splits * (GP * a.kv.head_dim + 2 * GP) * sizeof(float);
 }
 
-int launch_decode_mega(const MegaArgs &a, const MegaArgs *dev_args, int grid, cudaStream_t s) {
+int prepare_decode_mega(const MegaArgs &a, int grid) {
   if (!mega_check(a, grid)) return 0;
   const void *fn = pick_mega((int)a.kv.head_dim, a.kv.f16, (int)(a.n_heads_q / a.n_kv), mega_quant(a));
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mega_smem()) == cudaSuccess;
+}
+
+int launch_decode_mega(const MegaArgs &a, const MegaArgs *dev_args, int grid, cudaStream_t s) {
+  const void *fn = pick_mega((int)a.kv.head_dim, a.kv.f16, (int)(a.n_heads_q / a.n_kv), mega_quant(a));
+  if (!fn) return 0;
   const size_t smem = mega_smem();
-  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kMT);

@@ -30,7 +30,10 @@ struct DevMat {
 inline int64_t d_stride_for(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
 
 // ---- GEMV (decode, M tokens <= kGemvMaxM) ------------------------------
-enum GemvIn : int { GEMV_IN_Q8 = 0, GEMV_IN_F32 = 1, GEMV_IN_NORM = 2 };
+// GEMV_IN_PREQ (persistent step only): the RMSNorm input arrives already
+// block-quantized as (row x norm weights) with the producers' partial sums of
+// squares of the row; the norm scale is folded into the block scales.
+enum GemvIn : int { GEMV_IN_Q8 = 0, GEMV_IN_F32 = 1, GEMV_IN_NORM = 2, GEMV_IN_PREQ = 3 };
 enum GemvOut : int { GEMV_OUT_STORE = 0, GEMV_OUT_ADD = 1, GEMV_OUT_SWIGLU = 2 };
 constexpr int kGemvMaxM = 8;
 constexpr int kGemvMaxSmem = 200 * 1024;
@@ -54,6 +57,15 @@ struct GemvArgs {
   int8_t *yq = nullptr;         // SWIGLU (persistent step): y also as QuantizedActQ8,
   float *ys = nullptr;          //   each 32-block quantized by the CTA that completes it
   unsigned *ycnt = nullptr;     //   per-block row counters (zero between uses)
+  const float *ss_part = nullptr;  // GEMV_IN_PREQ: partial sums of squares of the row
+  int ss_n = 0;
+  // GEMV_OUT_ADD in the persistent step: the finished rows also become the
+  // next RMSNorm input: u = row x nx_norm (nx_u, block-quantized into nx_q /
+  // nx_s through nx_cnt) and this CTA's sum of squares (nx_ss[cta]).
+  const float *nx_norm = nullptr;
+  float *nx_u = nullptr, *nx_s = nullptr, *nx_ss = nullptr;
+  int8_t *nx_q = nullptr;
+  unsigned *nx_cnt = nullptr;
   int grid = 0;                 // CTAs (0 = auto)
   int pdl = 0;                  // launch with programmatic dependent launch
   int64_t pf_bytes = -1;        // L2 prefetch budget per CTA (-1 = default)
@@ -204,6 +216,12 @@ struct MegaArgs {
   int8_t *attn_q = nullptr, *ffn_q = nullptr;
   float *attn_s = nullptr, *ffn_s = nullptr;
   unsigned *ffn_cnt = nullptr;  // [F / 32] block counters of the SwiGLU output (zero between steps)
+  // next RMSNorm input, formed by the phase that finishes the hidden row:
+  float *hu = nullptr;          // [H] hidden x norm weights
+  int8_t *hq = nullptr;         // [H] its QuantizedActQ8 blocks
+  float *hs = nullptr;          // [H / 32] their scales
+  unsigned *hcnt = nullptr;     // [H / 32] block counters (zero between uses)
+  float *hss = nullptr;         // [grid] per-CTA sums of squares of the hidden row
   float *attn_part = nullptr;   // [n_kv][splits][4 * hd + 8] attention split partials
   unsigned *head_cnt = nullptr; // [n_kv] split arrival counters (zero between steps)
   unsigned *bar = nullptr;      // grid barrier: count, generation
@@ -212,7 +230,8 @@ struct MegaArgs {
   unsigned *am_cnt = nullptr;
   int *err = nullptr;           // error word (bit 1 token, 2 copy wait, 8 grid wait)
   int splits = 1;               // attention CTAs per KV head (<= 64)
-  int attn_split_tokens = 128;  // attended positions per attention split (fewer splits for short spans)
+  int attn_split_tokens = 128;
+  int l2_ahead = 8;             // stream chunks prefetched into L2 beyond the shared-memory ring  // attended positions per attention split (fewer splits for short spans)
 };
 // Whether the persistent decode step supports this model shape at `grid`
 // CTAs (head_dim, KV type, query heads per KV head, segment counts, shared
@@ -220,6 +239,9 @@ struct MegaArgs {
 int mega_check(const MegaArgs &a, int grid);
 // Bytes of the attention split partials (MegaArgs::attn_part).
 size_t mega_part_bytes(const MegaArgs &a);
+// Checks the shape (mega_check) and sets the kernel's shared-memory limit;
+// call once before the first launch.  Returns 0 when the shape does not fit.
+int prepare_decode_mega(const MegaArgs &a, int grid);
 // Launches one decode token as a cooperative kernel of `grid` CTAs; the
 // kernel reads its arguments from dev_args, a device copy of `a`.  Returns 0
 // when no instantiation fits or the launch was rejected.

@@ -815,10 +815,13 @@ static void setup_mega(Context &ctx, int sms) {
   a.err = ctx.d_err;
   a.splits = std::max(1, std::min(64, sms / (int)g.n_heads_kv));
   if (const char *v = getenv("JAL_MEGA_SPLIT_TOKENS")) a.attn_split_tokens = std::max(1, atoi(v));
-  if (!mega_check(a, sms)) return;
+  if (const char *v = getenv("JAL_MEGA_L2_AHEAD")) a.l2_ahead = std::max(0, std::min(64, atoi(v)));
+  if (!prepare_decode_mega(a, sms)) return;
   const size_t part = mega_part_bytes(a);
+  const size_t H = g.hidden_dim;
   auto lb = alloc(layers.size() * sizeof(MegaLayer) + 256 + part + 256 + g.n_heads_kv * 4 + 256 + 64 + 256 +
-                  sizeof(MegaArgs));
+                  sizeof(MegaArgs) + 256 + H * 4 + 256 + H + 256 + H / 32 * 4 + 256 + H / 32 * 4 + 256 + (size_t)sms * 4 +
+                  256);
   ctx.bufs.push_back(lb);
   JAL_CUDA(cudaMemset(lb->ptr, 0, lb->bytes));
   char *p = lb->as<char>();
@@ -830,6 +833,11 @@ static void setup_mega(Context &ctx, int sms) {
   a.head_cnt = (unsigned *)take(g.n_heads_kv * 4);
   a.bar = (unsigned *)take(8);
   MegaArgs *da = (MegaArgs *)take(sizeof(MegaArgs));
+  a.hu = (float *)take(H * 4);
+  a.hq = (int8_t *)take(H);
+  a.hs = (float *)take(H / 32 * 4);
+  a.hcnt = (unsigned *)take(H / 32 * 4);
+  a.hss = (float *)take((size_t)sms * 4);
   if ((size_t)(p - lb->as<char>()) > lb->bytes) fail(JAL_ERR_INVALID_ARGUMENT, "internal: persistent decode layout overflow");
   JAL_CUDA(cudaMemcpy(da, &a, sizeof(MegaArgs), cudaMemcpyHostToDevice));
   ctx.mega_dev_args = da;
