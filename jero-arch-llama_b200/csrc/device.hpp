@@ -224,14 +224,13 @@ struct MegaArgs {
   float *hss = nullptr;         // [grid] per-CTA sums of squares of the hidden row
   float *attn_part = nullptr;   // [n_kv][splits][4 * hd + 8] attention split partials
   unsigned *head_cnt = nullptr; // [n_kv] split arrival counters (zero between steps)
-  unsigned *bar = nullptr;      // grid barrier: count, generation
+  unsigned *bar = nullptr;      // grid barrier arrival count (zero between steps)
   float *am_val = nullptr;
   int *am_idx = nullptr;
   unsigned *am_cnt = nullptr;
   int *err = nullptr;           // error word (bit 1 token, 2 copy wait, 8 grid wait)
   int splits = 1;               // attention CTAs per KV head (<= 64)
-  int attn_split_tokens = 128;
-  int l2_ahead = 8;             // stream chunks prefetched into L2 beyond the shared-memory ring  // attended positions per attention split (fewer splits for short spans)
+  int attn_split_tokens = 128;  // attended positions per attention split (fewer splits for short spans)
 };
 // Whether the persistent decode step supports this model shape at `grid`
 // CTAs (head_dim, KV type, query heads per KV head, segment counts, shared

@@ -815,7 +815,6 @@ static void setup_mega(Context &ctx, int sms) {
   a.err = ctx.d_err;
   a.splits = std::max(1, std::min(64, sms / (int)g.n_heads_kv));
   if (const char *v = getenv("JAL_MEGA_SPLIT_TOKENS")) a.attn_split_tokens = std::max(1, atoi(v));
-  if (const char *v = getenv("JAL_MEGA_L2_AHEAD")) a.l2_ahead = std::max(0, std::min(64, atoi(v)));
   if (!prepare_decode_mega(a, sms)) return;
   const size_t part = mega_part_bytes(a);
   const size_t H = g.hidden_dim;
