@@ -247,6 +247,46 @@ const jal_cached_matrix *jal_model_cache_matrix(const jal_model_cache *c,
                                                 size_t layer, int which);
 
 /* ========================================================================
+ * Tensor parallelism (one process per GPU over NCCL)
+ *
+ * The reference runs on one host with rayon threads and has no tensor
+ * parallel path; these entry points are the jal_tp_init(nccl_unique_id,
+ * rank, world) the scope table asks for.  Shards: Q/K/V by whole KV heads
+ * (and their query heads), gate/up by FFN rows, O and down by input columns
+ * (whole 32-blocks), the LM head by vocabulary rows (per-rank slices of
+ * ceil(vocab / world) rows); embedding and norms are replicated and the O
+ * bias is added by rank 0.  One f32 all-reduce after O and after down per
+ * layer, one all-gather of the logits per step.  Contexts on a sharded cache
+ * run the fast numerics only; each rank calls the same sequence of
+ * prefill / decode entry points with the same tokens.
+ * ====================================================================== */
+typedef struct jal_tp jal_tp;
+
+typedef struct jal_tp_plan_t {
+  uint64_t rank, world;
+  uint64_t q_lo, q_n;    /* query heads */
+  uint64_t kv_lo, kv_n;  /* KV heads */
+  uint64_t f_lo, f_n;    /* FFN rows / down input columns */
+  uint64_t v_lo, v_n;    /* LM-head vocabulary rows */
+  uint64_t v_pad;        /* logits slice per rank in the all-gather */
+} jal_tp_plan_t;
+
+/* Shard plan (no GPU needed); fails with JAL_ERR_CAPABILITY_MISMATCH when
+ * heads or the FFN width do not split into whole heads / 32-blocks. */
+int jal_tp_plan(size_t n_heads_q, size_t n_heads_kv, size_t ffn_dim,
+                size_t vocab, int rank, int world, jal_tp_plan_t *out);
+/* 128-byte NCCL unique id: rank 0 creates it, the caller distributes it. */
+int jal_tp_unique_id(uint8_t *id_out);
+/* Joins the communicator on the current device (collective over ranks). */
+int jal_tp_init(const uint8_t *id, int rank, int world, jal_tp **out);
+void jal_tp_free(jal_tp *tp);
+/* jal_model_repack_cache_build for this rank's shard; `tp` must outlive
+ * the cache and every context made from it. */
+int jal_model_repack_cache_build_tp(const jal_recipe *r, const void *gguf,
+                                    size_t len, int device,
+                                    const jal_tp *tp, jal_model_cache **out);
+
+/* ========================================================================
  * ExecutionContext + prefill_step / decode_step
  * ====================================================================== */
 typedef struct jal_context jal_context;

@@ -76,8 +76,12 @@ class CudaError(K3Error):
     code = ERR_CUDA
 
 
+class NcclError(K3Error):
+    code = ERR_NCCL
+
+
 _ERRORS = {ERR_TENSOR_BOUNDS: TensorBoundsError, ERR_CAPABILITY_MISMATCH: CapabilityMismatch,
-           ERR_CONTEXT_LENGTH_EXCEEDED: ContextLengthExceeded, ERR_CUDA: CudaError}
+           ERR_CONTEXT_LENGTH_EXCEEDED: ContextLengthExceeded, ERR_CUDA: CudaError, ERR_NCCL: NcclError}
 
 
 class RecipeFields(C.Structure):
@@ -107,6 +111,12 @@ class SynthConfig(C.Structure):
 
 _P = C.c_void_p
 _SZ = C.c_size_t
+
+
+class TpPlanFields(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("rank", "world", "q_lo", "q_n", "kv_lo", "kv_n", "f_lo", "f_n",
+                                          "v_lo", "v_n", "v_pad")]
+
 
 # name -> (restype, argtypes)
 _SIGS = {
@@ -144,6 +154,11 @@ _SIGS = {
     "jal_recipe_validate_model": (C.c_int, [_P, _P, _SZ]),
     "jal_recipe_decode_scratch_bytes": (_SZ, [_P, _SZ]),
     "jal_model_repack_cache_build": (C.c_int, [_P, _P, _SZ, C.c_int, C.POINTER(_P)]),
+    "jal_model_repack_cache_build_tp": (C.c_int, [_P, _P, _SZ, C.c_int, _P, C.POINTER(_P)]),
+    "jal_tp_plan": (C.c_int, [_SZ, _SZ, _SZ, _SZ, C.c_int, C.c_int, C.POINTER(TpPlanFields)]),
+    "jal_tp_unique_id": (C.c_int, [_P]),
+    "jal_tp_init": (C.c_int, [_P, C.c_int, C.c_int, C.POINTER(_P)]),
+    "jal_tp_free": (None, [_P]),
     "jal_model_repack_cache_free": (None, [_P]),
     "jal_model_cache_num_layers": (_SZ, [_P]),
     "jal_model_cache_hidden_dim": (_SZ, [_P]),
@@ -439,12 +454,51 @@ class LlamaRecipe:
     def decode_scratch_bytes(self, seq_len_upper_bound: int) -> int:
         return lib().jal_recipe_decode_scratch_bytes(self._h, seq_len_upper_bound)
 
-    def build_repack_cache(self, gguf, device: int = 0) -> "ModelRepackCache":
-        """build_repack_cache (recipe.rs:481-509)."""
+    def build_repack_cache(self, gguf, device: int = 0, tp: "TensorParallel" = None) -> "ModelRepackCache":
+        """build_repack_cache (recipe.rs:481-509); with `tp`, this rank's shard."""
         buf = _as_buffer(gguf)
         out = _P()
-        _check(lib().jal_model_repack_cache_build(self._h, buf[0], buf[1], device, C.byref(out)))
-        return ModelRepackCache(out.value)
+        if tp is None:
+            _check(lib().jal_model_repack_cache_build(self._h, buf[0], buf[1], device, C.byref(out)))
+        else:
+            _check(lib().jal_model_repack_cache_build_tp(self._h, buf[0], buf[1], device, tp._h, C.byref(out)))
+        cache = ModelRepackCache(out.value)
+        cache._tp = tp  # the communicator outlives the cache
+        return cache
+
+
+# ---- tensor parallelism (one process per GPU, NCCL) -----------------------------
+def tp_plan(n_heads_q: int, n_heads_kv: int, ffn_dim: int, vocab: int, rank: int, world: int) -> dict:
+    """Shard plan of one rank (no GPU needed): head, FFN and vocabulary ranges."""
+    f = TpPlanFields()
+    _check(lib().jal_tp_plan(n_heads_q, n_heads_kv, ffn_dim, vocab, rank, world, C.byref(f)))
+    return {n: getattr(f, n) for n, _ in TpPlanFields._fields_}
+
+
+def tp_unique_id() -> bytes:
+    """128-byte NCCL unique id; rank 0 creates it and shares it with the other ranks."""
+    buf = (C.c_uint8 * 128)()
+    _check(lib().jal_tp_unique_id(C.addressof(buf)))
+    return bytes(buf)
+
+
+class TensorParallel:
+    """NCCL communicator of one rank on the current device (collective: every
+    rank constructs it with the same id)."""
+
+    def __init__(self, unique_id: bytes, rank: int, world: int):
+        if len(unique_id) != 128:
+            raise ValueError("the NCCL unique id is 128 bytes")
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        out = _P()
+        _check(lib().jal_tp_init(C.addressof(buf), rank, world, C.byref(out)))
+        self._h = out.value
+        self.rank, self.world = rank, world
+
+    def __del__(self):
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.jal_tp_free(self._h)
+            self._h = None
 
 
 def _as_buffer(b):

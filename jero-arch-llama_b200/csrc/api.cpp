@@ -35,6 +35,9 @@ struct jal_model_cache {
 struct jal_context {
   std::unique_ptr<Context> ctx;
 };
+struct jal_tp {
+  std::unique_ptr<TpComm> t;
+};
 
 #define NEED(p)                                                  \
   do {                                                           \
@@ -400,6 +403,52 @@ int jal_model_repack_cache_build(const jal_recipe *r, const void *gguf, size_t l
 }
 
 void jal_model_repack_cache_free(jal_model_cache *c) { delete c; }
+
+int jal_tp_plan(size_t n_heads_q, size_t n_heads_kv, size_t ffn_dim, size_t vocab, int rank, int world,
+                jal_tp_plan_t *out) {
+  return guard([&] {
+    NEED(out);
+    const TpPlan p = tp_plan(n_heads_q, n_heads_kv, ffn_dim, vocab, rank, world);
+    out->rank = (uint64_t)p.rank; out->world = (uint64_t)p.world;
+    out->q_lo = p.q_lo; out->q_n = p.q_n; out->kv_lo = p.kv_lo; out->kv_n = p.kv_n;
+    out->f_lo = p.f_lo; out->f_n = p.f_n; out->v_lo = p.v_lo; out->v_n = p.v_n; out->v_pad = p.v_pad;
+  });
+}
+
+int jal_tp_unique_id(uint8_t *id_out) {
+  return guard([&] {
+    NEED(id_out);
+    tp_unique_id(id_out);
+  });
+}
+
+int jal_tp_init(const uint8_t *id, int rank, int world, jal_tp **out) {
+  return guard([&] {
+    NEED(id);
+    NEED(out);
+    *out = nullptr;
+    auto h = std::make_unique<jal_tp>();
+    h->t.reset(tp_init(id, rank, world));
+    *out = h.release();
+  });
+}
+
+void jal_tp_free(jal_tp *tp) { delete tp; }
+
+int jal_model_repack_cache_build_tp(const jal_recipe *r, const void *gguf, size_t len, int device, const jal_tp *tp,
+                                    jal_model_cache **out) {
+  return guard([&] {
+    NEED(r);
+    NEED(gguf);
+    NEED(tp);
+    NEED(out);
+    *out = nullptr;
+    GgufFile g((const uint8_t *)gguf, len);
+    auto h = std::make_unique<jal_model_cache>();
+    h->c = build_model_cache(r->r, g, device, tp->t.get());
+    *out = h.release();
+  });
+}
 
 #define CACHE_GET(name, expr) \
   size_t name(const jal_model_cache *c) { return c ? (size_t)(expr) : 0; }

@@ -523,7 +523,7 @@ struct Uploader {
 };
 }  // namespace
 
-std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g, int device) {
+std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g, int device, const TpComm *tp) {
   if (g.tensor_count() == 0) fail(JAL_ERR_CAPABILITY_MISMATCH, "build_repack_cache requires resident model tensors");
   JAL_CUDA(cudaSetDevice(device));
   auto c = std::make_unique<ModelCache>();
@@ -536,25 +536,53 @@ std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g
   uint64_t vrows, vcols;
   resolve_2d(lm, ge.hidden_dim, &vrows, &vcols);
   c->vocab_size = vrows;
+  // This rank's shard (tp.hpp); rank 0 of 1 without tensor parallelism.
+  c->tp = tp;
+  c->plan = tp_plan(ge.n_heads_q, ge.n_heads_kv, ge.ffn_dim, vrows, tp ? tp->rank : 0, tp ? tp->world : 1);
+  const TpPlan &pl = c->plan;
+  c->lgeom = ge;
+  c->lgeom.n_heads_q = pl.q_n;
+  c->lgeom.n_heads_kv = pl.kv_n;
+  c->lgeom.total_q = pl.q_n * ge.head_dim;
+  c->lgeom.total_kv = pl.kv_n * ge.head_dim;
+  c->lgeom.ffn_dim = pl.f_n;
   cudaStream_t s;
   JAL_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
   struct StreamGuard { cudaStream_t s; ~StreamGuard() { cudaStreamSynchronize(s); cudaStreamDestroy(s); } } sg{s};
   const uint64_t H = ge.hidden_dim, F = ge.ffn_dim, Q = ge.total_q, KV = ge.total_kv;
+  const uint64_t HD = ge.head_dim;
+  // Shard extents: Q/K/V rows by heads, FFN rows (gate / up) and down input
+  // columns by FFN index, O input columns by query-head width.
+  const uint64_t Ql = pl.q_n * HD, q0 = pl.q_lo * HD, KVl = pl.kv_n * HD, kv0 = pl.kv_lo * HD;
+  const uint64_t Fl = pl.f_n, f0 = pl.f_lo;
 
-  // Raw upload of several tensors into one staging block, then repack.
-  auto stage_many = [&](const std::vector<const GgufTensor *> &ts, const std::vector<uint64_t> &rows,
-                        const std::vector<uint64_t> &cols, DevBufferPtr &blk) {
+  // Raw upload of several tensors (row ranges, optionally a column range
+  // of whole blocks: one pitched copy) into one staging block, then repack.
+  struct Piece {
+    const GgufTensor *t;
+    uint64_t row0, rows, full_cols, col0, cols;
+  };
+  auto stage_many = [&](const std::vector<Piece> &ps, DevBufferPtr &blk) {
     size_t total = 0;
     std::vector<size_t> offs;
-    for (size_t i = 0; i < ts.size(); i++) {
+    for (const Piece &p : ps) {
       offs.push_back(total);
-      total += (ggml_row_bytes(ts[i]->type, cols[i]) * rows[i] + 255) / 256 * 256;
+      total += (ggml_row_bytes(p.t->type, p.cols) * p.rows + 255) / 256 * 256;
     }
     blk = alloc(total);
     std::vector<const uint8_t *> out;
-    for (size_t i = 0; i < ts.size(); i++) {
-      size_t nb = ggml_row_bytes(ts[i]->type, cols[i]) * rows[i];
-      JAL_CUDA(cudaMemcpyAsync(blk->as<uint8_t>() + offs[i], ts[i]->data, nb, cudaMemcpyHostToDevice, s));
+    for (size_t i = 0; i < ps.size(); i++) {
+      const Piece &p = ps[i];
+      const size_t full = ggml_row_bytes(p.t->type, p.full_cols), part = ggml_row_bytes(p.t->type, p.cols);
+      const size_t skip = ggml_row_bytes(p.t->type, p.col0);
+      if ((p.col0 && !skip) || !part)
+        fail(JAL_ERR_CAPABILITY_MISMATCH, "column shard of %s is not block aligned", p.t->name.c_str());
+      const uint8_t *src = (const uint8_t *)p.t->data + p.row0 * full + skip;
+      if (part == full)
+        JAL_CUDA(cudaMemcpyAsync(blk->as<uint8_t>() + offs[i], src, part * p.rows, cudaMemcpyHostToDevice, s));
+      else
+        JAL_CUDA(cudaMemcpy2DAsync(blk->as<uint8_t>() + offs[i], part, src, full, part, p.rows, cudaMemcpyHostToDevice,
+                                   s));
       out.push_back(blk->as<uint8_t>() + offs[i]);
     }
     return out;
@@ -600,14 +628,14 @@ std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g
     opt("attn_q.bias", Q, offq, hq);
     opt("attn_k.bias", KV, offk, hk);
     opt("attn_v.bias", KV, offv, hv);
-    opt("attn_output.bias", H, offo, ho);
+    if (pl.rank == 0) opt("attn_output.bias", H, offo, ho);  // added once, before the all-reduce
     if (!b.empty()) {
       L.biases = alloc(b.size() * 4);
       JAL_CUDA(cudaMemcpyAsync(L.biases->ptr, b.data(), b.size() * 4, cudaMemcpyHostToDevice, s));
       const float *base = L.biases->as<float>();
-      if (hq) L.bq = base + offq;
-      if (hk) L.bk = base + offk;
-      if (hv) L.bv = base + offv;
+      if (hq) L.bq = base + offq + q0;  // this rank's heads
+      if (hk) L.bk = base + offk + kv0;
+      if (hv) L.bv = base + offv + kv0;
       if (ho) L.bo = base + offo;
     }
     const GgufTensor *tq = tensor2d(l, "attn_q.weight", H, Q), *tk = tensor2d(l, "attn_k.weight", H, KV),
@@ -620,42 +648,43 @@ std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g
     DevBufferPtr blk;
     std::vector<CachedMatrix> parts;
     DevMat stacked;
+    const std::vector<Piece> qkv_pieces = {{tq, q0, Ql, H, 0, H}, {tk, kv0, KVl, H, 0, H}, {tv, kv0, KVl, H, 0, H}};
     if (tq->type == tk->type && tk->type == tv->type) {
-      auto raws = stage_many({tq, tk, tv}, {Q, KV, KV}, {H, H, H}, blk);
-      repack_stacked(raws, {Q, KV, KV}, (int)tq->type, H, s, parts, stacked, L.storage);
+      auto raws = stage_many(qkv_pieces, blk);
+      repack_stacked(raws, {Ql, KVl, KVl}, (int)tq->type, H, s, parts, stacked, L.storage);
       L.wq = parts[0]; L.wk = parts[1]; L.wv = parts[2];
       L.qkv = stacked;
       L.qkv_stacked = device_quant((int)tq->type);
     } else {
-      auto raws = stage_many({tq, tk, tv}, {Q, KV, KV}, {H, H, H}, blk);
+      auto raws = stage_many(qkv_pieces, blk);
       std::vector<CachedMatrix> p1;
-      repack_stacked({raws[0]}, {Q}, (int)tq->type, H, s, p1, stacked, L.storage); L.wq = p1[0];
-      repack_stacked({raws[1]}, {KV}, (int)tk->type, H, s, p1, stacked, L.storage); L.wk = p1[0];
-      repack_stacked({raws[2]}, {KV}, (int)tv->type, H, s, p1, stacked, L.storage); L.wv = p1[0];
+      repack_stacked({raws[0]}, {Ql}, (int)tq->type, H, s, p1, stacked, L.storage); L.wq = p1[0];
+      repack_stacked({raws[1]}, {KVl}, (int)tk->type, H, s, p1, stacked, L.storage); L.wk = p1[0];
+      repack_stacked({raws[2]}, {KVl}, (int)tv->type, H, s, p1, stacked, L.storage); L.wv = p1[0];
     }
     JAL_CUDA(cudaStreamSynchronize(s));
     {
-      auto raws = stage_many({to}, {H}, {Q}, blk);
-      repack_stacked(raws, {H}, (int)to->type, Q, s, parts, stacked, L.storage);
+      auto raws = stage_many({{to, 0, H, Q, q0, Ql}}, blk);  // input columns of this rank's heads
+      repack_stacked(raws, {H}, (int)to->type, Ql, s, parts, stacked, L.storage);
       L.wo = parts[0];
     }
     JAL_CUDA(cudaStreamSynchronize(s));
     if (tg->type == tu->type) {
-      auto raws = stage_many({tg, tu}, {F, F}, {H, H}, blk);
-      repack_stacked(raws, {F, F}, (int)tg->type, H, s, parts, stacked, L.storage);
+      auto raws = stage_many({{tg, f0, Fl, H, 0, H}, {tu, f0, Fl, H, 0, H}}, blk);
+      repack_stacked(raws, {Fl, Fl}, (int)tg->type, H, s, parts, stacked, L.storage);
       L.wgate = parts[0]; L.wup = parts[1];
       L.gateup = stacked;
       L.gateup_stacked = device_quant((int)tg->type);
     } else {
-      auto raws = stage_many({tg, tu}, {F, F}, {H, H}, blk);
+      auto raws = stage_many({{tg, f0, Fl, H, 0, H}, {tu, f0, Fl, H, 0, H}}, blk);
       std::vector<CachedMatrix> p1;
-      repack_stacked({raws[0]}, {F}, (int)tg->type, H, s, p1, stacked, L.storage); L.wgate = p1[0];
-      repack_stacked({raws[1]}, {F}, (int)tu->type, H, s, p1, stacked, L.storage); L.wup = p1[0];
+      repack_stacked({raws[0]}, {Fl}, (int)tg->type, H, s, p1, stacked, L.storage); L.wgate = p1[0];
+      repack_stacked({raws[1]}, {Fl}, (int)tu->type, H, s, p1, stacked, L.storage); L.wup = p1[0];
     }
     JAL_CUDA(cudaStreamSynchronize(s));
     {
-      auto raws = stage_many({td}, {H}, {F}, blk);
-      repack_stacked(raws, {H}, (int)td->type, F, s, parts, stacked, L.storage);
+      auto raws = stage_many({{td, 0, H, F, f0, Fl}}, blk);  // input columns of this rank's FFN rows
+      repack_stacked(raws, {H}, (int)td->type, Fl, s, parts, stacked, L.storage);
       L.wdown = parts[0];
     }
     JAL_CUDA(cudaStreamSynchronize(s));
@@ -669,11 +698,11 @@ std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g
   // LM head (repack_cache.rs:2226-2242) and the raw embedding table.
   {
     DevBufferPtr blk;
-    auto raws = stage_many({lm}, {vrows}, {vcols}, blk);
+    auto raws = stage_many({{lm, pl.v_lo, pl.v_n, vcols, 0, vcols}}, blk);  // this rank's vocabulary rows
     std::vector<CachedMatrix> parts;
     DevMat stacked;
     std::vector<DevBufferPtr> st;
-    repack_stacked(raws, {vrows}, (int)lm->type, vcols, s, parts, stacked, st);
+    repack_stacked(raws, {pl.v_n}, (int)lm->type, vcols, s, parts, stacked, st);
     c->lm_head = parts[0];
     c->lm_head.storage = st;
     JAL_CUDA(cudaStreamSynchronize(s));
@@ -773,6 +802,7 @@ static bool env_flag(const char *n) {
 static void setup_mega(Context &ctx, int sms) {
   const char *e = getenv("JAL_DECODE");
   if (!e || strcmp(e, "mega") != 0 || ctx.cfg.numerics != JAL_NUMERICS_FAST) return;
+  if (ctx.cache->plan.world > 1) return;  // single-GPU kernel
   const ModelCache &c = *ctx.cache;
   const Geometry &g = ctx.g;
   int coop = 0;
@@ -852,8 +882,10 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->cfg = cfg0;
   if (ctx->cfg.page_size == 0) ctx->cfg.page_size = 64;
   if (ctx->cfg.n_ctx == 0) fail(JAL_ERR_INVALID_ARGUMENT, "n_ctx must be positive");
-  const Geometry &g = c.geom;
+  const Geometry &g = c.lgeom;  // this rank's heads and FFN rows
   ctx->g = g;
+  if (c.plan.world > 1 && ctx->cfg.numerics != JAL_NUMERICS_FAST)
+    fail(JAL_ERR_CAPABILITY_MISMATCH, "tensor parallel contexts run the fast numerics only");
   if (g.n_heads_q / g.n_heads_kv > 8) fail(JAL_ERR_CAPABILITY_MISMATCH, "GQA group size > 8 is not supported");
   if (g.head_dim != 64 && g.head_dim != 128) fail(JAL_ERR_CAPABILITY_MISMATCH, "head_dim must be 64 or 128");
   for (const Layer &L : c.layers) {
@@ -868,7 +900,8 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   JAL_CUDA(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking));
   ctx->stream = ctx->own_stream;
   const uint64_t n_ctx = ctx->cfg.n_ctx, ps = ctx->cfg.page_size, n_pages = (n_ctx + ps - 1) / ps;
-  const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv, V = c.vocab_size;
+  const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv;
+  const uint64_t V = c.plan.v_pad * c.plan.world;  // gathered logits (>= vocab)
   KvView &kv = ctx->kv;
   kv.f16 = ctx->cfg.kv_f16;
   kv.n_pages = (int64_t)n_pages; kv.page_size = (int64_t)ps; kv.n_kv = (int64_t)g.n_heads_kv;
@@ -912,7 +945,7 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->am_blocks = sms;
   size_t f32s = H + (Q + 2 * KV) + Q + Q / 32 + F + (F + 31) / 32 + V + sms;
   size_t bytes = f32s * 4 + Q + ((F + 31) / 32) * 32 + 4096 + (F / 32 + 1) * 4 + 64 + (size_t)sms * 4 + (n_ctx + 2) * 4 +
-                 32 * 256;
+                 32 * 256 + c.plan.v_pad * 4 + 256;
   auto db = alloc(bytes + 1024);
   ctx->bufs.push_back(db);
   JAL_CUDA(cudaMemset(db->ptr, 0, db->bytes));
@@ -931,6 +964,7 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->ffn_s = (float *)take((F + 31) / 32 * 4);
   ctx->ffn_cnt = (unsigned *)take((F + 31) / 32 * 4);
   ctx->logits = (float *)take(V * 4);
+  ctx->logits_local = c.plan.world > 1 ? (float *)take(c.plan.v_pad * 4) : ctx->logits;
   ctx->am_val = (float *)take(sms * 4);
   ctx->am_idx = (int *)take(sms * 4);
   ctx->am_cnt = (unsigned *)take(4);
@@ -1002,8 +1036,12 @@ void Context::enqueue_decode_step(bool pdl) {
     GemvArgs oa;
     oa.w = L.wo.dm; oa.rows = (int64_t)H; oa.m = 1; oa.in_mode = GEMV_IN_Q8;
     oa.xq = attn_q; oa.xs = attn_s; oa.xq_stride = (int64_t)Q;
-    oa.out_mode = GEMV_OUT_ADD; oa.y = hidden; oa.y_stride = (int64_t)H; oa.bias = L.bo; oa.pdl = pdl;
+    // tensor parallel: rank 0 adds its partial to the residual, the others
+    // store theirs, and the all-reduce sums them into the new residual
+    oa.out_mode = c.plan.rank == 0 ? GEMV_OUT_ADD : GEMV_OUT_STORE; oa.y = hidden; oa.y_stride = (int64_t)H;
+    oa.bias = L.bo; oa.pdl = pdl;
     launch_gemv(oa, stream);
+    if (c.tp) tp_all_reduce(*c.tp, hidden, H, stream);
     GemvArgs ga;
     ga.w = L.gateup; ga.rows = (int64_t)F; ga.m = 1; ga.in_mode = GEMV_IN_NORM;
     ga.x = hidden; ga.x_stride = (int64_t)H; ga.norm_w = L.ffn_norm; ga.eps = eps;
@@ -1012,15 +1050,18 @@ void Context::enqueue_decode_step(bool pdl) {
     GemvArgs da;
     da.w = L.wdown.dm; da.rows = (int64_t)H; da.m = 1; da.in_mode = GEMV_IN_F32;
     da.x = ffn; da.x_stride = (int64_t)F;
-    da.out_mode = GEMV_OUT_ADD; da.y = hidden; da.y_stride = (int64_t)H; da.pdl = pdl;
+    da.out_mode = c.plan.rank == 0 ? GEMV_OUT_ADD : GEMV_OUT_STORE; da.y = hidden; da.y_stride = (int64_t)H;
+    da.pdl = pdl;
     launch_gemv(da, stream);
+    if (c.tp) tp_all_reduce(*c.tp, hidden, H, stream);
     n += 5;
   }
   GemvArgs la;
-  la.w = c.lm_head.dm; la.rows = (int64_t)c.vocab_size; la.m = 1; la.in_mode = GEMV_IN_NORM;
+  la.w = c.lm_head.dm; la.rows = (int64_t)c.plan.v_n; la.m = 1; la.in_mode = GEMV_IN_NORM;
   la.x = hidden; la.x_stride = (int64_t)H; la.norm_w = c.output_norm->as<float>(); la.eps = eps;
-  la.out_mode = GEMV_OUT_STORE; la.y = logits; la.y_stride = (int64_t)c.vocab_size; la.pdl = pdl;
+  la.out_mode = GEMV_OUT_STORE; la.y = logits_local; la.y_stride = (int64_t)c.plan.v_pad; la.pdl = pdl;
   launch_gemv(la, stream);
+  if (c.tp) tp_all_gather(*c.tp, logits_local, logits, c.plan.v_pad, stream);
   launch_argmax(logits, (int64_t)c.vocab_size, am_val, am_idx, am_cnt, am_blocks, d_token, d_pos, d_hist, pdl, stream);
   n += 2;
   launches_per_step = n;
@@ -1176,8 +1217,9 @@ void Context::prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bo
       launch_act_quant(pf_attn, (int64_t)m, (int64_t)Q, (int64_t)Q, pf_xq, pf_xs, stream);
       GemmArgs oa;
       oa.w = L.wo.dm; oa.m = (int64_t)m; oa.rows = (int64_t)H; oa.xq = pf_xq; oa.xs = pf_xs;
-      oa.y = pf_hidden; oa.y_stride = (int64_t)H; oa.bias = L.bo; oa.accumulate = 1;
+      oa.y = pf_hidden; oa.y_stride = (int64_t)H; oa.bias = L.bo; oa.accumulate = c.plan.rank == 0;
       launch_gemm(oa, stream);
+      if (c.tp) tp_all_reduce(*c.tp, pf_hidden, m * H, stream);
       launch_rmsnorm_quant(pf_hidden, L.ffn_norm, (int64_t)m, (int64_t)H, eps, pf_xq, pf_xs, stream);
       GemmArgs ga;
       ga.w = L.gateup; ga.m = (int64_t)m; ga.rows = (int64_t)(2 * F); ga.xq = pf_xq; ga.xs = pf_xs;
@@ -1187,16 +1229,18 @@ void Context::prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bo
       launch_act_quant(pf_ffn, (int64_t)m, (int64_t)F, (int64_t)F, pf_xq, pf_xs, stream);
       GemmArgs da;
       da.w = L.wdown.dm; da.m = (int64_t)m; da.rows = (int64_t)H; da.xq = pf_xq; da.xs = pf_xs;
-      da.y = pf_hidden; da.y_stride = (int64_t)H; da.accumulate = 1;
+      da.y = pf_hidden; da.y_stride = (int64_t)H; da.accumulate = c.plan.rank == 0;
       launch_gemm(da, stream);
+      if (c.tp) tp_all_reduce(*c.tp, pf_hidden, m * H, stream);
     }
     JAL_CUDA(cudaGetLastError());
     if (compute_logits && off + m == n) {
       GemvArgs la;
-      la.w = c.lm_head.dm; la.rows = (int64_t)c.vocab_size; la.m = 1; la.in_mode = GEMV_IN_NORM;
+      la.w = c.lm_head.dm; la.rows = (int64_t)c.plan.v_n; la.m = 1; la.in_mode = GEMV_IN_NORM;
       la.x = pf_hidden + (m - 1) * H; la.x_stride = (int64_t)H; la.norm_w = c.output_norm->as<float>(); la.eps = eps;
-      la.out_mode = GEMV_OUT_STORE; la.y = logits; la.y_stride = (int64_t)c.vocab_size;
+      la.out_mode = GEMV_OUT_STORE; la.y = logits_local; la.y_stride = (int64_t)c.plan.v_pad;
       launch_gemv(la, stream);
+      if (c.tp) tp_all_gather(*c.tp, logits_local, logits, c.plan.v_pad, stream);
       JAL_CUDA(cudaGetLastError());
     }
   }

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "device.hpp"
+#include "tp.hpp"
 #include "gguf.hpp"
 #include "jal.h"
 
@@ -90,8 +91,13 @@ struct Layer {  // LayerRepackCache (repack_cache.rs:2084-2111)
 struct ModelCache {  // ModelRepackCache (repack_cache.rs:2129-2141)
   std::string architecture;
   int device = 0;
-  Geometry geom;
+  Geometry geom;            // the model's geometry
   uint64_t vocab_size = 0;
+  // Tensor parallelism (tp.hpp): this rank's shard.  Without it the plan is
+  // rank 0 of 1 and the local geometry is the model's.
+  const TpComm *tp = nullptr;  // not owned
+  TpPlan plan;
+  Geometry lgeom;           // heads, Q/K/V widths and FFN rows of this rank (hidden as geom)
   std::vector<Layer> layers;
   DevBufferPtr output_norm;
   CachedMatrix lm_head;
@@ -102,7 +108,8 @@ struct ModelCache {  // ModelRepackCache (repack_cache.rs:2129-2141)
   size_t total_aligned_bytes() const;
 };
 
-std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g, int device);
+std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g, int device,
+                                              const TpComm *tp = nullptr);
 
 struct ContextConfig {
   uint64_t n_ctx = 4096;
@@ -132,6 +139,7 @@ struct Context {
   float *cos_tab = nullptr, *sin_tab = nullptr, *cos_long = nullptr, *sin_long = nullptr;
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *attn_s = nullptr, *ffn = nullptr, *ffn_s = nullptr,
         *logits = nullptr, *am_val = nullptr;
+  float *logits_local = nullptr;  // this rank's LM-head rows (== logits without tensor parallelism)
   int8_t *attn_q = nullptr, *ffn_q = nullptr;
   unsigned *ffn_cnt = nullptr, *am_cnt = nullptr;
   int *am_idx = nullptr;

@@ -1,0 +1,138 @@
+"""Tensor parallelism: the shard plan, the row / column-parallel combination
+on CPU (gloo, two processes, oracle projections) and a two-GPU tensor
+parallel decode against the oracle.
+
+The two-GPU test needs two CUDA devices and is skipped with fewer; the
+others run without a GPU.
+"""
+import socket
+
+import numpy as np
+import pytest
+
+import gguf_py
+import tp_workers
+
+# (name, query heads, KV heads, FFN width, vocabulary) of the configurations
+# the scope table names, plus the tiny model.
+CONFIGS = [("llama3-8b", 32, 8, 14336, 128256), ("llama3-70b", 64, 8, 28672, 128256),
+           ("qwen2-7b", 28, 4, 18944, 152064), ("tiny", 8, 2, 1536, 4096)]
+
+FAST_MAX_ATOL = 6e-2   # fast numerics vs oracle: worst logit (the single-GPU bar)
+FAST_MEAN_ATOL = 1e-2  # fast numerics vs oracle: mean |dlogit| per step
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _spawn(target, world, args_of_rank, timeout=600):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=args_of_rank(r) + (q,)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            rank, err, res = q.get(timeout=timeout)
+            assert err is None, f"rank {rank}:\n{err}"
+            out[rank] = res
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+    return out
+
+
+@pytest.mark.parametrize("name,hq,hkv,ffn,vocab", CONFIGS)
+def test_tp_plan_partitions_heads_ffn_and_vocab(jal, name, hq, hkv, ffn, vocab):
+    G = hq // hkv
+    for world in (1, 2, 4, 8):
+        if hkv % world or ffn % (32 * world):
+            with pytest.raises(jal.CapabilityMismatch):
+                jal.tp_plan(hq, hkv, ffn, vocab, 0, world)
+            continue
+        plans = [jal.tp_plan(hq, hkv, ffn, vocab, r, world) for r in range(world)]
+        kv_next = f_next = v_next = 0
+        for r, p in enumerate(plans):
+            assert p["rank"] == r and p["world"] == world
+            assert p["kv_lo"] == kv_next and p["kv_n"] == hkv // world  # whole KV heads, in order
+            assert p["q_lo"] == p["kv_lo"] * G and p["q_n"] == p["kv_n"] * G  # their query heads
+            assert p["f_lo"] == f_next and p["f_n"] % 32 == 0 and p["f_lo"] % 32 == 0  # whole blocks
+            assert p["v_lo"] == v_next and p["v_n"] <= p["v_pad"]
+            kv_next, f_next, v_next = kv_next + p["kv_n"], f_next + p["f_n"], v_next + p["v_n"]
+        assert (kv_next, f_next, v_next) == (hkv, ffn, vocab)
+        assert plans[0]["v_pad"] * world >= vocab
+
+
+def test_tp_plan_rejects_uneven_splits(jal):
+    with pytest.raises(jal.CapabilityMismatch):
+        jal.tp_plan(32, 8, 14336, 128256, 0, 3)   # 8 KV heads over 3 ranks
+    with pytest.raises(jal.CapabilityMismatch):
+        jal.tp_plan(8, 2, 1376, 4096, 0, 2)       # 1376 = 43 blocks over 2 ranks
+    with pytest.raises(jal.K3Error):
+        jal.tp_plan(32, 8, 14336, 128256, 2, 2)   # rank out of range
+
+
+def test_row_and_column_parallel_combine_to_the_unsharded_projection(jal, oracle):
+    """World 2 on CPU (gloo): all-gathered column shards are the full
+    projection bit for bit; all-reduced row shards (block-aligned input
+    columns) are the full projection up to the f32 summation order."""
+    port = _free_port()
+    out = _spawn(tp_workers.row_col_parallel_worker, 2, lambda r: (r, 2, port), timeout=300)
+    for rank in (0, 1):
+        col, full_g, row, full_d = out[rank]
+        assert np.array_equal(col, full_g)
+        assert np.max(np.abs(row - full_d)) <= 1e-5 * np.max(np.abs(full_d))
+
+
+@pytest.mark.gpu
+def test_tensor_parallel_decode_two_gpus_matches_oracle(jal, oracle, torch_cuda):
+    """TP2 on two GPUs: the tiny model (FFN 1536 so that it splits into whole
+    blocks), prefill and 24 teacher-forced decode steps on the oracle's
+    greedy tokens.  Both ranks hold identical gathered logits; against the
+    oracle they meet the fast-numerics bars of the single-GPU path; the
+    on-device greedy loop advances the position on every rank."""
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    spec_kwargs = dict(ffn_dim=1536)
+    spec = jal.SynthSpec(**spec_kwargs)
+    seed = 515
+    buf = jal.synth_gguf(spec, seed)
+    _, tensors = gguf_py.parse(buf)
+    geom = dict(num_layers=spec.num_layers, hidden_dim=spec.hidden_dim, ffn_dim=spec.ffn_dim,
+                n_heads_q=spec.n_heads_q, n_heads_kv=spec.n_heads_kv, head_dim=spec.head_dim,
+                vocab_size=spec.vocab_size, rms_eps=spec.rms_eps, rope_theta=spec.rope_theta, neox=False)
+    om = oracle.Model(tensors, geom, nthreads=8)
+    prompt = np.random.Generator(np.random.PCG64(17)).integers(0, spec.vocab_size, 16).astype(np.uint32)
+    kvo = om.new_kv(256)
+    ref = [om.prefill(kvo, 256, prompt, 0)]
+    tokens = []
+    for step in range(24):
+        tok = int(np.argmax(ref[-1]))
+        tokens.append(tok)
+        ref.append(om.decode(kvo, 256, tok, len(prompt) + step))
+    ref = np.stack(ref)
+    uid = jal.tp_unique_id()
+    steps = 12
+    out = _spawn(tp_workers.gpu_tp_worker, 2,
+                 lambda r: (r, 2, uid, spec_kwargs, seed, prompt, np.asarray(tokens), steps))
+    l0, g0, p0 = out[0]
+    l1, g1, p1 = out[1]
+    assert np.array_equal(l0, l1), "ranks disagree on the gathered logits"
+    assert np.array_equal(g0, g1)
+    assert p0 == p1 == len(prompt) + steps
+    err = np.abs(l0[:, :spec.vocab_size] - ref)
+    print(f"TP2 vs oracle: worst |dlogit| {err.max():.3e}, worst mean {err.mean(1).max():.3e}")
+    assert err.max() <= FAST_MAX_ATOL
+    assert err.mean(1).max() <= FAST_MEAN_ATOL
+    # argmax may differ from the oracle's only at a near-tie of its logits
+    for step in range(len(ref)):
+        to, tg = int(np.argmax(ref[step])), int(np.argmax(l0[step]))
+        assert to == tg or ref[step][tg] >= ref[step][to] - FAST_MAX_ATOL
