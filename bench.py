@@ -280,6 +280,9 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="llama3-8b-q4_0", choices=["llama3-8b-q4_0", "tiny"])
+    ap.add_argument("--tp", action="store_true",
+                    help="with N > 1 ranks: one tensor-parallel model over the N GPUs (strong scaling) "
+                         "instead of N independent replicas")
     ap.add_argument("--profile", choices=["gemv", "decode", "attn"],
                     help="run a small fixed workload for ncu instead of the benchmark")
     args = ap.parse_args()
@@ -311,7 +314,12 @@ def main():
     gen_s = time.perf_counter() - t0
     recipe = jal.LlamaRecipe.from_gguf(gguf)
     t0 = time.perf_counter()
-    cache = recipe.build_repack_cache(gguf, device=local)
+    tp = None
+    if dist and args.tp:
+        uid = [jal.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp = jal.TensorParallel(uid[0], rank, world)
+    cache = recipe.build_repack_cache(gguf, device=local, tp=tp)
     build_s = time.perf_counter() - t0
     n_prefill = min(args.prefill, spec.context_length - args.warmup - args.steps - 8)
     n_ctx = n_prefill + 2 * (args.warmup + args.steps) + 16
@@ -319,7 +327,7 @@ def main():
     stream = torch.cuda.Stream()  # a capturable stream: decode steps replay a CUDA graph on it
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream)
-    rng = np.random.Generator(np.random.PCG64(SEED + rank))
+    rng = np.random.Generator(np.random.PCG64(SEED + (0 if tp else rank)))  # TP ranks feed the same tokens
     prompt = rng.integers(0, spec.vocab_size, n_prefill).astype(np.uint32)
 
     # Prefill (device-timed; includes the token upload and the logits read).
@@ -355,15 +363,18 @@ def main():
     launches = ctx.launches_per_step()
     bytes_token = cache.total_aligned_bytes() - spec.vocab_size * 0  # layer weights + head + norms
     kv_bytes = 2 * spec.num_layers * spec.n_heads_kv * spec.head_dim * 2 * (n_prefill + args.warmup + args.steps // 2)
+    if tp:
+        kv_bytes //= world  # per GPU: this rank's KV heads (bytes_token is already its shard)
     step_s = t_dec / args.steps
-    line = {"metric": METRIC, "value": round(world * args.steps / t_dec, 2), "unit": "tok/s", "n_gpus": world,
+    streams = 1 if tp else world  # token streams: one per replica, one for a tensor-parallel model
+    line = {"metric": METRIC, "value": round(streams * args.steps / t_dec, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic: seeded N(0,0.02) weights quantized to Q4_0, uniform-random token ids",
             "config": {"workload": f"{args.workload} decode bs=1 greedy after a {n_prefill}-token prefill",
                        "layers": spec.num_layers, "hidden": spec.hidden_dim, "heads": [spec.n_heads_q, spec.n_heads_kv],
                        "head_dim": spec.head_dim, "ffn": spec.ffn_dim, "vocab": spec.vocab_size,
-                       "weights": "Q4_0 (4.5 bpw in HBM)", "kv_cache": "paged fp16", "parallelism": f"replicas x{world}",
+                       "weights": "Q4_0 (4.5 bpw in HBM)", "kv_cache": "paged fp16", "parallelism": f"tp{world}" if tp else f"replicas x{world}",
                        "l2": "no flush: each step streams the 4.2 GB of weights (> L2)",
                        "gguf_gen_s": round(gen_s, 1), "repack_s": round(build_s, 2)},
             "decode_step": {"bytes_per_token": bytes_token + kv_bytes,
@@ -371,8 +382,8 @@ def main():
                             "frac_of_peak": round((bytes_token + kv_bytes) / step_s / 1e9 / peak, 4),
                             "peak_GBps": peak, "peak_kind": peak_kind},
             "prefill": {"tokens": int(n_prefill), "s": round(t_prefill, 4),
-                        "tok_per_s": round(world * n_prefill / t_prefill, 1)},
-            "e2e": {"value": round(world * args.steps / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 8,
+                        "tok_per_s": round(streams * n_prefill / t_prefill, 1)},
+            "e2e": {"value": round(streams * args.steps / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 + 8,
                     "d2h_bytes_per_step": 4 * spec.vocab_size},
             "gpu_launches": launches * (args.steps + args.warmup) + 0,
             "clocks": clk.summary()}
@@ -391,8 +402,10 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     del ctx
+    del cache
     if dist:
         dist.barrier()
+        del tp
         dist.destroy_process_group()
 
 
