@@ -375,7 +375,9 @@ DevBuffer::~DevBuffer() {
 
 static DevBufferPtr alloc(size_t n) { return std::make_shared<DevBuffer>(n); }
 
-static bool device_quant(int q) { return q == JAL_Q4_0 || q == JAL_Q8_0; }
+// Quants of the device GEMV / GEMM path; Q5_0 runs in the Q8_0 layout.
+static bool device_quant(int q) { return q == JAL_Q4_0 || q == JAL_Q5_0 || q == JAL_Q8_0; }
+static int device_layout(int q) { return q == JAL_Q5_0 ? JAL_Q8_0 : q; }
 
 CachedMatrix repack_matrix(const uint8_t *raw_dev, int quant, uint64_t rows, uint64_t cols, cudaStream_t s) {
   std::vector<CachedMatrix> parts;
@@ -402,7 +404,7 @@ void repack_stacked(const std::vector<const uint8_t *> &raws, const std::vector<
     JAL_CUDA(cudaMemsetAsync(buf->ptr, 0, buf->bytes, s));
     storage.push_back(buf);
     stacked = DevMat{};
-    stacked.quant = quant; stacked.rows = (int64_t)total; stacked.cols = (int64_t)cols;
+    stacked.quant = device_layout(quant); stacked.rows = (int64_t)total; stacked.cols = (int64_t)cols;
     stacked.qs = buf->as<uint8_t>(); stacked.d = (const uint16_t *)(buf->as<uint8_t>() + nib);
     stacked.qs_stride = qs_stride; stacked.d_stride = d_stride;
     uint64_t r0 = 0;

@@ -63,6 +63,36 @@ __global__ void k_repack_q8_0(const uint8_t *__restrict__ raw, int64_t rows, int
   d[r * d_stride + g] = sanitize_f16(h[0]);
 }
 
+// Q5_0 (unpack_row_i8, repack_cache.rs:840-871): the 5-bit values become
+// int8 (q = (nibble | qh bit << 4) - 16), so a Q5_0 matrix takes the Q8_0
+// device layout and runs the Q8_0 kernels (the reference evaluates both as
+// int8 blocks with one scale per 32).
+__global__ void k_repack_q5_0(const uint8_t *__restrict__ raw, int64_t rows, int64_t nb, uint8_t *__restrict__ qs,
+                              uint16_t *__restrict__ d, int64_t qs_stride, int64_t d_stride) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * nb) return;
+  int64_t r = idx / nb, g = idx % nb;
+  const uint8_t *blk = raw + (r * nb + g) * 22;
+  const uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
+  uint32_t w[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+      const int e = 4 * k + b, j = e & 15;
+      const uint32_t nib = e < 16 ? (blk[6 + j] & 15u) : (uint32_t)(blk[6 + j] >> 4);
+      const uint32_t hb = ((qh >> (e < 16 ? j : j + 16)) & 1u) << 4;
+      word |= (uint32_t)(uint8_t)(int8_t)((int)(nib | hb) - 16) << (8 * b);
+    }
+    w[k] = word;
+  }
+  uint4 *dst = (uint4 *)(qs + r * qs_stride + g * 32);
+  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  d[r * d_stride + g] = sanitize_f16((uint16_t)(blk[0] | (blk[1] << 8)));
+}
+
 void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, uint8_t *qs, uint16_t *d,
                    int64_t qs_stride, int64_t d_stride, cudaStream_t s) {
   int64_t nb = cols / 32, n = rows * nb;
@@ -71,6 +101,8 @@ void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, ui
   int64_t blocks = (n + threads - 1) / threads;
   if (quant == JAL_Q4_0)
     k_repack_q4_0<<<(unsigned)blocks, threads, 0, s>>>(raw, rows, nb, qs, d, qs_stride, d_stride);
+  else if (quant == JAL_Q5_0)
+    k_repack_q5_0<<<(unsigned)blocks, threads, 0, s>>>(raw, rows, nb, qs, d, qs_stride, d_stride);
   else
     k_repack_q8_0<<<(unsigned)blocks, threads, 0, s>>>(raw, rows, nb, qs, d, qs_stride, d_stride);
 }

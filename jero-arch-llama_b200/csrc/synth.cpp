@@ -106,6 +106,30 @@ void quantize_q4_0_block(const float *x, uint8_t *out) {
   }
 }
 
+// GGML's Q5_0 reference quantizer: d = max / -16, q = min(31, (i8)(x/d + 16.5)),
+// low nibbles in qs, bit 4 of element j in bit j of qh.
+void quantize_q5_0_block(const float *x, uint8_t *out) {
+  float amax = 0.f, max = 0.f;
+  for (int j = 0; j < 32; j++) {
+    float v = x[j];
+    if (amax < std::fabs(v)) { amax = std::fabs(v); max = v; }
+  }
+  float d = max / -16.0f, id = d != 0.f ? 1.0f / d : 0.0f;
+  uint16_t dh = f32_to_f16_rne(d);
+  memcpy(out, &dh, 2);
+  uint32_t qh = 0;
+  for (int j = 0; j < 16; j++) {
+    float x0 = x[j] * id, x1 = x[16 + j] * id;
+    int xi0 = (int8_t)(x0 + 16.5f), xi1 = (int8_t)(x1 + 16.5f);
+    if (xi0 > 31) xi0 = 31;
+    if (xi1 > 31) xi1 = 31;
+    out[6 + j] = (uint8_t)((xi0 & 0x0F) | ((xi1 & 0x0F) << 4));
+    qh |= (uint32_t)((xi0 & 0x10) >> 4) << j;
+    qh |= (uint32_t)((xi1 & 0x10) >> 4) << (j + 16);
+  }
+  memcpy(out + 2, &qh, 4);
+}
+
 void quantize_q8_0_block(const float *x, uint8_t *out) {
   float amax = 0.f;
   for (int j = 0; j < 32; j++) amax = std::fmax(amax, std::fabs(x[j]));
@@ -119,7 +143,7 @@ void quantize_q8_0_block(const float *x, uint8_t *out) {
 void write_matrix(int quant, size_t rows, size_t cols, uint64_t key, float std_dev, uint8_t *out, int nthreads) {
   size_t rb = ggml_row_bytes((uint32_t)quant, cols);
   if (!rb) fail(JAL_ERR_TENSOR_BOUNDS, "synth: cols %zu incompatible with quant %d", cols, quant);
-  if (quant != JAL_Q4_0 && quant != JAL_Q8_0 && quant != JAL_F32 && quant != JAL_F16)
+  if (quant != JAL_Q4_0 && quant != JAL_Q5_0 && quant != JAL_Q8_0 && quant != JAL_F32 && quant != JAL_F16)
     fail(JAL_ERR_CAPABILITY_MISMATCH, "synth: unsupported quant %d", quant);
   if (cols % 2) fail(JAL_ERR_TENSOR_BOUNDS, "synth: odd cols");
   (void)nthreads;
@@ -139,10 +163,11 @@ void write_matrix(int quant, size_t rows, size_t cols, uint64_t key, float std_d
       }
       continue;
     }
-    size_t bb = quant == JAL_Q4_0 ? 18 : 34;
+    size_t bb = quant == JAL_Q4_0 ? 18 : quant == JAL_Q5_0 ? 22 : 34;
     for (size_t b = 0; b < cols / 32; b++) {
       gen_block(key, base + b * 32, 32, std_dev, buf);
       if (quant == JAL_Q4_0) quantize_q4_0_block(buf, row + b * bb);
+      else if (quant == JAL_Q5_0) quantize_q5_0_block(buf, row + b * bb);
       else quantize_q8_0_block(buf, row + b * bb);
     }
   }

@@ -50,6 +50,30 @@ def test_repack_bit_exact_and_gemv_op_sweep(jal, oracle, torch_cuda, quant_name,
     assert rel_err(y.cpu().numpy(), want) <= REL_TOL
 
 
+def test_q5_0_repack_bit_exact_and_projection(jal, oracle, torch_cuda):
+    # Q5_0 unpacks to int8 like Q8_0 (unpack_row_i8, repack_cache.rs:840-871)
+    # and runs the Q8_0 device layout: reference tiles and scales bit for
+    # bit, projections (M = 1 and 5) within REL_TOL.
+    torch = torch_cuda
+    rows, cols = 4096, 4096
+    raw = jal.synth_matrix(jal.Q5_0, rows, cols, seed=321, name="q5.sweep")
+    mat = jal.CachedMatrix.repack(raw, jal.Q5_0, rows, cols)
+    assert mat.quant() == jal.Q5_0
+    ref = oracle.RepackedWeight(raw, jal.Q5_0, rows, cols)
+    tiles, scales = mat.export_ref_layout()
+    assert np.array_equal(tiles, ref.tiles())
+    assert np.array_equal(scales.view(np.uint32), ref.scales().view(np.uint32))
+    for m in (1, 5):
+        x = jal.synth_normal(m * cols, seed=322 + m, name="q5.act")
+        y = torch.zeros(m * rows, dtype=torch.float32, device="cuda")
+        mat.gemm(dev(torch, x), m, y)
+        torch.cuda.synchronize()
+        want = ref.project_batch(x, m)
+        got = y.cpu().numpy().reshape(m, rows)
+        for t in range(m):
+            assert rel_err(got[t], want[t]) <= REL_TOL
+
+
 @pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
 def test_dot16_partials_exact(jal, oracle, torch_cuda, quant_name):
     torch = torch_cuda

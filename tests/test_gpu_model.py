@@ -154,6 +154,15 @@ def test_tiny_qwen2_neox_bias_q8_0(jal, oracle, torch_cuda):
     run_fast(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(9), 24, 256)
 
 
+def test_tiny_llama_q5_0_weights(jal, oracle, torch_cuda):
+    # Q5_0 layer weights and LM head (the Q8_0 device layout): reference
+    # numerics bit-for-bit order and the fast path's statistical bars.
+    spec = jal.SynthSpec(weight_quant=jal.Q5_0, head_quant=jal.Q5_0)
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=55)
+    run_parity(om, ctx, prompt_of(13), 16, 256)
+    run_fast(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(13), 16, 256)
+
+
 def test_llama4_irope_and_sliding_window(jal, oracle, torch_cuda):
     spec = jal.SynthSpec(architecture="llama4", num_layers=4)
     mask = [False, True, False, True]

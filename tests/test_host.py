@@ -53,6 +53,25 @@ def test_synth_weights_are_normal_0_02(jal, oracle):
     assert abs(float(x.std()) - 1.0) < 0.02 and abs(float(x.mean())) < 0.02
 
 
+def test_synth_q5_0_blocks_round_trip_within_half_a_step(jal, oracle):
+    # The Q5_0 quantizer (GGML's reference rounding) against the same stream
+    # generated as f32: dequantized values within half a quantization step
+    # |d| / 2 (plus the f16 rounding of d), except the values clamped at code
+    # 31 on the side opposite the block's extreme, which are within one step.
+    rows, cols = 64, 1024
+    raw = jal.synth_matrix(jal.Q5_0, rows, cols, seed=12, name="q5")
+    f32 = jal.synth_matrix(jal.F32, rows, cols, seed=12, name="q5").view(np.float32).reshape(-1, 32)
+    blocks = raw.reshape(-1, 22)
+    for b in range(blocks.shape[0]):
+        deq = oracle.dequantize_block(jal.Q5_0, blocks[b])
+        d = abs(float(oracle.f16_to_f32_finite(int(blocks[b, 0]) | (int(blocks[b, 1]) << 8))))
+        err = np.abs(deq - f32[b])
+        slack = 1e-3 * float(np.max(np.abs(f32[b]))) + 1e-7
+        clamped = deq == np.float32(15.0 * -np.sign(f32[b][np.argmax(np.abs(f32[b]))]) * d)
+        assert np.all(err[~clamped] <= 0.5 * d + slack)
+        assert np.all(err[clamped] <= d + slack)
+
+
 def test_f16_rounding_is_nearest_even(jal):
     for v in [1.0, 0.5, 1e-3, 65504.0, 7e-8, 3.0517578125e-05, 1.0009765625, 1.00048828125, -2.5]:
         want = int(np.array([v], dtype=np.float32).astype(np.float16).view(np.uint16)[0])
