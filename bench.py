@@ -28,7 +28,7 @@ import time
 REPO = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.join(REPO, "jero-arch-llama_b200")
 METRIC = "Q4_0 decode tok/s (bs=1) + quant-GEMV HBM GB/s vs peak; prefill tok/s"
-SWEEP = [(4096, 4096), (11008, 4096), (4096, 11008), (14336, 4096)]
+SWEEP = [(4096, 4096), (11008, 4096), (4096, 11008), (14336, 4096), (128256, 4096)]
 L2_BYTES = 126 * 1024 * 1024
 SEED = 20251201
 

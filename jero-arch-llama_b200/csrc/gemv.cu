@@ -348,8 +348,11 @@ int w4_warps() {
 int64_t g_w4_pf = -1;
 int64_t w4_prefetch_bytes() {
   if (g_w4_pf < 0) {
+    // Default 0: register loads before the wait.  Llama-3-8B Q4_0 decode
+    // at position 2048: 1.81 ms per step, against 1.88 ms with a 64 KB L2
+    // prefetch per CTA instead.
     const char *e = getenv("JAL_W4_PF_KB");
-    g_w4_pf = e ? (int64_t)atoll(e) * 1024 : 64 * 1024;
+    g_w4_pf = e ? (int64_t)atoll(e) * 1024 : 0;
   }
   return g_w4_pf;
 }

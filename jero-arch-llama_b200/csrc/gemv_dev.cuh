@@ -395,6 +395,32 @@ __device__ __forceinline__ float w4_dot(const W4Row<QUANT> &r, const W4Act &x) {
   return acc;
 }
 
+// Row segment of one weight row in shared memory (same layout as in HBM:
+// quants, then the f16 scales): blocks bq[v] = seg * 128 + lane + 32 v, v < 4.
+// Blocks past the row end (ragged last segment) read block 0 and are zeroed
+// by mask bit v, without branches.
+template <int QUANT>
+__device__ __forceinline__ void w4s_load(const char *row, int nb, const int (&bq)[4], unsigned vmask,
+                                         W4Row<QUANT> &r) {
+  constexpr int BQ = QUANT == JAL_Q4_0 ? 16 : 32;  // quant bytes per block
+  const uint16_t *d = (const uint16_t *)(row + (size_t)nb * BQ);
+  uint32_t h[4];
+#pragma unroll
+  for (int v = 0; v < 4; v++) {
+    const bool ok = (vmask >> v) & 1u;
+    const uint4 q0 = *(const uint4 *)(row + (size_t)bq[v] * BQ);
+    r.q[(BQ / 4) * v + 0] = ok ? q0.x : 0u; r.q[(BQ / 4) * v + 1] = ok ? q0.y : 0u;
+    r.q[(BQ / 4) * v + 2] = ok ? q0.z : 0u; r.q[(BQ / 4) * v + 3] = ok ? q0.w : 0u;
+    if (BQ == 32) {
+      const uint4 q1 = *(const uint4 *)(row + (size_t)bq[v] * BQ + 16);
+      r.q[(BQ / 4) * v + 4] = ok ? q1.x : 0u; r.q[(BQ / 4) * v + 5] = ok ? q1.y : 0u;
+      r.q[(BQ / 4) * v + 6] = ok ? q1.z : 0u; r.q[(BQ / 4) * v + 7] = ok ? q1.w : 0u;
+    }
+    h[v] = ok ? (uint32_t)d[bq[v]] : 0u;
+  }
+  r.d = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+}
+
 __host__ __device__ inline int seg_count(int64_t cols) { return (int)((cols / 32 + kSegBlocks - 1) / kSegBlocks); }
 // Activation area of the segmented path: blocks padded to nseg * 128 (the
 // padding zero), then the norm weights for RMSNorm inputs.
