@@ -344,6 +344,13 @@ int jal_context_logits_device(const jal_context *ctx, const float **out);
 /* Number of kernels one decode step launches (graph nodes when graphs are
  * on). */
 int jal_context_last_step_launches(const jal_context *ctx, size_t *out);
+/* How the decode step of a tensor-parallel context combines the ranks'
+ * partial sums: JAL_TP_EXCHANGE_NONE (one rank), JAL_TP_EXCHANGE_NCCL
+ * (all-reduce after O and down) or JAL_TP_EXCHANGE_PEER (the O / down GEMVs
+ * store into every rank's slots over peer memory and the next RMSNorm GEMV
+ * adds them; set JAL_TP_NCCL=1 in the environment to force NCCL). */
+enum { JAL_TP_EXCHANGE_NONE = 0, JAL_TP_EXCHANGE_NCCL = 1, JAL_TP_EXCHANGE_PEER = 2 };
+int jal_context_tp_exchange(const jal_context *ctx, int *out);
 /* Issue the context's work on `stream` (a cudaStream_t; NULL restores the
  * context's own stream).  Lets callers order it with their own work and
  * time it with events recorded on the same stream. */

@@ -181,6 +181,7 @@ _SIGS = {
     "jal_context_export_kv": (C.c_int, [_P, _SZ, _P, _SZ]),
     "jal_context_logits_device": (C.c_int, [_P, C.POINTER(_P)]),
     "jal_context_last_step_launches": (C.c_int, [_P, C.POINTER(_SZ)]),
+    "jal_context_tp_exchange": (C.c_int, [_P, C.POINTER(C.c_int)]),
     "jal_context_set_stream": (C.c_int, [_P, _P]),
     "jal_synth_gguf_size": (C.c_int, [C.POINTER(SynthConfig), C.POINTER(_SZ)]),
     "jal_synth_gguf_write": (C.c_int, [C.POINTER(SynthConfig), C.c_uint64, _P, _SZ, C.c_int]),
@@ -623,6 +624,13 @@ class ExecutionContext:
         n = _SZ()
         _check(lib().jal_context_last_step_launches(self._h, C.byref(n)))
         return n.value
+
+    def tp_exchange(self) -> str:
+        """'none' (one rank), 'nccl' (all-reduce) or 'peer' (partial sums
+        exchanged over peer memory inside the GEMVs) for the decode step."""
+        v = C.c_int()
+        _check(lib().jal_context_tp_exchange(self._h, C.byref(v)))
+        return {0: "none", 1: "nccl", 2: "peer"}[v.value]
 
 
 # ---- synthetic GGUF models (include/jal_synth.h) -----------------------------

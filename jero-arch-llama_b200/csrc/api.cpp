@@ -519,7 +519,9 @@ int jal_context_reset(jal_context *ctx) {
 
 // Reads the context's device error word after a synchronised step: bit 1 =
 // an embedding lookup saw an out-of-range token, bit 2 = a bounded wait for
-// a KV copy in decode attention gave up.  The word is cleared afterwards.
+// a KV copy in decode attention gave up, bit 8 = a persistent-step grid
+// barrier wait gave up, bit 16 = a tensor-parallel exchange wait gave up.
+// The word is cleared afterwards.
 static void enqueue_error_read(Context &c) {
   JAL_CUDA(cudaMemcpyAsync(&c.h_token[4], c.d_err, 4, cudaMemcpyDeviceToHost, c.stream));
 }
@@ -537,6 +539,7 @@ static void check_device_error(Context &c) {
   }
   JAL_CUDA(cudaStreamSynchronize(c.stream));
   if (e & 8u) fail(JAL_ERR_TIMEOUT, "persistent decode step: a bounded grid barrier wait gave up");
+  if (e & 16u) fail(JAL_ERR_TIMEOUT, "tensor-parallel decode step: a bounded wait for the peers' partial sums gave up");
   if (e & 2u) fail(JAL_ERR_TIMEOUT, "decode step: a bounded wait for KV-tile or weight copies gave up");
   fail(JAL_ERR_TENSOR_BOUNDS, "embedding lookup saw an out-of-range token id");
 }
@@ -679,6 +682,15 @@ int jal_context_last_step_launches(const jal_context *h, size_t *out) {
     NEED(h);
     NEED(out);
     *out = h->ctx->launches_per_step;
+  });
+}
+
+int jal_context_tp_exchange(const jal_context *h, int *out) {
+  return guard([&] {
+    NEED(h);
+    NEED(out);
+    const Context &c = *h->ctx;
+    *out = c.cache->plan.world <= 1 ? JAL_TP_EXCHANGE_NONE : c.tp_sym ? JAL_TP_EXCHANGE_PEER : JAL_TP_EXCHANGE_NCCL;
   });
 }
 

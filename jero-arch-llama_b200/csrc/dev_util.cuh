@@ -167,6 +167,37 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 __device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Cross-GPU signalling over peer memory (tensor-parallel exchange).
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits until *cnt reaches the next multiple of per_step at or above its
+// first value (signals of one exchange step; a peer is never a whole step
+// ahead on the same counter).  Gives up after kPeerWaitNs and returns false.
+constexpr uint64_t kPeerWaitNs = 4000000000ull;
+__device__ __forceinline__ bool peer_wait_step(const unsigned long long *cnt, unsigned long long per_step) {
+  unsigned long long c = ld_acquire_sys(cnt);
+  unsigned long long target = (c + per_step - 1) / per_step * per_step;
+  if (target == 0) target = per_step;
+  if (c >= target) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_sys(cnt) >= target) return true;
+    if (global_ns() - t0 > kPeerWaitNs) return false;
+  }
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

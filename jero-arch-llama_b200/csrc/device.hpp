@@ -34,7 +34,11 @@ inline int64_t d_stride_for(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
 // block-quantized as (row x norm weights) with the producers' partial sums of
 // squares of the row; the norm scale is folded into the block scales.
 enum GemvIn : int { GEMV_IN_Q8 = 0, GEMV_IN_F32 = 1, GEMV_IN_NORM = 2, GEMV_IN_PREQ = 3 };
-enum GemvOut : int { GEMV_OUT_STORE = 0, GEMV_OUT_ADD = 1, GEMV_OUT_SWIGLU = 2 };
+// GEMV_OUT_PEER (tensor-parallel decode): each row value goes to every
+// rank's partial-sum slot over peer memory, then each CTA signals every rank.
+enum GemvOut : int { GEMV_OUT_STORE = 0, GEMV_OUT_ADD = 1, GEMV_OUT_SWIGLU = 2, GEMV_OUT_PEER = 3 };
+constexpr int kPeerMax = 8;
+constexpr int kErrPeerWait = 16;  // bit set in the context error word
 constexpr int kGemvMaxM = 8;
 constexpr int kGemvMaxSmem = 200 * 1024;
 
@@ -66,12 +70,31 @@ struct GemvArgs {
   float *nx_u = nullptr, *nx_s = nullptr, *nx_ss = nullptr;
   int8_t *nx_q = nullptr;
   unsigned *nx_cnt = nullptr;
+  // Tensor-parallel exchange over peer memory (decode, M = 1, IN_NORM).
+  // With peer_in set the prologue first waits until *peer_cnt reaches the
+  // next multiple of peer_per_step (bounded: kErrPeerWait in *err), then
+  // takes the row as x + peer_in[0 .. x_stride) + peer_in[x_stride ..) + ...
+  // (peer_world slices, added in rank order, so every rank gets the same
+  // bits) and CTA 0 stores that sum to x_out.
+  const float *peer_in = nullptr;
+  const unsigned long long *peer_cnt = nullptr;
+  unsigned long long peer_per_step = 0;
+  float *x_out = nullptr;
+  int *err = nullptr;
+  // GEMV_OUT_PEER: row value (+ bias) to peer_out[r][row] for r < peer_world;
+  // then every CTA adds 1 to *peer_sig[r] (release, system scope).
+  int peer_world = 0;
+  float *peer_out[kPeerMax] = {};
+  unsigned long long *peer_sig[kPeerMax] = {};
   int grid = 0;                 // CTAs (0 = auto)
   int pdl = 0;                  // launch with programmatic dependent launch
   int64_t pf_bytes = -1;        // L2 prefetch budget per CTA (-1 = default)
 };
 
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
+// True when launch_gemv runs `a` (with peer_in or GEMV_OUT_PEER) on the
+// segmented kernel whose prologue / epilogue implement the exchange.
+bool gemv_peer_supported(const GemvArgs &a);
 int gemv_default_grid(const GemvArgs &a);
 // Sets the kernels' shared-memory limits (call before any stream capture).
 void gemv_init();

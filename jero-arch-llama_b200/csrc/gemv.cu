@@ -31,6 +31,7 @@
 
 #include <cstdlib>
 
+#include "common.hpp"
 #include "dev_util.cuh"
 #include "device.hpp"
 #include "gemv_dev.cuh"
@@ -241,8 +242,12 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv(const GemvArgs 
 // kernel.  A segment costs the loads, 4 block dots and one warp reduction;
 // DEPTH segments are in flight per warp.  With nseg > 1 the per-segment sums
 // of a row are added in segment order at the end of the kernel.
-template <int QUANT, int OUT, int WARPS, int DEPTH>
+// OUTX = output mode | kPeerIn when the input is the tensor-parallel exchange.
+constexpr int kPeerIn = 4;
+template <int QUANT, int OUTX, int WARPS, int DEPTH>
 __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvArgs a) {
+  constexpr int OUT = OUTX & 3;
+  constexpr bool PEER_IN = (OUTX & kPeerIn) != 0;
   extern __shared__ __align__(16) char smem[];
   __shared__ float red[33];
   constexpr int UNITS = OUT == GEMV_OUT_SWIGLU ? 2 : 1;
@@ -287,7 +292,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvAr
     for (int j = 0; j < DEPTH; j++)
       if (j < total) w4_load<QUANT>(a.w, unit_row(j), seg, nb, lane, buf[j]);
   }
-  gemv_prologue_m1<WARPS>(a, smem, nb, nbp, red);
+  gemv_prologue_m1<WARPS, PEER_IN>(a, smem, nb, nbp, red);
   W4Act x;
 #pragma unroll
   for (int v = 0; v < 4; v++) {
@@ -316,7 +321,10 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvAr
         } else if (lane == 0) {
           const int64_t lr = r0 + li;
           float *yp = a.y + lr;
-          if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
+          if (OUT == GEMV_OUT_PEER) {
+            const float v = a.bias ? s + a.bias[lr] : s;
+            for (int r = 0; r < a.peer_world; r++) a.peer_out[r][lr] = v;
+          } else if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
           else if (OUT == GEMV_OUT_ADD) *yp = *yp + (a.bias ? s + a.bias[lr] : s);
           else *yp = swiglu_one(gate, s);
         }
@@ -330,8 +338,18 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvAr
       for (int q = 0; q < nseg; q++) s += part[li * nseg + q];
       const int64_t lr = r0 + li;
       float *yp = a.y + lr;
-      if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
+      if (OUT == GEMV_OUT_PEER) {
+        const float v = a.bias ? s + a.bias[lr] : s;
+        for (int r = 0; r < a.peer_world; r++) a.peer_out[r][lr] = v;
+      } else if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
       else *yp = *yp + (a.bias ? s + a.bias[lr] : s);
+    }
+  }
+  if (OUT == GEMV_OUT_PEER) {  // this CTA's rows are out: signal every rank
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int r = 0; r < a.peer_world; r++) red_release_sys_add(a.peer_sig[r], 1ull);
     }
   }
 }
@@ -517,6 +535,12 @@ void gemv_init() {
   set_w4_attrs<JAL_Q8_0, GEMV_OUT_STORE>();
   set_w4_attrs<JAL_Q8_0, GEMV_OUT_ADD>();
   set_w4_attrs<JAL_Q8_0, GEMV_OUT_SWIGLU>();
+  set_w4_attrs<JAL_Q4_0, GEMV_OUT_PEER>();
+  set_w4_attrs<JAL_Q8_0, GEMV_OUT_PEER>();
+  set_w4_attrs<JAL_Q4_0, GEMV_OUT_STORE | kPeerIn>();
+  set_w4_attrs<JAL_Q4_0, GEMV_OUT_SWIGLU | kPeerIn>();
+  set_w4_attrs<JAL_Q8_0, GEMV_OUT_STORE | kPeerIn>();
+  set_w4_attrs<JAL_Q8_0, GEMV_OUT_SWIGLU | kPeerIn>();
   done = true;
 }
 
@@ -538,6 +562,26 @@ int gemv_default_grid(const GemvArgs &a) {
   return (int)(need < cap ? need : cap);
 }
 
+bool gemv_peer_supported(const GemvArgs &a) {
+  if (a.m != 1 || a.peer_world < 1 || a.peer_world > kPeerMax) return false;
+  if (a.w.quant != JAL_Q4_0 && a.w.quant != JAL_Q8_0) return false;
+  // the exchange lives in the one-round-trip RMSNorm prologue (rows up to
+  // 1024 jobs of 8 elements) and in the segmented kernel's epilogue
+  if (a.peer_in && (a.in_mode != GEMV_IN_NORM || a.w.cols > 8192 || !a.peer_cnt || a.peer_per_step == 0))
+    return false;
+  if (a.out_mode == GEMV_OUT_PEER)
+    for (int r = 0; r < a.peer_world; r++)
+      if (!a.peer_out[r] || !a.peer_sig[r]) return false;
+  int grid = a.grid;
+  if (grid <= 0) {
+    int sms = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    grid = (int)(a.rows < sms ? a.rows : sms);
+  }
+  return w4_fits(a, grid);
+}
+
 void launch_gemv(const GemvArgs &a0, cudaStream_t s) {
   if (a0.rows <= 0) return;
   gemv_init();
@@ -552,15 +596,31 @@ void launch_gemv(const GemvArgs &a0, cudaStream_t s) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     w4_grid = (int)(a.rows < sms ? a.rows : sms);
   }
-  if (use_w4() && w4_fits(a, w4_grid)) {
+  const bool peer = a.peer_in != nullptr || a.out_mode == GEMV_OUT_PEER;
+  if (peer && !gemv_peer_supported(a))
+    fail(JAL_ERR_CAPABILITY_MISMATCH, "tensor-parallel exchange: GEMV shape not on the segmented kernel");
+  if ((use_w4() || peer) && w4_fits(a, w4_grid)) {
     const int grid = w4_grid;
-    if (a.w.quant == JAL_Q4_0) {
+    if (a.peer_in) {  // exchange input: RMSNorm rows into STORE (QKV, LM head) or SWIGLU (gate / up)
+      if (a.out_mode != GEMV_OUT_STORE && a.out_mode != GEMV_OUT_SWIGLU)
+        fail(JAL_ERR_CAPABILITY_MISMATCH, "tensor-parallel exchange input with output mode %d", a.out_mode);
+      const bool sw = a.out_mode == GEMV_OUT_SWIGLU;
+      if (a.w.quant == JAL_Q4_0) {
+        if (sw) launch_w4_t<JAL_Q4_0, GEMV_OUT_SWIGLU | kPeerIn>(a, grid, s);
+        else launch_w4_t<JAL_Q4_0, GEMV_OUT_STORE | kPeerIn>(a, grid, s);
+      } else {
+        if (sw) launch_w4_t<JAL_Q8_0, GEMV_OUT_SWIGLU | kPeerIn>(a, grid, s);
+        else launch_w4_t<JAL_Q8_0, GEMV_OUT_STORE | kPeerIn>(a, grid, s);
+      }
+    } else if (a.w.quant == JAL_Q4_0) {
       if (a.out_mode == GEMV_OUT_STORE) launch_w4_t<JAL_Q4_0, GEMV_OUT_STORE>(a, grid, s);
       else if (a.out_mode == GEMV_OUT_ADD) launch_w4_t<JAL_Q4_0, GEMV_OUT_ADD>(a, grid, s);
+      else if (a.out_mode == GEMV_OUT_PEER) launch_w4_t<JAL_Q4_0, GEMV_OUT_PEER>(a, grid, s);
       else launch_w4_t<JAL_Q4_0, GEMV_OUT_SWIGLU>(a, grid, s);
     } else {
       if (a.out_mode == GEMV_OUT_STORE) launch_w4_t<JAL_Q8_0, GEMV_OUT_STORE>(a, grid, s);
       else if (a.out_mode == GEMV_OUT_ADD) launch_w4_t<JAL_Q8_0, GEMV_OUT_ADD>(a, grid, s);
+      else if (a.out_mode == GEMV_OUT_PEER) launch_w4_t<JAL_Q8_0, GEMV_OUT_PEER>(a, grid, s);
       else launch_w4_t<JAL_Q8_0, GEMV_OUT_SWIGLU>(a, grid, s);
     }
     return;

@@ -208,7 +208,7 @@ __device__ void gemv_prologue_pre(const GemvArgs &a, char *smem, int nb, int nbp
 // (and their norm weights) into registers at once, so the prologue costs one
 // memory round trip plus the norm reduction.  Same quantization as
 // gemv_prologue; padding blocks [nb, nbp) are zeroed.
-template <int WARPS, int JMAX, bool NORM>
+template <int WARPS, int JMAX, bool NORM, bool PEER = false>
 __device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, int nb, int nbp, float *red) {
   constexpr int T = WARPS * 32;
   const int tid = threadIdx.x, jobs = nb * 4;
@@ -216,6 +216,13 @@ __device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, 
     ((uint4 *)smem)[b] = make_uint4(0, 0, 0, 0);
     ((uint4 *)(smem + nbp * 16))[b] = make_uint4(0, 0, 0, 0);
     put_scale_sum(smem, nbp, b, 0.0f, 0);
+  }
+  // Tensor-parallel exchange: wait for every rank's partial sums of this
+  // step (one thread polls; the CTA barrier orders the loads after it).
+  constexpr bool peer = NORM && PEER;
+  if (peer) {
+    if (tid == 0 && !peer_wait_step(a.peer_cnt, a.peer_per_step) && a.err) atomicOr(a.err, kErrPeerWait);
+    __syncthreads();
   }
   float v[JMAX][8], w[NORM ? JMAX : 1][8];
 #pragma unroll
@@ -226,6 +233,21 @@ __device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, 
       const float4 x0 = xp[0], x1 = xp[1];
       v[j][0] = x0.x; v[j][1] = x0.y; v[j][2] = x0.z; v[j][3] = x0.w;
       v[j][4] = x1.x; v[j][5] = x1.y; v[j][6] = x1.z; v[j][7] = x1.w;
+      if (peer) {  // residual + partials in rank order; written by peers, so read through L2
+        for (int r = 0; r < a.peer_world; r++) {
+          const float4 *pp = (const float4 *)(a.peer_in + (size_t)r * a.x_stride + i * 8);
+          const float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
+          v[j][0] = __fadd_rn(v[j][0], p0.x); v[j][1] = __fadd_rn(v[j][1], p0.y);
+          v[j][2] = __fadd_rn(v[j][2], p0.z); v[j][3] = __fadd_rn(v[j][3], p0.w);
+          v[j][4] = __fadd_rn(v[j][4], p1.x); v[j][5] = __fadd_rn(v[j][5], p1.y);
+          v[j][6] = __fadd_rn(v[j][6], p1.z); v[j][7] = __fadd_rn(v[j][7], p1.w);
+        }
+        if (blockIdx.x == 0 && a.x_out) {
+          float4 *op = (float4 *)(a.x_out + i * 8);
+          op[0] = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+          op[1] = make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+        }
+      }
       if (NORM) {
         const float4 *wp = (const float4 *)(a.norm_w + i * 8);
         const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
@@ -292,10 +314,14 @@ __device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, 
 // M = 1 prologue: the one-round-trip form when the row fits (RMSNorm rows up
 // to 8192 elements, f32 rows up to 16384), else gemv_prologue.  Q8 inputs
 // are already one round trip in gemv_prologue.
-template <int WARPS>
+// PEER: the tensor-parallel exchange input (RMSNorm rows only; the host
+// checks the shape).
+template <int WARPS, bool PEER = false>
 __device__ __forceinline__ void gemv_prologue_m1(const GemvArgs &a, char *smem, int nb, int nbp, float *red) {
   constexpr int T = WARPS * 32, JN = 1024 / T, JF = 2048 / T;
-  if (a.in_mode == GEMV_IN_NORM && nb * 4 <= JN * T) {
+  if (PEER) {
+    prologue_m1_impl<WARPS, JN, true, true>(a, smem, nb, nbp, red);
+  } else if (a.in_mode == GEMV_IN_NORM && nb * 4 <= JN * T) {
     prologue_m1_impl<WARPS, JN, true>(a, smem, nb, nbp, red);
   } else if (a.in_mode == GEMV_IN_F32 && nb * 4 <= JF * T) {
     prologue_m1_impl<WARPS, JF, false>(a, smem, nb, nbp, red);

@@ -876,6 +876,8 @@ static void setup_mega(Context &ctx, int sms) {
   ctx.mega_grid = sms;
 }
 
+static void setup_tp_exchange(Context &ctx, int sms);
+
 std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, const ContextConfig &cfg0) {
   JAL_CUDA(cudaSetDevice(c.device));
   auto ctx = std::make_unique<Context>();
@@ -947,7 +949,7 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->am_blocks = sms;
   size_t f32s = H + (Q + 2 * KV) + Q + Q / 32 + F + (F + 31) / 32 + V + sms;
   size_t bytes = f32s * 4 + Q + ((F + 31) / 32) * 32 + 4096 + (F / 32 + 1) * 4 + 64 + (size_t)sms * 4 + (n_ctx + 2) * 4 +
-                 32 * 256 + c.plan.v_pad * 4 + 256;
+                 32 * 256 + c.plan.v_pad * 4 + H * 4 + 512;
   auto db = alloc(bytes + 1024);
   ctx->bufs.push_back(db);
   JAL_CUDA(cudaMemset(db->ptr, 0, db->bytes));
@@ -971,7 +973,9 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->am_idx = (int *)take(sms * 4);
   ctx->am_cnt = (unsigned *)take(4);
   ctx->d_hist = (uint32_t *)take((n_ctx + 2) * 4);
+  ctx->hidden_b = (float *)take(H * 4);
   if ((size_t)(p - db->as<char>()) > db->bytes) fail(JAL_ERR_INVALID_ARGUMENT, "internal: decode scratch layout overflow");
+  if (c.tp && c.plan.world > 1) setup_tp_exchange(*ctx, sms);
   {  // reference-order scratch: normed row, int8 activations + scales, gate|up, q
     const uint64_t kmax = std::max<uint64_t>(std::max<uint64_t>(H, Q), F), kp = (kmax + 31) / 32 * 32;
     auto sb = alloc((H + kp / 32 + 2 * F + Q) * 4 + kp + 5 * 256);
@@ -989,6 +993,50 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   JAL_CUDA(cudaMallocHost(&ctx->h_token, 4 * 8));
   JAL_CUDA(cudaStreamSynchronize(ctx->stream));
   return ctx;
+}
+
+// Tensor-parallel exchange over peer memory for the decode step: a
+// symmetric allocation (counters, partial slots) mapped on every rank.
+// Collective over the ranks; on any mismatch (SM counts, a shape off the
+// segmented GEMV, no peer mapping) every rank keeps the NCCL all-reduce.
+static void setup_tp_exchange(Context &ctx, int sms) {
+  const ModelCache &c = *ctx.cache;
+  const int W = c.plan.world;
+  const uint64_t H = ctx.g.hidden_dim;
+  const size_t L = c.layers.size();
+  ctx.tp_cnt_bytes = (2 * L * 8 + 255) / 256 * 256;
+  // every rank must launch the producers with the same grid
+  ctx.tp_grid = (int)std::min<uint64_t>(H, (uint64_t)sms);
+  float g = (float)ctx.tp_grid;
+  JAL_CUDA(cudaMemcpyAsync(ctx.am_val, &g, 4, cudaMemcpyHostToDevice, ctx.stream));
+  tp_all_reduce(*c.tp, ctx.am_val, 1, ctx.stream);
+  float gsum = 0.0f;
+  JAL_CUDA(cudaMemcpyAsync(&gsum, ctx.am_val, 4, cudaMemcpyDeviceToHost, ctx.stream));
+  JAL_CUDA(cudaStreamSynchronize(ctx.stream));
+  // shapes are the same on every rank, so every rank decides alike
+  bool ok = gsum == g * (float)W && W <= kPeerMax && !env_flag("JAL_TP_NCCL");
+  if (ok && !c.layers.empty()) {
+    const Layer &L0 = c.layers[0];
+    float *dummy = ctx.hidden_b;
+    unsigned long long *dcnt = (unsigned long long *)ctx.hidden_b;
+    GemvArgs pa;  // producer (O / down)
+    pa.m = 1; pa.out_mode = GEMV_OUT_PEER; pa.peer_world = W; pa.grid = ctx.tp_grid; pa.rows = (int64_t)H;
+    for (int r = 0; r < W; r++) { pa.peer_out[r] = dummy; pa.peer_sig[r] = dcnt; }
+    GemvArgs po = pa, pd = pa;
+    po.w = L0.wo.dm; po.in_mode = GEMV_IN_Q8;
+    pd.w = L0.wdown.dm; pd.in_mode = GEMV_IN_F32;
+    GemvArgs ca;  // consumers (QKV, gate / up, LM head)
+    ca.m = 1; ca.in_mode = GEMV_IN_NORM; ca.peer_in = dummy; ca.peer_cnt = dcnt; ca.peer_per_step = 1;
+    ca.peer_world = W;
+    GemvArgs cq = ca, cg = ca, cl = ca;
+    cq.w = L0.qkv; cq.rows = L0.qkv.rows; cq.out_mode = GEMV_OUT_STORE;
+    cg.w = L0.gateup; cg.rows = (int64_t)ctx.g.ffn_dim; cg.out_mode = GEMV_OUT_SWIGLU; cg.up_offset = (int64_t)ctx.g.ffn_dim;
+    cl.w = c.lm_head.dm; cl.rows = (int64_t)c.plan.v_n; cl.out_mode = GEMV_OUT_STORE;
+    ok = gemv_peer_supported(po) && gemv_peer_supported(pd) && gemv_peer_supported(cq) && gemv_peer_supported(cg) &&
+         gemv_peer_supported(cl);
+  }
+  if (!ok) return;
+  ctx.tp_sym.reset(tp_symmetric_alloc(*c.tp, ctx.tp_cnt_bytes + 2 * (size_t)W * H * 4, ctx.stream));
 }
 
 size_t decode_scratch_bytes(const Recipe &r, uint64_t seq) {  // recipe.rs:529-547 (device buffers)
@@ -1016,12 +1064,39 @@ void Context::enqueue_decode_step(bool pdl) {
   launch_embed(c.emb_raw->as<uint8_t>(), c.emb_quant, (int64_t)H, (int64_t)c.emb_rows, d_token, 1, hidden, d_err, pdl,
                stream);
   n++;
+  // Tensor parallelism over peer memory: O and down (phases 2l, 2l + 1)
+  // store their partial rows into every rank's slot of parity phase % 2 and
+  // signal that phase's counter; the next RMSNorm GEMV waits, adds the
+  // partials to the residual it reads (hidden for even phases, hidden_b for
+  // odd ones) and writes the sum to the other buffer.
+  const bool xp = tp_sym != nullptr;
+  const int W = c.plan.world, rank = c.plan.rank;
+  auto x_counter = [&](int r, size_t phase) {
+    return (unsigned long long *)tp_sym->peer[r] + phase;
+  };
+  auto x_slots = [&](int r, size_t parity) {  // rank r's slots [world][H] of this parity
+    return (float *)((char *)tp_sym->peer[r] + tp_cnt_bytes) + parity * (size_t)W * H;
+  };
+  auto produce = [&](GemvArgs &a, size_t phase) {
+    a.out_mode = GEMV_OUT_PEER; a.y = nullptr; a.peer_world = W; a.grid = tp_grid;
+    for (int r = 0; r < W; r++) {
+      a.peer_out[r] = x_slots(r, phase % 2) + (size_t)rank * H;
+      a.peer_sig[r] = x_counter(r, phase);
+    }
+  };
+  auto consume = [&](GemvArgs &a, size_t phase) {
+    a.peer_in = x_slots(rank, phase % 2); a.peer_cnt = x_counter(rank, phase);
+    a.peer_per_step = (unsigned long long)W * (unsigned long long)tp_grid; a.peer_world = W; a.err = d_err;
+    a.x = phase % 2 ? hidden_b : hidden;
+    a.x_out = phase % 2 ? hidden : hidden_b;
+  };
   for (size_t l = 0; l < c.layers.size(); l++) {
     const Layer &L = c.layers[l];
     GemvArgs qa;
     qa.w = L.qkv; qa.rows = (int64_t)(Q + 2 * KV); qa.m = 1; qa.in_mode = GEMV_IN_NORM;
     qa.x = hidden; qa.x_stride = (int64_t)H; qa.norm_w = L.attn_norm; qa.eps = eps;
     qa.out_mode = GEMV_OUT_STORE; qa.y = qkv; qa.y_stride = (int64_t)(Q + 2 * KV); qa.pdl = pdl;
+    if (xp && l > 0) consume(qa, 2 * l - 1);
     launch_gemv(qa, stream);
     AttnDecodeArgs aa;
     aa.qkv = qkv; aa.bq = L.bq; aa.bk = L.bk; aa.bv = L.bv;
@@ -1042,26 +1117,33 @@ void Context::enqueue_decode_step(bool pdl) {
     // store theirs, and the all-reduce sums them into the new residual
     oa.out_mode = c.plan.rank == 0 ? GEMV_OUT_ADD : GEMV_OUT_STORE; oa.y = hidden; oa.y_stride = (int64_t)H;
     oa.bias = L.bo; oa.pdl = pdl;
+    if (xp) produce(oa, 2 * l);
     launch_gemv(oa, stream);
-    if (c.tp) tp_all_reduce(*c.tp, hidden, H, stream);
+    if (c.tp && !xp) tp_all_reduce(*c.tp, hidden, H, stream);
     GemvArgs ga;
     ga.w = L.gateup; ga.rows = (int64_t)F; ga.m = 1; ga.in_mode = GEMV_IN_NORM;
     ga.x = hidden; ga.x_stride = (int64_t)H; ga.norm_w = L.ffn_norm; ga.eps = eps;
     ga.out_mode = GEMV_OUT_SWIGLU; ga.y = ffn; ga.y_stride = (int64_t)F; ga.up_offset = (int64_t)F; ga.pdl = pdl;
+    if (xp) consume(ga, 2 * l);
     launch_gemv(ga, stream);
     GemvArgs da;
     da.w = L.wdown.dm; da.rows = (int64_t)H; da.m = 1; da.in_mode = GEMV_IN_F32;
     da.x = ffn; da.x_stride = (int64_t)F;
     da.out_mode = c.plan.rank == 0 ? GEMV_OUT_ADD : GEMV_OUT_STORE; da.y = hidden; da.y_stride = (int64_t)H;
     da.pdl = pdl;
+    if (xp) produce(da, 2 * l + 1);
     launch_gemv(da, stream);
-    if (c.tp) tp_all_reduce(*c.tp, hidden, H, stream);
+    if (c.tp && !xp) tp_all_reduce(*c.tp, hidden, H, stream);
     n += 5;
   }
   GemvArgs la;
   la.w = c.lm_head.dm; la.rows = (int64_t)c.plan.v_n; la.m = 1; la.in_mode = GEMV_IN_NORM;
   la.x = hidden; la.x_stride = (int64_t)H; la.norm_w = c.output_norm->as<float>(); la.eps = eps;
   la.out_mode = GEMV_OUT_STORE; la.y = logits_local; la.y_stride = (int64_t)c.plan.v_pad; la.pdl = pdl;
+  if (xp && !c.layers.empty()) {
+    consume(la, 2 * c.layers.size() - 1);
+    la.x_out = nullptr;  // the residual after the last layer is not needed again
+  }
   launch_gemv(la, stream);
   if (c.tp) tp_all_gather(*c.tp, logits_local, logits, c.plan.v_pad, stream);
   launch_argmax(logits, (int64_t)c.vocab_size, am_val, am_idx, am_cnt, am_blocks, d_token, d_pos, d_hist, pdl, stream);

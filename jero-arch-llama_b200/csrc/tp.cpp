@@ -6,6 +6,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.hpp"
 
@@ -107,6 +108,60 @@ void tp_all_reduce(const TpComm &t, float *buf, size_t n, cudaStream_t s) {
 
 void tp_all_gather(const TpComm &t, const float *send, float *recv, size_t n, cudaStream_t s) {
   check(nccl().all_gather(send, recv, n, ncclFloat32, (ncclComm_t)t.comm, s), "ncclAllGather");
+}
+
+TpSymmetric::~TpSymmetric() {
+  for (int r = 0; r < world && r < kTpMaxWorld; r++)
+    if (r != rank && peer[r]) cudaIpcCloseMemHandle(peer[r]);
+  if (local) cudaFree(local);
+}
+
+TpSymmetric *tp_symmetric_alloc(const TpComm &t, size_t bytes, cudaStream_t s) {
+  const int W = t.world;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handle size");
+  // one scratch: [W][64] handle bytes, then one float (the failure count)
+  void *scratch = nullptr;
+  JAL_CUDA(cudaMalloc(&scratch, (size_t)W * 64 + 64));
+  auto sym = new TpSymmetric();
+  sym->rank = t.rank;
+  sym->world = W;
+  float bad = W > kTpMaxWorld ? 1.0f : 0.0f;
+  cudaIpcMemHandle_t h = {};
+  if (cudaMalloc(&sym->local, bytes) != cudaSuccess || cudaMemsetAsync(sym->local, 0, bytes, s) != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, sym->local) != cudaSuccess) {
+    cudaGetLastError();
+    bad = 1.0f;
+  }
+  // The zeroing above is ordered before the exchange on `s`, so no peer can
+  // signal into this allocation before it is clean.
+  char *hs = (char *)scratch;
+  JAL_CUDA(cudaMemcpyAsync(hs + (size_t)t.rank * 64, &h, 64, cudaMemcpyHostToDevice, s));
+  check(nccl().all_gather(hs + (size_t)t.rank * 64, hs, 64, ncclUint8, (ncclComm_t)t.comm, s), "ncclAllGather");
+  std::vector<cudaIpcMemHandle_t> all((size_t)W);
+  JAL_CUDA(cudaMemcpyAsync(all.data(), hs, (size_t)W * 64, cudaMemcpyDeviceToHost, s));
+  JAL_CUDA(cudaStreamSynchronize(s));
+  if (bad == 0.0f) {
+    for (int r = 0; r < W; r++) {
+      if (r == t.rank) { sym->peer[r] = sym->local; continue; }
+      if (cudaIpcOpenMemHandle(&sym->peer[r], all[(size_t)r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        sym->peer[r] = nullptr;
+        bad = 1.0f;
+      }
+    }
+  }
+  float *fb = (float *)(hs + (size_t)W * 64);
+  JAL_CUDA(cudaMemcpyAsync(fb, &bad, 4, cudaMemcpyHostToDevice, s));
+  check(nccl().all_reduce(fb, fb, 1, ncclFloat32, ncclSum, (ncclComm_t)t.comm, s), "ncclAllReduce");
+  float total = 0.0f;
+  JAL_CUDA(cudaMemcpyAsync(&total, fb, 4, cudaMemcpyDeviceToHost, s));
+  JAL_CUDA(cudaStreamSynchronize(s));
+  cudaFree(scratch);
+  if (total != 0.0f) {
+    delete sym;
+    return nullptr;
+  }
+  return sym;
 }
 
 }  // namespace jal

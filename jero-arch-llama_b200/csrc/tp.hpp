@@ -42,4 +42,20 @@ TpComm *tp_init(const uint8_t *id128, int rank, int world);
 void tp_all_reduce(const TpComm &t, float *buf, size_t n, cudaStream_t s);
 void tp_all_gather(const TpComm &t, const float *send, float *recv, size_t n, cudaStream_t s);
 
+constexpr int kTpMaxWorld = 8;
+
+// Symmetric device memory: every rank allocates `bytes` (zeroed), the CUDA
+// IPC handles are all-gathered through NCCL and each rank maps the others'
+// allocations, so peer[r] is rank r's allocation in this process (peer[rank]
+// == local).  Collective: all ranks call it in the same order.
+struct TpSymmetric {
+  int rank = 0, world = 1;
+  void *local = nullptr;
+  void *peer[kTpMaxWorld] = {};
+  ~TpSymmetric();
+};
+// nullptr on every rank when any rank cannot map a peer (no peer access, or
+// more than kTpMaxWorld ranks); the ranks agree through an all-reduce.
+TpSymmetric *tp_symmetric_alloc(const TpComm &t, size_t bytes, cudaStream_t s);
+
 }  // namespace jal

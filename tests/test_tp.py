@@ -92,12 +92,15 @@ def test_row_and_column_parallel_combine_to_the_unsharded_projection(jal, oracle
 
 
 @pytest.mark.gpu
-def test_tensor_parallel_decode_two_gpus_matches_oracle(jal, oracle, torch_cuda):
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_tensor_parallel_decode_two_gpus_matches_oracle(jal, oracle, torch_cuda, exchange):
     """TP2 on two GPUs: the tiny model (FFN 1536 so that it splits into whole
     blocks), prefill and 24 teacher-forced decode steps on the oracle's
-    greedy tokens.  Both ranks hold identical gathered logits; against the
-    oracle they meet the fast-numerics bars of the single-GPU path; the
-    on-device greedy loop advances the position on every rank."""
+    greedy tokens, with the partial sums exchanged over peer memory inside
+    the GEMVs or all-reduced by NCCL.  Both ranks hold identical gathered
+    logits; against the oracle they meet the fast-numerics bars of the
+    single-GPU path; the on-device greedy loop advances the position on
+    every rank."""
     torch = torch_cuda
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two CUDA devices")
@@ -122,14 +125,15 @@ def test_tensor_parallel_decode_two_gpus_matches_oracle(jal, oracle, torch_cuda)
     uid = jal.tp_unique_id()
     steps = 12
     out = _spawn(tp_workers.gpu_tp_worker, 2,
-                 lambda r: (r, 2, uid, spec_kwargs, seed, prompt, np.asarray(tokens), steps))
-    l0, g0, p0 = out[0]
-    l1, g1, p1 = out[1]
+                 lambda r: (r, 2, uid, spec_kwargs, seed, prompt, np.asarray(tokens), steps, exchange))
+    l0, g0, p0, m0 = out[0]
+    l1, g1, p1, m1 = out[1]
+    assert m0 == m1 == exchange
     assert np.array_equal(l0, l1), "ranks disagree on the gathered logits"
     assert np.array_equal(g0, g1)
     assert p0 == p1 == len(prompt) + steps
     err = np.abs(l0[:, :spec.vocab_size] - ref)
-    print(f"TP2 vs oracle: worst |dlogit| {err.max():.3e}, worst mean {err.mean(1).max():.3e}")
+    print(f"TP2 ({exchange}) vs oracle: worst |dlogit| {err.max():.3e}, worst mean {err.mean(1).max():.3e}")
     assert err.max() <= FAST_MAX_ATOL
     assert err.mean(1).max() <= FAST_MEAN_ATOL
     # argmax may differ from the oracle's only at a near-tie of its logits

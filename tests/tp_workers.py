@@ -59,12 +59,16 @@ def row_col_parallel_worker(rank, world, port, out_q):
         out_q.put((rank, traceback.format_exc(), None))
 
 
-def gpu_tp_worker(rank, world, uid, spec_kwargs, seed, prompt, tokens, steps, out_q):
+def gpu_tp_worker(rank, world, uid, spec_kwargs, seed, prompt, tokens, steps, exchange, out_q):
     """One GPU per rank: this rank's shard of a synthetic model, prefill, the
     given tokens teacher-forced (logits of every step), then greedy decode on
-    the device."""
+    the device.  exchange "nccl" forces the all-reduce decode step."""
     try:
         import torch
+        if exchange == "nccl":
+            os.environ["JAL_TP_NCCL"] = "1"
+        else:
+            os.environ.pop("JAL_TP_NCCL", None)
         torch.cuda.set_device(rank)
         jal = _load_jal()
         jal.set_device(rank)
@@ -74,6 +78,7 @@ def gpu_tp_worker(rank, world, uid, spec_kwargs, seed, prompt, tokens, steps, ou
         recipe = jal.LlamaRecipe.from_gguf(buf)
         cache = recipe.build_repack_cache(buf, device=rank, tp=tp)
         ctx = jal.ExecutionContext(recipe, cache, n_ctx=256, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
+        mode = ctx.tp_exchange()
         logits = [ctx.prefill_step(prompt, 0)]
         for t in tokens:
             logits.append(ctx.decode_step(int(t)))
@@ -83,6 +88,6 @@ def gpu_tp_worker(rank, world, uid, spec_kwargs, seed, prompt, tokens, steps, ou
         pos = ctx2.position()
         del ctx, ctx2, cache
         torch.cuda.synchronize()
-        out_q.put((rank, None, (np.stack(logits), np.asarray(greedy), pos)))
+        out_q.put((rank, None, (np.stack(logits), np.asarray(greedy), pos, mode)))
     except Exception:
         out_q.put((rank, traceback.format_exc(), None))
