@@ -337,6 +337,7 @@ def main():
         nonlocal logits
         logits = ctx.prefill_step(prompt, 0)
 
+    do_prefill()  # warm-up (kernel loads, first-use NCCL connections); the timed pass rewrites the cache
     t_prefill = ev_time(torch, do_prefill, stream)
     tok = int(np.argmax(logits))
     # Decode warm-up, then K timed steps (one CUDA graph launch per token).
@@ -374,7 +375,7 @@ def main():
             "config": {"workload": f"{args.workload} decode bs=1 greedy after a {n_prefill}-token prefill",
                        "layers": spec.num_layers, "hidden": spec.hidden_dim, "heads": [spec.n_heads_q, spec.n_heads_kv],
                        "head_dim": spec.head_dim, "ffn": spec.ffn_dim, "vocab": spec.vocab_size,
-                       "weights": "Q4_0 (4.5 bpw in HBM)", "kv_cache": "paged fp16", "parallelism": f"tp{world}" if tp else f"replicas x{world}",
+                       "weights": "Q4_0 (4.5 bpw in HBM)", "kv_cache": "paged fp16", "parallelism": f"tp{world} ({ctx.tp_exchange()} exchange)" if tp else f"replicas x{world}",
                        "l2": "no flush: each step streams the 4.2 GB of weights (> L2)",
                        "gguf_gen_s": round(gen_s, 1), "repack_s": round(build_s, 2)},
             "decode_step": {"bytes_per_token": bytes_token + kv_bytes,

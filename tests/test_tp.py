@@ -94,8 +94,8 @@ def test_row_and_column_parallel_combine_to_the_unsharded_projection(jal, oracle
 @pytest.mark.gpu
 @pytest.mark.parametrize("exchange", ["peer", "nccl"])
 def test_tensor_parallel_decode_two_gpus_matches_oracle(jal, oracle, torch_cuda, exchange):
-    """TP2 on two GPUs: the tiny model (FFN 1536 so that it splits into whole
-    blocks), prefill and 24 teacher-forced decode steps on the oracle's
+    """TP2 on two GPUs: a small synthetic model (hidden 1024, 16/4 heads,
+    FFN 2048), prefill and 24 teacher-forced decode steps on the oracle's
     greedy tokens, with the partial sums exchanged over peer memory inside
     the GEMVs or all-reduced by NCCL.  Both ranks hold identical gathered
     logits; against the oracle they meet the fast-numerics bars of the
@@ -104,7 +104,9 @@ def test_tensor_parallel_decode_two_gpus_matches_oracle(jal, oracle, torch_cuda,
     torch = torch_cuda
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two CUDA devices")
-    spec_kwargs = dict(ffn_dim=1536)
+    # every TP2 shard row 32-byte aligned (the segmented GEMV that carries the
+    # peer exchange): O 512 and down 1024 input columns per rank
+    spec_kwargs = dict(hidden_dim=1024, n_heads_q=16, n_heads_kv=4, head_dim=64, ffn_dim=2048)
     spec = jal.SynthSpec(**spec_kwargs)
     seed = 515
     buf = jal.synth_gguf(spec, seed)
