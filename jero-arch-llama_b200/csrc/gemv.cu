@@ -347,9 +347,9 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvAr
   }
   if (OUT == GEMV_OUT_PEER) {  // this CTA's rows are out: signal every rank
     __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      for (int r = 0; r < a.peer_world; r++) red_release_sys_add(a.peer_sig[r], 1ull);
+    if (threadIdx.x == 0) {  // the CTA barrier and this fence order every thread's row stores first
+      fence_acq_rel_sys();
+      for (int r = 0; r < a.peer_world; r++) red_relaxed_sys_add(a.peer_sig[r], 1ull);
     }
   }
 }
