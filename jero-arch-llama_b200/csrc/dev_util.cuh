@@ -167,38 +167,47 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 __device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// Cross-GPU signalling over peer memory (tensor-parallel exchange).
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+// Cross-GPU exchange over peer memory (tensor parallelism): flagged 64-bit
+// words, stored and polled at system scope.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void ld_relaxed_sys_v2u64(const unsigned long long *p, unsigned long long &a,
+                                                     unsigned long long &b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_gpu_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Relaxed add; preceded by one fence.acq_rel.sys it forms the release
-// pattern, so several signals after one fence cost one fence.
-__device__ __forceinline__ void red_relaxed_sys_add(unsigned long long *p, unsigned long long v) {
-  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// Waits until *cnt reaches the next multiple of per_step at or above its
-// first value (signals of one exchange step; a peer is never a whole step
-// ahead on the same counter).  Gives up after kPeerWaitNs and returns false.
-constexpr uint64_t kPeerWaitNs = 4000000000ull;
-__device__ __forceinline__ bool peer_wait_step(const unsigned long long *cnt, unsigned long long per_step) {
-  unsigned long long c = ld_acquire_sys(cnt);
-  unsigned long long target = (c + per_step - 1) / per_step * per_step;
-  if (target == 0) target = per_step;
-  if (c >= target) return true;
-  const uint64_t t0 = global_ns();
-  while (true) {
-    __nanosleep(64);
-    if (ld_acquire_sys(cnt) >= target) return true;
-    if (global_ns() - t0 > kPeerWaitNs) return false;
+constexpr uint64_t kPeerWaitNs = 4000000000ull;  // a peer's words not there after 4 s: give up
+// Eight consecutive flagged words at p (16-byte aligned): waits until every
+// flag equals `flag` and adds their values to v[0..7] in order.  False when
+// the wait gave up (the values are then added as found).
+__device__ __forceinline__ bool peer_take8(const unsigned long long *p, uint32_t flag, float (&v)[8]) {
+  unsigned long long w[8];
+  uint64_t t0 = 0;
+  bool ok = true;
+  for (int it = 0;; it++) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) ld_relaxed_sys_v2u64(p + 2 * k, w[2 * k], w[2 * k + 1]);
+    bool all = true;
+#pragma unroll
+    for (int k = 0; k < 8; k++) all = all && (uint32_t)(w[k] >> 32) == flag;
+    if (all) break;
+    if (it == 0) t0 = global_ns();
+    else if (global_ns() - t0 > kPeerWaitNs) { ok = false; break; }
+    __nanosleep(32);
   }
+#pragma unroll
+  for (int k = 0; k < 8; k++) v[k] = __fadd_rn(v[k], __uint_as_float((uint32_t)w[k]));
+  return ok;
 }
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

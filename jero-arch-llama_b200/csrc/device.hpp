@@ -35,7 +35,7 @@ inline int64_t d_stride_for(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
 // squares of the row; the norm scale is folded into the block scales.
 enum GemvIn : int { GEMV_IN_Q8 = 0, GEMV_IN_F32 = 1, GEMV_IN_NORM = 2, GEMV_IN_PREQ = 3 };
 // GEMV_OUT_PEER (tensor-parallel decode): each row value goes to every
-// rank's partial-sum slot over peer memory, then each CTA signals every rank.
+// rank's partial-sum slot over peer memory as a flagged 64-bit word.
 enum GemvOut : int { GEMV_OUT_STORE = 0, GEMV_OUT_ADD = 1, GEMV_OUT_SWIGLU = 2, GEMV_OUT_PEER = 3 };
 constexpr int kPeerMax = 8;
 constexpr int kErrPeerWait = 16;  // bit set in the context error word
@@ -70,22 +70,24 @@ struct GemvArgs {
   float *nx_u = nullptr, *nx_s = nullptr, *nx_ss = nullptr;
   int8_t *nx_q = nullptr;
   unsigned *nx_cnt = nullptr;
-  // Tensor-parallel exchange over peer memory (decode, M = 1, IN_NORM).
-  // With peer_in set the prologue first waits until *peer_cnt reaches the
-  // next multiple of peer_per_step (bounded: kErrPeerWait in *err), then
-  // takes the row as x + peer_in[0 .. x_stride) + peer_in[x_stride ..) + ...
-  // (peer_world slices, added in rank order, so every rank gets the same
-  // bits) and CTA 0 stores that sum to x_out.
-  const float *peer_in = nullptr;
-  const unsigned long long *peer_cnt = nullptr;
-  unsigned long long peer_per_step = 0;
+  // Tensor-parallel exchange over peer memory (decode, M = 1).  A slot word
+  // is (flag << 32) | f32 bits, flag = epoch * 256 + phase + 1 with epoch
+  // the context's step counter (*peer_epoch) and phase < 255 the exchange
+  // within the step; a 64-bit store is single-copy atomic, so a word whose
+  // flag matches carries this step's value.
+  // IN_NORM with peer_in: the row is x + slot row 0 + slot row 1 + ...
+  // (peer_world rows of x_stride words, added in rank order, so every rank
+  // gets the same bits), each word waited for until its flag matches
+  // (bounded: kErrPeerWait in *err); CTA 0 stores the sum to x_out.
+  // GEMV_OUT_PEER: each row value (+ bias) is stored as a word to
+  // peer_out[r][row] for r < peer_world.
+  const unsigned long long *peer_in = nullptr;
+  const uint32_t *peer_epoch = nullptr;
+  int peer_phase = 0;
+  int peer_world = 0;
   float *x_out = nullptr;
   int *err = nullptr;
-  // GEMV_OUT_PEER: row value (+ bias) to peer_out[r][row] for r < peer_world;
-  // then every CTA adds 1 to *peer_sig[r] (release, system scope).
-  int peer_world = 0;
-  float *peer_out[kPeerMax] = {};
-  unsigned long long *peer_sig[kPeerMax] = {};
+  unsigned long long *peer_out[kPeerMax] = {};
   int grid = 0;                 // CTAs (0 = auto)
   int pdl = 0;                  // launch with programmatic dependent launch
   int64_t pf_bytes = -1;        // L2 prefetch budget per CTA (-1 = default)
@@ -303,6 +305,7 @@ void launch_embed(const uint8_t *emb_raw, int quant, int64_t hidden, int64_t voc
 // Greedy argmax over logits (lowest index wins ties); writes next token and
 // advances the device position.
 void launch_argmax(const float *logits, int64_t n, float *part_val, int *part_idx, unsigned *cnt, int n_blocks,
-                   uint32_t *token_out, int64_t *d_pos, uint32_t *hist, int pdl, cudaStream_t s);
+                   uint32_t *token_out, int64_t *d_pos, uint32_t *hist, int pdl, cudaStream_t s,
+                   uint32_t *epoch = nullptr);  // += 1 per call when set (tensor-parallel exchange)
 
 }  // namespace jal

@@ -287,6 +287,10 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvAr
   }
   pdl_wait();
   pdl_trigger();
+  // GEMV_OUT_PEER: flag of this step's words (the epoch advanced before the wait)
+  const unsigned long long xflag =
+      OUT == GEMV_OUT_PEER ? (unsigned long long)(ld_relaxed_gpu_u32(a.peer_epoch) * 256u + (uint32_t)a.peer_phase + 1u) << 32
+                           : 0ull;
   if (l2_first) {  // weight loads first: they overlap the prologue's round trip
 #pragma unroll
     for (int j = 0; j < DEPTH; j++)
@@ -322,8 +326,8 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvAr
           const int64_t lr = r0 + li;
           float *yp = a.y + lr;
           if (OUT == GEMV_OUT_PEER) {
-            const float v = a.bias ? s + a.bias[lr] : s;
-            for (int r = 0; r < a.peer_world; r++) a.peer_out[r][lr] = v;
+            const unsigned long long word = xflag | __float_as_uint(a.bias ? s + a.bias[lr] : s);
+            for (int r = 0; r < a.peer_world; r++) st_relaxed_sys_u64(a.peer_out[r] + lr, word);
           } else if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
           else if (OUT == GEMV_OUT_ADD) *yp = *yp + (a.bias ? s + a.bias[lr] : s);
           else *yp = swiglu_one(gate, s);
@@ -339,17 +343,10 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) k_gemv_w4(const GemvAr
       const int64_t lr = r0 + li;
       float *yp = a.y + lr;
       if (OUT == GEMV_OUT_PEER) {
-        const float v = a.bias ? s + a.bias[lr] : s;
-        for (int r = 0; r < a.peer_world; r++) a.peer_out[r][lr] = v;
+        const unsigned long long word = xflag | __float_as_uint(a.bias ? s + a.bias[lr] : s);
+        for (int r = 0; r < a.peer_world; r++) st_relaxed_sys_u64(a.peer_out[r] + lr, word);
       } else if (OUT == GEMV_OUT_STORE) *yp = a.bias ? s + a.bias[lr] : s;
       else *yp = *yp + (a.bias ? s + a.bias[lr] : s);
-    }
-  }
-  if (OUT == GEMV_OUT_PEER) {  // this CTA's rows are out: signal every rank
-    __syncthreads();
-    if (threadIdx.x == 0) {  // the CTA barrier and this fence order every thread's row stores first
-      fence_acq_rel_sys();
-      for (int r = 0; r < a.peer_world; r++) red_relaxed_sys_add(a.peer_sig[r], 1ull);
     }
   }
 }
@@ -567,11 +564,11 @@ bool gemv_peer_supported(const GemvArgs &a) {
   if (a.w.quant != JAL_Q4_0 && a.w.quant != JAL_Q8_0) return false;
   // the exchange lives in the one-round-trip RMSNorm prologue (rows up to
   // 1024 jobs of 8 elements) and in the segmented kernel's epilogue
-  if (a.peer_in && (a.in_mode != GEMV_IN_NORM || a.w.cols > 8192 || !a.peer_cnt || a.peer_per_step == 0))
-    return false;
+  if (!a.peer_epoch || a.peer_phase < 0 || a.peer_phase > 254) return false;
+  if (a.peer_in && (a.in_mode != GEMV_IN_NORM || a.w.cols > 8192 || a.x_stride % 2 != 0)) return false;
   if (a.out_mode == GEMV_OUT_PEER)
     for (int r = 0; r < a.peer_world; r++)
-      if (!a.peer_out[r] || !a.peer_sig[r]) return false;
+      if (!a.peer_out[r]) return false;
   int grid = a.grid;
   if (grid <= 0) {
     int sms = 0, dev = 0;

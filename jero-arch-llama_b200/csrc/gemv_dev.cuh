@@ -217,13 +217,11 @@ __device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, 
     ((uint4 *)(smem + nbp * 16))[b] = make_uint4(0, 0, 0, 0);
     put_scale_sum(smem, nbp, b, 0.0f, 0);
   }
-  // Tensor-parallel exchange: wait for every rank's partial sums of this
-  // step (one thread polls; the CTA barrier orders the loads after it).
+  // Tensor-parallel exchange: each thread waits for the flagged words of its
+  // own elements from every rank.
   constexpr bool peer = NORM && PEER;
-  if (peer) {
-    if (tid == 0 && !peer_wait_step(a.peer_cnt, a.peer_per_step) && a.err) atomicOr(a.err, kErrPeerWait);
-    __syncthreads();
-  }
+  const uint32_t flag = peer ? ld_relaxed_gpu_u32(a.peer_epoch) * 256u + (uint32_t)a.peer_phase + 1u : 0u;
+  bool peer_ok = true;
   float v[JMAX][8], w[NORM ? JMAX : 1][8];
 #pragma unroll
   for (int j = 0; j < JMAX; j++) {
@@ -233,15 +231,9 @@ __device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, 
       const float4 x0 = xp[0], x1 = xp[1];
       v[j][0] = x0.x; v[j][1] = x0.y; v[j][2] = x0.z; v[j][3] = x0.w;
       v[j][4] = x1.x; v[j][5] = x1.y; v[j][6] = x1.z; v[j][7] = x1.w;
-      if (peer) {  // residual + partials in rank order; written by peers, so read through L2
-        for (int r = 0; r < a.peer_world; r++) {
-          const float4 *pp = (const float4 *)(a.peer_in + (size_t)r * a.x_stride + i * 8);
-          const float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
-          v[j][0] = __fadd_rn(v[j][0], p0.x); v[j][1] = __fadd_rn(v[j][1], p0.y);
-          v[j][2] = __fadd_rn(v[j][2], p0.z); v[j][3] = __fadd_rn(v[j][3], p0.w);
-          v[j][4] = __fadd_rn(v[j][4], p1.x); v[j][5] = __fadd_rn(v[j][5], p1.y);
-          v[j][6] = __fadd_rn(v[j][6], p1.z); v[j][7] = __fadd_rn(v[j][7], p1.w);
-        }
+      if (peer) {  // residual + partials in rank order
+        for (int r = 0; r < a.peer_world; r++)
+          peer_ok = peer_take8(a.peer_in + (size_t)r * a.x_stride + i * 8, flag, v[j]) && peer_ok;
         if (blockIdx.x == 0 && a.x_out) {
           float4 *op = (float4 *)(a.x_out + i * 8);
           op[0] = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
@@ -259,6 +251,7 @@ __device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, 
       for (int e = 0; e < 8; e++) v[j][e] = 0.0f;
     }
   }
+  if (peer && !peer_ok && a.err) atomicOr(a.err, kErrPeerWait);
   float invn = 1.0f;
   if (NORM) {
     float ss = 0.0f;

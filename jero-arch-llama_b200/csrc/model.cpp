@@ -949,7 +949,7 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->am_blocks = sms;
   size_t f32s = H + (Q + 2 * KV) + Q + Q / 32 + F + (F + 31) / 32 + V + sms;
   size_t bytes = f32s * 4 + Q + ((F + 31) / 32) * 32 + 4096 + (F / 32 + 1) * 4 + 64 + (size_t)sms * 4 + (n_ctx + 2) * 4 +
-                 32 * 256 + c.plan.v_pad * 4 + H * 4 + 512;
+                 32 * 256 + c.plan.v_pad * 4 + H * 4 + 768;
   auto db = alloc(bytes + 1024);
   ctx->bufs.push_back(db);
   JAL_CUDA(cudaMemset(db->ptr, 0, db->bytes));
@@ -974,6 +974,7 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   ctx->am_cnt = (unsigned *)take(4);
   ctx->d_hist = (uint32_t *)take((n_ctx + 2) * 4);
   ctx->hidden_b = (float *)take(H * 4);
+  ctx->d_xepoch = (uint32_t *)take(4);
   if ((size_t)(p - db->as<char>()) > db->bytes) fail(JAL_ERR_INVALID_ARGUMENT, "internal: decode scratch layout overflow");
   if (c.tp && c.plan.world > 1) setup_tp_exchange(*ctx, sms);
   {  // reference-order scratch: normed row, int8 activations + scales, gate|up, q
@@ -996,38 +997,30 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
 }
 
 // Tensor-parallel exchange over peer memory for the decode step: a
-// symmetric allocation (counters, partial slots) mapped on every rank.
-// Collective over the ranks; on any mismatch (SM counts, a shape off the
-// segmented GEMV, no peer mapping) every rank keeps the NCCL all-reduce.
+// symmetric allocation of flagged-word slots mapped on every rank.
+// Collective over the ranks; on any mismatch (a shape off the segmented
+// GEMV, too many layers for the flag's phase field, no peer mapping) every
+// rank keeps the NCCL all-reduce.
 static void setup_tp_exchange(Context &ctx, int sms) {
+  (void)sms;
   const ModelCache &c = *ctx.cache;
   const int W = c.plan.world;
   const uint64_t H = ctx.g.hidden_dim;
   const size_t L = c.layers.size();
-  ctx.tp_cnt_bytes = (2 * L * 8 + 255) / 256 * 256;
-  // every rank must launch the producers with the same grid
-  ctx.tp_grid = (int)std::min<uint64_t>(H, (uint64_t)sms);
-  float g = (float)ctx.tp_grid;
-  JAL_CUDA(cudaMemcpyAsync(ctx.am_val, &g, 4, cudaMemcpyHostToDevice, ctx.stream));
-  tp_all_reduce(*c.tp, ctx.am_val, 1, ctx.stream);
-  float gsum = 0.0f;
-  JAL_CUDA(cudaMemcpyAsync(&gsum, ctx.am_val, 4, cudaMemcpyDeviceToHost, ctx.stream));
-  JAL_CUDA(cudaStreamSynchronize(ctx.stream));
   // shapes are the same on every rank, so every rank decides alike
-  bool ok = gsum == g * (float)W && W <= kPeerMax && !env_flag("JAL_TP_NCCL");
-  if (ok && !c.layers.empty()) {
+  bool ok = W <= kPeerMax && L >= 1 && 2 * L <= 255 && !env_flag("JAL_TP_NCCL");
+  if (ok) {
     const Layer &L0 = c.layers[0];
-    float *dummy = ctx.hidden_b;
-    unsigned long long *dcnt = (unsigned long long *)ctx.hidden_b;
+    unsigned long long *dummy = (unsigned long long *)ctx.hidden_b;
     GemvArgs pa;  // producer (O / down)
-    pa.m = 1; pa.out_mode = GEMV_OUT_PEER; pa.peer_world = W; pa.grid = ctx.tp_grid; pa.rows = (int64_t)H;
-    for (int r = 0; r < W; r++) { pa.peer_out[r] = dummy; pa.peer_sig[r] = dcnt; }
+    pa.m = 1; pa.out_mode = GEMV_OUT_PEER; pa.peer_world = W; pa.rows = (int64_t)H; pa.peer_epoch = ctx.d_xepoch;
+    for (int r = 0; r < W; r++) pa.peer_out[r] = dummy;
     GemvArgs po = pa, pd = pa;
     po.w = L0.wo.dm; po.in_mode = GEMV_IN_Q8;
     pd.w = L0.wdown.dm; pd.in_mode = GEMV_IN_F32;
     GemvArgs ca;  // consumers (QKV, gate / up, LM head)
-    ca.m = 1; ca.in_mode = GEMV_IN_NORM; ca.peer_in = dummy; ca.peer_cnt = dcnt; ca.peer_per_step = 1;
-    ca.peer_world = W;
+    ca.m = 1; ca.in_mode = GEMV_IN_NORM; ca.peer_in = dummy; ca.peer_epoch = ctx.d_xepoch; ca.peer_world = W;
+    ca.x_stride = (int64_t)H;
     GemvArgs cq = ca, cg = ca, cl = ca;
     cq.w = L0.qkv; cq.rows = L0.qkv.rows; cq.out_mode = GEMV_OUT_STORE;
     cg.w = L0.gateup; cg.rows = (int64_t)ctx.g.ffn_dim; cg.out_mode = GEMV_OUT_SWIGLU; cg.up_offset = (int64_t)ctx.g.ffn_dim;
@@ -1036,7 +1029,7 @@ static void setup_tp_exchange(Context &ctx, int sms) {
          gemv_peer_supported(cl);
   }
   if (!ok) return;
-  ctx.tp_sym.reset(tp_symmetric_alloc(*c.tp, ctx.tp_cnt_bytes + 2 * (size_t)W * H * 4, ctx.stream));
+  ctx.tp_sym.reset(tp_symmetric_alloc(*c.tp, 2 * (size_t)W * H * 8, ctx.stream));
 }
 
 size_t decode_scratch_bytes(const Recipe &r, uint64_t seq) {  // recipe.rs:529-547 (device buffers)
@@ -1065,28 +1058,24 @@ void Context::enqueue_decode_step(bool pdl) {
                stream);
   n++;
   // Tensor parallelism over peer memory: O and down (phases 2l, 2l + 1)
-  // store their partial rows into every rank's slot of parity phase % 2 and
-  // signal that phase's counter; the next RMSNorm GEMV waits, adds the
-  // partials to the residual it reads (hidden for even phases, hidden_b for
-  // odd ones) and writes the sum to the other buffer.
+  // store their partial rows as flagged words into every rank's slots of
+  // parity phase % 2; the next RMSNorm GEMV waits for the words of its step
+  // and phase, adds them to the residual it reads (hidden for even phases,
+  // hidden_b for odd ones) and writes the sum to the other buffer.  The
+  // argmax at the end of the step advances the flag epoch.
   const bool xp = tp_sym != nullptr;
   const int W = c.plan.world, rank = c.plan.rank;
-  auto x_counter = [&](int r, size_t phase) {
-    return (unsigned long long *)tp_sym->peer[r] + phase;
-  };
   auto x_slots = [&](int r, size_t parity) {  // rank r's slots [world][H] of this parity
-    return (float *)((char *)tp_sym->peer[r] + tp_cnt_bytes) + parity * (size_t)W * H;
+    return (unsigned long long *)tp_sym->peer[r] + parity * (size_t)W * H;
   };
   auto produce = [&](GemvArgs &a, size_t phase) {
-    a.out_mode = GEMV_OUT_PEER; a.y = nullptr; a.peer_world = W; a.grid = tp_grid;
-    for (int r = 0; r < W; r++) {
-      a.peer_out[r] = x_slots(r, phase % 2) + (size_t)rank * H;
-      a.peer_sig[r] = x_counter(r, phase);
-    }
+    a.out_mode = GEMV_OUT_PEER; a.y = nullptr; a.peer_world = W;
+    a.peer_epoch = d_xepoch; a.peer_phase = (int)phase;
+    for (int r = 0; r < W; r++) a.peer_out[r] = x_slots(r, phase % 2) + (size_t)rank * H;
   };
   auto consume = [&](GemvArgs &a, size_t phase) {
-    a.peer_in = x_slots(rank, phase % 2); a.peer_cnt = x_counter(rank, phase);
-    a.peer_per_step = (unsigned long long)W * (unsigned long long)tp_grid; a.peer_world = W; a.err = d_err;
+    a.peer_in = x_slots(rank, phase % 2); a.peer_world = W; a.err = d_err;
+    a.peer_epoch = d_xepoch; a.peer_phase = (int)phase;
     a.x = phase % 2 ? hidden_b : hidden;
     a.x_out = phase % 2 ? hidden : hidden_b;
   };
@@ -1146,7 +1135,8 @@ void Context::enqueue_decode_step(bool pdl) {
   }
   launch_gemv(la, stream);
   if (c.tp) tp_all_gather(*c.tp, logits_local, logits, c.plan.v_pad, stream);
-  launch_argmax(logits, (int64_t)c.vocab_size, am_val, am_idx, am_cnt, am_blocks, d_token, d_pos, d_hist, pdl, stream);
+  launch_argmax(logits, (int64_t)c.vocab_size, am_val, am_idx, am_cnt, am_blocks, d_token, d_pos, d_hist, pdl, stream,
+                xp ? d_xepoch : nullptr);
   n += 2;
   launches_per_step = n;
 }

@@ -141,13 +141,12 @@ struct Context {
         *logits = nullptr, *am_val = nullptr;
   float *logits_local = nullptr;  // this rank's LM-head rows (== logits without tensor parallelism)
   // Tensor-parallel exchange over peer memory (decode step): symmetric
-  // [2 L] u64 per-phase arrival counters, then partial-sum slots
-  // [2 parity][world][hidden] f32; hidden_b is the second residual buffer
-  // (the combining prologues read one and write the other).  Null: the
-  // step all-reduces through NCCL.
+  // partial-sum slots [2 parity][world][hidden] of flagged 64-bit words;
+  // d_xepoch counts the steps (the flags' epoch); hidden_b is the second
+  // residual buffer (the combining prologues read one and write the other).
+  // Null tp_sym: the step all-reduces through NCCL.
   std::unique_ptr<TpSymmetric> tp_sym;
-  size_t tp_cnt_bytes = 0;
-  int tp_grid = 0;
+  uint32_t *d_xepoch = nullptr;
   float *hidden_b = nullptr;
   int8_t *attn_q = nullptr, *ffn_q = nullptr;
   unsigned *ffn_cnt = nullptr, *am_cnt = nullptr;

@@ -112,7 +112,7 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 }
 
 __global__ void k_argmax(const float *logits, int64_t n, float *pv, int *pi, unsigned *cnt, uint32_t *token_out,
-                         int64_t *d_pos, uint32_t *hist, int pdl) {
+                         int64_t *d_pos, uint32_t *hist, int pdl, uint32_t *epoch) {
   __shared__ float sv[32];
   __shared__ int si[32];
   __shared__ bool last;
@@ -176,6 +176,7 @@ __global__ void k_argmax(const float *logits, int64_t n, float *pv, int *pi, uns
     if (hist) hist[*d_pos + 1] = tok;  // token of the next position
     *d_pos += 1;
   }
+  if (epoch) *epoch += 1u;  // tensor-parallel exchange: the next step's flags
   *cnt = 0u;
   if (pdl) pdl_trigger();
 }
@@ -209,7 +210,7 @@ void launch_gqa_attention_ref(const float *q, const float *k, const float *v, in
 }
 
 void launch_argmax(const float *logits, int64_t n, float *part_val, int *part_idx, unsigned *cnt, int n_blocks,
-                   uint32_t *token_out, int64_t *d_pos, uint32_t *hist, int pdl, cudaStream_t s) {
+                   uint32_t *token_out, int64_t *d_pos, uint32_t *hist, int pdl, cudaStream_t s, uint32_t *epoch) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)n_blocks);
   cfg.blockDim = dim3(256);
@@ -219,7 +220,7 @@ void launch_argmax(const float *logits, int64_t n, float *part_val, int *part_id
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaLaunchKernelEx(&cfg, k_argmax, logits, n, part_val, part_idx, cnt, token_out, d_pos, hist, pdl);
+  cudaLaunchKernelEx(&cfg, k_argmax, logits, n, part_val, part_idx, cnt, token_out, d_pos, hist, pdl, epoch);
 }
 
 }  // namespace jal
