@@ -1007,7 +1007,6 @@ static void setup_tp_exchange(Context &ctx, int sms) {
   const int W = c.plan.world;
   const uint64_t H = ctx.g.hidden_dim;
   const size_t L = c.layers.size();
-  // shapes are the same on every rank, so every rank decides alike
   bool ok = W <= kPeerMax && L >= 1 && 2 * L <= 255 && !env_flag("JAL_TP_NCCL");
   if (ok) {
     const Layer &L0 = c.layers[0];
@@ -1028,7 +1027,14 @@ static void setup_tp_exchange(Context &ctx, int sms) {
     ok = gemv_peer_supported(po) && gemv_peer_supported(pd) && gemv_peer_supported(cq) && gemv_peer_supported(cg) &&
          gemv_peer_supported(cl);
   }
-  if (!ok) return;
+  // Agree before the collective allocation (a rank that opts out by its
+  // environment must not leave the others waiting in it).
+  float no = ok ? 0.0f : 1.0f;
+  JAL_CUDA(cudaMemcpyAsync(ctx.am_val, &no, 4, cudaMemcpyHostToDevice, ctx.stream));
+  tp_all_reduce(*c.tp, ctx.am_val, 1, ctx.stream);
+  JAL_CUDA(cudaMemcpyAsync(&no, ctx.am_val, 4, cudaMemcpyDeviceToHost, ctx.stream));
+  JAL_CUDA(cudaStreamSynchronize(ctx.stream));
+  if (no != 0.0f) return;
   ctx.tp_sym.reset(tp_symmetric_alloc(*c.tp, 2 * (size_t)W * H * 8, ctx.stream));
 }
 
