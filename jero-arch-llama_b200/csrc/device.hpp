@@ -18,11 +18,11 @@
 namespace jal {
 
 struct DevMat {
-  int quant = 0;          // JAL_Q4_0, JAL_Q8_0, or JAL_F32 for dense rows
+  int quant = 0;          // JAL_Q4_0, JAL_Q8_0, or JAL_F16 / JAL_BF16 / JAL_F32 for dense rows
   int64_t rows = 0, cols = 0;
   const uint8_t *qs = nullptr;
   const uint16_t *d = nullptr;
-  const float *dense = nullptr;  // dense f32 rows (cols stride), float types
+  const void *dense = nullptr;  // dense rows in their GGUF element type (cols stride)
   int64_t qs_stride = 0;  // bytes per row (quants + scales)
   int64_t d_stride = 0;   // row stride of d in halves (qs_stride / 2)
 };
@@ -94,6 +94,11 @@ struct GemvArgs {
 };
 
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
+// Dense rows (dense.cu): M = 1, f32 or RMSNorm input, stored output; the
+// reference-order form takes the normed f32 row.
+bool dense_quant(int q);
+void launch_gemv_dense(const GemvArgs &a, cudaStream_t s);
+void launch_strict_gemv_dense(const DevMat &w, const float *x, int64_t rows, float *y, cudaStream_t s);
 // True when launch_gemv runs `a` (with peer_in or GEMV_OUT_PEER) on the
 // segmented kernel whose prologue / epilogue implement the exchange.
 bool gemv_peer_supported(const GemvArgs &a);
@@ -105,8 +110,6 @@ size_t gemv_smem_bytes(int in_mode, int m, int64_t cols);
 // ---- repack / export / activation quantizers ---------------------------
 void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, uint8_t *qs, uint16_t *d,
                    int64_t qs_stride, int64_t d_stride, cudaStream_t s);
-void launch_repack_dense(const uint8_t *raw, int quant, int64_t rows, int64_t cols, float *out,
-                         cudaStream_t s);
 void launch_export_ref(const DevMat &w, int8_t *tiles, float *scales, cudaStream_t s);
 void launch_act_quant(const float *x, int64_t m, int64_t k, int64_t x_stride, int8_t *q8, float *scales,
                       cudaStream_t s);

@@ -581,6 +581,10 @@ bool gemv_peer_supported(const GemvArgs &a) {
 
 void launch_gemv(const GemvArgs &a0, cudaStream_t s) {
   if (a0.rows <= 0) return;
+  if (dense_quant(a0.w.quant)) {
+    launch_gemv_dense(a0, s);
+    return;
+  }
   gemv_init();
   GemvArgs a = a0;
   // Token counts between template sizes run the next larger instantiation;

@@ -424,22 +424,25 @@ void repack_stacked(const std::vector<const uint8_t *> &raws, const std::vector<
     }
     return;
   }
-  if (quant == JAL_F32 || quant == JAL_F16 || quant == JAL_BF16) {
-    DevBufferPtr buf = alloc((size_t)total * cols * 4);
+  if (dense_quant(quant)) {
+    // Dense rows keep their GGUF element type (repack_dense's sanitising
+    // happens on load in the dense kernels).
+    const size_t es = quant == JAL_F32 ? 4 : 2;
+    DevBufferPtr buf = alloc((size_t)total * cols * es);
     storage.push_back(buf);
     stacked = DevMat{};
-    stacked.quant = JAL_F32; stacked.rows = (int64_t)total; stacked.cols = (int64_t)cols;
-    stacked.dense = buf->as<float>();
+    stacked.quant = quant; stacked.rows = (int64_t)total; stacked.cols = (int64_t)cols;
+    stacked.dense = buf->ptr;
     uint64_t r0 = 0;
     for (size_t i = 0; i < raws.size(); i++) {
-      launch_repack_dense(raws[i], quant, (int64_t)rows[i], (int64_t)cols, buf->as<float>() + r0 * cols, s);
-      JAL_CUDA(cudaGetLastError());
+      char *dst = (char *)buf->ptr + r0 * cols * es;
+      JAL_CUDA(cudaMemcpyAsync(dst, raws[i], (size_t)rows[i] * cols * es, cudaMemcpyDeviceToDevice, s));
       CachedMatrix m;
       m.quant = quant; m.rows = rows[i]; m.cols = cols;
       m.dm = stacked;
       m.dm.rows = (int64_t)rows[i];
-      m.dm.dense = buf->as<float>() + r0 * cols;
-      m.aligned_bytes = (size_t)rows[i] * cols * 4;
+      m.dm.dense = dst;
+      m.aligned_bytes = (size_t)rows[i] * cols * es;
       parts.push_back(m);
       r0 += rows[i];
     }
@@ -896,7 +899,10 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
     if (!L.qkv_stacked || !L.gateup_stacked || !device_quant(L.wo.quant) || !device_quant(L.wdown.quant))
       fail(JAL_ERR_CAPABILITY_MISMATCH, "the device forward needs Q4_0/Q8_0 layer matrices with uniform q/k/v and gate/up quants");
   }
-  if (!device_quant(c.lm_head.quant)) fail(JAL_ERR_CAPABILITY_MISMATCH, "LM head quant %d not supported on the device path", c.lm_head.quant);
+  if (!device_quant(c.lm_head.quant) && !dense_quant(c.lm_head.quant))
+    fail(JAL_ERR_CAPABILITY_MISMATCH, "LM head quant %d not supported on the device path", c.lm_head.quant);
+  if (dense_quant(c.lm_head.quant) && g.hidden_dim % 32 != 0)
+    fail(JAL_ERR_CAPABILITY_MISMATCH, "dense LM head: hidden dim %llu not a multiple of 32", (unsigned long long)g.hidden_dim);
   gemv_init();
   if (gemv_smem_bytes(GEMV_IN_F32, 1, (int64_t)g.ffn_dim) > (size_t)kGemvMaxSmem ||
       gemv_smem_bytes(GEMV_IN_NORM, 1, (int64_t)g.hidden_dim) > (size_t)kGemvMaxSmem)
@@ -1186,7 +1192,10 @@ void Context::enqueue_strict_token(bool logits_out, bool argmax) {
   if (logits_out) {
     launch_strict_rmsnorm(hidden, c.output_norm->as<float>(), (int64_t)H, eps, s_norm, stream);
     launch_act_quant(s_norm, 1, (int64_t)H, (int64_t)H, s_q8, s_sc, stream);
-    launch_strict_gemv(c.lm_head.dm, s_q8, s_sc, (int64_t)c.vocab_size, false, logits, nullptr, stream);
+    if (dense_quant(c.lm_head.dm.quant))
+      launch_strict_gemv_dense(c.lm_head.dm, s_norm, (int64_t)c.vocab_size, logits, stream);
+    else
+      launch_strict_gemv(c.lm_head.dm, s_q8, s_sc, (int64_t)c.vocab_size, false, logits, nullptr, stream);
   }
   if (argmax)
     launch_argmax(logits, (int64_t)c.vocab_size, am_val, am_idx, am_cnt, am_blocks, d_token, d_pos, d_hist, 0, stream);

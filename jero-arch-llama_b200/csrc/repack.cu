@@ -107,23 +107,6 @@ void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, ui
     k_repack_q8_0<<<(unsigned)blocks, threads, 0, s>>>(raw, rows, nb, qs, d, qs_stride, d_stride);
 }
 
-// repack_dense (repack_cache.rs:613-637): dense rows to f32 with
-// decode_row_payload_to_f32(sanitize_large = true).
-__global__ void k_repack_dense(const uint8_t *__restrict__ raw, int quant, int64_t n, float *__restrict__ out) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  float v;
-  if (quant == JAL_F32) v = sanitize_weight(((const float *)raw)[i]);
-  else if (quant == JAL_F16) v = f16_finite(((const uint16_t *)raw)[i]);
-  else v = bf16_finite(((const uint16_t *)raw)[i]);
-  out[i] = v;
-}
-
-void launch_repack_dense(const uint8_t *raw, int quant, int64_t rows, int64_t cols, float *out, cudaStream_t s) {
-  int64_t n = rows * cols;
-  if (!n) return;
-  k_repack_dense<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, quant, n, out);
-}
 
 // ---- export to the reference's portable layout (repack_cache.rs:639-694) --
 __device__ __forceinline__ int8_t weight_q(const DevMat &w, int64_t r, int64_t e) {

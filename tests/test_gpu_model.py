@@ -163,6 +163,18 @@ def test_tiny_llama_q5_0_weights(jal, oracle, torch_cuda):
     run_fast(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(13), 16, 256)
 
 
+@pytest.mark.parametrize("head", ["F16", "F32"])
+def test_tiny_llama_dense_lm_head(jal, oracle, torch_cuda, head):
+    # Unquantized output.weight, streamed in its GGUF element type by the
+    # dense GEMV: reference numerics (column-order f32 dot) bit-for-bit
+    # order, and the fast path's statistical bars.
+    spec = jal.SynthSpec(head_quant=getattr(jal, head))
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=91)
+    assert cache.total_aligned_bytes() > spec.vocab_size * spec.hidden_dim * (2 if head == "F16" else 4)
+    run_parity(om, ctx, prompt_of(5), 16, 256)
+    run_fast(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(5), 16, 256)
+
+
 def test_llama4_irope_and_sliding_window(jal, oracle, torch_cuda):
     spec = jal.SynthSpec(architecture="llama4", num_layers=4)
     mask = [False, True, False, True]
