@@ -7,8 +7,8 @@
 // GEMV_IN_NORM) with non-finite values zeroed, as QuantizedActQ8 keeps it.
 //
 // Fast kernel: one CTA of 16 warps per SM over a contiguous row range; a
-// warp streams one row at a time in 16-byte chunks (kUnroll chunks per lane
-// in flight) against the activation in shared memory.  Reference-order
+// warp streams one row at a time in 16-byte chunks (64 elements per lane in
+// flight) against the activation in shared memory.  Reference-order
 // kernel: one thread per row, acc += w * x in column order without
 // contraction (eval_row_range's dense branch, repack_cache.rs:739-751).
 #include <cuda_fp16.h>
@@ -24,12 +24,14 @@ namespace jal {
 namespace {
 
 constexpr int kDenseWarps = 16;
-constexpr int kUnroll = 8;
 
 template <int QUANT>
 struct DenseElt {
   static constexpr int kBytes = QUANT == JAL_F32 ? 4 : 2;
   static constexpr int kPerChunk = 16 / kBytes;  // elements per 16-byte chunk
+  // chunks in flight per lane: 64 elements either way (measured on the
+  // 128256x4096 head: 4.8 TB/s for F16 with 8, 5.1 TB/s for F32 with 16)
+  static constexpr int kUnroll = QUANT == JAL_F32 ? 16 : 8;
   __device__ static float at(const void *p, int64_t i) {
     if (QUANT == JAL_F32) return sanitize_weight(((const float *)p)[i]);
     if (QUANT == JAL_F16) return f16_finite(((const uint16_t *)p)[i]);
@@ -91,15 +93,15 @@ __global__ void __launch_bounds__(kDenseWarps * 32, 1) k_gemv_dense(const GemvAr
   for (int64_t r = r0 + warp; r < r0 + cnt; r += kDenseWarps) {
     const uint4 *row = (const uint4 *)((const char *)a.w.dense + r * cols * E::kBytes);
     float acc = 0.0f;
-    for (int64_t c0 = lane; c0 < nch; c0 += 32 * kUnroll) {
-      uint4 v[kUnroll];
+    for (int64_t c0 = lane; c0 < nch; c0 += 32 * E::kUnroll) {
+      uint4 v[E::kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; u++) {
+      for (int u = 0; u < E::kUnroll; u++) {
         const int64_t c = c0 + 32 * u;
         v[u] = c < nch ? ldg_stream16(row + c) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int u = 0; u < kUnroll; u++) {
+      for (int u = 0; u < E::kUnroll; u++) {
         const int64_t c = c0 + 32 * u;
         if (c < nch) acc = E::dot(v[u], xs + c * E::kPerChunk, acc);
       }
