@@ -134,10 +134,15 @@ int jal_quantize_row_q8_0(const float *x, size_t n, void *blocks,
  * decode_gemv.rs / dispatch.rs -- streaming raw-GGUF GEMV
  * ====================================================================== */
 /* gemv_decode_projection (decode_gemv.rs:1395-1407) and
- * project_lm_head_row_split (dispatch.rs:191-289) for Q4_0/Q5_0/Q8_0 rows
- * in raw GGUF block order: y = W x with the BlockQ8_0 activation quantizer
- * and per-32-block f32(sumi) * (dw * dx) accumulation (decode_gemv.rs:
- * 394-439, 622-642).  raw: device pointer to rows*cols GGUF elements. */
+ * project_lm_head_row_split (dispatch.rs:191-289) for rows in raw GGUF block
+ * order: y = W x.  Q4_0/Q5_0/Q8_0: BlockQ8_0 activation quantizer and
+ * per-32-block f32(sumi) * (dw * dx) accumulation (decode_gemv.rs: 394-439,
+ * 622-642).  Q4_K/Q5_K/Q6_K/TQ1_0/TQ2_0: BlockQ8_K quantizer and the
+ * per-super-block integer sums (decode_gemv.rs:320-346, 456-620), blocks
+ * added in order (equal to the reference bit for bit).  F16/BF16/F32: the
+ * 256-element chunked f32 dot of dot_dense_row_zero_alloc
+ * (decode_gemv.rs:1081-1166), also bit-exact.  raw: device pointer to
+ * rows*cols GGUF elements. */
 int jal_gemv_decode_projection(const void *raw, size_t raw_len, int quant,
                                size_t rows, size_t cols, const float *x,
                                float *y, void *stream);

@@ -222,16 +222,30 @@ int jal_gemv_decode_projection(const void *raw, size_t raw_len, int quant, size_
     NEED(raw);
     NEED(x);
     NEED(y);
-    if (quant != JAL_Q4_0 && quant != JAL_Q5_0 && quant != JAL_Q8_0)
+    const bool q32 = quant == JAL_Q4_0 || quant == JAL_Q5_0 || quant == JAL_Q8_0;
+    const bool dense = quant == JAL_F16 || quant == JAL_BF16 || quant == JAL_F32;
+    if (!q32 && !dense && !superblock_quant(quant))
       fail(JAL_ERR_CAPABILITY_MISMATCH, "unsupported quantization %d for M=1 GEMV projection", quant);
     size_t rb = ggml_row_bytes((uint32_t)quant, cols);
-    if (!rb) fail(JAL_ERR_TENSOR_BOUNDS, "cols %zu must be a multiple of 32", cols);
+    if (!rb) fail(JAL_ERR_TENSOR_BOUNDS, "cols %zu must be a multiple of the type's block", cols);
     if (raw_len < rows * rb) fail(JAL_ERR_TENSOR_BOUNDS, "truncated weight buffer");
     if (rows == 0) return;
     cudaStream_t s = as_stream(stream);
-    DevBuffer xb(cols / 32 * 36);
-    launch_quantize_row_q8_0(x, (int64_t)cols, xb.ptr, s);
-    launch_gemv_raw((const uint8_t *)raw, quant, (int64_t)rows, (int64_t)cols, xb.ptr, y, s);
+    if (dense) {
+      launch_gemv_raw_dense((const uint8_t *)raw, quant, (int64_t)rows, (int64_t)cols, x, y, s);
+    } else if (q32) {
+      DevBuffer xb(cols / 32 * 36);
+      launch_quantize_row_q8_0(x, (int64_t)cols, xb.ptr, s);
+      launch_gemv_raw((const uint8_t *)raw, quant, (int64_t)rows, (int64_t)cols, xb.ptr, y, s);
+      JAL_CUDA(cudaGetLastError());
+      JAL_CUDA(cudaStreamSynchronize(s));  // before xb is freed
+    } else {
+      DevBuffer xb(cols / 256 * kQ8KBlockBytes);
+      launch_quantize_row_q8_k(x, (int64_t)cols, xb.ptr, s);
+      launch_gemv_raw_superblock((const uint8_t *)raw, quant, (int64_t)rows, (int64_t)cols, xb.ptr, y, s);
+      JAL_CUDA(cudaGetLastError());
+      JAL_CUDA(cudaStreamSynchronize(s));  // before xb is freed
+    }
     JAL_CUDA(cudaGetLastError());
     JAL_CUDA(cudaStreamSynchronize(s));
   });

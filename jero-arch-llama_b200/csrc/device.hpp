@@ -123,6 +123,16 @@ void launch_dot16_partials(const DevMat &w, const int8_t *q8, int64_t r0, int64_
                            cudaStream_t s);
 void launch_gemv_raw(const uint8_t *raw, int quant, int64_t rows, int64_t cols, const void *xblocks,
                      float *y, cudaStream_t s);
+// Streaming GEMV of the super-block types (Q4_K, Q5_K, Q6_K, TQ1_0, TQ2_0)
+// against BlockQ8_K activations (kQ8KBlockBytes per 256 elements), and of
+// dense F16 / BF16 / F32 rows against the f32 activation (stream_gemv.cu).
+constexpr int kQ8KBlockBytes = 304;
+bool superblock_quant(int q);
+void launch_quantize_row_q8_k(const float *x, int64_t n, void *blocks, cudaStream_t s);
+void launch_gemv_raw_superblock(const uint8_t *raw, int quant, int64_t rows, int64_t cols, const void *xblocks,
+                                float *y, cudaStream_t s);
+void launch_gemv_raw_dense(const uint8_t *raw, int quant, int64_t rows, int64_t cols, const float *x, float *y,
+                           cudaStream_t s);
 
 // ---- GEMM (prefill) -------------------------------------------------------
 // y[m][rows] (= or +=) q8[m][K] x W^T with per-16-chunk integer partials.

@@ -177,6 +177,72 @@ def test_streaming_raw_gemv_decode_projection(jal, oracle, torch_cuda, quant_nam
     assert rel_err(y.cpu().numpy(), oracle.gemv_decode_projection(raw, quant, rows, cols, x)) <= REL_TOL
 
 
+def _raw_superblock_rows(jal, quant, rows, cols, seed):
+    """Random super-block rows (quant bytes uniform) with scale fields drawn
+    as f16 / bf16 of small normal values; the first block of row 0 gets an
+    Inf scale (sanitised to 0.0625 by the kernels)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    bb = {jal.Q4_K: 144, jal.Q5_K: 176, jal.Q6_K: 210, jal.TQ1_0: 54, jal.TQ2_0: 66}[quant]
+    nb = cols // 256
+    blk = rng.integers(0, 256, size=(rows, nb, bb), dtype=np.uint8)
+    def put16(off, vals):
+        blk[:, :, off:off + 2] = vals.astype("<u2").view(np.uint8).reshape(rows, nb, 2)
+    f16 = lambda sd: rng.normal(0, sd, (rows, nb)).astype(np.float16).view(np.uint16)
+    if quant in (jal.Q4_K, jal.Q5_K):
+        put16(0, f16(1e-3)); put16(2, f16(1e-3))
+    elif quant == jal.Q6_K:
+        put16(208, f16(1e-3))
+    elif quant == jal.TQ1_0:
+        put16(0, f16(1e-2))
+    else:  # TQ2_0: bf16 scale
+        put16(64, (rng.normal(0, 1e-2, (rows, nb)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16))
+    off = {jal.Q4_K: 0, jal.Q5_K: 0, jal.Q6_K: 208, jal.TQ1_0: 0, jal.TQ2_0: 64}[quant]
+    blk[0, 0, off:off + 2] = (0x00, 0x7C) if quant != jal.TQ2_0 else (0x80, 0x7F)
+    return blk.reshape(-1)
+
+
+def _raw_dense_rows(jal, quant, rows, cols, seed):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    w = rng.normal(0, 0.02, (rows, cols)).astype(np.float32)
+    if quant == jal.F32:
+        w[0, 3] = np.inf
+        return w.view(np.uint8).reshape(-1)
+    if quant == jal.F16:
+        h = w.astype(np.float16).view(np.uint16)
+        h[0, 3] = 0x7C00
+    else:
+        h = (w.view(np.uint32) >> 16).astype(np.uint16)
+        h[0, 3] = 0x7F80
+    return h.view(np.uint8).reshape(-1)
+
+
+@pytest.mark.parametrize("quant_name", ["Q4_K", "Q5_K", "Q6_K", "TQ1_0", "TQ2_0", "F16", "BF16", "F32"])
+def test_streaming_raw_gemv_superblock_and_dense_bit_exact(jal, oracle, torch_cuda, quant_name):
+    # gemv_decode_projection for the super-block types (BlockQ8_K activation)
+    # and dense rows: the device adds the per-block results in the
+    # reference's order, so every output equals the oracle's bit for bit.
+    # The second activation carries a NaN and an Inf (zeroed by the
+    # quantizer / the dense chunk mask); dense rows use 4000 columns so that
+    # the last 256-element chunk is partial.
+    torch = torch_cuda
+    quant = getattr(jal, quant_name)
+    dense = quant in (jal.F16, jal.BF16, jal.F32)
+    rows, cols = 1500, (4000 if dense else 4096)
+    raw = (_raw_dense_rows if dense else _raw_superblock_rows)(jal, quant, rows, cols, 31)
+    for k, x in enumerate([jal.synth_normal(cols, seed=32, name="stream.act"),
+                           jal.synth_normal(cols, seed=33, name="stream.act2")]):
+        if k == 1:
+            x[7], x[300] = np.nan, np.inf
+        y = torch.zeros(rows, dtype=torch.float32, device="cuda")
+        jal.gemv_decode_projection(dev(torch, raw), raw.nbytes, quant, rows, cols, dev(torch, x), y)
+        torch.cuda.synchronize()
+        want = oracle.gemv_decode_projection(raw, quant, rows, cols, x)
+        got = y.cpu().numpy()
+        assert np.all(np.isfinite(want))
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+            f"{int(np.sum(got != want))} rows differ, max |d| {np.max(np.abs(got - want)):.3e}"
+
+
 def test_unsupported_quant_fails_closed(jal, torch_cuda):
     with pytest.raises(jal.CapabilityMismatch):
         jal.CachedMatrix.repack(np.zeros(84, np.uint8), 10, 1, 256)
