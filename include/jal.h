@@ -136,8 +136,8 @@ int jal_quantize_row_q8_0(const float *x, size_t n, void *blocks,
 /* gemv_decode_projection (decode_gemv.rs:1395-1407) and
  * project_lm_head_row_split (dispatch.rs:191-289) for rows in raw GGUF block
  * order: y = W x.  Q4_0/Q5_0/Q8_0: BlockQ8_0 activation quantizer and
- * per-32-block f32(sumi) * (dw * dx) accumulation (decode_gemv.rs: 394-439,
- * 622-642).  Q4_K/Q5_K/Q6_K/TQ1_0/TQ2_0: BlockQ8_K quantizer and the
+ * per-32-block f32(sumi) * (dw * dx) accumulation in block order
+ * (decode_gemv.rs: 394-439, 622-642; bit-exact).  Q4_K/Q5_K/Q6_K/TQ1_0/TQ2_0: BlockQ8_K quantizer and the
  * per-super-block integer sums (decode_gemv.rs:320-346, 456-620), blocks
  * added in order (equal to the reference bit for bit).  F16/BF16/F32: the
  * 256-element chunked f32 dot of dot_dense_row_zero_alloc

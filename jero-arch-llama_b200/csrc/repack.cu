@@ -276,40 +276,51 @@ void launch_dot16_partials(const DevMat &w, const int8_t *q8, int64_t r0, int64_
 // ---- streaming raw-GGUF GEMV (decode_gemv.rs:394-439, 622-642) -----------
 // One warp per row; each lane takes whole 32-blocks; per-block term
 // f32(sumi) * (dw * dx) with the reference's zero short-circuit.
+// Lane l evaluates blocks l, l + 32, ...; the block results are added in
+// block order through shuffles, so each output equals run_gemv's sequential
+// sum (decode_gemv.rs:622-642) bit for bit.
 __global__ void k_gemv_raw(const uint8_t *__restrict__ raw, int quant, int64_t rows, int64_t cols,
                            const uint8_t *__restrict__ xb, float *__restrict__ y) {
   int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
   int lane = threadIdx.x % 32;
-  if (row >= rows) return;
+  if (row >= rows) return;  // whole warps leave together
   int64_t nb = cols / 32, bb = quant == JAL_Q4_0 ? 18 : quant == JAL_Q5_0 ? 22 : 34;
   const uint8_t *rp = raw + row * nb * bb;
   float acc = 0.0f;
-  for (int64_t b = lane; b < nb; b += 32) {
-    const uint8_t *w = rp + b * bb;
-    const uint8_t *xbk = xb + b * 36;
-    float dx = *(const float *)xbk;
-    const int8_t *xq = (const int8_t *)(xbk + 4);
-    float dw = f16_finite((uint16_t)(w[0] | (w[1] << 8)));
-    if (dw == 0.0f || dx == 0.0f) continue;
-    int32_t sumi = 0;
-    if (quant == JAL_Q4_0) {
-      for (int i = 0; i < 16; i++) {
-        int32_t q0 = (int32_t)(w[2 + i] & 15) - 8, q1 = (int32_t)(w[2 + i] >> 4) - 8;
-        sumi += q0 * xq[i] + q1 * xq[i + 16];
+  for (int64_t b0 = 0; b0 < nb; b0 += 32) {
+    const int64_t b = b0 + lane;
+    float t = 0.0f;
+    if (b < nb) {
+      const uint8_t *w = rp + b * bb;
+      const uint8_t *xbk = xb + b * 36;
+      float dx = *(const float *)xbk;
+      const int8_t *xq = (const int8_t *)(xbk + 4);
+      float dw = f16_finite((uint16_t)(w[0] | (w[1] << 8)));
+      if (dw != 0.0f && dx != 0.0f) {
+        int32_t sumi = 0;
+        if (quant == JAL_Q4_0) {
+          for (int i = 0; i < 16; i++) {
+            int32_t q0 = (int32_t)(w[2 + i] & 15) - 8, q1 = (int32_t)(w[2 + i] >> 4) - 8;
+            sumi += q0 * xq[i] + q1 * xq[i + 16];
+          }
+        } else if (quant == JAL_Q5_0) {
+          uint32_t qh = (uint32_t)w[2] | ((uint32_t)w[3] << 8) | ((uint32_t)w[4] << 16) | ((uint32_t)w[5] << 24);
+          for (int j = 0; j < 16; j++) {
+            int32_t h0 = (int32_t)(((qh >> j) & 1u) << 4), h1 = (int32_t)(((qh >> (j + 16)) & 1u) << 4);
+            int32_t q0 = ((int32_t)(w[6 + j] & 15) | h0) - 16, q1 = ((int32_t)(w[6 + j] >> 4) | h1) - 16;
+            sumi += q0 * xq[j] + q1 * xq[j + 16];
+          }
+        } else {
+          for (int i = 0; i < 32; i++) sumi += (int32_t)(int8_t)w[2 + i] * xq[i];
+        }
+        t = __fmul_rn((float)sumi, __fmul_rn(dw, dx));
       }
-    } else if (quant == JAL_Q5_0) {
-      uint32_t qh = (uint32_t)w[2] | ((uint32_t)w[3] << 8) | ((uint32_t)w[4] << 16) | ((uint32_t)w[5] << 24);
-      for (int j = 0; j < 16; j++) {
-        int32_t h0 = (int32_t)(((qh >> j) & 1u) << 4), h1 = (int32_t)(((qh >> (j + 16)) & 1u) << 4);
-        int32_t q0 = ((int32_t)(w[6 + j] & 15) | h0) - 16, q1 = ((int32_t)(w[6 + j] >> 4) | h1) - 16;
-        sumi += q0 * xq[j] + q1 * xq[j + 16];
-      }
-    } else {
-      for (int i = 0; i < 32; i++) sumi += (int32_t)(int8_t)w[2 + i] * xq[i];
     }
-    acc += __fmul_rn((float)sumi, __fmul_rn(dw, dx));
+    for (int k = 0; k < 32; k++) {
+      const float v = __shfl_sync(0xffffffffu, t, k);
+      if (b0 + k < nb) acc = __fadd_rn(acc, v);
+    }
   }
-  acc = warp_sum(acc);
   if (lane == 0) y[row] = acc;
 }
 
