@@ -352,9 +352,11 @@ def main():
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_dec, t_prefill = float(tt[0]), float(tt[1])
     # End to end through the C ABI with host buffers: per step the token goes
-    # up from pinned memory and the full logits row comes back.
+    # up from pinned memory and the full logits row comes back into a
+    # page-locked host array that the caller reuses.
     pos0 = ctx.position()
-    t_e2e = ev_time(torch, lambda: [ctx.decode_step(tok) for _ in range(args.steps)], stream)
+    host_logits = torch.empty(spec.vocab_size, dtype=torch.float32).pin_memory().numpy()
+    t_e2e = ev_time(torch, lambda: [ctx.decode_step(tok, out=host_logits) for _ in range(args.steps)], stream)
     if dist:
         tt = torch.tensor([t_e2e], dtype=torch.float64, device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)

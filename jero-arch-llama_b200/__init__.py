@@ -591,10 +591,20 @@ class ExecutionContext:
                                       self.vocab if logits is not None else 0))
         return logits
 
-    def decode_step(self, token: int, want_logits: bool = True):
-        """decode_step_with_cache (recipe.rs:555): logits of the new position (numpy) or None."""
+    def decode_step(self, token: int, want_logits: bool = True, out=None):
+        """decode_step_with_cache (recipe.rs:555): logits of the new position (numpy) or None.
+
+        `out`: a C-contiguous float32 numpy array of vocab length to receive
+        the logits (returned); a caller that reuses one page-locked array
+        (e.g. ``torch.empty(vocab).pin_memory().numpy()``) avoids a pageable
+        copy and a fresh allocation per step."""
         import numpy as np
-        logits = np.zeros(self.vocab, dtype=np.float32) if want_logits else None
+        if out is not None:
+            if out.dtype != np.float32 or out.shape != (self.vocab,) or not out.flags["C_CONTIGUOUS"]:
+                raise ValueError("out must be a contiguous float32 array of vocab length")
+            logits = out
+        else:
+            logits = np.zeros(self.vocab, dtype=np.float32) if want_logits else None
         _check(lib().jal_decode_step(self._h, token, logits.ctypes.data if logits is not None else None,
                                      self.vocab if logits is not None else 0))
         return logits

@@ -279,3 +279,25 @@ def test_persistent_decode_kernel_matches_oracle(jal, oracle, torch_cuda, monkey
     seq = ctx_greedy.decode_greedy(first, 32)
     assert [first] + [int(t) for t in seq[:-1]] == host
     assert ctx_greedy.position() == len(prompt) + 32
+
+
+def test_decode_step_into_caller_buffer(jal, torch_cuda):
+    # decode_step(out=...) writes the same logits into a reused page-locked
+    # array as into a fresh one.
+    torch = torch_cuda
+    spec = jal.TINY_LLAMA
+    buf = jal.synth_gguf(spec, 3)
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    cache = recipe.build_repack_cache(buf)
+    a = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST)
+    b = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST)
+    p = prompt_of(4)
+    a.prefill_step(p, 0)
+    b.prefill_step(p, 0)
+    host = torch.empty(spec.vocab_size, dtype=torch.float32).pin_memory().numpy()
+    for tok in (5, 77, 1024):
+        want = a.decode_step(tok)
+        got = b.decode_step(tok, out=host)
+        assert got is host and np.array_equal(got, want)
+    with pytest.raises(ValueError):
+        b.decode_step(1, out=np.zeros(3, np.float32))
