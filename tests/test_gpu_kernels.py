@@ -119,7 +119,7 @@ def test_quantize_row_q8_0_bit_exact(jal, oracle, torch_cuda):
     assert np.array_equal(blocks.cpu().numpy(), oracle.quantize_row_q8_0(x))
 
 
-@pytest.mark.parametrize("m", [2, 3, 4, 8, 37])
+@pytest.mark.parametrize("m", [2, 3, 4, 8, 37, 200])
 @pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
 def test_small_batch_gemv_and_gemm(jal, oracle, torch_cuda, m, quant_name):
     torch = torch_cuda
