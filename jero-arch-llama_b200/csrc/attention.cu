@@ -513,6 +513,158 @@ __global__ void __launch_bounds__(128) k_attn_prefill(const AttnPrefillArgs a) {
   }
 }
 
+// ---- prefill: causal flash attention on the tensor cores (f16 KV) --------
+// CTA = (query head, 64-query tile), 4 warps of 16 queries.  Per 64-key tile
+// K (row-major) and V (transposed) are staged in shared memory as f16; S =
+// Q K^T and O += P V run as mma.sync m16n8k16 f16 x f16 -> f32, with Q and
+// P rounded to f16 (K and V already are, in an f16 cache) and the online
+// softmax, scale and masks in f32.  Fragments (g = lane / 4, q = lane % 4):
+// A regs (row g, k 2q..2q+1), (g + 8, 2q..), (g, 2q + 8..), (g + 8, 2q + 8..);
+// B regs (k 2q..2q+1, col g), (2q + 8.., g); C (row g, cols 2q, 2q + 1),
+// (g + 8, ...).  The S accumulator of key tiles 2t, 2t + 1 is the P operand
+// of k-step t as it lies in registers.
+constexpr int kFQ = 64, kFK = 64;
+
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_prefill_mma(const AttnPrefillArgs a) {
+  constexpr int KS = HD / 16, NO = HD / 8, NK = kFK / 8;
+  constexpr int KSTR = HD + 8, VSTR = kFK + 8;  // padded rows (halves): conflict-free fragment loads
+  __shared__ __align__(16) __half k_s[kFK * KSTR];
+  __shared__ __align__(16) __half vt_s[HD * VSTR];
+  const int hq = blockIdx.x, tid = threadIdx.x, warp = tid / 32, lane = tid % 32, g = lane / 4, q = lane % 4;
+  const int64_t G = a.n_heads_q / a.kv.n_kv, hkv = hq / G;
+  const int64_t q0 = (int64_t)blockIdx.y * kFQ;
+  const int64_t nq = a.m - q0 < kFQ ? a.m - q0 : kFQ;
+  const int r0 = warp * 16 + g, r1 = r0 + 8;  // this lane's two query rows in the tile
+  const bool v0 = r0 < nq, v1 = r1 < nq;
+  const int64_t p0 = a.start_pos + q0 + r0, p1 = p0 + 8;
+  uint32_t qf[KS][4];
+  {
+    const float *q0p = a.qkv + (q0 + (v0 ? r0 : 0)) * a.qkv_stride + (int64_t)hq * HD;
+    const float *q1p = a.qkv + (q0 + (v1 ? r1 : 0)) * a.qkv_stride + (int64_t)hq * HD;
+#pragma unroll
+    for (int s = 0; s < KS; s++) {
+      const int d = 16 * s + 2 * q;
+      qf[s][0] = v0 ? pack_h2(q0p[d], q0p[d + 1]) : 0u;
+      qf[s][1] = v1 ? pack_h2(q1p[d], q1p[d + 1]) : 0u;
+      qf[s][2] = v0 ? pack_h2(q0p[d + 8], q0p[d + 9]) : 0u;
+      qf[s][3] = v1 ? pack_h2(q1p[d + 8], q1p[d + 9]) : 0u;
+    }
+  }
+  const int64_t last_pos = a.start_pos + q0 + nq - 1, first_pos = a.start_pos + q0;
+  int64_t kbeg = 0;
+  if (a.window > 0 && first_pos + 1 > a.window) kbeg = first_pos + 1 - a.window;
+  kbeg = kbeg / kFK * kFK;
+  float o[NO][4];
+#pragma unroll
+  for (int n = 0; n < NO; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  for (int64_t k0 = kbeg; k0 <= last_pos; k0 += kFK) {
+    __syncthreads();
+    for (int i = tid; i < kFK * HD / 8; i += 128) {
+      const int r = i / (HD / 8), c8 = i % (HD / 8);
+      const int64_t pos = k0 + r;
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (pos <= last_pos) {
+        const int64_t e = kv_elem(a.kv, a.layer, hkv, pos) + c8 * 8;
+        kv = *(const uint4 *)((const __half *)a.kv.k + e);
+        vv = *(const uint4 *)((const __half *)a.kv.v + e);
+      }
+      *(uint4 *)&k_s[r * KSTR + c8 * 8] = kv;
+      const __half *vh = reinterpret_cast<const __half *>(&vv);
+#pragma unroll
+      for (int j = 0; j < 8; j++) vt_s[(c8 * 8 + j) * VSTR + r] = vh[j];
+    }
+    __syncthreads();
+    // Skip the tile only when it is masked for every lane: mma.sync needs the
+    // whole warp, so the decision must be warp-uniform.
+    if (__all_sync(0xffffffffu, k0 > p1 || (!v0 && !v1))) continue;
+    float sc[NK][4];
+#pragma unroll
+    for (int j = 0; j < NK; j++) {
+      sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+      const __half *kr = k_s + (8 * j + g) * KSTR + 2 * q;
+#pragma unroll
+      for (int s = 0; s < KS; s++)
+        mma_f16_16816(sc[j], qf[s], *(const uint32_t *)(kr + 16 * s), *(const uint32_t *)(kr + 16 * s + 8));
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NK; j++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int64_t key = k0 + 8 * j + 2 * q + (i & 1);
+        const int64_t qp = i < 2 ? p0 : p1;
+        const bool ok = (i < 2 ? v0 : v1) && key <= qp && (a.window <= 0 || key + a.window > qp);
+        const float v = ok ? __fmul_rn(sc[j][i], a.scale) : -INFINITY;
+        sc[j][i] = v;
+        if (i < 2) mx0 = fmaxf(mx0, v);
+        else mx1 = fmaxf(mx1, v);
+      }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float al0 = m0 == -INFINITY ? 0.0f : expf(m0 - n0), al1 = m1 == -INFINITY ? 0.0f : expf(m1 - n1);
+    m0 = n0;
+    m1 = n1;
+    float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NK; j++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float p = sc[j][i] == -INFINITY ? 0.0f : expf(sc[j][i] - (i < 2 ? n0 : n1));
+        sc[j][i] = p;
+        if (i < 2) ps0 += p;
+        else ps1 += p;
+      }
+    l0 = l0 * al0 + ps0;  // this lane's keys; the quad is summed at the end
+    l1 = l1 * al1 + ps1;
+#pragma unroll
+    for (int n = 0; n < NO; n++) {
+      o[n][0] *= al0; o[n][1] *= al0;
+      o[n][2] *= al1; o[n][3] *= al1;
+    }
+#pragma unroll
+    for (int t = 0; t < kFK / 16; t++) {
+      const uint32_t pa[4] = {pack_h2(sc[2 * t][0], sc[2 * t][1]), pack_h2(sc[2 * t][2], sc[2 * t][3]),
+                              pack_h2(sc[2 * t + 1][0], sc[2 * t + 1][1]), pack_h2(sc[2 * t + 1][2], sc[2 * t + 1][3])};
+#pragma unroll
+      for (int n = 0; n < NO; n++) {
+        const __half *vr = vt_s + (8 * n + g) * VSTR + 16 * t + 2 * q;
+        mma_f16_16816(o[n], pa, *(const uint32_t *)vr, *(const uint32_t *)(vr + 8));
+      }
+    }
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float i0 = l0 > 0.0f ? __fdiv_rn(1.0f, l0) : 0.0f, i1 = l1 > 0.0f ? __fdiv_rn(1.0f, l1) : 0.0f;
+  const int64_t ostride = a.n_heads_q * HD;
+  float *out0 = a.out + (q0 + r0) * ostride + (int64_t)hq * HD + 2 * q;
+  float *out1 = a.out + (q0 + r1) * ostride + (int64_t)hq * HD + 2 * q;
+#pragma unroll
+  for (int n = 0; n < NO; n++) {
+    if (v0) { out0[8 * n] = o[n][0] * i0; out0[8 * n + 1] = o[n][1] * i0; }
+    if (v1) { out1[8 * n] = o[n][2] * i1; out1[8 * n + 1] = o[n][3] * i1; }
+  }
+}
+
 }  // namespace
 
 void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s) {
@@ -569,6 +721,12 @@ void launch_rope_append(const RopeAppendArgs &a, cudaStream_t s) {
 
 void launch_attn_prefill(const AttnPrefillArgs &a, cudaStream_t s) {
   if (!a.m) return;
+  if (a.kv.f16 && (a.kv.head_dim == 128 || a.kv.head_dim == 64)) {  // tensor cores
+    dim3 g2((unsigned)a.n_heads_q, (unsigned)((a.m + kFQ - 1) / kFQ));
+    if (a.kv.head_dim == 128) k_attn_prefill_mma<128><<<g2, 128, 0, s>>>(a);
+    else k_attn_prefill_mma<64><<<g2, 128, 0, s>>>(a);
+    return;
+  }
   dim3 grid((unsigned)a.n_heads_q, (unsigned)((a.m + kPQ - 1) / kPQ));
   auto go = [&](auto kern, int hd) {
     size_t smem = (size_t)(kPQ * hd + kPK * (hd + 1) + kPK * hd + kPQ * kPK) * sizeof(float);

@@ -301,3 +301,25 @@ def test_decode_step_into_caller_buffer(jal, torch_cuda):
         assert got is host and np.array_equal(got, want)
     with pytest.raises(ValueError):
         b.decode_step(1, out=np.zeros(3, np.float32))
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_long_prompt_f16_kv_prefill_attention(jal, oracle, torch_cuda, head_dim):
+    # A 200-token prompt with an f16 cache runs the tensor-core prefill
+    # attention over several 64-query and 64-key tiles: whole prompt, the
+    # same prompt in two chunks (keys of the first chunk read back from the
+    # cache), and a 40-token sliding window, all against the oracle with the
+    # fast-numerics bars.
+    spec = jal.SynthSpec(n_heads_q=512 // head_dim, n_heads_kv=max(1, 128 // head_dim), head_dim=head_dim)
+    p = prompt_of(9, n=200)
+    _, om, recipe, cache, _ = make(jal, oracle, spec, seed=61)
+    run_fast(om, new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST), p, 8, 256)
+    kvo = om.new_kv(256)
+    lo = om.prefill(kvo, 256, p, 0)
+    ctx = new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
+    ctx.prefill_step(p[:130], 0)
+    lg = ctx.prefill_step(p[130:], 130)
+    assert float(np.max(np.abs(lo - lg))) <= FAST_MAX_ATOL
+    _, omw, recipe_w, cache_w, _ = make(jal, oracle, spec, seed=61, sliding_window=40)
+    run_fast(omw, new_ctx(jal, recipe_w, cache_w, kv_dtype=jal.KV_F16, sliding_window=40,
+                          numerics=jal.NUMERICS_FAST), p, 8, 256)
