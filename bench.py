@@ -226,7 +226,9 @@ def profile_mode(args):
       decode - Llama-3-8B Q4_0, 32-token prompt, two decode steps between
                cudaProfilerStart / Stop;
       attn   - the same attention geometry with 2 layers, a --prefill prompt
-               and one decode step between cudaProfilerStart / Stop."""
+               and one decode step between cudaProfilerStart / Stop;
+      prefill - the 2-layer model, a --prefill-token prompt prefilled once
+               to warm up, then again between cudaProfilerStart / Stop."""
     import dataclasses
 
     import numpy as np
@@ -250,6 +252,22 @@ def profile_mode(args):
         return 0
     spec = jal.LLAMA3_8B_Q4_0
     n_prompt, n_steps = 32, 2
+    if args.profile == "prefill":
+        spec = dataclasses.replace(spec, num_layers=2)
+        gguf = jal.synth_gguf(spec, SEED)
+        recipe = jal.LlamaRecipe.from_gguf(gguf)
+        cache = recipe.build_repack_cache(gguf)
+        ctx = jal.ExecutionContext(recipe, cache, n_ctx=args.prefill + 64, kv_dtype=jal.KV_F16)
+        ctx.set_stream(stream)
+        prompt = np.random.Generator(np.random.PCG64(SEED)).integers(0, spec.vocab_size, args.prefill).astype(np.uint32)
+        ctx.prefill_step(prompt, 0)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        ctx.prefill_step(prompt, 0)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print("profile prefill ok")
+        return 0
     if args.profile == "attn":
         spec = dataclasses.replace(spec, num_layers=2)
         n_prompt, n_steps = args.prefill, 1
@@ -283,7 +301,7 @@ def main():
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1 ranks: one tensor-parallel model over the N GPUs (strong scaling) "
                          "instead of N independent replicas")
-    ap.add_argument("--profile", choices=["gemv", "decode", "attn"],
+    ap.add_argument("--profile", choices=["gemv", "decode", "attn", "prefill"],
                     help="run a small fixed workload for ncu instead of the benchmark")
     args = ap.parse_args()
     if args.profile:
