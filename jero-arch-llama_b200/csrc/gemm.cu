@@ -8,7 +8,8 @@
 // block is exact (|dot32| < 2^24).
 //
 // CTA tile: 128 tokens x 128 rows, 8 warps, K staged 4 blocks (128
-// elements) at a time in shared memory.  Warp w computes tokens
+// elements) at a time in shared memory, two stages alternating: the next
+// stage's blocks are in flight (cp.async) while the current one is used.  Warp w computes tokens
 // 16w..16w+15 against the 128 rows as 16 n-tiles of 8 rows, one MMA per
 // block and n-tile.  MMA
 // fragments (PTX m16n8k32 .s8, g = lane / 4, q = lane % 4): A (tokens x 32,
@@ -40,13 +41,27 @@ __device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t 
 // Four nibbles 0..15 (one per byte) to signed bytes n - 8.
 __device__ __forceinline__ uint32_t nib_s8(uint32_t v) { return ((v | 0x80808080u) - 0x08080808u) ^ 0x80808080u; }
 
+// One K stage of the CTA tile in shared memory (two of them alternate).
+template <int WB>
+struct GemmStage {
+  uint8_t w[KB][BN][WB];  // weight blocks, rows 16-byte aligned
+  int8_t x[KB][BM][32];   // activation blocks
+  float wd[KB][BN];       // weight block scales
+  float as[KB][BM];       // activation block scales
+};
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(valid ? 16 : 0) : "memory");
+}
+
 template <int QUANT>
 __global__ void __launch_bounds__(kThreads) k_gemm(const GemmArgs a) {
   constexpr int WB = QUANT == JAL_Q4_0 ? 16 : 32;  // weight bytes per block
-  __shared__ __align__(16) uint8_t w_s[KB][BN][WB];
-  __shared__ float wd_s[KB][BN];
-  __shared__ __align__(16) int8_t x_s[KB][BM][32];
-  __shared__ float as_s[KB][BM];
+  constexpr int NSW = KB * BN / kThreads, NSA = KB * BM / kThreads;  // scales per thread per stage
+  using Stage = GemmStage<WB>;
+  extern __shared__ __align__(16) char gsm[];
+  Stage *st = reinterpret_cast<Stage *>(gsm);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32, g = lane / 4, q = lane % 4;
   const int64_t t0 = (int64_t)blockIdx.y * BM, r0 = (int64_t)blockIdx.x * BN;
   const int64_t K = a.w.cols, nb = K / 32;
@@ -56,64 +71,96 @@ __global__ void __launch_bounds__(kThreads) k_gemm(const GemmArgs a) {
 #pragma unroll
     for (int i = 0; i < 4; i++) acc[n][i] = 0.0f;
 
-  for (int64_t b0 = 0; b0 < nb; b0 += KB) {
-    __syncthreads();
-    // Weights: KB blocks x 64 rows.
+  // Quant and activation blocks of a stage go to shared memory by cp.async
+  // (zero-filled outside the matrix); the scales pass through registers.
+  auto issue = [&](Stage &sb, int64_t b0) {
     for (int i = tid; i < KB * BN * (WB / 16); i += kThreads) {
-      int piece = i % (WB / 16), rr = (i / (WB / 16)) % BN, kb = i / (WB / 16) / BN;
-      int64_t r = r0 + rr, b = b0 + kb;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (r < a.rows && b < nb) v = *(const uint4 *)(a.w.qs + r * a.w.qs_stride + b * WB + piece * 16);
-      *(uint4 *)&w_s[kb][rr][piece * 16] = v;
+      const int piece = i % (WB / 16), rr = (i / (WB / 16)) % BN, kb = i / (WB / 16) / BN;
+      const int64_t r = r0 + rr, b = b0 + kb;
+      const bool ok = r < a.rows && b < nb;
+      cp_async16(&sb.w[kb][rr][piece * 16], ok ? a.w.qs + r * a.w.qs_stride + b * WB + piece * 16 : a.w.qs, ok);
     }
-    for (int i = tid; i < KB * BN; i += kThreads) {
-      int rr = i % BN, kb = i / BN;
-      int64_t r = r0 + rr, b = b0 + kb;
-      wd_s[kb][rr] = (r < a.rows && b < nb) ? f16_finite(a.w.d[r * a.w.d_stride + b]) : 0.0f;
-    }
-    // Activations: KB blocks x 64 tokens, and their block scales.
     for (int i = tid; i < KB * BM * 2; i += kThreads) {
-      int half = i % 2, tt = (i / 2) % BM, kb = i / 2 / BM;
-      int64_t t = t0 + tt, b = b0 + kb;
-      int4 v = make_int4(0, 0, 0, 0);
-      if (t < a.m && b < nb) v = *(const int4 *)(a.xq + t * K + b * 32 + half * 16);
-      *(int4 *)&x_s[kb][tt][half * 16] = v;
+      const int half = i % 2, tt = (i / 2) % BM, kb = i / 2 / BM;
+      const int64_t t = t0 + tt, b = b0 + kb;
+      const bool ok = t < a.m && b < nb;
+      cp_async16(&sb.x[kb][tt][half * 16], ok ? a.xq + t * K + b * 32 + half * 16 : a.xq, ok);
     }
-    for (int i = tid; i < KB * BM; i += kThreads) {
-      int tt = i % BM, kb = i / BM;
-      int64_t t = t0 + tt, b = b0 + kb;
-      as_s[kb][tt] = (t < a.m && b < nb) ? a.xs[t * nb + b] : 0.0f;
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float wreg[NSW], areg[NSA];
+  auto load_scales = [&](int64_t b0) {
+#pragma unroll
+    for (int j = 0; j < NSW; j++) {
+      const int i = tid + j * kThreads, rr = i % BN, kb = i / BN;
+      const int64_t r = r0 + rr, b = b0 + kb;
+      wreg[j] = (r < a.rows && b < nb) ? f16_finite(a.w.d[r * a.w.d_stride + b]) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < NSA; j++) {
+      const int i = tid + j * kThreads, tt = i % BM, kb = i / BM;
+      const int64_t t = t0 + tt, b = b0 + kb;
+      areg[j] = (t < a.m && b < nb) ? a.xs[t * nb + b] : 0.0f;
+    }
+  };
+  auto store_scales = [&](Stage &sb) {
+#pragma unroll
+    for (int j = 0; j < NSW; j++) {
+      const int i = tid + j * kThreads;
+      sb.wd[i / BN][i % BN] = wreg[j];
+    }
+#pragma unroll
+    for (int j = 0; j < NSA; j++) {
+      const int i = tid + j * kThreads;
+      sb.as[i / BM][i % BM] = areg[j];
+    }
+  };
+
+  const int64_t nst = (nb + KB - 1) / KB;
+  issue(st[0], 0);
+  load_scales(0);
+  store_scales(st[0]);
+  for (int64_t sidx = 0; sidx < nst; sidx++) {
+    Stage &cur = st[sidx & 1];
+    if (sidx + 1 < nst) {  // the other buffer was last read before the previous barrier
+      issue(st[(sidx + 1) & 1], (sidx + 1) * KB);
+      load_scales((sidx + 1) * KB);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
 #pragma unroll
     for (int kb = 0; kb < KB; kb++) {
       const int ta = warp * 16 + g;  // tokens ta and ta + 8
-      const uint32_t alo0 = *(const uint32_t *)&x_s[kb][ta][4 * q];
-      const uint32_t alo1 = *(const uint32_t *)&x_s[kb][ta + 8][4 * q];
-      const uint32_t ahi0 = *(const uint32_t *)&x_s[kb][ta][16 + 4 * q];
-      const uint32_t ahi1 = *(const uint32_t *)&x_s[kb][ta + 8][16 + 4 * q];
-      const float as0 = as_s[kb][ta], as1 = as_s[kb][ta + 8];
+      const uint32_t alo0 = *(const uint32_t *)&cur.x[kb][ta][4 * q];
+      const uint32_t alo1 = *(const uint32_t *)&cur.x[kb][ta + 8][4 * q];
+      const uint32_t ahi0 = *(const uint32_t *)&cur.x[kb][ta][16 + 4 * q];
+      const uint32_t ahi1 = *(const uint32_t *)&cur.x[kb][ta + 8][16 + 4 * q];
+      const float as0 = cur.as[kb][ta], as1 = cur.as[kb][ta + 8];
 #pragma unroll
       for (int n = 0; n < kNT; n++) {
         const int rb = n * 8 + g;  // this lane's B row
         uint32_t blo, bhi;
         if (QUANT == JAL_Q4_0) {
-          const uint32_t w = *(const uint32_t *)&w_s[kb][rb][4 * q];
+          const uint32_t w = *(const uint32_t *)&cur.w[kb][rb][4 * q];
           blo = nib_s8(w & 0x0F0F0F0Fu);
           bhi = nib_s8((w >> 4) & 0x0F0F0F0Fu);
         } else {
-          blo = *(const uint32_t *)&w_s[kb][rb][4 * q];
-          bhi = *(const uint32_t *)&w_s[kb][rb][16 + 4 * q];
+          blo = *(const uint32_t *)&cur.w[kb][rb][4 * q];
+          bhi = *(const uint32_t *)&cur.w[kb][rb][16 + 4 * q];
         }
         int c[4] = {0, 0, 0, 0};
         mma_s8_16832(c, alo0, alo1, ahi0, ahi1, blo, bhi);
-        const float ws0 = wd_s[kb][n * 8 + 2 * q], ws1 = wd_s[kb][n * 8 + 2 * q + 1];
+        const float ws0 = cur.wd[kb][n * 8 + 2 * q], ws1 = cur.wd[kb][n * 8 + 2 * q + 1];
         acc[n][0] = fmaf(__int2float_rn(c[0]), as0 * ws0, acc[n][0]);
         acc[n][1] = fmaf(__int2float_rn(c[1]), as0 * ws1, acc[n][1]);
         acc[n][2] = fmaf(__int2float_rn(c[2]), as1 * ws0, acc[n][2]);
         acc[n][3] = fmaf(__int2float_rn(c[3]), as1 * ws1, acc[n][3]);
       }
     }
+    __syncthreads();  // every warp is done with `cur` before it is refilled
+    if (sidx + 1 < nst) store_scales(st[(sidx + 1) & 1]);
   }
 #pragma unroll
   for (int n = 0; n < kNT; n++) {
@@ -135,8 +182,15 @@ __global__ void __launch_bounds__(kThreads) k_gemm(const GemmArgs a) {
 void launch_gemm(const GemmArgs &a, cudaStream_t s) {
   if (a.m <= 0 || a.rows <= 0) return;
   dim3 grid((unsigned)((a.rows + BN - 1) / BN), (unsigned)((a.m + BM - 1) / BM));
-  if (a.w.quant == JAL_Q4_0) k_gemm<JAL_Q4_0><<<grid, kThreads, 0, s>>>(a);
-  else k_gemm<JAL_Q8_0><<<grid, kThreads, 0, s>>>(a);
+  static bool attr = false;
+  constexpr size_t s4 = 2 * sizeof(GemmStage<16>), s8 = 2 * sizeof(GemmStage<32>);
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm<JAL_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s4);
+    cudaFuncSetAttribute(k_gemm<JAL_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)s8);
+    attr = true;
+  }
+  if (a.w.quant == JAL_Q4_0) k_gemm<JAL_Q4_0><<<grid, kThreads, s4, s>>>(a);
+  else k_gemm<JAL_Q8_0><<<grid, kThreads, s8, s>>>(a);
 }
 
 }  // namespace jal
