@@ -156,7 +156,9 @@ void gemm_noalloc(const DevMat &w, const float *x, int64_t m, float *y, cudaStre
 void launch_rope_rows(float *qk, int64_t m, int64_t row_len, int64_t head_dim, int64_t rotary_dim, int neox,
                       int64_t pos0, const float *inv_freq, cudaStream_t s);
 void launch_swiglu(const float *g, const float *u, int64_t n, float *out, cudaStream_t s);
-void launch_swiglu_rows(const float *gu, int64_t m, int64_t f, int64_t stride, float *out, cudaStream_t s);
+// SwiGLU rows straight into QuantizedActQ8 blocks (prefill down-projection input).
+void launch_swiglu_act_quant(const float *gu, int64_t m, int64_t f, int64_t stride, int8_t *q8, float *scales,
+                             cudaStream_t s);
 void launch_gqa_attention_ref(const float *q, const float *k, const float *v, int64_t m, int64_t nq, int64_t nkv,
                               int64_t hd, int64_t total_seq, int64_t start_pos, int64_t window, float scale,
                               float *out, cudaStream_t s);

@@ -1243,8 +1243,8 @@ void Context::ensure_prefill_capacity(uint64_t m) {
   JAL_CUDA(cudaStreamSynchronize(stream));  // the old scratch may still be in use
   const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv;
   const uint64_t K = std::max<uint64_t>(std::max<uint64_t>(H, Q), F);
-  size_t bytes = m * 4 + m * H * 4 + m * (Q + 2 * KV) * 4 + m * Q * 4 + m * 2 * F * 4 + m * F * 4 +
-                 m * ((K + 31) / 32) * 4 + m * ((K + 31) / 32 * 32) + 8 * 256;
+  size_t bytes = m * 4 + m * H * 4 + m * (Q + 2 * KV) * 4 + m * Q * 4 + m * 2 * F * 4 +
+                 m * ((K + 31) / 32) * 4 + m * ((K + 31) / 32 * 32) + 7 * 256;
   pf_buf = alloc(bytes);
   char *p = pf_buf->as<char>();
   auto take = [&](size_t n) { char *q = p; p += (n + 255) / 256 * 256; return q; };
@@ -1253,7 +1253,6 @@ void Context::ensure_prefill_capacity(uint64_t m) {
   pf_qkv = (float *)take(m * (Q + 2 * KV) * 4);
   pf_attn = (float *)take(m * Q * 4);
   pf_gu = (float *)take(m * 2 * F * 4);
-  pf_ffn = (float *)take(m * F * 4);
   pf_xs = (float *)take(m * ((K + 31) / 32) * 4);
   pf_xq = (int8_t *)take(m * ((K + 31) / 32 * 32));
   pf_cap = m;
@@ -1314,8 +1313,7 @@ void Context::prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bo
       ga.w = L.gateup; ga.m = (int64_t)m; ga.rows = (int64_t)(2 * F); ga.xq = pf_xq; ga.xs = pf_xs;
       ga.y = pf_gu; ga.y_stride = (int64_t)(2 * F);
       launch_gemm(ga, stream);
-      launch_swiglu_rows(pf_gu, (int64_t)m, (int64_t)F, (int64_t)(2 * F), pf_ffn, stream);
-      launch_act_quant(pf_ffn, (int64_t)m, (int64_t)F, (int64_t)F, pf_xq, pf_xs, stream);
+      launch_swiglu_act_quant(pf_gu, (int64_t)m, (int64_t)F, (int64_t)(2 * F), pf_xq, pf_xs, stream);
       GemmArgs da;
       da.w = L.wdown.dm; da.m = (int64_t)m; da.rows = (int64_t)H; da.xq = pf_xq; da.xs = pf_xs;
       da.y = pf_hidden; da.y_stride = (int64_t)H; da.accumulate = c.plan.rank == 0;

@@ -156,7 +156,7 @@ struct Context {
   uint64_t pf_cap = 0;
   DevBufferPtr pf_buf;
   uint32_t *pf_tokens = nullptr;
-  float *pf_hidden = nullptr, *pf_qkv = nullptr, *pf_attn = nullptr, *pf_gu = nullptr, *pf_ffn = nullptr,
+  float *pf_hidden = nullptr, *pf_qkv = nullptr, *pf_attn = nullptr, *pf_gu = nullptr,
         *pf_xs = nullptr;
   int8_t *pf_xq = nullptr;
   // host staging

@@ -39,12 +39,23 @@ __global__ void k_swiglu(const float *g, const float *u, int64_t n, float *out) 
   if (i < n) out[i] = swiglu1(g[i], u[i]);
 }
 
-// Rows of [gate | up] (stride floats) -> out[m][f].
-__global__ void k_swiglu_rows(const float *gu, int64_t m, int64_t f, int64_t stride, float *out) {
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= m * f) return;
-  int64_t t = i / f, j = i % f;
-  out[i] = swiglu1(gu[t * stride + j], gu[t * stride + f + j]);
+// SwiGLU of m rows of gate | up (row stride `stride`) straight into the
+// QuantizedActQ8 blocks of the next projection: the element values are
+// swiglu1's and the per-block quantization is k_act_quant's (repack_cache.rs:
+// 390-422), without an f32 row in between.  One warp per (row, 32-block).
+__global__ void k_swiglu_act_quant(const float *__restrict__ gu, int64_t m, int64_t f, int64_t stride,
+                                   int8_t *__restrict__ q8, float *__restrict__ scales) {
+  const int64_t nb = (f + 31) / 32;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (wid >= m * nb) return;  // whole warps leave together
+  const int64_t t = wid / nb, b = wid % nb, c = b * 32 + lane;
+  float v = c < f ? swiglu1(gu[t * stride + c], gu[t * stride + f + c]) : 0.0f;
+  if (!isfinite(v)) v = 0.0f;
+  const float amax = warp_max(fabsf(v));
+  const float scale = act_scale_from_amax(amax), inv = act_inv_from_scale(scale);
+  q8[t * nb * 32 + c] = c < f ? act_quant_one(v, inv) : (int8_t)0;
+  if (lane == 0) scales[t * nb + b] = scale;
 }
 
 // gqa_attention_prefill_portable (recipe.rs:2949-3022), one CTA per (token,
@@ -194,9 +205,11 @@ void launch_swiglu(const float *g, const float *u, int64_t n, float *out, cudaSt
   k_swiglu<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(g, u, n, out);
 }
 
-void launch_swiglu_rows(const float *gu, int64_t m, int64_t f, int64_t stride, float *out, cudaStream_t s) {
-  if (!m || !f) return;
-  k_swiglu_rows<<<(unsigned)((m * f + 255) / 256), 256, 0, s>>>(gu, m, f, stride, out);
+void launch_swiglu_act_quant(const float *gu, int64_t m, int64_t f, int64_t stride, int8_t *q8, float *scales,
+                             cudaStream_t s) {
+  const int64_t warps = m * ((f + 31) / 32);
+  if (!warps) return;
+  k_swiglu_act_quant<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(gu, m, f, stride, q8, scales);
 }
 
 void launch_gqa_attention_ref(const float *q, const float *k, const float *v, int64_t m, int64_t nq, int64_t nkv,
