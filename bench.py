@@ -64,53 +64,55 @@ def committed_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled through NVML in a
+    background thread during the timed region (reads only; no setting is
+    changed).  Falls back to an empty record when NVML is unavailable."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
-    def __init__(self, device):
-        self.device = device
-        self.proc = None
+    def __init__(self, device, period_s=0.01):
+        self.device, self.period = device, period_s
+        self.samples, self.max_mhz, self.error = [], None, None
+
+    def _run(self):
+        import pynvml as nv
+        h = nv.nvmlDeviceGetHandleByIndex(self.device)
+        self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((mhz, reasons))
+            except nv.NVMLError as e:  # keep the first error for the record
+                self.error = self.error or str(e)
+            self._stop.wait(self.period)
 
     def __enter__(self):
+        import threading
+        self._stop = threading.Event()
+        self._thread = None
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception as e:  # noqa: BLE001 - NVML missing: no clock record
+            self.error = f"nvml: {e}"
         return self
 
     def __exit__(self, *a):
-        self.lines = []
-        if self.proc:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = [m for m, _ in self.samples]
+        reasons = sorted(n for n, bit in self.REASONS.items() if any(r & bit for _, r in self.samples))
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+               "samples": len(sm), "source": "nvml"}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
 def ev_time(torch, fn, stream):
@@ -159,62 +161,87 @@ def gemv_sweep(jal, torch, peak, quants, iters=200):
     return res
 
 
-def cpu_baseline(jal, gguf, spec, steps):
-    """The oracle port timed on the host cores: a 1-layer model of the same
-    shape (layer 0 + embedding + head) is decoded for `steps` tokens and the
-    LM head projection is timed alone; tok/s = 1 / (L * t_layer + t_head)."""
+def host_cpu():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+SHAPES = {
+    "llama3-8b-q4_0": dict(num_layers=32, hidden_dim=4096, ffn_dim=14336, n_heads_q=32, n_heads_kv=8, head_dim=128,
+                           vocab_size=128256, rms_eps=1e-5, rope_theta=500000.0, weight_quant=2, embed_quant=2,
+                           head_quant=2),
+}
+
+
+def cpu_baseline(shape, steps, pos, seed=SEED):
+    """The oracle port (the reference's portable path restated in C) timed on
+    the host cores, without the product library: a 1-layer model with this
+    shape (layer 0, embedding and head, generated by the oracle's seeded
+    generator) decodes `steps` tokens at positions pos, pos + 1, ...; the KV
+    rows of positions [0, pos) hold seeded random values (the step's cost does
+    not depend on them).  The LM head projection is timed alone, and
+    tok/s = 1 / (L * t_layer + t_head)."""
     sys.path.insert(0, os.path.join(REPO, "tests"))
-    import gguf_py  # noqa: E402
     import numpy as np  # noqa: E402
     import oracle_py  # noqa: E402
 
-    _, tensors = gguf_py.parse(gguf)
-    keep = {k: v for k, v in tensors.items() if not k.startswith("blk.") or k.startswith("blk.0.")}
     threads = os.cpu_count() or 1
-    geom = dict(num_layers=1, hidden_dim=spec.hidden_dim, ffn_dim=spec.ffn_dim, n_heads_q=spec.n_heads_q,
-                n_heads_kv=spec.n_heads_kv, head_dim=spec.head_dim, vocab_size=spec.vocab_size,
-                rms_eps=spec.rms_eps, rope_theta=spec.rope_theta)
-    m = oracle_py.Model(keep, geom, nthreads=threads)
-    cap = 64
+    geom = dict(shape, num_layers=1)
+    t0 = time.perf_counter()
+    tensors = oracle_py.synth_llama_tensors(shape, seed, 1, nthreads=threads)
+    m = oracle_py.Model(tensors, geom, nthreads=threads, kv_f16=True)
+    gen_s = time.perf_counter() - t0
+    cap = pos + steps + 1
     kv = m.new_kv(cap)
-    m.prefill(kv, cap, [1, 2, 3, 4], 0)
+    kvd = shape["n_heads_kv"] * shape["head_dim"]
+    rng = np.random.Generator(np.random.PCG64(seed))
+    kv.reshape(2, cap, kvd)[:, :pos, :] = rng.standard_normal((2, pos, kvd), dtype=np.float32)
     head = tensors["output.weight"]
-    w = oracle_py.RepackedWeight(head.data, head.qtype, spec.vocab_size, spec.hidden_dim)
-    x = np.ones(spec.hidden_dim, dtype=np.float32)
+    w = oracle_py.RepackedWeight(head.data, head.qtype, shape["vocab_size"], shape["hidden_dim"])
+    x = rng.standard_normal(shape["hidden_dim"], dtype=np.float32)
     t0 = time.perf_counter()
     for i in range(steps):
-        m.decode(kv, cap, 5 + i, 4 + i)
+        m.decode(kv, cap, 5 + i, pos + i)
     t_step = (time.perf_counter() - t0) / steps
     t0 = time.perf_counter()
     for _ in range(steps):
         w.project_batch(x, 1, nthreads=threads)
     t_head = (time.perf_counter() - t0) / steps
     t_layer = max(t_step - t_head, 1e-9)
-    t_tok = spec.num_layers * t_layer + t_head
+    t_tok = shape["num_layers"] * t_layer + t_head
     return {"value": round(1.0 / t_tok, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{steps} decode steps of layer 0 + LM head of the same model ({t_step * 1e3:.1f} ms/step), "
-                      f"head alone {t_head * 1e3:.1f} ms; extrapolated to {spec.num_layers} layers"}
+            "cpu": host_cpu(),
+            "sample": f"{steps} decode steps at positions {pos}..{pos + steps - 1} of a 1-layer model of the same "
+                      f"shape (layer 0 + embedding + LM head, f16-rounded KV) = {t_step * 1e3:.1f} ms/step, LM head "
+                      f"alone {t_head * 1e3:.1f} ms; extrapolated to {shape['num_layers']} layers; model build "
+                      f"{gen_s:.1f} s (not timed)"}
 
 
 def reference_arm(args):
-    """--impl reference: the reference's portable CPU path (oracle port)."""
+    """--impl reference: the reference's portable CPU path (the oracle port,
+    since the Rust crate cannot be built here) on the host cores, at the
+    position the device arm decodes at.  It loads only the oracle library."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    jal = load_jal()
-    spec = jal.LLAMA3_8B_Q4_0
-    t0 = time.perf_counter()
-    gguf = jal.synth_gguf(spec, SEED)
-    gen_s = time.perf_counter() - t0
+    shape = SHAPES["llama3-8b-q4_0"]
     steps = max(1, args.steps)
-    base = cpu_baseline(jal, gguf, spec, steps)
+    pos = args.prefill + args.warmup
+    base = cpu_baseline(shape, steps, pos)
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus,
             "steps": steps, "warmup": args.warmup, "ms_per_step": round(1e3 / base["value"], 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic: seeded N(0,0.02) weights quantized to Q4_0, uniform token ids",
-            "config": {"workload": "llama3-8b-shaped Q4_0 decode bs=1 (CPU port of the reference's portable path)",
-                       "layers": spec.num_layers, "hidden": spec.hidden_dim, "ffn": spec.ffn_dim,
-                       "vocab": spec.vocab_size, "gguf_gen_s": round(gen_s, 1)},
+            "config": {"workload": f"llama3-8b-q4_0 decode bs=1 greedy after a {args.prefill}-token prefill",
+                       "layers": shape["num_layers"], "hidden": shape["hidden_dim"], "ffn": shape["ffn_dim"],
+                       "vocab": shape["vocab_size"], "kv_cache": "f16-rounded",
+                       "impl_detail": "C restatement of the reference's portable path (oracle), OpenMP panels"},
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -419,7 +446,7 @@ def main():
                             "algorithmic_bytes": dom["bytes"], "peak_kind": peak_kind}
         line["gpu_launches"] += sum(200 + 2 * max(2, -(-4 * L2_BYTES // (s["bytes"]))) for s in sweep)
     if rank == 0 and world == 1 and not args.no_cpu and args.workload == "llama3-8b-q4_0":
-        line["cpu_baseline"] = cpu_baseline(jal, gguf, spec, steps=3)
+        line["cpu_baseline"] = cpu_baseline(SHAPES["llama3-8b-q4_0"], 3, n_prefill + args.warmup)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del ctx

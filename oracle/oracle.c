@@ -1155,6 +1155,22 @@ static void add_bias(float *batch, const float *b, size_t dim, size_t m) {
     for (size_t i = 0; i < dim; i++) batch[t * dim + i] += b[i];
 }
 
+/* f32 -> f16 (round to nearest even) -> f32, for the f16 KV cache option. */
+static float f16_round(float v) {
+  uint16_t h = or_f32_to_f16_rne(v);
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1F, mant = h & 0x3FF, bits;
+  if (e == 0) {
+    if (mant == 0) bits = sign;
+    else {
+      int sh = 0;
+      while (!(mant & 0x400)) { mant <<= 1; sh++; }
+      bits = sign | ((uint32_t)(113 - sh) << 23) | ((mant & 0x3FF) << 13);
+    }
+  } else if (e == 31) bits = sign | 0x7F800000u | (mant << 13);
+  else bits = sign | ((e + 112u) << 23) | (mant << 13);
+  return f_from_bits(bits);
+}
+
 /* Shared per-layer body for M tokens at positions start..start+M (the cached
  * batched forward; decode is the M = 1 case and produces identical math). */
 static int forward_tokens(or_model *m, float *kv, size_t seq_cap, const uint32_t *toks, size_t M,
@@ -1201,6 +1217,11 @@ static int forward_tokens(or_model *m, float *kv, size_t seq_cap, const uint32_t
     float *kp = kv + (l * 2 + 0) * seq_cap * KV, *vp = kv + (l * 2 + 1) * seq_cap * KV;
     memcpy(kp + start * KV, k, M * KV * sizeof(float));
     memcpy(vp + start * KV, v, M * KV * sizeof(float));
+    if (g->kv_f16) /* an f16 cache holds the appended rows rounded to f16 */
+      for (size_t i = start * KV; i < end * KV; i++) {
+        kp[i] = f16_round(kp[i]);
+        vp[i] = f16_round(vp[i]);
+      }
     rc = or_gqa_attention(att, q, kp, vp, M, g->n_heads_q, g->n_heads_kv, hd, end, start,
                           g->sliding_window, scale, scores, end + 1);
     if (rc) break;

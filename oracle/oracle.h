@@ -142,6 +142,9 @@ typedef struct or_geometry {
   const uint8_t *skip_rope_layers; /* NULL or num_layers flags */
   or_rope_scaling scaling;
   size_t sliding_window;           /* 0 = none */
+  int kv_f16;                      /* 1 = K/V stored rounded to f16 (round to
+                                      nearest even), as a paged f16 cache holds
+                                      them; attention reads them back */
 } or_geometry;
 
 typedef struct or_model or_model;
@@ -156,6 +159,12 @@ int or_decode(or_model *m, float *kv, size_t seq_cap, uint32_t token,
 size_t or_model_vocab(const or_model *m);
 /* The final normed hidden of the last forward (diagnostics). */
 const float *or_model_last_hidden(const or_model *m);
+
+/* ---- seeded synthetic tensors (synth.c; fixtures, not reference code) --- */
+uint16_t or_f32_to_f16_rne(float f);
+int or_synth_matrix(int quant, size_t rows, size_t cols, uint64_t seed,
+                    const char *name, float std_dev, void *out, size_t len,
+                    int nthreads);
 
 #ifdef __cplusplus
 }

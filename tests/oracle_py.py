@@ -34,7 +34,7 @@ class Geometry(C.Structure):
     _fields_ = [("num_layers", _SZ), ("hidden_dim", _SZ), ("ffn_dim", _SZ), ("n_heads_q", _SZ),
                 ("n_heads_kv", _SZ), ("head_dim", _SZ), ("rotary_dim", _SZ), ("vocab_size", _SZ),
                 ("rms_eps", _F), ("rope_theta", _F), ("neox", _I), ("skip_rope_layers", _P),
-                ("scaling", RopeScaling), ("sliding_window", _SZ)]
+                ("scaling", RopeScaling), ("sliding_window", _SZ), ("kv_f16", _I)]
 
 
 class BlockQ8_0(C.Structure):
@@ -69,6 +69,8 @@ _sigs = {
     "or_prefill": (_I, [_P, _P, _SZ, _P, _SZ, _SZ, _I, _P]),
     "or_decode": (_I, [_P, _P, _SZ, C.c_uint32, _SZ, _P]),
     "or_model_vocab": (_SZ, [_P]),
+    "or_synth_matrix": (_I, [_I, _SZ, _SZ, C.c_uint64, C.c_char_p, _F, _P, _SZ, _I]),
+    "or_f32_to_f16_rne": (C.c_uint16, [_F]),
 }
 for _n, (_r, _a) in _sigs.items():
     _fn = getattr(L, _n)
@@ -231,7 +233,8 @@ def swiglu(g, u):
 class Model:
     """The cached recipe forward (prefill_step_with_cache / decode_step_with_cache)."""
 
-    def __init__(self, tensors, geom: dict, nthreads=1, skip_rope=None, scaling=None, sliding_window=0):
+    def __init__(self, tensors, geom: dict, nthreads=1, skip_rope=None, scaling=None, sliding_window=0,
+                 kv_f16=False):
         self._keep = []
         arr = (Tensor * len(tensors))()
         for i, t in enumerate(tensors.values()):
@@ -256,6 +259,7 @@ class Model:
         self._keep += keep
         g.scaling = sc
         g.sliding_window = sliding_window
+        g.kv_f16 = 1 if kv_f16 else 0
         h = _P()
         check(L.or_model_build(C.byref(g), C.addressof(arr), len(tensors), nthreads, C.byref(h)))
         self.h = h.value
@@ -281,3 +285,56 @@ class Model:
         logits = np.zeros(self.vocab, dtype=np.float32)
         check(L.or_decode(self.h, ptr(kv), seq_cap, token, pos, ptr(logits)))
         return logits
+
+
+_ROW = {0: (1, 4), 2: (32, 18), 8: (32, 34)}
+
+
+def synth_matrix(quant, rows, cols, seed, name, std=0.02, nthreads=1):
+    """Seeded synthetic rows x cols tensor in raw GGUF block order (the same
+    bytes as the product library's generator for the same arguments)."""
+    e, b = _ROW[quant]
+    out = np.empty(rows * (cols // e) * b, dtype=np.uint8)
+    check(L.or_synth_matrix(quant, rows, cols, seed, name.encode(), std, ptr(out), out.nbytes, nthreads))
+    return out
+
+
+class SynthTensor:
+    def __init__(self, name, dims, qtype, data):
+        self.name, self.dims, self.qtype, self.data = name, dims, qtype, data
+
+    @property
+    def nbytes(self):
+        return self.data.nbytes
+
+
+def synth_llama_tensors(shape, seed, layers, nthreads=1):
+    """Tensors of a seeded synthetic Llama-layout model with only the first
+    `layers` blocks (names, shapes and values as in the GGUF generator):
+    shape = dict(hidden_dim, ffn_dim, n_heads_q, n_heads_kv, head_dim,
+    vocab_size, weight_quant, embed_quant, head_quant)."""
+    H, F = shape["hidden_dim"], shape["ffn_dim"]
+    Q, KV = shape["n_heads_q"] * shape["head_dim"], shape["n_heads_kv"] * shape["head_dim"]
+    wq, ws = shape["weight_quant"], 0.02
+    ones = np.ones(H, dtype=np.float32).view(np.uint8)
+    t = {}
+
+    def add(name, q, cols, rows, ones_vec=False):
+        data = ones if ones_vec else synth_matrix(q, rows, cols, seed, name, ws, nthreads)
+        t[name] = SynthTensor(name, [cols] if ones_vec else [cols, rows], q, data)
+
+    add("token_embd.weight", shape["embed_quant"], H, shape["vocab_size"])
+    for layer in range(layers):
+        b = f"blk.{layer}."
+        add(b + "attn_norm.weight", 0, H, 1, True)
+        add(b + "attn_q.weight", wq, H, Q)
+        add(b + "attn_k.weight", wq, H, KV)
+        add(b + "attn_v.weight", wq, H, KV)
+        add(b + "attn_output.weight", wq, Q, H)
+        add(b + "ffn_norm.weight", 0, H, 1, True)
+        add(b + "ffn_gate.weight", wq, H, F)
+        add(b + "ffn_up.weight", wq, H, F)
+        add(b + "ffn_down.weight", wq, F, H)
+    add("output_norm.weight", 0, H, 1, True)
+    add("output.weight", shape["head_quant"], H, shape["vocab_size"])
+    return t
