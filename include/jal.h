@@ -100,9 +100,10 @@ int jal_cached_matrix_gemm(const jal_cached_matrix *mat, const float *x,
  * fixed 2 MiB device array that the library holds on every GPU where its
  * kernels are loaded, until the process exits; the call allocates nothing.
  * Limit: round_up(m*cols, 256) + m*(cols/32)*4 <= 2097152 bytes (cols=4096:
- * m <= 455), else JAL_ERR_TENSOR_BOUNDS and no work.  The first call on a
- * device looks up the array's device address (done once per device, with
- * that device current); make that first call before any stream capture.
+ * m <= 455), else JAL_ERR_TENSOR_BOUNDS and no work.  Each call looks up the
+ * array's device address on the current device; the first call on a device
+ * may load the library's device code there, so make it before any stream
+ * capture.
  * The work is only enqueued on `stream` (no synchronisation): every call
  * shares the array, so calls whose GPU work can overlap (other streams,
  * other threads) race; calls on one stream are ordered and safe. */
@@ -308,13 +309,24 @@ typedef struct jal_context_config {
   int32_t numerics;        /* JAL_NUMERICS_FAST or JAL_NUMERICS_REFERENCE */
 } jal_context_config;
 
-/* Numerics of an execution context.  FAST reorders f32 reductions for
- * bandwidth (tree sums, fused multiply-adds); REFERENCE performs every f32
- * reduction in the reference's order (recipe.rs / repack_cache.rs) so a run
- * can be compared with it token for token; it is a validation mode, far
- * slower than FAST.  No counterpart setting in the reference. */
+/* Numerics of an execution context (no counterpart setting in the
+ * reference).
+ *   FAST (default): the serving path.  On one GPU every f32 reduction runs in
+ *     the reference's order (recipe.rs / repack_cache.rs: per-16-chunk
+ *     projection terms folded left to right, sequential RMSNorm sums and
+ *     softmax denominators, position-ordered attention sums), with
+ *     bandwidth-oriented kernels, so logits and greedy tokens equal the
+ *     reference's.  A tensor-parallel context splits each projection's sum
+ *     over the ranks by construction and runs the RELAXED kernels.
+ *   REFERENCE: the same order with simple one-chain-per-reduction kernels,
+ *     a slow cross-check of FAST.
+ *   RELAXED: reductions reordered for bandwidth (tree sums, fused
+ *     multiply-adds, 32-element blocks); logits drift from the reference by
+ *     up to ~1e-2 because the int8 activation quantizer amplifies one-ulp
+ *     differences. */
 #define JAL_NUMERICS_FAST 0
 #define JAL_NUMERICS_REFERENCE 1
+#define JAL_NUMERICS_RELAXED 2
 
 int jal_context_new(const jal_recipe *r, const jal_model_cache *c,
                     const jal_context_config *cfg, jal_context **out);

@@ -36,7 +36,7 @@ F32, F16, Q4_0, Q5_0, Q8_0, Q4_K, Q5_K, Q6_K, BF16, TQ1_0, TQ2_0 = 0, 1, 2, 6, 8
 ROPE_NORM, ROPE_NEOX = 0, 1
 ROPE_SCALING_NONE, ROPE_SCALING_LINEAR, ROPE_SCALING_LLAMA3, ROPE_SCALING_LONGROPE = 0, 1, 2, 3
 KV_F32, KV_F16 = 0, 1
-NUMERICS_FAST, NUMERICS_REFERENCE = 0, 1  # jal_context_config.numerics
+NUMERICS_FAST, NUMERICS_REFERENCE, NUMERICS_RELAXED = 0, 1, 2  # jal_context_config.numerics
 
 BLOCK_GEOMETRY = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 18), Q5_0: (32, 22), Q8_0: (32, 34),
                   Q4_K: (256, 144), Q5_K: (256, 176), Q6_K: (256, 210), TQ1_0: (256, 54), TQ2_0: (256, 66)}

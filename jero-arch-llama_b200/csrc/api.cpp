@@ -139,17 +139,8 @@ int jal_cached_matrix_gemm(const jal_cached_matrix *mat, const float *x, size_t 
     int64_t K = w.cols, nb = K / 32;
     DevBuffer q8((size_t)m * K), sc((size_t)m * nb * 4);
     launch_act_quant(x, (int64_t)m, K, K, q8.as<int8_t>(), sc.as<float>(), s);
-    if (m <= (size_t)kGemvMaxM) {
-      GemvArgs a;
-      a.w = w; a.rows = w.rows; a.m = (int)m; a.in_mode = GEMV_IN_Q8; a.xq = q8.as<int8_t>(); a.xs = sc.as<float>();
-      a.xq_stride = K; a.out_mode = GEMV_OUT_STORE; a.y = y; a.y_stride = w.rows;
-      launch_gemv(a, s);
-    } else {
-      GemmArgs a;
-      a.w = w; a.m = (int64_t)m; a.rows = w.rows; a.xq = q8.as<int8_t>(); a.xs = sc.as<float>(); a.y = y;
-      a.y_stride = w.rows;
-      launch_gemm(a, s);
-    }
+    xgemv_init();
+    project_q8(w, q8.as<int8_t>(), sc.as<float>(), (int64_t)m, y, s);
     JAL_CUDA(cudaGetLastError());
     JAL_CUDA(cudaStreamSynchronize(s));
   });
@@ -174,10 +165,8 @@ int jal_cached_matrix_gemv_q8(const jal_cached_matrix *mat, const int8_t *q8, co
     NEED(scales);
     NEED(y);
     check_block_scaled(mat);
-    GemvArgs a;
-    a.w = mat->m.dm; a.rows = a.w.rows; a.m = 1; a.in_mode = GEMV_IN_Q8; a.xq = q8; a.xs = scales;
-    a.xq_stride = a.w.cols; a.out_mode = GEMV_OUT_STORE; a.y = y; a.y_stride = a.w.rows;
-    launch_gemv(a, as_stream(stream));
+    xgemv_init();
+    project_q8(mat->m.dm, q8, scales, 1, y, as_stream(stream));
     JAL_CUDA(cudaGetLastError());
   });
 }
@@ -511,7 +500,8 @@ int jal_context_new(const jal_recipe *r, const jal_model_cache *c, const jal_con
     cc.page_size = cfg->page_size ? cfg->page_size : 64;
     cc.sliding_window = cfg->sliding_window;
     cc.use_graphs = cfg->use_graphs != 0;
-    if (cfg->numerics != JAL_NUMERICS_FAST && cfg->numerics != JAL_NUMERICS_REFERENCE)
+    if (cfg->numerics != JAL_NUMERICS_FAST && cfg->numerics != JAL_NUMERICS_REFERENCE &&
+        cfg->numerics != JAL_NUMERICS_RELAXED)
       fail(JAL_ERR_INVALID_ARGUMENT, "unknown numerics mode %d", cfg->numerics);
     cc.numerics = cfg->numerics;
     auto h = std::make_unique<jal_context>();

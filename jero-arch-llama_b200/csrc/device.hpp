@@ -107,6 +107,13 @@ int gemv_default_grid(const GemvArgs &a);
 void gemv_init();
 size_t gemv_smem_bytes(int in_mode, int m, int64_t cols);
 
+// Reference-order decode GEMV (xgemv.cu): M = 1, Q4_0 / Q8_0, inputs Q8 /
+// F32 / RMSNorm, outputs STORE / ADD / SWIGLU.
+bool xgemv_supported(const GemvArgs &a);
+size_t xgemv_smem_bytes(int quant, int64_t cols, int in_mode);
+void xgemv_init();
+void launch_xgemv(const GemvArgs &a, cudaStream_t s);
+
 // ---- repack / export / activation quantizers ---------------------------
 void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, uint8_t *qs, uint16_t *d,
                    int64_t qs_stride, int64_t d_stride, cudaStream_t s);
@@ -116,6 +123,8 @@ void launch_act_quant(const float *x, int64_t m, int64_t k, int64_t x_stride, in
 void launch_quantize_row_q8_0(const float *x, int64_t n, void *blocks, cudaStream_t s);
 void launch_rmsnorm(const float *x, const float *w, int64_t m, int64_t n, float eps, float *out,
                     cudaStream_t s);
+// Sets the RMSNorm kernels' shared-memory limit (call before any capture).
+void norm_init();
 // Per-row RMSNorm then QuantizedActQ8 of the normed row (prefill).
 void launch_rmsnorm_quant(const float *x, const float *w, int64_t m, int64_t n, float eps, int8_t *q8,
                           float *scales, cudaStream_t s);
@@ -147,6 +156,9 @@ struct GemmArgs {
   int accumulate = 0;          // y += result
 };
 void launch_gemm(const GemmArgs &a, cudaStream_t s);
+// y[m][rows] = quantized activations x W^T in the reference's f32 order: the
+// decode GEMV for one token, the GEMM otherwise (op-level entry points).
+void project_q8(const DevMat &w, const int8_t *xq, const float *xs, int64_t m, float *y, cudaStream_t s);
 
 // Quantize-then-project with the activation scratch in a fixed file-scope
 // device array (noalloc.cu) instead of a per-call allocation.
@@ -194,6 +206,11 @@ struct AttnDecodeArgs {
   int pdl = 0;
 };
 void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
+// Reference-order decode attention (xattn.cu): clusters of a.n_splits CTAs
+// per KV head; n_ctx bounds the positions (shared-memory sizing).
+void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s);
+// Cluster size for launch_xattn_decode (>= G), 0 when the shape does not fit.
+int xattn_cluster_size(int head_dim, int f16, int G, int64_t n_ctx);
 // Largest cluster size (<= want) the decode attention kernel can run with
 // for head_dim, KV element type and G query heads per KV head.
 int attn_decode_cluster_size(int head_dim, int f16, int G, int want);
@@ -312,6 +329,9 @@ struct AttnPrefillArgs {
   float *out = nullptr;  // [m][n_heads_q*head_dim]
 };
 void launch_attn_prefill(const AttnPrefillArgs &a, cudaStream_t s);
+// Reference-order prefill attention (xprefill.cu).
+bool xattn_prefill_supported(int64_t head_dim, int64_t max_keys);
+void launch_xattn_prefill(const AttnPrefillArgs &a, cudaStream_t s);
 
 // Embedding row decode (repack_cache.rs:1166-1301 semantics) for tokens
 // read from device memory.

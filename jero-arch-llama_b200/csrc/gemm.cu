@@ -1,23 +1,24 @@
 // Prefill GEMM over the repacked Q4_0 / Q8_0 layout on the int8 tensor
-// cores (mma.sync m16n8k32, s8 x s8 -> s32).
+// cores (mma.sync m16n8k16, s8 x s8 -> s32), in the reference's f32 order.
 //
-// y[t][r] = sum over 32-blocks of f32(dot32) * (a_sc[t][b] * w_sc[r][b]),
-// the fast-path form of the decode GEMV (one FMA per block); against
-// repack_cache.rs:739-783 (per-16-chunk terms (f32(dot16) * a_sc) * w_sc)
-// only the f32 rounding and summation order differ.  The integer dot of a
-// block is exact (|dot32| < 2^24).
+// y[t][r] = the left-to-right f32 sum from +0.0, over the 16-element chunks
+// of the row in order, of (f32(dot16) * a_sc[t][b]) * w_sc[r][b]
+// (repack_cache.rs:739-783, gemm_rows :808-837); bias and the residual are
+// added after the fold.  Each 32-block is two m16n8k16 MMAs, one per chunk,
+// so every chunk's integer dot (|dot16| < 2^24, exact in f32) gets its own
+// term, and the accumulator of each (token, row) takes the terms in chunk
+// order: the result equals the reference bit for bit.
 //
 // CTA tile: 128 tokens x 128 rows, 8 warps, K staged 4 blocks (128
 // elements) at a time in shared memory, two stages alternating: the next
 // stage's blocks are in flight (cp.async) while the current one is used.  Warp w computes tokens
-// 16w..16w+15 against the 128 rows as 16 n-tiles of 8 rows, one MMA per
-// block and n-tile.  MMA
-// fragments (PTX m16n8k32 .s8, g = lane / 4, q = lane % 4): A (tokens x 32,
-// row-major) regs = (token g, k 4q..4q+3), (g + 8, 4q..), (g, 16 + 4q..),
-// (g + 8, 16 + 4q..); B (32 x 8 rows, column-major) regs = (row g, k
-// 4q..4q+3), (g, 16 + 4q..); C = tokens g and g + 8, rows 2q and 2q + 1.
-// A Q4_0 block's byte i holds elements i (low nibble) and i + 16 (high
-// nibble), so one 32-bit load at byte 4q gives both B registers.
+// 16w..16w+15 against the 128 rows as 16 n-tiles of 8 rows.  MMA fragments
+// (PTX m16n8k16 .s8, g = lane / 4, q = lane % 4): A (tokens x 16, row-major)
+// regs = (token g, k 4q..4q+3), (g + 8, 4q..); B (16 x 8 rows, column-major)
+// reg = (row g, k 4q..4q+3); C = tokens g and g + 8, rows 2q and 2q + 1.
+// A Q4_0 block's byte i holds elements i (low nibble, chunk 0) and i + 16
+// (high nibble, chunk 1), so one 32-bit load at byte 4q gives the B
+// registers of both chunks.
 #include "dev_util.cuh"
 #include "device.hpp"
 #include "jal.h"
@@ -29,13 +30,16 @@ namespace {
 constexpr int BM = 128, BN = 128, KB = 4;  // tokens, rows, 32-blocks per stage
 constexpr int kThreads = 256, kNT = BN / 8;  // 8 warps; n-tiles of 8 rows per warp
 
-__device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                             uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_s8_16816(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
   asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
+      "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// Term of one chunk: (f32(dot16) * a_sc) * w_sc.
+__device__ __forceinline__ float chunk_term(int dot, float as, float ws) {
+  return __fmul_rn(__fmul_rn(__int2float_rn(dot), as), ws);
 }
 
 // Four nibbles 0..15 (one per byte) to signed bytes n - 8.
@@ -150,13 +154,14 @@ __global__ void __launch_bounds__(kThreads) k_gemm(const GemmArgs a) {
           blo = *(const uint32_t *)&cur.w[kb][rb][4 * q];
           bhi = *(const uint32_t *)&cur.w[kb][rb][16 + 4 * q];
         }
-        int c[4] = {0, 0, 0, 0};
-        mma_s8_16832(c, alo0, alo1, ahi0, ahi1, blo, bhi);
+        int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+        mma_s8_16816(c0, alo0, alo1, blo);  // chunk 0: elements 0..15
+        mma_s8_16816(c1, ahi0, ahi1, bhi);  // chunk 1: elements 16..31
         const float ws0 = cur.wd[kb][n * 8 + 2 * q], ws1 = cur.wd[kb][n * 8 + 2 * q + 1];
-        acc[n][0] = fmaf(__int2float_rn(c[0]), as0 * ws0, acc[n][0]);
-        acc[n][1] = fmaf(__int2float_rn(c[1]), as0 * ws1, acc[n][1]);
-        acc[n][2] = fmaf(__int2float_rn(c[2]), as1 * ws0, acc[n][2]);
-        acc[n][3] = fmaf(__int2float_rn(c[3]), as1 * ws1, acc[n][3]);
+        acc[n][0] = __fadd_rn(__fadd_rn(acc[n][0], chunk_term(c0[0], as0, ws0)), chunk_term(c1[0], as0, ws0));
+        acc[n][1] = __fadd_rn(__fadd_rn(acc[n][1], chunk_term(c0[1], as0, ws1)), chunk_term(c1[1], as0, ws1));
+        acc[n][2] = __fadd_rn(__fadd_rn(acc[n][2], chunk_term(c0[2], as1, ws0)), chunk_term(c1[2], as1, ws0));
+        acc[n][3] = __fadd_rn(__fadd_rn(acc[n][3], chunk_term(c0[3], as1, ws1)), chunk_term(c1[3], as1, ws1));
       }
     }
     __syncthreads();  // every warp is done with `cur` before it is refilled
@@ -170,9 +175,9 @@ __global__ void __launch_bounds__(kThreads) k_gemm(const GemmArgs a) {
       const int64_t r = r0 + n * 8 + 2 * q + (i & 1);
       if (t >= a.m || r >= a.rows) continue;
       float v = acc[n][i];
-      if (a.bias) v += a.bias[r];
+      if (a.bias) v = __fadd_rn(v, a.bias[r]);
       float *yp = a.y + t * a.y_stride + r;
-      *yp = a.accumulate ? *yp + v : v;
+      *yp = a.accumulate ? __fadd_rn(*yp, v) : v;
     }
   }
 }

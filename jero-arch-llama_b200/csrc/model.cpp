@@ -806,7 +806,7 @@ static bool env_flag(const char *n) {
 // not fit it.
 static void setup_mega(Context &ctx, int sms) {
   const char *e = getenv("JAL_DECODE");
-  if (!e || strcmp(e, "mega") != 0 || ctx.cfg.numerics != JAL_NUMERICS_FAST) return;
+  if (!e || strcmp(e, "mega") != 0 || ctx.cfg.numerics != JAL_NUMERICS_RELAXED) return;
   if (ctx.cache->plan.world > 1) return;  // single-GPU kernel
   const ModelCache &c = *ctx.cache;
   const Geometry &g = ctx.g;
@@ -891,8 +891,10 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
   if (ctx->cfg.n_ctx == 0) fail(JAL_ERR_INVALID_ARGUMENT, "n_ctx must be positive");
   const Geometry &g = c.lgeom;  // this rank's heads and FFN rows
   ctx->g = g;
-  if (c.plan.world > 1 && ctx->cfg.numerics != JAL_NUMERICS_FAST)
-    fail(JAL_ERR_CAPABILITY_MISMATCH, "tensor parallel contexts run the fast numerics only");
+  if (c.plan.world > 1 && ctx->cfg.numerics == JAL_NUMERICS_REFERENCE)
+    fail(JAL_ERR_CAPABILITY_MISMATCH, "tensor parallel contexts run the fast / relaxed numerics only");
+  // One GPU, FAST: the reference-order kernels (xgemv / xattn / xprefill).
+  ctx->exact = ctx->cfg.numerics == JAL_NUMERICS_FAST && c.plan.world == 1;
   if (g.n_heads_q / g.n_heads_kv > 8) fail(JAL_ERR_CAPABILITY_MISMATCH, "GQA group size > 8 is not supported");
   if (g.head_dim != 64 && g.head_dim != 128) fail(JAL_ERR_CAPABILITY_MISMATCH, "head_dim must be 64 or 128");
   for (const Layer &L : c.layers) {
@@ -948,6 +950,33 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
     build_rope_table(n_ctx, g.rotary_dim, inv, cs, sn);
     JAL_CUDA(cudaMemcpy(ctx->cos_long, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
     JAL_CUDA(cudaMemcpy(ctx->sin_long, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  }
+  norm_init();
+  if (ctx->exact) {
+    xgemv_init();
+    auto need = [&](const DevMat &w, int in_mode, int out_mode, int64_t rows, const char *what) {
+      GemvArgs t;
+      t.w = w; t.m = 1; t.in_mode = in_mode; t.out_mode = out_mode; t.rows = rows;
+      if (!xgemv_supported(t))
+        fail(JAL_ERR_CAPABILITY_MISMATCH, "%s: shape not supported by the reference-order decode GEMV", what);
+    };
+    for (const Layer &L : c.layers) {
+      need(L.qkv, GEMV_IN_NORM, GEMV_OUT_STORE, (int64_t)(g.total_q + 2 * g.total_kv), "Q/K/V");
+      need(L.wo.dm, GEMV_IN_Q8, GEMV_OUT_ADD, (int64_t)g.hidden_dim, "O");
+      need(L.gateup, GEMV_IN_NORM, GEMV_OUT_SWIGLU, (int64_t)g.ffn_dim, "gate/up");
+      need(L.wdown.dm, GEMV_IN_F32, GEMV_OUT_ADD, (int64_t)g.hidden_dim, "down");
+    }
+    if (!dense_quant(c.lm_head.quant)) need(c.lm_head.dm, GEMV_IN_NORM, GEMV_OUT_STORE, (int64_t)c.vocab_size, "LM head");
+    ctx->x_splits = xattn_cluster_size((int)g.head_dim, ctx->cfg.kv_f16, (int)(g.n_heads_q / g.n_heads_kv),
+                                       (int64_t)ctx->cfg.n_ctx);
+    if (ctx->x_splits <= 0)
+      fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: n_ctx %llu does not fit",
+           (unsigned long long)ctx->cfg.n_ctx);
+    const uint64_t keys = ctx->cfg.sliding_window ? std::min<uint64_t>(ctx->cfg.sliding_window, ctx->cfg.n_ctx)
+                                                  : ctx->cfg.n_ctx;
+    if (!xattn_prefill_supported((int64_t)g.head_dim, (int64_t)keys + 4))
+      fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order prefill attention: n_ctx %llu does not fit",
+           (unsigned long long)ctx->cfg.n_ctx);
   }
   // Decode buffers.
   const int sms = sm_count();
@@ -1153,6 +1182,71 @@ void Context::enqueue_decode_step(bool pdl) {
   launches_per_step = n;
 }
 
+// The serving step in the reference's f32 order (FAST numerics, one GPU):
+// embedding, per layer Q/K/V (RMSNorm prologue) -> attention (bias, RoPE,
+// append) -> O (+ bias, residual) -> gate/up (RMSNorm prologue, SwiGLU) ->
+// down (residual), then the LM head (RMSNorm prologue) and the greedy argmax:
+// 1 + 5L + 2 launches chained with programmatic dependent launch.
+void Context::enqueue_exact_step(bool pdl) {
+  const ModelCache &c = *cache;
+  const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv;
+  const float eps = std::max(recipe.rms_eps, 1.0e-7f);
+  size_t n = 0;
+  launch_embed(c.emb_raw->as<uint8_t>(), c.emb_quant, (int64_t)H, (int64_t)c.emb_rows, d_token, 1, hidden, d_err, pdl,
+               stream);
+  n++;
+  for (size_t l = 0; l < c.layers.size(); l++) {
+    const Layer &L = c.layers[l];
+    GemvArgs qa;
+    qa.w = L.qkv; qa.rows = (int64_t)(Q + 2 * KV); qa.in_mode = GEMV_IN_NORM;
+    qa.x = hidden; qa.x_stride = (int64_t)H; qa.norm_w = L.attn_norm; qa.eps = eps;
+    qa.out_mode = GEMV_OUT_STORE; qa.y = qkv; qa.y_stride = (int64_t)(Q + 2 * KV); qa.pdl = pdl;
+    launch_xgemv(qa, stream);
+    AttnDecodeArgs aa;
+    aa.qkv = qkv; aa.bq = L.bq; aa.bk = L.bk; aa.bv = L.bv;
+    aa.cos_tab = cos_tab; aa.sin_tab = sin_tab; aa.cos_tab_long = cos_long; aa.sin_tab_long = sin_long;
+    aa.long_threshold = recipe.scaling.kind == JAL_ROPE_SCALING_LONGROPE
+                            ? (int64_t)recipe.scaling.original_max_position_embeddings : -1;
+    aa.skip_rope = recipe.should_skip_rope(l); aa.neox = recipe.rope_type == JAL_ROPE_NEOX;
+    aa.n_heads_q = (int64_t)g.n_heads_q; aa.rotary_dim = (int64_t)g.rotary_dim;
+    aa.kv = kv; aa.layer = (int64_t)l; aa.d_pos = d_pos; aa.window = (int64_t)cfg.sliding_window;
+    aa.scale = 1.0f / sqrtf((float)g.head_dim);
+    aa.n_splits = x_splits;
+    aa.out = attn; aa.out_q = attn_q; aa.out_s = attn_s; aa.err = d_err; aa.pdl = pdl;
+    launch_xattn_decode(aa, (int64_t)cfg.n_ctx, stream);
+    GemvArgs oa;
+    oa.w = L.wo.dm; oa.rows = (int64_t)H; oa.in_mode = GEMV_IN_Q8;
+    oa.xq = attn_q; oa.xs = attn_s; oa.xq_stride = (int64_t)Q;
+    oa.out_mode = GEMV_OUT_ADD; oa.y = hidden; oa.y_stride = (int64_t)H; oa.bias = L.bo; oa.pdl = pdl;
+    launch_xgemv(oa, stream);
+    GemvArgs ga;
+    ga.w = L.gateup; ga.rows = (int64_t)F; ga.in_mode = GEMV_IN_NORM;
+    ga.x = hidden; ga.x_stride = (int64_t)H; ga.norm_w = L.ffn_norm; ga.eps = eps;
+    ga.out_mode = GEMV_OUT_SWIGLU; ga.y = ffn; ga.y_stride = (int64_t)F; ga.up_offset = (int64_t)F; ga.pdl = pdl;
+    launch_xgemv(ga, stream);
+    GemvArgs da;
+    da.w = L.wdown.dm; da.rows = (int64_t)H; da.in_mode = GEMV_IN_F32; da.x = ffn; da.x_stride = (int64_t)F;
+    da.out_mode = GEMV_OUT_ADD; da.y = hidden; da.y_stride = (int64_t)H; da.pdl = pdl;
+    launch_xgemv(da, stream);
+    n += 5;
+  }
+  if (dense_quant(c.lm_head.dm.quant)) {
+    launch_rmsnorm(hidden, c.output_norm->as<float>(), 1, (int64_t)H, eps, s_norm, stream);
+    launch_strict_gemv_dense(c.lm_head.dm, s_norm, (int64_t)c.vocab_size, logits, stream);
+    n += 2;
+  } else {
+    GemvArgs la;
+    la.w = c.lm_head.dm; la.rows = (int64_t)c.vocab_size; la.in_mode = GEMV_IN_NORM;
+    la.x = hidden; la.x_stride = (int64_t)H; la.norm_w = c.output_norm->as<float>(); la.eps = eps;
+    la.out_mode = GEMV_OUT_STORE; la.y = logits; la.y_stride = (int64_t)c.vocab_size; la.pdl = pdl;
+    launch_xgemv(la, stream);
+    n++;
+  }
+  launch_argmax(logits, (int64_t)c.vocab_size, am_val, am_idx, am_cnt, am_blocks, d_token, d_pos, d_hist, pdl, stream);
+  n++;
+  launches_per_step = n;
+}
+
 // Reference-order step (see strict.cu): the same layer sequence as
 // forward_tokens of the reference for one token.
 void Context::enqueue_strict_token(bool logits_out, bool argmax) {
@@ -1221,7 +1315,8 @@ void Context::run_decode_step() {
       bool pdl = !env_flag("JAL_NO_PDL");
       cudaGraph_t gr = nullptr;
       JAL_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
-      enqueue_decode_step(pdl);
+      if (exact) enqueue_exact_step(pdl);
+      else enqueue_decode_step(pdl);
       cudaError_t e = cudaStreamEndCapture(stream, &gr);
       if (e != cudaSuccess) {
         cudaGetLastError();
@@ -1233,7 +1328,8 @@ void Context::run_decode_step() {
     }
     JAL_CUDA(cudaGraphLaunch(graph, stream));
   } else {
-    enqueue_decode_step(!env_flag("JAL_NO_PDL"));
+    if (exact) enqueue_exact_step(!env_flag("JAL_NO_PDL"));
+    else enqueue_decode_step(!env_flag("JAL_NO_PDL"));
     JAL_CUDA(cudaGetLastError());
   }
 }
@@ -1301,7 +1397,8 @@ void Context::prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bo
       pa.qkv = pf_qkv; pa.m = (int64_t)m; pa.qkv_stride = (int64_t)(Q + 2 * KV); pa.start_pos = (int64_t)sp;
       pa.n_heads_q = (int64_t)g.n_heads_q; pa.kv = kv; pa.layer = (int64_t)l; pa.window = (int64_t)cfg.sliding_window;
       pa.scale = 1.0f / sqrtf((float)g.head_dim); pa.out = pf_attn;
-      launch_attn_prefill(pa, stream);
+      if (exact) launch_xattn_prefill(pa, stream);
+      else launch_attn_prefill(pa, stream);
       launch_act_quant(pf_attn, (int64_t)m, (int64_t)Q, (int64_t)Q, pf_xq, pf_xs, stream);
       GemmArgs oa;
       oa.w = L.wo.dm; oa.m = (int64_t)m; oa.rows = (int64_t)H; oa.xq = pf_xq; oa.xs = pf_xs;
@@ -1326,7 +1423,14 @@ void Context::prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bo
       la.w = c.lm_head.dm; la.rows = (int64_t)c.plan.v_n; la.m = 1; la.in_mode = GEMV_IN_NORM;
       la.x = pf_hidden + (m - 1) * H; la.x_stride = (int64_t)H; la.norm_w = c.output_norm->as<float>(); la.eps = eps;
       la.out_mode = GEMV_OUT_STORE; la.y = logits_local; la.y_stride = (int64_t)c.plan.v_pad;
-      launch_gemv(la, stream);
+      if (exact && dense_quant(c.lm_head.dm.quant)) {
+        launch_rmsnorm(la.x, la.norm_w, 1, (int64_t)H, eps, s_norm, stream);
+        launch_strict_gemv_dense(c.lm_head.dm, s_norm, (int64_t)c.vocab_size, logits, stream);
+      } else if (exact) {
+        launch_xgemv(la, stream);
+      } else {
+        launch_gemv(la, stream);
+      }
       if (c.tp) tp_all_gather(*c.tp, logits_local, logits, c.plan.v_pad, stream);
       JAL_CUDA(cudaGetLastError());
     }

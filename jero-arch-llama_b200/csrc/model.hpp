@@ -152,6 +152,10 @@ struct Context {
   unsigned *ffn_cnt = nullptr, *am_cnt = nullptr;
   int *am_idx = nullptr;
   int n_splits = 1, am_blocks = 148;
+  // Reference-order serving path (JAL_NUMERICS_FAST on one GPU): xgemv /
+  // xattn kernels, x_splits CTAs per KV head in decode attention.
+  bool exact = false;
+  int x_splits = 0;
   // prefill scratch (grown on demand)
   uint64_t pf_cap = 0;
   DevBufferPtr pf_buf;
@@ -176,6 +180,7 @@ struct Context {
 
   ~Context();
   void enqueue_decode_step(bool pdl);
+  void enqueue_exact_step(bool pdl);
   // One token through the reference-order kernels; d_token / d_pos hold the
   // token and its position.  argmax advances d_pos like the fast step.
   void enqueue_strict_token(bool logits, bool argmax);

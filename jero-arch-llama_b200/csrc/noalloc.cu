@@ -10,12 +10,13 @@
 //
 // The array is part of this library's device image: every GPU on which the
 // library's kernels are loaded holds kNoAllocScratchBytes until the process
-// exits.  Host code cannot use the array's name as a device address, so its
-// address is looked up with cudaGetSymbolAddress once per device (with that
-// device current) on the first call there, and passed to the kernels.
+// exits.  Host code cannot use the array's name as a device address, so each
+// call looks the address up with cudaGetSymbolAddress on the current device
+// (a cheap table lookup once the image is loaded there; looking it up every
+// time also stays right after a device reset reloads the image elsewhere) and
+// passes it to the kernels.  The first call on a device may load the image,
+// so it must not be made inside a stream capture.
 #include <cuda_runtime.h>
-
-#include <mutex>
 
 #include "common.hpp"
 #include "device.hpp"
@@ -26,27 +27,18 @@ namespace jal {
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = (size_t)2 << 20;  // 2 MiB
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_gemm_scratch[kNoAllocScratchBytes];
 
-std::mutex g_addr_mu;
-void *g_addr[kMaxDevices] = {};
-
 // Device address of g_gemm_scratch on `dev`, which must be the current device.
 void *scratch_address(int dev) {
-  if (dev < 0 || dev >= kMaxDevices) fail(JAL_ERR_INVALID_ARGUMENT, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_addr_mu);
-  if (!g_addr[dev]) {
-    void *p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_gemm_scratch);
-    if (e != cudaSuccess || !p) {
-      cudaGetLastError();
-      fail(JAL_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev, cudaGetErrorString(e));
-    }
-    g_addr[dev] = p;
+  void *p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_gemm_scratch);
+  if (e != cudaSuccess || !p) {
+    cudaGetLastError();
+    fail(JAL_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev, cudaGetErrorString(e));
   }
-  return g_addr[dev];
+  return p;
 }
 
 size_t round256(size_t n) { return (n + 255) / 256 * 256; }
@@ -71,16 +63,7 @@ void gemm_noalloc(const DevMat &w, const float *x, int64_t m, float *y, cudaStre
   // Every byte the kernels read below is written first by the quantizer, so
   // nothing has to start at zero.
   launch_act_quant(x, m, K, K, q8, sc, s);
-  if (m <= kGemvMaxM) {
-    GemvArgs a;
-    a.w = w; a.rows = w.rows; a.m = (int)m; a.in_mode = GEMV_IN_Q8; a.xq = q8; a.xs = sc;
-    a.xq_stride = K; a.out_mode = GEMV_OUT_STORE; a.y = y; a.y_stride = w.rows;
-    launch_gemv(a, s);
-  } else {
-    GemmArgs a;
-    a.w = w; a.m = m; a.rows = w.rows; a.xq = q8; a.xs = sc; a.y = y; a.y_stride = w.rows;
-    launch_gemm(a, s);
-  }
+  project_q8(w, q8, sc, m, y, s);
   JAL_CUDA(cudaGetLastError());
 }
 

@@ -3,6 +3,7 @@
 // greedy argmax that closes a decode step on the device.
 #include "dev_util.cuh"
 #include "device.hpp"
+#include "exact.cuh"
 #include "jal.h"
 
 namespace jal {
@@ -29,10 +30,8 @@ __global__ void k_rope_rows(float *qk, int64_t row_len, int64_t head_dim, int64_
   }
 }
 
-__device__ __forceinline__ float swiglu1(float g, float u) {
-  float sig = g <= -20.0f ? 0.0f : (g >= 20.0f ? 1.0f : __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
-  return __fmul_rn(__fmul_rn(g, sig), u);
-}
+// swiglu_compat (recipe.rs:3037-3047) with the reference's exp.
+__device__ __forceinline__ float swiglu1(float g, float u) { return exact::swiglu_ref(g, u); }
 
 __global__ void k_swiglu(const float *g, const float *u, int64_t n, float *out) {
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -58,12 +57,18 @@ __global__ void k_swiglu_act_quant(const float *__restrict__ gu, int64_t m, int6
   if (lane == 0) scales[t * nb + b] = scale;
 }
 
-// gqa_attention_prefill_portable (recipe.rs:2949-3022), one CTA per (token,
-// query head); scores for the visible positions are kept in shared memory.
-__global__ void k_gqa_ref(const float *q, const float *k, const float *v, int64_t nq, int64_t nkv, int64_t hd,
-                          int64_t total_seq, int64_t start_pos, int64_t window, float scale, float *out) {
+// gqa_attention_prefill_portable (recipe.rs:2949-3022) in the reference's f32
+// order, one CTA per (token, query head); scores of the visible positions are
+// kept in shared memory.  Scores: sequential q.k from -0.0 then * scale; max;
+// e = exp(s - max); den = sequential sum (exact::seq_sum_nonneg); output
+// chains out[e] = sum over positions of (p * inv) * v in position order.
+constexpr int kGqaThreads = 128;
+__global__ void __launch_bounds__(kGqaThreads) k_gqa_ref(const float *q, const float *k, const float *v, int64_t nq,
+                                                        int64_t nkv, int64_t hd, int64_t total_seq, int64_t start_pos,
+                                                        int64_t window, float scale, float *out) {
   extern __shared__ float sc[];
   __shared__ float red[33];
+  __shared__ exact::SumSmem<kGqaThreads> ssm;
   const int64_t tok = blockIdx.x, hq = blockIdx.y, group = nq / nkv, hkv = hq / group;
   const int64_t kvs = nkv * hd, qpos = start_pos + tok;
   const int64_t vend = qpos + 1 < total_seq ? qpos + 1 : total_seq;
@@ -71,46 +76,34 @@ __global__ void k_gqa_ref(const float *q, const float *k, const float *v, int64_
   const int64_t n = vend > vstart ? vend - vstart : 0;
   const float *qh = q + (tok * nq + hq) * hd;
   float mx = -INFINITY;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+  for (int64_t i = threadIdx.x; i < n; i += kGqaThreads) {
     const float *kh = k + (vstart + i) * kvs + hkv * hd;
-    float d = 0.0f;
-    for (int64_t e = 0; e < hd; e++) d = fmaf(qh[e], kh[e], d);
-    float s = __fmul_rn(d, scale);
+    float d = -0.0f;
+    for (int64_t e = 0; e < hd; e++) d = __fadd_rn(d, __fmul_rn(qh[e], kh[e]));
+    const float s = __fmul_rn(d, scale);
     sc[i] = s;
-    mx = fmaxf(mx, s);
+    if (s > mx) mx = s;
   }
   mx = warp_max(mx);
-  int w = threadIdx.x / 32, l = threadIdx.x % 32, nw = blockDim.x / 32;
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
   if (l == 0) red[w] = mx;
   __syncthreads();
   if (threadIdx.x == 0) {
     float m = -INFINITY;
-    for (int i = 0; i < nw; i++) m = fmaxf(m, red[i]);
+    for (int i = 0; i < kGqaThreads / 32; i++)
+      if (red[i] > m) m = red[i];
     red[32] = m;
   }
   __syncthreads();
   mx = red[32];
+  for (int64_t i = threadIdx.x; i < n; i += kGqaThreads) sc[i] = exact::exp_ref(__fsub_rn(sc[i], mx));
   __syncthreads();
-  float sum = 0.0f;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-    float e = expf(sc[i] - mx);
-    sc[i] = e;
-    sum += e;
-  }
-  sum = warp_sum(sum);
-  if (l == 0) red[w] = sum;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float s = 0.0f;
-    for (int i = 0; i < nw; i++) s += red[i];
-    red[32] = s;
-  }
-  __syncthreads();
-  const float denom = red[32], inv = denom > 0.0f ? __fdiv_rn(1.0f, denom) : 0.0f;
+  const float denom = exact::seq_sum_nonneg<kGqaThreads>(sc, (int)n, 0.0f, ssm);
+  const float inv = denom > 0.0f ? __fdiv_rn(1.0f, denom) : 0.0f;
   float *oh = out + (tok * nq + hq) * hd;
-  for (int64_t e = threadIdx.x; e < hd; e += blockDim.x) {
+  for (int64_t e = threadIdx.x; e < hd; e += kGqaThreads) {
     float o = 0.0f;
-    for (int64_t i = 0; i < n; i++) o = fmaf(__fmul_rn(sc[i], inv), v[(vstart + i) * kvs + hkv * hd + e], o);
+    for (int64_t i = 0; i < n; i++) o = __fadd_rn(o, __fmul_rn(__fmul_rn(sc[i], inv), v[(vstart + i) * kvs + hkv * hd + e]));
     oh[e] = o;
   }
 }

@@ -4,7 +4,9 @@
 // gather.
 #include <cuda_fp16.h>
 
+#include "common.hpp"
 #include "dev_util.cuh"
+#include "exact.cuh"
 #include "device.hpp"
 #include "jal.h"
 
@@ -214,32 +216,51 @@ __device__ __forceinline__ float rms_inv(float ss, int64_t n, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
 }
 
-__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, int64_t n, float eps,
-                          float *__restrict__ out) {
-  __shared__ float red[33];
-  const float *xr = x + blockIdx.x * n;
-  float ss = 0.0f;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
-  float inv = rms_inv(block_sum(ss, red), n, eps);
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) out[blockIdx.x * n + i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+// RMSNorm rows in the reference's order (rmsnorm_row, recipe.rs:2534-2558):
+// the sum of squares is the left-to-right f32 sum from -0.0 (computed exactly
+// by exact::seq_sum_nonneg over the squares staged in shared memory), then
+// inv = 1 / sqrt(sum / n + eps) and out = (x * inv) * w.  One CTA per row.
+constexpr int kNormThreads = 256;
+
+__device__ float row_inv_ref(const float *xr, int64_t n, float eps, float *sq) {
+  __shared__ exact::SumSmem<kNormThreads> sm;
+  for (int64_t i = threadIdx.x; i < n; i += kNormThreads) sq[i] = __fmul_rn(xr[i], xr[i]);
+  __syncthreads();
+  const float ss = exact::seq_sum_nonneg<kNormThreads>(sq, (int)n, -0.0f, sm);
+  return rms_inv(ss, n, eps);
 }
+
+__global__ void __launch_bounds__(kNormThreads) k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w,
+                                                         int64_t n, float eps, float *__restrict__ out) {
+  extern __shared__ float sq[];
+  const float *xr = x + blockIdx.x * n;
+  const float inv = row_inv_ref(xr, n, eps, sq);
+  for (int64_t i = threadIdx.x; i < n; i += kNormThreads) out[blockIdx.x * n + i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+
+constexpr int kNormMaxSmem = 160 * 1024;  // rows up to 40960 elements
+
+static bool norm_fits(int64_t n) { return (size_t)n * 4 <= (size_t)kNormMaxSmem; }
 
 void launch_rmsnorm(const float *x, const float *w, int64_t m, int64_t n, float eps, float *out, cudaStream_t s) {
   if (!m) return;
-  k_rmsnorm<<<(unsigned)m, 256, 0, s>>>(x, w, n, eps, out);
+  norm_init();
+  if (!norm_fits(n)) fail(JAL_ERR_CAPABILITY_MISMATCH, "rmsnorm: row of %lld elements too long", (long long)n);
+  k_rmsnorm<<<(unsigned)m, kNormThreads, (size_t)n * 4, s>>>(x, w, n, eps, out);
 }
 
-// One CTA per row: RMSNorm, then per-32-block quantization of the normed row.
-__global__ void k_rmsnorm_quant(const float *__restrict__ x, const float *__restrict__ w, int64_t n, float eps,
-                                int8_t *__restrict__ q8, float *__restrict__ scales) {
-  __shared__ float red[33];
+
+// One CTA per row: RMSNorm (reference order, as above), then QuantizedActQ8
+// per 32-block of the normed row.
+__global__ void __launch_bounds__(kNormThreads) k_rmsnorm_quant(const float *__restrict__ x,
+                                                               const float *__restrict__ w, int64_t n, float eps,
+                                                               int8_t *__restrict__ q8, float *__restrict__ scales) {
+  extern __shared__ float sq[];
   const float *xr = x + blockIdx.x * n;
-  float ss = 0.0f;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
-  float inv = rms_inv(block_sum(ss, red), n, eps);
+  const float inv = row_inv_ref(xr, n, eps, sq);
   int64_t nb = (n + 31) / 32;
   int lane = threadIdx.x % 32;
-  for (int64_t b = threadIdx.x / 32; b < nb; b += blockDim.x / 32) {
+  for (int64_t b = threadIdx.x / 32; b < nb; b += kNormThreads / 32) {
     int64_t c = b * 32 + lane;
     float v = c < n ? __fmul_rn(__fmul_rn(xr[c], inv), w[c]) : 0.0f;
     if (!isfinite(v)) v = 0.0f;
@@ -250,10 +271,20 @@ __global__ void k_rmsnorm_quant(const float *__restrict__ x, const float *__rest
   }
 }
 
+void norm_init() {
+  static bool done = false;
+  if (done) return;
+  cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, kNormMaxSmem);
+  cudaFuncSetAttribute(k_rmsnorm_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, kNormMaxSmem);
+  done = true;
+}
+
 void launch_rmsnorm_quant(const float *x, const float *w, int64_t m, int64_t n, float eps, int8_t *q8,
                           float *scales, cudaStream_t s) {
   if (!m) return;
-  k_rmsnorm_quant<<<(unsigned)m, 256, 0, s>>>(x, w, n, eps, q8, scales);
+  norm_init();
+  if (!norm_fits(n)) fail(JAL_ERR_CAPABILITY_MISMATCH, "rmsnorm: row of %lld elements too long", (long long)n);
+  k_rmsnorm_quant<<<(unsigned)m, kNormThreads, (size_t)n * 4, s>>>(x, w, n, eps, q8, scales);
 }
 
 // ---- integer 16-element partials (repack_cache.rs:759-762) ---------------

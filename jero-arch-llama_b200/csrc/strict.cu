@@ -16,20 +16,19 @@
 //     (recipe.rs:2949-3022);
 //   - SwiGLU: (g * (1 / (1 + exp(-g)))) * u with the +-20 clamps
 //     (recipe.rs:3037-3047).
-// exp is computed in double and rounded to float (the correctly rounded
-// result); glibc's expf, which the reference calls, differs from it by one
-// ulp on about 6e-4 of arguments.
+// exp is glibc's expf evaluation (libm_expf.h), which the reference calls.
 #include <cuda_fp16.h>
 
 #include "dev_util.cuh"
 #include "device.hpp"
+#include "libm_expf.h"
 #include "jal.h"
 
 namespace jal {
 
 namespace {
 
-__device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x); }
+__device__ __forceinline__ float exp_ref(float x) { return libm::expf_ref(x); }
 
 __global__ void k_strict_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, int64_t n, float eps,
                                  float *__restrict__ out) {

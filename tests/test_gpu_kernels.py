@@ -1,7 +1,10 @@
 """Device kernels against the oracle (needs a B200).
 
-Bars: repack, activation quantizers and 16-element integer partials are
-bit-exact; f32 outputs within max|y - y_ref| / max|y_ref| <= 1e-3 (REL_TOL).
+Bars: repack, activation quantizers, 16-element integer partials and every
+projection, RMSNorm, SwiGLU and attention entry point, which all compute in
+the reference's f32 order, are equal to the oracle bit for bit.  The RoPE op
+(angles computed on the device) is held to max|y - y_ref| / max|y_ref| <= 1e-5,
+a normalised max error (rel_err below), not a per-element relative error.
 Inputs are seeded synthetic tensors with the shapes of the quant-GEMV op
 sweep (M x K in {4096x4096, 11008x4096, 4096x11008, 14336x4096}).
 """
@@ -47,13 +50,13 @@ def test_repack_bit_exact_and_gemv_op_sweep(jal, oracle, torch_cuda, quant_name,
     mat.gemm(dev(torch, x), 1, y)
     torch.cuda.synchronize()
     want = ref.project_batch(x, 1)[0]
-    assert rel_err(y.cpu().numpy(), want) <= REL_TOL
+    assert np.array_equal(y.cpu().numpy(), want)
 
 
 def test_q5_0_repack_bit_exact_and_projection(jal, oracle, torch_cuda):
     # Q5_0 unpacks to int8 like Q8_0 (unpack_row_i8, repack_cache.rs:840-871)
     # and runs the Q8_0 device layout: reference tiles and scales bit for
-    # bit, projections (M = 1 and 5) within REL_TOL.
+    # bit, projections (M = 1 and 5) equal to the oracle's.
     torch = torch_cuda
     rows, cols = 4096, 4096
     raw = jal.synth_matrix(jal.Q5_0, rows, cols, seed=321, name="q5.sweep")
@@ -70,8 +73,7 @@ def test_q5_0_repack_bit_exact_and_projection(jal, oracle, torch_cuda):
         torch.cuda.synchronize()
         want = ref.project_batch(x, m)
         got = y.cpu().numpy().reshape(m, rows)
-        for t in range(m):
-            assert rel_err(got[t], want[t]) <= REL_TOL
+        assert np.array_equal(got, want)
 
 
 @pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
@@ -132,9 +134,23 @@ def test_small_batch_gemv_and_gemm(jal, oracle, torch_cuda, m, quant_name):
     mat.gemm(dev(torch, x), m, y)
     torch.cuda.synchronize()
     want = oracle.RepackedWeight(raw, quant, rows, cols).project_batch(x, m)
-    got = y.cpu().numpy().reshape(m, rows)
-    for t in range(m):
-        assert rel_err(got[t], want[t]) <= REL_TOL
+    assert np.array_equal(y.cpu().numpy().reshape(m, rows), want)
+
+
+def test_prefill_gemm_llama3_8b_down_projection_2048_tokens(jal, oracle, torch_cuda):
+    # The 8B down projection (4096 rows x 14336 columns, Q4_0) over a
+    # 2048-token prefill batch, equal to the oracle's gemm_rows bit for bit.
+    torch = torch_cuda
+    rows, cols, m = 4096, 14336, 2048
+    raw = jal.synth_matrix(jal.Q4_0, rows, cols, seed=41, name="down8b")
+    mat = jal.CachedMatrix.repack(raw, jal.Q4_0, rows, cols)
+    x = jal.synth_normal(m * cols, seed=42, name="down8b.act")
+    y = torch.zeros(m * rows, dtype=torch.float32, device="cuda")
+    mat.gemm(dev(torch, x), m, y)
+    torch.cuda.synchronize()
+    import os
+    want = oracle.RepackedWeight(raw, jal.Q4_0, rows, cols).project_batch(x, m, nthreads=os.cpu_count() or 1)
+    assert np.array_equal(y.cpu().numpy().reshape(m, rows), want)
 
 
 @pytest.mark.parametrize("quant_name", ["Q4_0", "Q8_0"])
@@ -157,7 +173,7 @@ def test_wave2_shapes_vs_compute_row_dot(jal, oracle, torch_cuda, quant_name):
         for r in range(rows):
             exp = oracle.compute_row_dot(r, cols, quant, raw, x)
             assert abs(got[t, r] - exp) / max(bound, abs(exp)) < 1e-2
-        assert rel_err(got[t], want[t]) <= REL_TOL
+        assert np.array_equal(got[t], want[t])
 
 
 @pytest.mark.parametrize("quant_name", ["Q4_0", "Q5_0", "Q8_0"])
@@ -262,7 +278,7 @@ def test_ops_rmsnorm_rope_swiglu_attention(jal, oracle, torch_cuda):
     torch.cuda.synchronize()
     got = out.cpu().numpy().reshape(3, n)
     for t in range(3):
-        assert rel_err(got[t], oracle.rmsnorm_row(x[t * n:(t + 1) * n], w, 1e-5)) <= 1e-5
+        assert np.array_equal(got[t], oracle.rmsnorm_row(x[t * n:(t + 1) * n], w, 1e-5))
     # RoPE: 4 rows, 8 heads of 128 at positions 5..8, Norm and NeoX
     inv = oracle.fill_inv_freq(128, 500000.0, 16)
     for neox in (False, True):
@@ -279,7 +295,7 @@ def test_ops_rmsnorm_rope_swiglu_attention(jal, oracle, torch_cuda):
     o = torch.zeros(n, dtype=torch.float32, device="cuda")
     jal.swiglu(dev(torch, g), dev(torch, u), n, o)
     torch.cuda.synchronize()
-    assert rel_err(o.cpu().numpy(), oracle.swiglu(g, u)) <= 1e-6
+    assert np.array_equal(o.cpu().numpy(), oracle.swiglu(g, u))
     # GQA attention: 5 queries at start_pos 11 over 16 positions, 8/2 heads, hd 64, window 0 and 6
     nq, nkv, hd, total, m, sp = 8, 2, 64, 16, 5, 11
     q = jal.synth_normal(m * nq * hd, seed=26, name="att.q")
@@ -290,4 +306,41 @@ def test_ops_rmsnorm_rope_swiglu_attention(jal, oracle, torch_cuda):
         jal.gqa_attention(dev(torch, q), dev(torch, k), dev(torch, v), m, nq, nkv, hd, total, sp, window, 0.125, o)
         torch.cuda.synchronize()
         want = oracle.gqa_attention(q, k, v, m, nq, nkv, hd, total, sp, window, 0.125)
-        assert rel_err(o.cpu().numpy(), want) <= 1e-5
+        assert np.array_equal(o.cpu().numpy(), want)
+
+
+def test_rmsnorm_rows_sequential_sum_stress(jal, oracle, torch_cuda):
+    """RMSNorm equals the reference bit for bit on rows built to stress the
+    parallel form of its sequential sum of squares (exact::seq_sum_nonneg):
+    lengths from 1 to 40000, magnitudes over many binades within a row,
+    exact zeros, tiny (subnormal-square) values, values whose squares tie
+    against the running sum's rounding grid (small integers and halves), a
+    huge leading element, and a row that overflows to inf."""
+    torch = torch_cuda
+    rng = np.random.Generator(np.random.PCG64(77))
+    rows = []
+    for n in (1, 2, 3, 5, 31, 32, 33, 100, 255, 512, 1000, 4096, 5000, 8192, 14336, 40000):
+        rows.append(rng.standard_normal(n).astype(np.float32))
+    n = 4096
+    rows.append((rng.standard_normal(n) * np.exp2(rng.integers(-30, 30, n))).astype(np.float32))
+    z = rng.standard_normal(n).astype(np.float32)
+    z[::3] = 0.0
+    rows.append(z)
+    rows.append((rng.standard_normal(n) * 1e-23).astype(np.float32))
+    rows.append(rng.integers(-8, 9, n).astype(np.float32))
+    rows.append((rng.integers(-64, 65, n) * 0.5).astype(np.float32))
+    r = rng.standard_normal(n).astype(np.float32)
+    r[0] = 3.0e18
+    rows.append(r)
+    rows.append(np.linspace(1.0, 4096.0, n, dtype=np.float32))
+    rows.append(np.full(n, 2.0e19, dtype=np.float32))
+    rows.append(np.zeros(n, dtype=np.float32))
+    for i, x in enumerate(rows):
+        n = x.size
+        w = (1.0 + 0.01 * rng.standard_normal(n)).astype(np.float32)
+        out = torch.zeros(n, dtype=torch.float32, device="cuda")
+        jal.rmsnorm(dev(torch, x), dev(torch, w), 1, n, 1e-5, out)
+        torch.cuda.synchronize()
+        want = oracle.rmsnorm_row(x, w, 1e-5)
+        got = out.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"row {i} (n={n})"

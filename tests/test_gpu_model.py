@@ -4,19 +4,23 @@ The tiny Llama workload: 4 layers, dim 512, 8/2 heads, head_dim 64, FFN 1376,
 vocab 4096, Q4_0 layer weights, Q8_0 embedding and head, RoPE theta 1e4; a
 16-token prompt uniform in [0, 4096) and 64 greedy decode steps.
 
-Two numerics modes are checked:
-  - NUMERICS_REFERENCE performs every f32 reduction in the reference's order.
-    Bars: every step's logits within LOGIT_ATOL of the oracle's and an
-    identical greedy token sequence (exp is the correctly rounded value; the
-    reference's glibc expf differs by one ulp on ~6e-4 of arguments, which
-    moves logits by ~1e-7).
-  - NUMERICS_FAST (the serving path) reorders f32 sums.  Because the int8
-    activation quantizer is discontinuous, a one-ulp difference can flip one
-    rounding and move logits by up to ~3e-2 a few layers later; the fast path
-    is therefore checked teacher-forced against the oracle with bounds on the
-    worst and mean logit error, and its argmax may differ from the oracle's
-    only where the oracle's top logits are within that error of each other.
+Numerics modes:
+  - NUMERICS_FAST (the serving path, default) and NUMERICS_REFERENCE both
+    perform every f32 reduction in the reference's order.  Bars: every step's
+    logits within LOGIT_ATOL of the oracle's (the north star asks for 1e-2)
+    and an identical free-running greedy token sequence.  exp is the correctly
+    rounded value; the reference's glibc expf differs by one ulp on ~6e-4 of
+    arguments, which moves logits by ~1e-7.  With an f16 KV cache the oracle
+    rounds the appended K/V rows to f16 as the cache stores them.
+  - NUMERICS_RELAXED reorders f32 sums for bandwidth.  The int8 activation
+    quantizer is discontinuous, so a one-ulp difference can flip one rounding
+    and move logits by up to ~3e-2 a few layers later; it is checked
+    teacher-forced with bounds on the worst and mean logit error, and its
+    argmax may differ from the oracle's only where the oracle's top logits are
+    within that error of each other.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -24,10 +28,11 @@ import gguf_py
 
 pytestmark = pytest.mark.gpu
 
-LOGIT_ATOL = 1e-4      # reference numerics vs oracle, per logit
+LOGIT_ATOL = 1e-4      # FAST / REFERENCE numerics vs oracle, per logit
 N_DECODE = 64
-FAST_MAX_ATOL = 6e-2   # fast numerics vs oracle: worst logit
-FAST_MEAN_ATOL = 1e-2  # fast numerics vs oracle: mean |dlogit| per step (measured 4-6e-3 on the tiny models)
+RELAXED_MAX_ATOL = 6e-2   # relaxed numerics vs oracle: worst logit
+RELAXED_MEAN_ATOL = 1e-2  # relaxed numerics vs oracle: mean |dlogit| per step
+NTHREADS = max(1, min(os.cpu_count() or 1, 32))
 
 
 def geom_of(spec, neox=False):
@@ -40,8 +45,8 @@ def make(jal, oracle, spec, seed, neox=False, kv_dtype=None, n_ctx=256, recipe_h
          sliding_window=0, numerics=None):
     buf = jal.synth_gguf(spec, seed)
     _, tensors = gguf_py.parse(buf)
-    om = oracle.Model(tensors, geom_of(spec, neox), nthreads=8, sliding_window=sliding_window,
-                      **(oracle_kwargs or {}))
+    om = oracle.Model(tensors, geom_of(spec, neox), nthreads=NTHREADS, sliding_window=sliding_window,
+                      kv_f16=kv_dtype == jal.KV_F16, **(oracle_kwargs or {}))
     recipe = jal.LlamaRecipe.from_gguf(buf)
     if recipe_hook:
         recipe_hook(recipe)
@@ -62,7 +67,8 @@ def prompt_of(seed, n=16, vocab=4096):
 
 
 def run_parity(om, ctx, prompt, n_decode, cap, atol=LOGIT_ATOL):
-    """Reference numerics: logits within atol every step, identical greedy ids."""
+    """Reference-order numerics, free-running: each step decodes the argmax of
+    the previous step; logits within atol every step and identical greedy ids."""
     kvo = om.new_kv(cap)
     lo = om.prefill(kvo, cap, prompt, 0)
     lg = ctx.prefill_step(prompt, 0)
@@ -83,8 +89,8 @@ def run_parity(om, ctx, prompt, n_decode, cap, atol=LOGIT_ATOL):
     return tokens, kvo, worst
 
 
-def run_fast(om, ctx, prompt, n_decode, cap):
-    """Fast numerics, teacher-forced on the oracle's greedy tokens."""
+def run_relaxed(om, ctx, prompt, n_decode, cap):
+    """Relaxed numerics, teacher-forced on the oracle's greedy tokens."""
     kvo = om.new_kv(cap)
     lo = om.prefill(kvo, cap, prompt, 0)
     lg = ctx.prefill_step(prompt, 0)
@@ -96,7 +102,7 @@ def run_fast(om, ctx, prompt, n_decode, cap):
         to, tg = int(np.argmax(lo)), int(np.argmax(lg))
         agree.append(to == tg)
         # A different argmax is allowed only at a near-tie of the oracle's logits.
-        assert to == tg or lo[tg] >= lo[to] - FAST_MAX_ATOL, f"step {step}: argmax {tg} vs oracle {to}"
+        assert to == tg or lo[tg] >= lo[to] - RELAXED_MAX_ATOL, f"step {step}: argmax {tg} vs oracle {to}"
 
     check(lo, lg, -1)
     tok = int(np.argmax(lo))
@@ -105,8 +111,8 @@ def run_fast(om, ctx, prompt, n_decode, cap):
         lg = ctx.decode_step(tok)
         check(lo, lg, step)
         tok = int(np.argmax(lo))
-    assert max(errs) <= FAST_MAX_ATOL, f"worst |dlogit| {max(errs):.3e}"
-    assert max(means) <= FAST_MEAN_ATOL, f"worst mean |dlogit| {max(means):.3e}"
+    assert max(errs) <= RELAXED_MAX_ATOL, f"worst |dlogit| {max(errs):.3e}"
+    assert max(means) <= RELAXED_MEAN_ATOL, f"worst mean |dlogit| {max(means):.3e}"
     return max(errs), float(np.mean(agree))
 
 
@@ -122,18 +128,25 @@ def test_tiny_llama_greedy_64_matches_oracle_f32_kv(jal, oracle, torch_cuda):
     n_pos = len(prompt) + N_DECODE
     kvg = ctx.export_kv(n_pos, spec.num_layers, spec.n_heads_kv * spec.head_dim)
     kvr = kvo.reshape(spec.num_layers, 2, 256, -1)[:, :, :n_pos, :].ravel()
-    assert np.max(np.abs(kvg - kvr)) / np.max(np.abs(kvr)) <= 1e-5
-    # The on-device greedy loop (argmax on device) yields the same ids.
-    ctx2 = new_ctx(jal, recipe, cache)
+    assert np.array_equal(kvg, kvr)
+    # The serving path (FAST): the same bars, free-running, then the on-device
+    # greedy loop (argmax on device, one CUDA graph of 1 + 5L + 2 kernels per
+    # step) yields the same ids.
+    ctx_f = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST)
+    tokens_f, _, worst_f = run_parity(om, ctx_f, prompt, N_DECODE, 256)
+    print(f"tiny llama f32-KV fast numerics worst |dlogit| = {worst_f:.3e}")
+    assert tokens_f == tokens
+    assert ctx_f.launches_per_step() == 1 + 5 * spec.num_layers + 2
+    ctx2 = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST)
     l0 = ctx2.prefill_step(prompt, 0)
     first = int(np.argmax(l0))
     seq = ctx2.decode_greedy(first, N_DECODE)
     assert [first] + [int(t) for t in seq[:-1]] == tokens
     assert ctx2.position() == len(prompt) + N_DECODE
-    # Fast numerics: bounded error, one CUDA graph of 1 + 5L + 2 kernels per step.
-    ctx3 = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST)
-    worst_f, agree = run_fast(om, ctx3, prompt, N_DECODE, 256)
-    print(f"tiny llama fast numerics worst |dlogit| = {worst_f:.3e}, top-1 agreement {agree:.2f}")
+    # Relaxed numerics: bounded error.
+    ctx3 = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_RELAXED)
+    worst_r, agree = run_relaxed(om, ctx3, prompt, N_DECODE, 256)
+    print(f"tiny llama relaxed numerics worst |dlogit| = {worst_r:.3e}, top-1 agreement {agree:.2f}")
     assert ctx3.launches_per_step() == 1 + 5 * spec.num_layers + 2
 
 
@@ -141,8 +154,11 @@ def test_tiny_llama_greedy_fp16_paged_kv(jal, oracle, torch_cuda):
     spec = jal.TINY_LLAMA
     _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2024, kv_dtype=jal.KV_F16,
                                      numerics=jal.NUMERICS_FAST)
-    worst, agree = run_fast(om, ctx, prompt_of(7), N_DECODE, 256)
-    print(f"tiny llama fp16-KV fast worst |dlogit| = {worst:.3e}, top-1 agreement {agree:.2f}")
+    _, _, worst = run_parity(om, ctx, prompt_of(7), N_DECODE, 256)
+    print(f"tiny llama fp16-KV fast worst |dlogit| = {worst:.3e}")
+    worst_r, agree = run_relaxed(om, new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16,
+                                             numerics=jal.NUMERICS_RELAXED), prompt_of(7), N_DECODE, 256)
+    print(f"tiny llama fp16-KV relaxed worst |dlogit| = {worst_r:.3e}, top-1 agreement {agree:.2f}")
 
 
 def test_tiny_qwen2_neox_bias_q8_0(jal, oracle, torch_cuda):
@@ -151,28 +167,30 @@ def test_tiny_qwen2_neox_bias_q8_0(jal, oracle, torch_cuda):
     _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=77, neox=True)
     assert recipe.fields().rope_type == jal.ROPE_NEOX and cache.bias_count() == 3 * spec.num_layers
     run_parity(om, ctx, prompt_of(9), 24, 256)
-    run_fast(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(9), 24, 256)
+    run_parity(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(9), 24, 256)
+    run_relaxed(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_RELAXED), prompt_of(9), 24, 256)
 
 
 def test_tiny_llama_q5_0_weights(jal, oracle, torch_cuda):
-    # Q5_0 layer weights and LM head (the Q8_0 device layout): reference
-    # numerics bit-for-bit order and the fast path's statistical bars.
+    # Q5_0 layer weights and LM head (the Q8_0 device layout).
     spec = jal.SynthSpec(weight_quant=jal.Q5_0, head_quant=jal.Q5_0)
     _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=55)
     run_parity(om, ctx, prompt_of(13), 16, 256)
-    run_fast(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(13), 16, 256)
+    run_parity(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(13), 16, 256)
+    run_relaxed(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_RELAXED), prompt_of(13), 16, 256)
 
 
 @pytest.mark.parametrize("head", ["F16", "F32"])
 def test_tiny_llama_dense_lm_head(jal, oracle, torch_cuda, head):
-    # Unquantized output.weight, streamed in its GGUF element type by the
-    # dense GEMV: reference numerics (column-order f32 dot) bit-for-bit
-    # order, and the fast path's statistical bars.
+    # Unquantized output.weight, streamed in its GGUF element type: the
+    # reference's column-order f32 dot on the FAST and REFERENCE paths, the
+    # bandwidth-ordered dense GEMV on the relaxed one.
     spec = jal.SynthSpec(head_quant=getattr(jal, head))
     _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=91)
     assert cache.total_aligned_bytes() > spec.vocab_size * spec.hidden_dim * (2 if head == "F16" else 4)
     run_parity(om, ctx, prompt_of(5), 16, 256)
-    run_fast(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(5), 16, 256)
+    run_parity(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(5), 16, 256)
+    run_relaxed(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_RELAXED), prompt_of(5), 16, 256)
 
 
 def test_llama4_irope_and_sliding_window(jal, oracle, torch_cuda):
@@ -181,8 +199,10 @@ def test_llama4_irope_and_sliding_window(jal, oracle, torch_cuda):
     _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=5, recipe_hook=lambda r: r.with_irope_mask(mask),
                                      oracle_kwargs=dict(skip_rope=np.array(mask, np.uint8)), sliding_window=8)
     run_parity(om, ctx, prompt_of(3, n=12), 12, 256)
-    run_fast(om, new_ctx(jal, recipe, cache, sliding_window=8, numerics=jal.NUMERICS_FAST), prompt_of(3, n=12), 12,
-             256)
+    run_parity(om, new_ctx(jal, recipe, cache, sliding_window=8, numerics=jal.NUMERICS_FAST), prompt_of(3, n=12), 12,
+               256)
+    run_relaxed(om, new_ctx(jal, recipe, cache, sliding_window=8, numerics=jal.NUMERICS_RELAXED), prompt_of(3, n=12),
+                12, 256)
 
 
 def test_llama3_smooth_scaling_model(jal, oracle, torch_cuda):
@@ -197,6 +217,7 @@ def test_llama3_smooth_scaling_model(jal, oracle, torch_cuda):
     _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=6, recipe_hook=hook,
                                      oracle_kwargs=dict(scaling=dict(kind=2, factor=8.0, low=1.0, high=4.0, orig=64)))
     run_parity(om, ctx, prompt_of(4), 8, 256)
+    run_parity(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST), prompt_of(4), 8, 256)
 
 
 def test_batched_prefill_equals_sequential_and_chunked(jal, oracle, torch_cuda):
@@ -204,7 +225,8 @@ def test_batched_prefill_equals_sequential_and_chunked(jal, oracle, torch_cuda):
     spec = jal.TINY_LLAMA
     buf, om, recipe, cache, ctx = make(jal, oracle, spec, seed=31)
     prompt = prompt_of(5, n=20)
-    for numerics, atol in ((jal.NUMERICS_REFERENCE, 0.0), (jal.NUMERICS_FAST, FAST_MAX_ATOL)):
+    for numerics, atol in ((jal.NUMERICS_REFERENCE, 0.0), (jal.NUMERICS_FAST, 0.0),
+                           (jal.NUMERICS_RELAXED, RELAXED_MAX_ATOL)):
         ca = new_ctx(jal, recipe, cache, numerics=numerics)
         la = ca.prefill_step(prompt, 0)
         cb = new_ctx(jal, recipe, cache, numerics=numerics)
@@ -223,7 +245,7 @@ def test_batched_prefill_equals_sequential_and_chunked(jal, oracle, torch_cuda):
 def test_fail_closed_errors_keep_position(jal, oracle, torch_cuda):
     # lib.rs:783-871, 963-1036: fail closed without advancing the position
     spec = jal.TINY_LLAMA
-    for numerics in (jal.NUMERICS_FAST, jal.NUMERICS_REFERENCE):
+    for numerics in (jal.NUMERICS_FAST, jal.NUMERICS_REFERENCE, jal.NUMERICS_RELAXED):
         _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2, n_ctx=20, numerics=numerics)
         ctx.prefill_step(prompt_of(1, n=19), 0)
         with pytest.raises(jal.TensorBoundsError):
@@ -240,36 +262,36 @@ def test_fail_closed_errors_keep_position(jal, oracle, torch_cuda):
 
 @pytest.mark.parametrize("kv_name,quant_name", [("KV_F32", "Q4_0"), ("KV_F16", "Q4_0"), ("KV_F16", "Q8_0")])
 def test_persistent_decode_kernel_matches_oracle(jal, oracle, torch_cuda, monkeypatch, kv_name, quant_name):
-    """JAL_DECODE=mega: one cooperative launch per token (decode_mega.cu).
+    """JAL_DECODE=mega with relaxed numerics: one cooperative launch per token
+    (decode_mega.cu).
 
-    Same fast-numerics bars as the graph path (teacher-forced against the
-    oracle), plus self-consistency of the on-device greedy loop: the argmax
-    phase picks the host argmax of the same kernel's logits at every step.
-    FFN 1536 keeps every projection on the segmented path (blocks per row a
-    multiple of 4); the LM head has the layers' weight type (the kernel is
-    instantiated per weight type).
+    Relaxed bars (teacher-forced against the oracle), plus self-consistency of
+    the on-device greedy loop: the argmax phase picks the host argmax of the
+    same kernel's logits at every step.  FFN 1536 keeps every projection on
+    the segmented path (blocks per row a multiple of 4); the LM head has the
+    layers' weight type (the kernel is instantiated per weight type).
     """
     q = getattr(jal, quant_name)
     spec = jal.SynthSpec(ffn_dim=1536, weight_quant=q, head_quant=q)
     kv = getattr(jal, kv_name)
     buf = jal.synth_gguf(spec, 909)
     _, tensors = gguf_py.parse(buf)
-    om = oracle.Model(tensors, geom_of(spec), nthreads=8)
+    om = oracle.Model(tensors, geom_of(spec), nthreads=NTHREADS, kv_f16=kv == jal.KV_F16)
     recipe = jal.LlamaRecipe.from_gguf(buf)
     cache = recipe.build_repack_cache(buf)
     monkeypatch.setenv("JAL_DECODE", "mega")
-    ctx = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_FAST)
-    ctx_greedy = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_FAST)
+    ctx = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_RELAXED)
+    ctx_greedy = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_RELAXED)
     monkeypatch.delenv("JAL_DECODE")
     prompt = prompt_of(21)
-    worst, agree = run_fast(om, ctx, prompt, 48, 256)
+    worst, agree = run_relaxed(om, ctx, prompt, 48, 256)
     assert ctx.launches_per_step() == 1
     print(f"persistent decode {kv_name} {quant_name} worst |dlogit| = {worst:.3e}, top-1 agreement {agree:.2f}")
     # Host argmax of step-by-step logits == the kernel's own greedy loop.
     lg = ctx_greedy.prefill_step(prompt, 0)
     first = int(np.argmax(lg))
     monkeypatch.setenv("JAL_DECODE", "mega")
-    ctx_host = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_FAST)
+    ctx_host = new_ctx(jal, recipe, cache, kv_dtype=kv, numerics=jal.NUMERICS_RELAXED)
     monkeypatch.delenv("JAL_DECODE")
     ctx_host.prefill_step(prompt, 0)
     host, tok = [], first
@@ -305,21 +327,38 @@ def test_decode_step_into_caller_buffer(jal, torch_cuda):
 
 @pytest.mark.parametrize("head_dim", [64, 128])
 def test_long_prompt_f16_kv_prefill_attention(jal, oracle, torch_cuda, head_dim):
-    # A 200-token prompt with an f16 cache runs the tensor-core prefill
-    # attention over several 64-query and 64-key tiles: whole prompt, the
-    # same prompt in two chunks (keys of the first chunk read back from the
-    # cache), and a 40-token sliding window, all against the oracle with the
-    # fast-numerics bars.
+    # A 200-token prompt with an f16 cache runs the prefill attention over
+    # several key tiles: whole prompt, the same prompt in two chunks (keys of
+    # the first chunk read back from the cache), and a 40-token sliding
+    # window, all against the oracle (f16-rounded K/V) with the FAST bars; the
+    # relaxed path (tensor-core prefill attention) with its own bars.
     spec = jal.SynthSpec(n_heads_q=512 // head_dim, n_heads_kv=max(1, 128 // head_dim), head_dim=head_dim)
     p = prompt_of(9, n=200)
-    _, om, recipe, cache, _ = make(jal, oracle, spec, seed=61)
-    run_fast(om, new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST), p, 8, 256)
+    _, om, recipe, cache, _ = make(jal, oracle, spec, seed=61, kv_dtype=jal.KV_F16)
+    run_parity(om, new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST), p, 8, 256)
+    run_relaxed(om, new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_RELAXED), p, 8, 256)
     kvo = om.new_kv(256)
     lo = om.prefill(kvo, 256, p, 0)
     ctx = new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
     ctx.prefill_step(p[:130], 0)
     lg = ctx.prefill_step(p[130:], 130)
-    assert float(np.max(np.abs(lo - lg))) <= FAST_MAX_ATOL
-    _, omw, recipe_w, cache_w, _ = make(jal, oracle, spec, seed=61, sliding_window=40)
-    run_fast(omw, new_ctx(jal, recipe_w, cache_w, kv_dtype=jal.KV_F16, sliding_window=40,
-                          numerics=jal.NUMERICS_FAST), p, 8, 256)
+    assert float(np.max(np.abs(lo - lg))) <= LOGIT_ATOL
+    _, omw, recipe_w, cache_w, _ = make(jal, oracle, spec, seed=61, sliding_window=40, kv_dtype=jal.KV_F16)
+    run_parity(omw, new_ctx(jal, recipe_w, cache_w, kv_dtype=jal.KV_F16, sliding_window=40,
+                            numerics=jal.NUMERICS_FAST), p, 8, 256)
+
+
+def test_llama3_8b_shaped_two_layers_long_context(jal, oracle, torch_cuda):
+    """The benchmark's layer shape against the oracle: 2 layers of the
+    Llama-3-8B geometry (dim 4096, 32/8 heads, head_dim 128, FFN 14336, vocab
+    128256, Q4_0, RoPE theta 5e5) with an f16 KV cache, n_ctx 1024 (decode
+    attention on 16-CTA clusters) and a 640-token prompt (prefill GEMM over
+    4096 / 14336 columns, prefill attention over 640 keys), then 16
+    free-running greedy decode steps with the FAST bars."""
+    import dataclasses
+    spec = dataclasses.replace(jal.LLAMA3_8B_Q4_0, num_layers=2)
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=88, kv_dtype=jal.KV_F16, n_ctx=1024,
+                                     numerics=jal.NUMERICS_FAST)
+    prompt = prompt_of(12, n=640, vocab=spec.vocab_size)
+    tokens, _, worst = run_parity(om, ctx, prompt, 16, 1024)
+    print(f"8B-shaped 2-layer fast numerics worst |dlogit| = {worst:.3e}, tokens {tokens[:8]}")
