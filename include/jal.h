@@ -331,6 +331,30 @@ typedef struct jal_context_config {
 int jal_context_new(const jal_recipe *r, const jal_model_cache *c,
                     const jal_context_config *cfg, jal_context **out);
 void jal_context_free(jal_context *ctx);
+
+/* Caller-owned KV storage: the reference's KvCacheView, which the engine
+ * owns and the recipe appends into (recipe.rs:2319-2326, layer_kv_mut; the
+ * ExecutionContext holds only the position, lib.rs:1022-1035).  The paged
+ * K / V pools of `model` (this rank's KV heads for a tensor-parallel cache)
+ * for n_ctx positions, kv_dtype JAL_KV_F16 / JAL_KV_F32, page_size 0 = 64;
+ * zero-filled, on the model's device.  A cache outlives every context made
+ * over it and keeps its contents when a context is freed; contexts over one
+ * cache must not run at the same time. */
+typedef struct jal_kv_cache jal_kv_cache;
+int jal_kv_cache_alloc(const jal_model_cache *model, uint64_t n_ctx,
+                       int32_t kv_dtype, uint32_t page_size, jal_kv_cache **out);
+void jal_kv_cache_free(jal_kv_cache *kv);
+/* Device bytes the cache holds. */
+size_t jal_kv_cache_bytes(const jal_kv_cache *kv);
+/* jal_context_new over a caller-owned cache: cfg->kv_dtype and page_size
+ * must match the cache and cfg->n_ctx must not exceed it
+ * (JAL_ERR_CAPABILITY_MISMATCH / JAL_ERR_CONTEXT_LENGTH_EXCEEDED). */
+int jal_context_new_with_kv(const jal_recipe *r, const jal_model_cache *c,
+                            const jal_context_config *cfg, jal_kv_cache *kv,
+                            jal_context **out);
+/* Sets the position (ExecutionContext::position) to resume over a cache
+ * whose positions [0, pos) were filled earlier, e.g. by another context. */
+int jal_context_set_position(jal_context *ctx, size_t pos);
 /* ExecutionContext::position. */
 size_t jal_context_position(const jal_context *ctx);
 /* Drop all positions (KV content becomes stale). */

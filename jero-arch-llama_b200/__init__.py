@@ -80,8 +80,14 @@ class NcclError(K3Error):
     code = ERR_NCCL
 
 
+class DeviceTimeout(K3Error):
+    """A bounded device wait (a copy, a peer's exchange words) gave up."""
+    code = ERR_TIMEOUT
+
+
 _ERRORS = {ERR_TENSOR_BOUNDS: TensorBoundsError, ERR_CAPABILITY_MISMATCH: CapabilityMismatch,
-           ERR_CONTEXT_LENGTH_EXCEEDED: ContextLengthExceeded, ERR_CUDA: CudaError, ERR_NCCL: NcclError}
+           ERR_CONTEXT_LENGTH_EXCEEDED: ContextLengthExceeded, ERR_CUDA: CudaError, ERR_NCCL: NcclError,
+           ERR_TIMEOUT: DeviceTimeout}
 
 
 class RecipeFields(C.Structure):
@@ -172,6 +178,13 @@ _SIGS = {
     "jal_model_cache_total_aligned_bytes": (_SZ, [_P]),
     "jal_model_cache_matrix": (_P, [_P, _SZ, C.c_int]),
     "jal_context_new": (C.c_int, [_P, _P, C.POINTER(ContextConfig), C.POINTER(_P)]),
+    "jal_kv_cache_alloc": (C.c_int, [_P, C.c_uint64, C.c_int32, C.c_uint32, C.POINTER(_P)]),
+    "jal_kv_cache_free": (None, [_P]),
+    "jal_kv_cache_bytes": (_SZ, [_P]),
+    "jal_context_new_with_kv": (C.c_int, [_P, _P, C.POINTER(ContextConfig), _P, C.POINTER(_P)]),
+    "jal_context_set_position": (C.c_int, [_P, _SZ]),
+    "jal_context_test_stall_kv_copy": (C.c_int, [_P, C.c_uint32, C.c_uint64]),
+    "jal_test_peer_exchange_timeout": (C.c_int, [_P, C.c_uint64, C.POINTER(C.c_double)]),
     "jal_context_free": (None, [_P]),
     "jal_context_position": (_SZ, [_P]),
     "jal_context_reset": (C.c_int, [_P]),
@@ -551,18 +564,49 @@ class ModelRepackCache:
 
 
 # ---- ExecutionContext + prefill_step / decode_step --------------------------
+class KvCache:
+    """Caller-owned KV storage for a model (the reference's KvCacheView): it
+    outlives the contexts made over it and keeps its contents."""
+
+    def __init__(self, cache: "ModelRepackCache", n_ctx: int, kv_dtype: int = KV_F16, page_size: int = 64):
+        out = _P()
+        _check(lib().jal_kv_cache_alloc(cache.handle, n_ctx, kv_dtype, page_size, C.byref(out)))
+        self._h = out.value
+        self._cache = cache
+        self.n_ctx, self.kv_dtype, self.page_size = n_ctx, kv_dtype, page_size
+
+    def __del__(self):
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.jal_kv_cache_free(self._h)
+            self._h = None
+
+    @property
+    def handle(self) -> int:
+        return self._h
+
+    def nbytes(self) -> int:
+        return lib().jal_kv_cache_bytes(self._h)
+
+
 class ExecutionContext:
     def __init__(self, recipe: LlamaRecipe, cache: ModelRepackCache, n_ctx: int, kv_dtype: int = KV_F16,
                  page_size: int = 64, sliding_window: int = 0, use_graphs: bool = True,
-                 numerics: int = None):
+                 numerics: int = None, kv: KvCache = None):
         if numerics is None:
             numerics = NUMERICS_FAST
         cfg = ContextConfig(n_ctx, kv_dtype, page_size, sliding_window, 1 if use_graphs else 0, numerics)
         out = _P()
-        _check(lib().jal_context_new(recipe.handle, cache.handle, C.byref(cfg), C.byref(out)))
+        if kv is None:
+            _check(lib().jal_context_new(recipe.handle, cache.handle, C.byref(cfg), C.byref(out)))
+        else:
+            _check(lib().jal_context_new_with_kv(recipe.handle, cache.handle, C.byref(cfg), kv.handle, C.byref(out)))
         self._h = out.value
-        self._recipe, self._cache = recipe, cache
+        self._recipe, self._cache, self._kv = recipe, cache, kv
         self.vocab = cache.vocab_size()
+
+    def set_position(self, pos: int) -> None:
+        """Resume at `pos` over a KV cache whose positions [0, pos) are filled."""
+        _check(lib().jal_context_set_position(self._h, pos))
 
     def __del__(self):
         if getattr(self, "_h", None) and _lib is not None:

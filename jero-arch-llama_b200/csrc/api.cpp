@@ -2,6 +2,7 @@
 // exceptions into status codes and forward to the model / kernel layers.
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -12,6 +13,7 @@
 #include "device.hpp"
 #include "gguf.hpp"
 #include "jal.h"
+#include "jal_test.h"
 #include "model.hpp"
 
 namespace jal {
@@ -37,6 +39,9 @@ struct jal_context {
 };
 struct jal_tp {
   std::unique_ptr<TpComm> t;
+};
+struct jal_kv_cache {
+  std::unique_ptr<KvCache> kv;
 };
 
 #define NEED(p)                                                  \
@@ -487,6 +492,22 @@ const jal_cached_matrix *jal_model_cache_matrix(const jal_model_cache *cc, size_
 
 // ---- context --------------------------------------------------------------
 
+static ContextConfig context_config(const jal_context_config *cfg) {
+  ContextConfig cc;
+  cc.n_ctx = cfg->n_ctx;
+  if (cfg->kv_dtype != JAL_KV_F16 && cfg->kv_dtype != JAL_KV_F32)
+    fail(JAL_ERR_INVALID_ARGUMENT, "unknown KV dtype %d", cfg->kv_dtype);
+  cc.kv_f16 = cfg->kv_dtype == JAL_KV_F16;
+  cc.page_size = cfg->page_size ? cfg->page_size : 64;
+  cc.sliding_window = cfg->sliding_window;
+  cc.use_graphs = cfg->use_graphs != 0;
+  if (cfg->numerics != JAL_NUMERICS_FAST && cfg->numerics != JAL_NUMERICS_REFERENCE &&
+      cfg->numerics != JAL_NUMERICS_RELAXED)
+    fail(JAL_ERR_INVALID_ARGUMENT, "unknown numerics mode %d", cfg->numerics);
+  cc.numerics = cfg->numerics;
+  return cc;
+}
+
 int jal_context_new(const jal_recipe *r, const jal_model_cache *c, const jal_context_config *cfg, jal_context **out) {
   return guard([&] {
     NEED(r);
@@ -494,19 +515,51 @@ int jal_context_new(const jal_recipe *r, const jal_model_cache *c, const jal_con
     NEED(cfg);
     NEED(out);
     *out = nullptr;
-    ContextConfig cc;
-    cc.n_ctx = cfg->n_ctx;
-    cc.kv_f16 = cfg->kv_dtype == JAL_KV_F16;
-    cc.page_size = cfg->page_size ? cfg->page_size : 64;
-    cc.sliding_window = cfg->sliding_window;
-    cc.use_graphs = cfg->use_graphs != 0;
-    if (cfg->numerics != JAL_NUMERICS_FAST && cfg->numerics != JAL_NUMERICS_REFERENCE &&
-        cfg->numerics != JAL_NUMERICS_RELAXED)
-      fail(JAL_ERR_INVALID_ARGUMENT, "unknown numerics mode %d", cfg->numerics);
-    cc.numerics = cfg->numerics;
     auto h = std::make_unique<jal_context>();
-    h->ctx = create_context(r->r, *c->c, cc);
+    h->ctx = create_context(r->r, *c->c, context_config(cfg));
     *out = h.release();
+  });
+}
+
+int jal_kv_cache_alloc(const jal_model_cache *c, uint64_t n_ctx, int32_t kv_dtype, uint32_t page_size,
+                       jal_kv_cache **out) {
+  return guard([&] {
+    NEED(c);
+    NEED(out);
+    *out = nullptr;
+    if (kv_dtype != JAL_KV_F16 && kv_dtype != JAL_KV_F32) fail(JAL_ERR_INVALID_ARGUMENT, "unknown KV dtype %d", kv_dtype);
+    auto h = std::make_unique<jal_kv_cache>();
+    h->kv = create_kv_cache(*c->c, n_ctx, kv_dtype == JAL_KV_F16, page_size);
+    *out = h.release();
+  });
+}
+
+void jal_kv_cache_free(jal_kv_cache *kv) { delete kv; }
+
+size_t jal_kv_cache_bytes(const jal_kv_cache *kv) { return kv ? kv->kv->bytes() : 0; }
+
+int jal_context_new_with_kv(const jal_recipe *r, const jal_model_cache *c, const jal_context_config *cfg,
+                            jal_kv_cache *kv, jal_context **out) {
+  return guard([&] {
+    NEED(r);
+    NEED(c);
+    NEED(cfg);
+    NEED(kv);
+    NEED(out);
+    *out = nullptr;
+    auto h = std::make_unique<jal_context>();
+    h->ctx = create_context(r->r, *c->c, context_config(cfg), kv->kv.get());
+    *out = h.release();
+  });
+}
+
+int jal_context_set_position(jal_context *ctx, size_t pos) {
+  return guard([&] {
+    NEED(ctx);
+    if (pos > ctx->ctx->cfg.n_ctx)
+      fail(JAL_ERR_CONTEXT_LENGTH_EXCEEDED, "position %zu exceeds n_ctx %llu", pos,
+           (unsigned long long)ctx->ctx->cfg.n_ctx);
+    ctx->ctx->position = pos;
   });
 }
 
@@ -699,3 +752,53 @@ int jal_context_tp_exchange(const jal_context *h, int *out) {
 }
 
 }  // extern "C"
+
+// ---- test hooks (jal_test.h) ------------------------------------------------
+
+int jal_context_test_stall_kv_copy(jal_context *h, uint32_t extra_bytes, uint64_t wait_ns) {
+  return guard([&] {
+    NEED(h);
+    Context &c = *h->ctx;
+    if (!c.exact) fail(JAL_ERR_CAPABILITY_MISMATCH, "the stall hook drives the FAST single-GPU decode attention");
+    c.test_stall_tx = extra_bytes;
+    c.test_wait_ns = wait_ns;
+    if (c.graph) {  // the captured step holds the old arguments
+      JAL_CUDA(cudaStreamSynchronize(c.stream));
+      cudaGraphExecDestroy(c.graph);
+      c.graph = nullptr;
+    }
+  });
+}
+
+int jal_test_peer_exchange_timeout(const jal_cached_matrix *mat, uint64_t wait_ns, double *elapsed_ms) {
+  return guard([&] {
+    NEED(mat);
+    check_block_scaled(mat);
+    const DevMat &w = mat->m.dm;
+    const int64_t K = w.cols;
+    DevBuffer x((size_t)K * 4), nw((size_t)K * 4), slot((size_t)K * 8), y((size_t)w.rows * 4), words(64);
+    std::vector<float> one((size_t)K, 1.0f);
+    JAL_CUDA(cudaMemcpy(x.ptr, one.data(), (size_t)K * 4, cudaMemcpyHostToDevice));
+    JAL_CUDA(cudaMemcpy(nw.ptr, one.data(), (size_t)K * 4, cudaMemcpyHostToDevice));
+    JAL_CUDA(cudaMemset(slot.ptr, 0, slot.bytes));  // flag 0: never this step's (epoch 0, phase 0 -> flag 1)
+    JAL_CUDA(cudaMemset(words.ptr, 0, words.bytes));
+    GemvArgs a;
+    a.w = w; a.rows = w.rows; a.m = 1; a.in_mode = GEMV_IN_NORM; a.x = x.as<float>(); a.x_stride = K;
+    a.norm_w = nw.as<float>(); a.eps = 1e-5f; a.out_mode = GEMV_OUT_STORE; a.y = y.as<float>(); a.y_stride = w.rows;
+    a.peer_in = slot.as<unsigned long long>(); a.peer_world = 1; a.peer_phase = 0;
+    a.peer_epoch = (const uint32_t *)words.as<char>(); a.err = (int *)(words.as<char>() + 16);
+    a.peer_wait_ns = wait_ns;
+    if (!gemv_peer_supported(a)) fail(JAL_ERR_CAPABILITY_MISMATCH, "matrix shape not on the exchange GEMV");
+    gemv_init();
+    JAL_CUDA(cudaDeviceSynchronize());
+    const auto t0 = std::chrono::steady_clock::now();
+    launch_gemv(a, nullptr);
+    JAL_CUDA(cudaGetLastError());
+    JAL_CUDA(cudaDeviceSynchronize());
+    const auto t1 = std::chrono::steady_clock::now();
+    if (elapsed_ms) *elapsed_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
+    int err = 0;
+    JAL_CUDA(cudaMemcpy(&err, words.as<char>() + 16, 4, cudaMemcpyDeviceToHost));
+    if (err & kErrPeerWait) fail(JAL_ERR_TIMEOUT, "tensor-parallel exchange wait gave up (as arranged)");
+  });
+}

@@ -132,7 +132,7 @@ __device__ __forceinline__ float embed_value(const uint8_t *emb, int quant, int6
 
 // ---- mbarrier / bulk-copy helpers (shared::cta barrier, own-CTA destination;
 // no multicast)
-constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polls
+constexpr uint64_t kWaitNs = 2000000000ull;  // a copy not landed after 2 s: give up
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -152,11 +152,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Polls at most kWaitLimit times; false when the wait gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-  for (uint32_t it = 0; it < kWaitLimit; it++)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Waits for the phase with the given parity for at most limit_ns of wall
+// time (0 = kWaitNs); false when the wait gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t limit_ns = 0) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t lim = limit_ns ? limit_ns : kWaitNs, t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 64; i++)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > lim) return false;
+  }
 }
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
   asm volatile(
@@ -181,16 +191,14 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu_u32(const uint32_t *p) {
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
 constexpr uint64_t kPeerWaitNs = 4000000000ull;  // a peer's words not there after 4 s: give up
 // Eight consecutive flagged words at p (16-byte aligned): waits until every
 // flag equals `flag` and adds their values to v[0..7] in order.  False when
-// the wait gave up (the values are then added as found).
-__device__ __forceinline__ bool peer_take8(const unsigned long long *p, uint32_t flag, float (&v)[8]) {
+// the wait gave up after limit_ns (0 = kPeerWaitNs; the values are then
+// added as found).
+__device__ __forceinline__ bool peer_take8(const unsigned long long *p, uint32_t flag, float (&v)[8],
+                                           uint64_t limit_ns = 0) {
+  const uint64_t lim = limit_ns ? limit_ns : kPeerWaitNs;
   unsigned long long w[8];
   uint64_t t0 = 0;
   bool ok = true;
@@ -202,7 +210,7 @@ __device__ __forceinline__ bool peer_take8(const unsigned long long *p, uint32_t
     for (int k = 0; k < 8; k++) all = all && (uint32_t)(w[k] >> 32) == flag;
     if (all) break;
     if (it == 0) t0 = global_ns();
-    else if (global_ns() - t0 > kPeerWaitNs) { ok = false; break; }
+    else if (global_ns() - t0 > lim) { ok = false; break; }
     __nanosleep(32);
   }
 #pragma unroll

@@ -87,6 +87,7 @@ struct GemvArgs {
   int peer_world = 0;
   float *x_out = nullptr;
   int *err = nullptr;
+  uint64_t peer_wait_ns = 0;    // bound of the exchange wait (0 = 4 s)
   unsigned long long *peer_out[kPeerMax] = {};
   int grid = 0;                 // CTAs (0 = auto)
   int pdl = 0;                  // launch with programmatic dependent launch
@@ -204,13 +205,15 @@ struct AttnDecodeArgs {
   float *out_s = nullptr;
   int *err = nullptr;           // error word: bit 2 = a bounded copy wait gave up
   int pdl = 0;
+  uint64_t wait_ns = 0;         // bound of each copy wait (0 = 2 s)
+  uint32_t test_extra_tx = 0;   // test hook: the first V copy's barrier expects this many bytes more
 };
 void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
 // Reference-order decode attention (xattn.cu): clusters of a.n_splits CTAs
 // per KV head; n_ctx bounds the positions (shared-memory sizing).
 void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s);
 // Cluster size for launch_xattn_decode (>= G), 0 when the shape does not fit.
-int xattn_cluster_size(int head_dim, int f16, int G, int64_t n_ctx);
+int xattn_cluster_size(int head_dim, int f16, int G, int n_kv, int64_t n_ctx);
 // Largest cluster size (<= want) the decode attention kernel can run with
 // for head_dim, KV element type and G query heads per KV head.
 int attn_decode_cluster_size(int head_dim, int f16, int G, int want);

@@ -39,16 +39,18 @@ namespace exact {
 
 constexpr int kSeq = -10000;  // op binade marker: add the segment's terms one by one
 
-struct SumOp {
-  int a, b;        // term range [a, b)
-  int e;           // binade of the run, or kSeq
-  uint32_t inc0, inc1;
+// One entry of the run list: terms [a, b); binade e (or kSeq) in the low
+// 16 bits of `ed`, inc1 - inc0 in the high 16 bits; inc0.
+struct __align__(16) SumOp {
+  int a, b;
+  int ed;
+  uint32_t inc0;
 };
 
 template <int NT>
 struct SumSmem {
   double wtot[NT / 32];
-  int wcount[NT / 32];
+  int wcount[NT / 32], woff[NT / 32];
   SumOp ops[NT];
   float result;
 };
@@ -169,40 +171,60 @@ __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gti
   const bool next_head = __shfl_down_sync(0xffffffffu, head, 1);
   const bool tail = active && (lane == 31 || next_head || tid + 1 >= nseg);
   const unsigned tails = __ballot_sync(0xffffffffu, tail);
-  if (tail) {
-    SumOp op;
-    op.a = mono ? start : a;
-    op.b = b;
-    op.e = mono ? e : kSeq;
-    op.inc0 = c0;
-    op.inc1 = c1;
-    sm.ops[warp * 32 + __popc(tails & ((1u << lane) - 1u))] = op;
-  }
   if (lane == 0) sm.wcount[warp] = __popc(tails);
   group_sync<NT>(bar);
-
-  // 4. apply the runs in order
-  if (tid == 0) {
-    float s = s0;
+  if (tid == 0) {  // run-list offsets of the warps
+    int o = 0;
     for (int w = 0; w < NW; w++) {
-      const int cnt = sm.wcount[w];
-      for (int k = 0; k < cnt; k++) {
-        const SumOp op = sm.ops[w * 32 + k];
-        bool done = false;
-        if (op.e != kSeq) {
-          const uint32_t bits = __float_as_uint(s);
-          if ((int)(bits >> 23) == op.e + 127) {  // positive, in the run's binade
-            const uint32_t N = (bits & 0x7FFFFFu) | 0x800000u;
-            const uint32_t inc = (N & 1u) ? op.inc1 : op.inc0;
-            if (N + inc < 0x1000000u) {
-              s = __uint_as_float(bits + inc);
-              done = true;
-            }
+      sm.woff[w] = o;
+      o += sm.wcount[w];
+    }
+    sm.wcount[0] = o;  // total
+  }
+  group_sync<NT>(bar);
+  if (tail) {
+    SumOp op;
+    int ee = mono ? e : kSeq, delta = (int)c1 - (int)c0;
+    if (delta < -32767 || delta > 32767) ee = kSeq;  // cannot happen for sane inputs; stay exact
+    op.a = mono ? start : a;
+    op.b = b;
+    op.ed = (int)(((uint32_t)ee & 0xffffu) | ((uint32_t)delta << 16));
+    op.inc0 = c0;
+    sm.ops[sm.woff[warp] + __popc(tails & ((1u << lane) - 1u))] = op;
+  }
+  group_sync<NT>(bar);
+
+  // 4. apply the runs in order (each entry prefetched one step ahead)
+  if (tid == 0) {
+    const int total = sm.wcount[0];
+    float s = s0;
+    SumOp cur = sm.ops[0];
+    for (int k = 0; k < total; k++) {
+      const SumOp nxt = k + 1 < total ? sm.ops[k + 1] : cur;
+      const int e = (int)(short)(cur.ed & 0xffff);
+      bool done = false;
+      if (e != kSeq) {
+        const uint32_t bits = __float_as_uint(s);
+        if ((int)(bits >> 23) == e + 127) {  // positive, in the run's binade
+          const uint32_t N = (bits & 0x7FFFFFu) | 0x800000u;
+          const uint32_t inc = (N & 1u) ? (uint32_t)((int)cur.inc0 + (cur.ed >> 16)) : cur.inc0;
+          if (N + inc < 0x1000000u) {
+            s = __uint_as_float(bits + inc);
+            done = true;
           }
         }
-        if (!done)
-          for (int i = op.a; i < op.b; i++) s = __fadd_rn(s, t[i]);
       }
+      if (!done) {
+        for (int i0 = cur.a; i0 < cur.b; i0 += 16) {  // 16 loads in flight, then the adds in order
+          float v[16];
+#pragma unroll
+          for (int u = 0; u < 16; u++) v[u] = i0 + u < cur.b ? t[i0 + u] : 0.0f;
+#pragma unroll
+          for (int u = 0; u < 16; u++)
+            if (i0 + u < cur.b) s = __fadd_rn(s, v[u]);
+        }
+      }
+      cur = nxt;
     }
     sm.result = s;
   }

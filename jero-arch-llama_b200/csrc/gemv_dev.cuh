@@ -233,7 +233,7 @@ __device__ __forceinline__ void prologue_m1_impl(const GemvArgs &a, char *smem, 
       v[j][4] = x1.x; v[j][5] = x1.y; v[j][6] = x1.z; v[j][7] = x1.w;
       if (peer) {  // residual + partials in rank order
         for (int r = 0; r < a.peer_world; r++)
-          peer_ok = peer_take8(a.peer_in + (size_t)r * a.x_stride + i * 8, flag, v[j]) && peer_ok;
+          peer_ok = peer_take8(a.peer_in + (size_t)r * a.x_stride + i * 8, flag, v[j], a.peer_wait_ns) && peer_ok;
         if (blockIdx.x == 0 && a.x_out) {
           float4 *op = (float4 *)(a.x_out + i * 8);
           op[0] = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);

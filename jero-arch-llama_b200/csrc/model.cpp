@@ -881,7 +881,44 @@ static void setup_mega(Context &ctx, int sms) {
 
 static void setup_tp_exchange(Context &ctx, int sms);
 
-std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, const ContextConfig &cfg0) {
+size_t KvCache::bytes() const {
+  size_t b = 0;
+  for (const auto &p : bufs) b += p->bytes;
+  return b;
+}
+
+// Paged layout [layer][page][kv_head][slot][head_dim], K and V pools, with an
+// identity page table; zero-filled.
+std::unique_ptr<KvCache> create_kv_cache(const ModelCache &c, uint64_t n_ctx, int kv_f16, uint32_t page_size) {
+  if (n_ctx == 0) fail(JAL_ERR_INVALID_ARGUMENT, "n_ctx must be positive");
+  if (page_size == 0) page_size = 64;
+  JAL_CUDA(cudaSetDevice(c.device));
+  const Geometry &g = c.lgeom;
+  auto kc = std::make_unique<KvCache>();
+  kc->n_ctx = n_ctx;
+  kc->device = c.device;
+  const uint64_t ps = page_size, n_pages = (n_ctx + ps - 1) / ps;
+  KvView &kv = kc->kv;
+  kv.f16 = kv_f16 ? 1 : 0;
+  kv.n_pages = (int64_t)n_pages; kv.page_size = (int64_t)ps; kv.n_kv = (int64_t)g.n_heads_kv;
+  kv.head_dim = (int64_t)g.head_dim; kv.n_layers = (int64_t)g.num_layers;
+  const size_t kv_elems = (size_t)g.num_layers * n_pages * g.n_heads_kv * ps * g.head_dim;
+  const size_t esz = kv.f16 ? 2 : 4;
+  auto kb = alloc(kv_elems * esz), vb = alloc(kv_elems * esz);
+  JAL_CUDA(cudaMemset(kb->ptr, 0, kb->bytes));
+  JAL_CUDA(cudaMemset(vb->ptr, 0, vb->bytes));
+  kv.k = kb->ptr; kv.v = vb->ptr;
+  std::vector<int32_t> pt(n_pages);
+  for (uint64_t i = 0; i < n_pages; i++) pt[i] = (int32_t)i;
+  auto ptb = alloc(n_pages * 4);
+  JAL_CUDA(cudaMemcpy(ptb->ptr, pt.data(), n_pages * 4, cudaMemcpyHostToDevice));
+  kv.page_table = ptb->as<int32_t>();
+  kc->bufs = {kb, vb, ptb};
+  return kc;
+}
+
+std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, const ContextConfig &cfg0,
+                                        const KvCache *ext_kv) {
   JAL_CUDA(cudaSetDevice(c.device));
   auto ctx = std::make_unique<Context>();
   ctx->cache = &c;
@@ -911,27 +948,25 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
     fail(JAL_ERR_CAPABILITY_MISMATCH, "hidden/ffn dims exceed the decode GEMV shared-memory staging");
   JAL_CUDA(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking));
   ctx->stream = ctx->own_stream;
-  const uint64_t n_ctx = ctx->cfg.n_ctx, ps = ctx->cfg.page_size, n_pages = (n_ctx + ps - 1) / ps;
+  const uint64_t n_ctx = ctx->cfg.n_ctx;
   const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv;
   const uint64_t V = c.plan.v_pad * c.plan.world;  // gathered logits (>= vocab)
+  if (ext_kv) {  // a caller-owned cache: its geometry must be this model's
+    const KvView &e = ext_kv->kv;
+    if (ext_kv->device != c.device || e.n_layers != (int64_t)g.num_layers || e.n_kv != (int64_t)g.n_heads_kv ||
+        e.head_dim != (int64_t)g.head_dim)
+      fail(JAL_ERR_CAPABILITY_MISMATCH, "KV cache was allocated for another model geometry or device");
+    if (e.f16 != ctx->cfg.kv_f16 || (uint64_t)e.page_size != ctx->cfg.page_size)
+      fail(JAL_ERR_CAPABILITY_MISMATCH, "KV cache dtype / page size differ from the context configuration");
+    if (n_ctx > ext_kv->n_ctx)
+      fail(JAL_ERR_CONTEXT_LENGTH_EXCEEDED, "context n_ctx %llu exceeds the KV cache's %llu positions",
+           (unsigned long long)n_ctx, (unsigned long long)ext_kv->n_ctx);
+    ctx->kv = e;
+  } else {
+    ctx->own_kv = create_kv_cache(c, n_ctx, ctx->cfg.kv_f16, ctx->cfg.page_size);
+    ctx->kv = ctx->own_kv->kv;
+  }
   KvView &kv = ctx->kv;
-  kv.f16 = ctx->cfg.kv_f16;
-  kv.n_pages = (int64_t)n_pages; kv.page_size = (int64_t)ps; kv.n_kv = (int64_t)g.n_heads_kv;
-  kv.head_dim = (int64_t)g.head_dim; kv.n_layers = (int64_t)g.num_layers;
-  size_t kv_elems = (size_t)g.num_layers * n_pages * g.n_heads_kv * ps * g.head_dim;
-  size_t esz = kv.f16 ? 2 : 4;
-  auto kb = alloc(kv_elems * esz), vb = alloc(kv_elems * esz);
-  JAL_CUDA(cudaMemsetAsync(kb->ptr, 0, kb->bytes, ctx->stream));
-  JAL_CUDA(cudaMemsetAsync(vb->ptr, 0, vb->bytes, ctx->stream));
-  kv.k = kb->ptr; kv.v = vb->ptr;
-  ctx->bufs.push_back(kb);
-  ctx->bufs.push_back(vb);
-  std::vector<int32_t> pt(n_pages);
-  for (uint64_t i = 0; i < n_pages; i++) pt[i] = (int32_t)i;
-  auto ptb = alloc(n_pages * 4);
-  JAL_CUDA(cudaMemcpy(ptb->ptr, pt.data(), n_pages * 4, cudaMemcpyHostToDevice));
-  kv.page_table = ptb->as<int32_t>();
-  ctx->bufs.push_back(ptb);
   // RoPE tables.
   uint64_t half = g.rotary_dim / 2;
   std::vector<float> inv(half), cs, sn;
@@ -968,7 +1003,7 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
     }
     if (!dense_quant(c.lm_head.quant)) need(c.lm_head.dm, GEMV_IN_NORM, GEMV_OUT_STORE, (int64_t)c.vocab_size, "LM head");
     ctx->x_splits = xattn_cluster_size((int)g.head_dim, ctx->cfg.kv_f16, (int)(g.n_heads_q / g.n_heads_kv),
-                                       (int64_t)ctx->cfg.n_ctx);
+                                       (int)g.n_heads_kv, (int64_t)ctx->cfg.n_ctx);
     if (ctx->x_splits <= 0)
       fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: n_ctx %llu does not fit",
            (unsigned long long)ctx->cfg.n_ctx);
@@ -1213,6 +1248,7 @@ void Context::enqueue_exact_step(bool pdl) {
     aa.scale = 1.0f / sqrtf((float)g.head_dim);
     aa.n_splits = x_splits;
     aa.out = attn; aa.out_q = attn_q; aa.out_s = attn_s; aa.err = d_err; aa.pdl = pdl;
+    aa.test_extra_tx = test_stall_tx; aa.wait_ns = test_wait_ns;
     launch_xattn_decode(aa, (int64_t)cfg.n_ctx, stream);
     GemvArgs oa;
     oa.w = L.wo.dm; oa.rows = (int64_t)H; oa.in_mode = GEMV_IN_Q8;

@@ -111,6 +111,18 @@ struct ModelCache {  // ModelRepackCache (repack_cache.rs:2129-2141)
 std::unique_ptr<ModelCache> build_model_cache(const Recipe &r, const GgufFile &g, int device,
                                               const TpComm *tp = nullptr);
 
+// KV storage for one model geometry (this rank's KV heads): the K and V
+// page pools and the page table.  A context either owns one or runs over one
+// that its caller allocated (the reference's caller-owned KvCacheView).
+struct KvCache {
+  KvView kv;
+  uint64_t n_ctx = 0;
+  int device = 0;
+  std::vector<DevBufferPtr> bufs;
+  size_t bytes() const;
+};
+std::unique_ptr<KvCache> create_kv_cache(const ModelCache &c, uint64_t n_ctx, int kv_f16, uint32_t page_size);
+
 struct ContextConfig {
   uint64_t n_ctx = 4096;
   int kv_f16 = 1;
@@ -129,8 +141,9 @@ struct Context {
   cudaStream_t stream = nullptr;
   cudaStream_t own_stream = nullptr;
   uint64_t position = 0;
-  // KV
+  // KV: a view of own_kv, or of a caller-owned cache
   KvView kv;
+  std::unique_ptr<KvCache> own_kv;
   std::vector<DevBufferPtr> bufs;
   // device state
   int64_t *d_pos = nullptr;
@@ -156,6 +169,11 @@ struct Context {
   // xattn kernels, x_splits CTAs per KV head in decode attention.
   bool exact = false;
   int x_splits = 0;
+  // Test hook (jal_test.h): the decode attention's first V copy barrier
+  // expects test_stall_tx bytes more than are sent, so its bounded wait
+  // (test_wait_ns) runs out.
+  uint32_t test_stall_tx = 0;
+  uint64_t test_wait_ns = 0;
   // prefill scratch (grown on demand)
   uint64_t pf_cap = 0;
   DevBufferPtr pf_buf;
@@ -189,7 +207,10 @@ struct Context {
   void ensure_prefill_capacity(uint64_t m);
 };
 
-std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, const ContextConfig &cfg);
+// ext_kv: run over a caller-owned KV cache (must outlive the context);
+// nullptr: the context allocates its own.
+std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, const ContextConfig &cfg,
+                                        const KvCache *ext_kv = nullptr);
 size_t decode_scratch_bytes(const Recipe &r, uint64_t seq_len_upper_bound);
 
 // f32 RoPE helpers shared with the op entry points (recipe.rs:2560-2660).

@@ -9,22 +9,25 @@
 // Every product and sum is one f32 rounding, no fused multiply-add.
 //
 // Grid: one thread-block cluster of CS CTAs per KV head (CS >= G, the query
-// heads per KV head).  Phase A: every CTA builds q (bias, RoPE) for the G
-// heads and the new k / v (the CTA holding the current position appends
-// them; with an f16 cache the rounded values are what every step reads), then
-// scores its contiguous share of the positions from K rows that arrive by
-// bulk copies into a pitched shared-memory ring (one copy per position row,
-// pitch row + 16 bytes so a warp reading 32 rows at one offset stays
-// conflict-free), one sequential chain per (head, position).  The cluster
-// agrees on each head's max through distributed shared memory and every CTA
-// turns its scores into e_t.  Phase B: CTA g < G gathers head g's e_t in
-// position order, forms the exact sequential denominator
-// (exact::seq_sum_nonneg), and runs the HD output chains (thread d) over all
-// positions in order with V rows streamed through a second bulk-copy ring;
-// a producer warp refills a ring slot once every chain has passed it.  The
-// output row and its QuantizedActQ8 blocks (the O projection's input) are
-// written by that CTA.  Waits on copies are bounded: a wait that gives up
-// sets bit 2 of the context's error word and the kernel runs to its end.
+// heads per KV head).  V moves as stages of R positions that never cross a
+// page (R a power of two dividing the page size, R * row <= 16 KB), one bulk
+// copy per stage.
+// Phase A: every CTA builds q (bias, RoPE) for the G heads and the new k / v
+// (the CTA holding the current position appends them; with an f16 cache the
+// rounded values are what every step reads), then scores its contiguous
+// share of the positions: a thread per position loads its K row (prefetched
+// into L2 before griddepcontrol.wait) into registers, 256 bytes at a time as
+// independent 16-byte loads, and runs the G score chains over the dims in
+// order.  The cluster agrees on each head's max through
+// distributed shared memory and every CTA turns its scores into e_t.
+// Phase B: CTA g < G gathers head g's e_t in position order, forms the exact
+// sequential denominator (exact::seq_sum_nonneg) and runs the HD output
+// chains (thread d) over all positions in order.  Its V stages started
+// streaming into a ring before griddepcontrol.wait; a producer thread
+// refills a slot once every chain has passed it.  That CTA writes the output
+// row and its QuantizedActQ8 blocks (the O projection's input).  Waits on
+// copies are bounded: a wait that gives up sets bit value 2 of the context's
+// error word and the kernel runs to its end.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
@@ -40,30 +43,31 @@ namespace jal {
 namespace {
 
 constexpr int kXT = 256, kXW = kXT / 32;
-constexpr int kTK = 32, kNSK = 4;  // K ring: positions per stage, stages
-constexpr int kTV = 32;            // V ring: positions per stage
-constexpr int kErrCopyWait = 4;
+constexpr int kStageBytes = 16 * 1024;
+constexpr int kMaxNSV = 12;
+constexpr int kErrCopyWait = 2;  // bit of the context error word: a copy wait gave up
 
 template <int HD, bool F16>
 struct XA {
   static constexpr int ES = F16 ? 2 : 4;
   static constexpr int ROW = HD * ES;
-  static constexpr int KP = ROW + 16;
-  static constexpr int CH = 16 / ES;  // elements per 16-byte chunk
-  static constexpr int NSV = F16 ? 6 : 3;  // V ring stages
+  static constexpr int NCH = ROW / 16;  // 16-byte chunks per row
+  static constexpr int CH = 16 / ES;    // elements per chunk
+  static constexpr int GRP = NCH < 16 ? NCH : 16;  // chunks loaded at once (256 bytes)
 };
 
 struct XAttnLayout {
-  size_t kring, vring, sc, E, sum, total;
+  size_t vring, vsrc, sc, E, sum, total;
 };
 
-template <int HD, bool F16>
-__host__ __device__ inline XAttnLayout xattn_layout(int per_cap, int n_ctx) {
-  using A = XA<HD, F16>;
+// Stages of a span of n_ctx positions in units of R (an upper bound, R >= 8).
+__host__ __device__ inline int max_stages(int n_ctx) { return n_ctx / 8 + 2; }
+
+__host__ __device__ inline XAttnLayout xattn_layout(int nsv, int per_cap, int n_ctx) {
   XAttnLayout L;
   size_t o = 0;
-  L.kring = o; o += (size_t)kNSK * kTK * A::KP;
-  L.vring = o; o += (size_t)A::NSV * kTV * A::ROW;
+  L.vring = o; o += (size_t)nsv * kStageBytes;
+  L.vsrc = o; o += (size_t)max_stages(n_ctx) * 8;  // global address of each V stage
   L.sc = o; o += ((size_t)8 * per_cap * 4 + 15) / 16 * 16;
   L.E = o; o += ((size_t)n_ctx * 4 + 15) / 16 * 16;
   L.sum = o; o += (sizeof(exact::SumSmem<kXT>) + 15) / 16 * 16;
@@ -71,44 +75,55 @@ __host__ __device__ inline XAttnLayout xattn_layout(int per_cap, int n_ctx) {
   return L;
 }
 
-// Bulk copies of K (pitched) or V (dense) rows [t0, t0 + n) of KV head h.
-template <int HD, bool F16, bool PITCHED>
-__device__ void issue_rows(const KvView &kv, int64_t layer, int h, const void *base, char *dst, uint64_t *bar,
-                           int64_t t0, int n) {
-  using A = XA<HD, F16>;
-  mbar_expect_tx(bar, (uint32_t)(n * A::ROW));
-  if (PITCHED) {
-    for (int j = 0; j < n; j++) {
-      const int64_t e = adev::kv_elem(kv, layer, h, t0 + j);
-      bulk_g2s(dst + j * A::KP, (const char *)base + e * A::ES, (uint32_t)A::ROW, bar);
+// Stage k of positions [A, B): [max(A, (A/R + k) R), min(B, (A/R + k + 1) R)).
+struct StageRange {
+  int64_t t0;
+  int n;
+};
+__device__ __forceinline__ StageRange stage_of(int64_t A, int64_t B, int R, int k) {
+  const int64_t base = (A / R + k) * R;
+  const int64_t t0 = base > A ? base : A, t1 = base + R < B ? base + R : B;
+  return {t0, (int)(t1 - t0)};
+}
+__device__ __forceinline__ int stage_count(int64_t A, int64_t B, int R) {
+  return B > A ? (int)((B + R - 1) / R - A / R) : 0;
+}
+
+// Dims [c * CH, c * CH + CH) of a row chunk as floats.
+template <bool F16, int CH>
+__device__ __forceinline__ void chunk_vals(uint4 raw, float (&o)[CH]) {
+  if (F16) {
+    const __half2 *h = (const __half2 *)&raw;
+#pragma unroll
+    for (int k = 0; k < CH / 2; k++) {
+      const float2 f = __half22float2(h[k]);
+      o[2 * k] = f.x;
+      o[2 * k + 1] = f.y;
     }
   } else {
-    int done = 0;
-    while (done < n) {  // one copy per page run
-      const int64_t p = t0 + done, slot = p % kv.page_size;
-      const int run = (int)(kv.page_size - slot < n - done ? kv.page_size - slot : n - done);
-      const int64_t e = adev::kv_elem(kv, layer, h, p);
-      bulk_g2s(dst + done * A::ROW, (const char *)base + e * A::ES, (uint32_t)(run * A::ROW), bar);
-      done += run;
-    }
+    o[0] = __uint_as_float(raw.x);
+    o[1] = __uint_as_float(raw.y);
+    o[2] = __uint_as_float(raw.z);
+    o[3] = __uint_as_float(raw.w);
   }
 }
 
-template <int HD, bool F16>
-__global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int per_cap, int n_ctx) {
+template <int HD, bool F16, int GP>
+__global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int per_cap, int n_ctx, int R, int nsv) {
   namespace cg = cooperative_groups;
   using A = XA<HD, F16>;
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(128) char smem[];
-  __shared__ __align__(8) uint64_t kbar[kNSK], vfull[A::NSV], vempty[A::NSV];
-  __shared__ __align__(16) float q_s[8][HD];
+  __shared__ __align__(8) uint64_t vfull[kMaxNSV], vempty[kMaxNSV];
+  __shared__ __align__(16) float q_s[GP][HD];
   __shared__ __align__(16) float kn_s[HD], vn_s[HD];
   __shared__ float cs_s[2][HD / 2];
-  __shared__ float mx_s[8], red_s[kXW][8];
+  __shared__ float mx_s[8], red_s[kXW][GP];
   __shared__ float gmax_s[8];
   __shared__ int bad_s;
-  const XAttnLayout L = xattn_layout<HD, F16>(per_cap, n_ctx);
-  char *kring = smem + L.kring, *vring = smem + L.vring;
+  const XAttnLayout L = xattn_layout(nsv, per_cap, n_ctx);
+  char *vring = smem + L.vring;
+  const char **vsrc = (const char **)(smem + L.vsrc);
   float *sc = (float *)(smem + L.sc);  // [8][per_cap]: scores, then e_t
   float *E = (float *)(smem + L.E);
 
@@ -121,30 +136,39 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   const int64_t span = seq - lo, per = (span + cs - 1) / cs;
   const int64_t s0 = lo + rank * per, s1 = s0 + per < seq ? s0 + per : seq;
   const int len = s1 > s0 ? (int)(s1 - s0) : 0;
-  const int nk = (len + kTK - 1) / kTK;
   const bool vsum = rank < G;
-  const int nv = vsum ? (int)((span + kTV - 1) / kTV) : 0;
+  const int nv = vsum ? stage_count(lo, seq, R) : 0;
 
   if (tid == 0) {
-    for (int s = 0; s < kNSK; s++) mbar_init(&kbar[s], 1);
-    for (int s = 0; s < A::NSV; s++) {
+    for (int s = 0; s < nsv; s++) {
       mbar_init(&vfull[s], 1);
-      mbar_init(&vempty[s], HD);
+      mbar_init(&vempty[s], HD / 32);  // one arrival per consumer warp
     }
     bad_s = 0;
     fence_barrier_init();
     fence_proxy_async();
-    // Rows below the current position were written by earlier launches; the
-    // current row is patched from registers / shared memory below.
-    for (int k = 0; k < nk && k < kNSK; k++) {
-      const int64_t t0 = s0 + (int64_t)k * kTK;
-      issue_rows<HD, F16, true>(a.kv, a.layer, h, a.kv.k, kring + k * kTK * A::KP, &kbar[k], t0,
-                                (int)(s1 - t0 < kTK ? s1 - t0 : kTK));
+  }
+  __syncthreads();
+  // Rows below the current position were written by earlier launches (the
+  // current row is taken from shared memory below).  Thread k looks up stage
+  // k's page (all lookups in parallel): K stages of this CTA's share go to
+  // L2, the first V stages of the whole span into the ring; the addresses of
+  // every V stage are kept for the refills.
+  {
+    const int nks = stage_count(s0, s1, R);
+    for (int k = tid; k < nks; k += kXT) {
+      const StageRange st = stage_of(s0, s1, R, k);
+      l2_prefetch_bulk((const char *)a.kv.k + adev::kv_elem(a.kv, a.layer, h, st.t0) * A::ES,
+                       (uint64_t)st.n * A::ROW);
     }
-    for (int k = 0; k < nv && k < A::NSV; k++) {
-      const int64_t t0 = lo + (int64_t)k * kTV;
-      issue_rows<HD, F16, false>(a.kv, a.layer, h, a.kv.v, vring + k * kTV * A::ROW, &vfull[k], t0,
-                                 (int)(seq - t0 < kTV ? seq - t0 : kTV));
+    for (int k = tid; k < nv; k += kXT) {
+      const StageRange st = stage_of(lo, seq, R, k);
+      const char *src = (const char *)a.kv.v + adev::kv_elem(a.kv, a.layer, h, st.t0) * A::ES;
+      vsrc[k] = src;
+      if (k < nsv) {
+        mbar_expect_tx(&vfull[k], (uint32_t)(st.n * A::ROW) + (k == 0 ? a.test_extra_tx : 0u));
+        bulk_g2s(vring + k * kStageBytes, src, (uint32_t)(st.n * A::ROW), &vfull[k]);
+      }
     }
   }
   const bool rope = !a.skip_rope && pos > 0;
@@ -193,63 +217,64 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
       if (own_pos) adev::store_kv(g == G ? a.kv.k : a.kv.v, a.kv.f16, app + d, o);  // recipe.rs:2319-2326
     }
   }
+  for (int i = tid; i < (GP - G) * HD; i += kXT) q_s[G + i / HD][i % HD] = 0.0f;
   __syncthreads();
 
-  // Phase A: scores.  Warp w takes head w % GP of stage (round * R + w / GP).
-  const int GP = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
-  const int R = kXW / GP < kNSK ? kXW / GP : kNSK;  // stages per round (each in its own ring slot)
+  // Phase A: scores, one thread per position of this CTA's share.
   bool ok = true;
-  float lmax = -INFINITY;  // this thread's head: warp % GP
-  for (int k0 = 0; k0 < nk; k0 += R) {
-    const int k = k0 + warp / GP, g = warp % GP;
-    if (warp / GP < R && k < nk && g < G) {
-      const int slot = k % kNSK;
-      if (!mbar_wait_bounded(&kbar[slot], (uint32_t)((k / kNSK) & 1))) ok = false;
-      const int64_t t0 = s0 + (int64_t)k * kTK;
-      const int n = (int)(s1 - t0 < kTK ? s1 - t0 : kTK);
-      if (lane < n) {
-        const int64_t t = t0 + lane;
-        const char *row = kring + slot * kTK * A::KP + lane * A::KP;
-        const float *qg = q_s[g];
-        float d = -0.0f;
-        if (t == pos) {  // the current row: from the values just built
-          for (int e = 0; e < HD; e++) d = __fadd_rn(d, __fmul_rn(qg[e], kn_s[e]));
-        } else {
-#pragma unroll 4
-          for (int c = 0; c < HD / A::CH; c++) {
-            float kv[A::CH];
-            adev::load_vals<F16, A::CH>(row + c * 16, kv);
+  float lmax[GP];
 #pragma unroll
-            for (int e = 0; e < A::CH; e++) d = __fadd_rn(d, __fmul_rn(qg[c * A::CH + e], kv[e]));
-          }
+  for (int g = 0; g < GP; g++) lmax[g] = -INFINITY;
+  for (int j = tid; j < len; j += kXT) {
+    const int64_t t = s0 + j;
+    float d[GP];
+#pragma unroll
+    for (int g = 0; g < GP; g++) d[g] = -0.0f;
+    if (t == pos) {  // the current row: from the values just built
+      for (int e = 0; e < HD; e++)
+#pragma unroll
+        for (int g = 0; g < GP; g++) d[g] = __fadd_rn(d[g], __fmul_rn(q_s[g][e], kn_s[e]));
+    } else {
+      const uint4 *row = (const uint4 *)((const char *)a.kv.k + adev::kv_elem(a.kv, a.layer, h, t) * A::ES);
+#pragma unroll
+      for (int grp = 0; grp < A::NCH / A::GRP; grp++) {
+        uint4 raw[A::GRP];
+#pragma unroll
+        for (int c = 0; c < A::GRP; c++) raw[c] = row[grp * A::GRP + c];
+#pragma unroll
+        for (int c = 0; c < A::GRP; c++) {
+          float kv[A::CH];
+          chunk_vals<F16, A::CH>(raw[c], kv);
+          const int e0 = (grp * A::GRP + c) * A::CH;
+#pragma unroll
+          for (int e = 0; e < A::CH; e++)
+#pragma unroll
+            for (int g = 0; g < GP; g++) d[g] = __fadd_rn(d[g], __fmul_rn(q_s[g][e0 + e], kv[e]));
         }
-        const float s = __fmul_rn(d, a.scale);
-        sc[g * per_cap + (int)(t - s0)] = s;
-        if (s > lmax) lmax = s;
       }
     }
-    __syncthreads();  // the round's stages are consumed
-    if (tid == 0) {
-      fence_proxy_async();
-      for (int kk = k0; kk < k0 + R && kk < nk; kk++) {
-        const int kn = kk + kNSK;
-        if (kn < nk) {
-          const int64_t t0 = s0 + (int64_t)kn * kTK;
-          issue_rows<HD, F16, true>(a.kv, a.layer, h, a.kv.k, kring + (kn % kNSK) * kTK * A::KP, &kbar[kn % kNSK], t0,
-                                    (int)(s1 - t0 < kTK ? s1 - t0 : kTK));
-        }
+#pragma unroll
+    for (int g = 0; g < GP; g++) {
+      if (g < G) {
+        const float sv = __fmul_rn(d[g], a.scale);
+        sc[g * per_cap + j] = sv;
+        if (sv > lmax[g]) lmax[g] = sv;
       }
     }
   }
-  // Per-head max of this CTA (max is order-independent; NaN never wins, as
-  // with `if score > max_score`).
-  lmax = warp_max(lmax);
-  if (lane == 0) red_s[warp][warp % GP] = lmax;
+  // Per-head max of this CTA (order-independent; NaN never wins, as with
+  // `if score > max_score`).
+#pragma unroll
+  for (int g = 0; g < GP; g++) {
+    float m = warp_max(lmax[g]);
+    if (lane == 0) red_s[warp][g] = m;
+  }
   __syncthreads();
   if (tid < 8) {
     float m = -INFINITY;
-    for (int w = tid; w < kXW; w += GP)
-      if (tid < GP && red_s[w][tid] > m) m = red_s[w][tid];
+    if (tid < GP)
+      for (int w = 0; w < kXW; w++)
+        if (red_s[w][tid] > m) m = red_s[w][tid];
     mx_s[tid] = m;
   }
   if (!ok) bad_s = 1;
@@ -290,28 +315,43 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   if (tid < HD) {  // output chain d = tid over all positions
     const int d = tid;
     for (int k = 0; k < nv; k++) {
-      const int slot = k % A::NSV;
-      if (!mbar_wait_bounded(&vfull[slot], (uint32_t)((k / A::NSV) & 1))) ok = false;
-      const int64_t t0 = lo + (int64_t)k * kTV;
-      const int n = (int)(seq - t0 < kTV ? seq - t0 : kTV);
-      const char *vs = vring + slot * kTV * A::ROW;
-      const float *w = E + (t0 - lo);
-#pragma unroll 8
-      for (int j = 0; j < n; j++) {
-        float v = F16 ? __half2float(((const __half *)(vs + j * A::ROW))[d]) : ((const float *)(vs + j * A::ROW))[d];
-        if (t0 + j == pos) v = vn_s[d];
+      const int slot = k % nsv;
+      if (!mbar_wait_bounded(&vfull[slot], (uint32_t)((k / nsv) & 1), a.wait_ns)) ok = false;
+      const StageRange st = stage_of(lo, seq, R, k);
+      char *vs = vring + slot * kStageBytes;
+      if (st.t0 <= pos && pos < st.t0 + st.n) {  // the current row (only thread d reads element d)
+        const int j = (int)(pos - st.t0);
+        if (F16) ((__half *)(vs + j * A::ROW))[d] = __float2half_rn(vn_s[d]);
+        else ((float *)(vs + j * A::ROW))[d] = vn_s[d];
+      }
+      const float *w = E + (st.t0 - lo);
+      int j = 0;
+      for (; j + 16 <= st.n; j += 16) {
+        float v[16], ww[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+          v[u] = F16 ? __half2float(((const __half *)(vs + (j + u) * A::ROW))[d])
+                     : ((const float *)(vs + (j + u) * A::ROW))[d];
+          ww[u] = w[j + u];
+        }
+#pragma unroll
+        for (int u = 0; u < 16; u++) o = __fadd_rn(o, __fmul_rn(ww[u], v[u]));
+      }
+      for (; j < st.n; j++) {
+        const float v = F16 ? __half2float(((const __half *)(vs + j * A::ROW))[d]) : ((const float *)(vs + j * A::ROW))[d];
         o = __fadd_rn(o, __fmul_rn(w[j], v));
       }
-      mbar_arrive(&vempty[slot]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&vempty[slot]);
     }
   } else if (tid == HD) {  // producer: refill a slot once every chain passed it
-    for (int k = A::NSV; k < nv; k++) {
-      const int slot = k % A::NSV;
-      if (!mbar_wait_bounded(&vempty[slot], (uint32_t)(((k - A::NSV) / A::NSV) & 1))) ok = false;
+    for (int k = nsv; k < nv; k++) {
+      const int slot = k % nsv;
+      if (!mbar_wait_bounded(&vempty[slot], (uint32_t)(((k - nsv) / nsv) & 1), a.wait_ns)) ok = false;
       fence_proxy_async();
-      const int64_t t0 = lo + (int64_t)k * kTV;
-      issue_rows<HD, F16, false>(a.kv, a.layer, h, a.kv.v, vring + slot * kTV * A::ROW, &vfull[slot], t0,
-                                 (int)(seq - t0 < kTV ? seq - t0 : kTV));
+      const StageRange st = stage_of(lo, seq, R, k);
+      mbar_expect_tx(&vfull[slot], (uint32_t)(st.n * A::ROW));
+      bulk_g2s(vring + slot * kStageBytes, vsrc[k], (uint32_t)(st.n * A::ROW), &vfull[slot]);
     }
   }
   if (tid < HD) {
@@ -329,31 +369,53 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
 }
 
 template <int HD, bool F16>
-const void *xattn_fn() {
-  return (const void *)k_xattn<HD, F16>;
+const void *xattn_fn(int G) {
+  if (G <= 1) return (const void *)k_xattn<HD, F16, 1>;
+  if (G <= 2) return (const void *)k_xattn<HD, F16, 2>;
+  if (G <= 4) return (const void *)k_xattn<HD, F16, 4>;
+  return (const void *)k_xattn<HD, F16, 8>;
 }
 
-const void *pick_x(int hd, int f16) {
-  if (hd == 128) return f16 ? xattn_fn<128, true>() : xattn_fn<128, false>();
-  if (hd == 64) return f16 ? xattn_fn<64, true>() : xattn_fn<64, false>();
+const void *pick_x(int hd, int f16, int G) {
+  if (G > 8) return nullptr;
+  if (hd == 128) return f16 ? xattn_fn<128, true>(G) : xattn_fn<128, false>(G);
+  if (hd == 64) return f16 ? xattn_fn<64, true>(G) : xattn_fn<64, false>(G);
   return nullptr;
 }
 
-size_t x_smem(int hd, int f16, int per_cap, int n_ctx) {
-  if (hd == 128) return f16 ? xattn_layout<128, true>(per_cap, n_ctx).total : xattn_layout<128, false>(per_cap, n_ctx).total;
-  return f16 ? xattn_layout<64, true>(per_cap, n_ctx).total : xattn_layout<64, false>(per_cap, n_ctx).total;
+// Positions per stage: the largest power of two dividing the page size with
+// R * row <= 16 KB (and R <= 64: one thread per position in a round).
+int stage_rows(int hd, int f16, int64_t page_size) {
+  const int row = hd * (f16 ? 2 : 4);
+  int R = 1;
+  while (R * 2 <= 64 && R * 2 * row <= kStageBytes && page_size % (R * 2) == 0) R *= 2;
+  return R;
+}
+
+constexpr size_t kSmemCap = 225 * 1024;
+
+// Ring depth for V given what the rest of the layout needs (0 if < 3 fit).
+int v_stages(int per_cap, int n_ctx) {
+  const size_t rest = xattn_layout(0, per_cap, n_ctx).total + 8 * 1024;  // + static shared memory
+  if (rest >= kSmemCap) return 0;
+  int nsv = (int)((kSmemCap - rest) / kStageBytes);
+  if (nsv > kMaxNSV) nsv = kMaxNSV;
+  return nsv >= 3 ? nsv : 0;
 }
 
 }  // namespace
 
-int xattn_cluster_size(int head_dim, int f16, int G, int64_t n_ctx) {
-  const void *fn = pick_x(head_dim, f16);
+int xattn_cluster_size(int head_dim, int f16, int G, int n_kv, int64_t n_ctx) {
+  const void *fn = pick_x(head_dim, f16, G);
   if (!fn || G > 16) return 0;
-  const int want = n_ctx >= 1024 ? 16 : 8;
-  for (int cs = want; cs >= G && cs >= 1; cs /= 2) {
+  // The largest cluster (<= 16, >= G) for which every KV head's cluster is
+  // resident at once: a second wave would double the kernel's latency.
+  int best = 0;
+  for (int cs = 16; cs >= G && cs >= 1; cs /= 2) {
     const int per_cap = (int)((n_ctx + cs - 1) / cs);
-    const size_t smem = x_smem(head_dim, f16, per_cap, (int)n_ctx);
-    if (smem > 227 * 1024) continue;
+    const int nsv = v_stages(per_cap, (int)n_ctx);
+    if (!nsv) continue;
+    const size_t smem = xattn_layout(nsv, per_cap, (int)n_ctx).total;
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (cs > 8) cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaLaunchConfig_t cfg = {};
@@ -368,18 +430,27 @@ int xattn_cluster_size(int head_dim, int f16, int G, int64_t n_ctx) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess && n > 0) return cs;
-    cudaGetLastError();
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    if (n >= n_kv) return cs;
+    if (n > 0 && !best) best = cs;
   }
-  return 0;
+  return best;
 }
 
 void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s) {
-  const void *fn = pick_x((int)a.kv.head_dim, a.kv.f16);
+  const int G = (int)(a.n_heads_q / a.kv.n_kv);
+  const void *fn = pick_x((int)a.kv.head_dim, a.kv.f16, G);
   const int cs = a.n_splits;
-  if (!fn || cs < 1) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: unsupported shape");
-  const int per_cap = (int)((n_ctx + cs - 1) / cs);
-  const size_t smem = x_smem((int)a.kv.head_dim, a.kv.f16, per_cap, (int)n_ctx);
+  if (!fn || cs < G) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: unsupported shape");
+  int per_cap = (int)((n_ctx + cs - 1) / cs), nc = (int)n_ctx;
+  int nsv = v_stages(per_cap, nc), R = stage_rows((int)a.kv.head_dim, a.kv.f16, a.kv.page_size);
+  if (!nsv) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: n_ctx %lld does not fit", (long long)n_ctx);
+  if (R < 8) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: page size %lld not a multiple of 8",
+                  (long long)a.kv.page_size);
+  const size_t smem = xattn_layout(nsv, per_cap, nc).total;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.kv.n_kv * cs));
   cfg.blockDim = dim3(kXT);
@@ -394,8 +465,7 @@ void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s)
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.pdl ? 2 : 1;
-  int nc = (int)n_ctx;
-  void *args[] = {(void *)&a, (void *)&per_cap, (void *)&nc};
+  void *args[] = {(void *)&a, (void *)&per_cap, (void *)&nc, (void *)&R, (void *)&nsv};
   cudaLaunchKernelExC(&cfg, fn, args);
 }
 

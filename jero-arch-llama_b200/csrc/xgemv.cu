@@ -9,21 +9,23 @@
 // row i (recipe.rs:3024-3050).
 //
 // Structure: one CTA of 16 warps per SM owns a contiguous, balanced range of
-// output rows.  K is cut into slabs of 32 blocks (1024 columns).  For a batch
-// of up to 64 rows the CTA streams slab 0 of every row, then slab 1, and so
-// on: a warp takes one (row, slab) unit at a time, lane l owning block
-// 32 * slab + l; its quants and f16 scale arrive through a per-warp ring of
-// cp.async copies (DEPTH units ahead, the first ones issued before
-// griddepcontrol.wait), and its two chunk terms go to a shared-memory slab
-// buffer.  After each slab one owner thread per row folds that slab's 64
-// terms into the row's accumulator, in order, while the warps fill the
-// other buffer with the next slab.  The fold of a row therefore keeps pace
-// with its stream, and the only serial tail is the last slab's 64 adds.
+// output rows; warp w takes rows w, w + 16, ... of it, eight physical rows
+// (four gate / up pairs for SwiGLU) at a time.  A row is streamed in
+// segments of 128 blocks (4096 columns): lane l owns blocks 4l .. 4l + 3 of
+// the segment, loads their quants (64 bytes for Q4_0, 128 for Q8_0) and four
+// f16 scales with non-allocating vector loads, DEPTH units (row, segment)
+// ahead in registers (the first ones before griddepcontrol.wait), and writes
+// its eight chunk terms, in chunk order, into the warp's buffer row for that
+// physical row.  When the eight rows' segment is in the buffer, lanes 0 .. 7
+// each add one row's terms in order onto that row's accumulator.  No CTA
+// barrier is involved after the prologue; the serial adds (256 per segment)
+// of one batch run while the next batch's loads are in flight.
 //
 // The activation prologue (optional RMSNorm, then QuantizedActQ8 per
-// 32-block) is computed by every CTA into shared memory after the wait; the
-// RMSNorm sum of squares is the reference's sequential sum, computed with
-// exact::seq_sum_nonneg.
+// 32-block) is computed by every CTA into shared memory after the wait, in a
+// lane-interleaved layout (block 4l + v of a segment at slot 32v + l) so the
+// main loop's reads are conflict-free; the RMSNorm sum of squares is the
+// reference's sequential sum, computed with exact::seq_sum_nonneg.
 #include <cuda_fp16.h>
 
 #include "common.hpp"
@@ -37,286 +39,341 @@ namespace jal {
 namespace {
 
 constexpr int kNT = 512, kNW = kNT / 32;
-constexpr int kUnits = 64;   // physical rows per batch
-constexpr int kTP = 68;      // term row pitch (floats): 64 terms + 4 (conflict-free owner reads)
+constexpr int kSeg = 128;   // blocks per segment (4096 columns)
+constexpr int kBR = 8;      // physical rows per warp batch (fold lanes)
+constexpr int kBP = 260;    // buffer row pitch (floats): 256 terms + 4 (conflict-free fold reads)
 
 template <int QUANT>
 struct XCfg {
-  static constexpr int BQ = QUANT == JAL_Q4_0 ? 16 : 32;  // quant bytes per block
-  static constexpr int SLOT = 32 * BQ + 64;               // one unit: 32 blocks of quants + 32 f16 scales
-  static constexpr int DEPTH = QUANT == JAL_Q4_0 ? 8 : 5;
+  static constexpr int NQ4 = QUANT == JAL_Q4_0 ? 4 : 8;  // 16-byte quant loads per lane per unit
+  static constexpr int DEPTH = QUANT == JAL_Q4_0 ? 3 : 2;
 };
 
-// Shared memory carve-up (bytes, 16-aligned pieces).
+// Shared memory carve-up (bytes, 16-aligned pieces).  The prologue's
+// scratch (the f32 input row, the norm weights, the squares and the exact
+// sum's workspace) lives in the fold buffers' space, which the main loop
+// uses only after the prologue.
 struct XLayout {
-  int nb, nslab, nbp;
-  size_t act_q, act_m, terms, stage, xsq, sum, total;
+  int nb, nseg, nbp;
+  size_t act_lo, act_hi, act_m, buf, xin, nw, xsq, sum, total;
 };
 
-template <int QUANT>
 __host__ __device__ inline XLayout x_layout(int64_t cols, int in_mode) {
   XLayout L;
   L.nb = (int)(cols / 32);
-  L.nslab = (L.nb + 31) / 32;
-  L.nbp = L.nslab * 32;
+  L.nseg = (L.nb + kSeg - 1) / kSeg;
+  L.nbp = L.nseg * kSeg;
   size_t o = 0;
-  L.act_q = o; o += (size_t)L.nbp * 32;
+  L.act_lo = o; o += (size_t)L.nbp * 16;
+  L.act_hi = o; o += (size_t)L.nbp * 16;
   L.act_m = o; o += (size_t)L.nbp * 16;
-  L.terms = o; o += (size_t)2 * kUnits * kTP * 4;
-  L.stage = o; o += (size_t)kNW * XCfg<QUANT>::DEPTH * XCfg<QUANT>::SLOT;
-  L.xsq = o; if (in_mode == GEMV_IN_NORM) o += (size_t)L.nb * 32 * 4;
-  L.sum = o; if (in_mode == GEMV_IN_NORM) o += (sizeof(exact::SumSmem<kNT>) + 15) / 16 * 16;
-  L.total = o;
+  L.buf = o;
+  const size_t fold = (size_t)kNW * kBR * kBP * 4;
+  const size_t row = ((size_t)L.nb * 32 * 4 + 15) / 16 * 16;
+  size_t p = o;
+  L.xin = p; if (in_mode != GEMV_IN_Q8) p += row;
+  L.nw = p; if (in_mode == GEMV_IN_NORM) p += row;
+  L.xsq = p; if (in_mode == GEMV_IN_NORM) p += row;
+  L.sum = p; if (in_mode == GEMV_IN_NORM) p += (sizeof(exact::SumSmem<kNT>) + 15) / 16 * 16;
+  L.total = o + (fold > p - o ? fold : p - o);
   return L;
 }
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+// Slot of block b in the lane-interleaved activation layout.
+__device__ __forceinline__ int act_slot(int b) {
+  const int s = b / kSeg, i = b % kSeg;
+  return s * kSeg + (i & 3) * 32 + (i >> 2);
 }
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// Position in a warp's unit sequence: batch, slab, k-th unit of the warp.
-struct UnitCursor {
-  int b = 0, s = 0, k = 0, cnt = 0;
-};
 
 // Activation prologue: QuantizedActQ8 of the (optionally RMSNorm'd) input,
-// one warp per 32-block, lane = element.  act_q gets the int8 quants,
-// act_m {scale, sum of quants 0..15, sum of quants 16..31, 0}.
+// one warp per 32-block, lane = element.  Per block slot: quants 0..15 in
+// act_lo, 16..31 in act_hi, {scale, sum of quants 0..15, sum of 16..31, 0}
+// in act_m.  Padding blocks are zero.
 template <typename SumSM>
 __device__ void x_prologue(const GemvArgs &a, const XLayout &L, char *smem, SumSM *ssm) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  int8_t *aq = (int8_t *)(smem + L.act_q);
+  const int tid = threadIdx.x;
+  int8_t *alo = (int8_t *)(smem + L.act_lo), *ahi = (int8_t *)(smem + L.act_hi);
   float4 *am = (float4 *)(smem + L.act_m);
   const int K = L.nb * 32;
-  for (int b = L.nb + warp; b < L.nbp; b += kNW) {  // padding blocks
-    aq[b * 32 + lane] = 0;
-    if (lane == 0) am[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int b = L.nb + tid; b < L.nbp; b += kNT) {  // padding blocks
+    const int sl = act_slot(b);
+    ((uint4 *)alo)[sl] = make_uint4(0u, 0u, 0u, 0u);
+    ((uint4 *)ahi)[sl] = make_uint4(0u, 0u, 0u, 0u);
+    am[sl] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
+  // Four lanes per 32-block (lane sub = 0..3 holds elements 8 sub .. 8 sub +
+  // 7): the block max and the chunk sums combine over the four lanes.
+  const int jobs = L.nb * 4, jobs_r = (jobs + 31) & ~31;
+  auto store = [&](int i, bool valid, const int (&q)[8], float scale) {
+    const int b = i >> 2, sub = i & 3;
+    int s = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) s += q[e];
+    s += __shfl_xor_sync(0xffffffffu, s, 1);  // sub 0, 1: elements 0..15; sub 2, 3: 16..31
+    const int s_hi = __shfl_down_sync(0xffffffffu, s, 2);
+    if (valid) {
+      const int sl = act_slot(b);
+      const uint32_t p0 = (uint32_t)(q[0] & 0xff) | ((uint32_t)(q[1] & 0xff) << 8) | ((uint32_t)(q[2] & 0xff) << 16) |
+                          ((uint32_t)(q[3] & 0xff) << 24);
+      const uint32_t p1 = (uint32_t)(q[4] & 0xff) | ((uint32_t)(q[5] & 0xff) << 8) | ((uint32_t)(q[6] & 0xff) << 16) |
+                          ((uint32_t)(q[7] & 0xff) << 24);
+      int8_t *half = sub < 2 ? alo : ahi;
+      *(uint2 *)(half + sl * 16 + (sub & 1) * 8) = make_uint2(p0, p1);
+      if (sub == 0) am[sl] = make_float4(scale, __int_as_float(s), __int_as_float(s_hi), 0.f);
+    }
+  };
   if (a.in_mode == GEMV_IN_Q8) {
-    for (int b = warp; b < L.nb; b += kNW) {
-      const int q = a.xq[(int64_t)b * 32 + lane];
-      aq[b * 32 + lane] = (int8_t)q;
-      int s = q;
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      s += __shfl_xor_sync(0xffffffffu, s, 8);
-      const int s16 = __shfl_sync(0xffffffffu, s, 16);
-      if (lane == 0) am[b] = make_float4(a.xs[b], __int_as_float(s), __int_as_float(s16), 0.f);
+    for (int i = tid; i < jobs_r; i += kNT) {
+      const bool valid = i < jobs;
+      int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      float scale = 0.0f;
+      if (valid) {
+        const uint2 raw = *(const uint2 *)(a.xq + (int64_t)i * 8);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          q[e] = (int)(int8_t)((raw.x >> (8 * e)) & 0xff);
+          q[4 + e] = (int)(int8_t)((raw.y >> (8 * e)) & 0xff);
+        }
+        scale = a.xs[i >> 2];
+      }
+      store(i, valid, q, scale);
     }
     __syncthreads();
     return;
   }
-  float inv = 1.0f;
-  if (a.in_mode == GEMV_IN_NORM) {
-    float *xsq = (float *)(smem + L.xsq);
-    for (int i = tid; i < K; i += kNT) {
-      const float v = a.x[i];
-      xsq[i] = __fmul_rn(v, v);
+  // One pass of 16-byte loads, all issued before any use, stages the row
+  // (and the norm weights, and the squares) in shared memory.
+  float *xin = (float *)(smem + L.xin), *nw = (float *)(smem + L.nw), *xsq = (float *)(smem + L.xsq);
+  const bool norm = a.in_mode == GEMV_IN_NORM;
+  {
+    constexpr int U = 8;
+    const int n4 = K / 4;
+    for (int i0 = 0; i0 < n4; i0 += U * kNT) {
+      float4 xv[U], wv[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int i = i0 + u * kNT + tid;
+        if (i < n4) {
+          xv[u] = ((const float4 *)a.x)[i];
+          if (norm) wv[u] = ((const float4 *)a.norm_w)[i];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int i = i0 + u * kNT + tid;
+        if (i < n4) {
+          ((float4 *)xin)[i] = xv[u];
+          if (norm) {
+            ((float4 *)nw)[i] = wv[u];
+            ((float4 *)xsq)[i] = make_float4(__fmul_rn(xv[u].x, xv[u].x), __fmul_rn(xv[u].y, xv[u].y),
+                                             __fmul_rn(xv[u].z, xv[u].z), __fmul_rn(xv[u].w, xv[u].w));
+          }
+        }
+      }
     }
-    __syncthreads();
+  }
+  __syncthreads();
+  float inv = 1.0f;
+  if (norm) {
     const float ss = exact::seq_sum_nonneg<kNT>(xsq, K, -0.0f, *ssm);
     inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
   }
-  for (int b = warp; b < L.nb; b += kNW) {
-    const int i = b * 32 + lane;
-    float v = a.x[i];
-    if (a.in_mode == GEMV_IN_NORM) v = __fmul_rn(__fmul_rn(v, inv), a.norm_w[i]);
-    if (!isfinite(v)) v = 0.0f;
-    const float amax = warp_max(fabsf(v));
+  for (int i = tid; i < jobs_r; i += kNT) {
+    const bool valid = i < jobs;
+    float v[8];
+    if (valid) {
+      const float4 x0 = ((const float4 *)xin)[2 * i], x1 = ((const float4 *)xin)[2 * i + 1];
+      v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w; v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+      if (norm) {
+        const float4 w0 = ((const float4 *)nw)[2 * i], w1 = ((const float4 *)nw)[2 * i + 1];
+        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = __fmul_rn(__fmul_rn(v[e], inv), w[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; e++)
+        if (!isfinite(v[e])) v[e] = 0.0f;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = 0.0f;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(v[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     const float scale = act_scale_from_amax(amax), is = act_inv_from_scale(scale);
-    const int q = act_quant_one(v, is);
-    aq[i] = (int8_t)q;
-    int s = q;
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    s += __shfl_xor_sync(0xffffffffu, s, 8);
-    const int s16 = __shfl_sync(0xffffffffu, s, 16);
-    if (lane == 0) am[b] = make_float4(scale, __int_as_float(s), __int_as_float(s16), 0.f);
+    int q[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) q[e] = act_quant_one(v[e], is);
+    store(i, valid, q, scale);
   }
   __syncthreads();
 }
 
+// Quants and scales of one lane for one (row, segment) unit.
+template <int QUANT>
+struct XUnit {
+  uint4 q[XCfg<QUANT>::NQ4];
+  uint2 d;
+};
+
+template <int QUANT>
+__device__ __forceinline__ void x_load(const DevMat &w, int64_t row, int seg, int nb, int lane, XUnit<QUANT> &u) {
+  constexpr int NQ4 = XCfg<QUANT>::NQ4, BQ4 = NQ4 / 4;  // 16-byte pieces per block
+  const int b0 = seg * kSeg + 4 * lane;
+  const uint8_t *qp = w.qs + row * w.qs_stride + (int64_t)b0 * BQ4 * 16;
+#pragma unroll
+  for (int j = 0; j < NQ4; j++)
+    u.q[j] = (b0 + j / BQ4 < nb) ? ldg_stream16(qp + 16 * j) : make_uint4(0u, 0u, 0u, 0u);
+  u.d = b0 < nb ? ldg_stream8(w.d + row * w.d_stride + b0) : make_uint2(0u, 0u);
+}
+
+// The lane's eight chunk terms of a unit, in chunk order.
+template <int QUANT>
+__device__ __forceinline__ void x_terms(const XUnit<QUANT> &u, const int4 *alo, const int4 *ahi, const float4 *am,
+                                        int seg, int lane, float (&t)[8]) {
+  constexpr int BQ4 = XCfg<QUANT>::NQ4 / 4;
+  const __half2 d01 = *reinterpret_cast<const __half2 *>(&u.d.x);
+  const __half2 d23 = *reinterpret_cast<const __half2 *>(&u.d.y);
+  const float ws[4] = {__low2float(d01), __high2float(d01), __low2float(d23), __high2float(d23)};
+#pragma unroll
+  for (int v = 0; v < 4; v++) {
+    const int sl = seg * kSeg + v * 32 + lane;
+    const int4 xl = alo[sl], xh = ahi[sl];
+    const float4 m = am[sl];
+    int d0, d1;
+    if (QUANT == JAL_Q4_0) {
+      const uint4 q = u.q[v];
+      d0 = dp4a_us(q.x & 0x0F0F0F0Fu, xl.x, 0);
+      d0 = dp4a_us(q.y & 0x0F0F0F0Fu, xl.y, d0);
+      d0 = dp4a_us(q.z & 0x0F0F0F0Fu, xl.z, d0);
+      d0 = dp4a_us(q.w & 0x0F0F0F0Fu, xl.w, d0);
+      d1 = dp4a_us(q.x & 0xF0F0F0F0u, xh.x, 0);
+      d1 = dp4a_us(q.y & 0xF0F0F0F0u, xh.y, d1);
+      d1 = dp4a_us(q.z & 0xF0F0F0F0u, xh.z, d1);
+      d1 = dp4a_us(q.w & 0xF0F0F0F0u, xh.w, d1);
+      d0 -= 8 * __float_as_int(m.y);             // nibble n encodes n - 8
+      d1 = (d1 >> 4) - 8 * __float_as_int(m.z);  // high nibbles were multiplied by 16 in place
+    } else {
+      const uint4 q0 = u.q[BQ4 * v], q1 = u.q[BQ4 * v + 1];
+      d0 = dp4a_ss((int)q0.x, xl.x, 0);
+      d0 = dp4a_ss((int)q0.y, xl.y, d0);
+      d0 = dp4a_ss((int)q0.z, xl.z, d0);
+      d0 = dp4a_ss((int)q0.w, xl.w, d0);
+      d1 = dp4a_ss((int)q1.x, xh.x, 0);
+      d1 = dp4a_ss((int)q1.y, xh.y, d1);
+      d1 = dp4a_ss((int)q1.z, xh.z, d1);
+      d1 = dp4a_ss((int)q1.w, xh.w, d1);
+    }
+    t[2 * v] = __fmul_rn(__fmul_rn(__int2float_rn(d0), m.x), ws[v]);
+    t[2 * v + 1] = __fmul_rn(__fmul_rn(__int2float_rn(d1), m.x), ws[v]);
+  }
+}
+
 template <int QUANT, int OUT>
 __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
-  using C = XCfg<QUANT>;
-  constexpr int UNITS = OUT == GEMV_OUT_SWIGLU ? 2 : 1;
-  constexpr int RBL = kUnits / UNITS;  // logical rows per batch
+  constexpr int DEPTH = XCfg<QUANT>::DEPTH;
+  constexpr int PAIR = OUT == GEMV_OUT_SWIGLU ? 2 : 1;  // physical rows per logical row
+  constexpr int LPB = kBR / PAIR;                       // logical rows per batch
   extern __shared__ __align__(16) char smem[];
-  const XLayout L = x_layout<QUANT>(a.w.cols, a.in_mode);
+  const XLayout L = x_layout(a.w.cols, a.in_mode);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t base = a.rows / gridDim.x, rem = a.rows % gridDim.x;
   const int64_t r0 = (int64_t)blockIdx.x * base + ((int64_t)blockIdx.x < rem ? blockIdx.x : rem);
   const int cnt = (int)(base + ((int64_t)blockIdx.x < rem ? 1 : 0));
-  const int nbatch = (cnt + RBL - 1) / RBL;
-  char *stage = smem + L.stage + (size_t)warp * C::DEPTH * C::SLOT;
-  float *terms = (float *)(smem + L.terms);
+  // This warp's logical rows: r0 + warp + 16 i, i < nl.
+  const int nl = cnt > warp ? (cnt - 1 - warp) / kNW + 1 : 0;
+  const int nbatch = (nl + LPB - 1) / LPB;
+  const int nseg = L.nseg;
+  float *buf = (float *)(smem + L.buf) + (size_t)warp * kBR * kBP;
+  // Unit k of the warp: batch k / (kBR * nseg); within it segment-major over
+  // the batch's physical rows (gate, up, gate, up, ... for SwiGLU).
+  auto batch_rows = [&](int b) { return (nl - b * LPB < LPB ? nl - b * LPB : LPB) * PAIR; };
+  auto unit = [&](int k, int &b, int &sg, int &p) {
+    b = k / (kBR * nseg);
+    const int r = k - b * kBR * nseg, np = batch_rows(b);
+    sg = r / np;
+    p = r - sg * np;
+  };
+  const int total = nbatch ? (nbatch - 1) * kBR * nseg + batch_rows(nbatch - 1) * nseg : 0;
+  auto prow = [&](int b, int p) -> int64_t {
+    const int64_t lr = r0 + warp + (int64_t)(b * LPB + p / PAIR) * kNW;
+    return (PAIR == 2 && (p & 1)) ? a.up_offset + lr : lr;
+  };
 
-  auto batch_units = [&](int b) { return min(RBL, cnt - b * RBL) * UNITS; };
-  auto warp_cnt = [&](int b) {
-    const int nun = batch_units(b);
-    return nun > warp ? (nun - 1 - warp) / kNW + 1 : 0;
-  };
-  // Physical row of unit u in batch b (SWIGLU: gate rows, then up rows).
-  auto unit_row = [&](int b, int u) -> int64_t {
-    const int nl = min(RBL, cnt - b * RBL);
-    const int64_t lr = r0 + (int64_t)b * RBL;
-    if (UNITS == 2) return u < nl ? lr + u : a.up_offset + lr + (u - nl);
-    return lr + u;
-  };
-  auto advance = [&](UnitCursor &c) {
-    if (++c.k < c.cnt) return;
-    c.k = 0;
-    if (++c.s < L.nslab) return;
-    c.s = 0;
-    for (c.b++; c.b < nbatch; c.b++)
-      if ((c.cnt = warp_cnt(c.b)) > 0) return;
-  };
-  auto first = [&](UnitCursor &c) {
-    c = UnitCursor();
-    for (c.b = 0; c.b < nbatch; c.b++)
-      if ((c.cnt = warp_cnt(c.b)) > 0) return;
-  };
-  // Issue the copies of unit c into its slot; always commits one group.
-  auto issue = [&](const UnitCursor &c, int slot) {
-    if (c.b < nbatch) {
-      const int64_t pr = unit_row(c.b, warp + c.k * kNW);
-      const int blk = c.s * 32 + lane;
-      char *dst = stage + slot * C::SLOT;
-      if (blk < L.nb) {
-        const uint8_t *src = a.w.qs + pr * a.w.qs_stride + (int64_t)blk * C::BQ;
-        cp_async16(dst + lane * C::BQ, src);
-        if (C::BQ == 32) cp_async16(dst + lane * C::BQ + 16, src + 16);
-      }
-      const int pb = blk & ~1;
-      if (pb < L.nb) cp_async4(dst + 32 * C::BQ + pb * 2 - c.s * 64, (const char *)(a.w.d + pr * a.w.d_stride + pb));
+  XUnit<QUANT> ring[DEPTH];
+#pragma unroll
+  for (int j = 0; j < DEPTH; j++)
+    if (j < total) {
+      int b, sg, p;
+      unit(j, b, sg, p);
+      x_load<QUANT>(a.w, prow(b, p), sg, L.nb, lane, ring[j]);
     }
-    cp_commit();
-  };
-
-  UnitCursor ld, cp;
-  first(ld);
-  first(cp);
-  int q_ld = 0;
-#pragma unroll 1
-  for (int d = 0; d < C::DEPTH; d++) {
-    issue(ld, q_ld % C::DEPTH);
-    if (ld.b < nbatch) advance(ld);
-    q_ld++;
-  }
   pdl_wait();
   pdl_trigger();
   x_prologue(a, L, smem, (exact::SumSmem<kNT> *)(smem + L.sum));
-
-  const int8_t *aq = (const int8_t *)(smem + L.act_q);
+  const int4 *alo = (const int4 *)(smem + L.act_lo), *ahi = (const int4 *)(smem + L.act_hi);
   const float4 *am = (const float4 *)(smem + L.act_m);
-  int q_cp = 0, gslab = 0;
-  float acc0 = 0.0f, acc1 = 0.0f;  // owner accumulators (gate/up for SWIGLU)
-  for (int b = 0; b < nbatch; b++) {
-    const int nl = min(RBL, cnt - b * RBL);
-    const int mycnt = warp_cnt(b);
-    for (int s = 0; s < L.nslab; s++) {
-      float *tb = terms + (size_t)(gslab & 1) * kUnits * kTP;
-      const int blk = s * 32 + lane;
-      const bool live = blk < L.nb;
-      // this lane's activation block for the slab
-      int4 xlo = make_int4(0, 0, 0, 0), xhi = xlo;
-      float asc = 0.f;
-      int s0 = 0, s1 = 0;
-      if (live) {
-        xlo = *(const int4 *)(aq + blk * 32);
-        xhi = *(const int4 *)(aq + blk * 32 + 16);
-        const float4 m = am[blk];
-        asc = m.x;
-        s0 = __float_as_int(m.y);
-        s1 = __float_as_int(m.z);
-      }
-      for (int k = 0; k < mycnt; k++) {
-        cp_wait<C::DEPTH - 1>();
-        const char *src = stage + (q_cp % C::DEPTH) * C::SLOT;
-        if (live) {
-          int d0, d1;
-          if (QUANT == JAL_Q4_0) {
-            const uint4 w = *(const uint4 *)(src + lane * 16);
-            d0 = dp4a_us(w.x & 0x0F0F0F0Fu, xlo.x, 0);
-            d0 = dp4a_us(w.y & 0x0F0F0F0Fu, xlo.y, d0);
-            d0 = dp4a_us(w.z & 0x0F0F0F0Fu, xlo.z, d0);
-            d0 = dp4a_us(w.w & 0x0F0F0F0Fu, xlo.w, d0);
-            d1 = dp4a_us(w.x & 0xF0F0F0F0u, xhi.x, 0);
-            d1 = dp4a_us(w.y & 0xF0F0F0F0u, xhi.y, d1);
-            d1 = dp4a_us(w.z & 0xF0F0F0F0u, xhi.z, d1);
-            d1 = dp4a_us(w.w & 0xF0F0F0F0u, xhi.w, d1);
-            d0 -= 8 * s0;              // nibble n encodes n - 8
-            d1 = (d1 >> 4) - 8 * s1;   // high nibbles were multiplied by 16 in place
-          } else {
-            const uint4 w0 = *(const uint4 *)(src + lane * 32), w1 = *(const uint4 *)(src + lane * 32 + 16);
-            d0 = dp4a_ss((int)w0.x, xlo.x, 0);
-            d0 = dp4a_ss((int)w0.y, xlo.y, d0);
-            d0 = dp4a_ss((int)w0.z, xlo.z, d0);
-            d0 = dp4a_ss((int)w0.w, xlo.w, d0);
-            d1 = dp4a_ss((int)w1.x, xhi.x, 0);
-            d1 = dp4a_ss((int)w1.y, xhi.y, d1);
-            d1 = dp4a_ss((int)w1.z, xhi.z, d1);
-            d1 = dp4a_ss((int)w1.w, xhi.w, d1);
-          }
-          const float ws = __half2float(__ushort_as_half(*(const uint16_t *)(src + 32 * C::BQ + lane * 2)));
-          const float t0 = __fmul_rn(__fmul_rn(__int2float_rn(d0), asc), ws);
-          const float t1 = __fmul_rn(__fmul_rn(__int2float_rn(d1), asc), ws);
-          *(float2 *)(tb + (warp + k * kNW) * kTP + 2 * lane) = make_float2(t0, t1);
+
+  float acc = 0.0f;  // lane p < kBR: physical row p of the current batch
+  for (int k0 = 0; k0 < total; k0 += DEPTH) {
+#pragma unroll
+    for (int j = 0; j < DEPTH; j++) {
+      const int k = k0 + j;
+      if (k < total) {
+        int b, sg, p;
+        unit(k, b, sg, p);
+        float t[8];
+        x_terms<QUANT>(ring[j], alo, ahi, am, sg, lane, t);
+        if (k + DEPTH < total) {
+          int b2, sg2, p2;
+          unit(k + DEPTH, b2, sg2, p2);
+          x_load<QUANT>(a.w, prow(b2, p2), sg2, L.nb, lane, ring[j]);
         }
-        q_cp++;
-        issue(ld, q_ld % C::DEPTH);
-        if (ld.b < nbatch) advance(ld);
-        q_ld++;
-      }
-      __syncthreads();  // slab terms complete; the other buffer's fold is done
-      if (tid < nl) {
-        const int nt = 2 * min(32, L.nb - s * 32);
-        const float *r0p = tb + tid * kTP;
-        const float *r1p = tb + (nl + tid) * kTP;
-        int i = 0;
-        for (; i + 4 <= nt; i += 4) {
-          const float4 v = *(const float4 *)(r0p + i);
-          acc0 = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc0, v.x), v.y), v.z), v.w);
-          if (UNITS == 2) {
-            const float4 u = *(const float4 *)(r1p + i);
-            acc1 = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc1, u.x), u.y), u.z), u.w);
+        float *dst = buf + p * kBP + 8 * lane;
+        *(float4 *)dst = make_float4(t[0], t[1], t[2], t[3]);
+        *(float4 *)(dst + 4) = make_float4(t[4], t[5], t[6], t[7]);
+        const int np = batch_rows(b);
+        if (p == np - 1) {  // the batch's segment is complete: fold it
+          __syncwarp();
+          const int blk = L.nb - sg * kSeg < kSeg ? L.nb - sg * kSeg : kSeg;
+          const int nt = 2 * blk;
+          if (lane < np) {
+            const float *src = buf + lane * kBP;
+            int i = 0;
+            for (; i + 4 <= nt; i += 4) {
+              const float4 v = *(const float4 *)(src + i);
+              acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
+            }
+            for (; i < nt; i++) acc = __fadd_rn(acc, src[i]);
+          }
+          __syncwarp();
+          if (sg == nseg - 1) {  // rows of the batch are done
+            const float other = __shfl_down_sync(0xffffffffu, acc, 1);
+            if (lane < np && (PAIR == 1 || (lane & 1) == 0)) {
+              const int64_t lr = r0 + warp + (int64_t)(b * LPB + lane / PAIR) * kNW;
+              float *yp = a.y + lr;
+              if (OUT == GEMV_OUT_STORE) {
+                *yp = a.bias ? __fadd_rn(acc, a.bias[lr]) : acc;
+              } else if (OUT == GEMV_OUT_ADD) {
+                const float pv = a.bias ? __fadd_rn(acc, a.bias[lr]) : acc;
+                *yp = __fadd_rn(*yp, pv);
+              } else {
+                *yp = exact::swiglu_ref(acc, other);
+              }
+            }
+            acc = 0.0f;
           }
         }
-        for (; i < nt; i++) {
-          acc0 = __fadd_rn(acc0, r0p[i]);
-          if (UNITS == 2) acc1 = __fadd_rn(acc1, r1p[i]);
-        }
       }
-      gslab++;
-    }
-    if (tid < nl) {  // epilogue of the batch's rows
-      const int64_t lr = r0 + (int64_t)b * RBL + tid;
-      float *yp = a.y + lr;
-      if (OUT == GEMV_OUT_STORE) {
-        *yp = a.bias ? __fadd_rn(acc0, a.bias[lr]) : acc0;
-      } else if (OUT == GEMV_OUT_ADD) {
-        const float p = a.bias ? __fadd_rn(acc0, a.bias[lr]) : acc0;
-        *yp = __fadd_rn(*yp, p);
-      } else {
-        *yp = exact::swiglu_ref(acc0, acc1);
-      }
-      acc0 = acc1 = 0.0f;
     }
   }
-  cp_wait<0>();
 }
 
 template <int QUANT, int OUT>
 void launch_x(const GemvArgs &a, int grid, cudaStream_t s) {
-  const XLayout L = x_layout<QUANT>(a.w.cols, a.in_mode);
+  const XLayout L = x_layout(a.w.cols, a.in_mode);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kNT);
@@ -340,12 +397,14 @@ void set_x_attrs() {
 }  // namespace
 
 size_t xgemv_smem_bytes(int quant, int64_t cols, int in_mode) {
-  return quant == JAL_Q4_0 ? x_layout<JAL_Q4_0>(cols, in_mode).total : x_layout<JAL_Q8_0>(cols, in_mode).total;
+  (void)quant;
+  return x_layout(cols, in_mode).total;
 }
 
 bool xgemv_supported(const GemvArgs &a) {
   if (a.m != 1 || (a.w.quant != JAL_Q4_0 && a.w.quant != JAL_Q8_0)) return false;
   if (a.w.cols % 32 != 0 || a.w.qs_stride % 16 != 0 || (reinterpret_cast<uintptr_t>(a.w.qs) & 15) != 0) return false;
+  if (a.w.d_stride % 4 != 0) return false;  // 8-byte scale loads
   if (a.out_mode != GEMV_OUT_STORE && a.out_mode != GEMV_OUT_ADD && a.out_mode != GEMV_OUT_SWIGLU) return false;
   if (a.peer_in || a.in_mode == GEMV_IN_PREQ) return false;
   return xgemv_smem_bytes(a.w.quant, a.w.cols, a.in_mode) <= 227 * 1024;

@@ -362,3 +362,76 @@ def test_llama3_8b_shaped_two_layers_long_context(jal, oracle, torch_cuda):
     prompt = prompt_of(12, n=640, vocab=spec.vocab_size)
     tokens, _, worst = run_parity(om, ctx, prompt, 16, 1024)
     print(f"8B-shaped 2-layer fast numerics worst |dlogit| = {worst:.3e}, tokens {tokens[:8]}")
+
+
+def test_caller_owned_kv_cache_shared_by_two_contexts(jal, oracle, torch_cuda):
+    """A KV cache allocated by the caller (the reference's KvCacheView) and
+    two contexts over it: A prefills, is freed, and B resumes decoding at
+    A's position; its logits and greedy tokens equal a context that owns its
+    cache and the oracle's.  Mismatched configurations fail closed."""
+    spec = jal.TINY_LLAMA
+    _, om, recipe, cache, ref_ctx = make(jal, oracle, spec, seed=404, kv_dtype=jal.KV_F16, n_ctx=128,
+                                         numerics=jal.NUMERICS_FAST)
+    kv = jal.KvCache(cache, 128, jal.KV_F16)
+    assert kv.nbytes() >= 2 * spec.num_layers * 128 * spec.n_heads_kv * spec.head_dim * 2
+    prompt = prompt_of(31)
+    a = jal.ExecutionContext(recipe, cache, n_ctx=128, kv_dtype=jal.KV_F16, kv=kv)
+    la = a.prefill_step(prompt, 0)
+    lr = ref_ctx.prefill_step(prompt, 0)
+    assert np.array_equal(la, lr)
+    del a
+    b = jal.ExecutionContext(recipe, cache, n_ctx=128, kv_dtype=jal.KV_F16, kv=kv)
+    b.set_position(len(prompt))
+    tok = int(np.argmax(la))
+    for _ in range(12):
+        lb, lr = b.decode_step(tok), ref_ctx.decode_step(tok)
+        assert np.array_equal(lb, lr)
+        tok = int(np.argmax(lr))
+    assert b.position() == len(prompt) + 12
+    with pytest.raises(jal.CapabilityMismatch):
+        jal.ExecutionContext(recipe, cache, n_ctx=128, kv_dtype=jal.KV_F32, kv=kv)
+    with pytest.raises(jal.ContextLengthExceeded):
+        jal.ExecutionContext(recipe, cache, n_ctx=256, kv_dtype=jal.KV_F16, kv=kv)
+    with pytest.raises(jal.ContextLengthExceeded):
+        b.set_position(129)
+
+
+def test_bounded_kv_copy_wait_reports_timeout_and_context_recovers(jal, torch_cuda):
+    """Failure detection without a fault: the decode attention's first V-copy
+    barrier is armed for more bytes than the copy sends (jal_test.h), so its
+    bounded wait (5 ms here) gives up; the step returns JAL_ERR_TIMEOUT, the
+    position is unchanged, and once the hook is cleared the same step gives
+    the logits of an untouched context."""
+    import ctypes as C
+    spec = jal.TINY_LLAMA
+    buf = jal.synth_gguf(spec, 8)
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    cache = recipe.build_repack_cache(buf)
+    a = new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
+    b = new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
+    p = prompt_of(2)
+    a.prefill_step(p, 0)
+    b.prefill_step(p, 0)
+    lib = jal.lib()
+    assert lib.jal_context_test_stall_kv_copy(a.handle, 64, 5_000_000) == 0
+    with pytest.raises(jal.DeviceTimeout) as ei:
+        a.decode_step(7)
+    assert "gave up" in str(ei.value)
+    assert a.position() == len(p)
+    assert lib.jal_context_test_stall_kv_copy(a.handle, 0, 0) == 0
+    assert np.array_equal(a.decode_step(7), b.decode_step(7))
+    assert a.position() == len(p) + 1
+
+
+def test_bounded_peer_exchange_wait_reports_timeout(jal, torch_cuda):
+    """The tensor-parallel exchange wait, on one GPU: an RMSNorm GEMV whose
+    input slot carries flags that never match gives up after the bound
+    (10 ms here) and reports JAL_ERR_TIMEOUT; no rank, collective or peer
+    mapping is involved."""
+    import ctypes as C
+    raw = jal.synth_matrix(jal.Q4_0, 512, 4096, seed=3, name="peerwait")
+    mat = jal.CachedMatrix.repack(raw, jal.Q4_0, 512, 4096)
+    ms = C.c_double()
+    rc = jal.lib().jal_test_peer_exchange_timeout(mat._h, 10_000_000, C.byref(ms))
+    assert rc == jal.ERR_TIMEOUT, jal.lib().jal_last_error().decode()
+    assert 10.0 <= ms.value < 2000.0, ms.value

@@ -13,7 +13,7 @@ from conftest import REPO
 
 def header_functions():
     names = []
-    for h in ("jal.h", "jal_synth.h"):
+    for h in ("jal.h", "jal_synth.h", "jal_test.h"):
         src = open(os.path.join(REPO, "include", h)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
         names += re.findall(r"\b(jal_[a-z0-9_]+)\s*\(", src)
