@@ -16,18 +16,21 @@
 // to nearest, a tie going to the k that makes the result's mantissa even.  A
 // run of steps inside one binade is therefore an integer increment that
 // depends only on the parity of the starting mantissa: a pair (inc0, inc1).
-// Pairs compose associatively, so a block of threads
-//   1. sums its segments in double and scans them (an estimate P_i of s_i,
-//      within i * 2^-24 relative, which places each segment in a binade),
+// Pairs compose associatively, so a group of threads
+//   1. sums its segments (an odd number of consecutive terms per thread, so
+//      that strided shared-memory reads do not conflict, held in registers)
+//      and scans them: an estimate P_i of s_i within (i + c + 1) * 2^-24
+//      relative, which places each segment in a binade;
 //   2. builds each segment's pair (or marks it sequential when it may cross a
-//      binade, holds non-finite terms or starts below the normal range),
-//   3. composes equal-binade neighbours with a segmented warp scan, and
-//   4. one thread applies the short list of composed runs and sequential
-//      segments to the start value.
-// Step 4 checks each run: the start must lie in the run's binade and the
-// mantissa plus the increment must stay below 2^24.  Because s only grows,
-// that check is exact; a run that fails it is recomputed with plain adds.
-// The estimate in step 1 therefore affects speed only, never the result.
+//      binade, holds non-finite terms or starts below the normal range);
+//   3. composes equal-binade neighbours (and neighbouring sequential
+//      segments) with a segmented warp scan and concatenates the warps'
+//      short lists; and
+//   4. one thread applies the list in order to the start value.
+// Step 4 checks each run: the start must lie in the run's binade and so must
+// the end (start plus increment).  Because s only grows, that check is exact;
+// if one fails the whole sum is recomputed with plain adds, so the estimate
+// in step 1 affects speed only, never the result.
 #pragma once
 
 #include <cstdint>
@@ -37,21 +40,18 @@
 namespace jal {
 namespace exact {
 
-constexpr int kSeq = -10000;  // op binade marker: add the segment's terms one by one
-
-// One entry of the run list: terms [a, b); binade e (or kSeq) in the low
-// 16 bits of `ed`, inc1 - inc0 in the high 16 bits; inc0.
+// One entry of a warp's run list.  A composed run: {inc0, inc1, exponent
+// field of its binade (1..254)}; sequential segments: {first, end, 0}.
 struct __align__(16) SumOp {
-  int a, b;
-  int ed;
-  uint32_t inc0;
+  uint32_t x, y, E, pad;
 };
 
 template <int NT>
 struct SumSmem {
   double wtot[NT / 32];
-  int wcount[NT / 32], woff[NT / 32];
-  SumOp ops[NT];
+  int wcount[NT / 32];
+  int total;
+  SumOp ops[NT];  // the warps' lists, concatenated
   float result;
 };
 
@@ -61,6 +61,16 @@ template <int NT>
 __device__ __forceinline__ void group_sync(int bar) {
   if (bar == 0) __syncthreads();
   else asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(NT) : "memory");
+}
+
+constexpr int kSumChunk = 16;  // terms a thread holds in registers at once
+
+// Terms [base, base + 16) clamped to [base, end) (end > base): every load is
+// in bounds and all are in flight together; v[j] for base + j >= end repeats
+// the last term and is masked by the callers.
+__device__ __forceinline__ void load_chunk(const float *t, int base, int end, float (&v)[kSumChunk]) {
+#pragma unroll
+  for (int j = 0; j < kSumChunk; j++) v[j] = t[min(base + j, end - 1)];
 }
 
 // Reference-order result of s0 + t[0] + t[1] + ... + t[n-1] (f32, round to
@@ -73,22 +83,32 @@ __device__ __forceinline__ void group_sync(int bar) {
 template <int NT, typename SM>
 __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gtid = -1, int bar = 0) {
   static_assert(NT % 32 == 0 && NT <= 1024, "block size");
-  constexpr int NW = NT / 32;
+  constexpr int CH = kSumChunk;
   const int tid = gtid < 0 ? (int)threadIdx.x : gtid, lane = tid & 31, warp = tid >> 5;
   if (n <= 0) return s0;
   int c = (n + NT - 1) / NT;
-  if (c < 4) c = 4;
+  if (c < 3) c = 3;
+  c |= 1;
   const int nseg = (n + c - 1) / c;
   const bool active = tid < nseg;
   const int a = tid * c, b = active ? min(n, a + c) : a;
 
-  // 1. segment sums in double, block-wide exclusive scan
+  // 1. segment sums (pairwise in f32 within a chunk, relative error <= 4u
+  // per chunk, then in double) and their block-wide scan; a non-finite term
+  // makes its own and every later estimate non-finite, which sends those
+  // segments to step 4's adds
+  float v[CH];
   double D = 0.0;
-  bool finite = true;
-  for (int i = a; i < b; i++) {
-    const float v = t[i];
-    finite = finite && isfinite(v);
-    D += (double)v;
+  for (int base = a; base < b; base += CH) {
+    load_chunk(t, base, b, v);
+    float d[CH];
+#pragma unroll
+    for (int j = 0; j < CH; j++) d[j] = base + j < b ? v[j] : 0.0f;
+#pragma unroll
+    for (int w = 1; w < CH; w <<= 1)
+#pragma unroll
+      for (int j = 0; j < CH; j += 2 * w) d[j] = __fadd_rn(d[j], d[j + w]);
+    D += (double)d[0];
   }
   double incl = D;
 #pragma unroll
@@ -98,133 +118,139 @@ __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gti
   }
   if (lane == 31) sm.wtot[warp] = incl;
   group_sync<NT>(bar);
-  if (warp == 0) {
-    double v = lane < NW ? sm.wtot[lane] : 0.0;
+  double before = lane < warp ? sm.wtot[lane] : 0.0;  // lane < warp < NT / 32 <= 32
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double y = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += y;
-    }
-    if (lane < NW) sm.wtot[lane] = v;
-  }
-  group_sync<NT>(bar);
-  const double Pa = (double)s0 + (warp ? sm.wtot[warp - 1] : 0.0) + (incl - D), Pb = Pa + D;
+  for (int o = 16; o >= 1; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
+  const double Pa = (double)s0 + before + (incl - D), Pb = Pa + D;
 
-  // 2. this segment's run increment pair, if it stays in one binade
-  int e = kSeq;
-  uint32_t inc0 = 0, inc1 = 0;
-  if (active && tid > 0 && finite) {
+  // 2. this segment's run increment pair, if it stays in one binade.  A term
+  // t adds k = t / U rounded to nearest, U = 2^(e-23); x = t / U = t *
+  // 2^(23-e) is exact in f32, and for 0 <= x < 2^23 the f32 sum x + 2^23
+  // rounds it to the nearest integer (ties to even) in its low mantissa
+  // bits.  Only an exact half (a tie) depends on the running parity, so the
+  // common tie-free segment is a plain integer sum.
+  uint32_t E = 0, inc0 = 0, inc1 = 0;
+  if (active && tid > 0) {
+    // s_i is within 1.01 * i * u of the exact prefix; the estimate adds
+    // (c + 1) u from the f32 chunk sums (double rounding is far below that)
     const double u = 5.9604644775390625e-8;  // 2^-24
-    const double lo = Pa * (1.0 - (double)(a + 2) * u * 1.01), hi = Pb * (1.0 + (double)(b + 2) * u * 1.01);
-    if (lo >= 1.1754943508222875e-38 && hi < 3.0e38) {
+    const double lo = Pa * (1.0 - (double)(a + c + 3) * u * 1.01), hi = Pb * (1.0 + (double)(b + c + 3) * u * 1.01);
+    if (lo >= 1.0e-30 && hi < 3.0e38) {  // e >= -100: 2^(23-e) is a normal f32
       const int el = (int)((__double_as_longlong(lo) >> 52) & 0x7FF) - 1023;
       const int eh = (int)((__double_as_longlong(hi) >> 52) & 0x7FF) - 1023;
       if (el == eh) {
-        e = el;
-        for (int i = a; i < b; i++) {
-          const uint32_t bits = __float_as_uint(t[i]);
-          int E = (int)(bits >> 23);
-          uint32_t m = bits & 0x7FFFFFu;
-          if (E) m |= 0x800000u;
-          else E = 1;
-          const int sh = 127 + e - E;  // t / U = m / 2^sh
-          if (sh <= 0) { e = kSeq; break; }  // t >= 2^e: the step leaves the binade
-          if (sh >= 25) continue;           // t < U / 2: adds nothing
-          const uint32_t K = m >> sh, rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
-          if (rem == half) {  // tie: to the even result mantissa
-            inc0 += K + ((inc0 + K) & 1u);
-            inc1 += K + ((1u + inc1 + K) & 1u);
-          } else {
-            const uint32_t k = K + (rem > half ? 1u : 0u);
-            inc0 += k;
-            inc1 += k;
+        const float scale = __int_as_float((127 + 23 - el) << 23);  // 2^(23-e)
+        bool out = false, any_tie = false;
+        uint32_t ksum = 0;
+        for (int base = a; base < b; base += CH) {
+          if (base != a || b - a > CH) load_chunk(t, base, b, v);  // one chunk: still in registers
+#pragma unroll
+          for (int j = 0; j < CH; j++) {
+            const bool in = base + j < b;
+            const float x = fminf(__fmul_rn(v[j], scale), 8388608.0f);  // t / U, exact below 2^23
+            const float y = __fadd_rn(x, 8388608.0f);                     // 2^23 + nearest integer
+            out |= in && x >= 8388608.0f;                                 // t >= 2^e: leaves the binade
+            any_tie |= in && fabsf(__fsub_rn(x, __fsub_rn(y, 8388608.0f))) == 0.5f;
+            ksum += in ? __float_as_uint(y) - 0x4B000000u : 0u;
           }
-          inc0 = min(inc0, 1u << 25);
-          inc1 = min(inc1, 1u << 25);
+          ksum = min(ksum, 1u << 25);  // a run never adds more than 2^24; no wrap-around
         }
+        inc0 = inc1 = ksum;
+        if (any_tie && !out) {  // ties go to the even result mantissa: follow both parities
+          inc0 = inc1 = 0;
+          for (int i = a; i < b; i++) {
+            const float x = __fmul_rn(t[i], scale);
+            const float fl = floorf(x);
+            const uint32_t K = (uint32_t)fl;
+            if (__fsub_rn(x, fl) == 0.5f) {
+              inc0 += K + ((inc0 + K) & 1u);
+              inc1 += K + ((1u + inc1 + K) & 1u);
+            } else {
+              const uint32_t k = __float_as_uint(__fadd_rn(x, 8388608.0f)) - 0x4B000000u;
+              inc0 += k;
+              inc1 += k;
+            }
+            inc0 = min(inc0, 1u << 25);
+            inc1 = min(inc1, 1u << 25);
+          }
+        }
+        if (!out) E = (uint32_t)(el + 127);
       }
     }
   }
 
-  // 3. compose runs of equal binade within the warp (segmented inclusive scan)
-  const bool mono = active && e != kSeq;
-  const int e_prev = __shfl_up_sync(0xffffffffu, e, 1);
-  const bool mono_prev = __shfl_up_sync(0xffffffffu, mono, 1);
-  const bool head = !(mono && lane > 0 && mono_prev && e_prev == e);
+  // 3. compose equal neighbours within the warp: runs of one binade, and
+  // runs of sequential segments.  A segmented inclusive scan whose heads
+  // come from one ballot; then the warps' lists are concatenated in order.
+  const uint32_t E_prev = __shfl_up_sync(0xffffffffu, E, 1);
+  const bool head = lane == 0 || E_prev != E || !active;
+  const unsigned heads = __ballot_sync(0xffffffffu, head);
+  const int hl = 31 - __clz(heads & (0xffffffffu >> (31 - lane)));  // this lane's run head
   uint32_t c0 = inc0, c1 = inc1;
-  int start = a;
-  bool f = head;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t p0 = __shfl_up_sync(0xffffffffu, c0, o), p1 = __shfl_up_sync(0xffffffffu, c1, o);
-    const int ps = __shfl_up_sync(0xffffffffu, start, o);
-    const bool pf = __shfl_up_sync(0xffffffffu, f, o);
-    if (lane >= o && !f) {  // previous steps first, then these
-      const uint32_t n0 = p0 + ((p0 & 1u) ? c1 : c0);
-      const uint32_t n1 = p1 + (((1u + p1) & 1u) ? c1 : c0);
+    if (lane - o >= hl) {  // previous steps first, then these
+      const uint32_t n0 = p0 + ((p0 & 1u) ? c1 : c0), n1 = p1 + (((1u + p1) & 1u) ? c1 : c0);
       c0 = min(n0, 1u << 25);
       c1 = min(n1, 1u << 25);
-      start = ps;
-      f = pf;
     }
   }
-  const bool next_head = __shfl_down_sync(0xffffffffu, head, 1);
-  const bool tail = active && (lane == 31 || next_head || tid + 1 >= nseg);
+  const bool tail = active && (lane == 31 || ((heads >> (lane + 1)) & 1u));
   const unsigned tails = __ballot_sync(0xffffffffu, tail);
   if (lane == 0) sm.wcount[warp] = __popc(tails);
   group_sync<NT>(bar);
-  if (tid == 0) {  // run-list offsets of the warps
-    int o = 0;
-    for (int w = 0; w < NW; w++) {
-      sm.woff[w] = o;
-      o += sm.wcount[w];
-    }
-    sm.wcount[0] = o;  // total
-  }
-  group_sync<NT>(bar);
+  int off = lane < warp ? sm.wcount[lane] : 0;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) off += __shfl_xor_sync(0xffffffffu, off, o);
   if (tail) {
     SumOp op;
-    int ee = mono ? e : kSeq, delta = (int)c1 - (int)c0;
-    if (delta < -32767 || delta > 32767) ee = kSeq;  // cannot happen for sane inputs; stay exact
-    op.a = mono ? start : a;
-    op.b = b;
-    op.ed = (int)(((uint32_t)ee & 0xffffu) | ((uint32_t)delta << 16));
-    op.inc0 = c0;
-    sm.ops[sm.woff[warp] + __popc(tails & ((1u << lane) - 1u))] = op;
+    op.x = E ? c0 : (uint32_t)((warp * 32 + hl) * c);
+    op.y = E ? c1 : (uint32_t)b;
+    op.E = E;
+    op.pad = 0u;
+    sm.ops[off + __popc(tails & ((1u << lane) - 1u))] = op;
   }
+  if (tid == NT - 1) sm.total = off + __popc(tails);  // the last warp's offset + count
   group_sync<NT>(bar);
 
-  // 4. apply the runs in order (each entry prefetched one step ahead)
+  // 4. apply the list in order (entries loaded two ahead).  A run's checks
+  // (start and end in its binade) are collected and tested once at the end;
+  // if one failed -- the estimate cannot place a run wrongly, so this is a
+  // safety net only -- the sum is recomputed with plain adds.
   if (tid == 0) {
-    const int total = sm.wcount[0];
+    const int T = sm.total;
     float s = s0;
-    SumOp cur = sm.ops[0];
-    for (int k = 0; k < total; k++) {
-      const SumOp nxt = k + 1 < total ? sm.ops[k + 1] : cur;
-      const int e = (int)(short)(cur.ed & 0xffff);
-      bool done = false;
-      if (e != kSeq) {
+    bool ok = true;
+    SumOp cur = sm.ops[0], nxt = sm.ops[T > 1 ? 1 : 0];
+    for (int k = 0; k < T; k++) {
+      const SumOp nx2 = sm.ops[k + 2 < T ? k + 2 : T - 1];
+      if (cur.E) {
         const uint32_t bits = __float_as_uint(s);
-        if ((int)(bits >> 23) == e + 127) {  // positive, in the run's binade
-          const uint32_t N = (bits & 0x7FFFFFu) | 0x800000u;
-          const uint32_t inc = (N & 1u) ? (uint32_t)((int)cur.inc0 + (cur.ed >> 16)) : cur.inc0;
-          if (N + inc < 0x1000000u) {
-            s = __uint_as_float(bits + inc);
-            done = true;
-          }
-        }
-      }
-      if (!done) {
-        for (int i0 = cur.a; i0 < cur.b; i0 += 16) {  // 16 loads in flight, then the adds in order
-          float v[16];
+        const uint32_t nb = bits + ((bits & 1u) ? cur.y : cur.x);  // mantissa parity = parity of the bits
+        ok = ok & ((bits >> 23) == cur.E) & ((nb >> 23) == cur.E);  // positive; start and end in the binade
+        s = __uint_as_float(nb);
+      } else {
+        for (int i0 = (int)cur.x; i0 < (int)cur.y; i0 += CH) {  // all loads in flight, then the adds in order
+          float x[CH];
+          load_chunk(t, i0, (int)cur.y, x);
 #pragma unroll
-          for (int u = 0; u < 16; u++) v[u] = i0 + u < cur.b ? t[i0 + u] : 0.0f;
-#pragma unroll
-          for (int u = 0; u < 16; u++)
-            if (i0 + u < cur.b) s = __fadd_rn(s, v[u]);
+          for (int j = 0; j < CH; j++)
+            if (i0 + j < (int)cur.y) s = __fadd_rn(s, x[j]);
         }
       }
       cur = nxt;
+      nxt = nx2;
+    }
+    if (!ok) {
+      s = s0;
+      for (int i0 = 0; i0 < n; i0 += CH) {
+        float x[CH];
+        load_chunk(t, i0, n, x);
+#pragma unroll
+        for (int j = 0; j < CH; j++)
+          if (i0 + j < n) s = __fadd_rn(s, x[j]);
+      }
     }
     sm.result = s;
   }

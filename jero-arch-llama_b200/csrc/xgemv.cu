@@ -14,12 +14,13 @@
 // segments of 128 blocks (4096 columns): lane l owns blocks 4l .. 4l + 3 of
 // the segment, loads their quants (64 bytes for Q4_0, 128 for Q8_0) and four
 // f16 scales with non-allocating vector loads, DEPTH units (row, segment)
-// ahead in registers (the first ones before griddepcontrol.wait), and writes
-// its eight chunk terms, in chunk order, into the warp's buffer row for that
-// physical row.  When the eight rows' segment is in the buffer, lanes 0 .. 7
+// ahead in registers, and writes its eight chunk terms, in chunk order, into
+// the warp's buffer row for that physical row.  When the eight rows' segment is in the buffer, lanes 0 .. 7
 // each add one row's terms in order onto that row's accumulator.  No CTA
 // barrier is involved after the prologue; the serial adds (256 per segment)
-// of one batch run while the next batch's loads are in flight.
+// of one batch run while the next batch's loads are in flight.  Before
+// griddepcontrol.wait each CTA starts a bulk L2 prefetch of its rows, so
+// the weights stream from HBM while the activation prologue runs.
 //
 // The activation prologue (optional RMSNorm, then QuantizedActQ8 per
 // 32-block) is computed by every CTA into shared memory after the wait, in a
@@ -42,6 +43,9 @@ constexpr int kNT = 512, kNW = kNT / 32;
 constexpr int kSeg = 128;   // blocks per segment (4096 columns)
 constexpr int kBR = 8;      // physical rows per warp batch (fold lanes)
 constexpr int kBP = 260;    // buffer row pitch (floats): 256 terms + 4 (conflict-free fold reads)
+// L2 prefetch per CTA at launch: 148 CTAs x 512 KB stays well inside the
+// 126 MB L2 while covering whole projections up to ~75 MB.
+constexpr uint64_t kL2PrefetchBytes = 512 * 1024;
 
 template <int QUANT>
 struct XCfg {
@@ -211,6 +215,11 @@ __device__ void x_prologue(const GemvArgs &a, const XLayout &L, char *smem, SumS
   __syncthreads();
 }
 
+// f32 of an integer |d| < 2^22 without the conversion unit: 1.5 * 2^23 + d
+// is exact in f32 (its bits are those of 1.5 * 2^23 plus d), and so is the
+// difference.  Chunk dots stay below 16 * 128 * 127 < 2^22.
+__device__ __forceinline__ float exact_i2f(int d) { return __fsub_rn(__int_as_float(0x4B400000 + d), 12582912.0f); }
+
 // Quants and scales of one lane for one (row, segment) unit.
 template <int QUANT>
 struct XUnit {
@@ -266,8 +275,8 @@ __device__ __forceinline__ void x_terms(const XUnit<QUANT> &u, const int4 *alo, 
       d1 = dp4a_ss((int)q1.z, xh.z, d1);
       d1 = dp4a_ss((int)q1.w, xh.w, d1);
     }
-    t[2 * v] = __fmul_rn(__fmul_rn(__int2float_rn(d0), m.x), ws[v]);
-    t[2 * v + 1] = __fmul_rn(__fmul_rn(__int2float_rn(d1), m.x), ws[v]);
+    t[2 * v] = __fmul_rn(__fmul_rn(exact_i2f(d0), m.x), ws[v]);
+    t[2 * v + 1] = __fmul_rn(__fmul_rn(exact_i2f(d1), m.x), ws[v]);
   }
 }
 
@@ -287,14 +296,21 @@ __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
   const int nbatch = (nl + LPB - 1) / LPB;
   const int nseg = L.nseg;
   float *buf = (float *)(smem + L.buf) + (size_t)warp * kBR * kBP;
-  // Unit k of the warp: batch k / (kBR * nseg); within it segment-major over
-  // the batch's physical rows (gate, up, gate, up, ... for SwiGLU).
+  // Units of the warp in order: batch by batch; within a batch segment-major
+  // over its physical rows (gate, up, gate, up, ... for SwiGLU).  A cursor
+  // walks them without divisions.
   auto batch_rows = [&](int b) { return (nl - b * LPB < LPB ? nl - b * LPB : LPB) * PAIR; };
-  auto unit = [&](int k, int &b, int &sg, int &p) {
-    b = k / (kBR * nseg);
-    const int r = k - b * kBR * nseg, np = batch_rows(b);
-    sg = r / np;
-    p = r - sg * np;
+  struct Cursor {
+    int b, sg, p, np;
+  };
+  auto advance = [&](Cursor &c) {
+    if (++c.p == c.np) {
+      c.p = 0;
+      if (++c.sg == nseg) {
+        c.sg = 0;
+        c.np = batch_rows(++c.b);
+      }
+    }
   };
   const int total = nbatch ? (nbatch - 1) * kBR * nseg + batch_rows(nbatch - 1) * nseg : 0;
   auto prow = [&](int b, int p) -> int64_t {
@@ -302,17 +318,26 @@ __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
     return (PAIR == 2 && (p & 1)) ? a.up_offset + lr : lr;
   };
 
-  XUnit<QUANT> ring[DEPTH];
-#pragma unroll
-  for (int j = 0; j < DEPTH; j++)
-    if (j < total) {
-      int b, sg, p;
-      unit(j, b, sg, p);
-      x_load<QUANT>(a.w, prow(b, p), sg, L.nb, lane, ring[j]);
-    }
+  // This CTA's rows are one contiguous run of row records (two for SwiGLU):
+  // start streaming them into L2 before waiting on the previous kernel, so
+  // HBM works while the activation prologue runs.
+  if (tid == 0 && cnt > 0) {
+    const uint64_t rec = (uint64_t)a.w.qs_stride, cap = kL2PrefetchBytes / PAIR;
+    const uint64_t bytes = (uint64_t)cnt * rec < cap ? (uint64_t)cnt * rec : cap;
+    l2_prefetch_bulk(a.w.qs + r0 * a.w.qs_stride, bytes);
+    if (PAIR == 2) l2_prefetch_bulk(a.w.qs + (a.up_offset + r0) * a.w.qs_stride, bytes);
+  }
   pdl_wait();
   pdl_trigger();
   x_prologue(a, L, smem, (exact::SumSmem<kNT> *)(smem + L.sum));
+  XUnit<QUANT> ring[DEPTH];
+  Cursor cur = {0, 0, 0, nbatch ? batch_rows(0) : 0}, ahead = cur;
+#pragma unroll
+  for (int j = 0; j < DEPTH; j++)
+    if (j < total) {
+      x_load<QUANT>(a.w, prow(ahead.b, ahead.p), ahead.sg, L.nb, lane, ring[j]);
+      advance(ahead);
+    }
   const int4 *alo = (const int4 *)(smem + L.act_lo), *ahi = (const int4 *)(smem + L.act_hi);
   const float4 *am = (const float4 *)(smem + L.act_m);
 
@@ -322,19 +347,17 @@ __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
     for (int j = 0; j < DEPTH; j++) {
       const int k = k0 + j;
       if (k < total) {
-        int b, sg, p;
-        unit(k, b, sg, p);
+        const int b = cur.b, sg = cur.sg, p = cur.p, np = cur.np;
+        advance(cur);
         float t[8];
         x_terms<QUANT>(ring[j], alo, ahi, am, sg, lane, t);
         if (k + DEPTH < total) {
-          int b2, sg2, p2;
-          unit(k + DEPTH, b2, sg2, p2);
-          x_load<QUANT>(a.w, prow(b2, p2), sg2, L.nb, lane, ring[j]);
+          x_load<QUANT>(a.w, prow(ahead.b, ahead.p), ahead.sg, L.nb, lane, ring[j]);
+          advance(ahead);
         }
         float *dst = buf + p * kBP + 8 * lane;
         *(float4 *)dst = make_float4(t[0], t[1], t[2], t[3]);
         *(float4 *)(dst + 4) = make_float4(t[4], t[5], t[6], t[7]);
-        const int np = batch_rows(b);
         if (p == np - 1) {  // the batch's segment is complete: fold it
           __syncwarp();
           const int blk = L.nb - sg * kSeg < kSeg ? L.nb - sg * kSeg : kSeg;
