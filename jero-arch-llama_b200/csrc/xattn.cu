@@ -18,13 +18,15 @@
 // share of the positions: a thread per position loads its K row (prefetched
 // into L2 before griddepcontrol.wait) into registers, 256 bytes at a time as
 // independent 16-byte loads, and runs the G score chains over the dims in
-// order.  The cluster agrees on each head's max through
-// distributed shared memory and every CTA turns its scores into e_t.
-// Phase B: CTA g < G gathers head g's e_t in position order, forms the exact
-// sequential denominator (exact::seq_sum_nonneg) and runs the HD output
-// chains (thread d) over all positions in order.  Its V stages started
-// streaming into a ring before griddepcontrol.wait; a producer thread
-// refills a slot once every chain has passed it.  That CTA writes the output
+// order.  The cluster agrees on each head's max through distributed shared
+// memory (all ranks' maxima read at once), and every CTA writes its e_t
+// straight into the position-ordered array of the CTA that owns the head.
+// Phase B: CTA g < G forms head g's exact sequential denominator
+// (exact::seq_sum_nonneg) and runs the HD output chains (thread d) over all
+// positions in order, four weights per shared-memory load.  Its V stages
+// started streaming into a ring before griddepcontrol.wait (stage ranges
+// precomputed, one per thread); a producer thread refills a slot once every
+// chain has passed it.  That CTA writes the output
 // row and its QuantizedActQ8 blocks (the O projection's input).  Waits on
 // copies are bounded: a wait that gives up sets bit value 2 of the context's
 // error word and the kernel runs to its end.
@@ -42,7 +44,7 @@ namespace jal {
 
 namespace {
 
-constexpr int kXT = 256, kXW = kXT / 32;
+constexpr int kXT = 384, kXW = kXT / 32;  // one thread per position: 8 x 384 positions in one round
 constexpr int kStageBytes = 16 * 1024;
 constexpr int kMaxNSV = 12;
 constexpr int kErrCopyWait = 2;  // bit of the context error word: a copy wait gave up
@@ -57,7 +59,7 @@ struct XA {
 };
 
 struct XAttnLayout {
-  size_t vring, vsrc, sc, E, sum, total;
+  size_t vring, vsrc, srng, sc, E, sum, total;
 };
 
 // Stages of a span of n_ctx positions in units of R (an upper bound, R >= 8).
@@ -68,8 +70,9 @@ __host__ __device__ inline XAttnLayout xattn_layout(int nsv, int per_cap, int n_
   size_t o = 0;
   L.vring = o; o += (size_t)nsv * kStageBytes;
   L.vsrc = o; o += (size_t)max_stages(n_ctx) * 8;  // global address of each V stage
+  L.srng = o; o += ((size_t)max_stages(n_ctx) * 8 + 15) / 16 * 16;  // {first position, rows} of each V stage
   L.sc = o; o += ((size_t)8 * per_cap * 4 + 15) / 16 * 16;
-  L.E = o; o += ((size_t)n_ctx * 4 + 15) / 16 * 16;
+  L.E = o; o += ((size_t)n_ctx * 4 + 16 + 15) / 16 * 16;  // E[i] at lo % 4 + i: stage starts 16-byte aligned
   L.sum = o; o += (sizeof(exact::SumSmem<kXT>) + 15) / 16 * 16;
   L.total = o;
   return L;
@@ -119,13 +122,13 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   __shared__ __align__(16) float kn_s[HD], vn_s[HD];
   __shared__ float cs_s[2][HD / 2];
   __shared__ float mx_s[8], red_s[kXW][GP];
-  __shared__ float gmax_s[8];
+  __shared__ float gmax_s[8], xr_s[16][8];
   __shared__ int bad_s;
   const XAttnLayout L = xattn_layout(nsv, per_cap, n_ctx);
   char *vring = smem + L.vring;
   const char **vsrc = (const char **)(smem + L.vsrc);
-  float *sc = (float *)(smem + L.sc);  // [8][per_cap]: scores, then e_t
-  float *E = (float *)(smem + L.E);
+  int2 *srng = (int2 *)(smem + L.srng);
+  float *sc = (float *)(smem + L.sc);  // [8][per_cap]: scores
 
   const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
   const int h = blockIdx.x / cs, tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -136,6 +139,7 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   const int64_t span = seq - lo, per = (span + cs - 1) / cs;
   const int64_t s0 = lo + rank * per, s1 = s0 + per < seq ? s0 + per : seq;
   const int len = s1 > s0 ? (int)(s1 - s0) : 0;
+  float *E = (float *)(smem + L.E) + (lo & 3);  // E[i]: position lo + i
   const bool vsum = rank < G;
   const int nv = vsum ? stage_count(lo, seq, R) : 0;
 
@@ -165,6 +169,7 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
       const StageRange st = stage_of(lo, seq, R, k);
       const char *src = (const char *)a.kv.v + adev::kv_elem(a.kv, a.layer, h, st.t0) * A::ES;
       vsrc[k] = src;
+      srng[k] = make_int2((int)st.t0, st.n);
       if (k < nsv) {
         mbar_expect_tx(&vfull[k], (uint32_t)(st.n * A::ROW) + (k == 0 ? a.test_extra_tx : 0u));
         bulk_g2s(vring + k * kStageBytes, src, (uint32_t)(st.n * A::ROW), &vfull[k]);
@@ -247,9 +252,18 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
           chunk_vals<F16, A::CH>(raw[c], kv);
           const int e0 = (grp * A::GRP + c) * A::CH;
 #pragma unroll
-          for (int e = 0; e < A::CH; e++)
+          for (int e4 = 0; e4 < A::CH; e4 += 4) {
+            float4 qv[GP];
 #pragma unroll
-            for (int g = 0; g < GP; g++) d[g] = __fadd_rn(d[g], __fmul_rn(q_s[g][e0 + e], kv[e]));
+            for (int g = 0; g < GP; g++) qv[g] = *(const float4 *)&q_s[g][e0 + e4];
+#pragma unroll
+            for (int g = 0; g < GP; g++) {
+              d[g] = __fadd_rn(d[g], __fmul_rn(qv[g].x, kv[e4]));
+              d[g] = __fadd_rn(d[g], __fmul_rn(qv[g].y, kv[e4 + 1]));
+              d[g] = __fadd_rn(d[g], __fmul_rn(qv[g].z, kv[e4 + 2]));
+              d[g] = __fadd_rn(d[g], __fmul_rn(qv[g].w, kv[e4 + 3]));
+            }
+          }
         }
       }
     }
@@ -279,33 +293,29 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   }
   if (!ok) bad_s = 1;
   cluster.sync();
+  // Every rank's per-head maxima, read in parallel: thread r * G + g reads
+  // rank r's head g.
+  if (tid < cs * G) xr_s[tid / G][tid % G] = cluster.map_shared_rank(mx_s, tid / G)[tid % G];
+  __syncthreads();
   if (tid < G) {
     float m = -INFINITY;
-    for (int r = 0; r < cs; r++) {
-      const float v = cluster.map_shared_rank(mx_s, r)[tid];
-      if (v > m) m = v;
-    }
+    for (int r = 0; r < cs; r++)
+      if (xr_s[r][tid] > m) m = xr_s[r][tid];
     gmax_s[tid] = m;
   }
   __syncthreads();
-  for (int i = tid; len > 0 && i < G * len; i += kXT) {
-    const int g = i / len, j = i % len;
-    sc[g * per_cap + j] = exact::exp_ref(__fsub_rn(sc[g * per_cap + j], gmax_s[g]));
+  // e_t = exp(score - max) goes straight into E of the CTA that sums head g
+  // (rank g), at the position's place.
+  for (int g = 0; g < G; g++) {
+    float *dst = cluster.map_shared_rank(E, g) + (s0 - lo);
+    for (int j = tid; j < len; j += kXT) dst[j] = exact::exp_ref(__fsub_rn(sc[g * per_cap + j], gmax_s[g]));
   }
-  cluster.sync();  // every rank's e_t is ready
-
-  // Phase B: CTA g gathers head g's e_t in position order.
-  const int g = rank;
-  if (vsum)
-    for (int64_t i = tid; i < span; i += kXT) {
-      const int rr = (int)(i / per), j = (int)(i % per);
-      E[i] = cluster.map_shared_rank(sc, rr)[g * per_cap + j];
-    }
-  cluster.sync();  // no remote reads after this point
+  cluster.sync();  // every e_t has landed; no remote access after this point
   if (!vsum) {
     if (bad_s && tid == 0 && a.err) atomicOr(a.err, kErrCopyWait);
     return;
   }
+  const int g = rank;
   const float den = exact::seq_sum_nonneg<kXT>(E, (int)span, 0.0f, *(exact::SumSmem<kXT> *)(smem + L.sum));
   const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
   for (int64_t i = tid; i < span; i += kXT) E[i] = __fmul_rn(E[i], inv);
@@ -314,44 +324,58 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   float o = 0.0f;
   if (tid < HD) {  // output chain d = tid over all positions
     const int d = tid;
+    int slot = 0;
+    uint32_t par = 0;
     for (int k = 0; k < nv; k++) {
-      const int slot = k % nsv;
-      if (!mbar_wait_bounded(&vfull[slot], (uint32_t)((k / nsv) & 1), a.wait_ns)) ok = false;
-      const StageRange st = stage_of(lo, seq, R, k);
+      if (!mbar_wait_bounded(&vfull[slot], par, a.wait_ns)) ok = false;
+      const int2 st = srng[k];
       char *vs = vring + slot * kStageBytes;
-      if (st.t0 <= pos && pos < st.t0 + st.n) {  // the current row (only thread d reads element d)
-        const int j = (int)(pos - st.t0);
+      if (st.x <= pos && pos < st.x + st.y) {  // the current row (only thread d reads element d)
+        const int j = (int)(pos - st.x);
         if (F16) ((__half *)(vs + j * A::ROW))[d] = __float2half_rn(vn_s[d]);
         else ((float *)(vs + j * A::ROW))[d] = vn_s[d];
       }
-      const float *w = E + (st.t0 - lo);
+      const float *w = E + (st.x - lo);
       int j = 0;
-      for (; j + 16 <= st.n; j += 16) {
-        float v[16], ww[16];
+      if ((st.x & 3) == 0) {  // w 16-byte aligned: four weights per load
+        for (; j + 16 <= st.y; j += 16) {
+          float v[16];
+          float4 w4[4];
 #pragma unroll
-        for (int u = 0; u < 16; u++) {
-          v[u] = F16 ? __half2float(((const __half *)(vs + (j + u) * A::ROW))[d])
-                     : ((const float *)(vs + (j + u) * A::ROW))[d];
-          ww[u] = w[j + u];
+          for (int u = 0; u < 16; u++)
+            v[u] = F16 ? __half2float(((const __half *)(vs + (j + u) * A::ROW))[d])
+                       : ((const float *)(vs + (j + u) * A::ROW))[d];
+#pragma unroll
+          for (int u = 0; u < 4; u++) w4[u] = *(const float4 *)(w + j + 4 * u);
+          const float *ww = (const float *)w4;
+#pragma unroll
+          for (int u = 0; u < 16; u++) o = __fadd_rn(o, __fmul_rn(ww[u], v[u]));
         }
-#pragma unroll
-        for (int u = 0; u < 16; u++) o = __fadd_rn(o, __fmul_rn(ww[u], v[u]));
       }
-      for (; j < st.n; j++) {
+      for (; j < st.y; j++) {
         const float v = F16 ? __half2float(((const __half *)(vs + j * A::ROW))[d]) : ((const float *)(vs + j * A::ROW))[d];
         o = __fadd_rn(o, __fmul_rn(w[j], v));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&vempty[slot]);
+      if (++slot == nsv) {
+        slot = 0;
+        par ^= 1u;
+      }
     }
   } else if (tid == HD) {  // producer: refill a slot once every chain passed it
+    int slot = 0;
+    uint32_t par = 0;
     for (int k = nsv; k < nv; k++) {
-      const int slot = k % nsv;
-      if (!mbar_wait_bounded(&vempty[slot], (uint32_t)(((k - nsv) / nsv) & 1), a.wait_ns)) ok = false;
+      if (!mbar_wait_bounded(&vempty[slot], par, a.wait_ns)) ok = false;
       fence_proxy_async();
-      const StageRange st = stage_of(lo, seq, R, k);
-      mbar_expect_tx(&vfull[slot], (uint32_t)(st.n * A::ROW));
-      bulk_g2s(vring + slot * kStageBytes, vsrc[k], (uint32_t)(st.n * A::ROW), &vfull[slot]);
+      const int2 st = srng[k];
+      mbar_expect_tx(&vfull[slot], (uint32_t)(st.y * A::ROW));
+      bulk_g2s(vring + slot * kStageBytes, vsrc[k], (uint32_t)(st.y * A::ROW), &vfull[slot]);
+      if (++slot == nsv) {
+        slot = 0;
+        par ^= 1u;
+      }
     }
   }
   if (tid < HD) {
