@@ -168,6 +168,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     if (global_ns() - t0 > lim) return false;
   }
 }
+// As mbar_wait_bounded, sleeping ~128 ns between polls: for a waiter that
+// shares its SM sub-partition with latency-bound warps.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t *bar, uint32_t parity, uint64_t limit_ns = 0) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t lim = limit_ns ? limit_ns : kWaitNs, t0 = global_ns();
+  for (;;) {
+    __nanosleep(128);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > lim) return false;
+  }
+}
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),

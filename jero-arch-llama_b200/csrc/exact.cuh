@@ -24,8 +24,8 @@
 //   2. builds each segment's pair (or marks it sequential when it may cross a
 //      binade, holds non-finite terms or starts below the normal range);
 //   3. composes equal-binade neighbours (and neighbouring sequential
-//      segments) with a segmented warp scan and concatenates the warps'
-//      short lists; and
+//      segments) with a segmented scan over the group, which leaves a short
+//      list that alternates sequential segments and runs; and
 //   4. one thread applies the list in order to the start value.
 // Step 4 checks each run: the start must lie in the run's binade and so must
 // the end (start plus increment).  Because s only grows, that check is exact;
@@ -49,11 +49,20 @@ struct __align__(16) SumOp {
 template <int NT>
 struct SumSmem {
   double wtot[NT / 32];
-  int wcount[NT / 32];
+  uint32_t tc0[NT / 32], tc1[NT / 32], tcls[NT / 32], cls0[NT / 32];  // each warp's last lane; class of lane 0
+  int thl[NT / 32], wcount[NT / 32];
   int total;
-  SumOp ops[NT];  // the warps' lists, concatenated
+  SumOp ops[NT];  // the list of runs, in order
   float result;
 };
+
+// Composition of run increments: (a0, a1) for the earlier steps, then (c0,
+// c1); the result replaces (c0, c1).  Index = parity of the start mantissa.
+__device__ __forceinline__ void compose_inc(uint32_t a0, uint32_t a1, uint32_t &c0, uint32_t &c1) {
+  const uint32_t n0 = a0 + ((a0 & 1u) ? c1 : c0), n1 = a1 + (((1u + a1) & 1u) ? c1 : c0);
+  c0 = min(n0, 1u << 25);
+  c1 = min(n1, 1u << 25);
+}
 
 // Barrier over a group of NT threads: the whole block (bar 0) or the named
 // barrier `bar` shared by exactly NT threads.
@@ -64,6 +73,7 @@ __device__ __forceinline__ void group_sync(int bar) {
 }
 
 constexpr int kSumChunk = 16;  // terms a thread holds in registers at once
+constexpr int kSumSlack = 16;  // floats past the last term that may be read
 
 // Terms [base, base + 16) clamped to [base, end) (end > base): every load is
 // in bounds and all are in flight together; v[j] for base + j >= end repeats
@@ -79,7 +89,8 @@ __device__ __forceinline__ void load_chunk(const float *t, int base, int end, fl
 // 0.0` from +0.0).  All NT threads of a warp-aligned group call it with the
 // same arguments: gtid is the thread's index in the group and bar the group's
 // barrier (0 = the whole block, NT == blockDim.x).  t is readable by every
-// thread of the group (shared or global memory).
+// thread of the group (shared or global memory) up to t[n + kSumSlack - 1]:
+// the values past t[n - 1] are read and ignored.
 template <int NT, typename SM>
 __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gtid = -1, int bar = 0) {
   static_assert(NT % 32 == 0 && NT <= 1024, "block size");
@@ -127,8 +138,8 @@ __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gti
   // t adds k = t / U rounded to nearest, U = 2^(e-23); x = t / U = t *
   // 2^(23-e) is exact in f32, and for 0 <= x < 2^23 the f32 sum x + 2^23
   // rounds it to the nearest integer (ties to even) in its low mantissa
-  // bits.  Only an exact half (a tie) depends on the running parity, so the
-  // common tie-free segment is a plain integer sum.
+  // bits.  Only an exact half (a tie) depends on the running parity, which
+  // both accumulators follow.
   uint32_t E = 0, inc0 = 0, inc1 = 0;
   if (active && tid > 0) {
     // s_i is within 1.01 * i * u of the exact prefix; the estimate adds
@@ -140,8 +151,7 @@ __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gti
       const int eh = (int)((__double_as_longlong(hi) >> 52) & 0x7FF) - 1023;
       if (el == eh) {
         const float scale = __int_as_float((127 + 23 - el) << 23);  // 2^(23-e)
-        bool out = false, any_tie = false;
-        uint32_t ksum = 0;
+        bool out = false;
         for (int base = a; base < b; base += CH) {
           if (base != a || b - a > CH) load_chunk(t, base, b, v);  // one chunk: still in registers
 #pragma unroll
@@ -150,53 +160,79 @@ __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gti
             const float x = fminf(__fmul_rn(v[j], scale), 8388608.0f);  // t / U, exact below 2^23
             const float y = __fadd_rn(x, 8388608.0f);                     // 2^23 + nearest integer
             out |= in && x >= 8388608.0f;                                 // t >= 2^e: leaves the binade
-            any_tie |= in && fabsf(__fsub_rn(x, __fsub_rn(y, 8388608.0f))) == 0.5f;
-            ksum += in ? __float_as_uint(y) - 0x4B000000u : 0u;
+            const uint32_t k = in ? __float_as_uint(y) - 0x4B000000u : 0u;  // nearest, ties to even
+            const float r = __fsub_rn(x, __fsub_rn(y, 8388608.0f));
+            // a tie x = K + 1/2 adds the K or K + 1 that leaves the result
+            // mantissa even: it depends on the running parity
+            const bool tie = in && fabsf(r) == 0.5f;
+            const uint32_t K = r > 0.0f ? k : k - 1u;
+            inc0 += tie ? K + ((inc0 + K) & 1u) : k;
+            inc1 += tie ? K + ((1u + inc1 + K) & 1u) : k;
           }
-          ksum = min(ksum, 1u << 25);  // a run never adds more than 2^24; no wrap-around
-        }
-        inc0 = inc1 = ksum;
-        if (any_tie && !out) {  // ties go to the even result mantissa: follow both parities
-          inc0 = inc1 = 0;
-          for (int i = a; i < b; i++) {
-            const float x = __fmul_rn(t[i], scale);
-            const float fl = floorf(x);
-            const uint32_t K = (uint32_t)fl;
-            if (__fsub_rn(x, fl) == 0.5f) {
-              inc0 += K + ((inc0 + K) & 1u);
-              inc1 += K + ((1u + inc1 + K) & 1u);
-            } else {
-              const uint32_t k = __float_as_uint(__fadd_rn(x, 8388608.0f)) - 0x4B000000u;
-              inc0 += k;
-              inc1 += k;
-            }
-            inc0 = min(inc0, 1u << 25);
-            inc1 = min(inc1, 1u << 25);
-          }
+          inc0 = min(inc0, 1u << 25);  // a run never adds more than 2^24; no wrap-around
+          inc1 = min(inc1, 1u << 25);
         }
         if (!out) E = (uint32_t)(el + 127);
       }
     }
   }
 
-  // 3. compose equal neighbours within the warp: runs of one binade, and
-  // runs of sequential segments.  A segmented inclusive scan whose heads
-  // come from one ballot; then the warps' lists are concatenated in order.
-  const uint32_t E_prev = __shfl_up_sync(0xffffffffu, E, 1);
-  const bool head = lane == 0 || E_prev != E || !active;
-  const unsigned heads = __ballot_sync(0xffffffffu, head);
-  const int hl = 31 - __clz(heads & (0xffffffffu >> (31 - lane)));  // this lane's run head
+  // 3. compose equal neighbours: runs of one binade, and runs of sequential
+  // segments (class 0).  A segmented scan within each warp (heads from one
+  // ballot), a carry from the run's part in earlier warps, then the runs'
+  // ends (tails) write the list in order.  Neighbouring runs always differ
+  // in class, and two binade runs are never adjacent (a binade change
+  // happens inside a sequential segment), so the list alternates
+  // sequential, run, sequential, ... from segment 0, which is sequential.
+  const uint32_t cls = active ? E : 0xFFFFFFFFu;
+  const uint32_t cls_up = __shfl_up_sync(0xffffffffu, cls, 1);
+  const unsigned heads = __ballot_sync(0xffffffffu, lane == 0 || cls_up != cls);
+  const int hl = 31 - __clz(heads & (0xffffffffu >> (31 - lane)));  // this lane's run head in the warp
   uint32_t c0 = inc0, c1 = inc1;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t p0 = __shfl_up_sync(0xffffffffu, c0, o), p1 = __shfl_up_sync(0xffffffffu, c1, o);
-    if (lane - o >= hl) {  // previous steps first, then these
-      const uint32_t n0 = p0 + ((p0 & 1u) ? c1 : c0), n1 = p1 + (((1u + p1) & 1u) ? c1 : c0);
-      c0 = min(n0, 1u << 25);
-      c1 = min(n1, 1u << 25);
+    if (lane - o >= hl) compose_inc(p0, p1, c0, c1);  // previous steps first, then these
+  }
+  if (lane == 31) {
+    sm.tc0[warp] = c0;
+    sm.tc1[warp] = c1;
+    sm.tcls[warp] = cls;
+    sm.thl[warp] = hl;
+  }
+  if (lane == 0) sm.cls0[warp] = cls;
+  group_sync<NT>(bar);
+  // The run that lane 0 continues from earlier warps: a segmented scan over
+  // the warps' tails (lane l = warp l), done by every warp.
+  int start = (warp * 32 + hl) * c;  // first term of this lane's run
+  {
+    constexpr int NW = NT / 32;
+    const bool lv = lane < NW;
+    uint32_t q0 = lv ? sm.tc0[lane] : 0u, q1 = lv ? sm.tc1[lane] : 0u;
+    const uint32_t tcl = lv ? sm.tcls[lane] : 0xFFFFFFFFu, cl0 = lv ? sm.cls0[lane] : 0xFFFFFFFFu;
+    const int thl_l = lv ? sm.thl[lane] : 0;
+    const uint32_t tcl_up = __shfl_up_sync(0xffffffffu, tcl, 1);
+    const bool cont = lane > 0 && cl0 != 0xFFFFFFFFu && cl0 == tcl_up;  // warp lane's lane 0 continues a run
+    const unsigned wheads = __ballot_sync(0xffffffffu, !(cont && thl_l == 0));
+    const int wh = 31 - __clz(wheads & (0xffffffffu >> (31 - lane)));  // warp where warp lane's tail run starts
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t p0 = __shfl_up_sync(0xffffffffu, q0, o), p1 = __shfl_up_sync(0xffffffffu, q1, o);
+      if (lane - o >= wh) compose_inc(p0, p1, q0, q1);
+    }
+    const int rs = (wh * 32 + __shfl_sync(0xffffffffu, thl_l, wh)) * c;
+    const bool cont_w = __shfl_sync(0xffffffffu, cont, warp);
+    const uint32_t k0 = __shfl_sync(0xffffffffu, q0, warp > 0 ? warp - 1 : 0);
+    const uint32_t k1 = __shfl_sync(0xffffffffu, q1, warp > 0 ? warp - 1 : 0);
+    const int rs_prev = __shfl_sync(0xffffffffu, rs, warp > 0 ? warp - 1 : 0);
+    if (cont_w && hl == 0 && active) {
+      compose_inc(k0, k1, c0, c1);
+      start = rs_prev;
     }
   }
-  const bool tail = active && (lane == 31 || ((heads >> (lane + 1)) & 1u));
+  const uint32_t cls_dn = __shfl_down_sync(0xffffffffu, cls, 1);
+  const uint32_t next_cls = lane < 31 ? cls_dn : (warp + 1 < NT / 32 ? sm.cls0[warp + 1] : 0xFFFFFFFFu);
+  const bool tail = active && next_cls != cls;
   const unsigned tails = __ballot_sync(0xffffffffu, tail);
   if (lane == 0) sm.wcount[warp] = __popc(tails);
   group_sync<NT>(bar);
@@ -205,7 +241,7 @@ __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gti
   for (int o = 16; o >= 1; o >>= 1) off += __shfl_xor_sync(0xffffffffu, off, o);
   if (tail) {
     SumOp op;
-    op.x = E ? c0 : (uint32_t)((warp * 32 + hl) * c);
+    op.x = E ? c0 : (uint32_t)start;
     op.y = E ? c1 : (uint32_t)b;
     op.E = E;
     op.pad = 0u;
@@ -214,33 +250,57 @@ __device__ float seq_sum_nonneg(const float *t, int n, float s0, SM &sm, int gti
   if (tid == NT - 1) sm.total = off + __popc(tails);  // the last warp's offset + count
   group_sync<NT>(bar);
 
-  // 4. apply the list in order (entries loaded two ahead).  A run's checks
-  // (start and end in its binade) are collected and tested once at the end;
-  // if one failed -- the estimate cannot place a run wrongly, so this is a
-  // safety net only -- the sum is recomputed with plain adds.
+  // 4. apply the list: sequential entries at even places, runs at odd
+  // places.  A run's checks (start and end in its binade) are collected and
+  // tested once at the end; if one failed -- the estimate cannot place a run
+  // wrongly, so this is a safety net only -- the sum is recomputed with
+  // plain adds.
   if (tid == 0) {
     const int T = sm.total;
     float s = s0;
     bool ok = true;
-    SumOp cur = sm.ops[0], nxt = sm.ops[T > 1 ? 1 : 0];
-    for (int k = 0; k < T; k++) {
-      const SumOp nx2 = sm.ops[k + 2 < T ? k + 2 : T - 1];
-      if (cur.E) {
-        const uint32_t bits = __float_as_uint(s);
-        const uint32_t nb = bits + ((bits & 1u) ? cur.y : cur.x);  // mantissa parity = parity of the bits
-        ok = ok & ((bits >> 23) == cur.E) & ((nb >> 23) == cur.E);  // positive; start and end in the binade
-        s = __uint_as_float(nb);
-      } else {
-        for (int i0 = (int)cur.x; i0 < (int)cur.y; i0 += CH) {  // all loads in flight, then the adds in order
-          float x[CH];
-          load_chunk(t, i0, (int)cur.y, x);
+    // Entry k + 2 is loaded and the terms of the next sequential entry are
+    // in registers while entry k is applied; two list places per step.
+    auto load_seq = [&](const SumOp &q, float (&x)[CH]) {
+      const int base = q.E ? 0 : (int)q.x;  // a run's x is an increment, not a place
 #pragma unroll
-          for (int j = 0; j < CH; j++)
-            if (i0 + j < (int)cur.y) s = __fadd_rn(s, x[j]);
-        }
+      for (int j = 0; j < CH; j++) x[j] = t[base + j];  // t has CH readable floats past its end
+    };
+    auto step = [&](int k, const SumOp &sq, const SumOp &run, const float (&x)[CH]) {
+      ok = ok & (sq.E == 0u);  // the alternation holds by construction; checked all the same
+      const int len = (int)sq.y - (int)sq.x;
+#pragma unroll
+      for (int j = 0; j < CH; j++) s = __fadd_rn(s, j < len ? x[j] : -0.0f);  // s + -0 == s for every s
+      for (int i0 = (int)sq.x + CH; i0 < (int)sq.y; i0 += CH) {  // long sequential entries
+        float y[CH];
+#pragma unroll
+        for (int j = 0; j < CH; j++) y[j] = t[i0 + j];
+#pragma unroll
+        for (int j = 0; j < CH; j++) s = __fadd_rn(s, i0 + j < (int)sq.y ? y[j] : -0.0f);
       }
-      cur = nxt;
-      nxt = nx2;
+      if (k + 1 < T) {
+        const uint32_t bits = __float_as_uint(s);
+        const uint32_t nb = bits + ((bits & 1u) ? run.y : run.x);  // mantissa parity = parity of the bits
+        ok = ok & (run.E != 0u) & ((bits >> 23) == run.E) & ((nb >> 23) == run.E);  // start and end in the binade
+        s = __uint_as_float(nb);
+      }
+    };
+    auto at = [&](int k) { return sm.ops[k < T ? k : T - 1]; };
+    SumOp sq = at(0), run = at(1), nsq = at(2), nrun = at(3);
+    float xa[CH], xb[CH];
+    load_seq(sq, xa);
+    for (int k = 0; k < T; k += 4) {
+      load_seq(nsq, xb);
+      const SumOp sq2 = at(k + 4), run2 = at(k + 5);
+      step(k, sq, run, xa);
+      if (k + 2 >= T) break;
+      load_seq(sq2, xa);
+      const SumOp nsq2 = at(k + 6), nrun2 = at(k + 7);
+      step(k + 2, nsq, nrun, xb);
+      sq = sq2;
+      run = run2;
+      nsq = nsq2;
+      nrun = nrun2;
     }
     if (!ok) {
       s = s0;

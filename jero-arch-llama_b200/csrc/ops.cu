@@ -209,7 +209,7 @@ void launch_gqa_attention_ref(const float *q, const float *k, const float *v, in
                               int64_t hd, int64_t total_seq, int64_t start_pos, int64_t window, float scale,
                               float *out, cudaStream_t s) {
   if (!m) return;
-  size_t smem = (size_t)total_seq * sizeof(float);
+  size_t smem = ((size_t)total_seq + exact::kSumSlack) * sizeof(float);  // scores + the sum's read slack
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_gqa_ref, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k_gqa_ref<<<dim3((unsigned)m, (unsigned)nq), 128, smem, s>>>(q, k, v, nq, nkv, hd, total_seq, start_pos, window,
                                                               scale, out);

@@ -238,15 +238,16 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm(const float *__restric
   for (int64_t i = threadIdx.x; i < n; i += kNormThreads) out[blockIdx.x * n + i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
-constexpr int kNormMaxSmem = 160 * 1024;  // rows up to 40960 elements
+constexpr int kNormMaxSmem = 160 * 1024;  // rows up to 40944 elements
 
-static bool norm_fits(int64_t n) { return (size_t)n * 4 <= (size_t)kNormMaxSmem; }
+static size_t norm_smem(int64_t n) { return ((size_t)n + exact::kSumSlack) * 4; }  // squares + the sum's read slack
+static bool norm_fits(int64_t n) { return norm_smem(n) <= (size_t)kNormMaxSmem; }
 
 void launch_rmsnorm(const float *x, const float *w, int64_t m, int64_t n, float eps, float *out, cudaStream_t s) {
   if (!m) return;
   norm_init();
   if (!norm_fits(n)) fail(JAL_ERR_CAPABILITY_MISMATCH, "rmsnorm: row of %lld elements too long", (long long)n);
-  k_rmsnorm<<<(unsigned)m, kNormThreads, (size_t)n * 4, s>>>(x, w, n, eps, out);
+  k_rmsnorm<<<(unsigned)m, kNormThreads, norm_smem(n), s>>>(x, w, n, eps, out);
 }
 
 
@@ -284,7 +285,7 @@ void launch_rmsnorm_quant(const float *x, const float *w, int64_t m, int64_t n, 
   if (!m) return;
   norm_init();
   if (!norm_fits(n)) fail(JAL_ERR_CAPABILITY_MISMATCH, "rmsnorm: row of %lld elements too long", (long long)n);
-  k_rmsnorm_quant<<<(unsigned)m, kNormThreads, (size_t)n * 4, s>>>(x, w, n, eps, q8, scales);
+  k_rmsnorm_quant<<<(unsigned)m, kNormThreads, norm_smem(n), s>>>(x, w, n, eps, q8, scales);
 }
 
 // ---- integer 16-element partials (repack_cache.rs:759-762) ---------------

@@ -69,12 +69,12 @@ __host__ __device__ inline XAttnLayout xattn_layout(int nsv, int per_cap, int n_
   XAttnLayout L;
   size_t o = 0;
   L.vring = o; o += (size_t)nsv * kStageBytes;
-  L.vsrc = o; o += (size_t)max_stages(n_ctx) * 8;  // global address of each V stage
+  L.vsrc = o; o += ((size_t)max_stages(n_ctx) * 8 + 15) / 16 * 16;  // global address of each V stage
   L.srng = o; o += ((size_t)max_stages(n_ctx) * 8 + 15) / 16 * 16;  // {first position, rows} of each V stage
   L.sc = o; o += ((size_t)8 * per_cap * 4 + 15) / 16 * 16;
   L.E = o; o += ((size_t)n_ctx * 4 + 16 + 15) / 16 * 16;  // E[i] at lo % 4 + i: stage starts 16-byte aligned
-  L.sum = o; o += (sizeof(exact::SumSmem<kXT>) + 15) / 16 * 16;
-  L.total = o;
+  L.sum = o; o += (sizeof(exact::SumSmem<kXT>) + 15) / 16 * 16;  // also E's read slack
+  L.total = o;  // every piece starts 16-byte aligned (E's 16-byte loads, the sum's 16-byte entries)
   return L;
 }
 
@@ -363,11 +363,13 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
         par ^= 1u;
       }
     }
-  } else if (tid == HD) {  // producer: refill a slot once every chain passed it
+  } else if (tid == HD + 32) {  // producer (own warp): refill a slot once every chain passed it
     int slot = 0;
     uint32_t par = 0;
     for (int k = nsv; k < nv; k++) {
-      if (!mbar_wait_bounded(&vempty[slot], par, a.wait_ns)) ok = false;
+      // a stage takes the chains ~0.5 us: poll gently so the chain warp on
+      // this SM sub-partition keeps its issue slots
+      if (!mbar_wait_sleepy(&vempty[slot], par, a.wait_ns)) ok = false;
       fence_proxy_async();
       const int2 st = srng[k];
       mbar_expect_tx(&vfull[slot], (uint32_t)(st.y * A::ROW));

@@ -78,7 +78,7 @@ __host__ __device__ inline XLayout x_layout(int64_t cols, int in_mode) {
   L.xin = p; if (in_mode != GEMV_IN_Q8) p += row;
   L.nw = p; if (in_mode == GEMV_IN_NORM) p += row;
   L.xsq = p; if (in_mode == GEMV_IN_NORM) p += row;
-  L.sum = p; if (in_mode == GEMV_IN_NORM) p += (sizeof(exact::SumSmem<kNT>) + 15) / 16 * 16;
+  L.sum = p; if (in_mode == GEMV_IN_NORM) p += (sizeof(exact::SumSmem<kNT>) + 15) / 16 * 16;  // also the squares' read slack
   L.total = o + (fold > p - o ? fold : p - o);
   return L;
 }

@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kPT, 1) k_xattn_prefill(const AttnPrefillArgs 
 
 template <int HD, bool F16>
 void launch_p(const AttnPrefillArgs &a, int smax, cudaStream_t s) {
-  const size_t smem = 2 * (size_t)XP<HD, F16>::TILE + (size_t)kQB * smax * 4;
+  const size_t smem = 2 * (size_t)XP<HD, F16>::TILE + ((size_t)kQB * smax + exact::kSumSlack) * 4;  // + the sum's read slack
   cudaFuncSetAttribute(k_xattn_prefill<HD, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)a.n_heads_q, (unsigned)((a.m + kQB - 1) / kQB));
   k_xattn_prefill<HD, F16><<<grid, kPT, smem, s>>>(a, smax);
@@ -196,7 +196,7 @@ void launch_p(const AttnPrefillArgs &a, int smax, cudaStream_t s) {
 // Keys one CTA may score: the block's range is at most (window or start + m).
 bool xattn_prefill_supported(int64_t head_dim, int64_t max_keys) {
   if (head_dim != 64 && head_dim != 128) return false;
-  const size_t smem = 2 * (size_t)(kKT * (head_dim * 4 + 16)) + (size_t)kQB * (max_keys + kQB) * 4;
+  const size_t smem = 2 * (size_t)(kKT * (head_dim * 4 + 16)) + ((size_t)kQB * (max_keys + kQB) + exact::kSumSlack) * 4;
   return smem <= 220 * 1024;
 }
 

@@ -161,6 +161,17 @@ def test_tiny_llama_greedy_fp16_paged_kv(jal, oracle, torch_cuda):
     print(f"tiny llama fp16-KV relaxed worst |dlogit| = {worst_r:.3e}, top-1 agreement {agree:.2f}")
 
 
+@pytest.mark.parametrize("n_ctx", [72, 200])
+def test_decode_attention_shared_memory_layout_any_context(jal, oracle, torch_cuda, n_ctx):
+    """The decode attention's shared-memory pieces are placed from the context
+    length (one V-stage address per 8 positions, scores, e_t): bit equality at
+    context lengths whose stage tables have an odd number of entries."""
+    spec = jal.TINY_LLAMA
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=2024, kv_dtype=jal.KV_F16, n_ctx=n_ctx,
+                                     numerics=jal.NUMERICS_FAST)
+    run_parity(om, ctx, prompt_of(7), 12, n_ctx)
+
+
 def test_tiny_qwen2_neox_bias_q8_0(jal, oracle, torch_cuda):
     spec = jal.SynthSpec(architecture="qwen2", weight_quant=jal.Q8_0, qkv_bias=True, rope_theta=1e6, rms_eps=1e-6,
                          head_quant=-1)
