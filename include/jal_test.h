@@ -21,10 +21,10 @@
 extern "C" {
 #endif
 
-/* From the next decode step on, the decode attention's first V-copy barrier
- * of every KV head expects extra_bytes more than the copy sends, and each
- * copy wait gives up after wait_ns (0 = the default 2 s); extra_bytes = 0
- * and wait_ns = 0 restore normal operation.  Contexts of the FAST numerics
+/* From the next decode step on, the decode attention's last V-stage barrier
+ * (in every output CTA) expects extra_bytes more than the copy sends, and
+ * each copy wait gives up after wait_ns (0 = the default 2 s); extra_bytes =
+ * 0 and wait_ns = 0 restore normal operation.  Contexts of the FAST numerics
  * on one GPU only (JAL_ERR_CAPABILITY_MISMATCH otherwise). */
 int jal_context_test_stall_kv_copy(jal_context *ctx, uint32_t extra_bytes,
                                    uint64_t wait_ns);

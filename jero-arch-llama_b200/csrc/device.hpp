@@ -206,14 +206,43 @@ struct AttnDecodeArgs {
   int *err = nullptr;           // error word: bit 2 = a bounded copy wait gave up
   int pdl = 0;
   uint64_t wait_ns = 0;         // bound of each copy wait (0 = 2 s)
-  uint32_t test_extra_tx = 0;   // test hook: the first V copy's barrier expects this many bytes more
+  uint32_t test_extra_tx = 0;   // test hook: the first V copy's barrier expects this many bytes more (k_attn_decode)
+  float *w_out = nullptr;       // reference-order kernel: [n_heads_q][w_stride] weights e_t / den by position
+  int64_t w_stride = 0;
 };
 void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
-// Reference-order decode attention (xattn.cu): clusters of a.n_splits CTAs
-// per KV head; n_ctx bounds the positions (shared-memory sizing).
+// Reference-order decode attention, scores (xattn.cu): clusters of
+// a.n_splits CTAs per KV head build q / k / v, append k / v, and write each
+// query head's weights w_t = e_t * (1 / den) to a.w_out; n_ctx bounds the
+// positions (shared-memory sizing).
 void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s);
 // Cluster size for launch_xattn_decode (>= G), 0 when the shape does not fit.
 int xattn_cluster_size(int head_dim, int f16, int G, int n_kv, int64_t n_ctx);
+
+// Reference-order decode attention, output (xattn_v.cu): out_d = sum_t w_t
+// * v_td in position order, then its QuantizedActQ8 blocks.
+struct AttnVArgs {
+  KvView kv;
+  int64_t layer = 0, window = 0, n_heads_q = 0;
+  const int64_t *d_pos = nullptr;
+  const float *w = nullptr;  // [n_heads_q][w_stride], by position
+  int64_t w_stride = 0;
+  float *out = nullptr;
+  int8_t *out_q = nullptr;
+  float *out_s = nullptr;
+  int *err = nullptr;  // bit value 2: a bounded copy wait gave up
+  int pdl = 0;
+  uint64_t wait_ns = 0;
+  uint32_t test_extra_tx = 0;  // test hook: the last V stage's barrier expects this many bytes more
+};
+// Positions per V stage: the largest power of two <= 64 dividing the page size.
+int kv_stage_rows(int64_t page_size);
+bool xattn_v_supported(int64_t head_dim, int64_t page_size, int64_t n_ctx);
+// Encodes the 2D tensor map of one KV plane at `base` (rows of head_dim
+// elements, boxes of 32 dims x kv_stage_rows positions) into tm_out, a
+// 64-byte aligned 128-byte buffer.  False if the driver refuses.
+bool make_kv_tensor_map(const KvView &kv, const void *base, void *tm_out);
+void launch_xattn_v(const void *tm, const AttnVArgs &a, int64_t n_ctx, cudaStream_t s);
 // Largest cluster size (<= want) the decode attention kernel can run with
 // for head_dim, KV element type and G query heads per KV head.
 int attn_decode_cluster_size(int head_dim, int f16, int G, int want);

@@ -1012,6 +1012,14 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
     if (!xattn_prefill_supported((int64_t)g.head_dim, (int64_t)keys + 4))
       fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order prefill attention: n_ctx %llu does not fit",
            (unsigned long long)ctx->cfg.n_ctx);
+    if (!xattn_v_supported((int64_t)g.head_dim, kv.page_size, (int64_t)ctx->cfg.n_ctx))
+      fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention output: n_ctx %llu does not fit",
+           (unsigned long long)ctx->cfg.n_ctx);
+    if (!make_kv_tensor_map(kv, kv.v, ctx->tm_v))
+      fail(JAL_ERR_CUDA, "reference-order decode attention: the driver refused the V tensor map");
+    auto wb = alloc((size_t)g.n_heads_q * ctx->cfg.n_ctx * 4);
+    ctx->bufs.push_back(wb);
+    ctx->attn_w = wb->as<float>();
   }
   // Decode buffers.
   const int sms = sm_count();
@@ -1247,9 +1255,14 @@ void Context::enqueue_exact_step(bool pdl) {
     aa.kv = kv; aa.layer = (int64_t)l; aa.d_pos = d_pos; aa.window = (int64_t)cfg.sliding_window;
     aa.scale = 1.0f / sqrtf((float)g.head_dim);
     aa.n_splits = x_splits;
-    aa.out = attn; aa.out_q = attn_q; aa.out_s = attn_s; aa.err = d_err; aa.pdl = pdl;
-    aa.test_extra_tx = test_stall_tx; aa.wait_ns = test_wait_ns;
+    aa.w_out = attn_w; aa.w_stride = (int64_t)cfg.n_ctx; aa.err = d_err; aa.pdl = pdl;
     launch_xattn_decode(aa, (int64_t)cfg.n_ctx, stream);
+    AttnVArgs va;
+    va.kv = kv; va.layer = (int64_t)l; va.window = (int64_t)cfg.sliding_window; va.n_heads_q = (int64_t)g.n_heads_q;
+    va.d_pos = d_pos; va.w = attn_w; va.w_stride = (int64_t)cfg.n_ctx;
+    va.out = attn; va.out_q = attn_q; va.out_s = attn_s; va.err = d_err; va.pdl = pdl;
+    va.test_extra_tx = test_stall_tx; va.wait_ns = test_wait_ns;
+    launch_xattn_v(tm_v, va, (int64_t)cfg.n_ctx, stream);
     GemvArgs oa;
     oa.w = L.wo.dm; oa.rows = (int64_t)H; oa.in_mode = GEMV_IN_Q8;
     oa.xq = attn_q; oa.xs = attn_s; oa.xq_stride = (int64_t)Q;
@@ -1264,7 +1277,7 @@ void Context::enqueue_exact_step(bool pdl) {
     da.w = L.wdown.dm; da.rows = (int64_t)H; da.in_mode = GEMV_IN_F32; da.x = ffn; da.x_stride = (int64_t)F;
     da.out_mode = GEMV_OUT_ADD; da.y = hidden; da.y_stride = (int64_t)H; da.pdl = pdl;
     launch_xgemv(da, stream);
-    n += 5;
+    n += 6;
   }
   if (dense_quant(c.lm_head.dm.quant)) {
     launch_rmsnorm(hidden, c.output_norm->as<float>(), 1, (int64_t)H, eps, s_norm, stream);

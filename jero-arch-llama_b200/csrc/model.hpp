@@ -169,6 +169,10 @@ struct Context {
   // xattn kernels, x_splits CTAs per KV head in decode attention.
   bool exact = false;
   int x_splits = 0;
+  // The score kernel's weights w_t = e_t / den, [n_heads_q][n_ctx], and the
+  // 2D tensor map of the V plane the output kernel stages from.
+  float *attn_w = nullptr;
+  alignas(64) unsigned char tm_v[128] = {};
   // Test hook (jal_test.h): the decode attention's first V copy barrier
   // expects test_stall_tx bytes more than are sent, so its bounded wait
   // (test_wait_ns) runs out.

@@ -8,28 +8,21 @@
 //   out_d = sum_t (e_t * inv) * v_td, left to right over t from +0.0
 // Every product and sum is one f32 rounding, no fused multiply-add.
 //
+// This kernel stops at the weights w_t = e_t * inv, which it writes per
+// query head and position; xattn_v.cu runs the output chains.
+//
 // Grid: one thread-block cluster of CS CTAs per KV head (CS >= G, the query
-// heads per KV head).  V moves as stages of R positions that never cross a
-// page (R a power of two dividing the page size, R * row <= 16 KB), one bulk
-// copy per stage.
-// Phase A: every CTA builds q (bias, RoPE) for the G heads and the new k / v
-// (the CTA holding the current position appends them; with an f16 cache the
-// rounded values are what every step reads), then scores its contiguous
-// share of the positions: a thread per position loads its K row (prefetched
-// into L2 before griddepcontrol.wait) into registers, 256 bytes at a time as
-// independent 16-byte loads, and runs the G score chains over the dims in
-// order.  The cluster agrees on each head's max through distributed shared
-// memory (all ranks' maxima read at once), and every CTA writes its e_t
-// straight into the position-ordered array of the CTA that owns the head.
-// Phase B: CTA g < G forms head g's exact sequential denominator
-// (exact::seq_sum_nonneg) and runs the HD output chains (thread d) over all
-// positions in order, four weights per shared-memory load.  Its V stages
-// started streaming into a ring before griddepcontrol.wait (stage ranges
-// precomputed, one per thread); a producer thread refills a slot once every
-// chain has passed it.  That CTA writes the output
-// row and its QuantizedActQ8 blocks (the O projection's input).  Waits on
-// copies are bounded: a wait that gives up sets bit value 2 of the context's
-// error word and the kernel runs to its end.
+// heads per KV head).  Every CTA builds q (bias, RoPE) for the G heads and
+// the new k / v (the CTA holding the current position appends them; with an
+// f16 cache the rounded values are what every step reads), then scores its
+// contiguous share of the positions: a thread per position loads its K row
+// (prefetched into L2 before griddepcontrol.wait) into registers, 256 bytes
+// at a time as independent 16-byte loads, and runs the G score chains over
+// the dims in order.  The cluster agrees on each head's max through
+// distributed shared memory (all ranks' maxima read at once), and every CTA
+// writes its e_t straight into the position-ordered array of the CTA that
+// owns the head.  CTA g < G then forms head g's exact sequential denominator
+// (exact::seq_sum_nonneg) and writes w_t.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
@@ -45,9 +38,6 @@ namespace jal {
 namespace {
 
 constexpr int kXT = 384, kXW = kXT / 32;  // one thread per position: 8 x 384 positions in one round
-constexpr int kStageBytes = 16 * 1024;
-constexpr int kMaxNSV = 12;
-constexpr int kErrCopyWait = 2;  // bit of the context error word: a copy wait gave up
 
 template <int HD, bool F16>
 struct XA {
@@ -59,22 +49,16 @@ struct XA {
 };
 
 struct XAttnLayout {
-  size_t vring, vsrc, srng, sc, E, sum, total;
+  size_t sc, E, sum, total;
 };
 
-// Stages of a span of n_ctx positions in units of R (an upper bound, R >= 8).
-__host__ __device__ inline int max_stages(int n_ctx) { return n_ctx / 8 + 2; }
-
-__host__ __device__ inline XAttnLayout xattn_layout(int nsv, int per_cap, int n_ctx) {
+__host__ __device__ inline XAttnLayout xattn_layout(int per_cap, int n_ctx) {
   XAttnLayout L;
   size_t o = 0;
-  L.vring = o; o += (size_t)nsv * kStageBytes;
-  L.vsrc = o; o += ((size_t)max_stages(n_ctx) * 8 + 15) / 16 * 16;  // global address of each V stage
-  L.srng = o; o += ((size_t)max_stages(n_ctx) * 8 + 15) / 16 * 16;  // {first position, rows} of each V stage
   L.sc = o; o += ((size_t)8 * per_cap * 4 + 15) / 16 * 16;
-  L.E = o; o += ((size_t)n_ctx * 4 + 16 + 15) / 16 * 16;  // E[i] at lo % 4 + i: stage starts 16-byte aligned
+  L.E = o; o += ((size_t)n_ctx * 4 + 16 + 15) / 16 * 16;  // E[i] at lo % 4 + i
   L.sum = o; o += (sizeof(exact::SumSmem<kXT>) + 15) / 16 * 16;  // also E's read slack
-  L.total = o;  // every piece starts 16-byte aligned (E's 16-byte loads, the sum's 16-byte entries)
+  L.total = o;  // every piece starts 16-byte aligned (the sum's 16-byte entries)
   return L;
 }
 
@@ -112,22 +96,17 @@ __device__ __forceinline__ void chunk_vals(uint4 raw, float (&o)[CH]) {
 }
 
 template <int HD, bool F16, int GP>
-__global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int per_cap, int n_ctx, int R, int nsv) {
+__global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int per_cap, int n_ctx, int R) {
   namespace cg = cooperative_groups;
   using A = XA<HD, F16>;
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(128) char smem[];
-  __shared__ __align__(8) uint64_t vfull[kMaxNSV], vempty[kMaxNSV];
   __shared__ __align__(16) float q_s[GP][HD];
-  __shared__ __align__(16) float kn_s[HD], vn_s[HD];
+  __shared__ __align__(16) float kn_s[HD];
   __shared__ float cs_s[2][HD / 2];
   __shared__ float mx_s[8], red_s[kXW][GP];
   __shared__ float gmax_s[8], xr_s[16][8];
-  __shared__ int bad_s;
-  const XAttnLayout L = xattn_layout(nsv, per_cap, n_ctx);
-  char *vring = smem + L.vring;
-  const char **vsrc = (const char **)(smem + L.vsrc);
-  int2 *srng = (int2 *)(smem + L.srng);
+  const XAttnLayout L = xattn_layout(per_cap, n_ctx);
   float *sc = (float *)(smem + L.sc);  // [8][per_cap]: scores
 
   const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
@@ -141,39 +120,16 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   const int len = s1 > s0 ? (int)(s1 - s0) : 0;
   float *E = (float *)(smem + L.E) + (lo & 3);  // E[i]: position lo + i
   const bool vsum = rank < G;
-  const int nv = vsum ? stage_count(lo, seq, R) : 0;
 
-  if (tid == 0) {
-    for (int s = 0; s < nsv; s++) {
-      mbar_init(&vfull[s], 1);
-      mbar_init(&vempty[s], HD / 32);  // one arrival per consumer warp
-    }
-    bad_s = 0;
-    fence_barrier_init();
-    fence_proxy_async();
-  }
-  __syncthreads();
   // Rows below the current position were written by earlier launches (the
-  // current row is taken from shared memory below).  Thread k looks up stage
-  // k's page (all lookups in parallel): K stages of this CTA's share go to
-  // L2, the first V stages of the whole span into the ring; the addresses of
-  // every V stage are kept for the refills.
+  // current row is taken from shared memory below): thread k looks up stage k
+  // of this CTA's share (all lookups in parallel) and prefetches it to L2.
   {
     const int nks = stage_count(s0, s1, R);
     for (int k = tid; k < nks; k += kXT) {
       const StageRange st = stage_of(s0, s1, R, k);
       l2_prefetch_bulk((const char *)a.kv.k + adev::kv_elem(a.kv, a.layer, h, st.t0) * A::ES,
                        (uint64_t)st.n * A::ROW);
-    }
-    for (int k = tid; k < nv; k += kXT) {
-      const StageRange st = stage_of(lo, seq, R, k);
-      const char *src = (const char *)a.kv.v + adev::kv_elem(a.kv, a.layer, h, st.t0) * A::ES;
-      vsrc[k] = src;
-      srng[k] = make_int2((int)st.t0, st.n);
-      if (k < nsv) {
-        mbar_expect_tx(&vfull[k], (uint32_t)(st.n * A::ROW) + (k == 0 ? a.test_extra_tx : 0u));
-        bulk_g2s(vring + k * kStageBytes, src, (uint32_t)(st.n * A::ROW), &vfull[k]);
-      }
     }
   }
   const bool rope = !a.skip_rope && pos > 0;
@@ -218,7 +174,6 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
     } else {
       if (F16) o = __half2float(__float2half_rn(o));
       if (g == G) kn_s[d] = o;
-      else vn_s[d] = o;
       if (own_pos) adev::store_kv(g == G ? a.kv.k : a.kv.v, a.kv.f16, app + d, o);  // recipe.rs:2319-2326
     }
   }
@@ -226,7 +181,6 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   __syncthreads();
 
   // Phase A: scores, one thread per position of this CTA's share.
-  bool ok = true;
   float lmax[GP];
 #pragma unroll
   for (int g = 0; g < GP; g++) lmax[g] = -INFINITY;
@@ -291,7 +245,6 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
         if (red_s[w][tid] > m) m = red_s[w][tid];
     mx_s[tid] = m;
   }
-  if (!ok) bad_s = 1;
   cluster.sync();
   // Every rank's per-head maxima, read in parallel: thread r * G + g reads
   // rank r's head g.
@@ -311,87 +264,12 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
     for (int j = tid; j < len; j += kXT) dst[j] = exact::exp_ref(__fsub_rn(sc[g * per_cap + j], gmax_s[g]));
   }
   cluster.sync();  // every e_t has landed; no remote access after this point
-  if (!vsum) {
-    if (bad_s && tid == 0 && a.err) atomicOr(a.err, kErrCopyWait);
-    return;
-  }
+  if (!vsum) return;
   const int g = rank;
   const float den = exact::seq_sum_nonneg<kXT>(E, (int)span, 0.0f, *(exact::SumSmem<kXT> *)(smem + L.sum));
   const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
-  for (int64_t i = tid; i < span; i += kXT) E[i] = __fmul_rn(E[i], inv);
-  __syncthreads();
-
-  float o = 0.0f;
-  if (tid < HD) {  // output chain d = tid over all positions
-    const int d = tid;
-    int slot = 0;
-    uint32_t par = 0;
-    for (int k = 0; k < nv; k++) {
-      if (!mbar_wait_bounded(&vfull[slot], par, a.wait_ns)) ok = false;
-      const int2 st = srng[k];
-      char *vs = vring + slot * kStageBytes;
-      if (st.x <= pos && pos < st.x + st.y) {  // the current row (only thread d reads element d)
-        const int j = (int)(pos - st.x);
-        if (F16) ((__half *)(vs + j * A::ROW))[d] = __float2half_rn(vn_s[d]);
-        else ((float *)(vs + j * A::ROW))[d] = vn_s[d];
-      }
-      const float *w = E + (st.x - lo);
-      int j = 0;
-      if ((st.x & 3) == 0) {  // w 16-byte aligned: four weights per load
-        for (; j + 16 <= st.y; j += 16) {
-          float v[16];
-          float4 w4[4];
-#pragma unroll
-          for (int u = 0; u < 16; u++)
-            v[u] = F16 ? __half2float(((const __half *)(vs + (j + u) * A::ROW))[d])
-                       : ((const float *)(vs + (j + u) * A::ROW))[d];
-#pragma unroll
-          for (int u = 0; u < 4; u++) w4[u] = *(const float4 *)(w + j + 4 * u);
-          const float *ww = (const float *)w4;
-#pragma unroll
-          for (int u = 0; u < 16; u++) o = __fadd_rn(o, __fmul_rn(ww[u], v[u]));
-        }
-      }
-      for (; j < st.y; j++) {
-        const float v = F16 ? __half2float(((const __half *)(vs + j * A::ROW))[d]) : ((const float *)(vs + j * A::ROW))[d];
-        o = __fadd_rn(o, __fmul_rn(w[j], v));
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&vempty[slot]);
-      if (++slot == nsv) {
-        slot = 0;
-        par ^= 1u;
-      }
-    }
-  } else if (tid == HD + 32) {  // producer (own warp): refill a slot once every chain passed it
-    int slot = 0;
-    uint32_t par = 0;
-    for (int k = nsv; k < nv; k++) {
-      // a stage takes the chains ~0.5 us: poll gently so the chain warp on
-      // this SM sub-partition keeps its issue slots
-      if (!mbar_wait_sleepy(&vempty[slot], par, a.wait_ns)) ok = false;
-      fence_proxy_async();
-      const int2 st = srng[k];
-      mbar_expect_tx(&vfull[slot], (uint32_t)(st.y * A::ROW));
-      bulk_g2s(vring + slot * kStageBytes, vsrc[k], (uint32_t)(st.y * A::ROW), &vfull[slot]);
-      if (++slot == nsv) {
-        slot = 0;
-        par ^= 1u;
-      }
-    }
-  }
-  if (tid < HD) {
-    const int64_t e = (int64_t)(h * G + g) * HD + tid;
-    a.out[e] = o;
-    float v = isfinite(o) ? o : 0.0f;
-    const float amax = warp_max(fabsf(v));
-    const float scale = act_scale_from_amax(amax), is = act_inv_from_scale(scale);
-    a.out_q[e] = act_quant_one(v, is);
-    if (lane == 0) a.out_s[e / 32] = scale;
-  }
-  if (!ok) atomicOr(&bad_s, 1);
-  __syncthreads();
-  if (bad_s && tid == 0 && a.err) atomicOr(a.err, kErrCopyWait);
+  float *wg = a.w_out + (int64_t)(h * G + g) * a.w_stride + lo;  // this head's weights, by position
+  for (int64_t i = tid; i < span; i += kXT) wg[i] = __fmul_rn(E[i], inv);
 }
 
 template <int HD, bool F16>
@@ -409,25 +287,15 @@ const void *pick_x(int hd, int f16, int G) {
   return nullptr;
 }
 
-// Positions per stage: the largest power of two dividing the page size with
-// R * row <= 16 KB (and R <= 64: one thread per position in a round).
-int stage_rows(int hd, int f16, int64_t page_size) {
-  const int row = hd * (f16 ? 2 : 4);
+// Positions per K prefetch: the largest power of two <= 64 dividing the
+// page size.
+int stage_rows(int64_t page_size) {
   int R = 1;
-  while (R * 2 <= 64 && R * 2 * row <= kStageBytes && page_size % (R * 2) == 0) R *= 2;
+  while (R * 2 <= 64 && page_size % (R * 2) == 0) R *= 2;
   return R;
 }
 
-constexpr size_t kSmemCap = 225 * 1024;
-
-// Ring depth for V given what the rest of the layout needs (0 if < 3 fit).
-int v_stages(int per_cap, int n_ctx) {
-  const size_t rest = xattn_layout(0, per_cap, n_ctx).total + 8 * 1024;  // + static shared memory
-  if (rest >= kSmemCap) return 0;
-  int nsv = (int)((kSmemCap - rest) / kStageBytes);
-  if (nsv > kMaxNSV) nsv = kMaxNSV;
-  return nsv >= 3 ? nsv : 0;
-}
+constexpr size_t kSmemCap = 220 * 1024;
 
 }  // namespace
 
@@ -439,9 +307,8 @@ int xattn_cluster_size(int head_dim, int f16, int G, int n_kv, int64_t n_ctx) {
   int best = 0;
   for (int cs = 16; cs >= G && cs >= 1; cs /= 2) {
     const int per_cap = (int)((n_ctx + cs - 1) / cs);
-    const int nsv = v_stages(per_cap, (int)n_ctx);
-    if (!nsv) continue;
-    const size_t smem = xattn_layout(nsv, per_cap, (int)n_ctx).total;
+    const size_t smem = xattn_layout(per_cap, (int)n_ctx).total;
+    if (smem + 8 * 1024 > kSmemCap) continue;  // + static shared memory
     cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (cs > 8) cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaLaunchConfig_t cfg = {};
@@ -471,12 +338,12 @@ void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s)
   const void *fn = pick_x((int)a.kv.head_dim, a.kv.f16, G);
   const int cs = a.n_splits;
   if (!fn || cs < G) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: unsupported shape");
-  int per_cap = (int)((n_ctx + cs - 1) / cs), nc = (int)n_ctx;
-  int nsv = v_stages(per_cap, nc), R = stage_rows((int)a.kv.head_dim, a.kv.f16, a.kv.page_size);
-  if (!nsv) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: n_ctx %lld does not fit", (long long)n_ctx);
+  int per_cap = (int)((n_ctx + cs - 1) / cs), nc = (int)n_ctx, R = stage_rows(a.kv.page_size);
+  const size_t smem = xattn_layout(per_cap, nc).total;
+  if (smem + 8 * 1024 > kSmemCap)
+    fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: n_ctx %lld does not fit", (long long)n_ctx);
   if (R < 8) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: page size %lld not a multiple of 8",
                   (long long)a.kv.page_size);
-  const size_t smem = xattn_layout(nsv, per_cap, nc).total;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.kv.n_kv * cs));
   cfg.blockDim = dim3(kXT);
@@ -491,7 +358,7 @@ void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s)
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.pdl ? 2 : 1;
-  void *args[] = {(void *)&a, (void *)&per_cap, (void *)&nc, (void *)&R, (void *)&nsv};
+  void *args[] = {(void *)&a, (void *)&per_cap, (void *)&nc, (void *)&R};
   cudaLaunchKernelExC(&cfg, fn, args);
 }
 

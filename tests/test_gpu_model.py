@@ -130,13 +130,14 @@ def test_tiny_llama_greedy_64_matches_oracle_f32_kv(jal, oracle, torch_cuda):
     kvr = kvo.reshape(spec.num_layers, 2, 256, -1)[:, :, :n_pos, :].ravel()
     assert np.array_equal(kvg, kvr)
     # The serving path (FAST): the same bars, free-running, then the on-device
-    # greedy loop (argmax on device, one CUDA graph of 1 + 5L + 2 kernels per
-    # step) yields the same ids.
+    # greedy loop (argmax on device, one CUDA graph of 1 + 6L + 2 kernels per
+    # step: Q/K/V, attention scores, attention output, O, gate/up, down) yields
+    # the same ids.
     ctx_f = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST)
     tokens_f, _, worst_f = run_parity(om, ctx_f, prompt, N_DECODE, 256)
     print(f"tiny llama f32-KV fast numerics worst |dlogit| = {worst_f:.3e}")
     assert tokens_f == tokens
-    assert ctx_f.launches_per_step() == 1 + 5 * spec.num_layers + 2
+    assert ctx_f.launches_per_step() == 1 + 6 * spec.num_layers + 2
     ctx2 = new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_FAST)
     l0 = ctx2.prefill_step(prompt, 0)
     first = int(np.argmax(l0))
