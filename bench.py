@@ -422,7 +422,8 @@ def main():
             "config": {"workload": f"{args.workload} decode bs=1 greedy after a {n_prefill}-token prefill",
                        "layers": spec.num_layers, "hidden": spec.hidden_dim, "heads": [spec.n_heads_q, spec.n_heads_kv],
                        "head_dim": spec.head_dim, "ffn": spec.ffn_dim, "vocab": spec.vocab_size,
-                       "weights": "Q4_0 (4.5 bpw in HBM)", "kv_cache": "paged fp16", "parallelism": f"tp{world} ({ctx.tp_exchange()} exchange)" if tp else f"replicas x{world}",
+                       "weights": "Q4_0 (4.5 bpw in HBM)", "kv_cache": "paged fp16",
+                       "numerics": "reference f32 order (bit-exact with the oracle)" if not tp else "relaxed", "parallelism": f"tp{world} ({ctx.tp_exchange()} exchange)" if tp else f"replicas x{world}",
                        "l2": "no flush: each step streams the 4.2 GB of weights (> L2)",
                        "gguf_gen_s": round(gen_s, 1), "repack_s": round(build_s, 2)},
             "decode_step": {"bytes_per_token": bytes_token + kv_bytes,
@@ -440,7 +441,8 @@ def main():
         line["gemv_sweep"] = sweep
         dom = next(s for s in sweep if s["quant"] == "Q4_0" and s["M"] == 14336)
         traffic = committed_traffic().get("gemv_q4_0_14336x4096")
-        line["roofline"] = {"kernel": "k_gemv_w4<Q4_0,M=1> 14336x4096 (decode quant-GEMV)", "bound": "hbm",
+        line["roofline"] = {"kernel": "k_xgemv<Q4_0,store> 14336x4096 (reference-order decode quant-GEMV, int8 input)",
+                            "bound": "hbm",
                             "achieved": dom["GBps"], "peak": peak, "unit": "GB/s",
                             "frac": round(dom["GBps"] / peak, 4), "traffic": traffic,
                             "algorithmic_bytes": dom["bytes"], "peak_kind": peak_kind}

@@ -9,18 +9,20 @@
 // row i (recipe.rs:3024-3050).
 //
 // Structure: one CTA of 16 warps per SM owns a contiguous, balanced range of
-// output rows; warp w takes rows w, w + 16, ... of it, eight physical rows
-// (four gate / up pairs for SwiGLU) at a time.  A row is streamed in
-// segments of 128 blocks (4096 columns): lane l owns blocks 4l .. 4l + 3 of
-// the segment, loads their quants (64 bytes for Q4_0, 128 for Q8_0) and four
-// f16 scales with non-allocating vector loads, DEPTH units (row, segment)
-// ahead in registers, and writes its eight chunk terms, in chunk order, into
-// the warp's buffer row for that physical row.  When the eight rows' segment is in the buffer, lanes 0 .. 7
-// each add one row's terms in order onto that row's accumulator.  No CTA
-// barrier is involved after the prologue; the serial adds (256 per segment)
-// of one batch run while the next batch's loads are in flight.  Before
-// griddepcontrol.wait each CTA starts a bulk L2 prefetch of its rows, so
-// the weights stream from HBM while the activation prologue runs.
+// output rows, taken in chunks of up to 32 physical rows (gate / up rows
+// alternate for SwiGLU).  Warp 0 folds: lane r adds row r's terms in chunk
+// order, a 16-byte read of four terms at a time, so a row costs ~1.25
+// instructions per term whatever the number of rows.  Warps 1..15 produce
+// the terms: a unit is one row segment of 128 blocks (4096 columns); lane l
+// loads the quants (64 bytes for Q4_0, 128 for Q8_0) and four f16 scales of
+// blocks 4l .. 4l + 3 with non-allocating vector loads, DEPTH units ahead in
+// registers, and stores its eight chunk terms in place in the chunk's term
+// buffer ([rows][2 x columns / 32] floats); each unit arrives on its
+// segment's mbarrier, on which the fold warp waits.  Two term buffers
+// alternate when they fit, so producers fill chunk c + 1 while chunk c is
+// folded.  Before griddepcontrol.wait each CTA starts a bulk L2 prefetch of
+// its rows, so the weights stream from HBM while the activation prologue
+// runs.
 //
 // The activation prologue (optional RMSNorm, then QuantizedActQ8 per
 // 32-block) is computed by every CTA into shared memory after the wait, in a
@@ -40,9 +42,10 @@ namespace jal {
 namespace {
 
 constexpr int kNT = 512, kNW = kNT / 32;
-constexpr int kSeg = 128;   // blocks per segment (4096 columns)
-constexpr int kBR = 8;      // physical rows per warp batch (fold lanes)
-constexpr int kBP = 260;    // buffer row pitch (floats): 256 terms + 4 (conflict-free fold reads)
+constexpr int kSeg = 128;     // blocks per segment (4096 columns)
+constexpr int kProdW = kNW - 1;  // term-producing warps (warp 0 folds)
+constexpr int kMaxSeg = 8;    // columns <= 32768
+constexpr size_t kTermCap = 160 * 1024;  // term buffers + activation
 // L2 prefetch per CTA at launch: 148 CTAs x 512 KB stays well inside the
 // 126 MB L2 while covering whole projections up to ~75 MB.
 constexpr uint64_t kL2PrefetchBytes = 512 * 1024;
@@ -59,6 +62,7 @@ struct XCfg {
 // uses only after the prologue.
 struct XLayout {
   int nb, nseg, nbp;
+  int cr, nbuf, pitch;  // rows per chunk (fold lanes), term buffers, buffer row pitch (floats)
   size_t act_lo, act_hi, act_m, buf, xin, nw, xsq, sum, total;
 };
 
@@ -72,7 +76,13 @@ __host__ __device__ inline XLayout x_layout(int64_t cols, int in_mode) {
   L.act_hi = o; o += (size_t)L.nbp * 16;
   L.act_m = o; o += (size_t)L.nbp * 16;
   L.buf = o;
-  const size_t fold = (size_t)kNW * kBR * kBP * 4;
+  // A chunk's terms: [cr rows][2 nbp terms], pitch 2 nbp + 4 floats (an odd
+  // number of 16-byte units: the fold lanes' 16-byte reads do not conflict).
+  L.pitch = 2 * L.nbp + 4;
+  L.cr = 32;
+  while (L.cr > 8 && (size_t)L.cr * L.pitch * 4 + o > kTermCap) L.cr /= 2;
+  L.nbuf = 2 * (size_t)L.cr * L.pitch * 4 + o <= kTermCap ? 2 : 1;
+  const size_t fold = (size_t)L.nbuf * L.cr * L.pitch * 4;
   const size_t row = ((size_t)L.nb * 32 * 4 + 15) / 16 * 16;
   size_t p = o;
   L.xin = p; if (in_mode != GEMV_IN_Q8) p += row;
@@ -284,40 +294,26 @@ template <int QUANT, int OUT>
 __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
   constexpr int DEPTH = XCfg<QUANT>::DEPTH;
   constexpr int PAIR = OUT == GEMV_OUT_SWIGLU ? 2 : 1;  // physical rows per logical row
-  constexpr int LPB = kBR / PAIR;                       // logical rows per batch
   extern __shared__ __align__(16) char smem[];
+  __shared__ __align__(8) uint64_t seg_full[2][kMaxSeg], buf_empty[2];
   const XLayout L = x_layout(a.w.cols, a.in_mode);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t base = a.rows / gridDim.x, rem = a.rows % gridDim.x;
   const int64_t r0 = (int64_t)blockIdx.x * base + ((int64_t)blockIdx.x < rem ? blockIdx.x : rem);
   const int cnt = (int)(base + ((int64_t)blockIdx.x < rem ? 1 : 0));
-  // This warp's logical rows: r0 + warp + 16 i, i < nl.
-  const int nl = cnt > warp ? (cnt - 1 - warp) / kNW + 1 : 0;
-  const int nbatch = (nl + LPB - 1) / LPB;
-  const int nseg = L.nseg;
-  float *buf = (float *)(smem + L.buf) + (size_t)warp * kBR * kBP;
-  // Units of the warp in order: batch by batch; within a batch segment-major
-  // over its physical rows (gate, up, gate, up, ... for SwiGLU).  A cursor
-  // walks them without divisions.
-  auto batch_rows = [&](int b) { return (nl - b * LPB < LPB ? nl - b * LPB : LPB) * PAIR; };
-  struct Cursor {
-    int b, sg, p, np;
-  };
-  auto advance = [&](Cursor &c) {
-    if (++c.p == c.np) {
-      c.p = 0;
-      if (++c.sg == nseg) {
-        c.sg = 0;
-        c.np = batch_rows(++c.b);
-      }
-    }
-  };
-  const int total = nbatch ? (nbatch - 1) * kBR * nseg + batch_rows(nbatch - 1) * nseg : 0;
-  auto prow = [&](int b, int p) -> int64_t {
-    const int64_t lr = r0 + warp + (int64_t)(b * LPB + p / PAIR) * kNW;
+  const int nseg = L.nseg, cr = L.cr, nbuf = L.nbuf, pitch = L.pitch;
+  const int nphys = cnt * PAIR, nchunk = (nphys + cr - 1) / cr;
+  auto prow = [&](int p) -> int64_t {  // physical row p of this CTA: gate / up alternate for SwiGLU
+    const int64_t lr = r0 + p / PAIR;
     return (PAIR == 2 && (p & 1)) ? a.up_offset + lr : lr;
   };
-
+  if (tid == 0) {
+    for (int b = 0; b < 2; b++) {
+      for (int sg = 0; sg < kMaxSeg; sg++) mbar_init(&seg_full[b][sg], cr);  // one arrival per row of the chunk
+      mbar_init(&buf_empty[b], 1);
+    }
+    fence_barrier_init();
+  }
   // This CTA's rows are one contiguous run of row records (two for SwiGLU):
   // start streaming them into L2 before waiting on the previous kernel, so
   // HBM works while the activation prologue runs.
@@ -329,66 +325,111 @@ __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
   }
   pdl_wait();
   pdl_trigger();
-  x_prologue(a, L, smem, (exact::SumSmem<kNT> *)(smem + L.sum));
-  XUnit<QUANT> ring[DEPTH];
-  Cursor cur = {0, 0, 0, nbatch ? batch_rows(0) : 0}, ahead = cur;
-#pragma unroll
-  for (int j = 0; j < DEPTH; j++)
-    if (j < total) {
-      x_load<QUANT>(a.w, prow(ahead.b, ahead.p), ahead.sg, L.nb, lane, ring[j]);
-      advance(ahead);
-    }
+  x_prologue(a, L, smem, (exact::SumSmem<kNT> *)(smem + L.sum));  // ends with a CTA barrier
   const int4 *alo = (const int4 *)(smem + L.act_lo), *ahi = (const int4 *)(smem + L.act_hi);
   const float4 *am = (const float4 *)(smem + L.act_m);
+  float *terms = (float *)(smem + L.buf);  // [nbuf][cr][pitch]
 
-  float acc = 0.0f;  // lane p < kBR: physical row p of the current batch
-  for (int k0 = 0; k0 < total; k0 += DEPTH) {
+  if (warp == 0) {
+    // Fold warp: lane = physical row of the chunk; each row's terms are
+    // added in chunk order, segment by segment as the producers finish them.
+    for (int c = 0; c < nchunk; c++) {
+      const int b = c % nbuf;
+      const uint32_t par = (uint32_t)((c / nbuf) & 1);
+      const int p = c * cr + lane;
+      const bool valid = lane < cr && p < nphys;
+      const float *src = terms + ((size_t)b * cr + (lane < cr ? lane : 0)) * pitch;
+      float acc = 0.0f;
+      for (int sg = 0; sg < nseg; sg++) {
+        mbar_wait_bounded(&seg_full[b][sg], par);
+        const int blk = L.nb - sg * kSeg < kSeg ? L.nb - sg * kSeg : kSeg;
+        const float *t = src + sg * 2 * kSeg;
+        if (valid) {
+          int i = 0;
+          for (; i + 16 <= 2 * blk; i += 16) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) v[u] = *(const float4 *)(t + i + 4 * u);
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+              acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v[u].x), v[u].y), v[u].z), v[u].w);
+          }
+          for (; i < 2 * blk; i++) acc = __fadd_rn(acc, t[i]);
+        }
+      }
+      const float other = __shfl_down_sync(0xffffffffu, acc, 1);
+      if (valid && (PAIR == 1 || (lane & 1) == 0)) {
+        const int64_t lr = r0 + p / PAIR;
+        float *yp = a.y + lr;
+        if (OUT == GEMV_OUT_STORE) {
+          *yp = a.bias ? __fadd_rn(acc, a.bias[lr]) : acc;
+        } else if (OUT == GEMV_OUT_ADD) {
+          const float pv = a.bias ? __fadd_rn(acc, a.bias[lr]) : acc;
+          *yp = __fadd_rn(*yp, pv);
+        } else {
+          *yp = exact::swiglu_ref(acc, other);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&buf_empty[b]);
+    }
+    return;
+  }
+
+  // Producer warps: units (chunk, segment, row) in that order, unit g of
+  // the CTA to warp g % kProdW.  A unit is one row segment: lane l computes
+  // the eight chunk terms of blocks 4l .. 4l + 3 and stores them in place;
+  // the unit's warp then arrives on the segment's barrier (rows past the
+  // CTA's end arrive without work, so every barrier counts cr arrivals).
+  const int pw = warp - 1, upc = nseg * cr;
+  const int crs = 31 - __clz(cr);  // cr is a power of two
+  struct Cursor {
+    int c, u;  // chunk, unit in the chunk (segment-major)
+  };
+  auto advance = [&](Cursor &q) {
+    q.u += kProdW;
+    while (q.u >= upc) {
+      q.u -= upc;
+      q.c++;
+    }
+  };
+  XUnit<QUANT> ring[DEPTH];
+  Cursor cur = {0, pw}, ahead = cur;
+  while (ahead.u >= upc && upc > 0) {
+    ahead.u -= upc;
+    ahead.c++;
+  }
+  cur = ahead;
+#pragma unroll
+  for (int j = 0; j < DEPTH; j++) {
+    const int p = ahead.c * cr + (ahead.u & (cr - 1));
+    if (ahead.c < nchunk && p < nphys) x_load<QUANT>(a.w, prow(p), ahead.u >> crs, L.nb, lane, ring[j]);
+    advance(ahead);
+  }
+  int waited = -1;  // last chunk whose buffer this warp has waited for
+
+  for (int k0 = 0; cur.c < nchunk; k0 += DEPTH) {
 #pragma unroll
     for (int j = 0; j < DEPTH; j++) {
-      const int k = k0 + j;
-      if (k < total) {
-        const int b = cur.b, sg = cur.sg, p = cur.p, np = cur.np;
+      if (cur.c < nchunk) {
+        const int c = cur.c, sg = cur.u >> crs, rr = cur.u & (cr - 1), p = c * cr + rr, b = c % nbuf;
         advance(cur);
-        float t[8];
-        x_terms<QUANT>(ring[j], alo, ahi, am, sg, lane, t);
-        if (k + DEPTH < total) {
-          x_load<QUANT>(a.w, prow(ahead.b, ahead.p), ahead.sg, L.nb, lane, ring[j]);
-          advance(ahead);
+        if (c >= nbuf && c != waited) {  // the fold warp has released this buffer
+          mbar_wait_bounded(&buf_empty[b], (uint32_t)(((c / nbuf) - 1) & 1));
+          waited = c;
         }
-        float *dst = buf + p * kBP + 8 * lane;
-        *(float4 *)dst = make_float4(t[0], t[1], t[2], t[3]);
-        *(float4 *)(dst + 4) = make_float4(t[4], t[5], t[6], t[7]);
-        if (p == np - 1) {  // the batch's segment is complete: fold it
-          __syncwarp();
-          const int blk = L.nb - sg * kSeg < kSeg ? L.nb - sg * kSeg : kSeg;
-          const int nt = 2 * blk;
-          if (lane < np) {
-            const float *src = buf + lane * kBP;
-            int i = 0;
-            for (; i + 4 <= nt; i += 4) {
-              const float4 v = *(const float4 *)(src + i);
-              acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
-            }
-            for (; i < nt; i++) acc = __fadd_rn(acc, src[i]);
-          }
-          __syncwarp();
-          if (sg == nseg - 1) {  // rows of the batch are done
-            const float other = __shfl_down_sync(0xffffffffu, acc, 1);
-            if (lane < np && (PAIR == 1 || (lane & 1) == 0)) {
-              const int64_t lr = r0 + warp + (int64_t)(b * LPB + lane / PAIR) * kNW;
-              float *yp = a.y + lr;
-              if (OUT == GEMV_OUT_STORE) {
-                *yp = a.bias ? __fadd_rn(acc, a.bias[lr]) : acc;
-              } else if (OUT == GEMV_OUT_ADD) {
-                const float pv = a.bias ? __fadd_rn(acc, a.bias[lr]) : acc;
-                *yp = __fadd_rn(*yp, pv);
-              } else {
-                *yp = exact::swiglu_ref(acc, other);
-              }
-            }
-            acc = 0.0f;
-          }
+        if (p < nphys) {
+          float t[8];
+          x_terms<QUANT>(ring[j], alo, ahi, am, sg, lane, t);
+          float *dst = terms + ((size_t)b * cr + rr) * pitch + sg * 2 * kSeg + 8 * lane;
+          *(float4 *)dst = make_float4(t[0], t[1], t[2], t[3]);
+          *(float4 *)(dst + 4) = make_float4(t[4], t[5], t[6], t[7]);
         }
+        const int pa = ahead.c * cr + (ahead.u & (cr - 1));
+        if (ahead.c < nchunk && pa < nphys) x_load<QUANT>(a.w, prow(pa), ahead.u >> crs, L.nb, lane, ring[j]);
+        advance(ahead);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&seg_full[b][sg]);
       }
     }
   }
@@ -412,9 +453,9 @@ void launch_x(const GemvArgs &a, int grid, cudaStream_t s) {
 
 template <int QUANT>
 void set_x_attrs() {
-  cudaFuncSetAttribute(k_xgemv<QUANT, GEMV_OUT_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  cudaFuncSetAttribute(k_xgemv<QUANT, GEMV_OUT_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  cudaFuncSetAttribute(k_xgemv<QUANT, GEMV_OUT_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaFuncSetAttribute(k_xgemv<QUANT, GEMV_OUT_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(k_xgemv<QUANT, GEMV_OUT_ADD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+  cudaFuncSetAttribute(k_xgemv<QUANT, GEMV_OUT_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
 }
 
 }  // namespace
@@ -426,11 +467,12 @@ size_t xgemv_smem_bytes(int quant, int64_t cols, int in_mode) {
 
 bool xgemv_supported(const GemvArgs &a) {
   if (a.m != 1 || (a.w.quant != JAL_Q4_0 && a.w.quant != JAL_Q8_0)) return false;
+  if (x_layout(a.w.cols, a.in_mode).nseg > kMaxSeg) return false;
   if (a.w.cols % 32 != 0 || a.w.qs_stride % 16 != 0 || (reinterpret_cast<uintptr_t>(a.w.qs) & 15) != 0) return false;
   if (a.w.d_stride % 4 != 0) return false;  // 8-byte scale loads
   if (a.out_mode != GEMV_OUT_STORE && a.out_mode != GEMV_OUT_ADD && a.out_mode != GEMV_OUT_SWIGLU) return false;
   if (a.peer_in || a.in_mode == GEMV_IN_PREQ) return false;
-  return xgemv_smem_bytes(a.w.quant, a.w.cols, a.in_mode) <= 227 * 1024;
+  return xgemv_smem_bytes(a.w.quant, a.w.cols, a.in_mode) <= 220 * 1024;
 }
 
 void xgemv_init() {
