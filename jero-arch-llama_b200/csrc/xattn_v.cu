@@ -159,15 +159,30 @@ __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUte
         if (!mbar_wait_bounded(&pfull[ps], pp, a.wait_ns)) ok = false;
         const int n = srow[k].z;
         const float *pr = prod + (size_t)ps * kMaxR * 32 + lane;
-        int r = 0;
-        for (; r + 16 <= n; r += 16) {
-          float x[16];
+        if (n == kMaxR) {  // a full stage: block b + 1's loads go out before block b's adds
+          float x[2][16];
 #pragma unroll
-          for (int u = 0; u < 16; u++) x[u] = pr[(r + u) * 32];
+          for (int u = 0; u < 16; u++) x[0][u] = pr[u * 32];
 #pragma unroll
-          for (int u = 0; u < 16; u++) o = __fadd_rn(o, x[u]);
+          for (int b = 0; b < kMaxR / 16; b++) {
+            if (b + 1 < kMaxR / 16) {
+#pragma unroll
+              for (int u = 0; u < 16; u++) x[(b + 1) & 1][u] = pr[((b + 1) * 16 + u) * 32];
+            }
+#pragma unroll
+            for (int u = 0; u < 16; u++) o = __fadd_rn(o, x[b & 1][u]);
+          }
+        } else {
+          int r = 0;
+          for (; r + 16 <= n; r += 16) {
+            float x[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) x[u] = pr[(r + u) * 32];
+#pragma unroll
+            for (int u = 0; u < 16; u++) o = __fadd_rn(o, x[u]);
+          }
+          for (; r < n; r++) o = __fadd_rn(o, pr[r * 32]);
         }
-        for (; r < n; r++) o = __fadd_rn(o, pr[r * 32]);
         __syncwarp();
         if (lane == 0) mbar_arrive(&pempty[ps]);
         if (++ps == kPS) {
@@ -192,29 +207,43 @@ __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUte
         const int4 st = srow[k];
         const char *vsrc = vring + vs * A::STAGE;
         float *dst = prod + (size_t)ps * kMaxR * 32;
-        for (int g = p; g * A::RPG < st.z; g += kProd) {
-          const int r = g * A::RPG + rr;
-          if (r < st.z) {
-            const uint4 raw = *(const uint4 *)(vsrc + r * A::SROW + 16 * q);
-            const float wv = w_s[st.y - lo + r];
-            float pv[A::CH];
-            if (F16) {
-              const __half2 *hh = (const __half2 *)&raw;
+        const float *wst = w_s + (st.y - lo);
+        auto make = [&](int r, uint4 raw, float wv) {  // products of position r, dims CH q .. CH q + CH - 1
+          float pv[A::CH];
+          if (F16) {
+            const __half2 *hh = (const __half2 *)&raw;
 #pragma unroll
-              for (int j = 0; j < A::CH / 2; j++) {
-                const float2 f = __half22float2(hh[j]);
-                pv[2 * j] = __fmul_rn(wv, f.x);
-                pv[2 * j + 1] = __fmul_rn(wv, f.y);
-              }
-            } else {
-              pv[0] = __fmul_rn(wv, __uint_as_float(raw.x));
-              pv[1] = __fmul_rn(wv, __uint_as_float(raw.y));
-              pv[2] = __fmul_rn(wv, __uint_as_float(raw.z));
-              pv[3] = __fmul_rn(wv, __uint_as_float(raw.w));
+            for (int j = 0; j < A::CH / 2; j++) {
+              const float2 f = __half22float2(hh[j]);
+              pv[2 * j] = __fmul_rn(wv, f.x);
+              pv[2 * j + 1] = __fmul_rn(wv, f.y);
             }
+          } else {
+            pv[0] = __fmul_rn(wv, __uint_as_float(raw.x));
+            pv[1] = __fmul_rn(wv, __uint_as_float(raw.y));
+            pv[2] = __fmul_rn(wv, __uint_as_float(raw.z));
+            pv[3] = __fmul_rn(wv, __uint_as_float(raw.w));
+          }
 #pragma unroll
-            for (int j = 0; j < A::CH; j += 4)
-              *(float4 *)(dst + r * 32 + A::CH * q + j) = make_float4(pv[j], pv[j + 1], pv[j + 2], pv[j + 3]);
+          for (int j = 0; j < A::CH; j += 4)
+            *(float4 *)(dst + r * 32 + A::CH * q + j) = make_float4(pv[j], pv[j + 1], pv[j + 2], pv[j + 3]);
+        };
+        if (st.z == kMaxR) {  // a full stage: all of this warp's loads first, then the products
+          constexpr int GPP = kMaxR / A::RPG / kProd;  // position groups per producer warp
+          uint4 raw[GPP];
+          float wv[GPP];
+#pragma unroll
+          for (int i = 0; i < GPP; i++) {
+            const int r = (p + kProd * i) * A::RPG + rr;
+            raw[i] = *(const uint4 *)(vsrc + r * A::SROW + 16 * q);
+            wv[i] = wst[r];
+          }
+#pragma unroll
+          for (int i = 0; i < GPP; i++) make((p + kProd * i) * A::RPG + rr, raw[i], wv[i]);
+        } else {
+          for (int g = p; g * A::RPG < st.z; g += kProd) {
+            const int r = g * A::RPG + rr;
+            if (r < st.z) make(r, *(const uint4 *)(vsrc + r * A::SROW + 16 * q), wst[r]);
           }
         }
         __syncwarp();
