@@ -13,11 +13,12 @@
 // alternate for SwiGLU).  Warp 0 folds: lane r adds row r's terms in chunk
 // order, a 16-byte read of four terms at a time, so a row costs ~1.25
 // instructions per term whatever the number of rows.  Warps 1..15 produce
-// the terms: a unit is one row segment of 128 blocks (4096 columns); lane l
-// loads the quants (64 bytes for Q4_0, 128 for Q8_0) and four f16 scales of
-// blocks 4l .. 4l + 3 with non-allocating vector loads, DEPTH units ahead in
-// registers, and stores its eight chunk terms in place in the chunk's term
-// buffer ([rows][2 x columns / 32] floats); each unit arrives on its
+// the terms: a unit is one row segment of 128 blocks (4096 columns), read
+// with non-allocating 16-byte loads that cover 512 consecutive bytes per warp
+// instruction (Q4_0: lane l takes blocks 32v + l, two terms each; Q8_0: lane
+// l takes the 16-element chunks 32j + l, one term each), DEPTH units ahead in
+// registers; the lane stores its eight chunk terms in place in the chunk's
+// term buffer ([rows][2 x columns / 32] floats); each unit arrives on its
 // segment's mbarrier, on which the fold warp waits.  Two term buffers
 // alternate when they fit, so producers fill chunk c + 1 while chunk c is
 // folded.  Before griddepcontrol.wait each CTA starts a bulk L2 prefetch of
@@ -25,10 +26,11 @@
 // runs.
 //
 // The activation prologue (optional RMSNorm, then QuantizedActQ8 per
-// 32-block) is computed by every CTA into shared memory after the wait, in a
-// lane-interleaved layout (block 4l + v of a segment at slot 32v + l) so the
-// main loop's reads are conflict-free; the RMSNorm sum of squares is the
-// reference's sequential sum, computed with exact::seq_sum_nonneg.
+// 32-block) is computed by every CTA into shared memory after the wait: the
+// 16 quants of each block half in two arrays indexed by block (the second
+// shifted by 64 bytes, so Q8_0's alternating lo / hi reads use all 32
+// banks); the RMSNorm sum of squares is the reference's sequential sum,
+// computed with exact::seq_sum_nonneg.
 #include <cuda_fp16.h>
 
 #include "common.hpp"
@@ -72,7 +74,7 @@ __host__ __device__ inline XLayout x_layout(int64_t cols, int in_mode) {
   L.nseg = (L.nb + kSeg - 1) / kSeg;
   L.nbp = L.nseg * kSeg;
   size_t o = 0;
-  L.act_lo = o; o += (size_t)L.nbp * 16;
+  L.act_lo = o; o += (size_t)L.nbp * 16 + 64;
   L.act_hi = o; o += (size_t)L.nbp * 16;
   L.act_m = o; o += (size_t)L.nbp * 16;
   L.buf = o;
@@ -93,12 +95,6 @@ __host__ __device__ inline XLayout x_layout(int64_t cols, int in_mode) {
   return L;
 }
 
-// Slot of block b in the lane-interleaved activation layout.
-__device__ __forceinline__ int act_slot(int b) {
-  const int s = b / kSeg, i = b % kSeg;
-  return s * kSeg + (i & 3) * 32 + (i >> 2);
-}
-
 // Activation prologue: QuantizedActQ8 of the (optionally RMSNorm'd) input,
 // one warp per 32-block, lane = element.  Per block slot: quants 0..15 in
 // act_lo, 16..31 in act_hi, {scale, sum of quants 0..15, sum of 16..31, 0}
@@ -110,7 +106,7 @@ __device__ void x_prologue(const GemvArgs &a, const XLayout &L, char *smem, SumS
   float4 *am = (float4 *)(smem + L.act_m);
   const int K = L.nb * 32;
   for (int b = L.nb + tid; b < L.nbp; b += kNT) {  // padding blocks
-    const int sl = act_slot(b);
+    const int sl = b;
     ((uint4 *)alo)[sl] = make_uint4(0u, 0u, 0u, 0u);
     ((uint4 *)ahi)[sl] = make_uint4(0u, 0u, 0u, 0u);
     am[sl] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -126,7 +122,7 @@ __device__ void x_prologue(const GemvArgs &a, const XLayout &L, char *smem, SumS
     s += __shfl_xor_sync(0xffffffffu, s, 1);  // sub 0, 1: elements 0..15; sub 2, 3: 16..31
     const int s_hi = __shfl_down_sync(0xffffffffu, s, 2);
     if (valid) {
-      const int sl = act_slot(b);
+      const int sl = b;
       const uint32_t p0 = (uint32_t)(q[0] & 0xff) | ((uint32_t)(q[1] & 0xff) << 8) | ((uint32_t)(q[2] & 0xff) << 16) |
                           ((uint32_t)(q[3] & 0xff) << 24);
       const uint32_t p1 = (uint32_t)(q[4] & 0xff) | ((uint32_t)(q[5] & 0xff) << 8) | ((uint32_t)(q[6] & 0xff) << 16) |
@@ -230,63 +226,77 @@ __device__ void x_prologue(const GemvArgs &a, const XLayout &L, char *smem, SumS
 // difference.  Chunk dots stay below 16 * 128 * 127 < 2^22.
 __device__ __forceinline__ float exact_i2f(int d) { return __fsub_rn(__int_as_float(0x4B400000 + d), 12582912.0f); }
 
-// Quants and scales of one lane for one (row, segment) unit.
+// Quants and scales of one lane for one (row, segment) unit: four blocks
+// (Q4_0) or eight 16-element chunks (Q8_0), and their blocks' f16 scales.
 template <int QUANT>
 struct XUnit {
   uint4 q[XCfg<QUANT>::NQ4];
-  uint2 d;
+  uint16_t d[XCfg<QUANT>::NQ4];
 };
 
 template <int QUANT>
 __device__ __forceinline__ void x_load(const DevMat &w, int64_t row, int seg, int nb, int lane, XUnit<QUANT> &u) {
-  constexpr int NQ4 = XCfg<QUANT>::NQ4, BQ4 = NQ4 / 4;  // 16-byte pieces per block
-  const int b0 = seg * kSeg + 4 * lane;
-  const uint8_t *qp = w.qs + row * w.qs_stride + (int64_t)b0 * BQ4 * 16;
+  const uint8_t *qp = w.qs + row * w.qs_stride;
+  const uint16_t *dp = w.d + row * w.d_stride;
+  if (QUANT == JAL_Q4_0) {
 #pragma unroll
-  for (int j = 0; j < NQ4; j++)
-    u.q[j] = (b0 + j / BQ4 < nb) ? ldg_stream16(qp + 16 * j) : make_uint4(0u, 0u, 0u, 0u);
-  u.d = b0 < nb ? ldg_stream8(w.d + row * w.d_stride + b0) : make_uint2(0u, 0u);
+    for (int v = 0; v < 4; v++) {
+      const int b = seg * kSeg + 32 * v + lane;
+      u.q[v] = b < nb ? ldg_stream16(qp + (int64_t)b * 16) : make_uint4(0u, 0u, 0u, 0u);
+      u.d[v] = b < nb ? ldg_stream2(dp + b) : (uint16_t)0;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int t = 32 * j + lane, b = seg * kSeg + (t >> 1);
+      u.q[j] = b < nb ? ldg_stream16(qp + (int64_t)seg * kSeg * 32 + 16 * t) : make_uint4(0u, 0u, 0u, 0u);
+      u.d[j] = b < nb ? ldg_stream2(dp + b) : (uint16_t)0;
+    }
+  }
 }
 
-// The lane's eight chunk terms of a unit, in chunk order.
+// The lane's chunk terms of a unit, stored at their chunk positions of the
+// row's term array (dst = the segment's first term).  Blocks past the row's
+// end carry zero quants and scales and store zero terms, which the fold
+// does not read.
 template <int QUANT>
 __device__ __forceinline__ void x_terms(const XUnit<QUANT> &u, const int4 *alo, const int4 *ahi, const float4 *am,
-                                        int seg, int lane, float (&t)[8]) {
-  constexpr int BQ4 = XCfg<QUANT>::NQ4 / 4;
-  const __half2 d01 = *reinterpret_cast<const __half2 *>(&u.d.x);
-  const __half2 d23 = *reinterpret_cast<const __half2 *>(&u.d.y);
-  const float ws[4] = {__low2float(d01), __high2float(d01), __low2float(d23), __high2float(d23)};
+                                        int seg, int lane, float *dst) {
+  if (QUANT == JAL_Q4_0) {
 #pragma unroll
-  for (int v = 0; v < 4; v++) {
-    const int sl = seg * kSeg + v * 32 + lane;
-    const int4 xl = alo[sl], xh = ahi[sl];
-    const float4 m = am[sl];
-    int d0, d1;
-    if (QUANT == JAL_Q4_0) {
+    for (int v = 0; v < 4; v++) {
+      const int bi = 32 * v + lane, b = seg * kSeg + bi;
+      const int4 xl = alo[b], xh = ahi[b];
+      const float4 m = am[b];
       const uint4 q = u.q[v];
-      d0 = dp4a_us(q.x & 0x0F0F0F0Fu, xl.x, 0);
+      int d0 = dp4a_us(q.x & 0x0F0F0F0Fu, xl.x, 0);
       d0 = dp4a_us(q.y & 0x0F0F0F0Fu, xl.y, d0);
       d0 = dp4a_us(q.z & 0x0F0F0F0Fu, xl.z, d0);
       d0 = dp4a_us(q.w & 0x0F0F0F0Fu, xl.w, d0);
-      d1 = dp4a_us(q.x & 0xF0F0F0F0u, xh.x, 0);
+      int d1 = dp4a_us(q.x & 0xF0F0F0F0u, xh.x, 0);
       d1 = dp4a_us(q.y & 0xF0F0F0F0u, xh.y, d1);
       d1 = dp4a_us(q.z & 0xF0F0F0F0u, xh.z, d1);
       d1 = dp4a_us(q.w & 0xF0F0F0F0u, xh.w, d1);
       d0 -= 8 * __float_as_int(m.y);             // nibble n encodes n - 8
       d1 = (d1 >> 4) - 8 * __float_as_int(m.z);  // high nibbles were multiplied by 16 in place
-    } else {
-      const uint4 q0 = u.q[BQ4 * v], q1 = u.q[BQ4 * v + 1];
-      d0 = dp4a_ss((int)q0.x, xl.x, 0);
-      d0 = dp4a_ss((int)q0.y, xl.y, d0);
-      d0 = dp4a_ss((int)q0.z, xl.z, d0);
-      d0 = dp4a_ss((int)q0.w, xl.w, d0);
-      d1 = dp4a_ss((int)q1.x, xh.x, 0);
-      d1 = dp4a_ss((int)q1.y, xh.y, d1);
-      d1 = dp4a_ss((int)q1.z, xh.z, d1);
-      d1 = dp4a_ss((int)q1.w, xh.w, d1);
+      const float ws = __half2float(__ushort_as_half(u.d[v]));
+      *(float2 *)(dst + 2 * bi) = make_float2(__fmul_rn(__fmul_rn(exact_i2f(d0), m.x), ws),
+                                              __fmul_rn(__fmul_rn(exact_i2f(d1), m.x), ws));
     }
-    t[2 * v] = __fmul_rn(__fmul_rn(exact_i2f(d0), m.x), ws[v]);
-    t[2 * v + 1] = __fmul_rn(__fmul_rn(exact_i2f(d1), m.x), ws[v]);
+  } else {
+    const int4 *half = (lane & 1) ? ahi : alo;  // odd chunks are their blocks' second halves
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int t = 32 * j + lane, b = seg * kSeg + (t >> 1);
+      const int4 x = half[b];
+      const float4 m = am[b];
+      const uint4 q = u.q[j];
+      int d = dp4a_ss((int)q.x, x.x, 0);
+      d = dp4a_ss((int)q.y, x.y, d);
+      d = dp4a_ss((int)q.z, x.z, d);
+      d = dp4a_ss((int)q.w, x.w, d);
+      dst[t] = __fmul_rn(__fmul_rn(exact_i2f(d), m.x), __half2float(__ushort_as_half(u.d[j])));
+    }
   }
 }
 
@@ -377,9 +387,9 @@ __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
   }
 
   // Producer warps: units (chunk, segment, row) in that order, unit g of
-  // the CTA to warp g % kProdW.  A unit is one row segment: lane l computes
-  // the eight chunk terms of blocks 4l .. 4l + 3 and stores them in place;
-  // the unit's warp then arrives on the segment's barrier (rows past the
+  // the CTA to warp g % kProdW.  A unit is one row segment: each lane
+  // computes eight of its chunk terms and stores them in place; the unit's
+  // warp then arrives on the segment's barrier (rows past the
   // CTA's end arrive without work, so every barrier counts cr arrivals).
   const int pw = warp - 1, upc = nseg * cr;
   const int crs = 31 - __clz(cr);  // cr is a power of two
@@ -418,13 +428,7 @@ __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
           mbar_wait_bounded(&buf_empty[b], (uint32_t)(((c / nbuf) - 1) & 1));
           waited = c;
         }
-        if (p < nphys) {
-          float t[8];
-          x_terms<QUANT>(ring[j], alo, ahi, am, sg, lane, t);
-          float *dst = terms + ((size_t)b * cr + rr) * pitch + sg * 2 * kSeg + 8 * lane;
-          *(float4 *)dst = make_float4(t[0], t[1], t[2], t[3]);
-          *(float4 *)(dst + 4) = make_float4(t[4], t[5], t[6], t[7]);
-        }
+        if (p < nphys) x_terms<QUANT>(ring[j], alo, ahi, am, sg, lane, terms + ((size_t)b * cr + rr) * pitch + sg * 2 * kSeg);
         const int pa = ahead.c * cr + (ahead.u & (cr - 1));
         if (ahead.c < nchunk && pa < nphys) x_load<QUANT>(a.w, prow(pa), ahead.u >> crs, L.nb, lane, ring[j]);
         advance(ahead);
@@ -469,7 +473,6 @@ bool xgemv_supported(const GemvArgs &a) {
   if (a.m != 1 || (a.w.quant != JAL_Q4_0 && a.w.quant != JAL_Q8_0)) return false;
   if (x_layout(a.w.cols, a.in_mode).nseg > kMaxSeg) return false;
   if (a.w.cols % 32 != 0 || a.w.qs_stride % 16 != 0 || (reinterpret_cast<uintptr_t>(a.w.qs) & 15) != 0) return false;
-  if (a.w.d_stride % 4 != 0) return false;  // 8-byte scale loads
   if (a.out_mode != GEMV_OUT_STORE && a.out_mode != GEMV_OUT_ADD && a.out_mode != GEMV_OUT_SWIGLU) return false;
   if (a.peer_in || a.in_mode == GEMV_IN_PREQ) return false;
   return xgemv_smem_bytes(a.w.quant, a.w.cols, a.in_mode) <= 220 * 1024;
