@@ -324,7 +324,8 @@ def main():
     ap.add_argument("--prefill", type=int, default=2048)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="llama3-8b-q4_0", choices=["llama3-8b-q4_0", "tiny"])
+    ap.add_argument("--workload", default="llama3-8b-q4_0",
+                    choices=["llama3-8b-q4_0", "qwen2-7b-q8_0", "llama3-70b-q4_0", "tiny"])
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1 ranks: one tensor-parallel model over the N GPUs (strong scaling) "
                          "instead of N independent replicas")
@@ -351,7 +352,9 @@ def main():
                                 device_id=torch.device("cuda", local))
     jal = load_jal()
     jal.set_device(local)
-    spec = jal.LLAMA3_8B_Q4_0 if args.workload == "llama3-8b-q4_0" else jal.TINY_LLAMA
+    spec = {"llama3-8b-q4_0": jal.LLAMA3_8B_Q4_0, "qwen2-7b-q8_0": jal.QWEN2_7B_Q8_0,
+            "llama3-70b-q4_0": jal.LLAMA3_70B_Q4_0}.get(args.workload, jal.TINY_LLAMA)
+    wq = "Q8_0" if spec.weight_quant == jal.Q8_0 else "Q4_0"
     peak, peak_kind = measured_peaks()
 
     t0 = time.perf_counter()
@@ -418,13 +421,13 @@ def main():
     line = {"metric": METRIC, "value": round(streams * args.steps / t_dec, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 4),
             "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic: seeded N(0,0.02) weights quantized to Q4_0, uniform-random token ids",
+            "data": f"synthetic: seeded N(0,0.02) weights quantized to {wq}, uniform-random token ids",
             "config": {"workload": f"{args.workload} decode bs=1 greedy after a {n_prefill}-token prefill",
                        "layers": spec.num_layers, "hidden": spec.hidden_dim, "heads": [spec.n_heads_q, spec.n_heads_kv],
                        "head_dim": spec.head_dim, "ffn": spec.ffn_dim, "vocab": spec.vocab_size,
-                       "weights": "Q4_0 (4.5 bpw in HBM)", "kv_cache": "paged fp16",
+                       "weights": f"{wq} ({'8.5' if wq == 'Q8_0' else '4.5'} bpw in HBM)", "kv_cache": "paged fp16",
                        "numerics": "reference f32 order (bit-exact with the oracle)" if not tp else "relaxed", "parallelism": f"tp{world} ({ctx.tp_exchange()} exchange)" if tp else f"replicas x{world}",
-                       "l2": "no flush: each step streams the 4.2 GB of weights (> L2)",
+                       "l2": f"no flush: each step streams the {cache.total_aligned_bytes() / 1e9:.1f} GB of weights (> L2)",
                        "gguf_gen_s": round(gen_s, 1), "repack_s": round(build_s, 2)},
             "decode_step": {"bytes_per_token": bytes_token + kv_bytes,
                             "GBps": round((bytes_token + kv_bytes) / step_s / 1e9, 1),

@@ -376,6 +376,37 @@ def test_llama3_8b_shaped_two_layers_long_context(jal, oracle, torch_cuda):
     print(f"8B-shaped 2-layer fast numerics worst |dlogit| = {worst:.3e}, tokens {tokens[:8]}")
 
 
+def test_qwen2_7b_shaped_two_layers(jal, oracle, torch_cuda):
+    """The Qwen2-7B layer shape against the oracle: 2 layers of dim 3584
+    (112 blocks per row: a partial 4096-column segment), 28/4 heads, head_dim
+    128, FFN 18944 (down rows of five segments, the last partial), vocab
+    152064, Q8_0 weights and head, QKV bias, NeoX RoPE theta 1e6, f16 KV; a
+    96-token prompt, then 16 free-running greedy steps with the FAST bars."""
+    import dataclasses
+    spec = dataclasses.replace(jal.QWEN2_7B_Q8_0, num_layers=2)
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=91, neox=True, kv_dtype=jal.KV_F16, n_ctx=512,
+                                     numerics=jal.NUMERICS_FAST)
+    assert cache.bias_count() == 3 * spec.num_layers
+    prompt = prompt_of(13, n=96, vocab=spec.vocab_size)
+    tokens, _, worst = run_parity(om, ctx, prompt, 16, 512)
+    print(f"Qwen2-7B-shaped 2-layer fast numerics worst |dlogit| = {worst:.3e}, tokens {tokens[:8]}")
+
+
+def test_llama3_70b_shaped_two_layers(jal, oracle, torch_cuda):
+    """The Llama-3-70B layer shape against the oracle: 2 layers of dim 8192
+    (two segments per row), 64/8 heads (8 query heads per KV head), head_dim
+    128, FFN 28672 (down rows of seven segments), vocab 128256, Q4_0, RoPE
+    theta 5e5, f16 KV; a 64-token prompt, then 16 free-running greedy steps
+    with the FAST bars."""
+    import dataclasses
+    spec = dataclasses.replace(jal.LLAMA3_70B_Q4_0, num_layers=2)
+    _, om, recipe, cache, ctx = make(jal, oracle, spec, seed=92, kv_dtype=jal.KV_F16, n_ctx=512,
+                                     numerics=jal.NUMERICS_FAST)
+    prompt = prompt_of(14, n=64, vocab=spec.vocab_size)
+    tokens, _, worst = run_parity(om, ctx, prompt, 16, 512)
+    print(f"70B-shaped 2-layer fast numerics worst |dlogit| = {worst:.3e}, tokens {tokens[:8]}")
+
+
 def test_caller_owned_kv_cache_shared_by_two_contexts(jal, oracle, torch_cuda):
     """A KV cache allocated by the caller (the reference's KvCacheView) and
     two contexts over it: A prefills, is freed, and B resumes decoding at
