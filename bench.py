@@ -315,6 +315,61 @@ def profile_mode(args):
     return 0
 
 
+def batch_arm(args, jal, torch, np, spec, cache, recipe, n_prefill, n_ctx, gen_s, build_s, peak, peak_kind):
+    """--batch B: B independent sequences, each prefilled with its own prompt,
+    then K steps of jal_decode_batch (the B tokens of a step decoded at once;
+    value = B x K / time).  Each step goes through the C ABI and synchronises
+    on the device; the e2e line adds the [B, vocab] logits read into one
+    page-locked host array."""
+    B = args.batch
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctxs = [jal.ExecutionContext(recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F16) for _ in range(B)]
+    for c in ctxs:
+        c.set_stream(stream)
+    rng = np.random.Generator(np.random.PCG64(SEED))
+    prompts = [rng.integers(0, spec.vocab_size, n_prefill).astype(np.uint32) for _ in range(B)]
+    t_prefill = 0.0
+    for c, p in zip(ctxs, prompts):
+        t_prefill += ev_time(torch, lambda: c.prefill_step(p, 0), stream)
+    toks = rng.integers(0, spec.vocab_size, B).astype(np.uint32)
+    for _ in range(args.warmup):
+        jal.decode_batch(ctxs, toks, want_logits=False)
+    with ClockSampler(0) as clk:
+        t_dec = ev_time(torch, lambda: [jal.decode_batch(ctxs, toks, want_logits=False) for _ in range(args.steps)],
+                        stream)
+    host = torch.empty((B, spec.vocab_size), dtype=torch.float32).pin_memory().numpy()
+    t_e2e = ev_time(torch, lambda: [jal.decode_batch(ctxs, toks, out=host) for _ in range(args.steps)], stream)
+    wq = "Q8_0" if spec.weight_quant == jal.Q8_0 else "Q4_0"
+    bytes_token = cache.total_aligned_bytes()
+    kv_bytes = B * 2 * spec.num_layers * spec.n_heads_kv * spec.head_dim * 2 * (n_prefill + args.warmup + args.steps)
+    step_s = t_dec / args.steps
+    line = {"metric": METRIC, "value": round(B * args.steps / t_dec, 2), "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": f"synthetic: seeded N(0,0.02) weights quantized to {wq}, uniform-random token ids",
+            "config": {"workload": f"{args.workload} decode bs={B} (independent sequences) after {n_prefill}-token "
+                                   "prefills", "batch": B,
+                       "layers": spec.num_layers, "hidden": spec.hidden_dim, "heads": [spec.n_heads_q, spec.n_heads_kv],
+                       "head_dim": spec.head_dim, "ffn": spec.ffn_dim, "vocab": spec.vocab_size,
+                       "weights": f"{wq} ({'8.5' if wq == 'Q8_0' else '4.5'} bpw in HBM)", "kv_cache": "paged fp16",
+                       "numerics": "reference f32 order (bit-exact with the oracle)", "parallelism": "replicas x1",
+                       "l2": f"no flush: each step streams the {bytes_token / 1e9:.1f} GB of weights (> L2)",
+                       "gguf_gen_s": round(gen_s, 1), "repack_s": round(build_s, 2)},
+            "decode_step": {"bytes_per_step": bytes_token + kv_bytes,
+                            "GBps": round((bytes_token + kv_bytes) / step_s / 1e9, 1),
+                            "frac_of_peak": round((bytes_token + kv_bytes) / step_s / 1e9 / peak, 4),
+                            "peak_GBps": peak, "peak_kind": peak_kind},
+            "prefill": {"tokens": int(B * n_prefill), "s": round(t_prefill, 4),
+                        "tok_per_s": round(B * n_prefill / t_prefill, 1)},
+            "e2e": {"value": round(B * args.steps / t_e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B + 8 * B,
+                    "d2h_bytes_per_step": 4 * B * spec.vocab_size},
+            "gpu_launches": (3 + spec.num_layers * (7 + 2 * B)) * (args.warmup + 2 * args.steps),
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -326,6 +381,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="llama3-8b-q4_0",
                     choices=["llama3-8b-q4_0", "qwen2-7b-q8_0", "llama3-70b-q4_0", "tiny"])
+    ap.add_argument("--batch", type=int, default=1,
+                    help="decode this many independent sequences per step (jal_decode_batch), one GPU")
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1 ranks: one tensor-parallel model over the N GPUs (strong scaling) "
                          "instead of N independent replicas")
@@ -371,6 +428,8 @@ def main():
     build_s = time.perf_counter() - t0
     n_prefill = min(args.prefill, spec.context_length - args.warmup - args.steps - 8)
     n_ctx = n_prefill + 2 * (args.warmup + args.steps) + 16
+    if args.batch > 1:
+        return batch_arm(args, jal, torch, np, spec, cache, recipe, n_prefill, n_ctx, gen_s, build_s, peak, peak_kind)
     ctx = jal.ExecutionContext(recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F16)
     stream = torch.cuda.Stream()  # a capturable stream: decode steps replay a CUDA graph on it
     torch.cuda.set_stream(stream)

@@ -371,6 +371,24 @@ int jal_prefill_step(jal_context *ctx, const uint32_t *tokens, size_t n,
  * advances by one; unchanged on error. */
 int jal_decode_step(jal_context *ctx, uint32_t token, float *logits,
                     size_t logits_len);
+/* One decode step for n independent sequences at once, ctxs[i] holding
+ * sequence i (no counterpart in the reference, whose batched forward
+ * (recipe.rs:1489-1756) runs one sequence's prompt rows; this batches
+ * sequences the way a serving engine does).  The contexts share one model
+ * cache, run JAL_NUMERICS_FAST on one GPU and own distinct KV caches; token
+ * i is decoded at ctxs[i]'s position, which then advances by one.  The
+ * projections stream each weight matrix once for all n rows; every f32 sum
+ * keeps the reference's order, so sequence i's logits equal what
+ * jal_decode_step on ctxs[i] alone returns.  logits (host, n x vocab floats,
+ * row i for sequence i) may be NULL: jal_context_batch_logits_device(ctxs[0])
+ * then gives the device rows.  Work runs on ctxs[0]'s stream (replayed from
+ * a CUDA graph kept for the list of contexts when graphs are on); nothing
+ * changes on error. */
+int jal_decode_batch(jal_context *const *ctxs, size_t n, const uint32_t *tokens,
+                     float *logits, size_t logits_len);
+/* Device pointer to the last jal_decode_batch logits ([n][vocab] f32) of the
+ * batch whose first context is ctx. */
+int jal_context_batch_logits_device(const jal_context *ctx, const float **out);
 /* Greedy decode of n_steps tokens on the device, starting from `token` at
  * the current position (argmax, lowest index wins ties; the reference
  * leaves sampling to the engine).  tokens_out (host) gets n_steps ids. */

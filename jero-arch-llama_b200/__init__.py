@@ -191,6 +191,8 @@ _SIGS = {
     "jal_prefill_step": (C.c_int, [_P, _P, _SZ, _SZ, C.c_int, _P, _SZ]),
     "jal_decode_step": (C.c_int, [_P, C.c_uint32, _P, _SZ]),
     "jal_decode_greedy": (C.c_int, [_P, C.c_uint32, _SZ, _P]),
+    "jal_decode_batch": (C.c_int, [_P, _SZ, _P, _P, _SZ]),
+    "jal_context_batch_logits_device": (C.c_int, [_P, C.POINTER(_P)]),
     "jal_context_export_kv": (C.c_int, [_P, _SZ, _P, _SZ]),
     "jal_context_logits_device": (C.c_int, [_P, C.POINTER(_P)]),
     "jal_context_last_step_launches": (C.c_int, [_P, C.POINTER(_SZ)]),
@@ -685,6 +687,30 @@ class ExecutionContext:
         v = C.c_int()
         _check(lib().jal_context_tp_exchange(self._h, C.byref(v)))
         return {0: "none", 1: "nccl", 2: "peer"}[v.value]
+
+
+def decode_batch(contexts, tokens, want_logits: bool = True, out=None):
+    """One decode step for several independent sequences (jal_decode_batch):
+    token i at contexts[i]'s position.  The contexts share one model cache and
+    own distinct KV caches; each advances by one.  Returns the logits as a
+    [n, vocab] float32 array (or `out`, filled), or None."""
+    import numpy as np
+    n = len(contexts)
+    toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+    if toks.shape != (n,):
+        raise ValueError("one token per context")
+    hs = (_P * n)(*[c._h for c in contexts])
+    vocab = contexts[0].vocab
+    logits = None
+    if out is not None:
+        if out.dtype != np.float32 or out.shape != (n, vocab) or not out.flags["C_CONTIGUOUS"]:
+            raise ValueError("out must be a contiguous float32 [n, vocab] array")
+        logits = out
+    elif want_logits:
+        logits = np.empty((n, vocab), dtype=np.float32)
+    _check(lib().jal_decode_batch(hs, n, toks.ctypes.data, logits.ctypes.data if logits is not None else None,
+                                  logits.size if logits is not None else 0))
+    return logits
 
 
 # ---- synthetic GGUF models (include/jal_synth.h) -----------------------------

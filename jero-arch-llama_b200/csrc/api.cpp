@@ -653,6 +653,58 @@ int jal_decode_step(jal_context *h, uint32_t token, float *logits, size_t logits
   });
 }
 
+int jal_decode_batch(jal_context *const *hs, size_t n, const uint32_t *tokens, float *logits, size_t logits_len) {
+  return guard([&] {
+    NEED(hs);
+    NEED(tokens);
+    if (n == 0) fail(JAL_ERR_INVALID_ARGUMENT, "batch of zero sequences");
+    std::vector<Context *> cs(n);
+    for (size_t i = 0; i < n; i++) {
+      NEED(hs[i]);
+      cs[i] = hs[i]->ctx.get();
+    }
+    Context &c0 = *cs[0];
+    for (size_t i = 0; i < n; i++) {
+      Context &c = *cs[i];
+      if (c.cache != c0.cache) fail(JAL_ERR_INVALID_ARGUMENT, "batched decode: context %zu runs another model cache", i);
+      if (!c.exact)
+        fail(JAL_ERR_CAPABILITY_MISMATCH, "batched decode needs the reference-order numerics on one GPU (context %zu)", i);
+      if (c.position + 1 > c.cfg.n_ctx)
+        fail(JAL_ERR_CONTEXT_LENGTH_EXCEEDED, "context %zu: requested %llu > n_ctx %llu", i,
+             (unsigned long long)c.position + 1, (unsigned long long)c.cfg.n_ctx);
+      for (size_t j = 0; j < i; j++)
+        if (cs[j] == cs[i] || cs[j]->kv.k == c.kv.k)
+          fail(JAL_ERR_INVALID_ARGUMENT, "batched decode: contexts %zu and %zu share a KV cache", j, i);
+      check_tokens(c, &tokens[i], 1);
+    }
+    const size_t V = c0.cache->vocab_size;
+    if (logits && logits_len != n * V)
+      fail(JAL_ERR_TENSOR_BOUNDS, "logits len %zu != %zu x vocab %zu", logits_len, n, V);
+    JAL_CUDA(cudaSetDevice(c0.cache->device));
+    for (size_t i = 1; i < n; i++) JAL_CUDA(cudaStreamSynchronize(cs[i]->stream));  // their own work first
+    c0.ensure_prefill_capacity(n);
+    for (size_t i = 0; i < n; i++) {
+      *cs[i]->h_pos = (int64_t)cs[i]->position;
+      JAL_CUDA(cudaMemcpyAsync(cs[i]->d_pos, cs[i]->h_pos, 8, cudaMemcpyHostToDevice, c0.stream));
+    }
+    JAL_CUDA(cudaMemcpyAsync(c0.pf_tokens, tokens, n * 4, cudaMemcpyHostToDevice, c0.stream));
+    run_batch_decode(cs.data(), n);
+    if (logits) JAL_CUDA(cudaMemcpyAsync(logits, c0.bt_logits, n * V * 4, cudaMemcpyDeviceToHost, c0.stream));
+    enqueue_error_read(c0);
+    JAL_CUDA(cudaStreamSynchronize(c0.stream));
+    check_device_error(c0);
+    for (size_t i = 0; i < n; i++) cs[i]->position += 1;
+  });
+}
+
+int jal_context_batch_logits_device(const jal_context *h, const float **out) {
+  return guard([&] {
+    NEED(h);
+    NEED(out);
+    *out = h->ctx->bt_logits;
+  });
+}
+
 int jal_decode_greedy(jal_context *h, uint32_t token, size_t n_steps, uint32_t *tokens_out) {
   return guard([&] {
     NEED(h);

@@ -218,6 +218,9 @@ void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
 void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s);
 // Cluster size for launch_xattn_decode (>= G), 0 when the shape does not fit.
 int xattn_cluster_size(int head_dim, int f16, int G, int n_kv, int64_t n_ctx);
+// The smallest cluster size (>= G) for launch_xattn_decode at n_ctx, so that
+// several sequences' launches share the GPU (batched decode); 0 if none fits.
+int xattn_batch_cluster_size(int head_dim, int f16, int G, int64_t n_ctx);
 
 // Reference-order decode attention, output (xattn_v.cu): out_d = sum_t w_t
 // * v_td in position order, then its QuantizedActQ8 blocks.

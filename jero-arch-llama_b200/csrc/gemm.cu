@@ -182,10 +182,147 @@ __global__ void __launch_bounds__(kThreads) k_gemm(const GemmArgs a) {
   }
 }
 
+// ---- few tokens (M <= 16): batched decode ---------------------------------
+// The same chunk dots and the same per-(token, row) fold as k_gemm, tiled for
+// a skinny M: one m16 tile of tokens, CTAs of 32 rows (4 warps, one n-tile of
+// 8 rows each) so that even 3584-row projections spread over ~110 CTAs, and a
+// 4-stage cp.async ring of 16 blocks per stage for the bytes in flight.
+// Everything past the matrix or the token count is zero-filled and adds +0
+// terms, which leave every row's sum unchanged.
+constexpr int SBM = 16, SBN = 32, SKB = 16, SNS = 4, kSkThreads = 128;
+
+template <int WB>
+struct SkStage {
+  uint8_t w[SKB][SBN][WB];  // weight blocks
+  int8_t x[SKB][SBM][32];   // activation blocks
+  uint16_t wd[SBN][SKB];    // weight block scales (f16 bits), row-major
+  float as[SBM][SKB];       // activation block scales, token-major
+};
+
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem, bool valid) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(valid ? 4 : 0) : "memory");
+}
+
+template <int QUANT, bool HI>
+__global__ void __launch_bounds__(kSkThreads) k_gemm_skinny(const GemmArgs a) {
+  constexpr int WB = QUANT == JAL_Q4_0 ? 16 : 32;
+  using Stage = SkStage<WB>;
+  extern __shared__ __align__(16) char gsm[];
+  Stage *st = reinterpret_cast<Stage *>(gsm);
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32, g = lane / 4, q = lane % 4;
+  const int64_t r0 = (int64_t)blockIdx.x * SBN, K = a.w.cols, nb = K / 32;
+  const int m = (int)a.m;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  auto issue = [&](int64_t sidx) {
+    Stage &sb = st[sidx % SNS];
+    const int64_t b0 = sidx * SKB;
+    for (int i = tid; i < SKB * SBN * (WB / 16); i += kSkThreads) {
+      const int piece = i % (WB / 16), rr = (i / (WB / 16)) % SBN, kb = i / (WB / 16) / SBN;
+      const int64_t r = r0 + rr, b = b0 + kb;
+      const bool ok = r < a.rows && b < nb;
+      cp_async16(&sb.w[kb][rr][piece * 16], ok ? a.w.qs + r * a.w.qs_stride + b * WB + piece * 16 : a.w.qs, ok);
+    }
+    for (int i = tid; i < SKB * SBM * 2; i += kSkThreads) {
+      const int half = i % 2, tt = (i / 2) % SBM, kb = i / 2 / SBM;
+      const int64_t b = b0 + kb;
+      const bool ok = tt < m && b < nb;
+      cp_async16(&sb.x[kb][tt][half * 16], ok ? a.xq + tt * K + b * 32 + half * 16 : a.xq, ok);
+    }
+    for (int i = tid; i < SBN * SKB / 2; i += kSkThreads) {  // two scales per copy (the run is padded to 8)
+      const int rr = i / (SKB / 2), pr = i % (SKB / 2);
+      const int64_t r = r0 + rr, b = b0 + 2 * pr;
+      const bool ok = r < a.rows && b < nb;
+      cp_async4(&sb.wd[rr][2 * pr], ok ? a.w.d + r * a.w.d_stride + b : a.w.d, ok);
+    }
+    for (int i = tid; i < SBM * SKB; i += kSkThreads) {
+      const int tt = i / SKB, kb = i % SKB;
+      const int64_t b = b0 + kb;
+      const bool ok = tt < m && b < nb;
+      cp_async4(&sb.as[tt][kb], ok ? a.xs + tt * nb + b : a.xs, ok);
+    }
+  };
+  const int64_t nst = (nb + SKB - 1) / SKB;
+  for (int s = 0; s < SNS - 1; s++) {
+    if (s < nst) issue(s);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  const int rb = warp * 8 + g;  // this lane's B row
+  for (int64_t sidx = 0; sidx < nst; sidx++) {
+    if (sidx + SNS - 1 < nst) issue(sidx + SNS - 1);  // into the slot freed at the end of the last stage
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group %0;" ::"n"(SNS - 1) : "memory");
+    __syncthreads();
+    const Stage &cur = st[sidx % SNS];
+#pragma unroll 4
+    for (int kb = 0; kb < SKB; kb++) {
+      const uint32_t alo0 = *(const uint32_t *)&cur.x[kb][g][4 * q];
+      const uint32_t ahi0 = *(const uint32_t *)&cur.x[kb][g][16 + 4 * q];
+      const uint32_t alo1 = HI ? *(const uint32_t *)&cur.x[kb][g + 8][4 * q] : 0u;
+      const uint32_t ahi1 = HI ? *(const uint32_t *)&cur.x[kb][g + 8][16 + 4 * q] : 0u;
+      uint32_t blo, bhi;
+      if (QUANT == JAL_Q4_0) {
+        const uint32_t w = *(const uint32_t *)&cur.w[kb][rb][4 * q];
+        blo = nib_s8(w & 0x0F0F0F0Fu);
+        bhi = nib_s8((w >> 4) & 0x0F0F0F0Fu);
+      } else {
+        blo = *(const uint32_t *)&cur.w[kb][rb][4 * q];
+        bhi = *(const uint32_t *)&cur.w[kb][rb][16 + 4 * q];
+      }
+      int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+      mma_s8_16816(c0, alo0, alo1, blo);
+      mma_s8_16816(c1, ahi0, ahi1, bhi);
+      const float as0 = cur.as[g][kb];
+      const float ws0 = f16_finite(cur.wd[warp * 8 + 2 * q][kb]), ws1 = f16_finite(cur.wd[warp * 8 + 2 * q + 1][kb]);
+      acc[0] = __fadd_rn(__fadd_rn(acc[0], chunk_term(c0[0], as0, ws0)), chunk_term(c1[0], as0, ws0));
+      acc[1] = __fadd_rn(__fadd_rn(acc[1], chunk_term(c0[1], as0, ws1)), chunk_term(c1[1], as0, ws1));
+      if (HI) {
+        const float as1 = cur.as[g + 8][kb];
+        acc[2] = __fadd_rn(__fadd_rn(acc[2], chunk_term(c0[2], as1, ws0)), chunk_term(c1[2], as1, ws0));
+        acc[3] = __fadd_rn(__fadd_rn(acc[3], chunk_term(c0[3], as1, ws1)), chunk_term(c1[3], as1, ws1));
+      }
+    }
+    __syncthreads();  // every warp is done with this slot before it is refilled
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < (HI ? 4 : 2); i++) {
+    const int64_t t = g + (i < 2 ? 0 : 8);
+    const int64_t r = r0 + warp * 8 + 2 * q + (i & 1);
+    if (t >= a.m || r >= a.rows) continue;
+    float v = acc[i];
+    if (a.bias) v = __fadd_rn(v, a.bias[r]);
+    float *yp = a.y + t * a.y_stride + r;
+    *yp = a.accumulate ? __fadd_rn(*yp, v) : v;
+  }
+}
+
+template <int QUANT>
+void launch_skinny(const GemmArgs &a, cudaStream_t s) {
+  constexpr size_t smem = SNS * sizeof(SkStage<QUANT == JAL_Q4_0 ? 16 : 32>);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm_skinny<QUANT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(k_gemm_skinny<QUANT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr = true;
+  }
+  const dim3 grid((unsigned)((a.rows + SBN - 1) / SBN));
+  if (a.m > 8) k_gemm_skinny<QUANT, true><<<grid, kSkThreads, smem, s>>>(a);
+  else k_gemm_skinny<QUANT, false><<<grid, kSkThreads, smem, s>>>(a);
+}
+
 }  // namespace
 
 void launch_gemm(const GemmArgs &a, cudaStream_t s) {
   if (a.m <= 0 || a.rows <= 0) return;
+  // Few tokens with scale runs that 4-byte copies can read (16-byte rows,
+  // scales padded to a multiple of 8): the skinny tiling.
+  if (a.m <= SBM && a.w.d_stride % 8 == 0 && (reinterpret_cast<uintptr_t>(a.w.d) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(a.xs) & 3) == 0) {
+    if (a.w.quant == JAL_Q4_0) launch_skinny<JAL_Q4_0>(a, s);
+    else launch_skinny<JAL_Q8_0>(a, s);
+    return;
+  }
   dim3 grid((unsigned)((a.rows + BN - 1) / BN), (unsigned)((a.m + BM - 1) / BM));
   static bool attr = false;
   constexpr size_t s4 = 2 * sizeof(GemmStage<16>), s8 = 2 * sizeof(GemmStage<32>);

@@ -1,6 +1,7 @@
 // Recipe hydration, ModelRepackCache build, execution context and the
 // decode / prefill step sequences.  File:line citations refer to the
 // reference crate.
+#include <atomic>
 #include "model.hpp"
 
 #include <algorithm>
@@ -921,6 +922,8 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
                                         const KvCache *ext_kv) {
   JAL_CUDA(cudaSetDevice(c.device));
   auto ctx = std::make_unique<Context>();
+  static std::atomic<uint64_t> next_uid{1};
+  ctx->uid = next_uid++;
   ctx->cache = &c;
   ctx->recipe = r;
   ctx->cfg = cfg0;
@@ -1127,6 +1130,9 @@ size_t decode_scratch_bytes(const Recipe &r, uint64_t seq) {  // recipe.rs:529-5
 
 Context::~Context() {
   if (graph) cudaGraphExecDestroy(graph);
+  if (bt_graph) cudaGraphExecDestroy(bt_graph);
+  for (cudaStream_t s : bt_streams) { cudaStreamSynchronize(s); cudaStreamDestroy(s); }
+  for (cudaEvent_t e : bt_events) cudaEventDestroy(e);
   if (h_pos) cudaFreeHost(h_pos);
   if (h_token) cudaFreeHost(h_token);
   if (stream) cudaStreamSynchronize(stream);
@@ -1296,6 +1302,156 @@ void Context::enqueue_exact_step(bool pdl) {
   launches_per_step = n;
 }
 
+// Batched decode of independent sequences (no counterpart in the reference,
+// whose batched forward is one sequence's prompt): per layer RMSNorm +
+// QuantizedActQ8 of the n rows, the Q/K/V GEMM, per sequence the two
+// reference-order attention kernels on that context's KV cache and position
+// (writing its row of the O input; each sequence on its own side stream),
+// then the O, gate/up and down GEMMs with the residual adds, and the LM head
+// over the n rows.  Every f32 sum keeps the reference's order, so each row
+// equals the single-sequence step.
+void batch_decode_step(Context *const *cs, size_t n, const uint32_t *d_tokens) {
+  Context &c0 = *cs[0];
+  const ModelCache &c = *c0.cache;
+  const Geometry &g = c0.g;
+  const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv, V = c.vocab_size;
+  const float eps = std::max(c0.recipe.rms_eps, 1.0e-7f);
+  const int64_t m = (int64_t)n;
+  cudaStream_t s = c0.stream;
+  float *hid = c0.pf_hidden, *qkv = c0.pf_qkv, *att = c0.pf_attn, *gu = c0.pf_gu, *xs = c0.pf_xs;
+  int8_t *xq = c0.pf_xq;
+  launch_embed(c.emb_raw->as<uint8_t>(), c.emb_quant, (int64_t)H, (int64_t)c.emb_rows, d_tokens, m, hid, c0.d_err, 0,
+               s);
+  for (size_t l = 0; l < c.layers.size(); l++) {
+    const Layer &L = c.layers[l];
+    launch_rmsnorm_quant(hid, L.attn_norm, m, (int64_t)H, eps, xq, xs, s);
+    GemmArgs qa;
+    qa.w = L.qkv; qa.m = m; qa.rows = (int64_t)(Q + 2 * KV); qa.xq = xq; qa.xs = xs;
+    qa.y = qkv; qa.y_stride = (int64_t)(Q + 2 * KV);
+    launch_gemm(qa, s);
+    JAL_CUDA(cudaEventRecord(c0.bt_events[0], s));
+    for (size_t b = 0; b < n; b++) {
+      Context &cb = *cs[b];
+      cudaStream_t sb = c0.bt_streams[b];
+      JAL_CUDA(cudaStreamWaitEvent(sb, c0.bt_events[0], 0));
+      AttnDecodeArgs aa;
+      aa.qkv = qkv + b * (Q + 2 * KV); aa.bq = L.bq; aa.bk = L.bk; aa.bv = L.bv;
+      aa.cos_tab = cb.cos_tab; aa.sin_tab = cb.sin_tab; aa.cos_tab_long = cb.cos_long; aa.sin_tab_long = cb.sin_long;
+      aa.long_threshold = cb.recipe.scaling.kind == JAL_ROPE_SCALING_LONGROPE
+                              ? (int64_t)cb.recipe.scaling.original_max_position_embeddings : -1;
+      aa.skip_rope = cb.recipe.should_skip_rope(l); aa.neox = cb.recipe.rope_type == JAL_ROPE_NEOX;
+      aa.n_heads_q = (int64_t)g.n_heads_q; aa.rotary_dim = (int64_t)g.rotary_dim;
+      aa.kv = cb.kv; aa.layer = (int64_t)l; aa.d_pos = cb.d_pos; aa.window = (int64_t)cb.cfg.sliding_window;
+      aa.scale = 1.0f / sqrtf((float)g.head_dim);
+      aa.n_splits = cb.bt_splits;
+      aa.w_out = cb.attn_w; aa.w_stride = (int64_t)cb.cfg.n_ctx; aa.err = c0.d_err; aa.pdl = 0;
+      launch_xattn_decode(aa, (int64_t)cb.cfg.n_ctx, sb);
+      AttnVArgs va;
+      va.kv = cb.kv; va.layer = (int64_t)l; va.window = (int64_t)cb.cfg.sliding_window;
+      va.n_heads_q = (int64_t)g.n_heads_q; va.d_pos = cb.d_pos; va.w = cb.attn_w; va.w_stride = (int64_t)cb.cfg.n_ctx;
+      va.out = att + b * Q; va.out_q = xq + b * Q; va.out_s = xs + b * (Q / 32); va.err = c0.d_err; va.pdl = 0;
+      launch_xattn_v(cb.tm_v, va, (int64_t)cb.cfg.n_ctx, sb);
+      JAL_CUDA(cudaEventRecord(c0.bt_events[1 + b], sb));
+    }
+    for (size_t b = 0; b < n; b++) JAL_CUDA(cudaStreamWaitEvent(s, c0.bt_events[1 + b], 0));
+    GemmArgs oa;
+    oa.w = L.wo.dm; oa.m = m; oa.rows = (int64_t)H; oa.xq = xq; oa.xs = xs;
+    oa.y = hid; oa.y_stride = (int64_t)H; oa.bias = L.bo; oa.accumulate = 1;
+    launch_gemm(oa, s);
+    launch_rmsnorm_quant(hid, L.ffn_norm, m, (int64_t)H, eps, xq, xs, s);
+    GemmArgs ga;
+    ga.w = L.gateup; ga.m = m; ga.rows = (int64_t)(2 * F); ga.xq = xq; ga.xs = xs;
+    ga.y = gu; ga.y_stride = (int64_t)(2 * F);
+    launch_gemm(ga, s);
+    launch_swiglu_act_quant(gu, m, (int64_t)F, (int64_t)(2 * F), xq, xs, s);
+    GemmArgs da;
+    da.w = L.wdown.dm; da.m = m; da.rows = (int64_t)H; da.xq = xq; da.xs = xs;
+    da.y = hid; da.y_stride = (int64_t)H; da.accumulate = 1;
+    launch_gemm(da, s);
+  }
+  if (dense_quant(c.lm_head.dm.quant)) {
+    for (size_t b = 0; b < n; b++) {
+      launch_rmsnorm(hid + b * H, c.output_norm->as<float>(), 1, (int64_t)H, eps, c0.s_norm, s);
+      launch_strict_gemv_dense(c.lm_head.dm, c0.s_norm, (int64_t)V, c0.bt_logits + b * V, s);
+    }
+  } else {
+    launch_rmsnorm_quant(hid, c.output_norm->as<float>(), m, (int64_t)H, eps, xq, xs, s);
+    GemmArgs la;
+    la.w = c.lm_head.dm; la.m = m; la.rows = (int64_t)V; la.xq = xq; la.xs = xs;
+    la.y = c0.bt_logits; la.y_stride = (int64_t)V;
+    launch_gemm(la, s);
+  }
+  JAL_CUDA(cudaGetLastError());
+}
+
+void run_batch_decode(Context *const *cs, size_t n) {
+  Context &c0 = *cs[0];
+  const ModelCache &c = *c0.cache;
+  const uint64_t V = c.vocab_size;
+  cudaStream_t s = c0.stream;
+  if (c0.bt_cap < n) {
+    JAL_CUDA(cudaStreamSynchronize(s));
+    c0.bt_buf = alloc(n * V * 4);
+    c0.pf_gen++;
+    c0.bt_logits = c0.bt_buf->as<float>();
+    c0.bt_cap = n;
+  }
+  while (c0.bt_streams.size() < n) {
+    cudaStream_t t;
+    JAL_CUDA(cudaStreamCreateWithFlags(&t, cudaStreamNonBlocking));
+    c0.bt_streams.push_back(t);
+  }
+  while (c0.bt_events.size() < n + 1) {
+    cudaEvent_t e;
+    JAL_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    c0.bt_events.push_back(e);
+  }
+  std::vector<uint64_t> key = {n, c0.pf_gen};
+  for (size_t b = 0; b < n; b++) {
+    Context &cb = *cs[b];
+    if (!cb.bt_splits) {
+      cb.bt_splits = xattn_batch_cluster_size((int)cb.g.head_dim, cb.cfg.kv_f16, (int)(cb.g.n_heads_q / cb.g.n_heads_kv),
+                                              (int64_t)cb.cfg.n_ctx);
+      if (!cb.bt_splits) fail(JAL_ERR_CAPABILITY_MISMATCH, "batched decode: attention shape not supported");
+    }
+    key.push_back(cb.uid);
+  }
+  if (!c0.cfg.use_graphs) {
+    batch_decode_step(cs, n, c0.pf_tokens);
+    return;
+  }
+  if (!c0.bt_graph || c0.bt_key != key) {
+    if (c0.bt_graph) {
+      JAL_CUDA(cudaStreamSynchronize(s));
+      cudaGraphExecDestroy(c0.bt_graph);
+      c0.bt_graph = nullptr;
+    }
+    cudaGraph_t gr = nullptr;
+    JAL_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    try {
+      batch_decode_step(cs, n, c0.pf_tokens);
+    } catch (...) {
+      cudaStreamEndCapture(s, &gr);
+      if (gr) cudaGraphDestroy(gr);
+      cudaGetLastError();
+      throw;
+    }
+    cudaError_t e = cudaStreamEndCapture(s, &gr);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      fail(JAL_ERR_CUDA, "batched decode graph capture failed: %s", cudaGetErrorString(e));
+    }
+    e = cudaGraphInstantiate(&c0.bt_graph, gr, 0);
+    cudaGraphDestroy(gr);
+    if (e != cudaSuccess) {
+      c0.bt_graph = nullptr;
+      fail(JAL_ERR_CUDA, "batched decode graph instantiate failed: %s", cudaGetErrorString(e));
+    }
+    c0.bt_key = key;
+  }
+  JAL_CUDA(cudaGraphLaunch(c0.bt_graph, s));
+}
+
 // Reference-order step (see strict.cu): the same layer sequence as
 // forward_tokens of the reference for one token.
 void Context::enqueue_strict_token(bool logits_out, bool argmax) {
@@ -1391,6 +1547,7 @@ void Context::ensure_prefill_capacity(uint64_t m) {
   size_t bytes = m * 4 + m * H * 4 + m * (Q + 2 * KV) * 4 + m * Q * 4 + m * 2 * F * 4 +
                  m * ((K + 31) / 32) * 4 + m * ((K + 31) / 32 * 32) + 7 * 256;
   pf_buf = alloc(bytes);
+  pf_gen++;
   char *p = pf_buf->as<char>();
   auto take = [&](size_t n) { char *q = p; p += (n + 255) / 256 * 256; return q; };
   pf_tokens = (uint32_t *)take(m * 4);

@@ -185,6 +185,20 @@ struct Context {
   float *pf_hidden = nullptr, *pf_qkv = nullptr, *pf_attn = nullptr, *pf_gu = nullptr,
         *pf_xs = nullptr;
   int8_t *pf_xq = nullptr;
+  // batched decode scratch (batch_decode_step with this context first):
+  // logits [bt_cap][vocab]
+  uint64_t bt_cap = 0;
+  DevBufferPtr bt_buf;
+  float *bt_logits = nullptr;
+  // one side stream per sequence for the attention kernels, which run
+  // concurrently between the Q/K/V and O projections
+  std::vector<cudaStream_t> bt_streams;
+  std::vector<cudaEvent_t> bt_events;  // [0]: Q/K/V done; [1 + b]: sequence b's attention done
+  int bt_splits = 0;                   // score-kernel cluster size in batched steps
+  cudaGraphExec_t bt_graph = nullptr;  // the batched step of the contexts in bt_key
+  std::vector<uint64_t> bt_key;        // {n, scratch generation, the contexts' ids}
+  uint64_t uid = 0;                    // unique per context (graph keys)
+  uint64_t pf_gen = 0;                 // bumped when the prefill scratch moves
   // host staging
   int64_t *h_pos = nullptr;
   uint32_t *h_token = nullptr;
@@ -210,6 +224,18 @@ struct Context {
   void prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bool compute_logits);
   void ensure_prefill_capacity(uint64_t m);
 };
+
+// One decode step for n sequences at once, one context each (distinct KV
+// caches, one model cache, reference-order numerics on one GPU): the
+// projections run once over the n token rows (the reference-order GEMM), the
+// attention per context at its own position.  Each sequence's logits equal
+// its single-context decode step's.  Work goes on cs[0]'s stream (the
+// attention on side streams joined back to it); d_pos of every context must
+// hold its position; logits land in cs[0]->bt_logits.
+void batch_decode_step(Context *const *cs, size_t n, const uint32_t *d_tokens);
+// The batched step on cs[0]'s stream, replayed from a CUDA graph kept for
+// this list of contexts (captured on first use); tokens in cs[0]->pf_tokens.
+void run_batch_decode(Context *const *cs, size_t n);
 
 // ext_kv: run over a caller-owned KV cache (must outlive the context);
 // nullptr: the context allocates its own.

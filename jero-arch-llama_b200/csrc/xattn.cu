@@ -26,6 +26,9 @@
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
+#include <map>
+#include <mutex>
+
 #include "attn_dev.cuh"
 #include "common.hpp"
 #include "dev_util.cuh"
@@ -333,6 +336,22 @@ int xattn_cluster_size(int head_dim, int f16, int G, int n_kv, int64_t n_ctx) {
   return best;
 }
 
+int xattn_batch_cluster_size(int head_dim, int f16, int G, int64_t n_ctx) {
+  const void *fn = pick_x(head_dim, f16, G);
+  if (!fn || G > 16) return 0;
+  // The smallest cluster (>= G) whose shares fit: several sequences' score
+  // kernels then run side by side.
+  for (int cs = 1; cs <= 16; cs *= 2) {
+    if (cs < G) continue;
+    const int per_cap = (int)((n_ctx + cs - 1) / cs);
+    const size_t smem = xattn_layout(per_cap, (int)n_ctx).total;
+    if (smem + 8 * 1024 > kSmemCap) continue;
+    if (cs > 8) cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    return cs;
+  }
+  return 0;
+}
+
 void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s) {
   const int G = (int)(a.n_heads_q / a.kv.n_kv);
   const void *fn = pick_x((int)a.kv.head_dim, a.kv.f16, G);
@@ -344,6 +363,16 @@ void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s)
     fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: n_ctx %lld does not fit", (long long)n_ctx);
   if (R < 8) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: page size %lld not a multiple of 8",
                   (long long)a.kv.page_size);
+  {  // the kernel's shared-memory limit covers the largest share launched so far
+    static std::mutex mu;
+    static std::map<const void *, size_t> set;
+    std::lock_guard<std::mutex> lk(mu);
+    size_t &cur = set[fn];
+    if (smem > cur) {
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cur = smem;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.kv.n_kv * cs));
   cfg.blockDim = dim3(kXT);

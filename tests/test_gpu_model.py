@@ -407,6 +407,64 @@ def test_llama3_70b_shaped_two_layers(jal, oracle, torch_cuda):
     print(f"70B-shaped 2-layer fast numerics worst |dlogit| = {worst:.3e}, tokens {tokens[:8]}")
 
 
+def _batch_vs_single(jal, recipe, cache, prompts, n_steps, om=None, n_ctx=256):
+    """Decode the prompts' sequences together with jal_decode_batch and,
+    separately, each alone with jal_decode_step: every step's batched rows
+    must equal the single-sequence logits bit for bit; with an oracle the
+    first sequence is also held to the FAST bars."""
+    mk = lambda: new_ctx(jal, recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
+    bat, ref = [mk() for _ in prompts], [mk() for _ in prompts]
+    toks = []
+    for b, r, p in zip(bat, ref, prompts):
+        lb, lr = b.prefill_step(p, 0), r.prefill_step(p, 0)
+        assert np.array_equal(lb, lr)
+        toks.append(int(np.argmax(lb)))
+    if om is not None:
+        kvo = om.new_kv(n_ctx)
+        om.prefill(kvo, n_ctx, prompts[0], 0)
+    for step in range(n_steps):
+        lg = jal.decode_batch(bat, toks)
+        for i, r in enumerate(ref):
+            li = r.decode_step(toks[i])
+            assert np.array_equal(lg[i], li), f"step {step} sequence {i}: batched row differs from the single step"
+        if om is not None:
+            lo = om.decode(kvo, n_ctx, toks[0], len(prompts[0]) + step)
+            assert np.max(np.abs(lo - lg[0])) <= LOGIT_ATOL
+        toks = [int(np.argmax(lg[i])) for i in range(len(prompts))]
+    assert all(b.position() == len(p) + n_steps for b, p in zip(bat, prompts))
+
+
+def test_batched_decode_of_independent_sequences(jal, oracle, torch_cuda):
+    """jal_decode_batch on the tiny Llama: three sequences with prompts of
+    16, 5 and 30 tokens step together for 12 greedy steps (f16 KV, FAST);
+    each row equals its sequence decoded alone, the first tracks the oracle;
+    contexts that share a KV cache or run another numerics are refused."""
+    spec = jal.SynthSpec()
+    _, om, recipe, cache, _ = make(jal, oracle, spec, seed=31, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
+    prompts = [prompt_of(21, 16), prompt_of(22, 5), prompt_of(23, 30)]
+    _batch_vs_single(jal, recipe, cache, prompts, 12, om=om)
+    c1 = new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
+    with pytest.raises(jal.K3Error):
+        jal.decode_batch([c1, c1], [1, 2])
+    slow = new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_REFERENCE)
+    with pytest.raises(jal.K3Error):
+        jal.decode_batch([c1, slow], [1, 2])
+
+
+def test_batched_decode_qwen2_7b_shaped_batch_4(jal, torch_cuda):
+    """The batch-4 decode of the Qwen2-7B configuration on 2 layers of its
+    shape (Q8_0, QKV bias, NeoX RoPE, G = 7): four sequences with prompts of
+    40, 17, 64 and 9 tokens, 8 steps; each batched row equals the sequence
+    decoded alone, bit for bit."""
+    import dataclasses
+    spec = dataclasses.replace(jal.QWEN2_7B_Q8_0, num_layers=2)
+    buf = jal.synth_gguf(spec, 93)
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    cache = recipe.build_repack_cache(buf)
+    prompts = [prompt_of(31 + i, n, spec.vocab_size) for i, n in enumerate((40, 17, 64, 9))]
+    _batch_vs_single(jal, recipe, cache, prompts, 8)
+
+
 def test_caller_owned_kv_cache_shared_by_two_contexts(jal, oracle, torch_cuda):
     """A KV cache allocated by the caller (the reference's KvCacheView) and
     two contexts over it: A prefills, is freed, and B resumes decoding at
