@@ -191,12 +191,16 @@ __global__ void __launch_bounds__(kThreads) k_gemm(const GemmArgs a) {
 // terms, which leave every row's sum unchanged.
 constexpr int SBM = 16, SBN = 32, SKB = 16, SNS = 4, kSkThreads = 128;
 
+// Stage tiles keep each row's (token's) 16 blocks contiguous, so one warp's
+// copies read 512 consecutive bytes of a row, and pad rows by 16 bytes, so
+// the 8 rows (tokens) of an MMA fragment fall in different banks.
 template <int WB>
 struct SkStage {
-  uint8_t w[SKB][SBN][WB];  // weight blocks
-  int8_t x[SKB][SBM][32];   // activation blocks
-  uint16_t wd[SBN][SKB];    // weight block scales (f16 bits), row-major
-  float as[SBM][SKB];       // activation block scales, token-major
+  static constexpr int WP = SKB * WB + 16, XP = SKB * 32 + 16;
+  uint8_t w[SBN][WP];          // weight blocks of a row, in K order
+  int8_t x[SBM][XP];           // activation blocks of a token, in K order
+  uint16_t wd[SBN][SKB];       // weight block scales (f16 bits)
+  float as[SBM][SKB + 1];      // activation block scales
 };
 
 __device__ __forceinline__ void cp_async4(void *smem, const void *gmem, bool valid) {
@@ -208,6 +212,7 @@ template <int QUANT, bool HI>
 __global__ void __launch_bounds__(kSkThreads) k_gemm_skinny(const GemmArgs a) {
   constexpr int WB = QUANT == JAL_Q4_0 ? 16 : 32;
   using Stage = SkStage<WB>;
+  constexpr int WPC = SKB * WB / 16;  // 16-byte pieces of a row per stage
   extern __shared__ __align__(16) char gsm[];
   Stage *st = reinterpret_cast<Stage *>(gsm);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32, g = lane / 4, q = lane % 4;
@@ -217,17 +222,17 @@ __global__ void __launch_bounds__(kSkThreads) k_gemm_skinny(const GemmArgs a) {
   auto issue = [&](int64_t sidx) {
     Stage &sb = st[sidx % SNS];
     const int64_t b0 = sidx * SKB;
-    for (int i = tid; i < SKB * SBN * (WB / 16); i += kSkThreads) {
-      const int piece = i % (WB / 16), rr = (i / (WB / 16)) % SBN, kb = i / (WB / 16) / SBN;
-      const int64_t r = r0 + rr, b = b0 + kb;
+    for (int i = tid; i < SBN * WPC; i += kSkThreads) {
+      const int rr = i / WPC, off = i % WPC;
+      const int64_t r = r0 + rr, b = b0 + off * 16 / WB;
       const bool ok = r < a.rows && b < nb;
-      cp_async16(&sb.w[kb][rr][piece * 16], ok ? a.w.qs + r * a.w.qs_stride + b * WB + piece * 16 : a.w.qs, ok);
+      cp_async16(&sb.w[rr][off * 16], ok ? a.w.qs + r * a.w.qs_stride + b0 * WB + off * 16 : a.w.qs, ok);
     }
-    for (int i = tid; i < SKB * SBM * 2; i += kSkThreads) {
-      const int half = i % 2, tt = (i / 2) % SBM, kb = i / 2 / SBM;
-      const int64_t b = b0 + kb;
+    for (int i = tid; i < SBM * SKB * 2; i += kSkThreads) {
+      const int tt = i / (SKB * 2), off = i % (SKB * 2);
+      const int64_t b = b0 + off / 2;
       const bool ok = tt < m && b < nb;
-      cp_async16(&sb.x[kb][tt][half * 16], ok ? a.xq + tt * K + b * 32 + half * 16 : a.xq, ok);
+      cp_async16(&sb.x[tt][off * 16], ok ? a.xq + tt * K + b0 * 32 + off * 16 : a.xq, ok);
     }
     for (int i = tid; i < SBN * SKB / 2; i += kSkThreads) {  // two scales per copy (the run is padded to 8)
       const int rr = i / (SKB / 2), pr = i % (SKB / 2);
@@ -256,18 +261,18 @@ __global__ void __launch_bounds__(kSkThreads) k_gemm_skinny(const GemmArgs a) {
     const Stage &cur = st[sidx % SNS];
 #pragma unroll 4
     for (int kb = 0; kb < SKB; kb++) {
-      const uint32_t alo0 = *(const uint32_t *)&cur.x[kb][g][4 * q];
-      const uint32_t ahi0 = *(const uint32_t *)&cur.x[kb][g][16 + 4 * q];
-      const uint32_t alo1 = HI ? *(const uint32_t *)&cur.x[kb][g + 8][4 * q] : 0u;
-      const uint32_t ahi1 = HI ? *(const uint32_t *)&cur.x[kb][g + 8][16 + 4 * q] : 0u;
+      const uint32_t alo0 = *(const uint32_t *)&cur.x[g][kb * 32 + 4 * q];
+      const uint32_t ahi0 = *(const uint32_t *)&cur.x[g][kb * 32 + 16 + 4 * q];
+      const uint32_t alo1 = HI ? *(const uint32_t *)&cur.x[g + 8][kb * 32 + 4 * q] : 0u;
+      const uint32_t ahi1 = HI ? *(const uint32_t *)&cur.x[g + 8][kb * 32 + 16 + 4 * q] : 0u;
       uint32_t blo, bhi;
       if (QUANT == JAL_Q4_0) {
-        const uint32_t w = *(const uint32_t *)&cur.w[kb][rb][4 * q];
+        const uint32_t w = *(const uint32_t *)&cur.w[rb][kb * 16 + 4 * q];
         blo = nib_s8(w & 0x0F0F0F0Fu);
         bhi = nib_s8((w >> 4) & 0x0F0F0F0Fu);
       } else {
-        blo = *(const uint32_t *)&cur.w[kb][rb][4 * q];
-        bhi = *(const uint32_t *)&cur.w[kb][rb][16 + 4 * q];
+        blo = *(const uint32_t *)&cur.w[rb][kb * 32 + 4 * q];
+        bhi = *(const uint32_t *)&cur.w[rb][kb * 32 + 16 + 4 * q];
       }
       int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
       mma_s8_16816(c0, alo0, alo1, blo);

@@ -26,9 +26,6 @@
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
-#include <map>
-#include <mutex>
-
 #include "attn_dev.cuh"
 #include "common.hpp"
 #include "dev_util.cuh"
@@ -312,7 +309,11 @@ int xattn_cluster_size(int head_dim, int f16, int G, int n_kv, int64_t n_ctx) {
     const int per_cap = (int)((n_ctx + cs - 1) / cs);
     const size_t smem = xattn_layout(per_cap, (int)n_ctx).total;
     if (smem + 8 * 1024 > kSmemCap) continue;  // + static shared memory
-    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    {  // only ever raise the limit: contexts created earlier may launch larger shares
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess || (size_t)fa.maxDynamicSharedSizeBytes < smem)
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
     if (cs > 8) cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cs);
@@ -363,15 +364,10 @@ void launch_xattn_decode(const AttnDecodeArgs &a, int64_t n_ctx, cudaStream_t s)
     fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: n_ctx %lld does not fit", (long long)n_ctx);
   if (R < 8) fail(JAL_ERR_CAPABILITY_MISMATCH, "reference-order decode attention: page size %lld not a multiple of 8",
                   (long long)a.kv.page_size);
-  {  // the kernel's shared-memory limit covers the largest share launched so far
-    static std::mutex mu;
-    static std::map<const void *, size_t> set;
-    std::lock_guard<std::mutex> lk(mu);
-    size_t &cur = set[fn];
-    if (smem > cur) {
+  {  // raise the kernel's shared-memory limit when this share needs more
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, fn) == cudaSuccess && (size_t)fa.maxDynamicSharedSizeBytes < smem)
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      cur = smem;
-    }
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.kv.n_kv * cs));
