@@ -250,6 +250,8 @@ def reference_arm(args):
 def profile_mode(args):
     """Small fixed workloads for ncu (no JSON line):
       gemv   - four launches of the 14336x4096 Q4_0 decode GEMV (M = 1);
+      skinny - four launches of the 3584x18944 Q8_0 GEMM at M = 4 (the
+               batched decode's down projection of the Qwen2-7B shape);
       decode - Llama-3-8B Q4_0, 32-token prompt, two decode steps between
                cudaProfilerStart / Stop;
       attn   - the same attention geometry with 2 layers, a --prefill prompt
@@ -263,6 +265,17 @@ def profile_mode(args):
     jal = load_jal()
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
+    if args.profile == "skinny":
+        rows, cols, m = 3584, 18944, 4  # Qwen2-7B down projection at batch 4, Q8_0
+        raw = jal.synth_matrix(jal.Q8_0, rows, cols, seed=SEED, name="profile.skinny")
+        mat = jal.CachedMatrix.repack(raw, jal.Q8_0, rows, cols)
+        x = torch.from_numpy(jal.synth_normal(m * cols, seed=SEED, name="profile.act")).cuda()
+        y = torch.zeros(m * rows, dtype=torch.float32, device="cuda")
+        for _ in range(4):
+            mat.gemm(x, m, y, stream)
+        torch.cuda.synchronize()
+        print("profile skinny ok", float(y.abs().sum()))
+        return 0
     if args.profile == "gemv":
         rows, cols = 14336, 4096
         raw = jal.synth_matrix(jal.Q4_0, rows, cols, seed=SEED, name="profile.gemv")
@@ -386,7 +399,7 @@ def main():
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1 ranks: one tensor-parallel model over the N GPUs (strong scaling) "
                          "instead of N independent replicas")
-    ap.add_argument("--profile", choices=["gemv", "decode", "attn", "prefill"],
+    ap.add_argument("--profile", choices=["gemv", "skinny", "decode", "attn", "prefill"],
                     help="run a small fixed workload for ncu instead of the benchmark")
     args = ap.parse_args()
     if args.profile:
