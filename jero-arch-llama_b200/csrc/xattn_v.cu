@@ -39,6 +39,13 @@ constexpr int kProd = 2;      // producer warps
 constexpr int kVT = 32 * (2 + kProd);  // chain warp, producer warps, loader warp
 constexpr int kMaxR = 64;     // positions per stage
 constexpr int kErrCopyWait = 2;
+// Product stage: [32 dims][kPStr] floats, a dim's positions contiguous so the
+// chain lane reads four of them with one 16-byte load.  Position r of dim d
+// sits at column r ^ (8 (d / 8)): the producers' stores (8 positions x 4 dim
+// groups per warp instruction) then hit 32 different banks, and the chain's
+// 16-byte reads (row stride 68 words, 8 lanes per phase) stay conflict-free.
+constexpr int kPStr = kMaxR + 4;
+__device__ __forceinline__ int pcol(int r, int d) { return r ^ (8 * (d >> 3)); }
 
 template <bool F16>
 struct VA {
@@ -61,7 +68,7 @@ __host__ __device__ inline VLayout v_layout(int n_ctx) {
   VLayout L;
   size_t o = 0;
   L.vring = o; o += (size_t)kVS * VA<F16>::STAGE;       // 128-byte aligned pieces (tensor copy targets)
-  L.prod = o; o += (size_t)kPS * kMaxR * 32 * 4;
+  L.prod = o; o += (size_t)kPS * 32 * kPStr * 4;
   L.w = o; o += ((size_t)n_ctx * 4 + 127) / 128 * 128;
   L.srow = o; o += ((size_t)v_max_stages(n_ctx) * 16 + 127) / 128 * 128;
   L.total = o;
@@ -158,30 +165,26 @@ __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUte
       for (int k = 0; k < nv; k++) {
         if (!mbar_wait_bounded(&pfull[ps], pp, a.wait_ns)) ok = false;
         const int n = srow[k].z;
-        const float *pr = prod + (size_t)ps * kMaxR * 32 + lane;
+        const float *pr = prod + ((size_t)ps * 32 + lane) * kPStr;  // this dim's row
+        const int sw = 8 * (lane >> 3);
         if (n == kMaxR) {  // a full stage: block b + 1's loads go out before block b's adds
-          float x[2][16];
+          float4 x[2][4];
 #pragma unroll
-          for (int u = 0; u < 16; u++) x[0][u] = pr[u * 32];
+          for (int u = 0; u < 4; u++) x[0][u] = *(const float4 *)(pr + ((4 * u) ^ sw));
 #pragma unroll
           for (int b = 0; b < kMaxR / 16; b++) {
             if (b + 1 < kMaxR / 16) {
 #pragma unroll
-              for (int u = 0; u < 16; u++) x[(b + 1) & 1][u] = pr[((b + 1) * 16 + u) * 32];
+              for (int u = 0; u < 4; u++) x[(b + 1) & 1][u] = *(const float4 *)(pr + ((16 * (b + 1) + 4 * u) ^ sw));
             }
 #pragma unroll
-            for (int u = 0; u < 16; u++) o = __fadd_rn(o, x[b & 1][u]);
+            for (int u = 0; u < 4; u++) {
+              const float4 v = x[b & 1][u];
+              o = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(o, v.x), v.y), v.z), v.w);
+            }
           }
         } else {
-          int r = 0;
-          for (; r + 16 <= n; r += 16) {
-            float x[16];
-#pragma unroll
-            for (int u = 0; u < 16; u++) x[u] = pr[(r + u) * 32];
-#pragma unroll
-            for (int u = 0; u < 16; u++) o = __fadd_rn(o, x[u]);
-          }
-          for (; r < n; r++) o = __fadd_rn(o, pr[r * 32]);
+          for (int r = 0; r < n; r++) o = __fadd_rn(o, pr[r ^ sw]);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&pempty[ps]);
@@ -206,7 +209,7 @@ __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUte
         if (k >= kPS && !mbar_wait_bounded(&pempty[ps], pp ^ 1u, a.wait_ns)) ok = false;
         const int4 st = srow[k];
         const char *vsrc = vring + vs * A::STAGE;
-        float *dst = prod + (size_t)ps * kMaxR * 32;
+        float *dst = prod + (size_t)ps * 32 * kPStr;
         const float *wst = w_s + (st.y - lo);
         auto make = [&](int r, uint4 raw, float wv) {  // products of position r, dims CH q .. CH q + CH - 1
           float pv[A::CH];
@@ -225,8 +228,10 @@ __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUte
             pv[3] = __fmul_rn(wv, __uint_as_float(raw.w));
           }
 #pragma unroll
-          for (int j = 0; j < A::CH; j += 4)
-            *(float4 *)(dst + r * 32 + A::CH * q + j) = make_float4(pv[j], pv[j + 1], pv[j + 2], pv[j + 3]);
+          for (int j = 0; j < A::CH; j++) {
+            const int d = A::CH * q + j;
+            dst[d * kPStr + pcol(r, d)] = pv[j];
+          }
         };
         if (st.z == kMaxR) {  // a full stage: all of this warp's loads first, then the products
           constexpr int GPP = kMaxR / A::RPG / kProd;  // position groups per producer warp
