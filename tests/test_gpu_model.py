@@ -410,8 +410,9 @@ def test_llama3_70b_shaped_two_layers(jal, oracle, torch_cuda):
 def _batch_vs_single(jal, recipe, cache, prompts, n_steps, om=None, n_ctx=256):
     """Decode the prompts' sequences together with jal_decode_batch and,
     separately, each alone with jal_decode_step: every step's batched rows
-    must equal the single-sequence logits bit for bit; with an oracle the
-    first sequence is also held to the FAST bars."""
+    must equal the single-sequence logits bit for bit; with an oracle every
+    sequence is also run through the oracle on its own and held to the FAST
+    bars."""
     mk = lambda: new_ctx(jal, recipe, cache, n_ctx=n_ctx, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
     bat, ref = [mk() for _ in prompts], [mk() for _ in prompts]
     toks = []
@@ -419,29 +420,33 @@ def _batch_vs_single(jal, recipe, cache, prompts, n_steps, om=None, n_ctx=256):
         lb, lr = b.prefill_step(p, 0), r.prefill_step(p, 0)
         assert np.array_equal(lb, lr)
         toks.append(int(np.argmax(lb)))
+    kvos = []
     if om is not None:
-        kvo = om.new_kv(n_ctx)
-        om.prefill(kvo, n_ctx, prompts[0], 0)
+        for p in prompts:
+            kvos.append(om.new_kv(n_ctx))
+            om.prefill(kvos[-1], n_ctx, p, 0)
     for step in range(n_steps):
         lg = jal.decode_batch(bat, toks)
         for i, r in enumerate(ref):
             li = r.decode_step(toks[i])
             assert np.array_equal(lg[i], li), f"step {step} sequence {i}: batched row differs from the single step"
-        if om is not None:
-            lo = om.decode(kvo, n_ctx, toks[0], len(prompts[0]) + step)
-            assert np.max(np.abs(lo - lg[0])) <= LOGIT_ATOL
+        for i, kvo in enumerate(kvos):
+            lo = om.decode(kvo, n_ctx, toks[i], len(prompts[i]) + step)
+            assert np.max(np.abs(lo - lg[i])) <= LOGIT_ATOL, f"step {step} sequence {i} vs oracle"
+            assert int(np.argmax(lo)) == int(np.argmax(lg[i]))
         toks = [int(np.argmax(lg[i])) for i in range(len(prompts))]
     assert all(b.position() == len(p) + n_steps for b, p in zip(bat, prompts))
 
 
 def test_batched_decode_of_independent_sequences(jal, oracle, torch_cuda):
-    """jal_decode_batch on the tiny Llama: three sequences with prompts of
-    16, 5 and 30 tokens step together for 12 greedy steps (f16 KV, FAST);
-    each row equals its sequence decoded alone, the first tracks the oracle;
-    contexts that share a KV cache or run another numerics are refused."""
+    """jal_decode_batch on the tiny Llama at batch 4: sequences with prompts
+    of 16, 5, 30 and 11 tokens step together for 12 greedy steps (f16 KV,
+    FAST); each row equals its sequence decoded alone and the oracle's run of
+    that sequence (logits and greedy token); contexts that share a KV cache
+    or run another numerics are refused."""
     spec = jal.SynthSpec()
     _, om, recipe, cache, _ = make(jal, oracle, spec, seed=31, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
-    prompts = [prompt_of(21, 16), prompt_of(22, 5), prompt_of(23, 30)]
+    prompts = [prompt_of(21, 16), prompt_of(22, 5), prompt_of(23, 30), prompt_of(24, 11)]
     _batch_vs_single(jal, recipe, cache, prompts, 12, om=om)
     c1 = new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
     with pytest.raises(jal.K3Error):
