@@ -82,10 +82,17 @@ size_t jal_cached_matrix_aligned_bytes(const jal_cached_matrix *m);
  * (r%8)*16+t = q[r][ch*16+t]; scales[((r/8)*groups+g)*8 + r%8] as f32 from
  * f16_to_f32_finite.  Host output buffers; lengths are element counts:
  * tiles_len >= ceil(rows/8)*cols/16*128, scales_len >= ceil(rows/8)*groups*8.
- * Used to prove the repack bit-exact. */
+ * groups = cols/32, or cols/16 for Q6_K (BlockScaledI8 storage of the
+ * K-quants, unpack_row_i8, repack_cache.rs:890-993).  Used to prove the
+ * repack bit-exact. */
 int jal_cached_matrix_export_ref_layout(const jal_cached_matrix *m,
                                         int8_t *tiles, size_t tiles_len,
                                         float *scales, size_t scales_len);
+/* The group mins of a Q4_K / Q5_K repack (BlockScaledI8 mins,
+ * repack_cache.rs:639-694, 890-950) in the same [(r/8)*groups+g][r%8]
+ * layout: mins_len >= ceil(rows/8)*(cols/32)*8. */
+int jal_cached_matrix_export_ref_mins(const jal_cached_matrix *m, float *mins,
+                                      size_t mins_len);
 
 /* CachedMatrix::project_batch / gemm_rows (repack_cache.rs:1709-1787):
  * quantize the [m, cols] f32 activations per 32-block (QuantizedActQ8,

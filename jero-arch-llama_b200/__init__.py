@@ -191,6 +191,7 @@ _SIGS = {
     "jal_prefill_step": (C.c_int, [_P, _P, _SZ, _SZ, C.c_int, _P, _SZ]),
     "jal_decode_step": (C.c_int, [_P, C.c_uint32, _P, _SZ]),
     "jal_decode_greedy": (C.c_int, [_P, C.c_uint32, _SZ, _P]),
+    "jal_cached_matrix_export_ref_mins": (C.c_int, [_P, _P, _SZ]),
     "jal_decode_batch": (C.c_int, [_P, _SZ, _P, _P, _SZ]),
     "jal_context_batch_logits_device": (C.c_int, [_P, C.POINTER(_P)]),
     "jal_context_export_kv": (C.c_int, [_P, _SZ, _P, _SZ]),
@@ -311,11 +312,19 @@ class CachedMatrix:
         import numpy as np
         rows, cols = self.rows(), self.cols()
         nt = (rows + 7) // 8
+        group = 16 if self.quant() == Q6_K else 32
         tiles = np.zeros(nt * (cols // 16) * 128, dtype=np.int8)
-        scales = np.zeros(nt * (cols // 32) * 8, dtype=np.float32)
+        scales = np.zeros(nt * (cols // group) * 8, dtype=np.float32)
         _check(lib().jal_cached_matrix_export_ref_layout(self._h, tiles.ctypes.data, tiles.size,
                                                          scales.ctypes.data, scales.size))
         return tiles, scales
+
+    def export_ref_mins(self):
+        """Group mins (f32, Q4_K / Q5_K) in the reference's portable layout."""
+        import numpy as np
+        mins = np.zeros(((self.rows() + 7) // 8) * (self.cols() // 32) * 8, dtype=np.float32)
+        _check(lib().jal_cached_matrix_export_ref_mins(self._h, mins.ctypes.data, mins.size))
+        return mins
 
     def gemm(self, x, m: int, y, stream=None) -> None:
         """project_batch (repack_cache.rs:1724): y[m, rows] = quant(x[m, cols]) . W^T."""

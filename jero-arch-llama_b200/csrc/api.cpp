@@ -115,8 +115,15 @@ int jal_cached_matrix_export_ref_layout(const jal_cached_matrix *m, int8_t *tile
     NEED(tiles);
     NEED(scales);
     const DevMat &w = m->m.dm;
+    if (kquant(w.quant)) {
+      const size_t n_tiles = (size_t)(w.rows + 7) / 8, nt = n_tiles * (w.cols / 16) * 128,
+                   ns = n_tiles * (w.cols / kquant_group(w.quant)) * 8;
+      if (tiles_len < nt || scales_len < ns) fail(JAL_ERR_TENSOR_BOUNDS, "export buffers too small (%zu/%zu needed)", nt, ns);
+      export_kquant_ref(w, tiles, scales, nullptr);
+      return;
+    }
     if (w.quant != JAL_Q4_0 && w.quant != JAL_Q8_0)
-      fail(JAL_ERR_CAPABILITY_MISMATCH, "export is defined for block-scaled Q4_0/Q8_0 matrices");
+      fail(JAL_ERR_CAPABILITY_MISMATCH, "export is defined for block-scaled Q4_0/Q8_0 and K-quant matrices");
     size_t n_tiles = (size_t)(w.rows + 7) / 8, nt = n_tiles * (w.cols / 16) * 128, ns = n_tiles * (w.cols / 32) * 8;
     if (tiles_len < nt || scales_len < ns) fail(JAL_ERR_TENSOR_BOUNDS, "export buffers too small (%zu/%zu needed)", nt, ns);
     DevBuffer dt(nt), ds(ns * 4);
@@ -124,6 +131,19 @@ int jal_cached_matrix_export_ref_layout(const jal_cached_matrix *m, int8_t *tile
     JAL_CUDA(cudaGetLastError());
     JAL_CUDA(cudaMemcpy(tiles, dt.ptr, nt, cudaMemcpyDeviceToHost));
     JAL_CUDA(cudaMemcpy(scales, ds.ptr, ns * 4, cudaMemcpyDeviceToHost));
+  });
+}
+
+int jal_cached_matrix_export_ref_mins(const jal_cached_matrix *m, float *mins, size_t mins_len) {
+  return guard([&] {
+    NEED(m);
+    NEED(mins);
+    const DevMat &w = m->m.dm;
+    if (w.quant != JAL_Q4_K && w.quant != JAL_Q5_K)
+      fail(JAL_ERR_CAPABILITY_MISMATCH, "group mins exist for Q4_K / Q5_K matrices only");
+    const size_t ns = (size_t)(w.rows + 7) / 8 * (w.cols / 32) * 8;
+    if (mins_len < ns) fail(JAL_ERR_TENSOR_BOUNDS, "mins buffer too small (%zu needed)", ns);
+    export_kquant_ref(w, nullptr, nullptr, mins);
   });
 }
 
@@ -138,8 +158,18 @@ int jal_cached_matrix_gemm(const jal_cached_matrix *mat, const float *x, size_t 
     NEED(x);
     NEED(y);
     if (m == 0) return;
-    check_block_scaled(mat);
     const DevMat &w = mat->m.dm;
+    if (kquant(w.quant)) {
+      cudaStream_t s = as_stream(stream);
+      const int64_t K = w.cols, nb = K / 32;
+      DevBuffer q8((size_t)m * K), sc((size_t)m * nb * 4);
+      launch_act_quant(x, (int64_t)m, K, K, q8.as<int8_t>(), sc.as<float>(), s);
+      launch_kq_gemm(w, x, q8.as<int8_t>(), sc.as<float>(), (int64_t)m, y, s);
+      JAL_CUDA(cudaGetLastError());
+      JAL_CUDA(cudaStreamSynchronize(s));
+      return;
+    }
+    check_block_scaled(mat);
     cudaStream_t s = as_stream(stream);
     int64_t K = w.cols, nb = K / 32;
     DevBuffer q8((size_t)m * K), sc((size_t)m * nb * 4);

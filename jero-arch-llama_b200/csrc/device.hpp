@@ -25,6 +25,12 @@ struct DevMat {
   const void *dense = nullptr;  // dense rows in their GGUF element type (cols stride)
   int64_t qs_stride = 0;  // bytes per row (quants + scales)
   int64_t d_stride = 0;   // row stride of d in halves (qs_stride / 2)
+  // K-quant layout (JAL_Q4_K / Q5_K / Q6_K): qs holds one int8 quant per
+  // element (qs_stride bytes per row); ks / km the f32 scale / min of each
+  // group of 32 (16 for Q6_K) elements, k_stride floats per row; km null for
+  // Q6_K.
+  const float *ks = nullptr, *km = nullptr;
+  int64_t k_stride = 0;
 };
 
 inline int64_t d_stride_for(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
@@ -119,6 +125,17 @@ void launch_xgemv(const GemvArgs &a, cudaStream_t s);
 void launch_repack(const uint8_t *raw, int quant, int64_t rows, int64_t cols, uint8_t *qs, uint16_t *d,
                    int64_t qs_stride, int64_t d_stride, cudaStream_t s);
 void launch_export_ref(const DevMat &w, int8_t *tiles, float *scales, cudaStream_t s);
+// K-quant matrices (kquant.cu).
+bool kquant(int quant);
+int kquant_group(int quant);  // elements per scale group: 32, or 16 for Q6_K
+void launch_repack_kquant(const uint8_t *raw, int quant, int64_t rows, int64_t cols, int8_t *qs, int64_t qs_stride,
+                          float *ks, float *km, int64_t k_stride, cudaStream_t s);
+// y[m][rows] in the reference's order from the f32 activation x (for the
+// group sums) and its QuantizedActQ8 rows xq / xs.
+void launch_kq_gemm(const DevMat &w, const float *x, const int8_t *xq, const float *xs, int64_t m, float *y,
+                    cudaStream_t s);
+// Host copies of the reference's portable layout (tiles, scales, mins; any may be null).
+void export_kquant_ref(const DevMat &w, int8_t *tiles, float *scales, float *mins);
 void launch_act_quant(const float *x, int64_t m, int64_t k, int64_t x_stride, int8_t *q8, float *scales,
                       cudaStream_t s);
 void launch_quantize_row_q8_0(const float *x, int64_t n, void *blocks, cudaStream_t s);

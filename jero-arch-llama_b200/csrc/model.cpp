@@ -425,6 +425,37 @@ void repack_stacked(const std::vector<const uint8_t *> &raws, const std::vector<
     }
     return;
   }
+  if (kquant(quant)) {
+    if (cols % 256) fail(JAL_ERR_TENSOR_BOUNDS, "cols %llu not a multiple of 256", (unsigned long long)cols);
+    const int64_t ng = (int64_t)cols / kquant_group(quant), row_q = (int64_t)cols;
+    const bool mins = quant != JAL_Q6_K;
+    DevBufferPtr bq = alloc((size_t)total * row_q), bs = alloc((size_t)total * ng * 4);
+    DevBufferPtr bm = mins ? alloc((size_t)total * ng * 4) : nullptr;
+    storage.push_back(bq);
+    storage.push_back(bs);
+    if (bm) storage.push_back(bm);
+    stacked = DevMat{};
+    stacked.quant = quant; stacked.rows = (int64_t)total; stacked.cols = (int64_t)cols;
+    stacked.qs = bq->as<uint8_t>(); stacked.qs_stride = row_q;
+    stacked.ks = bs->as<float>(); stacked.km = bm ? bm->as<float>() : nullptr; stacked.k_stride = ng;
+    uint64_t r0 = 0;
+    for (size_t i = 0; i < raws.size(); i++) {
+      launch_repack_kquant(raws[i], quant, (int64_t)rows[i], (int64_t)cols, (int8_t *)(bq->as<uint8_t>() + r0 * row_q),
+                           row_q, bs->as<float>() + r0 * ng, bm ? bm->as<float>() + r0 * ng : nullptr, ng, s);
+      JAL_CUDA(cudaGetLastError());
+      CachedMatrix m;
+      m.quant = quant; m.rows = rows[i]; m.cols = cols;
+      m.dm = stacked;
+      m.dm.rows = (int64_t)rows[i];
+      m.dm.qs = stacked.qs + r0 * row_q;
+      m.dm.ks = stacked.ks + r0 * ng;
+      m.dm.km = stacked.km ? stacked.km + r0 * ng : nullptr;
+      m.aligned_bytes = (size_t)rows[i] * (row_q + ng * 4 * (mins ? 2 : 1));
+      parts.push_back(m);
+      r0 += rows[i];
+    }
+    return;
+  }
   if (dense_quant(quant)) {
     // Dense rows keep their GGUF element type (repack_dense's sanitising
     // happens on load in the dense kernels).

@@ -134,6 +134,10 @@ class RepackedWeight:
         n = self.s.n_tiles * self.s.scale_groups * 8
         return np.ctypeslib.as_array(C.cast(self.s.scales, C.POINTER(C.c_float)), shape=(n,)).copy()
 
+    def mins(self):
+        n = self.s.n_tiles * self.s.scale_groups * 8
+        return np.ctypeslib.as_array(C.cast(self.s.mins, C.POINTER(C.c_float)), shape=(n,)).copy()
+
     def project_batch(self, act, m, nthreads=1):
         act = np.ascontiguousarray(act, dtype=np.float32)
         out = np.zeros(m * self.rows, dtype=np.float32)

@@ -344,3 +344,35 @@ def test_rmsnorm_rows_sequential_sum_stress(jal, oracle, torch_cuda):
         want = oracle.rmsnorm_row(x, w, 1e-5)
         got = out.cpu().numpy()
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"row {i} (n={n})"
+
+
+@pytest.mark.parametrize("quant_name", ["Q4_K", "Q5_K", "Q6_K"])
+def test_kquant_repack_export_and_projection_bit_exact(jal, oracle, torch_cuda, quant_name):
+    """K-quant matrices in the repacked path (unpack_row_i8, repack_cache.rs:
+    890-993; the BlockScaledI8 fold with its min term, :739-783): 300 rows
+    (a partial 8-row tile) x 1024 columns of random super-blocks, one with an
+    Inf scale; the exported tiles, scales and mins equal the oracle's repack
+    bit for bit, and projections at M = 1 and 3 (activations with a NaN and an
+    Inf, which the group sums read as zero) equal the oracle's."""
+    torch = torch_cuda
+    quant = getattr(jal, quant_name)
+    rows, cols = 300, 1024
+    raw = _raw_superblock_rows(jal, quant, rows, cols, 71)
+    mat = jal.CachedMatrix.repack(raw, quant, rows, cols)
+    assert mat.quant() == quant and mat.rows() == rows and mat.cols() == cols
+    ref = oracle.RepackedWeight(raw, quant, rows, cols)
+    tiles, scales = mat.export_ref_layout()
+    assert np.array_equal(tiles, ref.tiles())
+    assert np.array_equal(scales.view(np.uint32), ref.scales().view(np.uint32))
+    if quant != jal.Q6_K:
+        assert np.array_equal(mat.export_ref_mins().view(np.uint32), ref.mins().view(np.uint32))
+    for m in (1, 3):
+        x = jal.synth_normal(m * cols, seed=72 + m, name="kq.act").copy()
+        x[5] = np.nan
+        x[cols + 7 if m > 1 else 9] = np.inf
+        y = torch.zeros(m * rows, dtype=torch.float32, device="cuda")
+        mat.gemm(dev(torch, x), m, y)
+        torch.cuda.synchronize()
+        want = ref.project_batch(x, m)
+        got = y.cpu().numpy().reshape(m, rows)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
