@@ -158,18 +158,37 @@ __global__ void __launch_bounds__(kPT, 1) k_xattn_prefill(const AttnPrefillArgs 
     const int64_t t0 = klo + (int64_t)k * kKT;
     const int n = (int)(khi + 1 - t0 < kKT ? khi + 1 - t0 : kKT);
     if (HD == 128 || jp < 2) {
-#pragma unroll
-      for (int u = 0; u < 2; u++) {
-        const int j = (HD == 128 ? 2 * jp : 2 * jp) + u;
-        if (j >= nq) continue;
-        const int64_t lo_j = qlo[j] > t0 ? qlo[j] : t0, hi_j = qhi[j] < t0 + n - 1 ? qhi[j] : t0 + n - 1;
-        const float *Wj = S + j * smax;
+      // Both chains of the thread walk the tile's keys together: keys in
+      // [a0, b0) belong to both queries, the rest to one of them.  Each
+      // chain still adds its terms in key order.
+      const int j0 = 2 * jp, j1 = 2 * jp + 1;
+      const bool v0 = j0 < nq, v1 = j1 < nq;
+      auto lo_of = [&](int j) { return (int)((qlo[j] > t0 ? qlo[j] : t0) - t0); };
+      auto hi_of = [&](int j) { return (int)((qhi[j] < t0 + n - 1 ? qhi[j] : t0 + n - 1) - t0); };  // inclusive
+      const int l0 = v0 ? lo_of(j0) : n, h0 = v0 ? hi_of(j0) : -1, l1 = v1 ? lo_of(j1) : n, h1 = v1 ? hi_of(j1) : -1;
+      const float *W0 = S + j0 * smax + (int)(t0 - klo), *W1 = S + j1 * smax + (int)(t0 - klo);
+      auto val = [&](int i) {
+        const char *row = vt + i * A::ROW;
+        return F16 ? __half2float(((const __half *)row)[d]) : ((const float *)row)[d];
+      };
+      // Each chain's keys [l, h] of this tile split into the part below the
+      // shared range [slo, shi], the shared range (one V load for both
+      // terms) and the part above it, taken in that order.
+      const int slo = l0 > l1 ? l0 : l1, shi = h0 < h1 ? h0 : h1;
+      if (slo > shi) {
+        for (int i = l0; i <= h0; i++) o[0] = __fadd_rn(o[0], __fmul_rn(W0[i], val(i)));
+        for (int i = l1; i <= h1; i++) o[1] = __fadd_rn(o[1], __fmul_rn(W1[i], val(i)));
+      } else {
+        for (int i = l0; i < slo; i++) o[0] = __fadd_rn(o[0], __fmul_rn(W0[i], val(i)));
+        for (int i = l1; i < slo; i++) o[1] = __fadd_rn(o[1], __fmul_rn(W1[i], val(i)));
 #pragma unroll 4
-        for (int64_t t = lo_j; t <= hi_j; t++) {
-          const char *row = vt + (t - t0) * A::ROW;
-          const float v = F16 ? __half2float(((const __half *)row)[d]) : ((const float *)row)[d];
-          o[u] = __fadd_rn(o[u], __fmul_rn(Wj[t - klo], v));
+        for (int i = slo; i <= shi; i++) {
+          const float v = val(i);
+          o[0] = __fadd_rn(o[0], __fmul_rn(W0[i], v));
+          o[1] = __fadd_rn(o[1], __fmul_rn(W1[i], v));
         }
+        for (int i = shi + 1; i <= h0; i++) o[0] = __fadd_rn(o[0], __fmul_rn(W0[i], val(i)));
+        for (int i = shi + 1; i <= h1; i++) o[1] = __fadd_rn(o[1], __fmul_rn(W1[i], val(i)));
       }
     }
     __syncthreads();
