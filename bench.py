@@ -250,6 +250,10 @@ def reference_arm(args):
 def profile_mode(args):
     """Small fixed workloads for ncu (no JSON line):
       gemv   - four launches of the 14336x4096 Q4_0 decode GEMV (M = 1);
+      trace  - the bench's Llama-3-8B Q4_0 model after a --prefill prompt:
+               the in-graph per-kernel breakdown of the decode step from the
+               kernels' own globaltimer stamps (jal_context_trace_decode_step),
+               median over 5 traced steps (prints a table, no profiler);
       skinny - four launches of the 3584x18944 Q8_0 GEMM at M = 4 (the
                batched decode's down projection of the Qwen2-7B shape);
       decode - Llama-3-8B Q4_0, 32-token prompt, two decode steps between
@@ -265,6 +269,8 @@ def profile_mode(args):
     jal = load_jal()
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
+    if args.profile == "trace":
+        return trace_mode(args, jal, torch, stream)
     if args.profile == "skinny":
         rows, cols, m = 3584, 18944, 4  # Qwen2-7B down projection at batch 4, Q8_0
         raw = jal.synth_matrix(jal.Q8_0, rows, cols, seed=SEED, name="profile.skinny")
@@ -325,6 +331,52 @@ def profile_mode(args):
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     print(f"profile {args.profile} ok")
+    return 0
+
+
+def trace_mode(args, jal, torch, stream):
+    import numpy as np
+    spec = jal.LLAMA3_8B_Q4_0
+    gguf = jal.synth_gguf(spec, SEED)
+    recipe = jal.LlamaRecipe.from_gguf(gguf)
+    cache = recipe.build_repack_cache(gguf)
+    n_prefill = args.prefill
+    ctx = jal.ExecutionContext(recipe, cache, n_ctx=n_prefill + 64, kv_dtype=jal.KV_F16)
+    ctx.set_stream(stream)
+    rng = np.random.Generator(np.random.PCG64(SEED))
+    ctx.prefill_step(rng.integers(0, spec.vocab_size, n_prefill).astype(np.uint32), 0)
+    ctx.decode_greedy(1, 4)
+    L = spec.num_layers
+    roles = ["Q/K/V GEMV", "scores k_xattn", "output k_xattn_v", "O GEMV", "gate/up GEMV", "down GEMV"]
+    runs = []
+    for _ in range(5):
+        t = ctx.trace_decode_step(int(rng.integers(0, spec.vocab_size))).astype(np.float64)
+        runs.append(t)
+    per = {r: {"dur": [], "excl": [], "gap": []} for r in roles + ["LM head"]}
+    spans = []
+    for t in runs:
+        idx = list(range(1, 1 + 6 * L)) + [1 + 6 * L]
+        spans.append((t[idx[-1], 1] - t[1, 0]) / 1e3)
+        prev_end = None
+        for k, i in enumerate(idx):
+            role = "LM head" if i == 1 + 6 * L else roles[(i - 1) % 6]
+            s, e = t[i]
+            per[role]["dur"].append((e - s) / 1e3)
+            if prev_end is not None:
+                per[role]["excl"].append((e - prev_end) / 1e3)
+                per[role]["gap"].append((s - prev_end) / 1e3)
+            prev_end = e
+    print(f"decode step at position ~{n_prefill}: {np.median(spans):.1f} us from the first Q/K/V CTA start to the "
+          f"LM head's end (median of 5 traced steps; embedding and argmax not stamped)")
+    print("| kernel | launches / step | in-kernel us (median) | critical-path us per launch (end to end) | "
+          "critical-path us per step | start - previous end us (median) |")
+    print("|---|---|---|---|---|---|")
+    for role, d in per.items():
+        n = len(d["dur"]) // len(runs)
+        ex = float(np.median(d["excl"])) if d["excl"] else float("nan")
+        tot = float(np.sum(d["excl"])) / len(runs) if d["excl"] else float("nan")
+        gap = float(np.median(d["gap"])) if d["gap"] else float("nan")
+        print(f"| {role} | {n} | {np.median(d['dur']):.2f} | {ex:.2f} | {tot:.1f} | {gap:.2f} |")
     return 0
 
 
@@ -399,7 +451,7 @@ def main():
     ap.add_argument("--tp", action="store_true",
                     help="with N > 1 ranks: one tensor-parallel model over the N GPUs (strong scaling) "
                          "instead of N independent replicas")
-    ap.add_argument("--profile", choices=["gemv", "skinny", "decode", "attn", "prefill"],
+    ap.add_argument("--profile", choices=["gemv", "skinny", "decode", "attn", "prefill", "trace"],
                     help="run a small fixed workload for ncu instead of the benchmark")
     args = ap.parse_args()
     if args.profile:

@@ -38,6 +38,17 @@ int jal_context_test_stall_kv_copy(jal_context *ctx, uint32_t extra_bytes,
 int jal_test_peer_exchange_timeout(const jal_cached_matrix *mat, uint64_t wait_ns,
                                    double *elapsed_ms);
 
+/* Step trace (a diagnostic, not a failure hook): decodes two greedy steps
+ * from `token` at the current position (the position advances by two) with
+ * the FAST single-GPU step captured in a graph whose reference-order kernels
+ * stamp the globaltimer; the second (warm) step's stamps land in out:
+ * out[2 i] = launch i's first CTA start, out[2 i + 1] = its last warp's end
+ * (ns; all ones / 0 for launches that record nothing: the embedding and the
+ * argmax).  *n_launches receives the step's launch count; out_len (elements)
+ * bounds what is copied.  The normal step graph is recaptured afterwards. */
+int jal_context_trace_decode_step(jal_context *ctx, uint32_t token, uint64_t *out,
+                                  size_t out_len, size_t *n_launches);
+
 #ifdef __cplusplus
 }
 #endif

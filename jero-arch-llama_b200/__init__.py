@@ -193,6 +193,7 @@ _SIGS = {
     "jal_decode_greedy": (C.c_int, [_P, C.c_uint32, _SZ, _P]),
     "jal_cached_matrix_export_ref_mins": (C.c_int, [_P, _P, _SZ]),
     "jal_decode_batch": (C.c_int, [_P, _SZ, _P, _P, _SZ]),
+    "jal_context_trace_decode_step": (C.c_int, [_P, C.c_uint32, _P, _SZ, C.POINTER(_SZ)]),
     "jal_context_batch_logits_device": (C.c_int, [_P, C.POINTER(_P)]),
     "jal_context_export_kv": (C.c_int, [_P, _SZ, _P, _SZ]),
     "jal_context_logits_device": (C.c_int, [_P, C.POINTER(_P)]),
@@ -680,6 +681,17 @@ class ExecutionContext:
         p = _P()
         _check(lib().jal_context_logits_device(self._h, C.byref(p)))
         return p.value
+
+    def trace_decode_step(self, token: int):
+        """Two greedy decode steps; the second's per-launch (start, end)
+        globaltimer stamps in ns as a [launches, 2] uint64 array (the
+        embedding and argmax launches read (2**64 - 1, 0)).  jal_test.h."""
+        import numpy as np
+        cap = 4096
+        out = np.zeros(2 * cap, dtype=np.uint64)
+        n = _SZ()
+        _check(lib().jal_context_trace_decode_step(self._h, token, out.ctypes.data, out.size, C.byref(n)))
+        return out[: 2 * min(n.value, cap)].reshape(-1, 2)
 
     def set_stream(self, stream) -> None:
         """Issue this context's work on `stream` (torch stream or cudaStream_t); None = own stream."""

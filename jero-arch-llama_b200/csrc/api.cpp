@@ -852,6 +852,63 @@ int jal_context_test_stall_kv_copy(jal_context *h, uint32_t extra_bytes, uint64_
   });
 }
 
+int jal_context_trace_decode_step(jal_context *h, uint32_t token, uint64_t *out, size_t out_len, size_t *n_launches) {
+  return guard([&] {
+    NEED(h);
+    NEED(out);
+    NEED(n_launches);
+    Context &c = *h->ctx;
+    if (!c.exact) fail(JAL_ERR_CAPABILITY_MISMATCH, "the step trace covers the FAST single-GPU decode step");
+    if (c.position + 1 > c.cfg.n_ctx)
+      fail(JAL_ERR_CONTEXT_LENGTH_EXCEEDED, "requested %llu > n_ctx %llu", (unsigned long long)c.position + 1,
+           (unsigned long long)c.cfg.n_ctx);
+    check_tokens(c, &token, 1);
+    JAL_CUDA(cudaSetDevice(c.cache->device));
+    JAL_CUDA(cudaStreamSynchronize(c.stream));
+    const size_t slots = 2 * (4 + 6 * c.cache->layers.size());
+    if (!c.trace_buf) {
+      c.trace_buf = std::make_shared<DevBuffer>(slots * 8);
+      c.d_trace = c.trace_buf->as<unsigned long long>();
+    }
+    std::vector<uint64_t> init(slots, 0);
+    for (size_t i = 0; i < slots; i += 2) init[i] = ~0ull;
+    JAL_CUDA(cudaMemcpy(c.d_trace, init.data(), slots * 8, cudaMemcpyHostToDevice));
+    auto drop_graph = [&] {
+      if (c.graph) {
+        JAL_CUDA(cudaStreamSynchronize(c.stream));
+        cudaGraphExecDestroy(c.graph);
+        c.graph = nullptr;
+      }
+    };
+    drop_graph();  // recaptured with the trace slots
+    c.trace_on = true;
+    *c.h_pos = (int64_t)c.position;
+    c.h_token[0] = token;
+    JAL_CUDA(cudaMemcpyAsync(c.d_pos, c.h_pos, 8, cudaMemcpyHostToDevice, c.stream));
+    JAL_CUDA(cudaMemcpyAsync(c.d_token, c.h_token, 4, cudaMemcpyHostToDevice, c.stream));
+    try {
+      c.run_decode_step();  // capture and the first replay (which pays the graph upload)
+      JAL_CUDA(cudaStreamSynchronize(c.stream));
+      JAL_CUDA(cudaMemcpy(c.d_trace, init.data(), slots * 8, cudaMemcpyHostToDevice));
+      c.run_decode_step();  // the traced step
+      JAL_CUDA(cudaStreamSynchronize(c.stream));
+    } catch (...) {
+      c.trace_on = false;
+      drop_graph();
+      throw;
+    }
+    c.trace_on = false;
+    drop_graph();
+    const size_t n = std::min(c.launches_per_step, out_len / 2);
+    *n_launches = c.launches_per_step;
+    JAL_CUDA(cudaMemcpy(out, c.d_trace, n * 2 * 8, cudaMemcpyDeviceToHost));
+    enqueue_error_read(c);
+    JAL_CUDA(cudaStreamSynchronize(c.stream));
+    check_device_error(c);
+    c.position += 2;
+  });
+}
+
 int jal_test_peer_exchange_timeout(const jal_cached_matrix *mat, uint64_t wait_ns, double *elapsed_ms) {
   return guard([&] {
     NEED(mat);

@@ -157,6 +157,21 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+
+// Step trace (diagnostic): with t non-null, a kernel records the globaltimer
+// of its first CTA start in t[0] (atomic min; the slot starts at all ones)
+// and of its last warp's exit in t[1] (atomic max; starts at 0).  Declared
+// first in the kernel, so the exit stamp runs on every return path.
+struct KernelTrace {
+  unsigned long long *t;
+  __device__ explicit KernelTrace(unsigned long long *p) : t(p) {
+    if (t && threadIdx.x == 0) atomicMin(t, (unsigned long long)global_ns());
+  }
+  __device__ ~KernelTrace() {
+    if (t && (threadIdx.x & 31) == 0) atomicMax(t + 1, (unsigned long long)global_ns());
+  }
+};
+
 // Waits for the phase with the given parity for at most limit_ns of wall
 // time (0 = kWaitNs); false when the wait gave up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t limit_ns = 0) {

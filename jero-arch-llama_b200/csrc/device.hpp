@@ -98,6 +98,7 @@ struct GemvArgs {
   int grid = 0;                 // CTAs (0 = auto)
   int pdl = 0;                  // launch with programmatic dependent launch
   int64_t pf_bytes = -1;        // L2 prefetch budget per CTA (-1 = default)
+  unsigned long long *trace = nullptr;  // step trace: {first CTA start, last warp end} (ns), see KernelTrace
 };
 
 void launch_gemv(const GemvArgs &a, cudaStream_t s);
@@ -226,6 +227,7 @@ struct AttnDecodeArgs {
   uint32_t test_extra_tx = 0;   // test hook: the first V copy's barrier expects this many bytes more (k_attn_decode)
   float *w_out = nullptr;       // reference-order kernel: [n_heads_q][w_stride] weights e_t / den by position
   int64_t w_stride = 0;
+  unsigned long long *trace = nullptr;  // step trace slot (KernelTrace)
 };
 void launch_attn_decode(const AttnDecodeArgs &a, cudaStream_t s);
 // Reference-order decode attention, scores (xattn.cu): clusters of
@@ -254,6 +256,7 @@ struct AttnVArgs {
   int pdl = 0;
   uint64_t wait_ns = 0;
   uint32_t test_extra_tx = 0;  // test hook: the last V stage's barrier expects this many bytes more
+  unsigned long long *trace = nullptr;  // step trace slot (KernelTrace)
 };
 // Positions per V stage: the largest power of two <= 64 dividing the page size.
 int kv_stage_rows(int64_t page_size);

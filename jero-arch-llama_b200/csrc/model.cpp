@@ -1272,12 +1272,14 @@ void Context::enqueue_exact_step(bool pdl) {
   const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv;
   const float eps = std::max(recipe.rms_eps, 1.0e-7f);
   size_t n = 0;
+  auto tr = [&](size_t i) { return trace_on ? d_trace + 2 * i : nullptr; };
   launch_embed(c.emb_raw->as<uint8_t>(), c.emb_quant, (int64_t)H, (int64_t)c.emb_rows, d_token, 1, hidden, d_err, pdl,
                stream);
   n++;
   for (size_t l = 0; l < c.layers.size(); l++) {
     const Layer &L = c.layers[l];
     GemvArgs qa;
+    qa.trace = tr(n);
     qa.w = L.qkv; qa.rows = (int64_t)(Q + 2 * KV); qa.in_mode = GEMV_IN_NORM;
     qa.x = hidden; qa.x_stride = (int64_t)H; qa.norm_w = L.attn_norm; qa.eps = eps;
     qa.out_mode = GEMV_OUT_STORE; qa.y = qkv; qa.y_stride = (int64_t)(Q + 2 * KV); qa.pdl = pdl;
@@ -1293,26 +1295,31 @@ void Context::enqueue_exact_step(bool pdl) {
     aa.scale = 1.0f / sqrtf((float)g.head_dim);
     aa.n_splits = x_splits;
     aa.w_out = attn_w; aa.w_stride = (int64_t)cfg.n_ctx; aa.err = d_err; aa.pdl = pdl;
+    aa.trace = tr(n + 1);
     launch_xattn_decode(aa, (int64_t)cfg.n_ctx, stream);
     AttnVArgs va;
     va.kv = kv; va.layer = (int64_t)l; va.window = (int64_t)cfg.sliding_window; va.n_heads_q = (int64_t)g.n_heads_q;
     va.d_pos = d_pos; va.w = attn_w; va.w_stride = (int64_t)cfg.n_ctx;
     va.out = attn; va.out_q = attn_q; va.out_s = attn_s; va.err = d_err; va.pdl = pdl;
     va.test_extra_tx = test_stall_tx; va.wait_ns = test_wait_ns;
+    va.trace = tr(n + 2);
     launch_xattn_v(tm_v, va, (int64_t)cfg.n_ctx, stream);
     GemvArgs oa;
     oa.w = L.wo.dm; oa.rows = (int64_t)H; oa.in_mode = GEMV_IN_Q8;
     oa.xq = attn_q; oa.xs = attn_s; oa.xq_stride = (int64_t)Q;
     oa.out_mode = GEMV_OUT_ADD; oa.y = hidden; oa.y_stride = (int64_t)H; oa.bias = L.bo; oa.pdl = pdl;
+    oa.trace = tr(n + 3);
     launch_xgemv(oa, stream);
     GemvArgs ga;
     ga.w = L.gateup; ga.rows = (int64_t)F; ga.in_mode = GEMV_IN_NORM;
     ga.x = hidden; ga.x_stride = (int64_t)H; ga.norm_w = L.ffn_norm; ga.eps = eps;
     ga.out_mode = GEMV_OUT_SWIGLU; ga.y = ffn; ga.y_stride = (int64_t)F; ga.up_offset = (int64_t)F; ga.pdl = pdl;
+    ga.trace = tr(n + 4);
     launch_xgemv(ga, stream);
     GemvArgs da;
     da.w = L.wdown.dm; da.rows = (int64_t)H; da.in_mode = GEMV_IN_F32; da.x = ffn; da.x_stride = (int64_t)F;
     da.out_mode = GEMV_OUT_ADD; da.y = hidden; da.y_stride = (int64_t)H; da.pdl = pdl;
+    da.trace = tr(n + 5);
     launch_xgemv(da, stream);
     n += 6;
   }
@@ -1325,6 +1332,7 @@ void Context::enqueue_exact_step(bool pdl) {
     la.w = c.lm_head.dm; la.rows = (int64_t)c.vocab_size; la.in_mode = GEMV_IN_NORM;
     la.x = hidden; la.x_stride = (int64_t)H; la.norm_w = c.output_norm->as<float>(); la.eps = eps;
     la.out_mode = GEMV_OUT_STORE; la.y = logits; la.y_stride = (int64_t)c.vocab_size; la.pdl = pdl;
+    la.trace = tr(n);
     launch_xgemv(la, stream);
     n++;
   }

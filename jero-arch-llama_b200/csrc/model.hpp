@@ -178,6 +178,11 @@ struct Context {
   // (test_wait_ns) runs out.
   uint32_t test_stall_tx = 0;
   uint64_t test_wait_ns = 0;
+  // Step trace (jal_test.h): with trace_on, the reference-order step's
+  // kernels record {start, end} of launch i in d_trace[2 i], [2 i + 1].
+  bool trace_on = false;
+  unsigned long long *d_trace = nullptr;
+  DevBufferPtr trace_buf;
   // prefill scratch (grown on demand)
   uint64_t pf_cap = 0;
   DevBufferPtr pf_buf;

@@ -97,6 +97,7 @@ __device__ __forceinline__ void chunk_vals(uint4 raw, float (&o)[CH]) {
 
 template <int HD, bool F16, int GP>
 __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int per_cap, int n_ctx, int R) {
+  const KernelTrace trace(a.trace);
   namespace cg = cooperative_groups;
   using A = XA<HD, F16>;
   cg::cluster_group cluster = cg::this_cluster();

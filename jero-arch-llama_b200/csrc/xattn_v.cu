@@ -86,6 +86,7 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
 template <bool F16>
 __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUtensorMap tmv, const AttnVArgs a, int n_ctx,
                                                    int R) {
+  const KernelTrace trace(a.trace);
   using A = VA<F16>;
   extern __shared__ __align__(128) char smem[];
   __shared__ __align__(8) uint64_t vfull[kVS], vempty[kVS], pfull[kPS], pempty[kPS];

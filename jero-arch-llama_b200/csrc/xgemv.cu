@@ -302,6 +302,7 @@ __device__ __forceinline__ void x_terms(const XUnit<QUANT> &u, const int4 *alo, 
 
 template <int QUANT, int OUT>
 __global__ void __launch_bounds__(kNT, 1) k_xgemv(const GemvArgs a) {
+  const KernelTrace trace(a.trace);
   constexpr int DEPTH = XCfg<QUANT>::DEPTH;
   constexpr int PAIR = OUT == GEMV_OUT_SWIGLU ? 2 : 1;  // physical rows per logical row
   extern __shared__ __align__(16) char smem[];

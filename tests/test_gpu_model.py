@@ -470,6 +470,31 @@ def test_batched_decode_qwen2_7b_shaped_batch_4(jal, torch_cuda):
     _batch_vs_single(jal, recipe, cache, prompts, 8)
 
 
+def test_decode_step_trace_stamps(jal, torch_cuda):
+    """jal_context_trace_decode_step: every stamped launch of the traced step
+    starts before it ends, launches start in stream order, the position
+    advances by two, and decoding afterwards still matches a context that
+    never traced."""
+    spec = jal.SynthSpec()
+    buf = jal.synth_gguf(spec, 41)
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    cache = recipe.build_repack_cache(buf)
+    mk = lambda: new_ctx(jal, recipe, cache, kv_dtype=jal.KV_F16, numerics=jal.NUMERICS_FAST)
+    a, b = mk(), mk()
+    p = prompt_of(5)
+    a.prefill_step(p, 0)
+    b.prefill_step(p, 0)
+    t = a.trace_decode_step(7)
+    assert a.position() == len(p) + 2 and t.shape[0] == a.launches_per_step()
+    stamped = [i for i in range(t.shape[0]) if t[i, 1] != 0]
+    assert len(stamped) == 6 * spec.num_layers + 1
+    assert all(t[i, 0] < t[i, 1] for i in stamped)
+    assert all(t[i, 0] <= t[j, 0] for i, j in zip(stamped, stamped[1:]))
+    toks = b.decode_greedy(7, 2)
+    la, lb = a.decode_step(int(toks[1])), b.decode_step(int(toks[1]))
+    assert np.array_equal(la, lb)
+
+
 def test_caller_owned_kv_cache_shared_by_two_contexts(jal, oracle, torch_cuda):
     """A KV cache allocated by the caller (the reference's KvCacheView) and
     two contexts over it: A prefills, is freed, and B resumes decoding at
