@@ -360,12 +360,25 @@ def trace_mode(args, jal, torch, stream):
         prev_end = None
         for k, i in enumerate(idx):
             role = "LM head" if i == 1 + 6 * L else roles[(i - 1) % 6]
-            s, e = t[i]
+            s, e = t[i, 0], t[i, 1]
             per[role]["dur"].append((e - s) / 1e3)
             if prev_end is not None:
                 per[role]["excl"].append((e - prev_end) / 1e3)
                 per[role]["gap"].append((s - prev_end) / 1e3)
             prev_end = e
+    # Phase marks of the attention kernels, us after the previous launch's end.
+    names = {1: ["grid dependency resolved", "scores done", "maxima exchanged", "exp terms in place",
+                 "denominator"],
+             2: ["grid dependency resolved", "weights in shared memory", "first product stage ready",
+                 "chain done"]}
+    marks = {1: [[] for _ in range(5)], 2: [[] for _ in range(4)]}
+    for t in runs:
+        for l in range(L):
+            for r in (1, 2):
+                i = 1 + 6 * l + r
+                for k in range(len(names[r])):
+                    if t[i, 2 + k] > 0:
+                        marks[r][k].append((t[i, 2 + k] - t[i - 1, 1]) / 1e3)
     print(f"decode step at position ~{n_prefill}: {np.median(spans):.1f} us from the first Q/K/V CTA start to the "
           f"LM head's end (median of 5 traced steps; embedding and argmax not stamped)")
     print("| kernel | launches / step | in-kernel us (median) | critical-path us per launch (end to end) | "
@@ -377,6 +390,9 @@ def trace_mode(args, jal, torch, stream):
         tot = float(np.sum(d["excl"])) / len(runs) if d["excl"] else float("nan")
         gap = float(np.median(d["gap"])) if d["gap"] else float("nan")
         print(f"| {role} | {n} | {np.median(d['dur']):.2f} | {ex:.2f} | {tot:.1f} | {gap:.2f} |")
+    for r, kname in ((1, "scores k_xattn"), (2, "output k_xattn_v")):
+        print(f"{kname} phases (latest CTA, us after the previous kernel's end, median): " +
+              ", ".join(f"{nm} {np.median(v):.2f}" for nm, v in zip(names[r], marks[r]) if v))
     return 0
 
 

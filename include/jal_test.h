@@ -41,11 +41,14 @@ int jal_test_peer_exchange_timeout(const jal_cached_matrix *mat, uint64_t wait_n
 /* Step trace (a diagnostic, not a failure hook): decodes two greedy steps
  * from `token` at the current position (the position advances by two) with
  * the FAST single-GPU step captured in a graph whose reference-order kernels
- * stamp the globaltimer; the second (warm) step's stamps land in out:
- * out[2 i] = launch i's first CTA start, out[2 i + 1] = its last warp's end
- * (ns; all ones / 0 for launches that record nothing: the embedding and the
- * argmax).  *n_launches receives the step's launch count; out_len (elements)
- * bounds what is copied.  The normal step graph is recaptured afterwards. */
+ * stamp the globaltimer; the second (warm) step's stamps land in out, 8 per
+ * launch: out[8 i] = launch i's first CTA start, out[8 i + 1] = its last
+ * warp's end, out[8 i + 2 + k] = the latest time any of its CTAs reached
+ * phase k (0 = not recorded; the attention kernels mark the grid-dependency
+ * wait, their phase boundaries and their chains).  Launches that record
+ * nothing (the embedding, the argmax) read all ones / 0.  *n_launches receives
+ * the step's launch count; out_len (elements) bounds what is copied.  The
+ * normal step graph is recaptured afterwards. */
 int jal_context_trace_decode_step(jal_context *ctx, uint32_t token, uint64_t *out,
                                   size_t out_len, size_t *n_launches);
 

@@ -683,15 +683,15 @@ class ExecutionContext:
         return p.value
 
     def trace_decode_step(self, token: int):
-        """Two greedy decode steps; the second's per-launch (start, end)
-        globaltimer stamps in ns as a [launches, 2] uint64 array (the
-        embedding and argmax launches read (2**64 - 1, 0)).  jal_test.h."""
+        """Two greedy decode steps; the second's per-launch globaltimer stamps
+        in ns as a [launches, 8] uint64 array: start, end, then the phase
+        marks (0 where none).  jal_test.h."""
         import numpy as np
         cap = 4096
-        out = np.zeros(2 * cap, dtype=np.uint64)
+        out = np.zeros(8 * cap, dtype=np.uint64)
         n = _SZ()
         _check(lib().jal_context_trace_decode_step(self._h, token, out.ctypes.data, out.size, C.byref(n)))
-        return out[: 2 * min(n.value, cap)].reshape(-1, 2)
+        return out[: 8 * min(n.value, cap)].reshape(-1, 8)
 
     def set_stream(self, stream) -> None:
         """Issue this context's work on `stream` (torch stream or cudaStream_t); None = own stream."""

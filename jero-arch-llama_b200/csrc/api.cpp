@@ -865,13 +865,13 @@ int jal_context_trace_decode_step(jal_context *h, uint32_t token, uint64_t *out,
     check_tokens(c, &token, 1);
     JAL_CUDA(cudaSetDevice(c.cache->device));
     JAL_CUDA(cudaStreamSynchronize(c.stream));
-    const size_t slots = 2 * (4 + 6 * c.cache->layers.size());
+    const size_t slots = kTraceSlots * (4 + 6 * c.cache->layers.size());
     if (!c.trace_buf) {
       c.trace_buf = std::make_shared<DevBuffer>(slots * 8);
       c.d_trace = c.trace_buf->as<unsigned long long>();
     }
     std::vector<uint64_t> init(slots, 0);
-    for (size_t i = 0; i < slots; i += 2) init[i] = ~0ull;
+    for (size_t i = 0; i < slots; i += kTraceSlots) init[i] = ~0ull;
     JAL_CUDA(cudaMemcpy(c.d_trace, init.data(), slots * 8, cudaMemcpyHostToDevice));
     auto drop_graph = [&] {
       if (c.graph) {
@@ -899,9 +899,9 @@ int jal_context_trace_decode_step(jal_context *h, uint32_t token, uint64_t *out,
     }
     c.trace_on = false;
     drop_graph();
-    const size_t n = std::min(c.launches_per_step, out_len / 2);
+    const size_t n = std::min(c.launches_per_step, out_len / kTraceSlots);
     *n_launches = c.launches_per_step;
-    JAL_CUDA(cudaMemcpy(out, c.d_trace, n * 2 * 8, cudaMemcpyDeviceToHost));
+    JAL_CUDA(cudaMemcpy(out, c.d_trace, n * kTraceSlots * 8, cudaMemcpyDeviceToHost));
     enqueue_error_read(c);
     JAL_CUDA(cudaStreamSynchronize(c.stream));
     check_device_error(c);

@@ -158,10 +158,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Step trace (diagnostic): with t non-null, a kernel records the globaltimer
-// of its first CTA start in t[0] (atomic min; the slot starts at all ones)
-// and of its last warp's exit in t[1] (atomic max; starts at 0).  Declared
-// first in the kernel, so the exit stamp runs on every return path.
+// Step trace (diagnostic): with t non-null (kTraceSlots per launch), a kernel
+// records the globaltimer of its first CTA start in t[0] (atomic min; the
+// slot starts at all ones), of its last warp's exit in t[1] (atomic max;
+// starts at 0), and mark(k) the latest time any CTA reached phase k in
+// t[2 + k].  Declared first in the kernel, so the exit stamp runs on every
+// return path.
 struct KernelTrace {
   unsigned long long *t;
   __device__ explicit KernelTrace(unsigned long long *p) : t(p) {
@@ -169,6 +171,9 @@ struct KernelTrace {
   }
   __device__ ~KernelTrace() {
     if (t && (threadIdx.x & 31) == 0) atomicMax(t + 1, (unsigned long long)global_ns());
+  }
+  __device__ void mark(int k) const {
+    if (t) atomicMax(t + 2 + k, (unsigned long long)global_ns());
   }
 };
 

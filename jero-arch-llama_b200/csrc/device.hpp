@@ -35,6 +35,9 @@ struct DevMat {
 
 inline int64_t d_stride_for(int64_t cols) { return ((cols / 32) + 7) / 8 * 8; }
 
+// Step trace slots per launch: {first CTA start, last warp end, 6 phase marks}.
+constexpr int kTraceSlots = 8;
+
 // ---- GEMV (decode, M tokens <= kGemvMaxM) ------------------------------
 // GEMV_IN_PREQ (persistent step only): the RMSNorm input arrives already
 // block-quantized as (row x norm weights) with the producers' partial sums of

@@ -1272,7 +1272,7 @@ void Context::enqueue_exact_step(bool pdl) {
   const uint64_t H = g.hidden_dim, F = g.ffn_dim, Q = g.total_q, KV = g.total_kv;
   const float eps = std::max(recipe.rms_eps, 1.0e-7f);
   size_t n = 0;
-  auto tr = [&](size_t i) { return trace_on ? d_trace + 2 * i : nullptr; };
+  auto tr = [&](size_t i) { return trace_on ? d_trace + kTraceSlots * i : nullptr; };
   launch_embed(c.emb_raw->as<uint8_t>(), c.emb_quant, (int64_t)H, (int64_t)c.emb_rows, d_token, 1, hidden, d_err, pdl,
                stream);
   n++;

@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
   __syncthreads();
   pdl_wait();
   pdl_trigger();
+  if (tid == 0) trace.mark(0);  // the grid dependency resolved
 
   // q (G heads) and the new k / v: bias, then RoPE (recipe.rs:2490-2518,
   // 2717-2773); the appended row is the stored (f16-rounded) value.
@@ -231,6 +232,7 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
       }
     }
   }
+  if (lane == 0) trace.mark(1);  // scores done (the latest warp of any CTA)
   // Per-head max of this CTA (order-independent; NaN never wins, as with
   // `if score > max_score`).
 #pragma unroll
@@ -247,6 +249,7 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
     mx_s[tid] = m;
   }
   cluster.sync();
+  if (tid == 0) trace.mark(2);  // maxima exchanged
   // Every rank's per-head maxima, read in parallel: thread r * G + g reads
   // rank r's head g.
   if (tid < cs * G) xr_s[tid / G][tid % G] = cluster.map_shared_rank(mx_s, tid / G)[tid % G];
@@ -265,9 +268,11 @@ __global__ void __launch_bounds__(kXT, 1) k_xattn(const AttnDecodeArgs a, int pe
     for (int j = tid; j < len; j += kXT) dst[j] = exact::exp_ref(__fsub_rn(sc[g * per_cap + j], gmax_s[g]));
   }
   cluster.sync();  // every e_t has landed; no remote access after this point
+  if (tid == 0) trace.mark(3);  // exp terms in place
   if (!vsum) return;
   const int g = rank;
   const float den = exact::seq_sum_nonneg<kXT>(E, (int)span, 0.0f, *(exact::SumSmem<kXT> *)(smem + L.sum));
+  if (tid == 0) trace.mark(4);  // denominator
   const float inv = den > 0.0f ? __fdiv_rn(1.0f, den) : 0.0f;
   float *wg = a.w_out + (int64_t)(h * G + g) * a.w_stride + lo;  // this head's weights, by position
   for (int64_t i = tid; i < span; i += kXT) wg[i] = __fmul_rn(E[i], inv);

@@ -144,6 +144,7 @@ __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUte
         tma_load_2d(vring + issued * A::STAGE, &tmv, 32 * sl, st.x, &vfull[issued]);
       }
       pdl_wait();
+      trace.mark(0);  // the grid dependency resolved
       for (int k = issued; k < nv; k++) {
         const int slot = k % kVS;
         if (k >= kVS && !mbar_wait_sleepy(&vempty[slot], (uint32_t)(((k - kVS) / kVS) & 1), a.wait_ns)) ok = false;
@@ -159,12 +160,14 @@ __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUte
     const float *wg = a.w + (int64_t)hq * a.w_stride;
     for (int64_t t = lo + (tid - 0); t < seq; t += 32 * (1 + kProd)) w_s[t - lo] = wg[t];
     asm volatile("bar.sync 1, %0;" ::"n"(32 * (1 + kProd)) : "memory");
+    if (tid == 0) trace.mark(1);  // weights in shared memory
     if (warp == 0) {  // chain: lane = dim
       float o = 0.0f;
       int ps = 0;
       uint32_t pp = 0;
       for (int k = 0; k < nv; k++) {
         if (!mbar_wait_bounded(&pfull[ps], pp, a.wait_ns)) ok = false;
+        if (k == 0 && lane == 0) trace.mark(2);  // first product stage ready
         const int n = srow[k].z;
         const float *pr = prod + ((size_t)ps * 32 + lane) * kPStr;  // this dim's row
         const int sw = 8 * (lane >> 3);
@@ -194,6 +197,7 @@ __global__ void __launch_bounds__(kVT, 1) k_xattn_v(const __grid_constant__ CUte
           pp ^= 1u;
         }
       }
+      if (lane == 0) trace.mark(3);  // chain done
       const int64_t e = (int64_t)hq * hd + 32 * sl + lane;
       a.out[e] = o;
       const float v = isfinite(o) ? o : 0.0f;

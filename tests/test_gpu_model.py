@@ -489,6 +489,7 @@ def test_decode_step_trace_stamps(jal, torch_cuda):
     stamped = [i for i in range(t.shape[0]) if t[i, 1] != 0]
     assert len(stamped) == 6 * spec.num_layers + 1
     assert all(t[i, 0] < t[i, 1] for i in stamped)
+    assert all(t[i, 2] > 0 for i in stamped if (i - 1) % 6 in (1, 2))  # attention phase marks
     assert all(t[i, 0] <= t[j, 0] for i, j in zip(stamped, stamped[1:]))
     toks = b.decode_greedy(7, 2)
     la, lb = a.decode_step(int(toks[1])), b.decode_step(int(toks[1]))
