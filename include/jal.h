@@ -330,7 +330,9 @@ typedef struct jal_context_config {
  *   RELAXED: reductions reordered for bandwidth (tree sums, fused
  *     multiply-adds, 32-element blocks); logits drift from the reference by
  *     up to ~1e-2 because the int8 activation quantizer amplifies one-ulp
- *     differences. */
+ *     differences.  Its prefill attention runs on f16 tensor cores and
+ *     rounds Q to f16, so query activations beyond +-65504 overflow there
+ *     (FAST and REFERENCE keep f32). */
 #define JAL_NUMERICS_FAST 0
 #define JAL_NUMERICS_REFERENCE 1
 #define JAL_NUMERICS_RELAXED 2
