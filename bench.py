@@ -172,21 +172,38 @@ def host_cpu():
     return "unknown"
 
 
+# The workloads' shapes for the CPU legs (kept here so that the reference arm
+# never imports the product package); GGML type ids: Q4_0 = 2, Q8_0 = 8.
 SHAPES = {
     "llama3-8b-q4_0": dict(num_layers=32, hidden_dim=4096, ffn_dim=14336, n_heads_q=32, n_heads_kv=8, head_dim=128,
-                           vocab_size=128256, rms_eps=1e-5, rope_theta=500000.0, weight_quant=2, embed_quant=2,
-                           head_quant=2),
+                           vocab_size=128256, context_length=8192, rms_eps=1e-5, rope_theta=500000.0, weight_quant=2,
+                           embed_quant=2, head_quant=2),
+    "qwen2-7b-q8_0": dict(num_layers=28, hidden_dim=3584, ffn_dim=18944, n_heads_q=28, n_heads_kv=4, head_dim=128,
+                          vocab_size=152064, context_length=4096, rms_eps=1e-6, rope_theta=1e6, weight_quant=8,
+                          embed_quant=8, head_quant=8, neox=True, qkv_bias=True, bias_std=0.02),
+    "llama3-70b-q4_0": dict(num_layers=80, hidden_dim=8192, ffn_dim=28672, n_heads_q=64, n_heads_kv=8, head_dim=128,
+                            vocab_size=128256, context_length=8448, rms_eps=1e-5, rope_theta=500000.0,
+                            weight_quant=2, embed_quant=2, head_quant=2),
+    "tiny": dict(num_layers=4, hidden_dim=512, ffn_dim=1376, n_heads_q=8, n_heads_kv=2, head_dim=64, vocab_size=4096,
+                 context_length=256, rms_eps=1e-5, rope_theta=10000.0, weight_quant=2, embed_quant=8, head_quant=8),
 }
 
 
-def cpu_baseline(shape, steps, pos, seed=SEED):
+def prefill_tokens(shape, args):
+    """The prompt length the device arm uses for this workload."""
+    return min(args.prefill, shape["context_length"] - args.warmup - args.steps - 8)
+
+
+def cpu_baseline(shape, steps, pos, seed=SEED, batch=1):
     """The oracle port (the reference's portable path restated in C) timed on
     the host cores, without the product library: a 1-layer model with this
     shape (layer 0, embedding and head, generated by the oracle's seeded
     generator) decodes `steps` tokens at positions pos, pos + 1, ...; the KV
     rows of positions [0, pos) hold seeded random values (the step's cost does
     not depend on them).  The LM head projection is timed alone, and
-    tok/s = 1 / (L * t_layer + t_head)."""
+    tok/s = 1 / (L * t_layer + t_head).  The reference decodes one sequence
+    per step, so `batch` sequences take batch steps and the aggregate rate is
+    the same."""
     sys.path.insert(0, os.path.join(REPO, "tests"))
     import numpy as np  # noqa: E402
     import oracle_py  # noqa: E402
@@ -220,27 +237,33 @@ def cpu_baseline(shape, steps, pos, seed=SEED):
             "sample": f"{steps} decode steps at positions {pos}..{pos + steps - 1} of a 1-layer model of the same "
                       f"shape (layer 0 + embedding + LM head, f16-rounded KV) = {t_step * 1e3:.1f} ms/step, LM head "
                       f"alone {t_head * 1e3:.1f} ms; extrapolated to {shape['num_layers']} layers; model build "
-                      f"{gen_s:.1f} s (not timed)"}
+                      f"{gen_s:.1f} s (not timed)"
+                      + (f"; {batch} sequences decode one after another (the reference has no multi-sequence "
+                         "decode), so the aggregate rate equals one sequence's" if batch > 1 else "")}
 
 
 def reference_arm(args):
     """--impl reference: the reference's portable CPU path (the oracle port,
-    since the Rust crate cannot be built here) on the host cores, at the
-    position the device arm decodes at.  It loads only the oracle library."""
+    since the Rust crate cannot be built here) on the host cores, for the
+    device arm's workload, batch and decode position.  It loads only the
+    oracle library."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    shape = SHAPES["llama3-8b-q4_0"]
+    shape = SHAPES[args.workload]
     steps = max(1, args.steps)
-    pos = args.prefill + args.warmup
-    base = cpu_baseline(shape, steps, pos)
+    warmup = max(args.warmup, 3)
+    n_prefill = prefill_tokens(shape, argparse.Namespace(prefill=args.prefill, warmup=warmup, steps=args.steps))
+    base = cpu_baseline(shape, steps, n_prefill + warmup, batch=args.batch)
+    wq = "Q8_0" if shape["weight_quant"] == 8 else "Q4_0"
+    bs = f"bs={args.batch} (independent sequences)" if args.batch > 1 else "bs=1"
     line = {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus,
-            "steps": steps, "warmup": args.warmup, "ms_per_step": round(1e3 / base["value"], 3),
+            "steps": steps, "warmup": warmup, "ms_per_step": round(1e3 * args.batch / base["value"], 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic: seeded N(0,0.02) weights quantized to Q4_0, uniform token ids",
-            "config": {"workload": f"llama3-8b-q4_0 decode bs=1 greedy after a {args.prefill}-token prefill",
-                       "layers": shape["num_layers"], "hidden": shape["hidden_dim"], "ffn": shape["ffn_dim"],
-                       "vocab": shape["vocab_size"], "kv_cache": "f16-rounded",
+            "data": f"synthetic: seeded N(0,0.02) weights quantized to {wq}, uniform token ids",
+            "config": {"workload": f"{args.workload} decode {bs} greedy after a {n_prefill}-token prefill",
+                       "batch": args.batch, "layers": shape["num_layers"], "hidden": shape["hidden_dim"],
+                       "ffn": shape["ffn_dim"], "vocab": shape["vocab_size"], "kv_cache": "f16-rounded",
                        "impl_detail": "C restatement of the reference's portable path (oracle), OpenMP panels"},
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -447,6 +470,8 @@ def batch_arm(args, jal, torch, np, spec, cache, recipe, n_prefill, n_ctx, gen_s
                     "d2h_bytes_per_step": 4 * B * spec.vocab_size},
             "gpu_launches": (3 + spec.num_layers * (7 + 2 * B)) * (args.warmup + 2 * args.steps),
             "clocks": clk.summary()}
+    if not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(SHAPES[args.workload], 3, n_prefill + args.warmup, batch=B)
     print(json.dumps(line), flush=True)
     return 0
 
@@ -507,7 +532,8 @@ def main():
         tp = jal.TensorParallel(uid[0], rank, world)
     cache = recipe.build_repack_cache(gguf, device=local, tp=tp)
     build_s = time.perf_counter() - t0
-    n_prefill = min(args.prefill, spec.context_length - args.warmup - args.steps - 8)
+    n_prefill = prefill_tokens(SHAPES[args.workload], args)
+    assert SHAPES[args.workload]["context_length"] == spec.context_length
     n_ctx = n_prefill + 2 * (args.warmup + args.steps) + 16
     if args.batch > 1:
         return batch_arm(args, jal, torch, np, spec, cache, recipe, n_prefill, n_ctx, gen_s, build_s, peak, peak_kind)
@@ -590,8 +616,8 @@ def main():
                             "frac": round(dom["GBps"] / peak, 4), "traffic": traffic,
                             "algorithmic_bytes": dom["bytes"], "peak_kind": peak_kind}
         line["gpu_launches"] += sum(200 + 2 * max(2, -(-4 * L2_BYTES // (s["bytes"]))) for s in sweep)
-    if rank == 0 and world == 1 and not args.no_cpu and args.workload == "llama3-8b-q4_0":
-        line["cpu_baseline"] = cpu_baseline(SHAPES["llama3-8b-q4_0"], 3, n_prefill + args.warmup)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(SHAPES[args.workload], 3, n_prefill + args.warmup)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del ctx

@@ -316,7 +316,8 @@ def synth_llama_tensors(shape, seed, layers, nthreads=1):
     """Tensors of a seeded synthetic Llama-layout model with only the first
     `layers` blocks (names, shapes and values as in the GGUF generator):
     shape = dict(hidden_dim, ffn_dim, n_heads_q, n_heads_kv, head_dim,
-    vocab_size, weight_quant, embed_quant, head_quant)."""
+    vocab_size, weight_quant, embed_quant, head_quant), optionally qkv_bias
+    (F32 Q/K/V biases, as Qwen2 has) with bias_std."""
     H, F = shape["hidden_dim"], shape["ffn_dim"]
     Q, KV = shape["n_heads_q"] * shape["head_dim"], shape["n_heads_kv"] * shape["head_dim"]
     wq, ws = shape["weight_quant"], 0.02
@@ -335,6 +336,10 @@ def synth_llama_tensors(shape, seed, layers, nthreads=1):
         add(b + "attn_k.weight", wq, H, KV)
         add(b + "attn_v.weight", wq, H, KV)
         add(b + "attn_output.weight", wq, Q, H)
+        if shape.get("qkv_bias"):
+            for nm, n in (("attn_q.bias", Q), ("attn_k.bias", KV), ("attn_v.bias", KV)):
+                t[b + nm] = SynthTensor(b + nm, [n], 0,
+                                        synth_matrix(0, 1, n, seed, b + nm, shape.get("bias_std", 0.02), nthreads))
         add(b + "ffn_norm.weight", 0, H, 1, True)
         add(b + "ffn_gate.weight", wq, H, F)
         add(b + "ffn_up.weight", wq, H, F)

@@ -44,6 +44,69 @@ def test_synth_gguf_deterministic_and_parseable(jal):
     assert np.all(t["blk.0.attn_norm.weight"].data.view(np.float32) == 1.0)
 
 
+@pytest.mark.parametrize("arch", ["llama", "qwen2"])
+def test_oracle_generator_matches_product_gguf_bytes(jal, oracle, arch):
+    # The CPU baseline builds its model from the oracle's generator so that
+    # it never loads the product library; every tensor (Qwen2's F32 Q/K/V
+    # biases included) must be the bytes the product's GGUF holds.
+    q = jal.Q8_0 if arch == "qwen2" else jal.Q4_0
+    spec = jal.SynthSpec(architecture=arch, num_layers=2, hidden_dim=256, ffn_dim=384, n_heads_q=4, n_heads_kv=2,
+                         head_dim=64, vocab_size=96, weight_quant=q, embed_quant=q, head_quant=q,
+                         qkv_bias=arch == "qwen2", bias_std=0.5)
+    _, t = gguf_py.parse(jal.synth_gguf(spec, seed=5))
+    shape = dict(hidden_dim=256, ffn_dim=384, n_heads_q=4, n_heads_kv=2, head_dim=64, vocab_size=96, weight_quant=q,
+                 embed_quant=q, head_quant=q, qkv_bias=arch == "qwen2", bias_std=0.5)
+    mine = oracle.synth_llama_tensors(shape, 5, 2, nthreads=2)
+    assert sorted(mine) == sorted(t)
+    for name, tensor in mine.items():
+        assert tensor.dims == t[name].dims and tensor.qtype == t[name].qtype, name
+        assert np.array_equal(tensor.data, t[name].data), name
+    assert ("blk.1.attn_v.bias" in mine) == (arch == "qwen2")
+
+
+def test_bench_cpu_shapes_match_the_device_workloads(jal):
+    # The CPU baseline and the reference arm time the shape the device arm
+    # decodes, for every workload the bench offers.
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(REPO, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    device = {"llama3-8b-q4_0": jal.LLAMA3_8B_Q4_0, "qwen2-7b-q8_0": jal.QWEN2_7B_Q8_0,
+              "llama3-70b-q4_0": jal.LLAMA3_70B_Q4_0, "tiny": jal.TINY_LLAMA}
+    assert sorted(bench.SHAPES) == sorted(device)
+    for name, shape in bench.SHAPES.items():
+        s = device[name]
+        for k in ("num_layers", "hidden_dim", "ffn_dim", "n_heads_q", "n_heads_kv", "head_dim", "vocab_size",
+                  "context_length", "weight_quant", "embed_quant", "head_quant"):
+            assert shape[k] == getattr(s, k), (name, k)
+        for k in ("rms_eps", "rope_theta"):
+            assert shape[k] == pytest.approx(getattr(s, k), rel=1e-7), (name, k)
+        assert bool(shape.get("qkv_bias")) == s.qkv_bias, name
+        assert bool(shape.get("neox")) == (s.architecture == "qwen2"), name
+
+
+def test_bench_reference_arm_line_without_the_product_library():
+    # bench.py --impl reference: one JSON line on the device arm's workload
+    # and batch, e2e with no host<->device bytes, and the product library
+    # never mapped into the process.
+    import json
+    import subprocess
+    import sys
+    code = ("import runpy, sys; sys.argv = ['bench.py', '--impl', 'reference', '--workload', 'tiny', '--steps', '2', "
+            "'--warmup', '3', '--batch', '3']; runpy.run_path('bench.py', run_name='__main__'); "
+            "print('MAPPED', open('/proc/self/maps').read().count('libjal.so'))")
+    out = subprocess.run([sys.executable, "-c", code], cwd=REPO, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = out.stdout.strip().splitlines()
+    assert lines[-1] == "MAPPED 0"
+    d = json.loads(lines[-2])
+    assert d["impl"] == "reference" and d["unit"] == "tok/s" and d["higher_is_better"] is True
+    assert d["config"]["batch"] == 3 and d["config"]["workload"].startswith("tiny decode bs=3")
+    assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"] > 0
+    assert d["cpu_baseline"]["cores"] >= 1 and "4 layers" in d["cpu_baseline"]["sample"]
+
+
 def test_synth_weights_are_normal_0_02(jal, oracle):
     raw = jal.synth_matrix(jal.Q8_0, 256, 1024, seed=3, name="probe", std=0.02)
     vals = np.concatenate([oracle.dequantize_block(8, raw[i * 34:(i + 1) * 34]) for i in range(raw.size // 34)])
