@@ -34,47 +34,60 @@ def f32_to_bf16_bits(val):
     return struct.unpack("<I", struct.pack("<f", float(f32(val))))[0] >> 16
 
 
-def fill_dense_f32(rows, cols, seed):
-    """tests/repack_wave2_parity.rs:46-58."""
+# The reference's two families of fill generators differ only in these
+# constants: tests/repack_wave2_parity.rs:46-180 (WAVE2) and
+# tests/batched_prefill_wave3.rs:45-179 (WAVE3).
+WAVE2 = dict(f32_step=0.025, half_step=0.03, q4_d=0.05, q5_d=0.04, k_d=0.02, k_dmin=0.006, q6k_d=0.015)
+WAVE3 = dict(f32_step=0.02, half_step=0.025, q4_d=0.04, q5_d=0.03, k_d=0.015, k_dmin=0.004, q6k_d=0.012)
+
+
+def _f16le(v):
+    return np.frombuffer(struct.pack("<H", f32_to_f16_bits_trunc(v)), dtype=np.uint8)
+
+
+def fill_dense_f32(rows, cols, seed, c=WAVE2):
+    """tests/repack_wave2_parity.rs:46-58, batched_prefill_wave3.rs:45-56."""
     idx = np.arange(rows * cols, dtype=np.int64)
-    val = (((idx * 19 + seed) % 97).astype(np.float32) - f32(48.0)) * f32(0.025)
+    val = (((idx * 19 + seed) % 97).astype(np.float32) - f32(48.0)) * f32(c["f32_step"])
     return val.astype("<f4").view(np.uint8).copy()
 
 
-def fill_dense_half(rows, cols, quant, seed):
-    """tests/repack_wave2_parity.rs:60-82 (quant 1 = F16, 30 = BF16)."""
+def fill_dense_half(rows, cols, quant, seed, c=WAVE2):
+    """tests/repack_wave2_parity.rs:60-82, batched_prefill_wave3.rs:58-79
+    (quant 1 = F16, 30 = BF16)."""
     mul, mod, off = (17, 67, 33.0) if quant == 1 else (23, 73, 36.0)
     out = np.zeros(rows * cols, dtype=np.uint16)
     for i in range(rows * cols):
-        v = (f32((i * mul + seed) % mod) - f32(off)) * f32(0.03)
+        v = (f32((i * mul + seed) % mod) - f32(off)) * f32(c["half_step"])
         out[i] = f32_to_f16_bits_trunc(v) if quant == 1 else f32_to_bf16_bits(v)
     return out.view(np.uint8).copy()
 
 
-def fill_q8_0(rows, cols, seed):
-    """tests/repack_wave2_parity.rs:84-98."""
+def fill_q8_0(rows, cols, seed, c=WAVE2):
+    """tests/repack_wave2_parity.rs:84-98, batched_prefill_wave3.rs:81-95
+    (the same in both)."""
     blocks = rows * cols // 32
     out = np.zeros(blocks * 34, dtype=np.uint8)
     for b in range(blocks):
         o = b * 34
         d = f32(0.015) + f32((b + seed) % 7) * f32(0.004)
-        out[o:o + 2] = np.frombuffer(struct.pack("<H", f32_to_f16_bits_trunc(d)), dtype=np.uint8)
+        out[o:o + 2] = _f16le(d)
         k = np.arange(32)
         signed = ((b * 11 + k * 7 + seed) % 81) - 40
         out[o + 2:o + 34] = signed.astype(np.int8).view(np.uint8)
     return out
 
 
-def fill_q4_0_or_q5_0(rows, cols, quant, seed):
-    """tests/repack_wave2_parity.rs:100-123 (quant 2 = Q4_0, 6 = Q5_0)."""
+def fill_q4_0_or_q5_0(rows, cols, quant, seed, c=WAVE2):
+    """tests/repack_wave2_parity.rs:100-123, batched_prefill_wave3.rs:97-120
+    (quant 2 = Q4_0, 6 = Q5_0)."""
     blocks = rows * cols // 32
     bb = 18 if quant == 2 else 22
     out = np.zeros(blocks * bb, dtype=np.uint8)
-    d = f32(0.05) if quant == 2 else f32(0.04)
-    dh = struct.pack("<H", f32_to_f16_bits_trunc(d))
+    dh = _f16le(f32(c["q4_d"]) if quant == 2 else f32(c["q5_d"]))
     for b in range(blocks):
         o = b * bb
-        out[o:o + 2] = np.frombuffer(dh, dtype=np.uint8)
+        out[o:o + 2] = dh
         qs = o + 2
         if quant == 6:
             qh = (0x5A3C96F1 + b * 13) & 0xFFFFFFFF
@@ -87,16 +100,17 @@ def fill_q4_0_or_q5_0(rows, cols, quant, seed):
     return out
 
 
-def fill_k_quant(rows, cols, quant, seed):
-    """tests/repack_wave2_parity.rs:125-166 (12 = Q4_K_M, 13 = Q5_K, 14 = Q6_K)."""
+def fill_k_quant(rows, cols, quant, seed, c=WAVE2):
+    """tests/repack_wave2_parity.rs:125-166, batched_prefill_wave3.rs:122-166
+    (12 = Q4_K_M, 13 = Q5_K, 14 = Q6_K)."""
     sblks = rows * cols // 256
     bb = {12: 144, 13: 176, 14: 210}[quant]
     out = np.zeros(sblks * bb, dtype=np.uint8)
     for sb in range(sblks):
         o = sb * bb
         if quant in (12, 13):
-            out[o:o + 2] = np.frombuffer(struct.pack("<H", f32_to_f16_bits_trunc(0.02)), dtype=np.uint8)
-            out[o + 2:o + 4] = np.frombuffer(struct.pack("<H", f32_to_f16_bits_trunc(0.006)), dtype=np.uint8)
+            out[o:o + 2] = _f16le(c["k_d"])
+            out[o + 2:o + 4] = _f16le(c["k_dmin"])
             for j in range(12):
                 out[o + 4 + j] = (sb * 7 + j * 11 + seed) % 64 + 1
             qs = o + 16
@@ -107,7 +121,7 @@ def fill_k_quant(rows, cols, quant, seed):
             for l_ in range(128):
                 out[qs + l_] = ((sb * 2 + l_ + seed) % 16) | (((sb * 5 + l_ + seed) % 16) << 4)
         else:
-            out[o + 208:o + 210] = np.frombuffer(struct.pack("<H", f32_to_f16_bits_trunc(0.015)), dtype=np.uint8)
+            out[o + 208:o + 210] = _f16le(c["q6k_d"])
             for l_ in range(128):
                 out[o + l_] = (sb * 7 + l_ * 3 + seed) % 256
             for l_ in range(64):
@@ -117,17 +131,17 @@ def fill_k_quant(rows, cols, quant, seed):
     return out
 
 
-def fill_quant_bytes(rows, cols, quant, seed):
-    """tests/repack_wave2_parity.rs:168-180."""
+def fill_quant_bytes(rows, cols, quant, seed, c=WAVE2):
+    """tests/repack_wave2_parity.rs:168-180, batched_prefill_wave3.rs:168-179."""
     if quant == 0:
-        return fill_dense_f32(rows, cols, seed)
+        return fill_dense_f32(rows, cols, seed, c)
     if quant in (1, 30):
-        return fill_dense_half(rows, cols, quant, seed)
+        return fill_dense_half(rows, cols, quant, seed, c)
     if quant == 8:
-        return fill_q8_0(rows, cols, seed)
+        return fill_q8_0(rows, cols, seed, c)
     if quant in (2, 6):
-        return fill_q4_0_or_q5_0(rows, cols, quant, seed)
-    return fill_k_quant(rows, cols, quant, seed)
+        return fill_q4_0_or_q5_0(rows, cols, quant, seed, c)
+    return fill_k_quant(rows, cols, quant, seed, c)
 
 
 def wave2_activation(m, cols):
@@ -174,3 +188,73 @@ def q4_k_m_two_rows():
     for i in range(128):
         raw[160 + i] = ((i * 11 + 1) & 0x0F) | (((i * 3 + 12) & 0x0F) << 4)
     return raw
+
+
+def wave3_model_gguf(arch, weight_quant, hidden=256):
+    """The two-layer mixed-type model of tests/batched_prefill_wave3.rs:215-310
+    (build_wave3_test_gguf + write_finite_gguf_payloads, :181-213): hidden =
+    ffn, 4 query / 2 KV heads of hidden / 4 dims, vocab 64, context 64.
+    Layer 0 holds q / o / gate / up / down in `weight_quant` (k, v Q8_0),
+    layer 1 Q8_0 / Q4_0 / Q5_0 projections with `weight_quant` down; norms in
+    F16 (llama) or BF16 (qwen2) except ffn_norm of layer 0 and the output
+    norm (F32); an F32 LM head; qwen2 adds F16 / F32 / BF16 Q/K/V and O
+    biases.  Payloads: tensor i (in file order) of two dims gets
+    fill_quant_bytes(rows, cols, quant, i + 1) with the WAVE3 constants; a
+    norm gets 0.85 + ((e + i) % 13) * 0.02, a bias
+    (((7 e + 11 i) % 29) - 14) * 0.04, in f32 arithmetic."""
+    import gguf_py
+
+    n_q, n_kv, vocab = 4, 2, 64
+    hd = hidden // n_q
+    kvd = n_kv * hd
+    norm_q = 30 if arch == "qwen2" else 1
+    wq = weight_quant
+    specs = [("token_embd.weight", 8, [hidden, vocab]),
+             ("blk.0.attn_norm.weight", norm_q, [hidden]),
+             ("blk.0.attn_q.weight", wq, [hidden, hidden]),
+             ("blk.0.attn_k.weight", 8, [hidden, kvd]),
+             ("blk.0.attn_v.weight", 8, [hidden, kvd]),
+             ("blk.0.attn_output.weight", wq, [hidden, hidden]),
+             ("blk.0.ffn_norm.weight", 0, [hidden]),
+             ("blk.0.ffn_gate.weight", wq, [hidden, hidden]),
+             ("blk.0.ffn_up.weight", wq, [hidden, hidden]),
+             ("blk.0.ffn_down.weight", wq, [hidden, hidden]),
+             ("blk.1.attn_norm.weight", norm_q, [hidden]),
+             ("blk.1.attn_q.weight", 8, [hidden, hidden]),
+             ("blk.1.attn_k.weight", 2, [hidden, kvd]),
+             ("blk.1.attn_v.weight", 6, [hidden, kvd]),
+             ("blk.1.attn_output.weight", 8, [hidden, hidden]),
+             ("blk.1.ffn_norm.weight", norm_q, [hidden]),
+             ("blk.1.ffn_gate.weight", 2, [hidden, hidden]),
+             ("blk.1.ffn_up.weight", 6, [hidden, hidden]),
+             ("blk.1.ffn_down.weight", wq, [hidden, hidden]),
+             ("output_norm.weight", 0, [hidden]),
+             ("output.weight", 0, [hidden, vocab])]
+    if arch == "qwen2":
+        specs += [("blk.0.attn_q.bias", 1, [hidden]), ("blk.0.attn_k.bias", 0, [kvd]),
+                  ("blk.0.attn_v.bias", 30, [kvd]), ("blk.0.attn_output.bias", 0, [hidden]),
+                  ("blk.1.attn_q.bias", 0, [hidden]), ("blk.1.attn_k.bias", 1, [kvd]),
+                  ("blk.1.attn_v.bias", 0, [kvd])]
+    tensors = []
+    for i, (name, q, dims) in enumerate(specs):
+        if len(dims) == 2:
+            payload = fill_quant_bytes(dims[1], dims[0], q, i + 1, WAVE3)
+        else:
+            e = np.arange(dims[0], dtype=np.int64)
+            if name.endswith("norm.weight"):
+                v = f32(0.85) + ((e + i) % 13).astype(np.float32) * f32(0.02)
+            else:
+                v = (((e * 7 + i * 11) % 29).astype(np.float32) - f32(14.0)) * f32(0.04)
+            if q == 0:
+                payload = v.astype("<f4").view(np.uint8)
+            elif q == 1:
+                payload = np.array([f32_to_f16_bits_trunc(x) for x in v], dtype="<u2").view(np.uint8)
+            else:
+                payload = np.array([f32_to_bf16_bits(x) for x in v], dtype="<u2").view(np.uint8)
+        tensors.append((name, q, dims, payload))
+    kvs = [("general.architecture", arch), ("general.alignment", 32), (f"{arch}.block_count", 2),
+           (f"{arch}.embedding_length", hidden), (f"{arch}.feed_forward_length", hidden),
+           (f"{arch}.attention.head_count", n_q), (f"{arch}.attention.head_count_kv", n_kv),
+           (f"{arch}.attention.key_length", hd), (f"{arch}.rope.freq_base", 10000.0),
+           (f"{arch}.attention.layer_norm_rms_epsilon", 1e-5), (f"{arch}.context_length", 64)]
+    return gguf_py.write(kvs, tensors)

@@ -293,3 +293,83 @@ def test_oracle_chunked_prefill_equals_single_shot(jal, oracle):
     m.prefill(kv_b, cap, prompt[:3], 0, compute_logits=False)
     lb = m.prefill(kv_b, cap, prompt[3:], 3)
     assert np.array_equal(la, lb) and np.array_equal(kv_a, kv_b)
+
+
+WAVE3_CASES = [("llama", 0), ("qwen2", 12), ("llama", 13), ("qwen2", 14)]  # F32, Q4_K_M, Q5_K, Q6_K
+
+
+@pytest.mark.parametrize("arch,quant", WAVE3_CASES)
+def test_oracle_mixed_type_model_batched_prefill_equals_sequential(jal, oracle, arch, quant):
+    # tests/batched_prefill_wave3.rs:398-471 on its own mixed-type model
+    # (dense, K-quant, Q4_0 / Q5_0 / Q8_0 matrices, F16 / BF16 norms and
+    # biases): prefill of M = 1, 8, 32 prompt tokens against prefill of the
+    # first + sequential decodes, logits and KV within the reference test's
+    # bound (|a - b| / max(|b|, 1) < 1e-5 dense, 2e-3 quantized).  In the
+    # oracle, as in the reference's portable path, the two are bit-equal.
+    import ref_fixtures
+    buf = ref_fixtures.wave3_model_gguf(arch, quant)
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    recipe.validate_model(buf)
+    assert recipe.architecture_id() == arch
+    _, tensors = gguf_py.parse(buf)
+    geom = dict(num_layers=2, hidden_dim=256, ffn_dim=256, n_heads_q=4, n_heads_kv=2, head_dim=64, vocab_size=64,
+                rms_eps=1e-5, rope_theta=10000.0, neox=arch == "qwen2")
+    m = oracle.Model(tensors, geom, nthreads=2)
+    cap = 64
+    tol = 1e-5 if quant == 0 else 2e-3
+    for n in (1, 8, 32):
+        prompt = [(i * 7 + 3) % 64 for i in range(n)]
+        kv_a = m.new_kv(cap)
+        la = m.prefill(kv_a, cap, prompt, 0)
+        kv_b = m.new_kv(cap)
+        lb = m.prefill(kv_b, cap, prompt[:1], 0)
+        for i, tok in enumerate(prompt[1:], start=1):
+            lb = m.decode(kv_b, cap, tok, i)
+        for a, b in ((la, lb), (kv_a, kv_b)):
+            assert np.all(np.isfinite(a)) and np.all(np.isfinite(b))
+            assert float(np.max(np.abs(a - b) / np.maximum(np.abs(b), 1.0))) < tol
+        assert np.array_equal(la, lb) and np.array_equal(kv_a, kv_b)
+        assert float(np.max(np.abs(la))) > 0.0
+
+
+def _wave3_oracle(jal, oracle, arch, quant, sliding_window=0):
+    import ref_fixtures
+    buf = ref_fixtures.wave3_model_gguf(arch, quant)
+    _, tensors = gguf_py.parse(buf)
+    geom = dict(num_layers=2, hidden_dim=256, ffn_dim=256, n_heads_q=4, n_heads_kv=2, head_dim=64, vocab_size=64,
+                rms_eps=1e-5, rope_theta=10000.0, neox=arch == "qwen2")
+    return oracle.Model(tensors, geom, nthreads=2, sliding_window=sliding_window)
+
+
+@pytest.mark.parametrize("arch,quant,window", [("llama", 0, 0), ("qwen2", 12, 0), ("llama", 6, 8)])
+def test_oracle_mixed_type_model_two_chunks_equal_single_shot(jal, oracle, arch, quant, window):
+    # tests/batched_prefill_wave3.rs:473-587: a 32-token prompt prefilled at
+    # once against chunks [0, 16) without logits and [16, 32) from position
+    # 16 (Q5_0 with an 8-token sliding window included), then one decode of
+    # token 19 at position 32 on each cache; bit-equal in the oracle.
+    m = _wave3_oracle(jal, oracle, arch, quant, window)
+    cap = 64
+    prompt = [(i * 5 + 1) % 64 for i in range(32)]
+    kv_a = m.new_kv(cap)
+    la = m.prefill(kv_a, cap, prompt, 0)
+    kv_b = m.new_kv(cap)
+    m.prefill(kv_b, cap, prompt[:16], 0, compute_logits=False)
+    lb = m.prefill(kv_b, cap, prompt[16:], 16)
+    assert np.array_equal(la, lb) and np.array_equal(kv_a, kv_b)
+    assert np.array_equal(m.decode(kv_a, cap, 19, 32), m.decode(kv_b, cap, 19, 32))
+    assert np.array_equal(kv_a, kv_b)
+
+
+def test_oracle_mixed_type_model_uneven_three_chunks(jal, oracle):
+    # tests/batched_prefill_wave3.rs:589-637: chunks [0, 7), [7, 19) without
+    # logits and [19, 32) with them equal the single-shot prefill.
+    m = _wave3_oracle(jal, oracle, "llama", 0)
+    cap = 64
+    prompt = [(i * 3 + 9) % 64 for i in range(32)]
+    kv_a = m.new_kv(cap)
+    la = m.prefill(kv_a, cap, prompt, 0)
+    kv_b = m.new_kv(cap)
+    for start, end in ((0, 7), (7, 19)):
+        m.prefill(kv_b, cap, prompt[start:end], start, compute_logits=False)
+    lb = m.prefill(kv_b, cap, prompt[19:], 19)
+    assert np.array_equal(la, lb) and np.array_equal(kv_a, kv_b)

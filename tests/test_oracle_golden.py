@@ -165,6 +165,30 @@ def test_wave2_repacked_gemm_vs_compute_row_dot(oracle, quant):
             assert abs(out[t, r] - exp) / max(bound, abs(exp)) < tol
 
 
+@pytest.mark.parametrize("quant", ADMITTED)
+def test_wave3_batched_projection_vs_compute_row_dot(oracle, quant):
+    # tests/batched_prefill_wave3.rs:327-396: 192 rows (three 64-row panels)
+    # x 256 columns of the wave-3 fill family, M = 1, 8, 32 activation rows
+    # ((((23 i + 11 M) % 79) - 39) * 0.025), each output within 1e-5 (dense)
+    # or 1.5e-2 (quantized) of compute_row_dot relative to
+    # max(|x|_2 sqrt(cols), 1, |expected|).
+    rows, cols = 192, 256
+    raw = fx.fill_quant_bytes(rows, cols, quant, ADMITTED.index(quant) + 3, fx.WAVE3)
+    w = oracle.RepackedWeight(raw, quant, rows, cols)
+    tol = 1e-5 if quant in (0, 1, 30) else 1.5e-2
+    for m in (1, 8, 32):
+        i = np.arange(m * cols, dtype=np.int64)
+        act = (((i * 23 + m * 11) % 79).astype(np.float32) - np.float32(39.0)) * np.float32(0.025)
+        out = w.project_batch(act, m)
+        assert np.array_equal(out, np.stack([w.project_batch(act[t * cols:(t + 1) * cols], 1)[0] for t in range(m)]))
+        for t in range(m):
+            x = act[t * cols:(t + 1) * cols]
+            scale = max(float(np.sqrt(np.sum(x * x))) * math.sqrt(cols), 1.0)
+            for r in range(rows):
+                exp = oracle.compute_row_dot(r, cols, quant, raw, x)
+                assert abs(out[t, r] - exp) / max(scale, abs(exp)) < tol
+
+
 def test_repack_layout_q4_0_matches_definition(oracle):
     # repack_quantized (repack_cache.rs:639-694): byte (r%8)*16+t of tile
     # (r/8)*k_chunks + ch holds q[r][ch*16+t]; scales[((r/8)*groups+g)*8+r%8].
