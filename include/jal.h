@@ -337,6 +337,12 @@ typedef struct jal_context_config {
 #define JAL_NUMERICS_REFERENCE 1
 #define JAL_NUMERICS_RELAXED 2
 
+/* Creates a context over model cache c.  The device step takes Q4_0 / Q5_0
+ * / Q8_0 layer matrices (uniform across q/k/v and across gate/up) and an LM
+ * head in Q4_0 / Q5_0 / Q8_0, F32 / F16 / BF16 or, with the FAST or
+ * REFERENCE numerics on one GPU, Q4_K / Q5_K / Q6_K (repacked, projected in
+ * the reference's order with its group-min term); anything else fails with
+ * JAL_ERR_CAPABILITY_MISMATCH. */
 int jal_context_new(const jal_recipe *r, const jal_model_cache *c,
                     const jal_context_config *cfg, jal_context **out);
 void jal_context_free(jal_context *ctx);

@@ -972,7 +972,9 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
     if (!L.qkv_stacked || !L.gateup_stacked || !device_quant(L.wo.quant) || !device_quant(L.wdown.quant))
       fail(JAL_ERR_CAPABILITY_MISMATCH, "the device forward needs Q4_0/Q8_0 layer matrices with uniform q/k/v and gate/up quants");
   }
-  if (!device_quant(c.lm_head.quant) && !dense_quant(c.lm_head.quant))
+  if (kquant(c.lm_head.quant) && (c.plan.world > 1 || ctx->cfg.numerics == JAL_NUMERICS_RELAXED))
+    fail(JAL_ERR_CAPABILITY_MISMATCH, "a K-quant LM head runs the reference-order numerics on one GPU only");
+  if (!device_quant(c.lm_head.quant) && !dense_quant(c.lm_head.quant) && !kquant(c.lm_head.quant))
     fail(JAL_ERR_CAPABILITY_MISMATCH, "LM head quant %d not supported on the device path", c.lm_head.quant);
   if (dense_quant(c.lm_head.quant) && g.hidden_dim % 32 != 0)
     fail(JAL_ERR_CAPABILITY_MISMATCH, "dense LM head: hidden dim %llu not a multiple of 32", (unsigned long long)g.hidden_dim);
@@ -1035,7 +1037,8 @@ std::unique_ptr<Context> create_context(const Recipe &r, const ModelCache &c, co
       need(L.gateup, GEMV_IN_NORM, GEMV_OUT_SWIGLU, (int64_t)g.ffn_dim, "gate/up");
       need(L.wdown.dm, GEMV_IN_F32, GEMV_OUT_ADD, (int64_t)g.hidden_dim, "down");
     }
-    if (!dense_quant(c.lm_head.quant)) need(c.lm_head.dm, GEMV_IN_NORM, GEMV_OUT_STORE, (int64_t)c.vocab_size, "LM head");
+    if (!dense_quant(c.lm_head.quant) && !kquant(c.lm_head.quant))
+      need(c.lm_head.dm, GEMV_IN_NORM, GEMV_OUT_STORE, (int64_t)c.vocab_size, "LM head");
     ctx->x_splits = xattn_cluster_size((int)g.head_dim, ctx->cfg.kv_f16, (int)(g.n_heads_q / g.n_heads_kv),
                                        (int)g.n_heads_kv, (int64_t)ctx->cfg.n_ctx);
     if (ctx->x_splits <= 0)
@@ -1262,6 +1265,17 @@ void Context::enqueue_decode_step(bool pdl) {
   launches_per_step = n;
 }
 
+// A K-quant LM head (Q4_K / Q5_K / Q6_K; llama.cpp's usual output type) in
+// the reference's order for one row: the final RMSNorm, QuantizedActQ8 of
+// the normed row and the repacked projection with the group-min term
+// (repack_cache.rs:739-783), into logits[vocab].
+static void kq_lm_head(const ModelCache &c, const float *x, int64_t H, float eps, float *s_norm, int8_t *s_q8,
+                       float *s_sc, float *logits, cudaStream_t s) {
+  launch_rmsnorm(x, c.output_norm->as<float>(), 1, H, eps, s_norm, s);
+  launch_act_quant(s_norm, 1, H, H, s_q8, s_sc, s);
+  launch_kq_gemm(c.lm_head.dm, s_norm, s_q8, s_sc, 1, logits, s);
+}
+
 // The serving step in the reference's f32 order (FAST numerics, one GPU):
 // embedding, per layer Q/K/V (RMSNorm prologue) -> attention (bias, RoPE,
 // append) -> O (+ bias, residual) -> gate/up (RMSNorm prologue, SwiGLU) ->
@@ -1327,6 +1341,9 @@ void Context::enqueue_exact_step(bool pdl) {
     launch_rmsnorm(hidden, c.output_norm->as<float>(), 1, (int64_t)H, eps, s_norm, stream);
     launch_strict_gemv_dense(c.lm_head.dm, s_norm, (int64_t)c.vocab_size, logits, stream);
     n += 2;
+  } else if (kquant(c.lm_head.dm.quant)) {
+    kq_lm_head(c, hidden, (int64_t)H, eps, s_norm, s_q8, s_sc, logits, stream);
+    n += 3;
   } else {
     GemvArgs la;
     la.w = c.lm_head.dm; la.rows = (int64_t)c.vocab_size; la.in_mode = GEMV_IN_NORM;
@@ -1413,6 +1430,9 @@ void batch_decode_step(Context *const *cs, size_t n, const uint32_t *d_tokens) {
       launch_rmsnorm(hid + b * H, c.output_norm->as<float>(), 1, (int64_t)H, eps, c0.s_norm, s);
       launch_strict_gemv_dense(c.lm_head.dm, c0.s_norm, (int64_t)V, c0.bt_logits + b * V, s);
     }
+  } else if (kquant(c.lm_head.dm.quant)) {
+    for (size_t b = 0; b < n; b++)
+      kq_lm_head(c, hid + b * H, (int64_t)H, eps, c0.s_norm, c0.s_q8, c0.s_sc, c0.bt_logits + b * V, s);
   } else {
     launch_rmsnorm_quant(hid, c.output_norm->as<float>(), m, (int64_t)H, eps, xq, xs, s);
     GemmArgs la;
@@ -1532,6 +1552,8 @@ void Context::enqueue_strict_token(bool logits_out, bool argmax) {
     launch_act_quant(s_norm, 1, (int64_t)H, (int64_t)H, s_q8, s_sc, stream);
     if (dense_quant(c.lm_head.dm.quant))
       launch_strict_gemv_dense(c.lm_head.dm, s_norm, (int64_t)c.vocab_size, logits, stream);
+    else if (kquant(c.lm_head.dm.quant))
+      launch_kq_gemm(c.lm_head.dm, s_norm, s_q8, s_sc, 1, logits, stream);
     else
       launch_strict_gemv(c.lm_head.dm, s_q8, s_sc, (int64_t)c.vocab_size, false, logits, nullptr, stream);
   }
@@ -1671,6 +1693,8 @@ void Context::prefill(const uint32_t *tokens, uint64_t n, uint64_t start_pos, bo
       if (exact && dense_quant(c.lm_head.dm.quant)) {
         launch_rmsnorm(la.x, la.norm_w, 1, (int64_t)H, eps, s_norm, stream);
         launch_strict_gemv_dense(c.lm_head.dm, s_norm, (int64_t)c.vocab_size, logits, stream);
+      } else if (exact && kquant(c.lm_head.dm.quant)) {
+        kq_lm_head(c, la.x, (int64_t)H, eps, s_norm, s_q8, s_sc, logits, stream);
       } else if (exact) {
         launch_xgemv(la, stream);
       } else {

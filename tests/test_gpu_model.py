@@ -205,6 +205,43 @@ def test_tiny_llama_dense_lm_head(jal, oracle, torch_cuda, head):
     run_relaxed(om, new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_RELAXED), prompt_of(5), 16, 256)
 
 
+def k_quant_head_gguf(buf, quant, seed=3):
+    """The GGUF with output.weight replaced by K-quant rows in the reference
+    tests' fill pattern (tests/repack_wave2_parity.rs:125-166)."""
+    import ref_fixtures
+    kv, t = gguf_py.parse(buf)
+    tensors = []
+    for name, ten in t.items():
+        if name == "output.weight":
+            cols, rows = ten.dims
+            tensors.append((name, quant, [cols, rows], ref_fixtures.fill_k_quant(rows, cols, quant, seed)))
+        else:
+            tensors.append((name, ten.qtype, ten.dims, ten.data))
+    return gguf_py.write(list(kv.items()), tensors)
+
+
+@pytest.mark.parametrize("head_quant", [14, 12])  # Q6_K, Q4_K_M
+def test_tiny_llama_k_quant_lm_head(jal, oracle, torch_cuda, head_quant):
+    # A Q6_K LM head (llama.cpp's usual output type for Q4_0 / Q8_0 models)
+    # or a Q4_K one (group mins): the final RMSNorm, QuantizedActQ8 and the
+    # repacked K-quant projection in the reference's order on the FAST,
+    # REFERENCE and batched paths against the oracle; the relaxed numerics
+    # refuse it.
+    spec = jal.SynthSpec()
+    buf = k_quant_head_gguf(jal.synth_gguf(spec, 37), head_quant)
+    _, tensors = gguf_py.parse(buf)
+    assert tensors["output.weight"].qtype == head_quant
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    cache = recipe.build_repack_cache(buf)
+    om = oracle.Model(tensors, geom_of(spec), nthreads=NTHREADS)
+    for numerics in (jal.NUMERICS_FAST, jal.NUMERICS_REFERENCE):
+        run_parity(om, new_ctx(jal, recipe, cache, numerics=numerics), prompt_of(7), 16, 256)
+    om16 = oracle.Model(tensors, geom_of(spec), nthreads=NTHREADS, kv_f16=True)
+    _batch_vs_single(jal, recipe, cache, [prompt_of(8, 9), prompt_of(9, 4)], 4, om=om16)
+    with pytest.raises(jal.CapabilityMismatch):
+        new_ctx(jal, recipe, cache, numerics=jal.NUMERICS_RELAXED)
+
+
 def test_llama4_irope_and_sliding_window(jal, oracle, torch_cuda):
     spec = jal.SynthSpec(architecture="llama4", num_layers=4)
     mask = [False, True, False, True]
