@@ -258,3 +258,86 @@ def wave3_model_gguf(arch, weight_quant, hidden=256):
            (f"{arch}.attention.key_length", hd), (f"{arch}.rope.freq_base", 10000.0),
            (f"{arch}.attention.layer_norm_rms_epsilon", 1e-5), (f"{arch}.context_length", 64)]
     return gguf_py.write(kvs, tensors)
+
+
+def wave4_fill_tensor(rows, cols, quant, seed):
+    """tests/wave4_zero_alloc_decode_gemv.rs:123-246 (fill_quantized_row /
+    fill_quantized_tensor_bytes): per-row patterns of r, the block index and
+    the seed; quantized blocks carry the f16 scale 2^-5 (and min 2^-7)."""
+    sc, mn = struct.pack("<H", 0x2800), struct.pack("<H", 0x2000)  # 0.03125, 0.0078125
+    rows_out = []
+    for r in range(rows):
+        c = np.arange(cols, dtype=np.int64)
+        if quant == 0:
+            v = (((r * 13 + c * 7 + seed) % 23).astype(np.float32) - f32(11.0)) * f32(0.02)
+            rows_out.append(v.astype("<f4").view(np.uint8))
+            continue
+        if quant == 1:
+            v = (((r * 11 + c * 5 + seed) % 19).astype(np.float32) - f32(9.0)) * f32(0.025)
+            rows_out.append(np.array([f32_to_f16_bits_trunc(x) for x in v], dtype="<u2").view(np.uint8))
+            continue
+        if quant == 30:
+            v = (((r * 17 + c * 3 + seed) % 17).astype(np.float32) - f32(8.0)) * f32(0.025)
+            rows_out.append(np.array([f32_to_bf16_bits(x) for x in v], dtype="<u2").view(np.uint8))
+            continue
+        out = bytearray()
+        nb = cols // (256 if quant in (12, 13, 14) else 32)
+        for b in range(nb):
+            if quant in (2, 6):
+                blk = bytearray(sc)
+                if quant == 6:
+                    blk += struct.pack("<I", 0x55AA55AA)
+                blk += bytes((((r + b + j + seed) % 15) | (((r + b + 2 * j + seed) % 15) << 4)) for j in range(16))
+            elif quant == 8:
+                blk = bytearray(sc) + bytes(np.array([((r + b * 3 + j + seed) % 29) - 14 for j in range(32)],
+                                                     dtype=np.int8).view(np.uint8))
+            elif quant == 12:
+                blk = bytearray(sc) + mn + bytes([0x21] * 12)
+                blk += bytes((((r + b + j + seed) % 15) | (((r + 2 * b + 3 * j + seed) % 15) << 4)) for j in range(128))
+            elif quant == 13:
+                blk = bytearray(sc) + mn + bytes([0x18] * 12) + bytes([0x33] * 32)
+                blk += bytes((((r + b + j + seed) % 15) | (((r + b + 3 * j + seed) % 15) << 4)) for j in range(128))
+            else:  # 14, Q6_K
+                blk = bytearray(((r + b + j * 5 + seed) & 0x77) for j in range(128))
+                blk += bytes([0x55] * 64) + bytes([0x03] * 16) + sc
+            out += blk
+        rows_out.append(np.frombuffer(bytes(out), dtype=np.uint8))
+    return np.concatenate(rows_out)
+
+
+def wave4_model_gguf(arch, quant, hidden=256, ffn=256, n_q=4, n_kv=2, head_dim=64, vocab=16):
+    """The one-layer single-quant model of
+    tests/wave4_zero_alloc_decode_gemv.rs:248-363 (build_synthetic_quant_gguf):
+    every matrix, the embedding and the head in `quant`, F32 norms
+    (0.9 + (i % 5) * 0.02) and, for qwen2, F32 Q/K/V biases
+    (((i % 7) - 3) * 0.01); matrix i (in file order) filled by
+    wave4_fill_tensor(rows, cols, quant, i + 1); context length 16."""
+    import gguf_py
+
+    Q, KV = n_q * head_dim, n_kv * head_dim
+    specs = [("token_embd.weight", quant, [hidden, vocab]), ("blk.0.attn_norm.weight", 0, [hidden]),
+             ("blk.0.attn_q.weight", quant, [hidden, Q]), ("blk.0.attn_k.weight", quant, [hidden, KV]),
+             ("blk.0.attn_v.weight", quant, [hidden, KV]), ("blk.0.attn_output.weight", quant, [Q, hidden]),
+             ("blk.0.ffn_norm.weight", 0, [hidden]), ("blk.0.ffn_gate.weight", quant, [hidden, ffn]),
+             ("blk.0.ffn_up.weight", quant, [hidden, ffn]), ("blk.0.ffn_down.weight", quant, [ffn, hidden]),
+             ("output_norm.weight", 0, [hidden]), ("output.weight", quant, [hidden, vocab])]
+    if arch == "qwen2":
+        specs += [("blk.0.attn_q.bias", 0, [Q]), ("blk.0.attn_k.bias", 0, [KV]), ("blk.0.attn_v.bias", 0, [KV])]
+    tensors = []
+    for i, (name, q, dims) in enumerate(specs):
+        if q == 0 and len(dims) == 1:
+            e = np.arange(dims[0], dtype=np.int64)
+            if "norm" in name:
+                v = f32(0.9) + (e % 5).astype(np.float32) * f32(0.02)
+            else:
+                v = ((e % 7).astype(np.float32) - f32(3.0)) * f32(0.01)
+            payload = v.astype("<f4").view(np.uint8)
+        else:
+            payload = wave4_fill_tensor(dims[1] if len(dims) > 1 else 1, dims[0], q, i + 1)
+        tensors.append((name, q, dims, payload))
+    kvs = [("general.architecture", arch), ("general.alignment", 32), (f"{arch}.block_count", 1),
+           (f"{arch}.embedding_length", hidden), (f"{arch}.feed_forward_length", ffn),
+           (f"{arch}.attention.head_count", n_q), (f"{arch}.attention.head_count_kv", n_kv),
+           (f"{arch}.attention.key_length", head_dim), (f"{arch}.attention.layer_norm_rms_epsilon", 1e-5),
+           (f"{arch}.rope.freq_base", 10000.0), (f"{arch}.context_length", 16)]
+    return gguf_py.write(kvs, tensors)

@@ -373,3 +373,34 @@ def test_oracle_mixed_type_model_uneven_three_chunks(jal, oracle):
         m.prefill(kv_b, cap, prompt[start:end], start, compute_logits=False)
     lb = m.prefill(kv_b, cap, prompt[19:], 19)
     assert np.array_equal(la, lb) and np.array_equal(kv_a, kv_b)
+
+
+WAVE4_CASES = [("llama", 0), ("llama", 1), ("qwen2", 30), ("llama", 2), ("qwen2", 6), ("llama", 8), ("qwen2", 12),
+               ("llama", 13), ("qwen2", 14)]  # F32, F16, BF16, Q4_0, Q5_0, Q8_0, Q4_K_M, Q5_K, Q6_K
+
+
+@pytest.mark.parametrize("arch,quant", WAVE4_CASES)
+def test_oracle_single_quant_models_decode(jal, oracle, arch, quant):
+    # tests/wave4_zero_alloc_decode_gemv.rs:365-493: a one-layer model with
+    # every matrix (embedding and LM head included) in one of the nine
+    # admitted types; prefill [1], then decodes of 2, 3, 4, 5 give finite
+    # logits, the same with 1 and 4 worker threads (the reference's paths
+    # agree bit for bit).  The product's recipe admits and validates each.
+    import ref_fixtures
+    buf = ref_fixtures.wave4_model_gguf(arch, quant)
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    recipe.validate_model(buf)
+    _, tensors = gguf_py.parse(buf)
+    geom = dict(num_layers=1, hidden_dim=256, ffn_dim=256, n_heads_q=4, n_heads_kv=2, head_dim=64, vocab_size=16,
+                rms_eps=1e-5, rope_theta=10000.0, neox=arch == "qwen2")
+    runs = []
+    for threads in (1, 4):
+        m = oracle.Model(tensors, geom, nthreads=threads)
+        kv = m.new_kv(16)
+        out = [m.prefill(kv, 16, [1], 0)]
+        for pos, tok in enumerate((2, 3, 4, 5), start=1):
+            out.append(m.decode(kv, 16, tok, pos))
+        assert all(np.all(np.isfinite(o)) for o in out)
+        runs.append((np.stack(out), kv))
+    assert np.array_equal(runs[0][0], runs[1][0]) and np.array_equal(runs[0][1], runs[1][1])
+    assert float(np.max(np.abs(runs[0][0]))) > 0.0

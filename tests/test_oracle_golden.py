@@ -248,3 +248,38 @@ def test_act_quantizer_semantics(oracle):
     assert q[0, 0] == int(np.round(np.float32(0.5) * inv)) and q[0, 1] == -127
     assert q[0, 3] == 0 and q[0, 4] == 0  # non-finite -> 0
     assert s[0, 1] == np.float32(3.0) / np.float32(127.0) and q[0, 32] == 127 and q[0, 42] == 0
+
+
+@pytest.mark.parametrize("quant", [2, 12, 13, 14, 8])
+def test_wave4_streaming_gemv_workers_1_4_8(oracle, quant):
+    # tests/wave4_zero_alloc_decode_gemv.rs:548-623: gemv_decode_projection
+    # of a 64 x 256 matrix (wave-4 fill, seed 9) with 1, 4 and 8 workers is
+    # bit-identical, each row within 0.05 + 1% of compute_row_dot.
+    rows, cols = 64, 256
+    raw = fx.wave4_fill_tensor(rows, cols, quant, 9)
+    i = np.arange(cols, dtype=np.int64)
+    x = (((i * 7 + 3) % 19).astype(np.float32) - np.float32(9.0)) * np.float32(0.05)
+    outs = [oracle.gemv_decode_projection(raw, quant, rows, cols, x, nthreads=t) for t in (1, 4, 8)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+    for r in range(rows):
+        exp = oracle.compute_row_dot(r, cols, quant, raw, x)
+        assert np.isfinite(outs[0][r]) and abs(outs[0][r] - exp) < 0.05 + abs(exp) * 0.01
+
+
+def test_wave4_152k_vocab_gemv_determinism(oracle):
+    # tests/wave4_zero_alloc_decode_gemv.rs:625-683: a 151936 x 256 Q4_0 head,
+    # zero except rows 0, 75968 and the last (wave-4 fill, seed row + 1),
+    # against a 0.125 activation: the streaming GEMV with 1, 4 and 8 workers
+    # agrees bit for bit, and the repacked projection (its own activation
+    # quantizer) is zero on exactly the same rows.
+    rows, cols, rb = 151_936, 256, 256 // 32 * 18
+    raw = np.zeros(rows * rb, dtype=np.uint8)
+    for r in (0, 75_968, rows - 1):
+        raw[r * rb:(r + 1) * rb] = fx.wave4_fill_tensor(1, cols, 2, r + 1)
+    x = np.full(cols, 0.125, dtype=np.float32)
+    outs = [oracle.gemv_decode_projection(raw, 2, rows, cols, x, nthreads=t) for t in (1, 4, 8)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+    rep = oracle.RepackedWeight(raw, 2, rows, cols).project_batch(x, 1, nthreads=8)[0]
+    nz = [0, 75_968, rows - 1]
+    assert np.all(outs[0][1:75_968] == 0.0) and np.all(outs[0][nz] != 0.0)
+    assert np.array_equal(rep == 0.0, outs[0] == 0.0)
