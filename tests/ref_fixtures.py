@@ -341,3 +341,93 @@ def wave4_model_gguf(arch, quant, hidden=256, ffn=256, n_q=4, n_kv=2, head_dim=6
            (f"{arch}.attention.key_length", head_dim), (f"{arch}.attention.layer_norm_rms_epsilon", 1e-5),
            (f"{arch}.rope.freq_base", 10000.0), (f"{arch}.context_length", 16)]
     return gguf_py.write(kvs, tensors)
+
+
+def authentic_matrix_bytes(rows, cols, quant, seed):
+    """tests/authentic_gguf_forward.rs:40-234 (build_realistic_matrix_bytes):
+    element or block patterns of the flat index and the seed with fixed f16
+    scales per type."""
+    n = rows * cols
+    i = np.arange(n, dtype=np.int64)
+    if quant == 0:
+        return ((((i * 13 + seed * 7) % 97).astype(np.float32) - f32(48.0)) * f32(0.015)).astype("<f4").view(np.uint8)
+    if quant == 1:
+        v = (((i * 11 + seed * 5) % 89).astype(np.float32) - f32(44.0)) * f32(0.02)
+        return np.array([f32_to_f16_bits_trunc(x) for x in v], dtype="<u2").view(np.uint8)
+    if quant == 30:
+        v = (((i * 17 + seed * 3) % 83).astype(np.float32) - f32(41.0)) * f32(0.02)
+        return np.array([f32_to_bf16_bits(x) for x in v], dtype="<u2").view(np.uint8)
+    out = bytearray()
+    if quant in (8, 2, 6):
+        d = _f16le({8: 0.025, 2: 0.125, 6: 0.0625}[quant]).tobytes()
+        for b in range(n // 32):
+            out += d
+            if quant == 8:
+                out += bytes(np.array([((b * 19 + k * 7 + seed) % 121) - 60 for k in range(32)],
+                                      dtype=np.int8).view(np.uint8))
+                continue
+            if quant == 6:
+                out += struct.pack("<I", ((b * 0x9E3779B9) ^ seed) & 0xFFFFFFFF)
+            out += bytes((((b * 7 + k * 3 + seed) & 0x0F) | (((b * 11 + k * 5 + seed) & 0x0F) << 4)) for k in range(16))
+        return np.frombuffer(bytes(out), dtype=np.uint8)
+    for b in range(n // 256):
+        if quant in (12, 13):
+            out += _f16le(0.05 if quant == 12 else 0.04).tobytes() + _f16le(0.02 if quant == 12 else 0.015).tobytes()
+            out += bytes(((b + s * 9 + seed) % 61) + 1 for s in range(12))
+            if quant == 13:
+                out += bytes(((b * 17 + h * 13 + seed) & 0xFF) for h in range(32))
+            out += bytes((((b * 5 + q * 3 + seed) & 0x0F) | (((b * 13 + q * 7 + seed) & 0x0F) << 4)) for q in range(128))
+        else:  # 14, Q6_K
+            out += bytes(((b * 7 + k * 11 + seed) & 0xFF) for k in range(128))
+            out += bytes(((b * 3 + k * 5 + seed) & 0xFF) for k in range(64))
+            out += bytes(np.array([((b + s * 3 + seed) % 15) - 7 for s in range(16)], dtype=np.int8).view(np.uint8))
+            out += _f16le(0.02).tobytes()
+    return np.frombuffer(bytes(out), dtype=np.uint8)
+
+
+def authentic_two_layer_gguf(arch, quant, with_biases, with_untied_output):
+    """tests/authentic_gguf_forward.rs:236-358 (build_two_layer_gguf): two
+    layers, hidden 256, FFN 512, 8 / 2 heads of 32 dims, vocab 67, theta 1e6
+    and eps 1e-6 for qwen2 (5e5 / 1e-5 for llama), context 64; every matrix
+    in `quant` (matrix i in file order filled by
+    authentic_matrix_bytes(rows, cols, quant, i + 1)), F32 norms
+    0.85 + (e % 13) * 0.02, optional F32 Q/K/V biases
+    (((7 e + 11 i) % 29) - 14) * 0.08 and an optional untied output.weight."""
+    import gguf_py
+
+    hidden, ffn, n_q, n_kv, hd, vocab = 256, 512, 8, 2, 32, 67
+    Q, KV = n_q * hd, n_kv * hd
+    specs = [("token_embd.weight", quant, [hidden, vocab])]
+    for l_ in range(2):
+        b = f"blk.{l_}."
+        specs += [(b + "attn_norm.weight", 0, [hidden]), (b + "attn_q.weight", quant, [hidden, Q]),
+                  (b + "attn_k.weight", quant, [hidden, KV]), (b + "attn_v.weight", quant, [hidden, KV]),
+                  (b + "attn_output.weight", quant, [Q, hidden]), (b + "ffn_norm.weight", 0, [hidden]),
+                  (b + "ffn_gate.weight", quant, [hidden, ffn]), (b + "ffn_up.weight", quant, [hidden, ffn]),
+                  (b + "ffn_down.weight", quant, [ffn, hidden])]
+    specs.append(("output_norm.weight", 0, [hidden]))
+    if with_biases:
+        for l_ in range(2):
+            specs += [(f"blk.{l_}.attn_q.bias", 0, [Q]), (f"blk.{l_}.attn_k.bias", 0, [KV]),
+                      (f"blk.{l_}.attn_v.bias", 0, [KV])]
+    if with_untied_output:
+        specs.append(("output.weight", quant, [hidden, vocab]))
+    tensors = []
+    for i, (name, q, dims) in enumerate(specs):
+        if len(dims) == 1:
+            e = np.arange(dims[0], dtype=np.int64)
+            if name.endswith("norm.weight"):
+                v = f32(0.85) + (e % 13).astype(np.float32) * f32(0.02)
+            else:
+                v = (((e * 7 + i * 11) % 29).astype(np.float32) - f32(14.0)) * f32(0.08)
+            payload = v.astype("<f4").view(np.uint8)
+        else:
+            payload = authentic_matrix_bytes(dims[1], dims[0], q, i + 1)
+        tensors.append((name, q, dims, payload))
+    qwen = arch == "qwen2"
+    kvs = [("general.architecture", arch), ("general.alignment", 32), (f"{arch}.block_count", 2),
+           (f"{arch}.embedding_length", hidden), (f"{arch}.feed_forward_length", ffn),
+           (f"{arch}.attention.head_count", n_q), (f"{arch}.attention.head_count_kv", n_kv),
+           (f"{arch}.attention.key_length", hd), (f"{arch}.rope.freq_base", 1e6 if qwen else 5e5),
+           (f"{arch}.attention.layer_norm_rms_epsilon", 1e-6 if qwen else 1e-5), (f"{arch}.context_length", 64)]
+    return gguf_py.write(kvs, tensors)

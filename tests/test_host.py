@@ -404,3 +404,69 @@ def test_oracle_single_quant_models_decode(jal, oracle, arch, quant):
         runs.append((np.stack(out), kv))
     assert np.array_equal(runs[0][0], runs[1][0]) and np.array_equal(runs[0][1], runs[1][1])
     assert float(np.max(np.abs(runs[0][0]))) > 0.0
+
+
+def _authentic_oracle(jal, oracle, arch, quant, biases, untied, threads=2):
+    import ref_fixtures
+    buf = ref_fixtures.authentic_two_layer_gguf(arch, quant, biases, untied)
+    recipe = jal.LlamaRecipe.from_gguf(buf)
+    recipe.validate_model(buf)
+    f = recipe.fields()
+    assert (f.num_layers, f.hidden_dim, f.ffn_dim, f.n_heads_q, f.n_heads_kv, f.head_dim, f.vocab_size) == \
+        (2, 256, 512, 8, 2, 32, 67)
+    _, tensors = gguf_py.parse(buf)
+    qwen = arch == "qwen2"
+    geom = dict(num_layers=2, hidden_dim=256, ffn_dim=512, n_heads_q=8, n_heads_kv=2, head_dim=32, vocab_size=67,
+                rms_eps=1e-6 if qwen else 1e-5, rope_theta=1e6 if qwen else 5e5, neox=qwen)
+    return oracle.Model(tensors, geom, nthreads=threads)
+
+
+def test_oracle_authentic_qwen2_biases_history_and_tied_head(jal, oracle):
+    # tests/authentic_gguf_forward.rs:531-628 on the oracle: QKV biases move
+    # the logits (sum |diff| > 1e-2), permuting the prefix before the same last
+    # token moves them (> 1e-4: causal attention over the whole history with
+    # K-RoPE), an untied output.weight differs from the tied embedding
+    # (> 1e-2), and an out-of-range token fails.
+    cap = 16
+    biased = _authentic_oracle(jal, oracle, "qwen2", 8, True, False)
+    plain = _authentic_oracle(jal, oracle, "qwen2", 8, False, False)
+    untied = _authentic_oracle(jal, oracle, "qwen2", 8, True, True)
+    la = biased.prefill(biased.new_kv(cap), cap, [2, 9, 4, 15], 0)
+    assert np.all(np.isfinite(la))
+    assert float(np.sum(np.abs(la - plain.prefill(plain.new_kv(cap), cap, [2, 9, 4, 15], 0)))) > 1e-2
+    assert float(np.sum(np.abs(la - biased.prefill(biased.new_kv(cap), cap, [9, 2, 4, 15], 0)))) > 1e-4
+    assert float(np.sum(np.abs(la - untied.prefill(untied.new_kv(cap), cap, [2, 9, 4, 15], 0)))) > 1e-2
+    with pytest.raises(oracle.OracleError, match="status 1$"):  # OR_ERR_TENSOR_BOUNDS
+        biased.prefill(biased.new_kv(cap), cap, [999], 0)
+
+
+@pytest.mark.parametrize("quant", [0, 1, 8, 2, 6, 12, 13, 14])
+def test_oracle_authentic_batched_prefill_vs_sequential(jal, oracle, quant):
+    # tests/authentic_gguf_forward.rs:630-691: prefill [3, 11, 27, 42] then
+    # decode 19 against prefill [3] + decodes, logits within 1e-4 (bit-equal
+    # in the oracle), untied head, FFN 512 > hidden 256, vocab 67.
+    m = _authentic_oracle(jal, oracle, "llama", quant, False, True)
+    cap = 16
+    kv_a = m.new_kv(cap)
+    m.prefill(kv_a, cap, [3, 11, 27, 42], 0)
+    la = m.decode(kv_a, cap, 19, 4)
+    kv_b = m.new_kv(cap)
+    m.prefill(kv_b, cap, [3], 0)
+    for pos, tok in enumerate((11, 27, 42), start=1):
+        m.decode(kv_b, cap, tok, pos)
+    lb = m.decode(kv_b, cap, 19, 4)
+    assert np.all(np.isfinite(la)) and np.max(np.abs(la - lb)) < 1e-4
+    assert np.array_equal(la, lb) and np.array_equal(kv_a, kv_b)
+
+
+def test_oracle_authentic_threads_1_vs_4(jal, oracle):
+    # tests/authentic_gguf_forward.rs:693-741: the qwen2 Q4_K_M model with
+    # biases and an untied head, prefill [1, 5, 9, 13, 17, 21] + decode 8 with
+    # 1 and 4 threads: within 1e-5 (bit-equal in the oracle).
+    outs = []
+    for threads in (1, 4):
+        m = _authentic_oracle(jal, oracle, "qwen2", 12, True, True, threads)
+        kv = m.new_kv(16)
+        m.prefill(kv, 16, [1, 5, 9, 13, 17, 21], 0)
+        outs.append(m.decode(kv, 16, 8, 6))
+    assert np.all(np.isfinite(outs[0])) and np.array_equal(outs[0], outs[1])

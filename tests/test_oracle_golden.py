@@ -283,3 +283,44 @@ def test_wave4_152k_vocab_gemv_determinism(oracle):
     nz = [0, 75_968, rows - 1]
     assert np.all(outs[0][1:75_968] == 0.0) and np.all(outs[0][nz] != 0.0)
     assert np.array_equal(rep == 0.0, outs[0] == 0.0)
+
+
+def _cos(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.dot(a, b) / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-12))
+
+
+@pytest.mark.parametrize("quant", ADMITTED)
+def test_authentic_repacked_gemv_and_gemm_parity(oracle, quant):
+    # tests/authentic_gguf_forward.rs:370-468: 133 rows (panels of 64 + 64 + 5,
+    # not a multiple of 8) x 256 columns of the realistic fills, M = 1 and 5
+    # activation rows ((((23 i + 5) % 101) - 50) * 0.03): each output within
+    # 1e-5 (dense) / 1e-2 (quantized) of compute_row_dot relative to
+    # max(|x|_2 sqrt(cols), |expected|, 1), cosine > 0.9998 per token, and the
+    # M = 1 projection equal to the first row of the M = 5 one within 1e-5.
+    rows, cols, m = 133, 256, 5
+    raw = fx.authentic_matrix_bytes(rows, cols, quant, ADMITTED.index(quant) + 10)
+    w = oracle.RepackedWeight(raw, quant, rows, cols)
+    i = np.arange(m * cols, dtype=np.int64)
+    act = (((i * 23 + 5) % 101).astype(np.float32) - np.float32(50.0)) * np.float32(0.03)
+    tol = 1e-5 if quant in (0, 1, 30) else 1e-2
+    single = w.project_batch(act[:cols], 1)[0]
+    batched = w.project_batch(act, m)
+    assert np.all(np.abs(single - batched[0]) < 1e-5)
+    for t in range(m):
+        x = act[t * cols:(t + 1) * cols]
+        ref = np.array([oracle.compute_row_dot(r, cols, quant, raw, x) for r in range(rows)], dtype=np.float32)
+        bound = np.maximum(max(float(np.linalg.norm(x)) * math.sqrt(cols), 1.0), np.abs(ref))
+        assert np.all(np.abs(batched[t] - ref) / bound < tol)
+        assert _cos(batched[t], ref) > 0.9998
+
+
+def test_authentic_q4_k_head_rows_identical_across_threads(oracle):
+    # tests/authentic_gguf_forward.rs:743-761: a 263 x 256 Q4_K_M head
+    # (seed 77) against a 0.25 activation, 1 vs 4 threads, bit-identical.
+    raw = fx.authentic_matrix_bytes(263, 256, 12, 77)
+    x = np.full(256, 0.25, dtype=np.float32)
+    w = oracle.RepackedWeight(raw, 12, 263, 256)
+    assert np.array_equal(w.project_batch(x, 1, nthreads=1), w.project_batch(x, 1, nthreads=4))
+    assert np.array_equal(oracle.gemv_decode_projection(raw, 12, 263, 256, x, nthreads=1),
+                          oracle.gemv_decode_projection(raw, 12, 263, 256, x, nthreads=4))
