@@ -470,3 +470,50 @@ def test_oracle_authentic_threads_1_vs_4(jal, oracle):
         m.prefill(kv, 16, [1, 5, 9, 13, 17, 21], 0)
         outs.append(m.decode(kv, 16, 8, 6))
     assert np.all(np.isfinite(outs[0])) and np.array_equal(outs[0], outs[1])
+
+
+def test_every_entry_point_fails_closed_on_null_arguments(jal):
+    # The boundary's error behaviour (K3Error-style status codes,
+    # lib.rs:1022-1035): every status-returning entry point called with null
+    # handles and zero sizes returns JAL_ERR_INVALID_ARGUMENT with a message
+    # (jal_set_device(0) only depends on whether a device exists), the size / count
+    # queries return 0 and the frees accept NULL, all without a crash (run in
+    # a child process so that a crash fails the test rather than the suite).
+    import json
+    import subprocess
+    import sys
+    code = r'''
+import ctypes as C, importlib, json, sys
+sys.path.insert(0, ".")
+jal = importlib.import_module("jero-arch-llama_b200")
+lib = jal.lib()
+out = {}
+for name, (res, args) in jal._SIGS.items():
+    if name in ("jal_last_error", "jal_version", "jal_f32_to_f16_bits"):
+        continue
+    vals = [0.0 if a is C.c_float else (0 if a in (C.c_int, C.c_int32, C.c_uint32, C.c_uint64, C.c_size_t) else None)
+            for a in args]
+    rc = getattr(lib, name)(*vals)
+    out[name] = [rc, (lib.jal_last_error() or b"").decode(errors="replace")]
+print(json.dumps(out))
+'''
+    p = subprocess.run([sys.executable, "-c", code], cwd=REPO, capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-2000:]
+    out = json.loads(p.stdout.strip().splitlines()[-1])
+    sigs = jal._SIGS
+    import ctypes as C
+    for name, (rc, msg) in out.items():
+        res = sigs[name][0]
+        if res is None:
+            assert rc is None, name
+        elif res is C.c_size_t or name in ("jal_recipe_should_skip_rope", "jal_recipe_supports_quant"):
+            assert rc == 0, name
+        elif name == "jal_cached_matrix_quant":
+            assert rc == -1
+        elif name == "jal_model_cache_matrix":
+            assert rc is None
+        elif name == "jal_set_device":  # device 0: present on a GPU machine, not here
+            assert rc in (jal.OK, jal.ERR_CUDA), name
+        else:
+            assert rc == jal.ERR_INVALID_ARGUMENT and msg.startswith("null argument"), (name, rc, msg)
+    assert len(out) >= 75
