@@ -517,3 +517,46 @@ print(json.dumps(out))
         else:
             assert rc == jal.ERR_INVALID_ARGUMENT and msg.startswith("null argument"), (name, rc, msg)
     assert len(out) >= 75
+
+
+def test_gguf_reader_fails_closed_on_corrupt_files(jal):
+    # GGUF files are untrusted input: 600 seeded corruptions of a valid file's
+    # header region (truncations, random bytes, random 64-bit counts and
+    # lengths) through LlamaRecipe.from_gguf + validate_model either parse or
+    # raise K3Error; none may crash (a child process runs them).
+    import subprocess
+    import sys
+    code = r'''
+import importlib, sys
+import numpy as np
+sys.path.insert(0, ".")
+jal = importlib.import_module("jero-arch-llama_b200")
+spec = jal.SynthSpec(num_layers=1, hidden_dim=128, ffn_dim=256, n_heads_q=4, n_heads_kv=2, head_dim=32,
+                     vocab_size=64)
+buf = jal.synth_gguf(spec, 3)
+rng = np.random.default_rng(2024)
+hdr = 4096
+counts = [0, 0]
+for it in range(600):
+    b = buf.copy()
+    kind = it % 3
+    if kind == 0:
+        b = b[: int(rng.integers(0, hdr))]
+    elif kind == 1:
+        for _ in range(int(rng.integers(1, 8))):
+            b[int(rng.integers(0, hdr))] = int(rng.integers(0, 256))
+    else:
+        pos = int(rng.integers(0, hdr - 8))
+        b[pos:pos + 8] = np.frombuffer(int(rng.integers(0, 2**63)).to_bytes(8, "little"), dtype=np.uint8)
+    try:
+        r = jal.LlamaRecipe.from_gguf(b)
+        r.validate_model(b)
+        counts[0] += 1
+    except jal.K3Error:
+        counts[1] += 1
+print(counts[0], counts[1])
+'''
+    p = subprocess.run([sys.executable, "-c", code], cwd=REPO, capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stderr[-2000:]
+    ok, err = map(int, p.stdout.split()[-2:])
+    assert ok + err == 600 and err > 100
