@@ -70,6 +70,33 @@ def test_tp_plan_partitions_heads_ffn_and_vocab(jal, name, hq, hkv, ffn, vocab):
         assert plans[0]["v_pad"] * world >= vocab
 
 
+def test_tp_plan_partition_property(jal):
+    # Any geometry and world size: the plan either refuses (KV heads or
+    # 32-blocks of the FFN do not split evenly) or its rank shards tile the
+    # KV heads, query heads, FFN rows and vocabulary exactly, in rank order.
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=300, deadline=None, derandomize=True)
+    @given(hkv=st.integers(1, 16), group=st.integers(1, 8), ffn_blocks=st.integers(1, 600),
+           vocab=st.integers(1, 300_000), world=st.sampled_from([1, 2, 3, 4, 8]))
+    def check(hkv, group, ffn_blocks, vocab, world):
+        hq, ffn = hkv * group, 32 * ffn_blocks
+        if hkv % world or ffn_blocks % world:
+            with pytest.raises(jal.CapabilityMismatch):
+                jal.tp_plan(hq, hkv, ffn, vocab, 0, world)
+            return
+        plans = [jal.tp_plan(hq, hkv, ffn, vocab, r, world) for r in range(world)]
+        nxt = dict(q=0, kv=0, f=0, v=0)
+        for p in plans:
+            for k in nxt:
+                assert p[k + "_lo"] == nxt[k]
+                nxt[k] += p[k + "_n"]
+            assert p["q_n"] == p["kv_n"] * group and p["f_n"] % 32 == 0 and p["v_n"] <= p["v_pad"]
+        assert nxt == dict(q=hq, kv=hkv, f=ffn, v=vocab)
+
+    check()
+
+
 def test_tp_plan_rejects_uneven_splits(jal):
     with pytest.raises(jal.CapabilityMismatch):
         jal.tp_plan(32, 8, 14336, 128256, 0, 3)   # 8 KV heads over 3 ranks
