@@ -560,3 +560,70 @@ print(counts[0], counts[1])
     assert p.returncode == 0, p.stderr[-2000:]
     ok, err = map(int, p.stdout.split()[-2:])
     assert ok + err == 600 and err > 100
+
+
+def _small_gguf_parts(jal):
+    spec = jal.SynthSpec(num_layers=1, hidden_dim=128, ffn_dim=256, n_heads_q=4, n_heads_kv=2, head_dim=32,
+                         vocab_size=64)
+    kv, t = gguf_py.parse(jal.synth_gguf(spec, 3))
+    return kv, [(n, x.qtype, x.dims, x.data) for n, x in t.items()]
+
+
+@pytest.mark.parametrize("key,value", [("rope.freq_base", float("nan")), ("rope.freq_base", -1.0),
+                                       ("rope.freq_base", "x"),
+                                       ("attention.layer_norm_rms_epsilon", float("inf")),
+                                       ("attention.layer_norm_rms_epsilon", 0.0),
+                                       ("feed_forward_length", 0), ("attention.key_length", 1)])
+def test_recipe_ignores_invalid_metadata_values(jal, key, value):
+    # recipe.rs:311-318, 346-386: a non-finite or non-positive theta / eps, a
+    # zero FFN width or a key length below 2 (or a value of the wrong type)
+    # is ignored: the field keeps the architecture default, or the value the
+    # tensor shapes give.
+    kv, tensors = _small_gguf_parts(jal)
+    kvs = [(k, value if k == "llama." + key else v) for k, v in kv.items()]
+    f = jal.LlamaRecipe.from_gguf(gguf_py.write(kvs, tensors)).fields()
+    d = jal.LlamaRecipe.new("llama").fields()
+    assert f.rope_theta == (d.rope_theta if key == "rope.freq_base" else 10000.0)
+    assert f.rms_eps == d.rms_eps
+    assert (f.ffn_dim, f.head_dim, f.hidden_dim, f.vocab_size) == (256, 32, 128, 64)
+
+
+def test_recipe_metadata_of_wrong_types_fails_closed(jal):
+    # Every metadata key of a valid file (plus the optional RoPE-scaling,
+    # window and iRoPE keys) replaced by a value of each other type: the
+    # recipe parses or raises K3Error, never crashes (child process).
+    import subprocess
+    import sys
+    code = r'''
+import importlib, sys
+sys.path.insert(0, "."); sys.path.insert(0, "tests")
+jal = importlib.import_module("jero-arch-llama_b200")
+import gguf_py
+spec = jal.SynthSpec(num_layers=1, hidden_dim=128, ffn_dim=256, n_heads_q=4, n_heads_kv=2, head_dim=32, vocab_size=64)
+kv, t = gguf_py.parse(jal.synth_gguf(spec, 3))
+tensors = [(n, x.qtype, x.dims, x.data) for n, x in t.items()]
+keys = list(kv.items())
+extra = [("llama.rope.scaling.type", "llama3"), ("llama.rope.scaling.factor", 8.0), ("llama.rope.dimension_count", 16),
+         ("llama.attention.sliding_window", 8), ("llama.rope.scaling.original_context_length", 8192),
+         ("llama.no_rope_layer_step", 4), ("llama.rope.scaling.low_freq_factor", 1.0)]
+bad = ["x", 0.5, -1.0, 0, 1, 2**31, 3, True, ("f32[]", [1.0, 2.0]), ("u32[]", [0]), ("str[]", ["a"]),
+       float("nan"), float("inf")]
+n = [0, 0]
+for i in range(len(keys) + len(extra)):
+    for v in bad:
+        kvs = list(keys) + ([] if i < len(keys) else [extra[i - len(keys)]])
+        j = i if i < len(keys) else len(kvs) - 1
+        kvs[j] = (kvs[j][0], v)
+        b = gguf_py.write(kvs, tensors)
+        try:
+            r = jal.LlamaRecipe.from_gguf(b)
+            r.validate_model(b)
+            n[0] += 1
+        except jal.K3Error:
+            n[1] += 1
+print(n[0], n[1])
+'''
+    p = subprocess.run([sys.executable, "-c", code], cwd=REPO, capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stderr[-2000:]
+    ok, err = map(int, p.stdout.split()[-2:])
+    assert ok > 0 and err > 0
