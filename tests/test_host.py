@@ -627,3 +627,19 @@ print(n[0], n[1])
     assert p.returncode == 0, p.stderr[-2000:]
     ok, err = map(int, p.stdout.split()[-2:])
     assert ok > 0 and err > 0
+
+
+def test_integration_rust_stub_matches_the_header():
+    # The Rust extern block a maintainer of the reference would add names only
+    # functions the C header declares, each with the header's parameter count.
+    doc = open(os.path.join(REPO, "INTEGRATION.md")).read()
+    block = doc[doc.index('extern "C" {'):doc.index("}\n```")]
+    stub = {m.group(1): len([a for a in m.group(2).split(",") if a.strip()])
+            for m in re.finditer(r"pub fn (jal_[a-z0-9_]+)\((.*?)\)", block, flags=re.S)}
+    src = "".join(open(os.path.join(REPO, "include", h)).read() for h in ("jal.h", "jal_test.h"))
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    decl = {m.group(1): len([a for a in m.group(2).split(",") if a.strip() and a.strip() != "void"])
+            for m in re.finditer(r"\b(jal_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", src, flags=re.S)}
+    assert len(stub) >= 20
+    for name, n in stub.items():
+        assert decl.get(name) == n, (name, n, decl.get(name))
